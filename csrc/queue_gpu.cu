@@ -1,0 +1,875 @@
+// GPU drivers for kiwi::queue / kiwi::invoke: the round-trip benchmark, the
+// raw PCIe floor, and correctness kernels for every queue kind.
+//
+// Counterparts in the reference (AMDResearch/kiwi):
+//   invoke_rtt      benchmarks/invoke/bench_latency.hip.cpp (ping_pong_latency_handle_kernel)
+//   pcie_floor      benchmarks/hardware/pcie_latency.hip.cpp:26-37 (pingpong_kernel)
+//   d2h_push_test   tests/queue/test_chunk_queue.hip.cpp, test_push_lane_masked
+//   h2d_*_test      tests/queue/test_host_to_device_concurrent, test_mpmc_h2d_concurrent
+#include <cuda_runtime.h>
+
+#include <atomic>
+#include <cstring>
+#include <thread>
+
+#include "kiwi/bench/gpu_bench.hpp"
+#include "kiwi/bench/host_bench.hpp"
+#include "kiwi/invoke/invoke.hpp"
+#include "kiwi/ptx.cuh"
+#include "kiwi/topology.hpp"
+
+namespace kiwi::bench {
+
+using namespace kiwi::queue;
+using kiwi::invoke::DeviceContext;
+
+namespace {
+
+KIWI_HD uint64_t splitmix64(uint64_t x) {
+    x += 0x9E3779B97F4A7C15ull;
+    x = (x ^ (x >> 30)) * 0xBF58476D1CE4E5B9ull;
+    x = (x ^ (x >> 27)) * 0x94D049BB133111EBull;
+    return x ^ (x >> 31);
+}
+
+KIWI_HD uint64_t pattern_word(uint64_t seed, uint64_t msg, uint32_t word) {
+    return splitmix64(seed ^ (msg * 0x100000001B3ull) ^ (static_cast<uint64_t>(word) << 48));
+}
+
+KIWI_DEV uint64_t dev_xorshift(uint64_t& s) {
+    s ^= s << 13;
+    s ^= s >> 7;
+    s ^= s << 17;
+    return s;
+}
+
+template <typename T>
+struct DevBuf {
+    T* p = nullptr;
+    explicit DevBuf(size_t n) {
+        KIWI_CUDA_CHECK(cudaMalloc(&p, (n ? n : 1) * sizeof(T)));
+        KIWI_CUDA_CHECK(cudaMemset(p, 0, (n ? n : 1) * sizeof(T)));
+    }
+    ~DevBuf() { cudaFree(p); }
+    DevBuf(const DevBuf&) = delete;
+    DevBuf& operator=(const DevBuf&) = delete;
+};
+
+struct PinnedFlag {
+    volatile uint32_t* p = nullptr;
+    PinnedFlag() {
+        void* q = nullptr;
+        KIWI_CUDA_CHECK(cudaHostAlloc(&q, 64, cudaHostAllocMapped | cudaHostAllocPortable));
+        std::memset(q, 0, 64);
+        p = static_cast<volatile uint32_t*>(q);
+    }
+    ~PinnedFlag() { cudaFreeHost(const_cast<uint32_t*>(p)); }
+};
+
+int pick_cpu(int cpu) {
+    if (cpu >= 0) return cpu;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const auto cpus = topology::gpu_local_cpus(dev);
+    // Avoid core 0 (interrupts); take the second local core when there is one.
+    if (cpus.size() > 1) return cpus[1];
+    return cpus.empty() ? -1 : cpus[0];
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------------------
+// GPU -> CPU -> GPU invoke round trip
+// ---------------------------------------------------------------------------
+
+struct RttShared {
+    unsigned long long found;  // reply line + 1 of the newest message a poller saw
+    uint64_t line;             // reply line the pollers should watch
+    uint64_t word[4];          // payload of line (index line & 3)
+    uint32_t stop;
+};
+
+template <typename Q>
+__global__ void __launch_bounds__(256) invoke_rtt_kernel(
+    DeviceContext<Q>* ctx, SpscH2DHandle reply, uint8_t cb, uint64_t iters, uint64_t warmup,
+    uint32_t bytes, uint64_t* payload_buf, uint64_t seed, uint64_t* lat_ns, uint32_t* lat_cyc,
+    uint64_t* totals, uint32_t* status, uint32_t poll_warps, uint64_t stagger_ns,
+    uint64_t timeout_ns, volatile uint32_t* done) {
+    __shared__ RttShared sh;
+    const uint32_t warp = threadIdx.x / 32;
+    const uint32_t lane = ptx::lane_id();
+    if (threadIdx.x == 0) {
+        sh.found = 0;
+        sh.line = reply.tail;
+        sh.stop = 0;
+    }
+    __syncthreads();
+
+    if (warp > 0) {
+        // Helper pollers: keep one read of the watched reply line in flight each,
+        // staggered so their reads reach host memory evenly spaced.
+        __nanosleep(static_cast<uint32_t>(stagger_ns * (warp - 1)));
+        const uint64_t mask = reply.capacity() - 1;
+        while (true) {
+            if (*reinterpret_cast<volatile uint32_t*>(&sh.stop)) break;
+            const uint64_t line = *reinterpret_cast<volatile uint64_t*>(&sh.line);
+            const uint32_t tag = lap_tag(line, reply.log2cap);
+            uint4 v = make_uint4(0, 0, 0, 0);
+            bool ok = true;
+            if (lane < 2) {
+                v = ptx::ld_volatile_v4(&reply.ring[(line & mask) * kChunksPerLine + lane]);
+                ok = v.y == tag && v.w == tag;
+            }
+            if (__all_sync(ptx::kFullMask, ok)) {
+                const uint32_t lo = __shfl_sync(ptx::kFullMask, v.x, 1);
+                const uint32_t hi = __shfl_sync(ptx::kFullMask, v.z, 1);
+                if (lane == 0) {
+                    reinterpret_cast<volatile uint64_t*>(sh.word)[line & 3] =
+                        (static_cast<uint64_t>(hi) << 32) | lo;
+                    __threadfence_block();
+                    atomicMax(&sh.found, static_cast<unsigned long long>(line + 1));
+                }
+            }
+        }
+        return;
+    }
+
+    auto h = ctx->get_device_handle(0);
+    uint64_t s = seed ? seed : 0x9E3779B97F4A7C15ull;
+    uint32_t st = 0;
+    bool ok = true;
+    const uint64_t total = iters + warmup;
+    uint64_t t_begin = 0, c_begin = 0;
+    for (uint64_t i = 0; i < total; ++i) {
+        const uint64_t x = dev_xorshift(s);
+        if (i == warmup) {
+            t_begin = ptx::globaltimer();
+            c_begin = ptx::clock64();
+        }
+        if (bytes != 8) {
+            if (lane == 0) payload_buf[0] = x;
+            __syncwarp();
+        }
+        const uint64_t t0 = ptx::globaltimer();
+        const uint64_t c0 = ptx::clock64();
+        if (bytes == 8) {
+            while (!h.invoke(cb, x)) {
+            }
+        } else {
+            while (!h.invoke_global(cb, payload_buf, bytes)) {
+            }
+        }
+        uint64_t w = 0;
+        if (poll_warps == 0) {
+            uint32_t b, m;
+            if (reply.pop(w, b, m, timeout_ns) != Status::kOk) {
+                st = static_cast<uint32_t>(Status::kTimeout);
+                break;
+            }
+            w = ptx::bcast64(w, 0);
+        } else {
+            const uint64_t want = reply.tail + 1;
+            ptx::Deadline dl(timeout_ns);
+            bool timed_out = false;
+            while (*reinterpret_cast<volatile unsigned long long*>(&sh.found) < want) {
+                if (dl.expired()) {
+                    timed_out = true;
+                    break;
+                }
+            }
+            if (timed_out) {
+                st = static_cast<uint32_t>(Status::kTimeout);
+                break;
+            }
+            w = reinterpret_cast<volatile uint64_t*>(sh.word)[reply.tail & 3];
+            reply.advance(1);
+            if (lane == 0) *reinterpret_cast<volatile uint64_t*>(&sh.line) = reply.tail;
+        }
+        const uint64_t t1 = ptx::globaltimer();
+        const uint64_t c1 = ptx::clock64();
+        if (w != x + 1) ok = false;
+        if (i >= warmup && lane == 0) {
+            lat_ns[i - warmup] = t1 - t0;
+            lat_cyc[i - warmup] = static_cast<uint32_t>(c1 - c0);
+        }
+    }
+    if (lane == 0) {
+        totals[0] = ptx::globaltimer() - t_begin;
+        totals[1] = ptx::clock64() - c_begin;
+        status[0] = st;
+        status[1] = ok ? 1u : 0u;
+        *reinterpret_cast<volatile uint32_t*>(&sh.stop) = 1;
+    }
+    ctx->save_device_handle(0, h);
+    reply.flush_consumer_index();
+    __syncwarp();
+    if (lane == 0) {
+        __threadfence_system();
+        *done = 1;
+    }
+}
+
+template <typename Q>
+static RttResult run_invoke_rtt(const RttConfig& cfg) {
+    if (cfg.payload_bytes < 8 || cfg.payload_bytes > kMaxMessageBytes) {
+        throw kiwi::error("invoke_rtt: payload_bytes must be in [8, 4096]");
+    }
+    if (cfg.poll_warps > 7) throw kiwi::error("invoke_rtt: poll_warps must be <= 7");
+    kiwi::invoke::Context<Q> ctx(1, cfg.capacity, MemKind::kMappedPinned);
+    SPSCH2DQueue reply(64, MemKind::kMappedPinned);
+    uint64_t callbacks = 0;
+    const uint8_t cb = ctx.register_raw_callback(
+        [&](const uint8_t* p, uint32_t n) {
+            uint64_t v;
+            std::memcpy(&v, p, 8);
+            v += 1;
+            while (!reply.try_push(&v, 8, n)) host::cpu_relax();
+            ++callbacks;
+        },
+        cfg.payload_bytes);
+
+    DevBuf<uint64_t> payload(kMaxMessageBytes / 8);
+    {
+        std::vector<uint64_t> pat(kMaxMessageBytes / 8);
+        for (size_t i = 0; i < pat.size(); ++i) pat[i] = pattern_word(cfg.seed, 0, static_cast<uint32_t>(i));
+        KIWI_CUDA_CHECK(cudaMemcpy(payload.p, pat.data(), kMaxMessageBytes, cudaMemcpyHostToDevice));
+    }
+    DevBuf<uint64_t> lat(cfg.iters);
+    DevBuf<uint32_t> cyc(cfg.iters);
+    DevBuf<uint64_t> totals(2);
+    DevBuf<uint32_t> status(2);
+    PinnedFlag done;
+    cudaStream_t stream;
+    KIWI_CUDA_CHECK(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking));
+
+    const int cpu = pick_cpu(cfg.cpu);
+    if (cpu >= 0) topology::bind_current_thread({cpu});
+    const uint32_t threads = 32 * (1 + cfg.poll_warps);
+    invoke_rtt_kernel<Q><<<1, threads, 0, stream>>>(
+        ctx.device_context(), reply.device_handle(), cb, cfg.iters, cfg.warmup, cfg.payload_bytes,
+        payload.p, cfg.seed, lat.p, cyc.p, totals.p, status.p, cfg.poll_warps,
+        /*stagger_ns=*/cfg.poll_warps ? 800 / cfg.poll_warps : 0, cfg.timeout_ns, done.p);
+    KIWI_CUDA_CHECK(cudaGetLastError());
+
+    auto poll = ctx.poll_state(0);
+    uint64_t idle = 0;
+    while (true) {
+        if (poll.ready()) {
+            ctx.progress(0);
+            poll.refresh();
+            idle = 0;
+            continue;
+        }
+        if (*done.p) break;
+        if ((++idle & 0xfffff) == 0 && cudaStreamQuery(stream) != cudaErrorNotReady) break;
+    }
+    ctx.progress(0);
+    KIWI_CUDA_CHECK(cudaStreamSynchronize(stream));
+    cudaStreamDestroy(stream);
+
+    RttResult r;
+    r.lat_ns.resize(cfg.iters);
+    std::vector<uint32_t> c32(cfg.iters);
+    uint64_t tot[2];
+    uint32_t stv[2];
+    KIWI_CUDA_CHECK(cudaMemcpy(r.lat_ns.data(), lat.p, cfg.iters * 8, cudaMemcpyDeviceToHost));
+    KIWI_CUDA_CHECK(cudaMemcpy(c32.data(), cyc.p, cfg.iters * 4, cudaMemcpyDeviceToHost));
+    KIWI_CUDA_CHECK(cudaMemcpy(tot, totals.p, sizeof(tot), cudaMemcpyDeviceToHost));
+    KIWI_CUDA_CHECK(cudaMemcpy(stv, status.p, sizeof(stv), cudaMemcpyDeviceToHost));
+    r.lat_cycles.assign(c32.begin(), c32.end());
+    r.total_ns = tot[0];
+    r.total_cycles = tot[1];
+    r.status = stv[0];
+    r.callbacks = callbacks;
+    r.ok = stv[0] == 0 && stv[1] == 1 && callbacks == cfg.iters + cfg.warmup;
+    ctx.check_device_errors();
+    return r;
+}
+
+RttResult invoke_rtt(const RttConfig& cfg) {
+    return cfg.mpsc ? run_invoke_rtt<MPSCD2HQueue>(cfg) : run_invoke_rtt<SPSCD2HQueue>(cfg);
+}
+
+// ---------------------------------------------------------------------------
+// Raw PCIe store-and-poll floor
+// ---------------------------------------------------------------------------
+
+__global__ void pcie_floor_kernel(uint64_t* d2h, const uint64_t* h2d, uint64_t iters,
+                                  uint64_t warmup, uint64_t* lat_ns, uint32_t* lat_cyc,
+                                  uint64_t* totals, uint32_t* status, uint64_t timeout_ns) {
+    if (threadIdx.x != 0) return;
+    uint64_t t_begin = 0, c_begin = 0;
+    for (uint64_t i = 0; i < iters + warmup; ++i) {
+        if (i == warmup) {
+            t_begin = ptx::globaltimer();
+            c_begin = ptx::clock64();
+        }
+        const uint64_t t0 = ptx::globaltimer();
+        const uint64_t c0 = ptx::clock64();
+        ptx::st_volatile_u64(d2h, i + 1);
+        ptx::Deadline dl(timeout_ns);
+        while (ptx::ld_volatile_u64(h2d) != i + 1) {
+            if (dl.expired()) {
+                status[0] = static_cast<uint32_t>(Status::kTimeout);
+                ptx::st_volatile_u64(d2h, ~0ull);
+                return;
+            }
+        }
+        const uint64_t t1 = ptx::globaltimer();
+        const uint64_t c1 = ptx::clock64();
+        if (i >= warmup) {
+            lat_ns[i - warmup] = t1 - t0;
+            lat_cyc[i - warmup] = static_cast<uint32_t>(c1 - c0);
+        }
+    }
+    totals[0] = ptx::globaltimer() - t_begin;
+    totals[1] = ptx::clock64() - c_begin;
+    status[1] = 1;
+    ptx::fence_sys();
+    ptx::st_volatile_u64(d2h, ~0ull);
+}
+
+RttResult pcie_floor(uint64_t iters, uint64_t warmup, int cpu, uint64_t timeout_ns) {
+    detail::Block words(128, MemKind::kMappedPinned);
+    volatile uint64_t* d2h = words.as<volatile uint64_t>();
+    volatile uint64_t* h2d = words.as<volatile uint64_t>() + 8;  // separate cache line
+    DevBuf<uint64_t> lat(iters);
+    DevBuf<uint32_t> cyc(iters);
+    DevBuf<uint64_t> totals(2);
+    DevBuf<uint32_t> status(2);
+    cudaStream_t stream;
+    KIWI_CUDA_CHECK(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking));
+    const int c = pick_cpu(cpu);
+    if (c >= 0) topology::bind_current_thread({c});
+    pcie_floor_kernel<<<1, 32, 0, stream>>>(const_cast<uint64_t*>(d2h), const_cast<uint64_t*>(h2d),
+                                            iters, warmup, lat.p, cyc.p, totals.p, status.p,
+                                            timeout_ns);
+    KIWI_CUDA_CHECK(cudaGetLastError());
+    uint64_t expect = 1;
+    uint64_t idle = 0;
+    while (true) {
+        const uint64_t v = *d2h;
+        if (v == ~0ull) break;
+        if (v == expect) {
+            *h2d = v;
+            ++expect;
+            idle = 0;
+        } else if ((++idle & 0xfffff) == 0 && cudaStreamQuery(stream) != cudaErrorNotReady) {
+            break;
+        }
+    }
+    KIWI_CUDA_CHECK(cudaStreamSynchronize(stream));
+    cudaStreamDestroy(stream);
+    RttResult r;
+    r.lat_ns.resize(iters);
+    std::vector<uint32_t> c32(iters);
+    uint64_t tot[2];
+    uint32_t stv[2];
+    KIWI_CUDA_CHECK(cudaMemcpy(r.lat_ns.data(), lat.p, iters * 8, cudaMemcpyDeviceToHost));
+    KIWI_CUDA_CHECK(cudaMemcpy(c32.data(), cyc.p, iters * 4, cudaMemcpyDeviceToHost));
+    KIWI_CUDA_CHECK(cudaMemcpy(tot, totals.p, sizeof(tot), cudaMemcpyDeviceToHost));
+    KIWI_CUDA_CHECK(cudaMemcpy(stv, status.p, sizeof(stv), cudaMemcpyDeviceToHost));
+    r.lat_cycles.assign(c32.begin(), c32.end());
+    r.total_ns = tot[0];
+    r.total_cycles = tot[1];
+    r.status = stv[0];
+    r.ok = stv[0] == 0 && stv[1] == 1;
+    return r;
+}
+
+// ---------------------------------------------------------------------------
+// Device-to-host push correctness
+// ---------------------------------------------------------------------------
+
+enum PushMode : int { kModeGlobal = 0, kModeLanes = 1, kModeReg = 2, kModeLaneMasked = 3 };
+
+struct LaneMsg {
+    uint64_t w[8];
+};
+
+template <uint32_t S>
+struct RegMsg {
+    uint8_t b[S];
+};
+
+KIWI_DEV void fill_words(uint64_t* dst, uint64_t seed, uint64_t msg, uint32_t nwords) {
+    for (uint32_t k = ptx::lane_id(); k < nwords; k += 32) dst[k] = pattern_word(seed, msg, k);
+}
+
+/// Message id of warp w, sequence s: unique across warps.
+KIWI_HD uint64_t msg_id(uint32_t w, uint64_t s) { return (static_cast<uint64_t>(w) << 32) | s; }
+
+template <typename H, int MODE, uint32_t REG_BYTES>
+__global__ void __launch_bounds__(128) d2h_push_kernel(H* handles, uint32_t msgs, const uint32_t* sizes,
+                                                       uint32_t nsizes, uint64_t seed,
+                                                       uint64_t seq_base, uint64_t* scratch) {
+    const uint32_t warp = (blockIdx.x * blockDim.x + threadIdx.x) / 32;
+    const uint32_t lane = ptx::lane_id();
+    H h = handles[std::is_same<H, SpscD2HHandle>::value ? 0 : 0];
+    uint64_t* buf = scratch + static_cast<uint64_t>(warp) * (kMaxMessageBytes / 8 + 1);
+    for (uint32_t i = 0; i < msgs; ++i) {
+        const uint64_t seq = seq_base + i;
+        const uint64_t id = msg_id(warp, seq);
+        const uint32_t meta = (warp << 20) | static_cast<uint32_t>(seq & 0xfffff);
+        if constexpr (MODE == kModeGlobal) {
+            const uint32_t bytes = sizes[seq % nsizes];
+            fill_words(buf, seed, id, (bytes + 7) / 8);
+            __syncwarp();
+            while (!h.push_global(buf, bytes, meta)) {
+            }
+            __syncwarp();
+        } else if constexpr (MODE == kModeLanes) {
+            const uint32_t bytes = sizes[seq % nsizes];
+            const uint64_t w = pattern_word(seed, id, lane);
+            while (!h.push_lanes(w, bytes, meta)) {
+            }
+        } else if constexpr (MODE == kModeReg) {
+            RegMsg<REG_BYTES> m;
+            for (uint32_t k = 0; k < REG_BYTES; ++k) {
+                m.b[k] = static_cast<uint8_t>(pattern_word(seed, id, k / 8) >> (8 * (k % 8)));
+            }
+            while (!h.push_reg(m, meta)) {
+            }
+        } else {
+            // Each lane pushes its own message; lane-specific id and size.
+            const uint64_t lid = msg_id(warp, seq * 32 + lane);
+            const bool active = ((seq * 7 + lane * 3) % 5) != 0;
+            const uint32_t bytes = static_cast<uint32_t>(8 + (seq * 13 + lane * 11) % 57);
+            LaneMsg m;
+#pragma unroll
+            for (uint32_t k = 0; k < 8; ++k) m.w[k] = pattern_word(seed, lid, k);
+            const uint32_t lmeta = (warp << 20) | static_cast<uint32_t>((seq * 32 + lane) & 0xfffff);
+            while (!h.push_lane_masked(m, bytes, lmeta, active)) {
+            }
+        }
+    }
+    if constexpr (std::is_same<H, SpscD2HHandle>::value) {
+        if (lane == 0 && warp == 0) handles[0] = h;
+    }
+}
+
+template <typename H, int MODE, uint32_t REG_BYTES>
+static void launch_push(H* d_handle, uint32_t warps, uint32_t msgs, const uint32_t* d_sizes,
+                        uint32_t nsizes, uint64_t seed, uint64_t seq_base, uint64_t* scratch,
+                        cudaStream_t stream) {
+    const uint32_t threads = warps >= 4 ? 128 : 32 * warps;
+    const uint32_t blocks = (warps * 32 + threads - 1) / threads;
+    d2h_push_kernel<H, MODE, REG_BYTES><<<blocks, threads, 0, stream>>>(d_handle, msgs, d_sizes, nsizes,
+                                                                        seed, seq_base, scratch);
+    KIWI_CUDA_CHECK(cudaGetLastError());
+}
+
+template <typename H>
+static void launch_mode(int mode, uint32_t reg_bytes, H* d_handle, uint32_t warps, uint32_t msgs,
+                        const uint32_t* d_sizes, uint32_t nsizes, uint64_t seed, uint64_t seq_base,
+                        uint64_t* scratch, cudaStream_t stream) {
+    switch (mode) {
+        case kModeGlobal:
+            launch_push<H, kModeGlobal, 8>(d_handle, warps, msgs, d_sizes, nsizes, seed, seq_base, scratch, stream);
+            break;
+        case kModeLanes:
+            launch_push<H, kModeLanes, 8>(d_handle, warps, msgs, d_sizes, nsizes, seed, seq_base, scratch, stream);
+            break;
+        case kModeLaneMasked:
+            launch_push<H, kModeLaneMasked, 8>(d_handle, warps, msgs, d_sizes, nsizes, seed, seq_base, scratch, stream);
+            break;
+        case kModeReg:
+            switch (reg_bytes) {
+                case 8: launch_push<H, kModeReg, 8>(d_handle, warps, msgs, d_sizes, nsizes, seed, seq_base, scratch, stream); break;
+                case 20: launch_push<H, kModeReg, 20>(d_handle, warps, msgs, d_sizes, nsizes, seed, seq_base, scratch, stream); break;
+                case 56: launch_push<H, kModeReg, 56>(d_handle, warps, msgs, d_sizes, nsizes, seed, seq_base, scratch, stream); break;
+                case 200: launch_push<H, kModeReg, 200>(d_handle, warps, msgs, d_sizes, nsizes, seed, seq_base, scratch, stream); break;
+                case 512: launch_push<H, kModeReg, 512>(d_handle, warps, msgs, d_sizes, nsizes, seed, seq_base, scratch, stream); break;
+                default: throw kiwi::error("d2h_push_test: reg mode sizes are 8, 20, 56, 200, 512");
+            }
+            break;
+        default: throw kiwi::error("d2h_push_test: unknown mode");
+    }
+}
+
+static bool check_payload(const uint8_t* got, uint32_t bytes, uint64_t seed, uint64_t id) {
+    for (uint32_t k = 0; k < bytes; ++k) {
+        const uint8_t want = static_cast<uint8_t>(pattern_word(seed, id, k / 8) >> (8 * (k % 8)));
+        if (got[k] != want) return false;
+    }
+    return true;
+}
+
+PushTestResult d2h_push_test(const std::string& mode_name, bool mpsc, uint64_t capacity,
+                             uint32_t warps, uint32_t msgs_per_warp,
+                             const std::vector<uint32_t>& sizes_in, uint32_t launches,
+                             uint64_t seed) {
+    int mode = kModeGlobal;
+    if (mode_name == "global") mode = kModeGlobal;
+    else if (mode_name == "lanes") mode = kModeLanes;
+    else if (mode_name == "reg") mode = kModeReg;
+    else if (mode_name == "lane_masked") mode = kModeLaneMasked;
+    else throw kiwi::error("d2h_push_test: mode must be global, lanes, reg or lane_masked");
+    if (!mpsc && warps != 1) throw kiwi::error("d2h_push_test: SPSC takes exactly one producer warp");
+    std::vector<uint32_t> sizes = sizes_in.empty() ? std::vector<uint32_t>{8} : sizes_in;
+    const uint32_t reg_bytes = sizes[0];
+    if (mode == kModeReg) sizes = {reg_bytes};
+
+    std::unique_ptr<SPSCD2HQueue> sq;
+    std::unique_ptr<MPSCD2HQueue> mq;
+    D2HRingBase* base = nullptr;
+    if (mpsc) {
+        mq = std::make_unique<MPSCD2HQueue>(capacity, MemKind::kMappedPinned);
+        base = mq.get();
+    } else {
+        sq = std::make_unique<SPSCD2HQueue>(capacity, MemKind::kMappedPinned);
+        base = sq.get();
+    }
+    DevBuf<uint32_t> d_sizes(sizes.size());
+    KIWI_CUDA_CHECK(cudaMemcpy(d_sizes.p, sizes.data(), sizes.size() * 4, cudaMemcpyHostToDevice));
+    DevBuf<uint64_t> scratch(static_cast<size_t>(warps) * (kMaxMessageBytes / 8 + 1));
+    DevBuf<uint8_t> d_handle(sizeof(MpscD2HHandle) > sizeof(SpscD2HHandle) ? sizeof(MpscD2HHandle)
+                                                                            : sizeof(SpscD2HHandle));
+    if (mpsc) {
+        auto h = mq->device_handle();
+        KIWI_CUDA_CHECK(cudaMemcpy(d_handle.p, &h, sizeof(h), cudaMemcpyHostToDevice));
+    } else {
+        auto h = sq->device_handle();
+        KIWI_CUDA_CHECK(cudaMemcpy(d_handle.p, &h, sizeof(h), cudaMemcpyHostToDevice));
+    }
+    cudaStream_t stream;
+    KIWI_CUDA_CHECK(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking));
+
+    PushTestResult res;
+    std::vector<uint64_t> next(warps, 0);
+    alignas(64) uint8_t buf[kMaxMessageBytes];
+    auto note = [&](const std::string& s) {
+        if (res.first_error.empty()) res.first_error = s;
+    };
+    for (uint32_t l = 0; l < launches; ++l) {
+        const uint64_t seq_base = static_cast<uint64_t>(l) * msgs_per_warp;
+        if (mpsc) {
+            launch_mode<MpscD2HHandle>(mode, reg_bytes, reinterpret_cast<MpscD2HHandle*>(d_handle.p), warps,
+                                       msgs_per_warp, d_sizes.p, static_cast<uint32_t>(sizes.size()), seed,
+                                       seq_base, scratch.p, stream);
+        } else {
+            launch_mode<SpscD2HHandle>(mode, reg_bytes, reinterpret_cast<SpscD2HHandle*>(d_handle.p), warps,
+                                       msgs_per_warp, d_sizes.p, static_cast<uint32_t>(sizes.size()), seed,
+                                       seq_base, scratch.p, stream);
+        }
+        // Expected messages this launch.
+        uint64_t expected = 0;
+        std::vector<std::vector<uint64_t>> plan(warps);  // lane-masked: per-warp list of (seq*32+lane)
+        if (mode == kModeLaneMasked) {
+            for (uint32_t w = 0; w < warps; ++w) {
+                for (uint64_t s = seq_base; s < seq_base + msgs_per_warp; ++s) {
+                    for (uint32_t ln = 0; ln < 32; ++ln) {
+                        if (((s * 7 + ln * 3) % 5) != 0) plan[w].push_back(s * 32 + ln);
+                    }
+                }
+                expected += plan[w].size();
+            }
+            std::fill(next.begin(), next.end(), 0);
+        } else {
+            expected = static_cast<uint64_t>(warps) * msgs_per_warp;
+        }
+        uint64_t got = 0;
+        uint64_t idle = 0;
+        while (got < expected) {
+            uint32_t meta = 0, bytes = 0;
+            if (!base->try_pop(buf, &meta, &bytes)) {
+                if ((++idle & 0xffff) == 0) {
+                    const cudaError_t q = cudaStreamQuery(stream);
+                    if (q != cudaErrorNotReady) {
+                        // Kernel finished; drain what is left then stop.
+                        while (base->try_pop(buf, &meta, &bytes)) {
+                            ++got;
+                        }
+                        if (got < expected) note("kernel finished with messages missing");
+                        break;
+                    }
+                }
+                continue;
+            }
+            ++got;
+            const uint32_t w = meta >> 20;
+            if (w >= warps) {
+                ++res.mismatches;
+                note("bad warp id in metadata");
+                continue;
+            }
+            if (mode == kModeLaneMasked) {
+                if (next[w] >= plan[w].size()) {
+                    ++res.order_errors;
+                    continue;
+                }
+                const uint64_t lseq = plan[w][next[w]++];
+                if ((meta & 0xfffff) != (lseq & 0xfffff)) {
+                    ++res.order_errors;
+                    note("lane-masked order");
+                    continue;
+                }
+                const uint64_t s = lseq / 32;
+                const uint32_t ln = static_cast<uint32_t>(lseq % 32);
+                const uint32_t want_bytes = static_cast<uint32_t>(8 + (s * 13 + ln * 11) % 57);
+                if (bytes != want_bytes || !check_payload(buf, bytes, seed, msg_id(w, lseq))) {
+                    ++res.mismatches;
+                    note("lane-masked payload");
+                }
+            } else {
+                const uint64_t s = seq_base + next[w];
+                if ((meta & 0xfffff) != (s & 0xfffff)) {
+                    ++res.order_errors;
+                    note("order: warp " + std::to_string(w));
+                }
+                ++next[w];
+                const uint32_t want_bytes = sizes[s % sizes.size()];
+                if (bytes != want_bytes || !check_payload(buf, bytes, seed, msg_id(w, s))) {
+                    ++res.mismatches;
+                    note("payload: warp " + std::to_string(w) + " seq " + std::to_string(s) +
+                         " bytes " + std::to_string(bytes));
+                }
+            }
+        }
+        res.popped += got;
+        KIWI_CUDA_CHECK(cudaStreamSynchronize(stream));
+        if (mode != kModeLaneMasked) std::fill(next.begin(), next.end(), 0);
+    }
+    cudaStreamDestroy(stream);
+    res.device_error = base->error().code;
+    return res;
+}
+
+// ---------------------------------------------------------------------------
+// Host-to-device SPSC
+// ---------------------------------------------------------------------------
+
+__global__ void h2d_spsc_kernel(SpscH2DHandle h, uint32_t count, bool registers, uint64_t* out,
+                                uint32_t* lens, uint32_t* metas, uint32_t* status, uint64_t timeout_ns) {
+    const uint32_t lane = ptx::lane_id();
+    for (uint32_t i = 0; i < count; ++i) {
+        uint64_t* dst = out + static_cast<uint64_t>(i) * (kMaxMessageBytes / 8);
+        uint32_t bytes = 0, meta = 0;
+        ptx::Deadline dl(timeout_ns);
+        if (registers) {
+            uint64_t w;
+            while (!h.try_pop(w, bytes, meta)) {
+                if (dl.expired()) {
+                    status[0] = static_cast<uint32_t>(Status::kTimeout);
+                    h.flush_consumer_index();
+                    return;
+                }
+            }
+            if (lane < (bytes + 7) / 8) dst[lane] = w;
+        } else {
+            while (!h.try_pop_to(dst, bytes, meta)) {
+                if (dl.expired()) {
+                    status[0] = static_cast<uint32_t>(Status::kTimeout);
+                    h.flush_consumer_index();
+                    return;
+                }
+            }
+        }
+        if (lane == 0) {
+            lens[i] = bytes;
+            metas[i] = meta;
+        }
+    }
+    h.flush_consumer_index();
+}
+
+PushTestResult h2d_spsc_test(uint64_t capacity, uint32_t count, const std::vector<uint32_t>& sizes_in,
+                             bool registers, uint32_t notify_interval, uint64_t seed) {
+    std::vector<uint32_t> sizes = sizes_in.empty() ? std::vector<uint32_t>{8} : sizes_in;
+    for (uint32_t s : sizes) {
+        if (registers && s > 248) throw kiwi::error("h2d_spsc_test: register pops hold <= 248 bytes");
+    }
+    SPSCH2DQueue q(capacity, MemKind::kMappedPinned, notify_interval);
+    DevBuf<uint64_t> out(static_cast<size_t>(count) * (kMaxMessageBytes / 8));
+    DevBuf<uint32_t> lens(count), metas(count), status(1);
+    cudaStream_t stream;
+    KIWI_CUDA_CHECK(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking));
+    h2d_spsc_kernel<<<1, 32, 0, stream>>>(q.device_handle(), count, registers, out.p, lens.p, metas.p,
+                                          status.p, 2000000000ull);
+    KIWI_CUDA_CHECK(cudaGetLastError());
+    std::vector<uint8_t> msg(kMaxMessageBytes);
+    uint64_t spins = 0;
+    bool gave_up = false;
+    for (uint32_t i = 0; i < count && !gave_up; ++i) {
+        const uint32_t bytes = sizes[i % sizes.size()];
+        for (uint32_t k = 0; k < bytes; ++k) msg[k] = static_cast<uint8_t>(pattern_word(seed, i, k / 8) >> (8 * (k % 8)));
+        while (!q.try_push(msg.data(), bytes, i)) {
+            host::cpu_relax();
+            if ((++spins & 0xfffff) == 0 && cudaStreamQuery(stream) != cudaErrorNotReady) {
+                gave_up = true;
+                break;
+            }
+        }
+    }
+    KIWI_CUDA_CHECK(cudaStreamSynchronize(stream));
+    cudaStreamDestroy(stream);
+    PushTestResult res;
+    std::vector<uint64_t> h_out(static_cast<size_t>(count) * (kMaxMessageBytes / 8));
+    std::vector<uint32_t> h_lens(count), h_metas(count);
+    uint32_t st = 0;
+    KIWI_CUDA_CHECK(cudaMemcpy(h_out.data(), out.p, h_out.size() * 8, cudaMemcpyDeviceToHost));
+    KIWI_CUDA_CHECK(cudaMemcpy(h_lens.data(), lens.p, count * 4, cudaMemcpyDeviceToHost));
+    KIWI_CUDA_CHECK(cudaMemcpy(h_metas.data(), metas.p, count * 4, cudaMemcpyDeviceToHost));
+    KIWI_CUDA_CHECK(cudaMemcpy(&st, status.p, 4, cudaMemcpyDeviceToHost));
+    res.device_error = st;
+    for (uint32_t i = 0; i < count; ++i) {
+        const uint32_t bytes = sizes[i % sizes.size()];
+        const uint8_t* got = reinterpret_cast<const uint8_t*>(&h_out[static_cast<size_t>(i) * (kMaxMessageBytes / 8)]);
+        if (h_lens[i] != bytes || h_metas[i] != i || !check_payload(got, bytes, seed, i)) {
+            ++res.mismatches;
+            if (res.first_error.empty()) res.first_error = "message " + std::to_string(i);
+        } else {
+            ++res.popped;
+        }
+    }
+    if (q.consumer_position() != q.producer_position()) {
+        if (res.first_error.empty()) res.first_error = "consumer position not flushed";
+        ++res.mismatches;
+    }
+    return res;
+}
+
+// ---------------------------------------------------------------------------
+// Host-to-device MPMC
+// ---------------------------------------------------------------------------
+
+__global__ void h2d_mpmc_kernel(MpmcH2DHandle h, uint64_t total, unsigned long long* consumed,
+                                unsigned long long* out_count, uint64_t* out_words, uint32_t* out_meta,
+                                uint32_t* out_len, uint32_t* status, uint64_t timeout_ns) {
+    const uint32_t lane = ptx::lane_id();
+    ptx::Deadline dl(timeout_ns);
+    while (true) {
+        uint64_t done = 0;
+        if (lane == 0) done = ptx::ld_volatile_u64(consumed);
+        done = ptx::bcast64(done);
+        if (done >= total) return;
+        uint64_t w;
+        uint32_t bytes, meta;
+        if (h.try_pop(w, bytes, meta)) {
+            unsigned long long idx = 0;
+            if (lane == 0) idx = atomicAdd(out_count, 1ull);
+            idx = ptx::bcast64(idx);
+            if (idx < total) {
+                if (lane < 7) out_words[idx * 7 + lane] = w;
+                if (lane == 0) {
+                    out_meta[idx] = meta;
+                    out_len[idx] = bytes;
+                    atomicAdd(consumed, 1ull);
+                }
+            }
+            dl = ptx::Deadline(timeout_ns);
+        } else if (dl.expired()) {
+            if (lane == 0) status[0] = static_cast<uint32_t>(Status::kTimeout);
+            return;
+        }
+    }
+}
+
+PushTestResult h2d_mpmc_test(uint64_t slots, uint32_t slot_lines, uint32_t producers,
+                             uint32_t msgs_per_producer, uint32_t warps, uint64_t seed) {
+    MPMCH2DQueue q(slots, slot_lines, MemKind::kMappedPinned);
+    const uint32_t payload = q.slot_payload_bytes() < 56 ? q.slot_payload_bytes() : 56;
+    const uint64_t total = static_cast<uint64_t>(producers) * msgs_per_producer;
+    DevBuf<unsigned long long> consumed(1), out_count(1);
+    DevBuf<uint64_t> out_words(total * 7);
+    DevBuf<uint32_t> out_meta(total), out_len(total), status(1);
+    cudaStream_t stream;
+    KIWI_CUDA_CHECK(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking));
+    const uint32_t threads = warps >= 4 ? 128 : 32 * warps;
+    const uint32_t blocks = (warps * 32 + threads - 1) / threads;
+    h2d_mpmc_kernel<<<blocks, threads, 0, stream>>>(q.device_handle(), total, consumed.p, out_count.p,
+                                                    out_words.p, out_meta.p, out_len.p, status.p,
+                                                    2000000000ull);
+    KIWI_CUDA_CHECK(cudaGetLastError());
+    std::atomic<bool> stop{false};
+    std::vector<std::thread> th;
+    for (uint32_t p = 0; p < producers; ++p) {
+        th.emplace_back([&, p] {
+            uint8_t msg[64];
+            for (uint32_t i = 0; i < msgs_per_producer && !stop; ++i) {
+                const uint64_t id = (static_cast<uint64_t>(p) << 32) | i;
+                for (uint32_t k = 0; k < payload; ++k) msg[k] = static_cast<uint8_t>(pattern_word(seed, id, k / 8) >> (8 * (k % 8)));
+                while (!q.try_push(msg, payload, (p << 20) | i)) {
+                    if (stop) return;
+                    host::cpu_relax();
+                }
+            }
+        });
+    }
+    // Watchdog: if the kernel ends early (timeout), release the producers.
+    while (cudaStreamQuery(stream) == cudaErrorNotReady) std::this_thread::sleep_for(std::chrono::microseconds(50));
+    stop = true;
+    for (auto& t : th) t.join();
+    KIWI_CUDA_CHECK(cudaStreamSynchronize(stream));
+    cudaStreamDestroy(stream);
+    PushTestResult res;
+    std::vector<uint64_t> words(total * 7);
+    std::vector<uint32_t> meta(total), len(total);
+    uint32_t st = 0;
+    unsigned long long cnt = 0;
+    KIWI_CUDA_CHECK(cudaMemcpy(words.data(), out_words.p, words.size() * 8, cudaMemcpyDeviceToHost));
+    KIWI_CUDA_CHECK(cudaMemcpy(meta.data(), out_meta.p, total * 4, cudaMemcpyDeviceToHost));
+    KIWI_CUDA_CHECK(cudaMemcpy(len.data(), out_len.p, total * 4, cudaMemcpyDeviceToHost));
+    KIWI_CUDA_CHECK(cudaMemcpy(&st, status.p, 4, cudaMemcpyDeviceToHost));
+    KIWI_CUDA_CHECK(cudaMemcpy(&cnt, out_count.p, 8, cudaMemcpyDeviceToHost));
+    res.device_error = st;
+    std::vector<uint8_t> seen(total, 0);
+    for (uint64_t i = 0; i < cnt && i < total; ++i) {
+        const uint32_t p = meta[i] >> 20, s = meta[i] & 0xfffff;
+        if (p >= producers || s >= msgs_per_producer) {
+            ++res.mismatches;
+            continue;
+        }
+        const uint64_t flat = static_cast<uint64_t>(p) * msgs_per_producer + s;
+        if (seen[flat]++) ++res.order_errors;  // duplicate
+        const uint64_t id = (static_cast<uint64_t>(p) << 32) | s;
+        if (len[i] != payload || !check_payload(reinterpret_cast<const uint8_t*>(&words[i * 7]), payload, seed, id)) {
+            ++res.mismatches;
+        }
+        ++res.popped;
+    }
+    if (res.popped != total && res.first_error.empty()) res.first_error = "missing messages";
+    return res;
+}
+
+__global__ void h2d_timeout_kernel(SpscH2DHandle h, uint64_t timeout_ns, uint32_t* status) {
+    uint64_t w;
+    uint32_t b, m;
+    const Status s = h.pop(w, b, m, timeout_ns);
+    if (ptx::lane_id() == 0) status[0] = static_cast<uint32_t>(s);
+}
+
+uint32_t h2d_timeout_test(uint64_t timeout_ns) {
+    SPSCH2DQueue q(16, MemKind::kMappedPinned);
+    DevBuf<uint32_t> status(1);
+    h2d_timeout_kernel<<<1, 32>>>(q.device_handle(), timeout_ns, status.p);
+    KIWI_CUDA_CHECK(cudaGetLastError());
+    KIWI_CUDA_CHECK(cudaDeviceSynchronize());
+    uint32_t st = 0;
+    KIWI_CUDA_CHECK(cudaMemcpy(&st, status.p, 4, cudaMemcpyDeviceToHost));
+    const ErrorRecord e = q.error();
+    if (st == static_cast<uint32_t>(Status::kTimeout) && e.code != st) return 0xffffffffu;  // not recorded
+    return st;
+}
+
+std::vector<KernelAttr> queue_kernel_attributes() {
+    std::vector<KernelAttr> out;
+    auto add = [&](const char* name, const void* fn) {
+        cudaFuncAttributes a{};
+        KIWI_CUDA_CHECK(cudaFuncGetAttributes(&a, fn));
+        out.push_back({name, static_cast<int>(a.localSizeBytes), a.numRegs});
+    };
+    add("invoke_rtt<SPSC>", reinterpret_cast<const void*>(&invoke_rtt_kernel<SPSCD2HQueue>));
+    add("invoke_rtt<MPSC>", reinterpret_cast<const void*>(&invoke_rtt_kernel<MPSCD2HQueue>));
+    add("push_global<SPSC>", reinterpret_cast<const void*>(&d2h_push_kernel<SpscD2HHandle, kModeGlobal, 8>));
+    add("push_lanes<SPSC>", reinterpret_cast<const void*>(&d2h_push_kernel<SpscD2HHandle, kModeLanes, 8>));
+    add("push_reg56<SPSC>", reinterpret_cast<const void*>(&d2h_push_kernel<SpscD2HHandle, kModeReg, 56>));
+    add("push_reg200<SPSC>", reinterpret_cast<const void*>(&d2h_push_kernel<SpscD2HHandle, kModeReg, 200>));
+    add("push_global<MPSC>", reinterpret_cast<const void*>(&d2h_push_kernel<MpscD2HHandle, kModeGlobal, 8>));
+    add("push_lanes<MPSC>", reinterpret_cast<const void*>(&d2h_push_kernel<MpscD2HHandle, kModeLanes, 8>));
+    add("h2d_spsc_pop", reinterpret_cast<const void*>(&h2d_spsc_kernel));
+    add("h2d_mpmc_pop", reinterpret_cast<const void*>(&h2d_mpmc_kernel));
+    return out;
+}
+
+}  // namespace kiwi::bench

@@ -1,0 +1,78 @@
+// GPU queue / invoke benchmarks and correctness drivers (host API, no torch).
+// Each function launches its kernel, runs the host side of the protocol on the
+// calling thread, synchronises, and returns what it measured or received.
+#pragma once
+
+#include <cstdint>
+#include <string>
+#include <vector>
+
+namespace kiwi::bench {
+
+struct RttConfig {
+    uint64_t iters = 100000;
+    uint64_t warmup = 10000;
+    uint32_t payload_bytes = 8;    // request payload (8 B .. 4 KB)
+    uint64_t seed = 1;
+    int cpu = -1;                  // host thread core (-1: GPU-local core chosen by caller)
+    uint64_t capacity = 4096;      // request ring lines
+    bool mpsc = false;             // use the MPSC request queue
+    uint32_t poll_warps = 1;       // warps polling the reply line (staggered)
+    uint64_t timeout_ns = 2000000000ull;
+};
+
+struct RttResult {
+    std::vector<uint64_t> lat_ns;      // per iteration, %globaltimer
+    std::vector<uint64_t> lat_cycles;  // per iteration, %clock64
+    uint64_t total_ns = 0;             // whole timed loop, %globaltimer
+    uint64_t total_cycles = 0;
+    uint64_t callbacks = 0;
+    uint32_t status = 0;               // kiwi::Status of the device loop
+    bool ok = false;                   // every reply matched payload + 1
+};
+
+/// GPU -> CPU -> GPU invoke round trip: the kernel invokes a host callback with
+/// a seeded payload, the callback replies payload + 1 through an H2D ring.
+RttResult invoke_rtt(const RttConfig& cfg);
+
+/// Raw floor: the GPU stores a counter to host memory and polls a host word
+/// the CPU sets in reply.  No queue logic.
+RttResult pcie_floor(uint64_t iters, uint64_t warmup, int cpu, uint64_t timeout_ns);
+
+struct PushTestResult {
+    uint64_t popped = 0;
+    uint64_t mismatches = 0;     // payload / length / metadata errors
+    uint64_t order_errors = 0;   // per-warp sequence errors
+    uint32_t device_error = 0;   // ErrorRecord code
+    std::string first_error;
+};
+
+/// Device-to-host push paths.  mode: "global", "lanes", "reg", "lane_masked".
+/// sizes: the message sizes to cycle through.  launches > 1 re-launches with the
+/// saved SPSC handle.  For MPSC, `warps` producer warps push concurrently.
+PushTestResult d2h_push_test(const std::string& mode, bool mpsc, uint64_t capacity,
+                             uint32_t warps, uint32_t msgs_per_warp,
+                             const std::vector<uint32_t>& sizes, uint32_t launches,
+                             uint64_t seed);
+
+/// Host-to-device SPSC: the host pushes `count` messages of the given sizes
+/// while one warp pops them into device memory; returns mismatches.
+PushTestResult h2d_spsc_test(uint64_t capacity, uint32_t count, const std::vector<uint32_t>& sizes,
+                             bool registers, uint32_t notify_interval, uint64_t seed);
+
+/// Host-to-device MPMC: `producers` host threads push, `warps` warps pop.
+PushTestResult h2d_mpmc_test(uint64_t slots, uint32_t slot_lines, uint32_t producers,
+                             uint32_t msgs_per_producer, uint32_t warps, uint64_t seed);
+
+/// A device wait that nothing satisfies must return kTimeout (not hang).
+uint32_t h2d_timeout_test(uint64_t timeout_ns);
+
+struct KernelAttr {
+    std::string name;
+    int local_bytes;
+    int registers;
+};
+/// Local-memory use of the queue hot-path kernels (must be 0: register resident).
+std::vector<KernelAttr> queue_kernel_attributes();
+
+}  // namespace kiwi::bench

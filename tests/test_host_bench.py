@@ -1,0 +1,28 @@
+"""Host-only ring benchmark, small sizes: checks order and checksum."""
+import numpy as np
+
+import kiwi_b200
+
+
+def test_pingpong_small():
+    C = kiwi_b200.native()
+    r = C.bench.host_ring_pingpong(20000, 1000, 4096, 8, 0, -1, -1)
+    assert r["ok"]
+    lat = r["latencies_ns"]
+    assert len(lat) == 20000 and np.all(lat > 0)
+
+
+def test_stream_small_and_large_payload():
+    C = kiwi_b200.native()
+    assert C.bench.host_ring_stream(50000, 4096, 8, 3, -1, -1)["ok"]
+    assert C.bench.host_ring_stream(2000, 256, 4096, 3, -1, -1)["ok"]
+
+
+def test_xorshift_reference_values():
+    C = kiwi_b200.native()
+    # Marsaglia xorshift64 (13, 7, 17) from state 1.
+    s = 1
+    s ^= (s << 13) & (2**64 - 1)
+    s ^= s >> 7
+    s ^= (s << 17) & (2**64 - 1)
+    assert C.bench.xorshift64(1) == s

@@ -1,0 +1,122 @@
+"""kiwi::invoke on the host: registry, serialisation, dispatch, progress
+threads.  Messages are enqueued by a CPU stand-in for the device
+(reference: tests/invoke/test_invoke_basic.hip.cpp of AMDResearch/kiwi)."""
+import struct
+import threading
+import time
+
+import pytest
+
+from kiwi_b200 import invoke
+
+
+def test_typed_callback_dispatch():
+    ctx = invoke.Context(num_endpoints=2, capacity=64, host_only=True)
+    got = []
+    cb = ctx.register_callback(lambda a, b, c: got.append((a, b, c)), "<Qif")
+    assert cb == 0
+    ctx.emulate_invoke(1, cb, struct.pack("<Qif", 7, -3, 1.5))
+    ctx.emulate_invoke(1, cb, struct.pack("<Qif", 8, 4, 2.5))
+    assert ctx.progress(0) == 0
+    assert ctx.progress(1) == 2
+    assert got == [(7, -3, 1.5), (8, 4, 2.5)]
+
+
+def test_raw_callback_any_size_and_order():
+    ctx = invoke.Context(1, 256, host_only=True)
+    seen = []
+    cb = ctx.register_callback(lambda p: seen.append(p))
+    msgs = [bytes([i % 256]) * i for i in range(0, 300, 7)]
+    for m in msgs:
+        ctx.emulate_invoke(0, cb, m)
+    assert ctx.progress(0, max_callbacks=3) == 3
+    ctx.progress(0)
+    assert seen == msgs
+
+
+def test_size_mismatch_raises():
+    ctx = invoke.Context(1, 16, host_only=True)
+    cb = ctx.register_callback(lambda a: None, "<Q")
+    ctx.emulate_invoke(0, cb, b"1234")
+    with pytest.raises(Exception, match="expects 8"):
+        ctx.progress(0)
+
+
+def test_unregistered_id_raises():
+    ctx = invoke.Context(1, 16, host_only=True)
+    ctx.emulate_invoke(0, 5, b"")
+    with pytest.raises(Exception, match="unregistered"):
+        ctx.progress(0)
+
+
+def test_registry_limit_256():
+    ctx = invoke.Context(1, 16, host_only=True)
+    for i in range(invoke.MAX_CALLBACKS):
+        assert ctx.register_callback(lambda p: None) == i
+    with pytest.raises(Exception, match="full"):
+        ctx.register_callback(lambda p: None)
+
+
+def test_register_rejects_args_the_ring_cannot_hold():
+    ctx = invoke.Context(1, 1, host_only=True)
+    ctx.register_callback(lambda *a: None, "<3Q")  # 24 B: one line
+    with pytest.raises(Exception, match="capacity"):
+        ctx.register_callback(lambda *a: None, "<4Q")  # 32 B: two lines
+
+
+def test_callback_exception_propagates():
+    ctx = invoke.Context(1, 16, host_only=True)
+
+    def boom(p):
+        raise ValueError("boom")
+
+    cb = ctx.register_callback(boom)
+    ctx.emulate_invoke(0, cb, b"x")
+    with pytest.raises(ValueError, match="boom"):
+        ctx.progress(0)
+
+
+def test_progress_threads_run_callbacks():
+    ctx = invoke.Context(num_endpoints=4, capacity=64, host_only=True)
+    lock = threading.Lock()
+    seen = []
+
+    def f(ep, i):
+        with lock:
+            seen.append((ep, i))
+
+    cb = ctx.register_callback(f, "<II")
+    ctx.start(num_threads=2)
+    for i in range(50):
+        for ep in range(4):
+            while True:
+                try:
+                    ctx.emulate_invoke(ep, cb, struct.pack("<II", ep, i))
+                    break
+                except Exception:
+                    time.sleep(0.001)
+    deadline = time.time() + 10
+    while len(seen) < 200 and time.time() < deadline:
+        time.sleep(0.01)
+    ctx.stop()
+    assert len(seen) == 200
+    for ep in range(4):
+        assert [i for e, i in seen if e == ep] == list(range(50))
+
+
+def test_progress_thread_error_surfaces():
+    ctx = invoke.Context(1, 16, host_only=True)
+    cb = ctx.register_callback(lambda p: 1 / 0)
+    ctx.start(1)
+    ctx.emulate_invoke(0, cb, b"")
+    time.sleep(0.2)
+    with pytest.raises(ZeroDivisionError):
+        ctx.stop()
+
+
+def test_mpsc_context_host_only():
+    ctx = invoke.Context(1, 32, mpsc=True, host_only=True)
+    got = []
+    cb = ctx.register_callback(lambda v: got.append(v), "<d")
+    ctx.emulate_invoke(0, cb, struct.pack("<d", 3.25))
+    assert ctx.progress(0) == 1 and got == [3.25]
