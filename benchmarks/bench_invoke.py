@@ -48,21 +48,25 @@ def main():
     ap.add_argument("--iters", type=int, default=1_000_000)
     ap.add_argument("--warmup", type=int, default=10_000)
     ap.add_argument("--sweep", action="store_true", help="payload sweep 8 B .. 4 KB")
-    ap.add_argument("--poll-warps", type=int, nargs="*", default=[0, 2, 4])
+    ap.add_argument("--poll-warps", type=int, nargs="*", default=[0, 2])
+    ap.add_argument("--stagger", type=int, nargs="*", default=[150, 200, 250, 300])
     ap.add_argument("--cpu", type=int, default=-1)
     args = ap.parse_args()
     C = kiwi_b200.native()
     summarize("pcie_floor", C.bench.pcie_floor(args.iters, args.warmup, args.cpu))
+    for st in args.stagger:
+        r = C.bench.invoke_rtt(args.iters, args.warmup, 8, 1, args.cpu, 4096, False, 0, 2_000_000_000, True, st)
+        summarize("invoke_rtt", r, {"payload_bytes": 8, "reply": "mailbox", "stagger_ns": st, "queue": "spsc"})
     for pw in args.poll_warps:
-        r = C.bench.invoke_rtt(args.iters, args.warmup, 8, 1, args.cpu, 4096, False, pw)
-        summarize("invoke_rtt", r, {"payload_bytes": 8, "poll_warps": pw, "queue": "spsc"})
-    r = C.bench.invoke_rtt(args.iters // 4, args.warmup, 8, 1, args.cpu, 4096, True, 0)
-    summarize("invoke_rtt", r, {"payload_bytes": 8, "poll_warps": 0, "queue": "mpsc"})
+        r = C.bench.invoke_rtt(args.iters // 4, args.warmup, 8, 1, args.cpu, 4096, False, pw)
+        summarize("invoke_rtt", r, {"payload_bytes": 8, "reply": "ring", "poll_warps": pw, "queue": "spsc"})
+    r = C.bench.invoke_rtt(args.iters // 4, args.warmup, 8, 1, args.cpu, 4096, True, 0, 2_000_000_000, True, 200)
+    summarize("invoke_rtt", r, {"payload_bytes": 8, "reply": "mailbox", "stagger_ns": 200, "queue": "mpsc"})
     if args.sweep:
         for b in [8, 16, 32, 64, 128, 256, 512, 1024, 2048, 4096]:
             r = C.bench.invoke_rtt(max(args.iters // 20, 1000), args.warmup // 10, b, 1, args.cpu, 4096, False,
-                                   max(args.poll_warps))
-            summarize("invoke_rtt_sweep", r, {"payload_bytes": b, "poll_warps": max(args.poll_warps)})
+                                   2)
+            summarize("invoke_rtt_sweep", r, {"payload_bytes": b, "reply": "ring", "poll_warps": 2})
 
 
 if __name__ == "__main__":

@@ -1,0 +1,267 @@
+// Python bindings of kiwi::ep: the fused expert-parallel MoE layer.
+//
+// Parity: the reference's KiwiEpOp (apps/ep/python/kiwi_ep_bindings.hip.cpp:123-574
+// of AMDResearch/kiwi) binds dispatch/combine of rows only.  MoeLayer binds the
+// whole B200 layer: routing, FP8/NVFP4 dispatch over NVLink, expert-major
+// layout, the two tcgen05 grouped GEMMs (SwiGLU fused into the first, routing
+// weight into the second), combine over NVLink and the final reduction, all
+// enqueued on the current torch stream with no host synchronisation.
+#include <ATen/cuda/CUDAContext.h>
+#include <pybind11/pybind11.h>
+#include <pybind11/stl.h>
+#include <torch/extension.h>
+
+#include "kiwi/ep/config.hpp"
+#include "kiwi/ep/kernels.hpp"
+#include "kiwi/gemm/grouped_gemm.hpp"
+#include "kiwi/p2p/heap.hpp"
+
+namespace py = pybind11;
+using namespace kiwi;
+
+namespace {
+
+cudaStream_t cur_stream() { return at::cuda::getCurrentCUDAStream().stream(); }
+
+ep::EpConfig config_from_dict(const py::dict& d) {
+    ep::EpConfig c{};
+    c.world = d["world"].cast<int>();
+    c.rank = d["rank"].cast<int>();
+    c.hidden = d["hidden"].cast<int>();
+    c.num_experts = d["num_experts"].cast<int>();
+    c.topk = d["topk"].cast<int>();
+    c.max_tokens = d["max_tokens"].cast<int>();
+    const std::string q = d["quant"].cast<std::string>();
+    if (q == "none" || q == "bf16") c.quant = static_cast<int>(ep::Quant::kNone);
+    else if (q == "fp8") c.quant = static_cast<int>(ep::Quant::kFp8);
+    else if (q == "nvfp4" || q == "fp4") c.quant = static_cast<int>(ep::Quant::kNvfp4);
+    else throw kiwi::error("unknown quant format " + q);
+    return ep::finalize(c);
+}
+
+py::dict config_to_dict(const ep::EpConfig& c) {
+    py::dict d;
+    d["world"] = c.world;
+    d["rank"] = c.rank;
+    d["hidden"] = c.hidden;
+    d["num_experts"] = c.num_experts;
+    d["experts_per_rank"] = c.experts_per_rank;
+    d["topk"] = c.topk;
+    d["max_tokens"] = c.max_tokens;
+    d["quant"] = c.quant;
+    d["row_bytes"] = c.row_bytes;
+    d["scale_bytes"] = c.scale_bytes;
+    d["meta_bytes"] = c.meta_bytes;
+    d["off_flags"] = c.off_flags;
+    d["off_meta"] = c.off_meta;
+    d["off_row"] = c.off_row;
+    d["off_scale"] = c.off_scale;
+    d["off_comb"] = c.off_comb;
+    d["heap_bytes"] = c.heap_bytes;
+    d["max_pairs"] = c.max_pairs();
+    d["local_per_token"] = c.local_per_token();
+    return d;
+}
+
+class MoeLayer {
+public:
+    MoeLayer(p2p::SymmetricHeap& heap, const py::dict& cfg, int64_t ffn, torch::Tensor w13, torch::Tensor w2,
+             uint64_t timeout_ns)
+        : heap_(heap), cfg_(config_from_dict(cfg)), ffn_(ffn), w13_(w13), w2_(w2), timeout_ns_(timeout_ns) {
+        TORCH_CHECK(heap.size() >= cfg_.heap_bytes, "symmetric heap too small: need ", cfg_.heap_bytes, " bytes");
+        TORCH_CHECK(heap.rank() == cfg_.rank && heap.world() == cfg_.world, "heap rank/world differ from config");
+        const int64_t el = cfg_.experts_per_rank;
+        TORCH_CHECK(w13.is_cuda() && w13.scalar_type() == torch::kBFloat16 && w13.is_contiguous() &&
+                        w13.dim() == 2 && w13.size(0) == el * 2 * ffn && w13.size(1) == cfg_.hidden,
+                    "w13 must be contiguous bf16 [experts_per_rank * 2 * ffn, hidden] (gate/up interleaved by 128)");
+        TORCH_CHECK(w2.is_cuda() && w2.scalar_type() == torch::kBFloat16 && w2.is_contiguous() && w2.dim() == 2 &&
+                        w2.size(0) == el * cfg_.hidden && w2.size(1) == ffn,
+                    "w2 must be contiguous bf16 [experts_per_rank * hidden, ffn]");
+        TORCH_CHECK((2 * ffn) % 256 == 0 && cfg_.hidden % 256 == 0 && ffn % 64 == 0 && cfg_.hidden % 64 == 0,
+                    "GEMM tiling needs 2*ffn and hidden multiples of 256, ffn of 64");
+        auto dev = w13.device();
+        auto i32 = torch::TensorOptions().dtype(torch::kInt32).device(dev);
+        auto f32 = torch::TensorOptions().dtype(torch::kFloat32).device(dev);
+        auto bf = torch::TensorOptions().dtype(torch::kBFloat16).device(dev);
+        const int64_t pairs = cfg_.max_pairs();
+        epoch_ = torch::zeros({4}, i32);
+        done_ = torch::zeros({4}, i32);
+        counts_ = torch::zeros({el}, i32);
+        cursor_ = torch::zeros({el}, i32);
+        offsets_ = torch::zeros({el + 1}, i32);
+        tiles1_ = torch::zeros({el + 1}, i32);
+        tiles2_ = torch::zeros({el + 1}, i32);
+        slot_tokens_ = torch::zeros({ep::kMaxTopk}, i32);
+        pair_slot_ = torch::zeros({pairs}, i32);
+        pair_w_ = torch::zeros({pairs}, f32);
+        slot_pos_ = torch::full({static_cast<int64_t>(cfg_.slots()) * cfg_.local_per_token()}, -1, i32);
+        a_ = torch::zeros({pairs, cfg_.hidden}, bf);
+        h_ = torch::zeros({pairs, ffn}, bf);
+        y_ = torch::zeros({pairs, cfg_.hidden}, bf);
+        error_ = torch::zeros({4}, i32);
+        gemm_error_ = torch::zeros({1}, i32);
+
+        ws_.epoch = reinterpret_cast<uint32_t*>(epoch_.data_ptr<int32_t>());
+        ws_.done_ctas = reinterpret_cast<uint32_t*>(done_.data_ptr<int32_t>());
+        ws_.expert_count = counts_.data_ptr<int32_t>();
+        ws_.cursor = cursor_.data_ptr<int32_t>();
+        ws_.offsets = offsets_.data_ptr<int32_t>();
+        ws_.tiles1 = tiles1_.data_ptr<int32_t>();
+        ws_.tiles2 = tiles2_.data_ptr<int32_t>();
+        ws_.slot_tokens = slot_tokens_.data_ptr<int32_t>();
+        ws_.pair_slot = pair_slot_.data_ptr<int32_t>();
+        ws_.pair_w = pair_w_.data_ptr<float>();
+        ws_.slot_pos = slot_pos_.data_ptr<int32_t>();
+        ws_.a = reinterpret_cast<__nv_bfloat16*>(a_.data_ptr());
+        ws_.error = reinterpret_cast<uint32_t*>(error_.data_ptr<int32_t>());
+
+        tmap_a1_ = gemm::make_tmap_bf16_2d(a_.data_ptr(), pairs, cfg_.hidden, 128);
+        tmap_b1_ = gemm::make_tmap_bf16_2d(w13.data_ptr(), w13.size(0), cfg_.hidden, 256);
+        tmap_a2_ = gemm::make_tmap_bf16_2d(h_.data_ptr(), pairs, ffn, 128);
+        tmap_b2_ = gemm::make_tmap_bf16_2d(w2.data_ptr(), w2.size(0), ffn, 256);
+    }
+
+    // ---- stages (all on the current stream) ----
+    void route(torch::Tensor logits, torch::Tensor idx, torch::Tensor w) {
+        TORCH_CHECK(logits.scalar_type() == torch::kFloat32 && logits.is_contiguous(), "logits must be fp32");
+        TORCH_CHECK(logits.size(1) == cfg_.num_experts, "logits must be [T, num_experts]");
+        ep::launch_route(logits.data_ptr<float>(), static_cast<int>(logits.size(0)), cfg_.num_experts, cfg_.topk,
+                         idx.data_ptr<int32_t>(), w.data_ptr<float>(), cur_stream());
+    }
+
+    void dispatch(torch::Tensor x, torch::Tensor idx, torch::Tensor w) {
+        check_tokens(x, idx, w);
+        cudaStream_t s = cur_stream();
+        ep::launch_begin(cfg_, ws_, s);
+        ep::launch_dispatch(cfg_, heap_.view(), reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()),
+                            idx.data_ptr<int32_t>(), w.data_ptr<float>(), static_cast<int>(x.size(0)), ws_, 0, s);
+    }
+
+    void receive() {
+        cudaStream_t s = cur_stream();
+        ep::launch_recv_count(cfg_, heap_.view(), ws_, timeout_ns_, s);
+        gemm::build_schedule(ws_.expert_count, cfg_.experts_per_rank, static_cast<int>(2 * ffn_), 256, ws_.offsets,
+                             ws_.tiles1, s);
+        gemm::build_schedule(ws_.expert_count, cfg_.experts_per_rank, cfg_.hidden, 256, ws_.offsets, ws_.tiles2, s);
+        ep::launch_recv_scatter(cfg_, heap_.view(), ws_, s);
+    }
+
+    void experts() {
+        cudaStream_t s = cur_stream();
+        gemm::GroupedArgs g1{};
+        g1.group_offset = ws_.offsets;
+        g1.tile_prefix = ws_.tiles1;
+        g1.num_groups = cfg_.experts_per_rank;
+        g1.n = static_cast<int32_t>(2 * ffn_);
+        g1.k = cfg_.hidden;
+        g1.c = reinterpret_cast<__nv_bfloat16*>(h_.data_ptr());
+        g1.ldc = ffn_;
+        g1.row_scale = nullptr;
+        g1.error = reinterpret_cast<uint32_t*>(gemm_error_.data_ptr<int32_t>());
+        gemm::grouped_gemm(tmap_a1_, tmap_b1_, g1, /*swiglu=*/true, 0, s);
+        gemm::GroupedArgs g2 = g1;
+        g2.tile_prefix = ws_.tiles2;
+        g2.n = cfg_.hidden;
+        g2.k = static_cast<int32_t>(ffn_);
+        g2.c = reinterpret_cast<__nv_bfloat16*>(y_.data_ptr());
+        g2.ldc = cfg_.hidden;
+        g2.row_scale = ws_.pair_w;
+        gemm::grouped_gemm(tmap_a2_, tmap_b2_, g2, /*swiglu=*/false, 0, s);
+    }
+
+    void combine(torch::Tensor idx, torch::Tensor out) {
+        cudaStream_t s = cur_stream();
+        TORCH_CHECK(out.scalar_type() == torch::kBFloat16 && out.is_contiguous() && out.size(1) == cfg_.hidden,
+                    "out must be contiguous bf16 [T, hidden]");
+        ep::launch_combine_send(cfg_, heap_.view(), reinterpret_cast<const __nv_bfloat16*>(y_.data_ptr()), ws_, 0, s);
+        ep::launch_combine_recv(cfg_, heap_.view(), idx.data_ptr<int32_t>(), static_cast<int>(out.size(0)),
+                                reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), ws_, timeout_ns_, s);
+    }
+
+    /// The whole layer: x [T, hidden] bf16, idx [T, topk] int32, w [T, topk] fp32 -> out [T, hidden] bf16.
+    void forward(torch::Tensor x, torch::Tensor idx, torch::Tensor w, torch::Tensor out) {
+        dispatch(x, idx, w);
+        receive();
+        experts();
+        combine(idx, out);
+    }
+
+    py::tuple error() const {
+        auto e = error_.cpu();
+        auto g = gemm_error_.cpu();
+        return py::make_tuple(e[0].item<int>(), e[1].item<int>(), e[2].item<int>(), e[3].item<int>(), g[0].item<int>());
+    }
+    void clear_error() {
+        error_.zero_();
+        gemm_error_.zero_();
+    }
+
+    py::dict config() const { return config_to_dict(cfg_); }
+    torch::Tensor expert_counts() const { return counts_; }
+    torch::Tensor expert_offsets() const { return offsets_; }
+    torch::Tensor pair_slot() const { return pair_slot_; }
+    torch::Tensor pair_weight() const { return pair_w_; }
+    torch::Tensor expert_input() const { return a_; }
+    torch::Tensor expert_hidden() const { return h_; }
+    torch::Tensor expert_output() const { return y_; }
+    torch::Tensor epoch() const { return epoch_; }
+
+private:
+    void check_tokens(const torch::Tensor& x, const torch::Tensor& idx, const torch::Tensor& w) {
+        TORCH_CHECK(x.scalar_type() == torch::kBFloat16 && x.is_contiguous() && x.size(1) == cfg_.hidden,
+                    "x must be contiguous bf16 [T, hidden]");
+        TORCH_CHECK(x.size(0) <= cfg_.max_tokens, "more tokens than max_tokens");
+        TORCH_CHECK(idx.scalar_type() == torch::kInt32 && idx.is_contiguous() && idx.size(0) == x.size(0) &&
+                        idx.size(1) == cfg_.topk,
+                    "idx must be contiguous int32 [T, topk]");
+        TORCH_CHECK(w.scalar_type() == torch::kFloat32 && w.is_contiguous() && w.size(0) == x.size(0) &&
+                        w.size(1) == cfg_.topk,
+                    "w must be contiguous fp32 [T, topk]");
+    }
+
+    p2p::SymmetricHeap& heap_;
+    ep::EpConfig cfg_;
+    int64_t ffn_;
+    torch::Tensor w13_, w2_;
+    uint64_t timeout_ns_;
+    torch::Tensor epoch_, done_, counts_, cursor_, offsets_, tiles1_, tiles2_, slot_tokens_, pair_slot_, pair_w_,
+        slot_pos_, a_, h_, y_, error_, gemm_error_;
+    ep::EpWorkspace ws_{};
+    CUtensorMap tmap_a1_, tmap_b1_, tmap_a2_, tmap_b2_;
+};
+
+}  // namespace
+
+void register_ep(py::module_& m) {
+    auto e = m.def_submodule("ep", "kiwi::ep (expert-parallel MoE)");
+    e.attr("MAX_TOPK") = ep::kMaxTopk;
+    e.def("finalize_config", [](const py::dict& d) { return config_to_dict(config_from_dict(d)); });
+    e.def("route",
+          [](torch::Tensor logits, int topk, torch::Tensor idx, torch::Tensor w) {
+              ep::launch_route(logits.data_ptr<float>(), static_cast<int>(logits.size(0)),
+                               static_cast<int>(logits.size(1)), topk, idx.data_ptr<int32_t>(), w.data_ptr<float>(),
+                               cur_stream());
+          },
+          "Top-k routing with softmax over the selected logits (fp32 logits [T, E]).");
+    py::class_<MoeLayer>(e, "MoeLayer")
+        .def(py::init<p2p::SymmetricHeap&, const py::dict&, int64_t, torch::Tensor, torch::Tensor, uint64_t>(),
+             py::arg("heap"), py::arg("config"), py::arg("ffn"), py::arg("w13"), py::arg("w2"),
+             py::arg("timeout_ns") = 5000000000ull, py::keep_alive<1, 2>())
+        .def("route", &MoeLayer::route)
+        .def("dispatch", &MoeLayer::dispatch)
+        .def("receive", &MoeLayer::receive)
+        .def("experts", &MoeLayer::experts)
+        .def("combine", &MoeLayer::combine)
+        .def("forward", &MoeLayer::forward)
+        .def("error", &MoeLayer::error)
+        .def("clear_error", &MoeLayer::clear_error)
+        .def_property_readonly("config", &MoeLayer::config)
+        .def_property_readonly("expert_counts", &MoeLayer::expert_counts)
+        .def_property_readonly("expert_offsets", &MoeLayer::expert_offsets)
+        .def_property_readonly("pair_slot", &MoeLayer::pair_slot)
+        .def_property_readonly("pair_weight", &MoeLayer::pair_weight)
+        .def_property_readonly("expert_input", &MoeLayer::expert_input)
+        .def_property_readonly("expert_hidden", &MoeLayer::expert_hidden)
+        .def_property_readonly("expert_output", &MoeLayer::expert_output)
+        .def_property_readonly("epoch", &MoeLayer::epoch);
+}

@@ -1,0 +1,617 @@
+// kiwi::ep kernels: routing, fused quantise + NVLink dispatch, receive-side
+// count / scatter + dequantise, combine send and combine reduce.
+//
+// Parity with the reference's EP kernels (AMDResearch/kiwi):
+//   dispatch  apps/ep/dispatch.hip.cpp:334-993  (dedup by destination rank,
+//             slot per (source rank, token), readiness per source, unpack)
+//   combine   apps/ep/combine.hip.cpp:558-1033  (return rows to the source,
+//             reduce over ranks)
+// The reference moves rows through CPU proxies (RDMA) or HIP-IPC stores and
+// leaves routing, quantisation and the expert FFN to the caller.  Here the
+// dispatch kernel also routes and quantises (1x128 FP8 with fp32 scales, or
+// NVFP4 16-element blocks with e4m3 scales), stores with 16-byte st.global
+// straight into every destination GPU's heap over NVLink, and the receive
+// side lays rows out expert-major for the tcgen05 grouped GEMM.
+// Completion per round: the last CTA of a grid (atomic counter) issues a
+// system-scope release store of (epoch << 32 | tokens) to every rank's flag;
+// receivers wait with ld.acquire.sys under a deadline.
+#include <cuda_bf16.h>
+#include <cuda_fp4.h>
+#include <cuda_fp8.h>
+#include <cuda_runtime.h>
+
+#include "kiwi/ep/kernels.hpp"
+#include "kiwi/ptx.cuh"
+
+namespace kiwi::ep {
+
+namespace {
+
+constexpr int kThreads = 256;
+constexpr float kFp8Max = 448.0f;
+constexpr float kFp4Max = 6.0f;
+
+KIWI_DEV void set_error(const EpWorkspace& ws, uint32_t code, uint32_t site, uint32_t info, int rank) {
+    if (atomicCAS(&ws.error[0], 0u, code) == 0u) {
+        ws.error[1] = site;
+        ws.error[2] = info;
+        ws.error[3] = static_cast<uint32_t>(rank);
+    }
+}
+
+KIWI_DEV const uint8_t* meta_ptr(const EpConfig& c, const uint8_t* base, uint64_t slot) {
+    return base + c.meta_off(slot);
+}
+
+/// Loads 16 bytes that a peer GPU stored into this GPU's memory: L2 only
+/// (.cg), never a possibly stale L1 line.
+KIWI_DEV uint4 ld_cg_v4(const void* p) {
+    uint4 v;
+    asm volatile("ld.global.cg.v4.u32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p));
+    return v;
+}
+KIWI_DEV uint32_t ld_cg_u32(const void* p) {
+    uint32_t v;
+    asm volatile("ld.global.cg.u32 %0, [%1];" : "=r"(v) : "l"(p));
+    return v;
+}
+KIWI_DEV float ld_cg_f32(const void* p) { return __uint_as_float(ld_cg_u32(p)); }
+
+KIWI_DEV void bf16x8_to_f32(uint4 u, float (&f)[8]) {
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const float2 t = __bfloat1622float2(h[i]);
+        f[2 * i] = t.x;
+        f[2 * i + 1] = t.y;
+    }
+}
+
+KIWI_DEV uint4 f32x8_to_bf16(const float (&f)[8]) {
+    uint4 u;
+    uint32_t* w = reinterpret_cast<uint32_t*>(&u);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        __nv_bfloat162 h = __floats2bfloat162_rn(f[2 * i], f[2 * i + 1]);
+        w[i] = *reinterpret_cast<uint32_t*>(&h);
+    }
+    return u;
+}
+
+/// Last-CTA completion: after every CTA has issued its stores, the last one
+/// to arrive publishes `value` to flag offset `flag_off` on every rank.
+KIWI_DEV void grid_done_signal(const EpConfig& c, const p2p::HeapView& h, uint32_t* counter, uint64_t flag_off,
+                               uint64_t value) {
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        ptx::fence_sys();
+        const uint32_t prev = atomicAdd(counter, 1u);
+        if (prev == gridDim.x - 1) {
+            ptx::fence_sys();
+            for (int r = 0; r < c.world; ++r) ptx::st_release_sys_u64(h.base[r] + flag_off, value);
+            *reinterpret_cast<volatile uint32_t*>(counter) = 0;
+        }
+    }
+}
+
+/// Threads [0, world) wait until every rank's flag at `flag_of(src)` carries
+/// `epoch`; returns false (error recorded) on timeout.  Block-collective.
+template <typename FlagOf>
+KIWI_DEV bool wait_all_flags(const EpConfig& c, const p2p::HeapView& h, const EpWorkspace& ws, uint32_t epoch,
+                             FlagOf flag_of, uint32_t site, uint64_t timeout_ns, uint32_t* tokens_out) {
+    __shared__ int s_fail;
+    if (threadIdx.x == 0) s_fail = 0;
+    __syncthreads();
+    if (threadIdx.x < static_cast<unsigned>(c.world)) {
+        const uint64_t* f = reinterpret_cast<const uint64_t*>(h.base[h.rank] + flag_of(threadIdx.x));
+        ptx::Deadline dl(timeout_ns);
+        uint64_t v = ptx::ld_acquire_sys_u64(f);
+        while (static_cast<uint32_t>(v >> 32) != epoch) {
+            if (dl.expired()) {
+                set_error(ws, static_cast<uint32_t>(Status::kTimeout), site, threadIdx.x, c.rank);
+                s_fail = 1;
+                break;
+            }
+            v = ptx::ld_acquire_sys_u64(f);
+        }
+        if (tokens_out) tokens_out[threadIdx.x] = static_cast<uint32_t>(v);
+    }
+    __syncthreads();
+    return s_fail == 0;
+}
+
+// ---------------------------------------------------------------------------
+
+__global__ void begin_kernel(EpConfig c, EpWorkspace ws) {
+    if (threadIdx.x == 0 && blockIdx.x == 0) {
+        *ws.epoch += 1;
+        if (*reinterpret_cast<volatile uint32_t*>(ws.error) != 0) {
+            // Errors persist until the owner clears them; never run a round on a poisoned workspace silently.
+        }
+    }
+    for (int e = threadIdx.x; e < c.experts_per_rank; e += blockDim.x) {
+        ws.expert_count[e] = 0;
+        ws.cursor[e] = 0;
+    }
+}
+
+template <int MAXV>
+__global__ void __launch_bounds__(kThreads) route_kernel(const float* logits, int tokens, int experts, int topk,
+                                                         int32_t* idx, float* w) {
+    const int lane = threadIdx.x & 31;
+    const int t = (blockIdx.x * blockDim.x + threadIdx.x) / 32;
+    if (t >= tokens) return;
+    const float* row = logits + static_cast<int64_t>(t) * experts;
+    float v[MAXV];
+#pragma unroll
+    for (int i = 0; i < MAXV; ++i) {
+        const int j = lane + 32 * i;
+        v[i] = j < experts ? row[j] : -INFINITY;
+    }
+    float top_v[kMaxTopk];
+    int top_i[kMaxTopk];
+#pragma unroll
+    for (int r = 0; r < kMaxTopk; ++r) {
+        if (r >= topk) break;
+        float bv = -INFINITY;
+        int bi = 0x7fffffff;
+#pragma unroll
+        for (int i = 0; i < MAXV; ++i) {
+            const int j = lane + 32 * i;
+            if (v[i] > bv || (v[i] == bv && j < bi)) {
+                bv = v[i];
+                bi = j;
+            }
+        }
+#pragma unroll
+        for (int d = 16; d > 0; d >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, bv, d);
+            const int oi = __shfl_xor_sync(0xffffffffu, bi, d);
+            if (ov > bv || (ov == bv && oi < bi)) {
+                bv = ov;
+                bi = oi;
+            }
+        }
+        top_v[r] = bv;
+        top_i[r] = bi;
+#pragma unroll
+        for (int i = 0; i < MAXV; ++i) {
+            if (lane + 32 * i == bi) v[i] = -INFINITY;
+        }
+    }
+    float sum = 0.f;
+#pragma unroll
+    for (int r = 0; r < kMaxTopk; ++r) {
+        if (r < topk) sum += __expf(top_v[r] - top_v[0]);
+    }
+#pragma unroll
+    for (int r = 0; r < kMaxTopk; ++r) {
+        if (r < topk && lane == r) {
+            idx[static_cast<int64_t>(t) * topk + r] = top_i[r];
+            w[static_cast<int64_t>(t) * topk + r] = __expf(top_v[r] - top_v[0]) / sum;
+        }
+    }
+}
+
+/// FP8 1x128: lane covers 16 elements of a 512-element chunk; 8 lanes share a block scale.
+KIWI_DEV void quant_fp8_16(const uint4 (&in)[2], float& scale, uint4& out) {
+    float f[16];
+    float a[8];
+    bf16x8_to_f32(in[0], a);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) f[i] = a[i];
+    bf16x8_to_f32(in[1], a);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) f[8 + i] = a[i];
+    float amax = 0.f;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) amax = fmaxf(amax, fabsf(f[i]));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 4));
+    scale = amax > 0.f ? amax / kFp8Max : 1.0f;
+    const float inv = amax > 0.f ? kFp8Max / amax : 0.f;
+    uint16_t q[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        q[i] = __nv_cvt_float2_to_fp8x2(make_float2(f[2 * i] * inv, f[2 * i + 1] * inv), __NV_SATFINITE, __NV_E4M3);
+    }
+    out = make_uint4(q[0] | (uint32_t(q[1]) << 16), q[2] | (uint32_t(q[3]) << 16), q[4] | (uint32_t(q[5]) << 16),
+                     q[6] | (uint32_t(q[7]) << 16));
+}
+
+KIWI_DEV void dequant_fp8_16(uint4 q, float scale, uint4 (&out)[2]) {
+    const uint16_t* p = reinterpret_cast<const uint16_t*>(&q);
+    float f[16];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const __half2_raw hr = __nv_cvt_fp8x2_to_halfraw2(static_cast<__nv_fp8x2_storage_t>(p[i]), __NV_E4M3);
+        const float2 t = __half22float2(*reinterpret_cast<const __half2*>(&hr));
+        f[2 * i] = t.x * scale;
+        f[2 * i + 1] = t.y * scale;
+    }
+    float a[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) a[i] = f[i];
+    out[0] = f32x8_to_bf16(a);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) a[i] = f[8 + i];
+    out[1] = f32x8_to_bf16(a);
+}
+
+/// NVFP4: lane covers 16 elements = one 16-element block (e4m3 block scale,
+/// relative to a per-row fp32 scale so block scales stay in e4m3 range).
+KIWI_DEV void quant_fp4_16(const uint4 (&in)[2], float row_scale, uint8_t& sbyte, uint2& out) {
+    float f[16];
+    float a[8];
+    bf16x8_to_f32(in[0], a);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) f[i] = a[i];
+    bf16x8_to_f32(in[1], a);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) f[8 + i] = a[i];
+    float amax = 0.f;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) amax = fmaxf(amax, fabsf(f[i]));
+    // block scale in e4m3 units of row_scale: s = amax / (6 * row_scale)
+    const float s = row_scale > 0.f ? amax / (kFp4Max * row_scale) : 0.f;
+    const __nv_fp8_storage_t sq = __nv_cvt_float_to_fp8(s, __NV_SATFINITE, __NV_E4M3);
+    const __half_raw sh = __nv_cvt_fp8_to_halfraw(sq, __NV_E4M3);
+    const float sdec = __half2float(*reinterpret_cast<const __half*>(&sh)) * row_scale;
+    const float inv = sdec > 0.f ? 1.0f / sdec : 0.f;
+    sbyte = sq;
+    uint8_t b[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        b[i] = __nv_cvt_float2_to_fp4x2(make_float2(f[2 * i] * inv, f[2 * i + 1] * inv), __NV_E2M1, cudaRoundNearest);
+    }
+    out = make_uint2(b[0] | (uint32_t(b[1]) << 8) | (uint32_t(b[2]) << 16) | (uint32_t(b[3]) << 24),
+                     b[4] | (uint32_t(b[5]) << 8) | (uint32_t(b[6]) << 16) | (uint32_t(b[7]) << 24));
+}
+
+KIWI_DEV void dequant_fp4_16(uint2 q, float block_scale, uint4 (&out)[2]) {
+    const uint8_t* p = reinterpret_cast<const uint8_t*>(&q);
+    float f[16];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const __half2_raw hr = __nv_cvt_fp4x2_to_halfraw2(static_cast<__nv_fp4x2_storage_t>(p[i]), __NV_E2M1);
+        const float2 t = __half22float2(*reinterpret_cast<const __half2*>(&hr));
+        f[2 * i] = t.x * block_scale;
+        f[2 * i + 1] = t.y * block_scale;
+    }
+    float a[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) a[i] = f[i];
+    out[0] = f32x8_to_bf16(a);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) a[i] = f[8 + i];
+    out[1] = f32x8_to_bf16(a);
+}
+
+template <int QUANT>
+__global__ void __launch_bounds__(kThreads) dispatch_kernel(EpConfig c, p2p::HeapView h, const __nv_bfloat16* x,
+                                                            const int32_t* idx, const float* w, int tokens,
+                                                            EpWorkspace ws) {
+    const int lane = threadIdx.x & 31;
+    const int warps = gridDim.x * (blockDim.x / 32);
+    const uint32_t epoch = *reinterpret_cast<volatile uint32_t*>(ws.epoch);
+    const int me = c.rank;
+    for (int t = (blockIdx.x * blockDim.x + threadIdx.x) / 32; t < tokens; t += warps) {
+        const int e = lane < c.topk ? idx[static_cast<int64_t>(t) * c.topk + lane] : -1;
+        const float wt = lane < c.topk ? w[static_cast<int64_t>(t) * c.topk + lane] : 0.f;
+        const bool ok_e = e >= 0 && e < c.num_experts;
+        const uint32_t mask = __reduce_or_sync(0xffffffffu, ok_e ? (1u << (e / c.experts_per_rank)) : 0u);
+        const uint64_t slot = c.slot_index(me, t);
+        // Metadata (header, ids, weights) to every destination.
+        for (uint32_t m = mask; m; m &= m - 1) {
+            const int r = __ffs(m) - 1;
+            uint8_t* mp = h.base[r] + c.meta_off(slot);
+            if (lane < c.topk) {
+                reinterpret_cast<int32_t*>(mp + sizeof(DispatchMetaHeader))[lane] = e;
+                reinterpret_cast<float*>(mp + sizeof(DispatchMetaHeader) + 4 * c.topk)[lane] = wt;
+            }
+            if (lane == 0) {
+                ptx::st_v4(mp, make_uint4(epoch, static_cast<uint32_t>(t), 0, 0));
+            }
+        }
+        const __nv_bfloat16* xr = x + static_cast<int64_t>(t) * c.hidden;
+        if constexpr (QUANT == static_cast<int>(Quant::kNone)) {
+            for (int col = lane * 8; col < c.hidden; col += 256) {
+                const uint4 v = ptx::ld_nc_v4(xr + col);
+                for (uint32_t m = mask; m; m &= m - 1) {
+                    const int r = __ffs(m) - 1;
+                    ptx::st_v4(h.base[r] + c.row_off(slot) + 2ull * col, v);
+                }
+            }
+        } else if constexpr (QUANT == static_cast<int>(Quant::kFp8)) {
+            for (int base = 0; base < c.hidden; base += 512) {
+                const int col = base + lane * 16;
+                uint4 in[2];
+                in[0] = ptx::ld_nc_v4(xr + col);
+                in[1] = ptx::ld_nc_v4(xr + col + 8);
+                float scale;
+                uint4 q;
+                quant_fp8_16(in, scale, q);
+                for (uint32_t m = mask; m; m &= m - 1) {
+                    const int r = __ffs(m) - 1;
+                    ptx::st_v4(h.base[r] + c.row_off(slot) + col, q);
+                    if ((lane & 7) == 0) {
+                        reinterpret_cast<float*>(h.base[r] + c.scale_off(slot))[col / kFp8Block] = scale;
+                    }
+                }
+            }
+        } else {
+            // NVFP4: per-row fp32 scale first (row amax / (448 * 6)), then 16-element blocks.
+            float amax = 0.f;
+            for (int col = lane * 8; col < c.hidden; col += 256) {
+                float f[8];
+                bf16x8_to_f32(ptx::ld_nc_v4(xr + col), f);
+#pragma unroll
+                for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(f[i]));
+            }
+#pragma unroll
+            for (int d = 16; d > 0; d >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, d));
+            const float row_scale = amax > 0.f ? amax / (kFp8Max * kFp4Max) : 0.f;
+            for (int base = 0; base < c.hidden; base += 512) {
+                const int col = base + lane * 16;
+                uint4 in[2];
+                in[0] = ptx::ld_nc_v4(xr + col);
+                in[1] = ptx::ld_nc_v4(xr + col + 8);
+                uint8_t sb;
+                uint2 q;
+                quant_fp4_16(in, row_scale, sb, q);
+                for (uint32_t m = mask; m; m &= m - 1) {
+                    const int r = __ffs(m) - 1;
+                    *reinterpret_cast<uint2*>(h.base[r] + c.row_off(slot) + col / 2) = q;
+                    h.base[r][c.scale_off(slot) + 4 + col / kFp4Block] = sb;
+                }
+            }
+            if (lane == 0) {
+                for (uint32_t m = mask; m; m &= m - 1) {
+                    const int r = __ffs(m) - 1;
+                    reinterpret_cast<float*>(h.base[r] + c.scale_off(slot))[0] = row_scale;
+                }
+            }
+        }
+    }
+    grid_done_signal(c, h, &ws.done_ctas[0], c.dispatch_flag(me),
+                     (static_cast<uint64_t>(epoch) << 32) | static_cast<uint32_t>(tokens));
+}
+
+__global__ void __launch_bounds__(kThreads) recv_count_kernel(EpConfig c, p2p::HeapView h, EpWorkspace ws,
+                                                              uint64_t timeout_ns) {
+    __shared__ uint32_t s_tokens[kMaxRanks];
+    const uint32_t epoch = *reinterpret_cast<volatile uint32_t*>(ws.epoch);
+    if (!wait_all_flags(c, h, ws, epoch, [&](int src) { return c.dispatch_flag(src); }, kSiteDispatchWait,
+                        timeout_ns, s_tokens)) {
+        return;
+    }
+    if (blockIdx.x == 0 && threadIdx.x < static_cast<unsigned>(c.world)) ws.slot_tokens[threadIdx.x] = s_tokens[threadIdx.x];
+    const int e0 = c.rank * c.experts_per_rank;
+    const uint8_t* base = h.base[h.rank];
+    for (uint64_t s = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x; s < c.slots();
+         s += static_cast<uint64_t>(gridDim.x) * blockDim.x) {
+        const int src = static_cast<int>(s / c.max_tokens);
+        const int t = static_cast<int>(s % c.max_tokens);
+        if (t >= static_cast<int>(s_tokens[src])) continue;
+        const uint8_t* mp = meta_ptr(c, base, s);
+        if (ld_cg_u32(mp) != epoch) continue;
+        const int32_t* ids = reinterpret_cast<const int32_t*>(mp + sizeof(DispatchMetaHeader));
+        for (int j = 0; j < c.topk; ++j) {
+            const int e = static_cast<int>(ld_cg_u32(ids + j)) - e0;
+            if (e >= 0 && e < c.experts_per_rank) atomicAdd(&ws.expert_count[e], 1);
+        }
+    }
+}
+
+template <int QUANT>
+__global__ void __launch_bounds__(kThreads) recv_scatter_kernel(EpConfig c, p2p::HeapView h, EpWorkspace ws) {
+    const int lane = threadIdx.x & 31;
+    const int warps = gridDim.x * (blockDim.x / 32);
+    const uint32_t epoch = *reinterpret_cast<volatile uint32_t*>(ws.epoch);
+    const int e0 = c.rank * c.experts_per_rank;
+    const int lpt = c.local_per_token();
+    const uint8_t* base = h.base[h.rank];
+    const int64_t max_pairs = c.max_pairs();
+    for (uint64_t s = (blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x) / 32; s < c.slots();
+         s += warps) {
+        const int src = static_cast<int>(s / c.max_tokens);
+        const int t = static_cast<int>(s % c.max_tokens);
+        const uint8_t* mp = meta_ptr(c, base, s);
+        bool valid = t < ws.slot_tokens[src];
+        if (valid) valid = ld_cg_u32(mp) == epoch;
+        int e = -1;
+        float wt = 0.f;
+        if (valid && lane < c.topk) {
+            e = static_cast<int>(ld_cg_u32(reinterpret_cast<const int32_t*>(mp + sizeof(DispatchMetaHeader)) + lane)) - e0;
+            wt = ld_cg_f32(reinterpret_cast<const float*>(mp + sizeof(DispatchMetaHeader) + 4 * c.topk) + lane);
+        }
+        const bool local = valid && lane < c.topk && e >= 0 && e < c.experts_per_rank;
+        const uint32_t lmask = __ballot_sync(0xffffffffu, local);
+        int pos = -1;
+        if (local) {
+            pos = ws.offsets[e] + atomicAdd(&ws.cursor[e], 1);
+            if (pos < max_pairs) {
+                ws.pair_slot[pos] = static_cast<int32_t>(s);
+                ws.pair_w[pos] = wt;
+            } else {
+                set_error(ws, static_cast<uint32_t>(Status::kBadArgument), kSiteCapacity, pos, c.rank);
+                pos = -1;
+            }
+            ws.slot_pos[s * lpt + __popc(lmask & ((1u << lane) - 1))] = pos;
+        }
+        const int nloc = __popc(lmask);
+        if (lane >= nloc && lane < lpt) ws.slot_pos[s * lpt + lane] = -1;
+        if (nloc == 0) continue;
+        // Copy (and dequantise) the row once per local expert.
+        for (int cb = 0; cb < c.hidden; cb += 512) {
+            const int col = cb + lane * 16;
+            uint4 out[2];
+            if constexpr (QUANT == static_cast<int>(Quant::kNone)) {
+                out[0] = ld_cg_v4(base + c.row_off(s) + 2ull * col);
+                out[1] = ld_cg_v4(base + c.row_off(s) + 2ull * col + 16);
+            } else if constexpr (QUANT == static_cast<int>(Quant::kFp8)) {
+                const uint4 q = ld_cg_v4(base + c.row_off(s) + col);
+                const float sc = ld_cg_f32(base + c.scale_off(s) + 4ull * (col / kFp8Block));
+                dequant_fp8_16(q, sc, out);
+            } else {
+                uint2 q;
+                const uint4 qq = ld_cg_v4(base + c.row_off(s) + (col / 32) * 16);  // 16 B = 32 elements
+                q = (lane & 1) ? make_uint2(qq.z, qq.w) : make_uint2(qq.x, qq.y);
+                const float rs = ld_cg_f32(base + c.scale_off(s));
+                const uint8_t sb = static_cast<uint8_t>(ld_cg_u32(base + c.scale_off(s) + 4 + ((col / kFp4Block) & ~3)) >>
+                                                        (8 * ((col / kFp4Block) & 3)));
+                const __half_raw sh = __nv_cvt_fp8_to_halfraw(sb, __NV_E4M3);
+                dequant_fp4_16(q, __half2float(*reinterpret_cast<const __half*>(&sh)) * rs, out);
+            }
+            for (uint32_t m = lmask; m; m &= m - 1) {
+                const int p = __shfl_sync(0xffffffffu, pos, __ffs(m) - 1);
+                if (p >= 0) {
+                    __nv_bfloat16* dst = ws.a + static_cast<int64_t>(p) * c.hidden + col;
+                    ptx::st_v4(dst, out[0]);
+                    ptx::st_v4(dst + 8, out[1]);
+                }
+            }
+        }
+    }
+}
+
+__global__ void __launch_bounds__(kThreads) combine_send_kernel(EpConfig c, p2p::HeapView h,
+                                                                const __nv_bfloat16* y, EpWorkspace ws) {
+    const int lane = threadIdx.x & 31;
+    const int warps = gridDim.x * (blockDim.x / 32);
+    const uint32_t epoch = *reinterpret_cast<volatile uint32_t*>(ws.epoch);
+    const int lpt = c.local_per_token();
+    for (uint64_t s = (blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x) / 32; s < c.slots();
+         s += warps) {
+        const int p = lane < lpt ? ws.slot_pos[s * lpt + lane] : -1;
+        const uint32_t pm = __ballot_sync(0xffffffffu, p >= 0);
+        if (pm == 0) continue;
+        const int src = static_cast<int>(s / c.max_tokens);
+        const int t = static_cast<int>(s % c.max_tokens);
+        uint8_t* dst = h.base[src] + c.comb_off(c.rank, t);
+        for (int col = lane * 8; col < c.hidden; col += 256) {
+            float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+            for (uint32_t m = pm; m; m &= m - 1) {
+                const int pp = __shfl_sync(0xffffffffu, p, __ffs(m) - 1);
+                float f[8];
+                bf16x8_to_f32(ptx::ld_v4(y + static_cast<int64_t>(pp) * c.hidden + col), f);
+#pragma unroll
+                for (int i = 0; i < 8; ++i) acc[i] += f[i];
+            }
+            ptx::st_v4(dst + 2ull * col, f32x8_to_bf16(acc));
+        }
+    }
+    grid_done_signal(c, h, &ws.done_ctas[1], c.combine_flag(c.rank), (static_cast<uint64_t>(epoch) << 32) | 1u);
+}
+
+__global__ void __launch_bounds__(kThreads) combine_recv_kernel(EpConfig c, p2p::HeapView h, const int32_t* idx,
+                                                                int tokens, __nv_bfloat16* out, EpWorkspace ws,
+                                                                uint64_t timeout_ns) {
+    const int lane = threadIdx.x & 31;
+    const int warps = gridDim.x * (blockDim.x / 32);
+    const uint32_t epoch = *reinterpret_cast<volatile uint32_t*>(ws.epoch);
+    if (!wait_all_flags(c, h, ws, epoch, [&](int src) { return c.combine_flag(src); }, kSiteCombineWait, timeout_ns,
+                        nullptr)) {
+        return;
+    }
+    const uint8_t* base = h.base[h.rank];
+    for (int t = (blockIdx.x * blockDim.x + threadIdx.x) / 32; t < tokens; t += warps) {
+        const int e = lane < c.topk ? idx[static_cast<int64_t>(t) * c.topk + lane] : -1;
+        const bool ok_e = e >= 0 && e < c.num_experts;
+        const uint32_t mask = __reduce_or_sync(0xffffffffu, ok_e ? (1u << (e / c.experts_per_rank)) : 0u);
+        for (int col = lane * 8; col < c.hidden; col += 256) {
+            float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+            for (uint32_t m = mask; m; m &= m - 1) {
+                const int r = __ffs(m) - 1;
+                float f[8];
+                bf16x8_to_f32(ld_cg_v4(base + c.comb_off(r, t) + 2ull * col), f);
+#pragma unroll
+                for (int i = 0; i < 8; ++i) acc[i] += f[i];
+            }
+            ptx::st_v4(out + static_cast<int64_t>(t) * c.hidden + col, f32x8_to_bf16(acc));
+        }
+    }
+}
+
+int default_grid() {
+    static int n = 0;
+    if (n == 0) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    }
+    return n;
+}
+
+}  // namespace
+
+void launch_begin(const EpConfig& c, const EpWorkspace& ws, cudaStream_t s) {
+    begin_kernel<<<1, 256, 0, s>>>(c, ws);
+    KIWI_CUDA_CHECK(cudaGetLastError());
+}
+
+void launch_route(const float* logits, int tokens, int experts, int topk, int32_t* idx, float* w, cudaStream_t s) {
+    if (topk < 1 || topk > kMaxTopk) throw kiwi::error("route: topk must be in [1, 16]");
+    if (tokens == 0) return;
+    const int blocks = (tokens * 32 + kThreads - 1) / kThreads;
+    if (experts <= 64) route_kernel<2><<<blocks, kThreads, 0, s>>>(logits, tokens, experts, topk, idx, w);
+    else if (experts <= 256) route_kernel<8><<<blocks, kThreads, 0, s>>>(logits, tokens, experts, topk, idx, w);
+    else if (experts <= 1024) route_kernel<32><<<blocks, kThreads, 0, s>>>(logits, tokens, experts, topk, idx, w);
+    else throw kiwi::error("route: at most 1024 experts");
+    KIWI_CUDA_CHECK(cudaGetLastError());
+}
+
+void launch_dispatch(const EpConfig& c, const p2p::HeapView& h, const __nv_bfloat16* x, const int32_t* idx,
+                     const float* w, int tokens, const EpWorkspace& ws, int grid, cudaStream_t s) {
+    if (tokens > c.max_tokens) throw kiwi::error("dispatch: more tokens than max_tokens");
+    if (grid <= 0) grid = default_grid();
+    switch (static_cast<Quant>(c.quant)) {
+        case Quant::kNone:
+            dispatch_kernel<0><<<grid, kThreads, 0, s>>>(c, h, x, idx, w, tokens, ws);
+            break;
+        case Quant::kFp8:
+            dispatch_kernel<1><<<grid, kThreads, 0, s>>>(c, h, x, idx, w, tokens, ws);
+            break;
+        case Quant::kNvfp4:
+            dispatch_kernel<2><<<grid, kThreads, 0, s>>>(c, h, x, idx, w, tokens, ws);
+            break;
+    }
+    KIWI_CUDA_CHECK(cudaGetLastError());
+}
+
+void launch_recv_count(const EpConfig& c, const p2p::HeapView& h, const EpWorkspace& ws, uint64_t timeout_ns,
+                       cudaStream_t s) {
+    const uint64_t blocks = (c.slots() + kThreads - 1) / kThreads;
+    const int grid = static_cast<int>(blocks < 4u * default_grid() ? blocks : 4u * default_grid());
+    recv_count_kernel<<<grid, kThreads, 0, s>>>(c, h, ws, timeout_ns);
+    KIWI_CUDA_CHECK(cudaGetLastError());
+}
+
+void launch_recv_scatter(const EpConfig& c, const p2p::HeapView& h, const EpWorkspace& ws, cudaStream_t s) {
+    const int grid = 2 * default_grid();
+    switch (static_cast<Quant>(c.quant)) {
+        case Quant::kNone: recv_scatter_kernel<0><<<grid, kThreads, 0, s>>>(c, h, ws); break;
+        case Quant::kFp8: recv_scatter_kernel<1><<<grid, kThreads, 0, s>>>(c, h, ws); break;
+        case Quant::kNvfp4: recv_scatter_kernel<2><<<grid, kThreads, 0, s>>>(c, h, ws); break;
+    }
+    KIWI_CUDA_CHECK(cudaGetLastError());
+}
+
+void launch_combine_send(const EpConfig& c, const p2p::HeapView& h, const __nv_bfloat16* y, const EpWorkspace& ws,
+                         int grid, cudaStream_t s) {
+    if (grid <= 0) grid = 2 * default_grid();
+    combine_send_kernel<<<grid, kThreads, 0, s>>>(c, h, y, ws);
+    KIWI_CUDA_CHECK(cudaGetLastError());
+}
+
+void launch_combine_recv(const EpConfig& c, const p2p::HeapView& h, const int32_t* idx, int tokens,
+                         __nv_bfloat16* out, const EpWorkspace& ws, uint64_t timeout_ns, cudaStream_t s) {
+    const int grid = 2 * default_grid();
+    combine_recv_kernel<<<grid, kThreads, 0, s>>>(c, h, idx, tokens, out, ws, timeout_ns);
+    KIWI_CUDA_CHECK(cudaGetLastError());
+}
+
+}  // namespace kiwi::ep

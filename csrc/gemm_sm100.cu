@@ -1,0 +1,362 @@
+// Grouped BF16 GEMM on sm_100a tensor cores (tcgen05 + TMEM + TMA).
+//
+//   for each group g:  C[off_g : off_g + rows_g, :] = epilogue( A[off_g : .., :K] . B[g]^T )
+//
+// A is [total_rows, K] bf16 (K-major), B is [G * N, K] bf16 (K-major, one
+// N x K matrix per group), C is bf16.  Group row counts live on the device
+// (the MoE router fills them), so the tile schedule is built on the device
+// and nothing here synchronises with the host: the launch is graph-capturable.
+//
+// Kernel shape (one CTA per SM, persistent over tiles):
+//   warp 0       TMA producer: 128x64 A tile + BNx64 B tile per stage (SW128)
+//   warp 1       TMEM owner + MMA issuer: tcgen05.mma kind::f16, M=128, N=BN, K=16
+//   warps 2..5   epilogue: tcgen05.ld 32 columns at a time, optional SwiGLU /
+//                per-row scale, bf16 stores
+//   4 smem stages (A 16 KB + B 32 KB each), two TMEM accumulators of BN
+//   columns so the epilogue of tile i overlaps the MMAs of tile i+1.
+// Every mbarrier wait is bounded; a timeout sets *error and the CTA unwinds
+// and frees its TMEM.
+//
+// SwiGLU epilogue: B rows of tile n hold [gate rows 128n..128n+127 |
+// up rows 128n..128n+127] (interleave_gate_up() builds that layout), so one
+// accumulator tile holds both halves and the epilogue writes silu(g) * u.
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include "kiwi/gemm/grouped_gemm.hpp"
+#include "kiwi/p2p/driver.hpp"
+#include "kiwi/sm100.cuh"
+
+namespace kiwi::gemm {
+
+namespace {
+
+constexpr int kBM = 128;
+constexpr int kBK = 64;
+constexpr int kStages = 4;
+constexpr int kThreads = 192;
+
+template <int BN>
+struct Smem {
+    static constexpr int kABytes = kBM * kBK * 2;
+    static constexpr int kBBytes = BN * kBK * 2;
+    static constexpr int kStageBytes = kABytes + kBBytes;
+    static constexpr int kBarOffset = kStages * kStageBytes;
+    static constexpr int kBytes = kBarOffset + 256 + 1024;  // barriers + tmem slot + alignment slack
+};
+
+__device__ __forceinline__ void locate_tile(const int32_t* tile_prefix, int num_groups, int n_tiles, int tile,
+                                            int& g, int& m_tile, int& n_tile) {
+    int lo = 0, hi = num_groups - 1;
+    while (lo < hi) {  // first g with tile_prefix[g + 1] > tile
+        const int mid = (lo + hi) >> 1;
+        if (__ldg(&tile_prefix[mid + 1]) > tile) hi = mid;
+        else lo = mid + 1;
+    }
+    g = lo;
+    const int local = tile - __ldg(&tile_prefix[g]);
+    m_tile = local / n_tiles;
+    n_tile = local - m_tile * n_tiles;
+}
+
+__device__ __forceinline__ float silu(float x) { return x / (1.0f + __expf(-x)); }
+
+__device__ __forceinline__ void store_row32(__nv_bfloat16* dst, const float (&v)[32]) {
+    uint4 out[4];
+    uint32_t* w = reinterpret_cast<uint32_t*>(out);
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+        __nv_bfloat162 h = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
+        w[i] = *reinterpret_cast<uint32_t*>(&h);
+    }
+    uint4* d = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) d[i] = out[i];
+}
+
+template <int BN, bool SWIGLU>
+__global__ void __launch_bounds__(kThreads, 1)
+    grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
+                        GroupedArgs p) {
+    using S = Smem<BN>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::kBarOffset);
+    uint64_t* empty = full + kStages;
+    uint64_t* tmem_full = empty + kStages;
+    uint64_t* tmem_empty = tmem_full + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tmem_empty + 2);
+    __shared__ int s_abort;
+
+    const int warp = threadIdx.x / 32;
+    const int lane = threadIdx.x & 31;
+    const int n_tiles = p.n / BN;
+    const int k_blocks = p.k / kBK;
+    const int total_tiles = __ldg(&p.tile_prefix[p.num_groups]);
+
+    if (threadIdx.x == 0) {
+        s_abort = 0;
+        for (int s = 0; s < kStages; ++s) {
+            sm100::mbar_init(&full[s], 1);
+            sm100::mbar_init(&empty[s], 1);
+        }
+        for (int a = 0; a < 2; ++a) {
+            sm100::mbar_init(&tmem_full[a], 1);
+            sm100::mbar_init(&tmem_empty[a], 128);
+        }
+        sm100::fence_mbar_init();
+    }
+    if (warp == 0 && lane == 0) {
+        sm100::tma_prefetch_desc(&tmap_a);
+        sm100::tma_prefetch_desc(&tmap_b);
+    }
+    if (warp == 1) sm100::tmem_alloc(tmem_slot, 2 * BN);
+    sm100::tc_fence_before();
+    __syncthreads();
+    sm100::tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    auto fail = [&](uint32_t code) {
+        *reinterpret_cast<volatile int*>(&s_abort) = 1;
+        if (p.error) atomicCAS(p.error, 0u, code);
+    };
+
+    if (warp == 0) {
+        if (lane == 0) {
+            int stage = 0;
+            uint32_t phase = 0;
+            for (int tile = blockIdx.x; tile < total_tiles && !*reinterpret_cast<volatile int*>(&s_abort); tile += gridDim.x) {
+                int g, mt, nt;
+                locate_tile(p.tile_prefix, p.num_groups, n_tiles, tile, g, mt, nt);
+                const int row0 = __ldg(&p.group_offset[g]) + mt * kBM;
+                const int brow0 = g * p.n + nt * BN;
+                for (int kb = 0; kb < k_blocks; ++kb) {
+                    if (!sm100::mbar_wait(&empty[stage], phase ^ 1)) {
+                        fail(1);
+                        break;
+                    }
+                    uint8_t* sa = smem + stage * S::kStageBytes;
+                    uint8_t* sb = sa + S::kABytes;
+                    sm100::mbar_arrive_expect_tx(&full[stage], S::kStageBytes);
+                    sm100::tma_load_2d(sa, &tmap_a, &full[stage], kb * kBK, row0);
+                    sm100::tma_load_2d(sb, &tmap_b, &full[stage], kb * kBK, brow0);
+                    if (++stage == kStages) {
+                        stage = 0;
+                        phase ^= 1;
+                    }
+                }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            const uint32_t idesc = sm100::idesc_bf16_f32(kBM, BN);
+            int stage = 0;
+            uint32_t phase = 0;
+            int acc = 0;
+            uint32_t acc_phase = 0;
+            for (int tile = blockIdx.x; tile < total_tiles && !*reinterpret_cast<volatile int*>(&s_abort); tile += gridDim.x) {
+                if (!sm100::mbar_wait(&tmem_empty[acc], acc_phase ^ 1)) {
+                    fail(2);
+                    break;
+                }
+                sm100::tc_fence_after();
+                const uint32_t d = tmem_base + acc * BN;
+                bool ok = true;
+                for (int kb = 0; kb < k_blocks; ++kb) {
+                    if (!sm100::mbar_wait(&full[stage], phase)) {
+                        fail(3);
+                        ok = false;
+                        break;
+                    }
+                    sm100::tc_fence_after();
+                    uint8_t* sa = smem + stage * S::kStageBytes;
+                    uint8_t* sb = sa + S::kABytes;
+                    const uint64_t adesc = sm100::sw128_kmajor_desc(sa);
+                    const uint64_t bdesc = sm100::sw128_kmajor_desc(sb);
+#pragma unroll
+                    for (int kk = 0; kk < kBK / 16; ++kk) {
+                        // +32 bytes of K per step inside the 128-byte swizzle atom.
+                        sm100::mma_bf16(d, adesc + 2 * kk, bdesc + 2 * kk, idesc, (kb | kk) != 0 ? 1u : 0u);
+                    }
+                    sm100::mma_commit(&empty[stage]);
+                    if (++stage == kStages) {
+                        stage = 0;
+                        phase ^= 1;
+                    }
+                }
+                if (!ok) break;
+                sm100::mma_commit(&tmem_full[acc]);
+                if (++acc == 2) {
+                    acc = 0;
+                    acc_phase ^= 1;
+                }
+            }
+        }
+    } else {
+        // Epilogue: warps 2..5; TMEM lane quadrant = warp % 4.
+        const int q = warp & 3;
+        const int row_in_tile = q * 32 + lane;
+        int acc = 0;
+        uint32_t acc_phase = 0;
+        for (int tile = blockIdx.x; tile < total_tiles && !*reinterpret_cast<volatile int*>(&s_abort); tile += gridDim.x) {
+            int g, mt, nt;
+            locate_tile(p.tile_prefix, p.num_groups, n_tiles, tile, g, mt, nt);
+            if (!sm100::mbar_wait(&tmem_full[acc], acc_phase)) {
+                fail(4);
+                break;
+            }
+            sm100::tc_fence_after();
+            const int g_off = __ldg(&p.group_offset[g]);
+            const int g_rows = __ldg(&p.group_offset[g + 1]) - g_off;
+            const int r = mt * kBM + row_in_tile;
+            const bool valid = r < g_rows;
+            const int64_t out_row = static_cast<int64_t>(g_off) + r;
+            const float scale = (valid && p.row_scale) ? p.row_scale[out_row] : 1.0f;
+            const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN;
+            if constexpr (SWIGLU) {
+                __nv_bfloat16* crow = p.c + out_row * p.ldc + nt * (BN / 2);
+#pragma unroll 1
+                for (int c = 0; c < BN / 2; c += 32) {
+                    float gv[32], uv[32];
+                    sm100::tmem_ld_32cols(taddr + c, gv);
+                    sm100::tmem_ld_32cols(taddr + BN / 2 + c, uv);
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) gv[i] = silu(gv[i]) * uv[i] * scale;
+                    if (valid) store_row32(crow + c, gv);
+                }
+            } else {
+                __nv_bfloat16* crow = p.c + out_row * p.ldc + nt * BN;
+#pragma unroll 1
+                for (int c = 0; c < BN; c += 32) {
+                    float v[32];
+                    sm100::tmem_ld_32cols(taddr + c, v);
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) v[i] *= scale;
+                    if (valid) store_row32(crow + c, v);
+                }
+            }
+            sm100::tc_fence_before();
+            sm100::mbar_arrive(&tmem_empty[acc]);
+            if (++acc == 2) {
+                acc = 0;
+                acc_phase ^= 1;
+            }
+        }
+    }
+    sm100::tc_fence_before();
+    __syncthreads();
+    sm100::tc_fence_after();
+    if (warp == 1) sm100::tmem_dealloc(tmem_base, 2 * BN);
+}
+
+/// One block: exclusive scan of group row counts -> offsets, and of the tile
+/// counts -> tile_prefix.  Works for up to 1024 groups.
+__global__ void build_schedule_kernel(const int32_t* counts, int num_groups, int n_tiles, int32_t* offsets,
+                                      int32_t* tile_prefix) {
+    __shared__ int32_t s_rows[1024];
+    __shared__ int32_t s_tiles[1024];
+    const int t = threadIdx.x;
+    const int rows = t < num_groups ? counts[t] : 0;
+    s_rows[t] = rows;
+    s_tiles[t] = ((rows + kBM - 1) / kBM) * n_tiles;
+    __syncthreads();
+    for (int d = 1; d < blockDim.x; d <<= 1) {
+        const int a = t >= d ? s_rows[t - d] : 0;
+        const int b = t >= d ? s_tiles[t - d] : 0;
+        __syncthreads();
+        s_rows[t] += a;
+        s_tiles[t] += b;
+        __syncthreads();
+    }
+    if (t < num_groups) {
+        offsets[t + 1] = s_rows[t];
+        tile_prefix[t + 1] = s_tiles[t];
+    }
+    if (t == 0) {
+        offsets[0] = 0;
+        tile_prefix[0] = 0;
+    }
+}
+
+}  // namespace
+
+CUtensorMap make_tmap_bf16_2d(const void* ptr, uint64_t rows, uint64_t cols, uint32_t box_rows) {
+    static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
+    if (!encode) {
+        void* fn = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        KIWI_CUDA_CHECK(cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &fn, 12000, cudaEnableDefault, &q));
+        if (q != cudaDriverEntryPointSuccess || !fn) throw kiwi::error("cuTensorMapEncodeTiled unavailable");
+        encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    }
+    if (reinterpret_cast<uintptr_t>(ptr) % 16 != 0 || (cols * 2) % 16 != 0) {
+        throw kiwi::error("make_tmap_bf16_2d: base and row stride must be 16-byte aligned");
+    }
+    CUtensorMap m;
+    const cuuint64_t dims[2] = {cols, rows};
+    const cuuint64_t strides[1] = {cols * 2};
+    const cuuint32_t box[2] = {static_cast<cuuint32_t>(kBK), box_rows};
+    const cuuint32_t estr[2] = {1, 1};
+    const CUresult r = encode(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+                              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    p2p::check_cu(r, "cuTensorMapEncodeTiled");
+    return m;
+}
+
+void build_schedule(const int32_t* counts, int num_groups, int n, int bn, int32_t* offsets, int32_t* tile_prefix,
+                    cudaStream_t stream) {
+    if (num_groups < 1 || num_groups > 1024) throw kiwi::error("build_schedule: 1..1024 groups");
+    int threads = 32;
+    while (threads < num_groups) threads <<= 1;
+    build_schedule_kernel<<<1, threads, 0, stream>>>(counts, num_groups, n / bn, offsets, tile_prefix);
+    KIWI_CUDA_CHECK(cudaGetLastError());
+}
+
+int num_sms() {
+    static int n = 0;
+    if (n == 0) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    }
+    return n;
+}
+
+void grouped_gemm(const CUtensorMap& tmap_a, const CUtensorMap& tmap_b, const GroupedArgs& args, bool swiglu,
+                  int grid, cudaStream_t stream) {
+    constexpr int BN = 256;
+    if (args.n % BN != 0 || args.k % kBK != 0) {
+        throw kiwi::error("grouped_gemm: N must be a multiple of 256 and K of 64");
+    }
+    const int smem = Smem<BN>::kBytes;
+    if (grid <= 0) grid = num_sms();
+    if (swiglu) {
+        static bool attr = false;
+        if (!attr) {
+            KIWI_CUDA_CHECK(cudaFuncSetAttribute(grouped_gemm_kernel<BN, true>,
+                                                 cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+            attr = true;
+        }
+        grouped_gemm_kernel<BN, true><<<grid, kThreads, smem, stream>>>(tmap_a, tmap_b, args);
+    } else {
+        static bool attr = false;
+        if (!attr) {
+            KIWI_CUDA_CHECK(cudaFuncSetAttribute(grouped_gemm_kernel<BN, false>,
+                                                 cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+            attr = true;
+        }
+        grouped_gemm_kernel<BN, false><<<grid, kThreads, smem, stream>>>(tmap_a, tmap_b, args);
+    }
+    KIWI_CUDA_CHECK(cudaGetLastError());
+}
+
+KernelInfo gemm_kernel_info(bool swiglu) {
+    cudaFuncAttributes a{};
+    if (swiglu) KIWI_CUDA_CHECK(cudaFuncGetAttributes(&a, grouped_gemm_kernel<256, true>));
+    else KIWI_CUDA_CHECK(cudaFuncGetAttributes(&a, grouped_gemm_kernel<256, false>));
+    return {static_cast<int>(a.localSizeBytes), a.numRegs, Smem<256>::kBytes};
+}
+
+}  // namespace kiwi::gemm

@@ -25,6 +25,7 @@ using namespace kiwi;
 
 void register_p2p(py::module_& m);
 void register_ep(py::module_& m);
+void register_ops(py::module_& m);
 
 namespace {
 
@@ -336,7 +337,8 @@ PYBIND11_MODULE(_C, m) {
     };
     b.def("invoke_rtt",
           [rtt_to_dict](uint64_t iters, uint64_t warmup, uint32_t bytes, uint64_t seed, int cpu, uint64_t cap,
-                        bool mpsc, uint32_t poll_warps, uint64_t timeout_ns) {
+                        bool mpsc, uint32_t poll_warps, uint64_t timeout_ns, bool mailbox, uint32_t stagger_ns,
+                        uint32_t initial_delay_ns, uint32_t pipeline, bool adaptive) {
               bench::RttConfig c;
               c.iters = iters;
               c.warmup = warmup;
@@ -347,6 +349,11 @@ PYBIND11_MODULE(_C, m) {
               c.mpsc = mpsc;
               c.poll_warps = poll_warps;
               c.timeout_ns = timeout_ns;
+              c.mailbox = mailbox;
+              c.stagger_ns = stagger_ns;
+              c.initial_delay_ns = initial_delay_ns;
+              c.pipeline = pipeline;
+              c.adaptive = adaptive;
               bench::RttResult r;
               {
                   py::gil_scoped_release nogil;
@@ -356,7 +363,8 @@ PYBIND11_MODULE(_C, m) {
           },
           py::arg("iters") = 100000, py::arg("warmup") = 10000, py::arg("payload_bytes") = 8, py::arg("seed") = 1,
           py::arg("cpu") = -1, py::arg("capacity") = 4096, py::arg("mpsc") = false, py::arg("poll_warps") = 0,
-          py::arg("timeout_ns") = 2000000000ull);
+          py::arg("timeout_ns") = 2000000000ull, py::arg("mailbox") = false, py::arg("stagger_ns") = 200,
+          py::arg("initial_delay_ns") = 300, py::arg("pipeline") = 1, py::arg("adaptive") = true);
     b.def("pcie_floor",
           [rtt_to_dict](uint64_t iters, uint64_t warmup, int cpu, uint64_t timeout_ns) {
               bench::RttResult r;
@@ -368,6 +376,20 @@ PYBIND11_MODULE(_C, m) {
           },
           py::arg("iters") = 100000, py::arg("warmup") = 10000, py::arg("cpu") = -1,
           py::arg("timeout_ns") = 2000000000ull);
+
+    b.def("rtt_lab",
+          [rtt_to_dict](uint64_t iters, uint64_t warmup, uint32_t pollers, uint32_t mirrors, uint32_t stagger,
+                        uint32_t fence, uint32_t pipeline, int cpu, uint32_t delay) {
+              bench::RttResult r;
+              {
+                  py::gil_scoped_release nogil;
+                  r = bench::rtt_lab(iters, warmup, pollers, mirrors, stagger, fence, pipeline, cpu, delay);
+              }
+              return rtt_to_dict(r);
+          },
+          py::arg("iters") = 100000, py::arg("warmup") = 10000, py::arg("pollers") = 0, py::arg("mirrors") = 1,
+          py::arg("stagger_ns") = 0, py::arg("fence") = 0, py::arg("pipeline") = 1, py::arg("cpu") = -1,
+          py::arg("initial_delay_ns") = 0);
 
     auto push_to_dict = [](const bench::PushTestResult& r) {
         py::dict d;
@@ -438,4 +460,5 @@ PYBIND11_MODULE(_C, m) {
 
     register_p2p(m);
     register_ep(m);
+    register_ops(m);
 }

@@ -1,0 +1,93 @@
+// Python bindings of the sm_100a compute ops (kiwi_b200._C.ops).
+#include <ATen/cuda/CUDAContext.h>
+#include <pybind11/pybind11.h>
+#include <pybind11/stl.h>
+#include <torch/extension.h>
+
+#include "kiwi/gemm/grouped_gemm.hpp"
+
+namespace py = pybind11;
+using namespace kiwi;
+
+namespace {
+
+cudaStream_t cur_stream() { return at::cuda::getCurrentCUDAStream().stream(); }
+
+/// A grouped GEMM bound to fixed A and B buffers (their tensor maps are built once).
+class GroupedGemm {
+public:
+    GroupedGemm(torch::Tensor a, torch::Tensor b, int64_t num_groups)
+        : a_(a), b_(b), num_groups_(static_cast<int>(num_groups)) {
+        TORCH_CHECK(a.is_cuda() && b.is_cuda(), "A and B must be CUDA tensors");
+        TORCH_CHECK(a.scalar_type() == torch::kBFloat16 && b.scalar_type() == torch::kBFloat16, "bf16 only");
+        TORCH_CHECK(a.dim() == 2 && b.dim() == 2 && a.is_contiguous() && b.is_contiguous(), "2-D contiguous");
+        TORCH_CHECK(a.size(1) == b.size(1), "A and B must share K");
+        TORCH_CHECK(b.size(0) % num_groups == 0, "B rows must be num_groups * N");
+        k_ = static_cast<int>(a.size(1));
+        n_ = static_cast<int>(b.size(0) / num_groups);
+        TORCH_CHECK(k_ % 64 == 0 && n_ % 256 == 0, "K % 64 == 0 and N % 256 == 0 required");
+        tmap_a_ = gemm::make_tmap_bf16_2d(a.data_ptr(), a.size(0), k_, 128);
+        tmap_b_ = gemm::make_tmap_bf16_2d(b.data_ptr(), b.size(0), k_, 256);
+        auto iopts = torch::TensorOptions().dtype(torch::kInt32).device(a.device());
+        offsets_ = torch::zeros({num_groups_ + 1}, iopts);
+        tile_prefix_ = torch::zeros({num_groups_ + 1}, iopts);
+        error_ = torch::zeros({1}, iopts);
+    }
+
+    /// counts: int32[G] rows per group (device); out: bf16 [rows, N] or [rows, N/2] with swiglu.
+    void run(torch::Tensor counts, torch::Tensor out, bool swiglu, py::object row_scale, int grid) {
+        TORCH_CHECK(counts.is_cuda() && counts.scalar_type() == torch::kInt32 && counts.numel() == num_groups_,
+                    "counts must be int32[num_groups] on the device");
+        TORCH_CHECK(out.scalar_type() == torch::kBFloat16 && out.is_contiguous(), "out must be contiguous bf16");
+        TORCH_CHECK(out.size(1) == (swiglu ? n_ / 2 : n_), "out has the wrong number of columns");
+        TORCH_CHECK(out.size(0) >= a_.size(0), "out needs at least as many rows as A");
+        const float* rs = nullptr;
+        if (!row_scale.is_none()) {
+            torch::Tensor t = row_scale.cast<torch::Tensor>();
+            TORCH_CHECK(t.scalar_type() == torch::kFloat32 && t.is_cuda(), "row_scale must be fp32 CUDA");
+            rs = t.data_ptr<float>();
+            row_scale_ref_ = t;
+        }
+        cudaStream_t s = cur_stream();
+        gemm::build_schedule(counts.data_ptr<int32_t>(), num_groups_, n_, 256, offsets_.data_ptr<int32_t>(),
+                             tile_prefix_.data_ptr<int32_t>(), s);
+        gemm::GroupedArgs args{};
+        args.group_offset = offsets_.data_ptr<int32_t>();
+        args.tile_prefix = tile_prefix_.data_ptr<int32_t>();
+        args.num_groups = num_groups_;
+        args.n = n_;
+        args.k = k_;
+        args.c = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
+        args.ldc = out.size(1);
+        args.row_scale = rs;
+        args.error = reinterpret_cast<uint32_t*>(error_.data_ptr<int32_t>());
+        gemm::grouped_gemm(tmap_a_, tmap_b_, args, swiglu, grid, s);
+    }
+
+    torch::Tensor offsets() const { return offsets_; }
+    torch::Tensor tile_prefix() const { return tile_prefix_; }
+    torch::Tensor error() const { return error_; }
+
+private:
+    torch::Tensor a_, b_, offsets_, tile_prefix_, error_, row_scale_ref_;
+    int num_groups_, n_, k_;
+    CUtensorMap tmap_a_, tmap_b_;
+};
+
+}  // namespace
+
+void register_ops(py::module_& m) {
+    auto o = m.def_submodule("ops", "sm_100a compute kernels");
+    py::class_<GroupedGemm>(o, "GroupedGemm")
+        .def(py::init<torch::Tensor, torch::Tensor, int64_t>(), py::arg("a"), py::arg("b"), py::arg("num_groups"))
+        .def("run", &GroupedGemm::run, py::arg("counts"), py::arg("out"), py::arg("swiglu") = false,
+             py::arg("row_scale") = py::none(), py::arg("grid") = 0)
+        .def_property_readonly("offsets", &GroupedGemm::offsets)
+        .def_property_readonly("tile_prefix", &GroupedGemm::tile_prefix)
+        .def_property_readonly("error", &GroupedGemm::error);
+    o.def("gemm_kernel_info", [](bool swiglu) {
+        const auto i = gemm::gemm_kernel_info(swiglu);
+        return py::make_tuple(i.local_bytes, i.registers, i.smem_bytes);
+    });
+    o.def("num_sms", &gemm::num_sms);
+}

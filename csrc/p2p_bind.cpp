@@ -1,0 +1,119 @@
+// Python bindings of kiwi::p2p: symmetric heap, FD exchange, P2P kernels.
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAStream.h>
+#include <pybind11/functional.h>
+#include <pybind11/pybind11.h>
+#include <pybind11/stl.h>
+#include <torch/extension.h>
+#include <unistd.h>
+
+#include "kiwi/p2p/heap.hpp"
+#include "kiwi/p2p/p2p_ops.hpp"
+
+namespace py = pybind11;
+using namespace kiwi;
+using namespace kiwi::p2p;
+
+namespace {
+cudaStream_t cur_stream() { return at::cuda::getCurrentCUDAStream().stream(); }
+
+torch::Tensor view_tensor(void* base, uint64_t heap_size, int device, uint64_t offset, std::vector<int64_t> shape,
+                          torch::Dtype dtype) {
+    int64_t numel = 1;
+    for (auto d : shape) numel *= d;
+    const uint64_t bytes = static_cast<uint64_t>(numel) * c10::elementSize(dtype);
+    if (offset + bytes > heap_size) throw kiwi::error("kiwi::p2p: tensor view exceeds the heap");
+    auto opts = torch::TensorOptions().dtype(dtype).device(torch::kCUDA, device);
+    return torch::from_blob(static_cast<uint8_t*>(base) + offset, shape, opts);
+}
+
+uint64_t* u64_ptr(const torch::Tensor& t) {
+    TORCH_CHECK(t.is_cuda() && t.scalar_type() == torch::kInt64, "expected a CUDA int64 tensor");
+    return reinterpret_cast<uint64_t*>(t.data_ptr<int64_t>());
+}
+uint32_t* u32_ptr(const torch::Tensor& t) {
+    TORCH_CHECK(t.is_cuda() && t.scalar_type() == torch::kInt32, "expected a CUDA int32 tensor");
+    return reinterpret_cast<uint32_t*>(t.data_ptr<int32_t>());
+}
+}  // namespace
+
+void register_p2p(py::module_& m) {
+    auto p = m.def_submodule("p2p", "kiwi::p2p (NVLink peer memory)");
+    p.attr("MAX_RANKS") = kMaxRanks;
+    p.def("exchange_fds", &exchange_fds, py::arg("job"), py::arg("rank"), py::arg("world"), py::arg("fd"),
+          py::arg("timeout_s") = 60.0, py::call_guard<py::gil_scoped_release>());
+    p.def("broadcast_fd", &broadcast_fd, py::arg("job"), py::arg("rank"), py::arg("world"), py::arg("root"),
+          py::arg("fd"), py::arg("timeout_s") = 60.0, py::call_guard<py::gil_scoped_release>());
+    p.def("multicast_supported", &SymmetricHeap::multicast_supported);
+
+    py::class_<SymmetricHeap>(p, "SymmetricHeap")
+        .def(py::init([](int device, size_t bytes, int rank, int world, const std::string& job, bool mc,
+                         py::object barrier) {
+                 SymmetricHeap::Barrier b;
+                 if (!barrier.is_none()) {
+                     auto fn = std::make_shared<py::object>(barrier);
+                     b = [fn] {
+                         py::gil_scoped_acquire g;
+                         (*fn)();
+                     };
+                 }
+                 py::gil_scoped_release nogil;
+                 return new SymmetricHeap(device, bytes, rank, world, job, mc, b);
+             }),
+             py::arg("device"), py::arg("bytes"), py::arg("rank"), py::arg("world"), py::arg("job"),
+             py::arg("multicast") = false, py::arg("barrier") = py::none())
+        .def_property_readonly("size", &SymmetricHeap::size)
+        .def_property_readonly("rank", &SymmetricHeap::rank)
+        .def_property_readonly("world", &SymmetricHeap::world)
+        .def_property_readonly("local_ptr", [](SymmetricHeap& h) { return reinterpret_cast<uintptr_t>(h.local()); })
+        .def_property_readonly("mc_ptr", [](SymmetricHeap& h) { return reinterpret_cast<uintptr_t>(h.multicast()); })
+        .def("peer_ptr", [](SymmetricHeap& h, int r) { return reinterpret_cast<uintptr_t>(h.peer(r)); })
+        .def("tensor",
+             [](SymmetricHeap& h, uint64_t offset, std::vector<int64_t> shape, torch::Dtype dtype) {
+                 int dev = 0;
+                 cudaGetDevice(&dev);
+                 return view_tensor(h.local(), h.size(), dev, offset, shape, dtype);
+             },
+             "View of this rank's heap memory (local only).")
+        .def("pingpong",
+             [](SymmetricHeap& h, int peer, bool initiator, uint64_t bytes, uint64_t iters, uint64_t warmup,
+                uint64_t src_off, uint64_t dst_off, uint64_t flag_off, torch::Tensor lat, torch::Tensor status,
+                uint32_t max_blocks, uint64_t timeout_ns) {
+                 launch_pingpong(h.view(), peer, initiator, bytes, iters, warmup, src_off, dst_off, flag_off,
+                                 u64_ptr(lat), u32_ptr(status), max_blocks, timeout_ns, cur_stream());
+             })
+        .def("put_bw",
+             [](SymmetricHeap& h, int peer, bool sender, uint64_t bytes, uint64_t reps, uint64_t src_off,
+                uint64_t dst_off, uint64_t flag_off, uint64_t round, torch::Tensor elapsed, torch::Tensor status,
+                uint32_t max_blocks, uint64_t timeout_ns) {
+                 launch_put_bw(h.view(), peer, sender, bytes, reps, src_off, dst_off, flag_off, round,
+                               u64_ptr(elapsed), u32_ptr(status), max_blocks, timeout_ns, cur_stream());
+             })
+        .def("get",
+             [](SymmetricHeap& h, int peer, uint64_t bytes, uint64_t reps, uint64_t src_off, uint64_t dst_off,
+                torch::Tensor lat, uint32_t max_blocks) {
+                 launch_get(h.view(), peer, bytes, reps, src_off, dst_off, u64_ptr(lat), max_blocks, cur_stream());
+             })
+        .def("all_pairs",
+             [](SymmetricHeap& h, uint64_t data_off, uint64_t flag_off, uint64_t words, uint32_t round,
+                torch::Tensor status, uint64_t timeout_ns) {
+                 launch_all_pairs(h.view(), data_off, flag_off, words, round, u32_ptr(status), timeout_ns,
+                                  cur_stream());
+             })
+        .def("mc_broadcast",
+             [](SymmetricHeap& h, int root, uint64_t src_off, uint64_t dst_off, uint64_t bytes, uint64_t flag_off) {
+                 launch_mc_broadcast(h.view(), root, src_off, dst_off, bytes, flag_off, cur_stream());
+             })
+        .def("mc_allreduce_f32",
+             [](SymmetricHeap& h, uint64_t off, uint64_t count) {
+                 launch_mc_allreduce_f32(h.view(), off, count, cur_stream());
+             })
+        .def("wait_flag",
+             [](SymmetricHeap& h, uint64_t flag_off, uint64_t want, torch::Tensor status, uint64_t timeout_ns) {
+                 launch_wait_flag(h.view(), flag_off, want, u32_ptr(status), timeout_ns, cur_stream());
+             })
+        .def("barrier",
+             [](SymmetricHeap& h, uint64_t flag_off, uint64_t round, torch::Tensor status, uint64_t timeout_ns) {
+                 launch_heap_barrier(h.view(), flag_off, round, u32_ptr(status), timeout_ns, cur_stream());
+             });
+}

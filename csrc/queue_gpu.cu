@@ -15,6 +15,7 @@
 #include "kiwi/bench/gpu_bench.hpp"
 #include "kiwi/bench/host_bench.hpp"
 #include "kiwi/invoke/invoke.hpp"
+#include "kiwi/queue/mailbox.cuh"
 #include "kiwi/ptx.cuh"
 #include "kiwi/topology.hpp"
 
@@ -94,7 +95,7 @@ __global__ void __launch_bounds__(256) invoke_rtt_kernel(
     DeviceContext<Q>* ctx, SpscH2DHandle reply, uint8_t cb, uint64_t iters, uint64_t warmup,
     uint32_t bytes, uint64_t* payload_buf, uint64_t seed, uint64_t* lat_ns, uint32_t* lat_cyc,
     uint64_t* totals, uint32_t* status, uint32_t poll_warps, uint64_t stagger_ns,
-    uint64_t timeout_ns, volatile uint32_t* done) {
+    uint64_t timeout_ns, volatile uint32_t* done, MailboxHandle mbox, uint32_t use_mailbox) {
     __shared__ RttShared sh;
     const uint32_t warp = threadIdx.x / 32;
     const uint32_t lane = ptx::lane_id();
@@ -135,6 +136,7 @@ __global__ void __launch_bounds__(256) invoke_rtt_kernel(
     }
 
     auto h = ctx->get_device_handle(0);
+    MailboxHandle mb = mbox;  // local copy: the adaptive delay lives in registers
     uint64_t s = seed ? seed : 0x9E3779B97F4A7C15ull;
     uint32_t st = 0;
     bool ok = true;
@@ -152,11 +154,34 @@ __global__ void __launch_bounds__(256) invoke_rtt_kernel(
         }
         const uint64_t t0 = ptx::globaltimer();
         const uint64_t c0 = ptx::clock64();
-        if (bytes == 8) {
-            while (!h.invoke(cb, x)) {
+        if (use_mailbox) {
+            // The public call/return path: invoke(seq, x) + mirrored mailbox reply.
+            uint64_t w = 0;
+            const uint32_t seq = static_cast<uint32_t>(i + 1);
+            const Status cs = bytes == 8 ? h.call(cb, mb, seq, w, timeout_ns, x)
+                                         : Status::kBadArgument;
+            const uint64_t t1 = ptx::globaltimer();
+            const uint64_t c1 = ptx::clock64();
+            if (cs != Status::kOk) {
+                st = static_cast<uint32_t>(cs);
+                break;
             }
-        } else {
-            while (!h.invoke_global(cb, payload_buf, bytes)) {
+            if (w != x + 1) ok = false;
+            if (i >= warmup && lane == 0) {
+                lat_ns[i - warmup] = t1 - t0;
+                lat_cyc[i - warmup] = static_cast<uint32_t>(c1 - c0);
+            }
+            continue;
+        }
+        {
+            ptx::Deadline pdl(timeout_ns);
+            bool pushed = false;
+            while (!(pushed = (bytes == 8 ? h.invoke(cb, x) : h.invoke_global(cb, payload_buf, bytes)))) {
+                if (pdl.expired()) break;
+            }
+            if (!pushed) {
+                st = static_cast<uint32_t>(Status::kTimeout);
+                break;
             }
         }
         uint64_t w = 0;
@@ -217,8 +242,15 @@ static RttResult run_invoke_rtt(const RttConfig& cfg) {
     if (cfg.poll_warps > 7) throw kiwi::error("invoke_rtt: poll_warps must be <= 7");
     kiwi::invoke::Context<Q> ctx(1, cfg.capacity, MemKind::kMappedPinned);
     SPSCH2DQueue reply(64, MemKind::kMappedPinned);
+    ReplyMailbox mailbox(MemKind::kMappedPinned, cfg.stagger_ns, cfg.initial_delay_ns, cfg.pipeline, cfg.adaptive);
     uint64_t callbacks = 0;
-    const uint8_t cb = ctx.register_raw_callback(
+    if (cfg.mailbox && cfg.payload_bytes != 8) throw kiwi::error("invoke_rtt: the mailbox path sends 8-byte payloads");
+    const uint8_t cb = cfg.mailbox ? ctx.register_call(std::function<uint64_t(uint64_t)>([&](uint64_t v) {
+                                                           ++callbacks;
+                                                           return v + 1;
+                                                       }),
+                                                       mailbox)
+                                   : ctx.register_raw_callback(
         [&](const uint8_t* p, uint32_t n) {
             uint64_t v;
             std::memcpy(&v, p, 8);
@@ -227,6 +259,7 @@ static RttResult run_invoke_rtt(const RttConfig& cfg) {
             ++callbacks;
         },
         cfg.payload_bytes);
+    if (cfg.mailbox && cfg.poll_warps) throw kiwi::error("invoke_rtt: poll_warps applies to ring replies only");
 
     DevBuf<uint64_t> payload(kMaxMessageBytes / 8);
     {
@@ -244,11 +277,12 @@ static RttResult run_invoke_rtt(const RttConfig& cfg) {
 
     const int cpu = pick_cpu(cfg.cpu);
     if (cpu >= 0) topology::bind_current_thread({cpu});
-    const uint32_t threads = 32 * (1 + cfg.poll_warps);
+    const uint32_t threads = 32 * (1 + (cfg.mailbox ? 0 : cfg.poll_warps));
     invoke_rtt_kernel<Q><<<1, threads, 0, stream>>>(
         ctx.device_context(), reply.device_handle(), cb, cfg.iters, cfg.warmup, cfg.payload_bytes,
         payload.p, cfg.seed, lat.p, cyc.p, totals.p, status.p, cfg.poll_warps,
-        /*stagger_ns=*/cfg.poll_warps ? 800 / cfg.poll_warps : 0, cfg.timeout_ns, done.p);
+        /*stagger_ns=*/cfg.poll_warps ? 800 / cfg.poll_warps : 0, cfg.timeout_ns, done.p, mailbox.device_handle(),
+        cfg.mailbox ? 1u : 0u);
     KIWI_CUDA_CHECK(cudaGetLastError());
 
     auto poll = ctx.poll_state(0);
@@ -377,6 +411,166 @@ RttResult pcie_floor(uint64_t iters, uint64_t warmup, int cpu, uint64_t timeout_
     return r;
 }
 
+
+// ---------------------------------------------------------------------------
+// Round-trip protocol lab: measures store-and-poll variants so the invoke
+// reply path can use the fastest one on this platform.
+//   pollers   warps polling the host ack (0: the storing thread polls itself)
+//   mirrors   the host writes the ack to this many separate 128-byte lines;
+//             poller p reads line p % mirrors
+//   stagger   ns between pollers' first reads (then free-running)
+//   fence     fence.sc.sys after the GPU's store
+//   pipeline  one thread keeps `pipeline` loads in flight (staggered)
+// ---------------------------------------------------------------------------
+
+struct LabShared {
+    unsigned long long found;
+    uint32_t stop;
+};
+
+__global__ void __launch_bounds__(288) rtt_lab_kernel(uint64_t* d2h, const uint64_t* acks, uint32_t mirrors,
+                                                     uint64_t iters, uint64_t warmup, uint64_t* lat_ns,
+                                                     uint32_t* lat_cyc, uint64_t* totals, uint32_t* status,
+                                                     uint32_t pollers, uint32_t stagger_ns, uint32_t fence,
+                                                     uint32_t pipeline, uint64_t timeout_ns, uint32_t initial_delay_ns) {
+    __shared__ LabShared sh;
+    const uint32_t warp = threadIdx.x / 32;
+    const uint32_t lane = ptx::lane_id();
+    if (threadIdx.x == 0) {
+        sh.found = 0;
+        sh.stop = 0;
+    }
+    __syncthreads();
+    if (warp > 0) {
+        if (lane != 0) return;
+        const uint32_t p = warp - 1;
+        const uint64_t* a = acks + static_cast<uint64_t>(p % mirrors) * 16;
+        const uint64_t t_start = ptx::globaltimer() + static_cast<uint64_t>(stagger_ns) * p;
+        while (ptx::globaltimer() < t_start) {
+        }
+        while (!*reinterpret_cast<volatile uint32_t*>(&sh.stop)) {
+            const uint64_t v = ptx::ld_volatile_u64(a);
+            if (v > *reinterpret_cast<volatile unsigned long long*>(&sh.found)) atomicMax(&sh.found, v);
+        }
+        return;
+    }
+    if (lane != 0) return;
+    uint64_t t_begin = 0, c_begin = 0;
+    for (uint64_t i = 0; i < iters + warmup; ++i) {
+        if (i == warmup) {
+            t_begin = ptx::globaltimer();
+            c_begin = ptx::clock64();
+        }
+        const uint64_t want = i + 1;
+        const uint64_t t0 = ptx::globaltimer();
+        const uint64_t c0 = ptx::clock64();
+        ptx::st_volatile_u64(d2h, want);
+        if (fence) ptx::fence_sys();
+        if (initial_delay_ns) {
+            const uint64_t td = ptx::globaltimer();
+            while (ptx::globaltimer() < td + initial_delay_ns) {
+            }
+        }
+        ptx::Deadline dl(timeout_ns);
+        bool ok = true;
+        if (pollers > 0) {
+            while (*reinterpret_cast<volatile unsigned long long*>(&sh.found) < want) {
+                if (dl.expired()) { ok = false; break; }
+            }
+        } else if (pipeline <= 1) {
+            while (ptx::ld_volatile_u64(acks) < want) {
+                if (dl.expired()) { ok = false; break; }
+            }
+        } else {
+            // Keep `pipeline` (<= 4) loads in flight, each issued stagger_ns apart.
+            const uint64_t* a0 = acks;
+            const uint64_t* a1 = acks + (1 % mirrors) * 16;
+            const uint64_t* a2 = acks + (2 % mirrors) * 16;
+            const uint64_t* a3 = acks + (3 % mirrors) * 16;
+            uint64_t v0 = ptx::ld_volatile_u64(a0), v1 = 0, v2 = 0, v3 = 0;
+            uint64_t t = ptx::globaltimer();
+            while (ptx::globaltimer() < t + stagger_ns) {}
+            v1 = ptx::ld_volatile_u64(a1);
+            if (pipeline > 2) { t = ptx::globaltimer(); while (ptx::globaltimer() < t + stagger_ns) {} v2 = ptx::ld_volatile_u64(a2); }
+            if (pipeline > 3) { t = ptx::globaltimer(); while (ptx::globaltimer() < t + stagger_ns) {} v3 = ptx::ld_volatile_u64(a3); }
+            while (true) {
+                if (v0 >= want) break;
+                v0 = ptx::ld_volatile_u64(a0);
+                if (v1 >= want) break;
+                v1 = ptx::ld_volatile_u64(a1);
+                if (pipeline > 2) { if (v2 >= want) break; v2 = ptx::ld_volatile_u64(a2); }
+                if (pipeline > 3) { if (v3 >= want) break; v3 = ptx::ld_volatile_u64(a3); }
+                if (dl.expired()) { ok = false; break; }
+            }
+        }
+        const uint64_t t1 = ptx::globaltimer();
+        const uint64_t c1 = ptx::clock64();
+        if (!ok) {
+            status[0] = static_cast<uint32_t>(Status::kTimeout);
+            break;
+        }
+        if (i >= warmup) {
+            lat_ns[i - warmup] = t1 - t0;
+            lat_cyc[i - warmup] = static_cast<uint32_t>(c1 - c0);
+        }
+    }
+    totals[0] = ptx::globaltimer() - t_begin;
+    totals[1] = ptx::clock64() - c_begin;
+    status[1] = 1;
+    *reinterpret_cast<volatile uint32_t*>(&sh.stop) = 1;
+    ptx::fence_sys();
+    ptx::st_volatile_u64(d2h, ~0ull);
+}
+
+RttResult rtt_lab(uint64_t iters, uint64_t warmup, uint32_t pollers, uint32_t mirrors, uint32_t stagger_ns,
+                  uint32_t fence, uint32_t pipeline, int cpu, uint32_t initial_delay_ns) {
+    if (pollers > 8 || mirrors == 0 || mirrors > 8 || pipeline > 4) throw kiwi::error("rtt_lab: bad arguments");
+    detail::Block words(64 + 8 * 128, MemKind::kMappedPinned);
+    volatile uint64_t* d2h = words.as<volatile uint64_t>();
+    volatile uint64_t* acks = words.as<volatile uint64_t>() + 8;  // ack mirror m at acks[16 * m]
+    DevBuf<uint64_t> lat(iters);
+    DevBuf<uint32_t> cyc(iters);
+    DevBuf<uint64_t> totals(2);
+    DevBuf<uint32_t> status(2);
+    cudaStream_t stream;
+    KIWI_CUDA_CHECK(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking));
+    const int c = pick_cpu(cpu);
+    if (c >= 0) topology::bind_current_thread({c});
+    rtt_lab_kernel<<<1, 32 * (1 + pollers), 0, stream>>>(
+        const_cast<uint64_t*>(d2h), const_cast<uint64_t*>(acks), mirrors, iters, warmup, lat.p, cyc.p, totals.p,
+        status.p, pollers, stagger_ns, fence, pipeline, 2000000000ull, initial_delay_ns);
+    KIWI_CUDA_CHECK(cudaGetLastError());
+    uint64_t expect = 1, idle = 0;
+    while (true) {
+        const uint64_t v = *d2h;
+        if (v == ~0ull) break;
+        if (v == expect) {
+            for (uint32_t m = 0; m < mirrors; ++m) acks[16 * m] = v;
+            ++expect;
+            idle = 0;
+        } else if ((++idle & 0xfffff) == 0 && cudaStreamQuery(stream) != cudaErrorNotReady) {
+            break;
+        }
+    }
+    KIWI_CUDA_CHECK(cudaStreamSynchronize(stream));
+    cudaStreamDestroy(stream);
+    RttResult r;
+    r.lat_ns.resize(iters);
+    std::vector<uint32_t> c32(iters);
+    uint64_t tot[2];
+    uint32_t stv[2];
+    KIWI_CUDA_CHECK(cudaMemcpy(r.lat_ns.data(), lat.p, iters * 8, cudaMemcpyDeviceToHost));
+    KIWI_CUDA_CHECK(cudaMemcpy(c32.data(), cyc.p, iters * 4, cudaMemcpyDeviceToHost));
+    KIWI_CUDA_CHECK(cudaMemcpy(tot, totals.p, sizeof(tot), cudaMemcpyDeviceToHost));
+    KIWI_CUDA_CHECK(cudaMemcpy(stv, status.p, sizeof(stv), cudaMemcpyDeviceToHost));
+    r.lat_cycles.assign(c32.begin(), c32.end());
+    r.total_ns = tot[0];
+    r.total_cycles = tot[1];
+    r.status = stv[0];
+    r.ok = stv[0] == 0 && stv[1] == 1;
+    return r;
+}
+
 // ---------------------------------------------------------------------------
 // Device-to-host push correctness
 // ---------------------------------------------------------------------------
@@ -392,12 +586,39 @@ struct RegMsg {
     uint8_t b[S];
 };
 
+/// Fills a register message byte pattern with fully unrolled stores so the
+/// object stays in registers (a runtime-indexed loop would put it in local memory).
+template <uint32_t S>
+KIWI_DEV void fill_reg_msg(RegMsg<S>& m, uint64_t seed, uint64_t id) {
+#pragma unroll
+    for (uint32_t w = 0; w < (S + 7) / 8; ++w) {
+        const uint64_t v = pattern_word(seed, id, w);
+#pragma unroll
+        for (uint32_t k = 0; k < 8; ++k) {
+            if (w * 8 + k < S) m.b[w * 8 + k] = static_cast<uint8_t>(v >> (8 * k));
+        }
+    }
+}
+
 KIWI_DEV void fill_words(uint64_t* dst, uint64_t seed, uint64_t msg, uint32_t nwords) {
     for (uint32_t k = ptx::lane_id(); k < nwords; k += 32) dst[k] = pattern_word(seed, msg, k);
 }
 
 /// Message id of warp w, sequence s: unique across warps.
 KIWI_HD uint64_t msg_id(uint32_t w, uint64_t s) { return (static_cast<uint64_t>(w) << 32) | s; }
+
+/// Retries a push until it succeeds or `timeout_ns` passes (then records kTimeout).
+template <typename H, typename F>
+KIWI_DEV bool push_bounded(H& h, F&& push, uint64_t timeout_ns = 2000000000ull) {
+    ptx::Deadline dl(timeout_ns);
+    while (!push()) {
+        if (dl.expired()) {
+            dev::report(h.err, Status::kTimeout, site_d2h_push, 0);
+            return false;
+        }
+    }
+    return true;
+}
 
 template <typename H, int MODE, uint32_t REG_BYTES>
 __global__ void __launch_bounds__(128) d2h_push_kernel(H* handles, uint32_t msgs, const uint32_t* sizes,
@@ -415,21 +636,16 @@ __global__ void __launch_bounds__(128) d2h_push_kernel(H* handles, uint32_t msgs
             const uint32_t bytes = sizes[seq % nsizes];
             fill_words(buf, seed, id, (bytes + 7) / 8);
             __syncwarp();
-            while (!h.push_global(buf, bytes, meta)) {
-            }
+            if (!push_bounded(h, [&] { return h.push_global(buf, bytes, meta); })) return;
             __syncwarp();
         } else if constexpr (MODE == kModeLanes) {
             const uint32_t bytes = sizes[seq % nsizes];
             const uint64_t w = pattern_word(seed, id, lane);
-            while (!h.push_lanes(w, bytes, meta)) {
-            }
+            if (!push_bounded(h, [&] { return h.push_lanes(w, bytes, meta); })) return;
         } else if constexpr (MODE == kModeReg) {
             RegMsg<REG_BYTES> m;
-            for (uint32_t k = 0; k < REG_BYTES; ++k) {
-                m.b[k] = static_cast<uint8_t>(pattern_word(seed, id, k / 8) >> (8 * (k % 8)));
-            }
-            while (!h.push_reg(m, meta)) {
-            }
+            fill_reg_msg(m, seed, id);
+            if (!push_bounded(h, [&] { return h.push_reg(m, meta); })) return;
         } else {
             // Each lane pushes its own message; lane-specific id and size.
             const uint64_t lid = msg_id(warp, seq * 32 + lane);
@@ -439,8 +655,7 @@ __global__ void __launch_bounds__(128) d2h_push_kernel(H* handles, uint32_t msgs
 #pragma unroll
             for (uint32_t k = 0; k < 8; ++k) m.w[k] = pattern_word(seed, lid, k);
             const uint32_t lmeta = (warp << 20) | static_cast<uint32_t>((seq * 32 + lane) & 0xfffff);
-            while (!h.push_lane_masked(m, bytes, lmeta, active)) {
-            }
+            if (!push_bounded(h, [&] { return h.push_lane_masked(m, bytes, lmeta, active); })) return;
         }
     }
     if constexpr (std::is_same<H, SpscD2HHandle>::value) {

@@ -17,7 +17,12 @@ struct RttConfig {
     int cpu = -1;                  // host thread core (-1: GPU-local core chosen by caller)
     uint64_t capacity = 4096;      // request ring lines
     bool mpsc = false;             // use the MPSC request queue
-    uint32_t poll_warps = 1;       // warps polling the reply line (staggered)
+    uint32_t poll_warps = 1;       // ring replies: warps polling the reply line (staggered)
+    bool mailbox = true;           // replies through the mirrored ReplyMailbox (call/return API)
+    uint32_t stagger_ns = 200;     // mailbox: delay between the two in-flight polls
+    uint32_t initial_delay_ns = 300; // mailbox: (starting) delay before the first poll
+    uint32_t pipeline = 1;           // mailbox: polls in flight (1 or 2)
+    bool adaptive = true;            // mailbox: adapt the delay
     uint64_t timeout_ns = 2000000000ull;
 };
 
@@ -38,6 +43,10 @@ RttResult invoke_rtt(const RttConfig& cfg);
 /// Raw floor: the GPU stores a counter to host memory and polls a host word
 /// the CPU sets in reply.  No queue logic.
 RttResult pcie_floor(uint64_t iters, uint64_t warmup, int cpu, uint64_t timeout_ns);
+
+/// Store-and-poll protocol variants (see csrc/queue_gpu.cu rtt_lab_kernel).
+RttResult rtt_lab(uint64_t iters, uint64_t warmup, uint32_t pollers, uint32_t mirrors, uint32_t stagger_ns,
+                  uint32_t fence, uint32_t pipeline, int cpu, uint32_t initial_delay_ns = 0);
 
 struct PushTestResult {
     uint64_t popped = 0;

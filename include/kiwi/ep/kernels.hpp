@@ -1,0 +1,64 @@
+// kiwi::ep device workspace and kernel launchers (csrc/ep_kernels.cu).
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include "kiwi/ep/config.hpp"
+#include "kiwi/p2p/heap.hpp"
+
+namespace kiwi::ep {
+
+/// Rank-local device scratch of one EP layer (allocated by the owner).
+struct EpWorkspace {
+    uint32_t* epoch;          // [1] round counter, bumped by begin()
+    uint32_t* done_ctas;      // [4] last-CTA counters (dispatch, combine)
+    int32_t* expert_count;    // [experts_per_rank]
+    int32_t* cursor;          // [experts_per_rank]
+    int32_t* offsets;         // [experts_per_rank + 1]
+    int32_t* tiles1;          // [experts_per_rank + 1] tile prefix of GEMM1
+    int32_t* tiles2;          // [experts_per_rank + 1] tile prefix of GEMM2
+    int32_t* slot_tokens;     // [world] tokens each source sent this round
+    int32_t* pair_slot;       // [max_pairs] source slot of each expert row
+    float* pair_w;            // [max_pairs] routing weight of each expert row
+    int32_t* slot_pos;        // [slots * local_per_token] expert rows of a slot (-1 = none)
+    __nv_bfloat16* a;         // [max_pairs, hidden] dequantised expert-major rows
+    uint32_t* error;          // [4] {code, site, info, rank}
+};
+
+/// Error sites recorded in EpWorkspace::error[1].
+enum EpSite : uint32_t {
+    kSiteDispatchWait = 1,
+    kSiteCombineWait = 2,
+    kSiteCapacity = 3,
+};
+
+void launch_begin(const EpConfig& c, const EpWorkspace& ws, cudaStream_t s);
+
+/// Top-k routing with softmax over the selected logits (logits fp32 [T, E]).
+void launch_route(const float* logits, int tokens, int experts, int topk, int32_t* idx, float* w, cudaStream_t s);
+
+/// Quantises (per cfg.quant) and stores each token's row, scales and metadata
+/// into every destination rank's receive slot; the last CTA signals all ranks.
+void launch_dispatch(const EpConfig& c, const p2p::HeapView& h, const __nv_bfloat16* x, const int32_t* idx,
+                     const float* w, int tokens, const EpWorkspace& ws, int grid, cudaStream_t s);
+
+/// Waits for every source's dispatch flag and counts rows per local expert.
+void launch_recv_count(const EpConfig& c, const p2p::HeapView& h, const EpWorkspace& ws, uint64_t timeout_ns,
+                       cudaStream_t s);
+
+/// Assigns expert-major rows, records the slot -> rows map and dequantises
+/// each received row into ws.a.
+void launch_recv_scatter(const EpConfig& c, const p2p::HeapView& h, const EpWorkspace& ws, cudaStream_t s);
+
+/// Sums each slot's (already weighted) expert outputs y and stores the bf16
+/// row into the source rank's combine slot; the last CTA signals all ranks.
+void launch_combine_send(const EpConfig& c, const p2p::HeapView& h, const __nv_bfloat16* y, const EpWorkspace& ws,
+                         int grid, cudaStream_t s);
+
+/// Waits for every rank's combine flag and reduces the returned rows of each
+/// local token (over the ranks it was sent to) into out [T, hidden].
+void launch_combine_recv(const EpConfig& c, const p2p::HeapView& h, const int32_t* idx, int tokens,
+                         __nv_bfloat16* out, const EpWorkspace& ws, uint64_t timeout_ns, cudaStream_t s);
+
+}  // namespace kiwi::ep

@@ -1,0 +1,48 @@
+// Host API of the sm_100a grouped BF16 GEMM (csrc/gemm_sm100.cu).
+#pragma once
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "kiwi/common.hpp"
+
+namespace kiwi::gemm {
+
+struct GroupedArgs {
+    const int32_t* group_offset;  // [G + 1] device: first row of each group in A and C
+    const int32_t* tile_prefix;   // [G + 1] device: cumulative 128 x BN tiles per group
+    int32_t num_groups;
+    int32_t n;                    // B rows per group (C columns before SwiGLU halves them)
+    int32_t k;
+    int32_t pad_;
+    __nv_bfloat16* c;
+    int64_t ldc;                  // C row stride, elements
+    const float* row_scale;       // optional per-row factor applied in the epilogue
+    uint32_t* error;              // device word: non-zero if a bounded wait ran out
+};
+
+struct KernelInfo {
+    int local_bytes;
+    int registers;
+    int smem_bytes;
+};
+
+/// Tensor map of a row-major [rows, cols] bf16 matrix, box [box_rows, 64],
+/// 128-byte swizzle (the layout the kernel's shared-memory descriptors expect).
+CUtensorMap make_tmap_bf16_2d(const void* ptr, uint64_t rows, uint64_t cols, uint32_t box_rows);
+
+/// Builds group offsets and the tile prefix from per-group row counts (device).
+void build_schedule(const int32_t* counts, int num_groups, int n, int bn, int32_t* offsets, int32_t* tile_prefix,
+                    cudaStream_t stream);
+
+/// Launches the persistent grouped GEMM (BN = 256).  `grid` <= 0: one CTA per SM.
+void grouped_gemm(const CUtensorMap& tmap_a, const CUtensorMap& tmap_b, const GroupedArgs& args, bool swiglu,
+                  int grid, cudaStream_t stream);
+
+KernelInfo gemm_kernel_info(bool swiglu);
+int num_sms();
+
+}  // namespace kiwi::gemm

@@ -18,6 +18,7 @@
 
 #include "kiwi/invoke/serializer.hpp"
 #include "kiwi/queue/handles.cuh"
+#include "kiwi/queue/mailbox.cuh"
 
 namespace kiwi::invoke {
 
@@ -37,6 +38,21 @@ struct InvokeHandle {
         } p;
         ArgPack<Args...>::serialize(p.b, args...);
         return queue.push_reg(p, callback_id);
+    }
+
+    /// Call with a return value: sends (seq, args...) to a callback registered
+    /// with Context::register_call and waits (bounded) for its 8-byte result in
+    /// `mailbox`.  `seq` must be non-zero and differ from the previous call's on
+    /// this mailbox (a per-warp counter).  Returns kTimeout if the push or the
+    /// reply does not complete within `timeout_ns`.
+    template <typename... Args>
+    KIWI_DEV Status call(uint8_t callback_id, const queue::MailboxHandle& mailbox, uint32_t seq, uint64_t& result,
+                         uint64_t timeout_ns, const Args&... args) {
+        ptx::Deadline dl(timeout_ns);
+        while (!invoke(callback_id, seq, args...)) {
+            if (dl.expired()) return Status::kTimeout;
+        }
+        return mailbox.wait(seq, result, timeout_ns);
     }
 
     KIWI_DEV bool invoke_shared(uint8_t callback_id, const void* smem_args, uint32_t bytes) {

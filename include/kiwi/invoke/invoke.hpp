@@ -81,6 +81,18 @@ public:
         return registry_->add(std::make_unique<TypedCallback<Args...>>(std::move(fn)));
     }
 
+    /// Registers a callback with a return value for DeviceHandle::call(): the
+    /// message carries (seq, args...); the result is posted to `mailbox` under
+    /// `seq`.  The mailbox must outlive the context's use of the callback.
+    template <typename... Args>
+    uint8_t register_call(std::function<uint64_t(Args...)> fn, queue::ReplyMailbox& mailbox) {
+        queue::ReplyMailbox* mb = &mailbox;
+        std::function<void(uint32_t, Args...)> thunk = [fn = std::move(fn), mb](uint32_t seq, Args... args) {
+            mb->post(seq, fn(args...));
+        };
+        return register_callback<uint32_t, Args...>(std::move(thunk));
+    }
+
     /// Registers a byte-level callback.  `expected_bytes` = exact payload size,
     /// or CallbackBase::kAnySize to accept any size up to kMaxMessageBytes.
     uint8_t register_raw_callback(RawCallback::Fn fn, uint32_t expected_bytes) {

@@ -1,0 +1,35 @@
+// Host launchers for the kiwi::p2p kernels (csrc/p2p_gpu.cu).
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include "kiwi/p2p/heap.hpp"
+
+namespace kiwi::p2p {
+
+void launch_pingpong(const HeapView& h, int peer, bool initiator, uint64_t bytes, uint64_t iters, uint64_t warmup,
+                     uint64_t src_off, uint64_t dst_off, uint64_t flag_off, uint64_t* lat_ns, uint32_t* status,
+                     uint32_t max_blocks, uint64_t timeout_ns, cudaStream_t s);
+
+void launch_put_bw(const HeapView& h, int peer, bool sender, uint64_t bytes, uint64_t reps, uint64_t src_off,
+                   uint64_t dst_off, uint64_t flag_off, uint64_t round, uint64_t* elapsed, uint32_t* status,
+                   uint32_t max_blocks, uint64_t timeout_ns, cudaStream_t s);
+
+void launch_get(const HeapView& h, int peer, uint64_t bytes, uint64_t reps, uint64_t src_off, uint64_t dst_off,
+                uint64_t* lat_ns, uint32_t max_blocks, cudaStream_t s);
+
+void launch_all_pairs(const HeapView& h, uint64_t data_off, uint64_t flag_off, uint64_t words, uint32_t round,
+                      uint32_t* status, uint64_t timeout_ns, cudaStream_t s);
+
+void launch_mc_broadcast(const HeapView& h, int root, uint64_t src_off, uint64_t dst_off, uint64_t bytes,
+                         uint64_t flag_off, cudaStream_t s);
+
+void launch_mc_allreduce_f32(const HeapView& h, uint64_t off, uint64_t count, cudaStream_t s);
+
+void launch_wait_flag(const HeapView& h, uint64_t flag_off, uint64_t want, uint32_t* status, uint64_t timeout_ns,
+                      cudaStream_t s);
+
+void launch_heap_barrier(const HeapView& h, uint64_t flag_off, uint64_t round, uint32_t* status, uint64_t timeout_ns,
+                         cudaStream_t s);
+
+}  // namespace kiwi::p2p

@@ -1,0 +1,62 @@
+"""tcgen05 grouped BF16 GEMM vs a plain PyTorch fp32 reference of the same op."""
+import pytest
+import torch
+
+import kiwi_b200
+
+pytestmark = pytest.mark.gpu
+
+
+def _ref(a, b, counts, n, swiglu, row_scale=None):
+    outs = []
+    off = 0
+    for g, c in enumerate(counts):
+        ag = a[off:off + c].float()
+        bg = b[g * n:(g + 1) * n].float()
+        y = ag @ bg.t()
+        if swiglu:
+            cols = []
+            for t in range(n // 256):
+                gate = y[:, t * 256:t * 256 + 128]
+                up = y[:, t * 256 + 128:t * 256 + 256]
+                cols.append(torch.nn.functional.silu(gate) * up)
+            y = torch.cat(cols, dim=1)
+        if row_scale is not None:
+            y = y * row_scale[off:off + c, None]
+        outs.append(y)
+        off += c
+    return torch.cat(outs, 0)
+
+
+@pytest.mark.parametrize("counts,n,k,swiglu", [
+    ([5, 130, 0, 256], 256, 128, False),
+    ([128], 512, 64, False),
+    ([1, 0, 300], 512, 192, True),
+    ([257, 64], 1024, 7168 // 4, True),
+])
+def test_grouped_gemm_matches_fp32(counts, n, k, swiglu):
+    torch.manual_seed(0)
+    C = kiwi_b200.native()
+    rows = sum(counts)
+    a = (torch.randn(max(rows, 1), k, device="cuda") * 0.5).bfloat16()
+    b = (torch.randn(len(counts) * n, k, device="cuda") * 0.05).bfloat16()
+    out = torch.full((max(rows, 1), n // 2 if swiglu else n), float("nan"), device="cuda", dtype=torch.bfloat16)
+    plan = C.ops.GroupedGemm(a, b, len(counts))
+    cnt = torch.tensor(counts, dtype=torch.int32, device="cuda")
+    scale = torch.rand(max(rows, 1), device="cuda") + 0.5
+    plan.run(cnt, out, swiglu, scale)
+    torch.cuda.synchronize()
+    assert int(plan.error.item()) == 0
+    ref = _ref(a, b, counts, n, swiglu, scale)
+    got = out[:rows].float()
+    assert torch.isfinite(got).all()
+    err = (got - ref).abs().max().item()
+    tol = 2e-2 * ref.abs().max().item() + 1e-2
+    assert err <= tol, (err, tol)
+
+
+def test_gemm_kernels_use_no_local_memory():
+    C = kiwi_b200.native()
+    for sw in (False, True):
+        local, regs, smem = C.ops.gemm_kernel_info(sw)
+        assert local == 0, (sw, local)
