@@ -31,6 +31,10 @@ ep::EpConfig config_from_dict(const py::dict& d) {
     c.num_experts = d["num_experts"].cast<int>();
     c.topk = d["topk"].cast<int>();
     c.max_tokens = d["max_tokens"].cast<int>();
+    if (py::isinstance<py::int_>(d["quant"])) {
+        c.quant = d["quant"].cast<int>();
+        return ep::finalize(c);
+    }
     const std::string q = d["quant"].cast<std::string>();
     if (q == "none" || q == "bf16") c.quant = static_cast<int>(ep::Quant::kNone);
     else if (q == "fp8") c.quant = static_cast<int>(ep::Quant::kFp8);
@@ -158,6 +162,7 @@ public:
         g1.ldc = ffn_;
         g1.row_scale = nullptr;
         g1.error = reinterpret_cast<uint32_t*>(gemm_error_.data_ptr<int32_t>());
+        g1.max_rows = cfg_.max_pairs();
         gemm::grouped_gemm(tmap_a1_, tmap_b1_, g1, /*swiglu=*/true, 0, s);
         gemm::GroupedArgs g2 = g1;
         g2.tile_prefix = ws_.tiles2;

@@ -440,7 +440,14 @@ __global__ void __launch_bounds__(kThreads) recv_scatter_kernel(EpConfig c, p2p:
                 set_error(ws, static_cast<uint32_t>(Status::kBadArgument), kSiteCapacity, pos, c.rank);
                 pos = -1;
             }
-            ws.slot_pos[s * lpt + __popc(lmask & ((1u << lane) - 1))] = pos;
+            const int r = __popc(lmask & ((1u << lane) - 1));
+            if (r < lpt) {
+                ws.slot_pos[s * lpt + r] = pos;
+            } else {
+                // More local experts than local_per_token: only possible with
+                // repeated expert ids in caller-supplied routing.
+                set_error(ws, static_cast<uint32_t>(Status::kBadArgument), kSiteCapacity, r, c.rank);
+            }
         }
         const int nloc = __popc(lmask);
         if (lane >= nloc && lane < lpt) ws.slot_pos[s * lpt + lane] = -1;

@@ -210,8 +210,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int g_off = __ldg(&p.group_offset[g]);
             const int g_rows = __ldg(&p.group_offset[g + 1]) - g_off;
             const int r = mt * kBM + row_in_tile;
-            const bool valid = r < g_rows;
             const int64_t out_row = static_cast<int64_t>(g_off) + r;
+            const bool valid = r < g_rows && out_row < p.max_rows;
             const float scale = (valid && p.row_scale) ? p.row_scale[out_row] : 1.0f;
             const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN;
             if constexpr (SWIGLU) {

@@ -61,6 +61,7 @@ public:
         args.ldc = out.size(1);
         args.row_scale = rs;
         args.error = reinterpret_cast<uint32_t*>(error_.data_ptr<int32_t>());
+        args.max_rows = out.size(0);
         gemm::grouped_gemm(tmap_a_, tmap_b_, args, swiglu, grid, s);
     }
 

@@ -22,6 +22,7 @@ struct GroupedArgs {
     int64_t ldc;                  // C row stride, elements
     const float* row_scale;       // optional per-row factor applied in the epilogue
     uint32_t* error;              // device word: non-zero if a bounded wait ran out
+    int64_t max_rows;             // rows C holds: rows at or past it are never stored
 };
 
 struct KernelInfo {

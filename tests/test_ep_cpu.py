@@ -1,0 +1,123 @@
+"""EP configuration, heap layout and the fp32 reference model (CPU).
+
+Mirrors the reference's layout unit tests (apps/ep/tests/test_rcomp_readiness_layout.hip.cpp,
+test_ep_block_count.hip.cpp of AMDResearch/kiwi): capacities, alignment and
+non-overlap of every heap region for world sizes 1..16.
+"""
+import pytest
+import torch
+
+import kiwi_b200
+from kiwi_b200.models import moe
+
+C = kiwi_b200.native()
+
+
+def cfg(**kw):
+    d = dict(world=8, rank=3, hidden=7168, num_experts=256, topk=8, max_tokens=4096, quant="fp8")
+    d.update(kw)
+    return C.ep.finalize_config(d)
+
+
+def test_fp8_layout_of_the_benchmark_config():
+    c = cfg()
+    assert c["experts_per_rank"] == 32
+    assert c["row_bytes"] == 7168 and c["scale_bytes"] == 7168 // 128 * 4
+    assert c["meta_bytes"] == 16 + 8 * 8
+    slots = 8 * 4096
+    regions = [("off_flags", 2 * 16 * 128), ("off_meta", slots * c["meta_bytes"]),
+               ("off_row", slots * c["row_bytes"]), ("off_scale", slots * c["scale_bytes"]),
+               ("off_comb", slots * 7168 * 2)]
+    ends = []
+    for name, size in regions:
+        assert c[name] % 256 == 0, name
+        ends.append((c[name], c[name] + size))
+    for (a0, a1), (b0, b1) in zip(ends, ends[1:]):
+        assert a1 <= b0
+    assert c["heap_bytes"] >= ends[-1][1]
+    assert c["max_pairs"] == 8 * 4096 * 8
+    assert c["local_per_token"] == 8
+
+
+@pytest.mark.parametrize("world", [1, 2, 4, 8, 16])
+@pytest.mark.parametrize("quant", ["fp8", "nvfp4", "none"])
+def test_layout_alignment(world, quant):
+    c = cfg(world=world, rank=world - 1, num_experts=256 if world <= 16 else 256, quant=quant)
+    for k in ("off_meta", "off_row", "off_scale", "off_comb"):
+        assert c[k] % 256 == 0
+    assert c["row_bytes"] % 16 == 0 and c["scale_bytes"] % 16 == 0 and c["meta_bytes"] % 16 == 0
+    if quant == "nvfp4":
+        assert c["row_bytes"] == 7168 // 2
+        assert c["scale_bytes"] >= 7168 // 16 + 4
+
+
+@pytest.mark.parametrize("bad", [dict(world=0), dict(rank=8), dict(num_experts=100), dict(topk=17),
+                                 dict(topk=0), dict(hidden=1000), dict(quant="int3"), dict(max_tokens=0)])
+def test_config_rejects(bad):
+    with pytest.raises(Exception):
+        cfg(**bad)
+
+
+def test_interleave_gate_up_layout():
+    w1 = torch.arange(512 * 4, dtype=torch.float32).view(512, 4)
+    w3 = -w1
+    w13 = moe.interleave_gate_up(w1, w3)
+    assert w13.shape == (1024, 4)
+    for t in range(4):
+        assert torch.equal(w13[256 * t:256 * t + 128], w1[128 * t:128 * t + 128])
+        assert torch.equal(w13[256 * t + 128:256 * t + 256], w3[128 * t:128 * t + 128])
+
+
+def test_route_reference_softmax_over_topk():
+    logits = torch.randn(50, 64)
+    idx, w = moe.route_reference(logits, 6)
+    assert idx.shape == (50, 6) and torch.allclose(w.sum(-1), torch.ones(50))
+    v, _ = torch.topk(logits, 6)
+    assert torch.equal(idx.long(), torch.topk(logits, 6).indices)
+    assert (w[:, :-1] >= w[:, 1:]).all()
+
+
+def test_fp8_reference_error_bound():
+    x = torch.randn(64, 1024)
+    xq = moe.quant_fp8_reference(x)
+    # e4m3 has 3 mantissa bits: relative error <= 2^-4 of each block's amax scale
+    blocks = x.view(64, 8, 128)
+    err = (xq - x).view(64, 8, 128).abs()
+    bound = blocks.abs().amax(-1, keepdim=True) / 448 * 32 / 2 + 1e-6  # half ulp at the top binade
+    assert (err <= bound).all()
+
+
+def test_nvfp4_reference_grid_and_error():
+    x = torch.randn(16, 512)
+    xq = moe.quant_nvfp4_reference(x)
+    rel = ((xq - x).abs().sum() / x.abs().sum()).item()
+    assert rel < 0.15
+    assert torch.equal(moe.quant_nvfp4_reference(torch.zeros(2, 512)), torch.zeros(2, 512))
+
+
+def test_reference_layer_is_linear_in_routing_weight():
+    c = moe.MoEConfig(hidden=256, ffn=128, num_experts=8, topk=2, tokens_per_rank=5, quant="none")
+    x, logits = moe.synthetic_inputs(c, 0, "cpu")
+    idx, w = moe.route_reference(logits, 2)
+    y1 = moe.moe_reference(c, x, idx, w, device="cpu")
+    y2 = moe.moe_reference(c, x, idx, 2 * w, device="cpu")
+    assert torch.allclose(2 * y1, y2, rtol=1e-4, atol=1e-5)
+
+
+def test_weights_depend_only_on_global_expert_id():
+    c = moe.MoEConfig(hidden=256, ffn=128, num_experts=8, topk=2)
+    w13_1, w2_1 = moe.local_expert_weights(c, 0, 1, "cpu")
+    w13_2, w2_2 = moe.local_expert_weights(c, 1, 2, "cpu")
+    e_local = 4
+    assert torch.equal(w13_1[e_local * 256:], w13_2)
+    assert torch.equal(w2_1[e_local * 256:], w2_2)
+
+
+def test_zipf_skews_routing():
+    c = moe.CONFIGS["nvfp4"]
+    small = moe.MoEConfig(hidden=512, ffn=256, num_experts=64, topk=6, tokens_per_rank=4096, zipf=1.2)
+    _, logits = moe.synthetic_inputs(small, 0, "cpu")
+    idx, _ = moe.route_reference(logits, 6)
+    counts = torch.bincount(idx.flatten().long(), minlength=64).float()
+    assert counts.max() / counts.mean() > 3.0
+    assert c.quant == "nvfp4" and c.topk == 6

@@ -1,0 +1,104 @@
+"""The fused EP MoE layer on one B200 (world of 1: every store goes through
+the same NVLink-path code into the local heap) vs the fp32 reference."""
+import pytest
+import torch
+
+import kiwi_b200
+from kiwi_b200.models import moe
+from kiwi_b200.parallel.ep import EpDispatchCombine, ExpertParallelMoE
+
+pytestmark = pytest.mark.gpu
+
+
+def small_cfg(quant, tokens=200, hidden=1024, ffn=256, experts=16, topk=4, zipf=0.0):
+    return moe.MoEConfig(hidden=hidden, ffn=ffn, num_experts=experts, topk=topk, tokens_per_rank=tokens,
+                         quant=quant, zipf=zipf, name="test")
+
+
+def _check(layer, cfg, x, logits, out):
+    torch.cuda.synchronize()
+    layer.check()
+    idx, w = moe.route_reference(logits, cfg.topk)
+    ref = moe.moe_reference(cfg, x, idx, w, device=x.device)
+    got = out.float()
+    scale = ref.abs().max().item()
+    err = (got - ref).abs().max().item()
+    assert err <= 2e-2 * scale + 1e-3, (err, scale)
+
+
+@pytest.mark.parametrize("quant", ["fp8", "nvfp4", "none"])
+def test_layer_matches_reference(quant):
+    cfg = small_cfg(quant)
+    layer = ExpertParallelMoE(cfg)
+    for step in range(3):  # several rounds: epochs advance, slots reused
+        x, logits = moe.synthetic_inputs(cfg, 0, "cuda", step=step)
+        out = layer(x, logits).clone()
+        _check(layer, cfg, x, logits, out)
+
+
+def test_routing_kernel_matches_topk():
+    cfg = small_cfg("fp8", tokens=300, experts=64, topk=6)
+    _, logits = moe.synthetic_inputs(cfg, 0, "cuda")
+    idx = torch.empty(300, 6, dtype=torch.int32, device="cuda")
+    w = torch.empty(300, 6, dtype=torch.float32, device="cuda")
+    kiwi_b200.native().ep.route(logits, 6, idx, w)
+    ridx, rw = moe.route_reference(logits, 6)
+    assert torch.equal(idx, ridx)
+    assert torch.allclose(w, rw, atol=1e-6)
+
+
+def test_expert_counts_and_partial_token_counts():
+    cfg = small_cfg("fp8", tokens=256, experts=16, topk=4)
+    layer = ExpertParallelMoE(cfg)
+    x, logits = moe.synthetic_inputs(cfg, 0, "cuda", tokens=77)
+    out = layer(x, logits).clone()
+    _check(layer, cfg, x, logits, out)
+    idx, _ = moe.route_reference(logits, 4)
+    assert torch.equal(layer.expert_counts.cpu(), torch.bincount(idx.flatten().long(), minlength=16).int().cpu())
+
+
+def test_zero_tokens_round():
+    cfg = small_cfg("fp8", tokens=64)
+    layer = ExpertParallelMoE(cfg)
+    x, logits = moe.synthetic_inputs(cfg, 0, "cuda", tokens=0)
+    out = layer(x, logits)
+    torch.cuda.synchronize()
+    layer.check()
+    assert out.shape == (0, cfg.hidden)
+    x, logits = moe.synthetic_inputs(cfg, 0, "cuda", tokens=64)
+    _check(layer, cfg, x, logits, layer(x, logits).clone())
+
+
+def test_skewed_routing_and_cuda_graph_replay():
+    cfg = small_cfg("fp8", tokens=128, zipf=1.2)
+    layer = ExpertParallelMoE(cfg)
+    x, logits = moe.synthetic_inputs(cfg, 0, "cuda")
+    layer(x, logits)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        out = layer(x, logits)
+    for step in range(3):
+        x2, l2 = moe.synthetic_inputs(cfg, 0, "cuda", step=step + 10)
+        x.copy_(x2)
+        logits.copy_(l2)
+        g.replay()
+        _check(layer, cfg, x, logits, out.clone())
+
+
+def test_transport_only_dispatch_combine():
+    t = EpDispatchCombine(hidden=512, num_experts=8, topk=2, max_tokens=64, quant="none")
+    x = torch.randn(64, 512, device="cuda").bfloat16()
+    logits = torch.randn(64, 8, device="cuda")
+    idx, w = moe.route_reference(logits, 2)
+    rows, counts, slots, weights = t.dispatch(x, w, idx)
+    torch.cuda.synchronize()
+    n = int(counts.sum().item())
+    assert n == 64 * 2
+    # each received row is its token's row; combine of weight*row must give sum_k w_k * x
+    tok = (slots[:n] % 64).long()
+    assert torch.equal(rows[:n], x[tok])
+    out = t.combine(rows[:n].float().mul(weights[:n, None]).bfloat16())
+    torch.cuda.synchronize()
+    ref = x.float() * w.sum(-1, keepdim=True)
+    assert (out.float() - ref).abs().max().item() < 3e-2

@@ -1,0 +1,63 @@
+"""FD exchange over abstract Unix sockets between processes (CPU only):
+the bootstrap the symmetric heap uses, tested with memfd objects."""
+import multiprocessing as mp
+import os
+import uuid
+
+import pytest
+
+
+def _worker(job, rank, world, q):
+    import kiwi_b200
+
+    C = kiwi_b200.native()
+    fd = os.memfd_create(f"kiwi-test-{rank}")
+    os.write(fd, f"rank{rank}".encode())
+    try:
+        fds = C.p2p.exchange_fds(job, rank, world, fd, 20.0)
+        got = []
+        for f in fds:
+            os.lseek(f, 0, 0)
+            got.append(os.read(f, 16).decode())
+            os.close(f)
+        q.put((rank, got))
+    except Exception as e:  # pragma: no cover
+        q.put((rank, repr(e)))
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_exchange_fds(world):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    job = uuid.uuid4().hex[:12]
+    ps = [ctx.Process(target=_worker, args=(job, r, world, q)) for r in range(world)]
+    for p in ps:
+        p.start()
+    res = dict(q.get(timeout=120) for _ in range(world))
+    for p in ps:
+        p.join(timeout=60)
+    for r in range(world):
+        assert res[r] == [f"rank{i}" for i in range(world)], res[r]
+
+
+def _lonely(job, q):
+    import kiwi_b200
+
+    C = kiwi_b200.native()
+    fd = os.memfd_create("kiwi-lonely")
+    try:
+        C.p2p.exchange_fds(job, 0, 2, fd, 1.0)
+        q.put("no error")
+    except Exception as e:
+        q.put(str(e))
+
+
+def test_missing_peer_times_out():
+    """A rank that never joins makes the exchange fail after its timeout (no hang)."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    p = ctx.Process(target=_lonely, args=(uuid.uuid4().hex[:12], q))
+    p.start()
+    msg = q.get(timeout=60)
+    p.join(timeout=30)
+    assert "timed out" in msg
