@@ -1,0 +1,144 @@
+// Allocation-free C entry point of the grouped BF16 GEMM.
+//
+// This entry point has no counterpart in the reference (AMDResearch/kiwi has
+// no GEMM at all); it is an addition of this library.
+//
+// Who needs it: callers that must not allocate device memory while they run.
+// Typical cases are a serving engine that reserves all GPU memory for its own
+// pool at start-up (any cudaMalloc later fails or fragments that pool), C or
+// C++ hosts that cannot reach PyTorch's caching allocator, and code that issues
+// work while another component is capturing the stream into a CUDA graph,
+// where cudaMalloc is not permitted.  The regular entry point
+// (kiwi_b200._C.ops.GroupedGemm) allocates its schedule buffers with torch;
+// this one keeps them in a fixed device array instead.
+//
+// Contract:
+//   * The caller passes every input and output: A [a_rows, k] bf16, B
+//     [num_groups * n, k] bf16 (both row-major, 16-byte aligned), per-group row
+//     counts (int32 device array), C [c_rows, n] bf16 (or [c_rows, n / 2] with
+//     swiglu), an optional fp32 per-row scale, and the CUDA stream.
+//   * Scratch (group offsets, tile prefix, error word) lives in the file-scope
+//     device array below: kNoallocMaxGroups = 1024 groups at most, 8.5 KB.  Every
+//     GPU that loads this library holds the array until the process exits.
+//   * The first call on a device (with that device current) resolves the
+//     array's device address with cudaGetSymbolAddress and caches it; make that
+//     first call before any stream capture that includes this entry point.
+//   * All calls share the array, which keeps the last call's contents: the
+//     error word is cleared (cudaMemsetAsync) at the start of every call and the
+//     schedule is rewritten by every call.  Calls that overlap on the same GPU
+//     (for example on two streams) race on the array, so serialise them; calls
+//     on different GPUs use different copies of the array and do not race.
+//   * No cudaMalloc, cudaFree or allocating library routine is called.
+//   * Returns 0 on success; a non-zero code and a message readable through
+//     kiwi_noalloc_last_error() otherwise (sizes beyond the maximum, bad
+//     alignment, CUDA errors).
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <mutex>
+#include <string>
+
+#include "kiwi/gemm/grouped_gemm.hpp"
+
+namespace {
+
+constexpr int kNoallocMaxGroups = 1024;
+constexpr int kScratchWords = 2 * (kNoallocMaxGroups + 1) + 64;  // offsets, tile prefix, error word (+ pad)
+constexpr int kMaxDevices = 64;
+
+static __device__ __align__(256) int32_t g_noalloc_scratch[kScratchWords];
+
+std::mutex g_mu;
+int32_t* g_scratch_ptr[kMaxDevices] = {};
+thread_local std::string g_last_error;
+
+int fail(int code, const std::string& msg) {
+    g_last_error = msg;
+    return code;
+}
+
+/// Device address of this device's copy of the scratch array (resolved once per device).
+int32_t* scratch_for_current_device(std::string& err) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) {
+        err = std::string("cudaGetDevice failed: ") + cudaGetErrorString(e);
+        return nullptr;
+    }
+    if (dev < 0 || dev >= kMaxDevices) {
+        err = "device index beyond the supported 64 devices";
+        return nullptr;
+    }
+    std::lock_guard<std::mutex> g(g_mu);
+    if (g_scratch_ptr[dev] == nullptr) {
+        void* p = nullptr;
+        e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (e != cudaSuccess || p == nullptr) {
+            err = std::string("cudaGetSymbolAddress(scratch) failed: ") + cudaGetErrorString(e);
+            return nullptr;
+        }
+        g_scratch_ptr[dev] = static_cast<int32_t*>(p);
+    }
+    return g_scratch_ptr[dev];
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+}  // namespace
+
+extern "C" __attribute__((visibility("default"))) int kiwi_noalloc_max_groups() { return kNoallocMaxGroups; }
+
+extern "C" __attribute__((visibility("default"))) const char* kiwi_noalloc_last_error() {
+    return g_last_error.c_str();
+}
+
+/// C[g rows] = A[g rows] . B[g]^T per group g (optionally SwiGLU and a per-row
+/// scale in the epilogue), without allocating.  See the file comment.
+extern "C" __attribute__((visibility("default"))) int kiwi_grouped_gemm_bf16_noalloc(
+    const void* a, int64_t a_rows, const void* b, int32_t num_groups, int32_t n, int32_t k, const int32_t* counts,
+    void* c, int64_t c_rows, int32_t swiglu, const float* row_scale, void* stream) {
+    g_last_error.clear();
+    if (num_groups < 1 || num_groups > kNoallocMaxGroups) {
+        return fail(1, "kiwi_grouped_gemm_bf16_noalloc: num_groups must be in [1, " +
+                           std::to_string(kNoallocMaxGroups) + "], got " + std::to_string(num_groups));
+    }
+    if (n <= 0 || n % 256 != 0 || k <= 0 || k % 64 != 0) {
+        return fail(2, "kiwi_grouped_gemm_bf16_noalloc: n must be a positive multiple of 256 and k of 64");
+    }
+    if (!a || !b || !c || !counts || a_rows <= 0 || c_rows <= 0) {
+        return fail(3, "kiwi_grouped_gemm_bf16_noalloc: null pointer or empty A/C");
+    }
+    if (!aligned16(a) || !aligned16(b) || !aligned16(c)) {
+        return fail(4, "kiwi_grouped_gemm_bf16_noalloc: A, B and C must be 16-byte aligned");
+    }
+    std::string err;
+    int32_t* scratch = scratch_for_current_device(err);
+    if (!scratch) return fail(5, "kiwi_grouped_gemm_bf16_noalloc: " + err);
+    int32_t* offsets = scratch;
+    int32_t* tiles = scratch + (kNoallocMaxGroups + 1);
+    int32_t* error_word = scratch + 2 * (kNoallocMaxGroups + 1);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    try {
+        const cudaError_t e = cudaMemsetAsync(error_word, 0, sizeof(int32_t), s);
+        if (e != cudaSuccess) return fail(6, std::string("cudaMemsetAsync failed: ") + cudaGetErrorString(e));
+        const CUtensorMap tmap_a = kiwi::gemm::make_tmap_bf16_2d(a, static_cast<uint64_t>(a_rows), k, 128);
+        const CUtensorMap tmap_b =
+            kiwi::gemm::make_tmap_bf16_2d(b, static_cast<uint64_t>(num_groups) * n, k, 256);
+        kiwi::gemm::build_schedule(counts, num_groups, n, 256, offsets, tiles, s);
+        kiwi::gemm::GroupedArgs args{};
+        args.group_offset = offsets;
+        args.tile_prefix = tiles;
+        args.num_groups = num_groups;
+        args.n = n;
+        args.k = k;
+        args.c = static_cast<__nv_bfloat16*>(c);
+        args.ldc = swiglu ? n / 2 : n;
+        args.row_scale = row_scale;
+        args.error = reinterpret_cast<uint32_t*>(error_word);
+        args.max_rows = c_rows;
+        kiwi::gemm::grouped_gemm(tmap_a, tmap_b, args, swiglu != 0, 0, s);
+    } catch (const std::exception& ex) {
+        return fail(7, std::string("kiwi_grouped_gemm_bf16_noalloc: ") + ex.what());
+    }
+    return 0;
+}
