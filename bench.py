@@ -39,7 +39,7 @@ KERNELS_PER_STEP = 11           # begin, route, dispatch, recv_count, 2 schedule
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=40)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="kiwi", choices=["kiwi", "reference", "nccl"])
     ap.add_argument("--config", default="deepseek_fp8")
@@ -91,22 +91,26 @@ def main():
     def step(xx, ll):
         return layer(xx, ll)
 
-    for _ in range(args.warmup):
-        step(x, logits)
-    torch.cuda.synchronize()
-    if args.impl == "kiwi":
-        layer.check()
+    clocks = ClockSampler(device_index=_physical_index())
+    with clocks:
+        for _ in range(args.warmup):
+            step(x, logits)
+        torch.cuda.synchronize()
+        if args.impl == "kiwi":
+            layer.check()
+        clocks.wait_first_sample()
 
-    # ---- timed region: K device-timed steps ----
-    kdist.barrier()
-    torch.cuda.synchronize()
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(device_index=_physical_index()) as clocks:
+        # ---- timed region: K device-timed steps ----
+        kdist.barrier()
+        torch.cuda.synchronize()
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        clocks.mark_start()
         start.record()
         for _ in range(args.steps):
             step(x, logits)
         end.record()
         torch.cuda.synchronize()
+        clocks.mark_end()
     kdist.barrier()
     ms = kdist.max_over_ranks(start.elapsed_time(end) / args.steps)
     if args.impl == "kiwi":
@@ -189,7 +193,8 @@ def main():
                        f"{cfg.num_experts // world * 3 * cfg.hidden * cfg.ffn * 2 / 1e9:.1f} GB per GPU)"},
             "dispatch_combine_us": ms * 1e3,
             "tflops_per_gpu": flops / (ms / 1e3) / 1e12,
-            "clocks": {"sm_mhz": clk["sm_mhz"], "sm_max_mhz": clk["sm_max_mhz"], "reasons": clk["reasons"]},
+            "clocks": {"sm_mhz": clk["sm_mhz"], "sm_max_mhz": clk["sm_max_mhz"], "reasons": clk["reasons"],
+                       "samples": clk["samples"]},
             "e2e": e2e, "gpu_launches": KERNELS_PER_STEP * args.steps if args.impl == "kiwi" else None,
             "latency_mode": lat, "invoke_rtt": invoke, "impl": args.impl,
         }

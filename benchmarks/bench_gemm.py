@@ -1,0 +1,66 @@
+"""Grouped BF16 GEMM: kiwi tcgen05 kernel vs torch._grouped_mm (cuBLAS/CUTLASS)
+on the expert-FFN shapes of the EP benchmark, per rank.
+
+    python benchmarks/bench_gemm.py
+
+Shapes: GEMM1 (K=7168 -> N=2*2048, SwiGLU epilogue for kiwi) and GEMM2
+(K=2048 -> N=7168) for 32 experts x 1024 rows (one rank of 8) and 256 experts
+x 128 rows (one rank of 1).  TFLOP/s from CUDA events over 20 launches after
+warm-up; weights (B) exceed L2 in every shape.
+"""
+import json
+import os
+import sys
+
+sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+import torch  # noqa: E402
+
+import kiwi_b200  # noqa: E402
+
+
+def timeit(fn, iters=20):
+    for _ in range(3):
+        fn()
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(iters):
+        fn()
+    e.record()
+    torch.cuda.synchronize()
+    return s.elapsed_time(e) / iters
+
+
+def main():
+    C = kiwi_b200.native()
+    torch.manual_seed(0)
+    for name, groups, rows, k, n, swiglu in [
+        ("gemm1_ep8", 32, 1024, 7168, 4096, True),
+        ("gemm2_ep8", 32, 1024, 2048, 7168, False),
+        ("gemm1_ep1", 256, 128, 7168, 4096, True),
+        ("gemm2_ep1", 256, 128, 2048, 7168, False),
+    ]:
+        total = groups * rows
+        a = (torch.randn(total, k, device="cuda") * 0.5).bfloat16()
+        b = (torch.randn(groups * n, k, device="cuda") * 0.02).bfloat16()
+        counts = torch.full((groups,), rows, dtype=torch.int32, device="cuda")
+        out = torch.empty(total, n // 2 if swiglu else n, device="cuda", dtype=torch.bfloat16)
+        plan = C.ops.GroupedGemm(a, b, groups)
+        ms = timeit(lambda: plan.run(counts, out, swiglu))
+        flops = 2.0 * total * n * k
+        bw = (b.numel() * 2 + a.numel() * 2 + out.numel() * 2) / (ms / 1e3) / 1e12
+        offs = torch.cumsum(counts, 0).to(torch.int32)
+        bt = b.view(groups, n, k).transpose(-2, -1)
+        try:
+            tms = timeit(lambda: torch._grouped_mm(a, bt, offs=offs, out_dtype=torch.bfloat16))
+        except Exception as ex:  # pragma: no cover
+            tms = float("nan")
+            print("torch._grouped_mm failed:", ex, file=sys.stderr)
+        print("RESULT " + json.dumps({"bench": name, "groups": groups, "rows": rows, "k": k, "n": n,
+                                      "kiwi_ms": ms, "kiwi_tflops": flops / ms / 1e9,
+                                      "kiwi_hbm_TBps_min_traffic": bw,
+                                      "torch_grouped_mm_ms": tms, "torch_tflops": flops / tms / 1e9}), flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -485,6 +485,28 @@ __global__ void __launch_bounds__(kThreads) recv_scatter_kernel(EpConfig c, p2p:
     }
 }
 
+/// Sums up to 16 bf16 rows (`ptrs[j] + col`, j < n) into fp32: every load is
+/// issued before the first add so all of them are in flight together.
+template <typename Loader>
+KIWI_DEV void sum_rows(int n, Loader load, float (&acc)[8]) {
+    uint4 v[kMaxTopk];
+#pragma unroll
+    for (int j = 0; j < kMaxTopk; ++j) {
+        if (j < n) v[j] = load(j);
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+#pragma unroll
+    for (int j = 0; j < kMaxTopk; ++j) {
+        if (j < n) {
+            float f[8];
+            bf16x8_to_f32(v[j], f);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) acc[i] += f[i];
+        }
+    }
+}
+
 __global__ void __launch_bounds__(kThreads) combine_send_kernel(EpConfig c, p2p::HeapView h,
                                                                 const __nv_bfloat16* y, EpWorkspace ws) {
     const int lane = threadIdx.x & 31;
@@ -496,18 +518,16 @@ __global__ void __launch_bounds__(kThreads) combine_send_kernel(EpConfig c, p2p:
         const int p = lane < lpt ? ws.slot_pos[s * lpt + lane] : -1;
         const uint32_t pm = __ballot_sync(0xffffffffu, p >= 0);
         if (pm == 0) continue;
+        const int npos = __popc(pm);  // positions are packed at the front of the slot's list
+        int pl[kMaxTopk];
+#pragma unroll
+        for (int j = 0; j < kMaxTopk; ++j) pl[j] = __shfl_sync(0xffffffffu, p, j);
         const int src = static_cast<int>(s / c.max_tokens);
         const int t = static_cast<int>(s % c.max_tokens);
         uint8_t* dst = h.base[src] + c.comb_off(c.rank, t);
         for (int col = lane * 8; col < c.hidden; col += 256) {
-            float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-            for (uint32_t m = pm; m; m &= m - 1) {
-                const int pp = __shfl_sync(0xffffffffu, p, __ffs(m) - 1);
-                float f[8];
-                bf16x8_to_f32(ptx::ld_v4(y + static_cast<int64_t>(pp) * c.hidden + col), f);
-#pragma unroll
-                for (int i = 0; i < 8; ++i) acc[i] += f[i];
-            }
+            float acc[8];
+            sum_rows(npos, [&](int j) { return ptx::ld_v4(y + static_cast<int64_t>(pl[j]) * c.hidden + col); }, acc);
             ptx::st_v4(dst + 2ull * col, f32x8_to_bf16(acc));
         }
     }
@@ -529,15 +549,22 @@ __global__ void __launch_bounds__(kThreads) combine_recv_kernel(EpConfig c, p2p:
         const int e = lane < c.topk ? idx[static_cast<int64_t>(t) * c.topk + lane] : -1;
         const bool ok_e = e >= 0 && e < c.num_experts;
         const uint32_t mask = __reduce_or_sync(0xffffffffu, ok_e ? (1u << (e / c.experts_per_rank)) : 0u);
-        for (int col = lane * 8; col < c.hidden; col += 256) {
-            float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-            for (uint32_t m = mask; m; m &= m - 1) {
-                const int r = __ffs(m) - 1;
-                float f[8];
-                bf16x8_to_f32(ld_cg_v4(base + c.comb_off(r, t) + 2ull * col), f);
+        int rl[kMaxTopk];
+        int nr = 0;
+        {
+            uint32_t m = mask;
 #pragma unroll
-                for (int i = 0; i < 8; ++i) acc[i] += f[i];
+            for (int j = 0; j < kMaxTopk; ++j) {
+                rl[j] = m ? __ffs(m) - 1 : 0;
+                if (m) {
+                    ++nr;
+                    m &= m - 1;
+                }
             }
+        }
+        for (int col = lane * 8; col < c.hidden; col += 256) {
+            float acc[8];
+            sum_rows(nr, [&](int j) { return ld_cg_v4(base + c.comb_off(rl[j], t) + 2ull * col); }, acc);
             ptx::st_v4(out + static_cast<int64_t>(t) * c.hidden + col, f32x8_to_bf16(acc));
         }
     }

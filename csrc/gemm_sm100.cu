@@ -55,9 +55,13 @@ __device__ __forceinline__ void locate_tile(const int32_t* tile_prefix, int num_
         else lo = mid + 1;
     }
     g = lo;
+    // n-tile outermost within a group: the m-tiles that share one B (weight)
+    // tile are adjacent in the schedule, run concurrently on neighbouring SMs
+    // and read that tile from L2 instead of HBM.
     const int local = tile - __ldg(&tile_prefix[g]);
-    m_tile = local / n_tiles;
-    n_tile = local - m_tile * n_tiles;
+    const int m_tiles = (__ldg(&tile_prefix[g + 1]) - __ldg(&tile_prefix[g])) / n_tiles;
+    n_tile = local / m_tiles;
+    m_tile = local - n_tile * m_tiles;
 }
 
 __device__ __forceinline__ float silu(float x) { return x / (1.0f + __expf(-x)); }

@@ -31,13 +31,11 @@ struct InvokeHandle {
 
     template <typename... Args>
     KIWI_DEV bool invoke(uint8_t callback_id, const Args&... args) {
-        constexpr uint32_t n = ArgPack<Args...>::total_bytes;
-        static_assert(n <= 512, "register-resident invoke arguments are limited to 512 bytes");
-        struct Payload {
-            uint8_t b[n];
-        } p;
-        ArgPack<Args...>::serialize(p.b, args...);
-        return queue.push_reg(p, callback_id);
+        using P = ArgPack<Args...>;
+        static_assert(P::total_bytes <= 512, "register-resident invoke arguments are limited to 512 bytes");
+        PackedWords<P::kWords> p;
+        P::pack_words(p.w, args...);
+        return queue.push_reg_n(p, P::total_bytes, callback_id);
     }
 
     /// Call with a return value: sends (seq, args...) to a callback registered
@@ -69,10 +67,8 @@ struct InvokeHandle {
         if constexpr (n == 0) {
             return queue.push_lane_masked(uint64_t{0}, 0, callback_id, active);
         } else {
-            struct Payload {
-                uint8_t b[n];
-            } p;
-            ArgPack<Args...>::serialize(p.b, args...);
+            PackedWords<ArgPack<Args...>::kWords> p;
+            ArgPack<Args...>::pack_words(p.w, args...);
             return queue.push_lane_masked(p, n, callback_id, active);
         }
     }

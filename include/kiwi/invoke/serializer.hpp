@@ -15,6 +15,39 @@
 
 namespace kiwi::invoke {
 
+template <typename T, uint32_t N>
+KIWI_HD void put_word(uint64_t (&w)[N], uint32_t& off, const T& v) {
+    uint64_t u = 0;
+    if constexpr (sizeof(T) == 1) {
+        uint8_t t;
+        memcpy(&t, &v, 1);
+        u = t;
+    } else if constexpr (sizeof(T) == 2) {
+        uint16_t t;
+        memcpy(&t, &v, 2);
+        u = t;
+    } else if constexpr (sizeof(T) == 4) {
+        uint32_t t;
+        memcpy(&t, &v, 4);
+        u = t;
+    } else if constexpr (sizeof(T) == 8) {
+        memcpy(&u, &v, 8);
+    }
+    if constexpr (sizeof(T) == 1 || sizeof(T) == 2 || sizeof(T) == 4 || sizeof(T) == 8) {
+        const uint32_t word = off / 8, shift = 8 * (off % 8);
+        w[word] |= u << shift;
+        if (shift + 8 * sizeof(T) > 64) w[word + 1] |= u >> (64 - shift);
+    } else {
+        // Other sizes: byte by byte (constant offsets; still register resident when unrolled).
+        const uint8_t* b = reinterpret_cast<const uint8_t*>(&v);
+        for (uint32_t i = 0; i < sizeof(T); ++i) {
+            const uint32_t o = off + i;
+            w[o / 8] |= static_cast<uint64_t>(b[i]) << (8 * (o % 8));
+        }
+    }
+    off += sizeof(T);
+}
+
 template <typename... Args>
 struct ArgPack {
     static_assert((std::is_trivially_copyable_v<Args> && ...),
@@ -28,6 +61,19 @@ struct ArgPack {
         (void)dst;
     }
 
+    static constexpr uint32_t kWords = (total_bytes + 7) / 8 > 0 ? (total_bytes + 7) / 8 : 1;
+
+    /// Register-friendly serialisation into 64-bit words: every argument of
+    /// 1, 2, 4 or 8 bytes is placed with shifts at its constant offset, so no
+    /// byte array (and no local memory) is needed on the device.  The byte
+    /// image equals serialize()'s (little-endian, packed).
+    KIWI_HD static void pack_words(uint64_t (&w)[kWords], const Args&... args) {
+        for (uint32_t i = 0; i < kWords; ++i) w[i] = 0;
+        uint32_t off = 0;
+        (put_word(w, off, args), ...);
+        (void)off;
+    }
+
     static std::tuple<Args...> deserialize(const uint8_t* src) {
         std::tuple<Args...> out;
         uint32_t off = 0;
@@ -35,6 +81,12 @@ struct ArgPack {
                    out);
         return out;
     }
+};
+
+/// Fixed-size word image of a packed argument list (what a device invoke sends).
+template <uint32_t N>
+struct alignas(8) PackedWords {
+    uint64_t w[N];
 };
 
 }  // namespace kiwi::invoke

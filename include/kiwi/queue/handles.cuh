@@ -16,6 +16,9 @@
 // the queue's ErrorRecord (host memory); bounded waits record kTimeout.
 #pragma once
 
+#include <type_traits>
+#include <utility>
+
 #include "kiwi/queue/wire.hpp"
 #if defined(__CUDACC__)
 #include "kiwi/ptx.cuh"
@@ -65,9 +68,22 @@ KIWI_DEV void write_message(Chunk* ring, uint32_t log2cap, uint64_t head, uint32
     }
 }
 
+template <typename T, typename = void>
+struct has_word_array : std::false_type {};
+template <typename T>
+struct has_word_array<T, std::void_t<decltype(std::declval<const T&>().w[0])>>
+    : std::is_same<std::decay_t<decltype(std::declval<const T&>().w[0])>, uint64_t> {};
+
 /// Selects 8-byte word `i` of a register-resident object (all lanes hold it).
 template <typename T>
 KIWI_DEV uint64_t select_word(const T& msg, uint32_t i) {
+    if constexpr (has_word_array<T>::value) {
+        constexpr uint32_t kW = sizeof(T) / 8;
+        uint64_t out = 0;
+#pragma unroll
+        for (uint32_t w = 0; w < kW; ++w) out = (w == i) ? msg.w[w] : out;
+        return out;
+    } else {
     constexpr uint32_t kWords = (sizeof(T) + 7) / 8;
     struct alignas(8) Padded {
         uint8_t b[kWords * 8];
@@ -81,6 +97,7 @@ KIWI_DEV uint64_t select_word(const T& msg, uint32_t i) {
         out = (w == i) ? v : out;
     }
     return out;
+    }
 }
 
 KIWI_DEV uint64_t load_word(const void* p, uint32_t i) {
@@ -141,8 +158,14 @@ struct SpscD2HHandle {
     /// The message is a register-resident object every lane holds.
     template <typename T>
     KIWI_DEV bool push_reg(const T& msg, uint32_t metadata = 0) {
+        return push_reg_n(msg, sizeof(T), metadata);
+    }
+
+    /// As push_reg, sending only the first `bytes` (<= sizeof(T)) bytes of msg.
+    template <typename T>
+    KIWI_DEV bool push_reg_n(const T& msg, uint32_t bytes, uint32_t metadata = 0) {
         static_assert(sizeof(T) <= 512, "push_reg holds at most 512 bytes in registers");
-        constexpr uint32_t bytes = sizeof(T);
+        if (bytes > sizeof(T)) bytes = sizeof(T);
         if (oversize(bytes)) return true;
         const uint32_t nlines = message_lines(bytes);
         if (!reserve(nlines)) return false;
@@ -277,8 +300,13 @@ struct MpscD2HHandle {
 
     template <typename T>
     KIWI_DEV bool push_reg(const T& msg, uint32_t metadata = 0) {
+        return push_reg_n(msg, sizeof(T), metadata);
+    }
+
+    template <typename T>
+    KIWI_DEV bool push_reg_n(const T& msg, uint32_t bytes, uint32_t metadata = 0) {
         static_assert(sizeof(T) <= 512, "push_reg holds at most 512 bytes in registers");
-        constexpr uint32_t bytes = sizeof(T);
+        if (bytes > sizeof(T)) bytes = sizeof(T);
         if (oversize(bytes)) return true;
         uint64_t base;
         if (!claim_lines(message_lines(bytes), base)) return false;

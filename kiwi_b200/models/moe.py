@@ -110,7 +110,8 @@ def quant_fp8_reference(x, block=128):
     xf = x.float().view(t, h // block, block)
     amax = xf.abs().amax(-1, keepdim=True)
     scale = torch.where(amax > 0, amax / FP8_MAX, torch.ones_like(amax))
-    q = (xf / scale).clamp(-FP8_MAX, FP8_MAX).to(torch.float8_e4m3fn)
+    inv = torch.where(amax > 0, FP8_MAX / amax, torch.zeros_like(amax))  # multiply by the reciprocal, as on the device
+    q = (xf * inv).clamp(-FP8_MAX, FP8_MAX).to(torch.float8_e4m3fn)
     return (q.float() * scale).view(t, h)
 
 

@@ -15,7 +15,7 @@ def small_cfg(quant, tokens=200, hidden=1024, ffn=256, experts=16, topk=4, zipf=
                          quant=quant, zipf=zipf, name="test")
 
 
-def _check(layer, cfg, x, logits, out):
+def _check(layer, cfg, x, logits, out, rel=2e-2):
     torch.cuda.synchronize()
     layer.check()
     idx, w = moe.route_reference(logits, cfg.topk)
@@ -23,17 +23,40 @@ def _check(layer, cfg, x, logits, out):
     got = out.float()
     scale = ref.abs().max().item()
     err = (got - ref).abs().max().item()
-    assert err <= 2e-2 * scale + 1e-3, (err, scale)
+    assert err <= rel * scale + 1e-3, (err, scale)
 
 
 @pytest.mark.parametrize("quant", ["fp8", "nvfp4", "none"])
 def test_layer_matches_reference(quant):
     cfg = small_cfg(quant)
     layer = ExpertParallelMoE(cfg)
+    # NVFP4 keeps one mantissa bit: a single rounding disagreement between two
+    # correct quantisers moves an output by a visible fraction of its range.
+    rel = 5e-2 if quant == "nvfp4" else 2e-2
     for step in range(3):  # several rounds: epochs advance, slots reused
         x, logits = moe.synthetic_inputs(cfg, 0, "cuda", step=step)
         out = layer(x, logits).clone()
-        _check(layer, cfg, x, logits, out)
+        _check(layer, cfg, x, logits, out, rel)
+
+
+@pytest.mark.parametrize("quant", ["fp8", "nvfp4", "none"])
+def test_dispatched_rows_match_reference_quantisation(quant):
+    """Each expert-major row the receive side produced equals the reference
+    quantise-dequantise of its source token (bf16-rounded)."""
+    cfg = small_cfg(quant, tokens=64)
+    layer = ExpertParallelMoE(cfg)
+    x, logits = moe.synthetic_inputs(cfg, 0, "cuda")
+    layer(x, logits)
+    torch.cuda.synchronize()
+    n = int(layer.expert_counts.sum().item())
+    rows = layer.native.expert_input[:n].float()
+    tok = (layer.native.pair_slot[:n] % cfg.tokens_per_rank).long()
+    ref = moe.dispatch_reference(x, quant).bfloat16().float()[tok]
+    # Elements may land one quantisation step apart where the scaled value sits on
+    # a rounding boundary (x * (448 / amax) in the kernel vs the reference's
+    # fp32 arithmetic); anything more than a tiny fraction is a layout bug.
+    bad = (rows - ref).abs() > 1e-6 + 1e-2 * ref.abs()
+    assert bad.float().mean().item() < 5e-3, (bad.float().mean().item(), (rows - ref).abs().max().item())
 
 
 def test_routing_kernel_matches_topk():

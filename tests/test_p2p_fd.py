@@ -17,8 +17,9 @@ def _worker(job, rank, world, q):
         fds = C.p2p.exchange_fds(job, rank, world, fd, 20.0)
         got = []
         for f in fds:
-            os.lseek(f, 0, 0)
-            got.append(os.read(f, 16).decode())
+            # pread: descriptors passed with SCM_RIGHTS share one file offset
+            # across processes, so seek + read would race with the peers.
+            got.append(os.pread(f, 16, 0).decode())
             os.close(f)
         q.put((rank, got))
     except Exception as e:  # pragma: no cover
