@@ -19,7 +19,7 @@ import kiwi_b200  # noqa: E402
 
 
 def timeit(fn, iters=20):
-    for _ in range(3):
+    for _ in range(min(3, iters)):
         fn()
     torch.cuda.synchronize()
     s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -31,31 +31,46 @@ def timeit(fn, iters=20):
     return s.elapsed_time(e) / iters
 
 
+SHAPES = [
+    ("gemm1_ep8", 32, 1024, 7168, 4096, True),
+    ("gemm2_ep8", 32, 1024, 2048, 7168, False),
+    ("gemm1_ep1", 256, 128, 7168, 4096, True),
+    ("gemm2_ep1", 256, 128, 2048, 7168, False),
+]
+
+
 def main():
+    import argparse
+
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--shape", default=None, help="run one shape only (e.g. gemm1_ep8)")
+    ap.add_argument("--groups", type=int, default=None, help="override the group count")
+    ap.add_argument("--iters", type=int, default=20)
+    ap.add_argument("--no-torch", action="store_true")
+    args = ap.parse_args()
     C = kiwi_b200.native()
     torch.manual_seed(0)
-    for name, groups, rows, k, n, swiglu in [
-        ("gemm1_ep8", 32, 1024, 7168, 4096, True),
-        ("gemm2_ep8", 32, 1024, 2048, 7168, False),
-        ("gemm1_ep1", 256, 128, 7168, 4096, True),
-        ("gemm2_ep1", 256, 128, 2048, 7168, False),
-    ]:
+    for name, groups, rows, k, n, swiglu in SHAPES:
+        if args.shape and name != args.shape:
+            continue
+        groups = args.groups or groups
         total = groups * rows
         a = (torch.randn(total, k, device="cuda") * 0.5).bfloat16()
         b = (torch.randn(groups * n, k, device="cuda") * 0.02).bfloat16()
         counts = torch.full((groups,), rows, dtype=torch.int32, device="cuda")
         out = torch.empty(total, n // 2 if swiglu else n, device="cuda", dtype=torch.bfloat16)
         plan = C.ops.GroupedGemm(a, b, groups)
-        ms = timeit(lambda: plan.run(counts, out, swiglu))
+        ms = timeit(lambda: plan.run(counts, out, swiglu), args.iters)
         flops = 2.0 * total * n * k
         bw = (b.numel() * 2 + a.numel() * 2 + out.numel() * 2) / (ms / 1e3) / 1e12
         offs = torch.cumsum(counts, 0).to(torch.int32)
         bt = b.view(groups, n, k).transpose(-2, -1)
-        try:
-            tms = timeit(lambda: torch._grouped_mm(a, bt, offs=offs, out_dtype=torch.bfloat16))
-        except Exception as ex:  # pragma: no cover
-            tms = float("nan")
-            print("torch._grouped_mm failed:", ex, file=sys.stderr)
+        tms = float("nan")
+        if not args.no_torch:
+            try:
+                tms = timeit(lambda: torch._grouped_mm(a, bt, offs=offs, out_dtype=torch.bfloat16), args.iters)
+            except Exception as ex:  # pragma: no cover
+                print("torch._grouped_mm failed:", ex, file=sys.stderr)
         print("RESULT " + json.dumps({"bench": name, "groups": groups, "rows": rows, "k": k, "n": n,
                                       "kiwi_ms": ms, "kiwi_tflops": flops / ms / 1e9,
                                       "kiwi_hbm_TBps_min_traffic": bw,

@@ -7,6 +7,8 @@ Ranks pair up (0<->1, 2<->3, ...).  For each size 8 B .. max (powers of two):
   * kiwi_pingpong: the initiator puts `size` bytes into its partner's heap and
     signals (release add on a flag word); the partner waits (acquire), puts back,
     signals.  One-way latency = round trip / 2 (device %globaltimer, p50).
+  * kiwi_put_ll8 (payloads up to 4 KB): one warp, every 8-byte word carries
+    4 data bytes and the sequence number -- no fence, no separate flag.
   * kiwi_put_bw: back-to-back puts of `size` bytes, one signal at the end.
   * kiwi_get: reads of `size` bytes from the partner's heap.
   * nccl_sendrecv: torch.distributed send/recv ping-pong of the same size,
@@ -41,7 +43,8 @@ def main():
     flag_off = 0
     src_off = 4096
     dst_off = src_off + maxb
-    heap = SymmetricHeap(dst_off + maxb + 4096)
+    ll_base = dst_off + maxb + 4096
+    heap = SymmetricHeap(ll_base + 65536)
     h = heap.native
     g = torch.Generator(device="cuda").manual_seed(1234 + rank)
     src = heap.tensor(src_off, [maxb], torch.uint8)
@@ -61,6 +64,20 @@ def main():
         kdist.barrier()
         assert int(status[0].item()) == 0, f"pingpong timed out at {size}"
         one_way = float(np.percentile(lat.cpu().numpy(), 50)) / 2 / 1e3 if initiator else 0.0
+        # LL8 (data + sequence per 8-byte word, no fence / flag) for payloads up to 4 KB
+        ll8 = 0.0
+        if size <= 4096:
+            words = max(1, size // 4)
+            ll_off = ll_base
+            heap.tensor(ll_off, [words * 8], torch.uint8).zero_()
+            lat2 = torch.zeros(iters, dtype=torch.int64, device="cuda")
+            torch.cuda.synchronize()
+            kdist.barrier()
+            h.pingpong_ll8(peer, initiator, words, iters, 5, ll_off, lat2, status, 5_000_000_000)
+            torch.cuda.synchronize()
+            kdist.barrier()
+            assert int(status[0].item()) == 0, f"ll8 pingpong timed out at {size}"
+            ll8 = float(np.percentile(lat2.cpu().numpy(), 50)) / 2 / 1e3 if initiator else 0.0
         # bandwidth
         flag.zero_()
         el = torch.zeros(1, dtype=torch.int64, device="cuda")
@@ -98,6 +115,7 @@ def main():
             nccl_us = s.elapsed_time(e) / n_it / 2 * 1e3
         row = {"bytes": size,
                "kiwi_put_oneway_us": kdist.max_over_ranks(one_way),
+               "kiwi_put_ll8_oneway_us": kdist.max_over_ranks(ll8),
                "kiwi_put_GBps": kdist.max_over_ranks(bw),
                "kiwi_get_us": kdist.max_over_ranks(get_us),
                "nccl_sendrecv_oneway_us": kdist.max_over_ranks(nccl_us)}

@@ -235,6 +235,93 @@ private:
     CUtensorMap tmap_a1_, tmap_b1_, tmap_a2_, tmap_b2_;
 };
 
+
+/// Transport-only EP op with the reference's dispatch/combine contract.
+class Transport {
+public:
+    Transport(p2p::SymmetricHeap& heap, const py::dict& cfg, uint64_t timeout_ns)
+        : heap_(heap), cfg_(config_from_dict(cfg)), timeout_ns_(timeout_ns) {
+        TORCH_CHECK(heap.size() >= cfg_.heap_bytes, "symmetric heap too small: need ", cfg_.heap_bytes, " bytes");
+        auto dev = torch::Device(torch::kCUDA, c10::cuda::current_device());
+        auto i32 = torch::TensorOptions().dtype(torch::kInt32).device(dev);
+        auto f32 = torch::TensorOptions().dtype(torch::kFloat32).device(dev);
+        auto u8 = torch::TensorOptions().dtype(torch::kUInt8).device(dev);
+        const int64_t el = cfg_.experts_per_rank;
+        const int64_t slots = static_cast<int64_t>(cfg_.slots());
+        epoch_ = torch::zeros({4}, i32);
+        done_ = torch::zeros({4}, i32);
+        counts_ = torch::zeros({el}, i32);
+        cursor_ = torch::zeros({el}, i32);
+        slot_tokens_ = torch::zeros({ep::kMaxTopk}, i32);
+        error_ = torch::zeros({4}, i32);
+        slot_compact_ = torch::full({slots}, -1, i32);
+        recv_count_ = torch::zeros({1}, i32);
+        rows_ = torch::zeros({slots, cfg_.row_bytes}, u8);
+        scales_ = torch::zeros({slots, std::max<int64_t>(cfg_.scale_bytes, 16)}, u8);
+        idx_ = torch::zeros({slots, cfg_.topk}, i32);
+        w_ = torch::zeros({slots, cfg_.topk}, f32);
+        src_pos_ = torch::zeros({slots}, i32);
+        ws_.epoch = reinterpret_cast<uint32_t*>(epoch_.data_ptr<int32_t>());
+        ws_.done_ctas = reinterpret_cast<uint32_t*>(done_.data_ptr<int32_t>());
+        ws_.expert_count = counts_.data_ptr<int32_t>();
+        ws_.cursor = cursor_.data_ptr<int32_t>();
+        ws_.slot_tokens = slot_tokens_.data_ptr<int32_t>();
+        ws_.error = reinterpret_cast<uint32_t*>(error_.data_ptr<int32_t>());
+    }
+
+    py::tuple dispatch(torch::Tensor x, torch::Tensor idx, torch::Tensor w) {
+        TORCH_CHECK(x.scalar_type() == torch::kBFloat16 && x.is_contiguous() && x.size(1) == cfg_.hidden,
+                    "x must be contiguous bf16 [T, hidden]");
+        TORCH_CHECK(x.size(0) <= cfg_.max_tokens, "more tokens than max_tokens");
+        TORCH_CHECK(idx.scalar_type() == torch::kInt32 && idx.is_contiguous() && idx.size(1) == cfg_.topk, "idx");
+        TORCH_CHECK(w.scalar_type() == torch::kFloat32 && w.is_contiguous() && w.size(1) == cfg_.topk, "w");
+        cudaStream_t s = cur_stream();
+        idx_in_ = idx;
+        tokens_ = static_cast<int>(x.size(0));
+        ep::launch_begin(cfg_, ws_, s);
+        ep::launch_dispatch(cfg_, heap_.view(), reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()),
+                            idx.data_ptr<int32_t>(), w.data_ptr<float>(), tokens_, ws_, 0, s);
+        ep::launch_recv_count(cfg_, heap_.view(), ws_, timeout_ns_, s);
+        ep::launch_recv_compact(cfg_, heap_.view(), ws_, slot_compact_.data_ptr<int32_t>(),
+                                recv_count_.data_ptr<int32_t>(), s);
+        ep::launch_gather_rows(cfg_, heap_.view(), ws_, slot_compact_.data_ptr<int32_t>(), rows_.data_ptr<uint8_t>(),
+                               scales_.data_ptr<uint8_t>(), idx_.data_ptr<int32_t>(), w_.data_ptr<float>(),
+                               src_pos_.data_ptr<int32_t>(), s);
+        return py::make_tuple(rows_, w_, scales_, idx_, recv_count_);
+    }
+
+    torch::Tensor combine(torch::Tensor rows, torch::Tensor out) {
+        TORCH_CHECK(rows.scalar_type() == torch::kBFloat16 && rows.is_contiguous() && rows.size(1) == cfg_.hidden,
+                    "rows must be contiguous bf16 [>= recv_count, hidden]");
+        TORCH_CHECK(out.scalar_type() == torch::kBFloat16 && out.is_contiguous() && out.size(0) >= tokens_ &&
+                        out.size(1) == cfg_.hidden,
+                    "out must be contiguous bf16 [T, hidden]");
+        TORCH_CHECK(idx_in_.defined(), "combine needs a prior dispatch");
+        cudaStream_t s = cur_stream();
+        ep::launch_combine_rows(cfg_, heap_.view(), reinterpret_cast<const __nv_bfloat16*>(rows.data_ptr()),
+                                src_pos_.data_ptr<int32_t>(), recv_count_.data_ptr<int32_t>(), ws_, s);
+        ep::launch_combine_recv(cfg_, heap_.view(), idx_in_.data_ptr<int32_t>(), tokens_,
+                                reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), ws_, timeout_ns_, s);
+        return out;
+    }
+
+    py::tuple error() const {
+        auto e = error_.cpu();
+        return py::make_tuple(e[0].item<int>(), e[1].item<int>(), e[2].item<int>(), e[3].item<int>());
+    }
+    torch::Tensor src_token_pos() const { return src_pos_; }
+    py::dict config() const { return config_to_dict(cfg_); }
+
+private:
+    p2p::SymmetricHeap& heap_;
+    ep::EpConfig cfg_;
+    uint64_t timeout_ns_;
+    int tokens_ = 0;
+    torch::Tensor epoch_, done_, counts_, cursor_, slot_tokens_, error_, slot_compact_, recv_count_, rows_, scales_,
+        idx_, w_, src_pos_, idx_in_;
+    ep::EpWorkspace ws_{};
+};
+
 }  // namespace
 
 void register_ep(py::module_& m) {
@@ -248,6 +335,14 @@ void register_ep(py::module_& m) {
                                cur_stream());
           },
           "Top-k routing with softmax over the selected logits (fp32 logits [T, E]).");
+    py::class_<Transport>(e, "Transport")
+        .def(py::init<p2p::SymmetricHeap&, const py::dict&, uint64_t>(), py::arg("heap"), py::arg("config"),
+             py::arg("timeout_ns") = 5000000000ull, py::keep_alive<1, 2>())
+        .def("dispatch", &Transport::dispatch)
+        .def("combine", &Transport::combine)
+        .def("error", &Transport::error)
+        .def_property_readonly("src_token_pos", &Transport::src_token_pos)
+        .def_property_readonly("config", &Transport::config);
     py::class_<MoeLayer>(e, "MoeLayer")
         .def(py::init<p2p::SymmetricHeap&, const py::dict&, int64_t, torch::Tensor, torch::Tensor, uint64_t>(),
              py::arg("heap"), py::arg("config"), py::arg("ffn"), py::arg("w13"), py::arg("w2"),

@@ -570,6 +570,91 @@ __global__ void __launch_bounds__(kThreads) combine_recv_kernel(EpConfig c, p2p:
     }
 }
 
+
+// ---------------------------------------------------------------------------
+// Transport-only path (rows in, rows out), MORI semantics.
+// ---------------------------------------------------------------------------
+
+__global__ void __launch_bounds__(1024) recv_compact_kernel(EpConfig c, p2p::HeapView h, EpWorkspace ws,
+                                                            int32_t* slot_compact, int32_t* recv_count) {
+    __shared__ int32_t s_scan[1024];
+    __shared__ int32_t s_base;
+    const uint32_t epoch = *reinterpret_cast<volatile uint32_t*>(ws.epoch);
+    const uint8_t* base = h.base[h.rank];
+    if (threadIdx.x == 0) s_base = 0;
+    __syncthreads();
+    for (uint64_t s0 = 0; s0 < c.slots(); s0 += blockDim.x) {
+        const uint64_t s = s0 + threadIdx.x;
+        int valid = 0;
+        if (s < c.slots()) {
+            const int src = static_cast<int>(s / c.max_tokens);
+            const int t = static_cast<int>(s % c.max_tokens);
+            valid = (t < ws.slot_tokens[src] && ld_cg_u32(meta_ptr(c, base, s)) == epoch) ? 1 : 0;
+        }
+        s_scan[threadIdx.x] = valid;
+        __syncthreads();
+        for (int d = 1; d < blockDim.x; d <<= 1) {
+            const int v = threadIdx.x >= static_cast<unsigned>(d) ? s_scan[threadIdx.x - d] : 0;
+            __syncthreads();
+            s_scan[threadIdx.x] += v;
+            __syncthreads();
+        }
+        if (s < c.slots()) slot_compact[s] = valid ? s_base + s_scan[threadIdx.x] - 1 : -1;
+        __syncthreads();
+        if (threadIdx.x == blockDim.x - 1) s_base += s_scan[threadIdx.x];
+        __syncthreads();
+    }
+    if (threadIdx.x == 0) *recv_count = s_base;
+}
+
+__global__ void __launch_bounds__(kThreads) gather_rows_kernel(EpConfig c, p2p::HeapView h, EpWorkspace ws,
+                                                               const int32_t* slot_compact, uint8_t* out_rows,
+                                                               uint8_t* out_scales, int32_t* out_idx, float* out_w,
+                                                               int32_t* out_src_pos) {
+    const int lane = threadIdx.x & 31;
+    const int warps = gridDim.x * (blockDim.x / 32);
+    const uint8_t* base = h.base[h.rank];
+    for (uint64_t s = (blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x) / 32; s < c.slots();
+         s += warps) {
+        const int pos = slot_compact[s];
+        if (pos < 0) continue;
+        const uint8_t* mp = meta_ptr(c, base, s);
+        if (lane < c.topk) {
+            out_idx[static_cast<int64_t>(pos) * c.topk + lane] =
+                static_cast<int32_t>(ld_cg_u32(mp + sizeof(DispatchMetaHeader) + 4 * lane));
+            out_w[static_cast<int64_t>(pos) * c.topk + lane] =
+                ld_cg_f32(mp + sizeof(DispatchMetaHeader) + 4 * c.topk + 4 * lane);
+        }
+        if (lane == 0) out_src_pos[pos] = static_cast<int32_t>(s);
+        const uint8_t* row = base + c.row_off(s);
+        uint8_t* dst = out_rows + static_cast<int64_t>(pos) * c.row_bytes;
+        for (int off = lane * 16; off < c.row_bytes; off += 512) ptx::st_v4(dst + off, ld_cg_v4(row + off));
+        if (c.scale_bytes) {
+            const uint8_t* sc = base + c.scale_off(s);
+            uint8_t* sd = out_scales + static_cast<int64_t>(pos) * c.scale_bytes;
+            for (int off = lane * 16; off < c.scale_bytes; off += 512) ptx::st_v4(sd + off, ld_cg_v4(sc + off));
+        }
+    }
+}
+
+__global__ void __launch_bounds__(kThreads) combine_rows_kernel(EpConfig c, p2p::HeapView h,
+                                                                const __nv_bfloat16* rows, const int32_t* src_pos,
+                                                                const int32_t* recv_count, EpWorkspace ws) {
+    const int lane = threadIdx.x & 31;
+    const int warps = gridDim.x * (blockDim.x / 32);
+    const uint32_t epoch = *reinterpret_cast<volatile uint32_t*>(ws.epoch);
+    const int n = *recv_count;
+    for (int i = (blockIdx.x * blockDim.x + threadIdx.x) / 32; i < n; i += warps) {
+        const int sp = src_pos[i];
+        const int src = sp / c.max_tokens;
+        const int t = sp % c.max_tokens;
+        uint8_t* dst = h.base[src] + c.comb_off(c.rank, t);
+        const __nv_bfloat16* r = rows + static_cast<int64_t>(i) * c.hidden;
+        for (int col = lane * 8; col < c.hidden; col += 256) ptx::st_v4(dst + 2ull * col, ptx::ld_v4(r + col));
+    }
+    grid_done_signal(c, h, &ws.done_ctas[1], c.combine_flag(c.rank), (static_cast<uint64_t>(epoch) << 32) | 1u);
+}
+
 int default_grid() {
     static int n = 0;
     if (n == 0) {
@@ -645,6 +730,26 @@ void launch_combine_recv(const EpConfig& c, const p2p::HeapView& h, const int32_
                          __nv_bfloat16* out, const EpWorkspace& ws, uint64_t timeout_ns, cudaStream_t s) {
     const int grid = 2 * default_grid();
     combine_recv_kernel<<<grid, kThreads, 0, s>>>(c, h, idx, tokens, out, ws, timeout_ns);
+    KIWI_CUDA_CHECK(cudaGetLastError());
+}
+
+void launch_recv_compact(const EpConfig& c, const p2p::HeapView& h, const EpWorkspace& ws, int32_t* slot_compact,
+                         int32_t* recv_count, cudaStream_t s) {
+    recv_compact_kernel<<<1, 1024, 0, s>>>(c, h, ws, slot_compact, recv_count);
+    KIWI_CUDA_CHECK(cudaGetLastError());
+}
+
+void launch_gather_rows(const EpConfig& c, const p2p::HeapView& h, const EpWorkspace& ws,
+                        const int32_t* slot_compact, uint8_t* out_rows, uint8_t* out_scales, int32_t* out_idx,
+                        float* out_w, int32_t* out_src_pos, cudaStream_t s) {
+    gather_rows_kernel<<<2 * default_grid(), kThreads, 0, s>>>(c, h, ws, slot_compact, out_rows, out_scales, out_idx,
+                                                              out_w, out_src_pos);
+    KIWI_CUDA_CHECK(cudaGetLastError());
+}
+
+void launch_combine_rows(const EpConfig& c, const p2p::HeapView& h, const __nv_bfloat16* rows,
+                         const int32_t* src_pos, const int32_t* recv_count, const EpWorkspace& ws, cudaStream_t s) {
+    combine_rows_kernel<<<2 * default_grid(), kThreads, 0, s>>>(c, h, rows, src_pos, recv_count, ws);
     KIWI_CUDA_CHECK(cudaGetLastError());
 }
 

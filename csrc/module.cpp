@@ -437,6 +437,34 @@ PYBIND11_MODULE(_C, m) {
           },
           py::arg("slots") = 16, py::arg("slot_lines") = 2, py::arg("producers") = 2,
           py::arg("msgs_per_producer") = 100, py::arg("warps") = 4, py::arg("seed") = 5);
+    b.def("invoke_throughput",
+          [](uint32_t endpoints, uint32_t threads, uint32_t msgs, uint32_t bytes, uint64_t cap) {
+              bench::ThroughputResult r;
+              {
+                  py::gil_scoped_release nogil;
+                  r = bench::invoke_throughput(endpoints, threads, msgs, bytes, cap);
+              }
+              py::dict d;
+              d["messages"] = r.messages;
+              d["device_ns"] = r.device_ns;
+              d["ok"] = r.ok;
+              return d;
+          },
+          py::arg("endpoints") = 4, py::arg("threads") = 1, py::arg("msgs_per_endpoint") = 10000,
+          py::arg("payload_bytes") = 8, py::arg("capacity") = 4096);
+    b.def("push_cost",
+          [](uint32_t msgs, uint32_t bytes) {
+              bench::PushCostResult r;
+              {
+                  py::gil_scoped_release nogil;
+                  r = bench::push_cost(msgs, bytes);
+              }
+              py::dict d;
+              d["cycles_per_push"] = r.cycles_per_push;
+              d["ok"] = r.ok;
+              return d;
+          },
+          py::arg("msgs") = 10000, py::arg("payload_bytes") = 8);
     b.def("h2d_timeout_test", [](uint64_t ns) {
         py::gil_scoped_release nogil;
         return bench::h2d_timeout_test(ns);

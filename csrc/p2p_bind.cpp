@@ -7,6 +7,7 @@
 #include <torch/extension.h>
 #include <unistd.h>
 
+#include "kiwi/p2p/context.hpp"
 #include "kiwi/p2p/heap.hpp"
 #include "kiwi/p2p/p2p_ops.hpp"
 
@@ -46,6 +47,20 @@ void register_p2p(py::module_& m) {
           py::arg("fd"), py::arg("timeout_s") = 60.0, py::call_guard<py::gil_scoped_release>());
     p.def("multicast_supported", &SymmetricHeap::multicast_supported);
 
+    py::class_<Context>(p, "Context")
+        .def(py::init<SymmetricHeap&, size_t, uint64_t>(), py::arg("heap"), py::arg("num_queues") = 1,
+             py::arg("queue_capacity") = 2048, py::keep_alive<1, 2>())
+        .def("spawn_proxy_threads", &Context::spawn_proxy_threads, py::arg("num_threads") = 1,
+             py::arg("cpus") = std::vector<int>{})
+        .def("join_proxy_threads", &Context::join_proxy_threads, py::call_guard<py::gil_scoped_release>())
+        .def_property_readonly("copies_issued", &Context::copies_issued)
+        .def("ce_put_selftest",
+             [](Context& c, int dst, uint64_t src_off, uint64_t dst_off, uint64_t bytes, uint32_t n,
+                uint64_t flag_off, uint64_t counter_off, torch::Tensor status, uint64_t timeout_ns) {
+                 launch_ce_put_selftest(c.device_context(), dst, src_off, dst_off, bytes, n, flag_off, counter_off,
+                                        u32_ptr(status), timeout_ns, cur_stream());
+             });
+
     py::class_<SymmetricHeap>(p, "SymmetricHeap")
         .def(py::init([](int device, size_t bytes, int rank, int world, const std::string& job, bool mc,
                          py::object barrier) {
@@ -81,6 +96,12 @@ void register_p2p(py::module_& m) {
                 uint32_t max_blocks, uint64_t timeout_ns) {
                  launch_pingpong(h.view(), peer, initiator, bytes, iters, warmup, src_off, dst_off, flag_off,
                                  u64_ptr(lat), u32_ptr(status), max_blocks, timeout_ns, cur_stream());
+             })
+        .def("pingpong_ll8",
+             [](SymmetricHeap& h, int peer, bool initiator, uint32_t words, uint64_t iters, uint64_t warmup,
+                uint64_t buf_off, torch::Tensor lat, torch::Tensor status, uint64_t timeout_ns) {
+                 launch_pingpong_ll8(h.view(), peer, initiator, words, iters, warmup, buf_off, u64_ptr(lat),
+                                     u32_ptr(status), timeout_ns, cur_stream());
              })
         .def("put_bw",
              [](SymmetricHeap& h, int peer, bool sender, uint64_t bytes, uint64_t reps, uint64_t src_off,

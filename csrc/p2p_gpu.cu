@@ -69,6 +69,46 @@ __global__ void __launch_bounds__(512) pingpong_kernel(HeapView h, int peer, int
     }
 }
 
+/// LL8 ping-pong (one warp, messages of `words` 32-bit words): data and
+/// sequence travel together, so there is no fence and no separate flag.
+__global__ void pingpong_ll8_kernel(HeapView h, int peer, int initiator, uint32_t words, uint64_t iters,
+                                    uint64_t warmup, uint64_t buf_off, uint64_t* lat_ns, uint32_t* status,
+                                    uint64_t timeout_ns) {
+    __shared__ uint32_t msg[1024];
+    const uint64_t* inbox = reinterpret_cast<const uint64_t*>(h.base[h.rank] + buf_off);
+    for (uint32_t i = threadIdx.x; i < words; i += 32) msg[i] = i * 2654435761u;
+    __syncwarp();
+    for (uint64_t it = 0; it < iters + warmup; ++it) {
+        const uint32_t seq = static_cast<uint32_t>(it + 1);
+        uint64_t t0 = 0;
+        if (initiator) {
+            if (threadIdx.x == 0) t0 = ptx::globaltimer();
+            put_ll8_warp(h, peer, buf_off, msg, words, seq);
+            if (recv_ll8_warp(inbox, msg, words, seq, timeout_ns) != Status::kOk) {
+                if (threadIdx.x == 0) record_error(status, Status::kTimeout, static_cast<uint32_t>(it));
+                return;
+            }
+            if (threadIdx.x == 0 && it >= warmup) lat_ns[it - warmup] = ptx::globaltimer() - t0;
+        } else {
+            if (recv_ll8_warp(inbox, msg, words, seq, timeout_ns) != Status::kOk) {
+                if (threadIdx.x == 0) record_error(status, Status::kTimeout, static_cast<uint32_t>(it));
+                return;
+            }
+            put_ll8_warp(h, peer, buf_off, msg, words, seq);
+        }
+        __syncwarp();
+    }
+}
+
+void launch_pingpong_ll8(const HeapView& h, int peer, bool initiator, uint32_t words, uint64_t iters,
+                         uint64_t warmup, uint64_t buf_off, uint64_t* lat_ns, uint32_t* status, uint64_t timeout_ns,
+                         cudaStream_t s) {
+    if (words == 0 || words > 1024) throw kiwi::error("pingpong_ll8: 1..1024 words");
+    pingpong_ll8_kernel<<<1, 32, 0, s>>>(h, peer, initiator ? 1 : 0, words, iters, warmup, buf_off, lat_ns, status,
+                                         timeout_ns);
+    KIWI_CUDA_CHECK(cudaGetLastError());
+}
+
 /// One-directional put bandwidth: `reps` back-to-back puts of `bytes`, one
 /// signal per block at the end; the receiver answers with one signal.
 __global__ void __launch_bounds__(512) put_bw_kernel(HeapView h, int peer, int sender, uint64_t bytes, uint64_t reps,
@@ -269,6 +309,64 @@ void launch_wait_flag(const HeapView& h, uint64_t flag_off, uint64_t want, uint3
 void launch_heap_barrier(const HeapView& h, uint64_t flag_off, uint64_t round, uint32_t* status, uint64_t timeout_ns,
                          cudaStream_t s) {
     heap_barrier_kernel<<<1, 32, 0, s>>>(h, flag_off, round, status, timeout_ns);
+    KIWI_CUDA_CHECK(cudaGetLastError());
+}
+
+}  // namespace kiwi::p2p
+
+// ---------------------------------------------------------------------------
+// Control-plane self test: one warp posts `n` copy-engine puts of `bytes`
+// (src_off -> dst_off + i*bytes on rank `dst`), each followed by a flag the
+// proxy writes; the warp waits (bounded) for every flag and the local counter.
+// ---------------------------------------------------------------------------
+#include "kiwi/p2p/ghandle.cuh"
+
+namespace kiwi::p2p {
+
+__global__ void ce_put_selftest_kernel(GContext ctx, int dst, uint64_t src_off, uint64_t dst_off, uint64_t bytes,
+                                       uint32_t n, uint64_t flag_off, uint64_t counter_off, uint32_t* status,
+                                       uint64_t timeout_ns) {
+    GHandle g(ctx, 0);
+    for (uint32_t i = 0; i < n; ++i) {
+        CePutDesc d{};
+        d.dst_rank = static_cast<uint32_t>(dst);
+        d.flag_rank = static_cast<uint32_t>(dst);
+        d.dst_off = dst_off + i * bytes;
+        d.src_off = src_off;
+        d.bytes = bytes;
+        d.flag_off = flag_off;
+        d.flag_value = i + 1;
+        d.counter_off = counter_off;
+        d.counter_value = i + 1;
+        if (g.post_ce_put(d, timeout_ns) != Status::kOk) {
+            if (ptx::lane_id() == 0) status[0] = 1;
+            return;
+        }
+    }
+    if (dst == ctx.heap.rank) {
+        if (g.wait_local(flag_off, Cmp::kGe, n, timeout_ns) != Status::kOk) {
+            if (ptx::lane_id() == 0) status[0] = 2;
+            return;
+        }
+    }
+    if (g.wait_local(counter_off, Cmp::kGe, n, timeout_ns) != Status::kOk) {
+        if (ptx::lane_id() == 0) status[0] = 3;
+        return;
+    }
+    if (g.post_host_signal(ctx.heap.rank, flag_off + 8, 0xabcdull, timeout_ns) != Status::kOk) {
+        if (ptx::lane_id() == 0) status[0] = 4;
+        return;
+    }
+    if (g.wait_local(flag_off + 8, Cmp::kEq, 0xabcdull, timeout_ns) != Status::kOk) {
+        if (ptx::lane_id() == 0) status[0] = 5;
+    }
+}
+
+void launch_ce_put_selftest(const GContext& ctx, int dst, uint64_t src_off, uint64_t dst_off, uint64_t bytes,
+                            uint32_t n, uint64_t flag_off, uint64_t counter_off, uint32_t* status,
+                            uint64_t timeout_ns, cudaStream_t s) {
+    ce_put_selftest_kernel<<<1, 32, 0, s>>>(ctx, dst, src_off, dst_off, bytes, n, flag_off, counter_off, status,
+                                            timeout_ns);
     KIWI_CUDA_CHECK(cudaGetLastError());
 }
 

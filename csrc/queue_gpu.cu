@@ -9,6 +9,9 @@
 #include <cuda_runtime.h>
 
 #include <atomic>
+#include <chrono>
+
+#include "kiwi/invoke/progress.hpp"
 #include <cstring>
 #include <thread>
 
@@ -568,6 +571,122 @@ RttResult rtt_lab(uint64_t iters, uint64_t warmup, uint32_t pollers, uint32_t mi
     r.total_cycles = tot[1];
     r.status = stv[0];
     r.ok = stv[0] == 0 && stv[1] == 1;
+    return r;
+}
+
+
+// ---------------------------------------------------------------------------
+// Invoke throughput and push cost (reference: benchmarks/invoke/
+// bench_throughput.hip.cpp:39, bench_overhead.hip.cpp:54-119)
+// ---------------------------------------------------------------------------
+
+__global__ void invoke_throughput_kernel(DeviceContext<SPSCD2HQueue>* ctx, uint8_t cb, uint32_t msgs,
+                                         uint32_t payload_words, uint64_t* t_begin_end, uint32_t* status,
+                                         uint64_t timeout_ns) {
+    auto h = ctx->get_device_handle(blockIdx.x);
+    const uint32_t lane = ptx::lane_id();
+    if (blockIdx.x == 0 && lane == 0) t_begin_end[0] = ptx::globaltimer();
+    for (uint32_t i = 0; i < msgs; ++i) {
+        const uint64_t w = (static_cast<uint64_t>(blockIdx.x) << 32) | i;
+        ptx::Deadline dl(timeout_ns);
+        while (!h.queue.push_lanes(w, payload_words * 8, cb)) {
+            if (dl.expired()) {
+                if (lane == 0) status[0] = 1;
+                ctx->save_device_handle(blockIdx.x, h);
+                return;
+            }
+        }
+    }
+    ctx->save_device_handle(blockIdx.x, h);
+    __syncwarp();
+    if (lane == 0) atomicMax(reinterpret_cast<unsigned long long*>(&t_begin_end[1]), ptx::globaltimer());
+}
+
+ThroughputResult invoke_throughput(uint32_t endpoints, uint32_t threads, uint32_t msgs_per_endpoint,
+                                   uint32_t payload_bytes, uint64_t capacity) {
+    if (payload_bytes % 8 || payload_bytes > 256) throw kiwi::error("invoke_throughput: payload 8..256, multiple of 8");
+    kiwi::invoke::Context<SPSCD2HQueue> ctx(endpoints, capacity, MemKind::kMappedPinned);
+    std::atomic<uint64_t> count{0};
+    const uint8_t cb = ctx.register_raw_callback(
+        [&](const uint8_t*, uint32_t) { count.fetch_add(1, std::memory_order_relaxed); },
+        kiwi::invoke::CallbackBase::kAnySize);
+    DevBuf<uint64_t> t(2);
+    DevBuf<uint32_t> status(1);
+    kiwi::invoke::ProgressThreads<SPSCD2HQueue> pt(ctx);
+    int dev = 0;
+    cudaGetDevice(&dev);
+    auto cpus = topology::gpu_local_cpus(dev);
+    if (cpus.size() > 1) cpus.erase(cpus.begin());
+    pt.start(threads, cpus);
+    invoke_throughput_kernel<<<endpoints, 32>>>(ctx.device_context(), cb, msgs_per_endpoint, payload_bytes / 8, t.p,
+                                                status.p, 2000000000ull);
+    KIWI_CUDA_CHECK(cudaGetLastError());
+    KIWI_CUDA_CHECK(cudaDeviceSynchronize());
+    const uint64_t want = static_cast<uint64_t>(endpoints) * msgs_per_endpoint;
+    const auto deadline = std::chrono::steady_clock::now() + std::chrono::seconds(10);
+    while (count.load() < want && std::chrono::steady_clock::now() < deadline) std::this_thread::yield();
+    pt.stop();
+    uint64_t tv[2];
+    uint32_t st = 0;
+    KIWI_CUDA_CHECK(cudaMemcpy(tv, t.p, sizeof(tv), cudaMemcpyDeviceToHost));
+    KIWI_CUDA_CHECK(cudaMemcpy(&st, status.p, 4, cudaMemcpyDeviceToHost));
+    ThroughputResult r;
+    r.messages = count.load();
+    r.device_ns = tv[1] - tv[0];
+    r.ok = st == 0 && r.messages == want;
+    return r;
+}
+
+__global__ void push_cost_kernel(SpscD2HHandle h, uint32_t msgs, uint32_t bytes, uint64_t* cycles, uint32_t* status) {
+    const uint32_t lane = ptx::lane_id();
+    uint64_t total = 0;
+    for (uint32_t i = 0; i < msgs; ++i) {
+        const uint64_t c0 = ptx::clock64();
+        bool ok = h.push_lanes(i, bytes, 0);
+        const uint64_t c1 = ptx::clock64();
+        if (!ok) {
+            // Ring full: wait for the host without counting the wait.
+            ptx::Deadline dl(2000000000ull);
+            while (!h.push_lanes(i, bytes, 0)) {
+                if (dl.expired()) {
+                    if (lane == 0) status[0] = 1;
+                    return;
+                }
+            }
+        } else {
+            total += c1 - c0;
+        }
+    }
+    if (lane == 0) cycles[0] = total;
+}
+
+PushCostResult push_cost(uint32_t msgs, uint32_t bytes) {
+    SPSCD2HQueue q(1 << 16, MemKind::kMappedPinned);
+    DevBuf<uint64_t> cyc(1);
+    DevBuf<uint32_t> status(1);
+    cudaStream_t stream;
+    KIWI_CUDA_CHECK(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking));
+    push_cost_kernel<<<1, 32, 0, stream>>>(q.device_handle(), msgs, bytes, cyc.p, status.p);
+    KIWI_CUDA_CHECK(cudaGetLastError());
+    alignas(64) uint8_t buf[kMaxMessageBytes];
+    uint32_t meta, b;
+    uint64_t popped = 0, idle = 0;
+    while (popped < msgs) {
+        if (q.try_pop(buf, &meta, &b)) {
+            ++popped;
+        } else if ((++idle & 0xfffff) == 0 && cudaStreamQuery(stream) != cudaErrorNotReady) {
+            break;
+        }
+    }
+    KIWI_CUDA_CHECK(cudaStreamSynchronize(stream));
+    cudaStreamDestroy(stream);
+    uint64_t c = 0;
+    uint32_t st = 0;
+    KIWI_CUDA_CHECK(cudaMemcpy(&c, cyc.p, 8, cudaMemcpyDeviceToHost));
+    KIWI_CUDA_CHECK(cudaMemcpy(&st, status.p, 4, cudaMemcpyDeviceToHost));
+    PushCostResult r;
+    r.cycles_per_push = msgs ? static_cast<double>(c) / msgs : 0;
+    r.ok = st == 0 && popped == msgs;
     return r;
 }
 

@@ -48,6 +48,23 @@ RttResult pcie_floor(uint64_t iters, uint64_t warmup, int cpu, uint64_t timeout_
 RttResult rtt_lab(uint64_t iters, uint64_t warmup, uint32_t pollers, uint32_t mirrors, uint32_t stagger_ns,
                   uint32_t fence, uint32_t pipeline, int cpu, uint32_t initial_delay_ns = 0);
 
+struct ThroughputResult {
+    uint64_t messages = 0;
+    uint64_t device_ns = 0;  // first push to last push (device %globaltimer)
+    bool ok = false;
+};
+/// `endpoints` producer warps invoke a counting callback `msgs_per_endpoint`
+/// times each; `threads` native progress threads consume.
+ThroughputResult invoke_throughput(uint32_t endpoints, uint32_t threads, uint32_t msgs_per_endpoint,
+                                   uint32_t payload_bytes, uint64_t capacity);
+
+struct PushCostResult {
+    double cycles_per_push = 0;
+    bool ok = false;
+};
+/// SM cycles one warp spends in push_lanes (ring never full: host drains).
+PushCostResult push_cost(uint32_t msgs, uint32_t bytes);
+
 struct PushTestResult {
     uint64_t popped = 0;
     uint64_t mismatches = 0;     // payload / length / metadata errors

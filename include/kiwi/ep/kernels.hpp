@@ -61,4 +61,23 @@ void launch_combine_send(const EpConfig& c, const p2p::HeapView& h, const __nv_b
 void launch_combine_recv(const EpConfig& c, const p2p::HeapView& h, const int32_t* idx, int tokens,
                          __nv_bfloat16* out, const EpWorkspace& ws, uint64_t timeout_ns, cudaStream_t s);
 
+// ---- transport-only (MORI-compatible) path ----
+
+/// One block: deterministic compaction of this round's valid slots in
+/// (source rank, token) order; slot_compact[s] = output row or -1, *recv_count = total.
+/// Call after launch_recv_count (which waited for every source).
+void launch_recv_compact(const EpConfig& c, const p2p::HeapView& h, const EpWorkspace& ws, int32_t* slot_compact,
+                         int32_t* recv_count, cudaStream_t s);
+
+/// Copies each valid slot's row (wire bytes), scales, top-k ids and weights into
+/// the compacted outputs and records src_pos = src * max_tokens + token.
+void launch_gather_rows(const EpConfig& c, const p2p::HeapView& h, const EpWorkspace& ws,
+                        const int32_t* slot_compact, uint8_t* out_rows, uint8_t* out_scales, int32_t* out_idx,
+                        float* out_w, int32_t* out_src_pos, cudaStream_t s);
+
+/// Sends row i of `rows` (bf16 [recv_count, hidden]) to its token's rank
+/// (src_pos[i]); the last CTA signals every rank's combine flag.
+void launch_combine_rows(const EpConfig& c, const p2p::HeapView& h, const __nv_bfloat16* rows,
+                         const int32_t* src_pos, const int32_t* recv_count, const EpWorkspace& ws, cudaStream_t s);
+
 }  // namespace kiwi::ep

@@ -35,8 +35,30 @@ KIWI_HD void put_word(uint64_t (&w)[N], uint32_t& off, const T& v) {
     }
     if constexpr (sizeof(T) == 1 || sizeof(T) == 2 || sizeof(T) == 4 || sizeof(T) == 8) {
         const uint32_t word = off / 8, shift = 8 * (off % 8);
+        if (shift == 0) {
+            w[word] |= u;
+            off += sizeof(T);
+            return;
+        }
         w[word] |= u << shift;
         if (shift + 8 * sizeof(T) > 64) w[word + 1] |= u >> (64 - shift);
+    } else if constexpr (sizeof(T) % 8 == 0 && alignof(T) >= 8) {
+        // 8-byte-aligned structs (descriptors): word by word.
+        if (off % 8 == 0) {
+            for (uint32_t i = 0; i < sizeof(T) / 8; ++i) {
+                uint64_t t;
+                memcpy(&t, reinterpret_cast<const char*>(&v) + 8 * i, 8);
+                w[off / 8 + i] = t;
+            }
+        } else {
+            for (uint32_t i = 0; i < sizeof(T) / 8; ++i) {
+                uint64_t t;
+                memcpy(&t, reinterpret_cast<const char*>(&v) + 8 * i, 8);
+                const uint32_t o = off + 8 * i, shift = 8 * (o % 8);
+                w[o / 8] |= t << shift;
+                w[o / 8 + 1] |= t >> (64 - shift);
+            }
+        }
     } else {
         // Other sizes: byte by byte (constant offsets; still register resident when unrolled).
         const uint8_t* b = reinterpret_cast<const uint8_t*>(&v);

@@ -8,7 +8,9 @@
 // peer's heap itself (the host/queue path carries control only), so:
 //   put      = warp- or block-cooperative 16-byte stores to the peer mapping
 //   signal   = st.release.sys / red.release.sys.add on the peer's flag word
-//   wait     = ld.acquire.sys polling with a deadline (never unbounded)
+//   wait     = ld.relaxed.sys polling with a deadline (never unbounded), then
+//              one fence.acq_rel.sys
+//   put_ll8  = small messages whose 8-byte words carry data + sequence (no fence)
 //   get      = 16-byte loads from the peer mapping
 // Ordering: a signal issued after __syncwarp()/__syncthreads() releases every
 // store the warp/block made before it (PTX release is cumulative over writes
@@ -94,13 +96,52 @@ KIWI_DEV bool cmp_ok(uint64_t v, Cmp c, uint64_t want) {
 
 /// Waits (one thread) until *flag satisfies `c` against `want`, or the
 /// deadline passes (returns kTimeout; the caller decides what to record).
+/// Polls with relaxed system-scope loads and issues one acquire fence after
+/// the value is seen, instead of paying an acquire on every poll.
 KIWI_DEV Status wait(const uint64_t* flag, Cmp c, uint64_t want, uint64_t timeout_ns) {
-    if (cmp_ok(ptx::ld_acquire_sys_u64(flag), c, want)) return Status::kOk;
-    ptx::Deadline dl(timeout_ns);
-    while (!cmp_ok(ptx::ld_acquire_sys_u64(flag), c, want)) {
-        if (dl.expired()) return Status::kTimeout;
+    if (!cmp_ok(ptx::ld_relaxed_sys_u64(flag), c, want)) {
+        ptx::Deadline dl(timeout_ns);
+        while (!cmp_ok(ptx::ld_relaxed_sys_u64(flag), c, want)) {
+            if (dl.expired()) return Status::kTimeout;
+        }
     }
+    ptx::fence_acq_rel_sys();
     return Status::kOk;
+}
+
+// ---- LL8 small-message path: every 8-byte word carries 4 data bytes and a
+// 32-bit sequence number, so a receiver that sees the sequence in a word sees
+// its data; no fence or flag is needed (8-byte single-copy atomicity only).
+
+/// Warp-cooperative LL8 put of `nwords` 32-bit words into rank's heap at dst_off
+/// (8 bytes per word on the wire).
+KIWI_DEV void put_ll8_warp(const HeapView& h, int rank, uint64_t dst_off, const uint32_t* src, uint32_t nwords,
+                           uint32_t seq) {
+    uint64_t* dst = reinterpret_cast<uint64_t*>(h.base[rank] + dst_off);
+    for (uint32_t i = ptx::lane_id(); i < nwords; i += 32) {
+        ptx::st_volatile_u64(dst + i, static_cast<uint64_t>(src[i]) | (static_cast<uint64_t>(seq) << 32));
+    }
+}
+
+/// Warp-cooperative LL8 receive: waits until every word of the local buffer
+/// carries `seq`, copying the data words to `out`.  Returns kTimeout on expiry.
+KIWI_DEV Status recv_ll8_warp(const uint64_t* local, uint32_t* out, uint32_t nwords, uint32_t seq,
+                              uint64_t timeout_ns) {
+    bool ok = true;
+    for (uint32_t i = ptx::lane_id(); i < nwords; i += 32) {
+        ptx::Deadline dl(timeout_ns);
+        uint64_t v = ptx::ld_volatile_u64(local + i);
+        while (static_cast<uint32_t>(v >> 32) != seq) {
+            if (dl.expired()) {
+                ok = false;
+                break;
+            }
+            v = ptx::ld_volatile_u64(local + i);
+        }
+        if (!ok) break;
+        out[i] = static_cast<uint32_t>(v);
+    }
+    return __all_sync(ptx::kFullMask, ok) ? Status::kOk : Status::kTimeout;
 }
 
 // ---- NVLS multimem (one instruction reaches every rank bound to the object) ----

@@ -3,6 +3,7 @@
 
 #include <cuda_runtime.h>
 
+#include "kiwi/p2p/context.hpp"
 #include "kiwi/p2p/heap.hpp"
 
 namespace kiwi::p2p {
@@ -10,6 +11,10 @@ namespace kiwi::p2p {
 void launch_pingpong(const HeapView& h, int peer, bool initiator, uint64_t bytes, uint64_t iters, uint64_t warmup,
                      uint64_t src_off, uint64_t dst_off, uint64_t flag_off, uint64_t* lat_ns, uint32_t* status,
                      uint32_t max_blocks, uint64_t timeout_ns, cudaStream_t s);
+
+void launch_pingpong_ll8(const HeapView& h, int peer, bool initiator, uint32_t words, uint64_t iters,
+                         uint64_t warmup, uint64_t buf_off, uint64_t* lat_ns, uint32_t* status, uint64_t timeout_ns,
+                         cudaStream_t s);
 
 void launch_put_bw(const HeapView& h, int peer, bool sender, uint64_t bytes, uint64_t reps, uint64_t src_off,
                    uint64_t dst_off, uint64_t flag_off, uint64_t round, uint64_t* elapsed, uint32_t* status,
@@ -31,5 +36,9 @@ void launch_wait_flag(const HeapView& h, uint64_t flag_off, uint64_t want, uint3
 
 void launch_heap_barrier(const HeapView& h, uint64_t flag_off, uint64_t round, uint32_t* status, uint64_t timeout_ns,
                          cudaStream_t s);
+
+void launch_ce_put_selftest(const GContext& ctx, int dst, uint64_t src_off, uint64_t dst_off, uint64_t bytes,
+                            uint32_t n, uint64_t flag_off, uint64_t counter_off, uint32_t* status,
+                            uint64_t timeout_ns, cudaStream_t s);
 
 }  // namespace kiwi::p2p

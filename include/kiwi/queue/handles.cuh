@@ -84,19 +84,33 @@ KIWI_DEV uint64_t select_word(const T& msg, uint32_t i) {
         for (uint32_t w = 0; w < kW; ++w) out = (w == i) ? msg.w[w] : out;
         return out;
     } else {
-    constexpr uint32_t kWords = (sizeof(T) + 7) / 8;
-    struct alignas(8) Padded {
-        uint8_t b[kWords * 8];
-    } p{};
-    memcpy(p.b, &msg, sizeof(T));
-    uint64_t out = 0;
+        // Assemble each word from pieces at constant offsets (fully unrolled),
+        // so even large byte structs stay in registers.
+        constexpr uint32_t kWords = (sizeof(T) + 7) / 8;
+        constexpr uint32_t kPiece = (alignof(T) >= 4 && sizeof(T) % 4 == 0) ? 4 : 1;
+        const char* base = reinterpret_cast<const char*>(&msg);
+        uint64_t out = 0;
 #pragma unroll
-    for (uint32_t w = 0; w < kWords; ++w) {
-        uint64_t v;
-        memcpy(&v, p.b + 8 * w, 8);
-        out = (w == i) ? v : out;
-    }
-    return out;
+        for (uint32_t w = 0; w < kWords; ++w) {
+            uint64_t v = 0;
+#pragma unroll
+            for (uint32_t b = 0; b < 8; b += kPiece) {
+                const uint32_t idx = 8 * w + b;
+                if (idx < sizeof(T)) {
+                    if constexpr (kPiece == 4) {
+                        uint32_t piece;
+                        memcpy(&piece, base + idx, 4);
+                        v |= static_cast<uint64_t>(piece) << (8 * b);
+                    } else {
+                        uint8_t piece;
+                        memcpy(&piece, base + idx, 1);
+                        v |= static_cast<uint64_t>(piece) << (8 * b);
+                    }
+                }
+            }
+            out = (w == i) ? v : out;
+        }
+        return out;
     }
 }
 

@@ -158,4 +158,98 @@ class EpDispatchCombine:
         return out
 
 
-__all__ = ["ExpertParallelMoE", "EpDispatchCombine", "layer_config"]
+class KiwiEpOp:
+    """Expert-parallel dispatch/combine with the reference's operator contract
+    (``KiwiEpOp`` of apps/ep/python/kiwi_ep_bindings.hip.cpp:123-574 of
+    AMDResearch/kiwi, MORI ``EpDispatchCombineOp`` compatible):
+
+    * ``dispatch(input, weights, scales, indices)`` -> ``(out, out_weights,
+      out_scales, out_indices, recv_count)``: the rows this rank received, one
+      per (source rank, token) that routes at least one expert here, in
+      (source rank, token) order, as operator-owned views.  ``out`` holds the
+      wire format (``dispatch_dtype`` bf16, or FP8 e4m3 bytes with fp32 1x128
+      scales in ``out_scales``, or packed NVFP4 with e4m3 block scales after a
+      4-byte fp32 row scale).  The quantisation happens inside dispatch, so
+      ``scales`` is accepted and ignored.
+    * ``combine(input, weights, indices, out=None)`` -> ``(out, None)``: row i
+      of ``input`` goes back to the rank and token it came from; each token's
+      rows are summed (no routing weights applied, as MORI).
+    """
+
+    _DTYPES = {torch.bfloat16: "none", torch.float8_e4m3fn: "fp8", "fp8": "fp8", "nvfp4": "nvfp4", "none": "none"}
+
+    def __init__(self, hidden_dim, topk, num_experts_per_rank, max_num_inp_token_per_rank,
+                 dispatch_dtype=torch.bfloat16, combine_dtype=torch.bfloat16, group=None, timeout_s=5.0, **_ignored):
+        if combine_dtype != torch.bfloat16:
+            raise ValueError("combine_dtype must be torch.bfloat16")
+        quant = self._DTYPES.get(dispatch_dtype)
+        if quant is None:
+            raise ValueError(f"unsupported dispatch_dtype {dispatch_dtype}")
+        self.group = group
+        self.rank = kdist.rank(group)
+        self.world_size = kdist.world_size(group)
+        self.hidden_dim = hidden_dim
+        self.topk = topk
+        self.max_tokens = max_num_inp_token_per_rank
+        self.layout = _C.ep.finalize_config(dict(
+            world=self.world_size, rank=self.rank, hidden=hidden_dim, num_experts=num_experts_per_rank * self.world_size,
+            topk=topk, max_tokens=max_num_inp_token_per_rank, quant=quant))
+        self.heap = SymmetricHeap(self.layout["heap_bytes"], group)
+        self._op = _C.ep.Transport(self.heap.native, self.layout, int(timeout_s * 1e9))
+        self._quant = quant
+        self._last_tokens = 0
+        self._out = None
+
+    def dispatch(self, input, weights, scales=None, indices=None, **_launch_kwargs):
+        rows, w, sc, idx, count = self._op.dispatch(input.contiguous(), indices.to(torch.int32).contiguous(),
+                                                    weights.float().contiguous())
+        self._last_tokens = input.shape[0]
+        if self._quant == "none":
+            rows = rows.view(torch.bfloat16)
+        elif self._quant == "fp8":
+            rows = rows.view(torch.float8_e4m3fn)
+            sc = sc.view(torch.float32)
+        return rows, w, (None if self._quant == "none" else sc), idx, count
+
+    dispatch_send = dispatch
+
+    def dispatch_recv(self, **_kwargs):
+        """dispatch() already completes the receive (kept for call-shape parity)."""
+
+    def combine(self, input, weights=None, indices=None, out=None, **_launch_kwargs):
+        t = self._last_tokens
+        if out is None:
+            if self._out is None or self._out.shape[0] < self.max_tokens:
+                self._out = torch.empty(self.max_tokens, self.hidden_dim, dtype=torch.bfloat16, device=input.device)
+            out = self._out[:t]
+        self._op.combine(input.contiguous(), out)
+        return out, None
+
+    combine_send = combine
+
+    def combine_recv(self, **_kwargs):
+        return self._out[:self._last_tokens] if self._out is not None else None, None
+
+    def reset(self):
+        """Nothing to clear: slots are epoch-tagged (kept for call-shape parity)."""
+
+    def max_num_tokens_to_recv(self):
+        return self.world_size * self.max_tokens
+
+    def max_num_tokens_to_send(self):
+        return self.world_size * self.max_tokens
+
+    def max_num_tokens_to_send_per_rank(self):
+        return self.max_tokens
+
+    def get_dispatch_src_token_pos(self):
+        """Encoded source position (src_rank * max_tokens + token) of each received row."""
+        return self._op.src_token_pos
+
+    def check(self):
+        code, site, info, rank = self._op.error()
+        if code:
+            raise RuntimeError(f"kiwi ep error: code={code} site={site} info={info} rank={rank}")
+
+
+__all__ = ["ExpertParallelMoE", "EpDispatchCombine", "KiwiEpOp", "layer_config"]

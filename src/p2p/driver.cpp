@@ -47,6 +47,7 @@ const Driver& driver() {
         load(d.cuDeviceGet, "cuDeviceGet", 2000);
         load(d.cuGetErrorString, "cuGetErrorString", 6000);
         load(d.cuCtxGetCurrent, "cuCtxGetCurrent", 4000);
+        load(d.cuStreamWriteValue64, "cuStreamWriteValue64", 11070);
     });
     return d;
 }

@@ -125,3 +125,34 @@ def test_transport_only_dispatch_combine():
     torch.cuda.synchronize()
     ref = x.float() * w.sum(-1, keepdim=True)
     assert (out.float() - ref).abs().max().item() < 3e-2
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float8_e4m3fn])
+def test_kiwi_ep_op_contract(dtype):
+    """Reference/MORI contract: received rows in (source, token) order; combine
+    returns each row to its token and sums them without routing weights."""
+    from kiwi_b200.parallel.ep import KiwiEpOp
+
+    op = KiwiEpOp(hidden_dim=512, topk=3, num_experts_per_rank=8, max_num_inp_token_per_rank=40,
+                  dispatch_dtype=dtype)
+    x = torch.randn(40, 512, device="cuda").bfloat16()
+    logits = torch.randn(40, 8, device="cuda")
+    idx, w = moe.route_reference(logits, 3)
+    rows, ow, sc, oidx, cnt = op.dispatch(x, w, None, idx)
+    torch.cuda.synchronize()
+    op.check()
+    n = int(cnt.item())
+    assert n == 40  # world of 1: every token arrives once
+    pos = op.get_dispatch_src_token_pos()[:n].long()
+    assert torch.equal(pos, torch.arange(40, device="cuda"))
+    assert torch.equal(oidx[:n], idx) and torch.allclose(ow[:n], w)
+    if dtype == torch.bfloat16:
+        assert torch.equal(rows[:n], x)
+        deq = rows[:n].float()
+    else:
+        deq = (rows[:n].float().view(n, 4, 128) * sc[:n].view(torch.float32)[:, :4, None]).view(n, 512)
+        assert (deq - moe.quant_fp8_reference(x)).abs().max().item() < 1e-6
+    out, _ = op.combine(deq.bfloat16(), None, idx)
+    torch.cuda.synchronize()
+    op.check()
+    assert torch.equal(out, deq.bfloat16())

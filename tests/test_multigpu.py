@@ -81,7 +81,8 @@ def _ep_layer(rank, world, quant):
         idx, w = moe.route_reference(logits, cfg.topk)
         ref = moe.moe_reference(cfg, x, idx, w, device=x.device)
         err = (out.float() - ref).abs().max().item()
-        assert err <= 2e-2 * ref.abs().max().item() + 1e-3, (rank, step, err)
+        rel = 5e-2 if quant == "nvfp4" else 2e-2  # one mantissa bit: see tests/test_ep_gpu.py
+        assert err <= rel * ref.abs().max().item() + 1e-3, (rank, step, err)
 
 
 def _nvls(rank, world):

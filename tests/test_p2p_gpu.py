@@ -1,0 +1,54 @@
+"""kiwi::p2p on one B200: symmetric heap mapping, the control plane (device
+posts copy-engine puts and host signals that proxy threads execute), gets."""
+import pytest
+import torch
+
+import kiwi_b200
+from kiwi_b200.parallel.p2p import SymmetricHeap
+
+pytestmark = pytest.mark.gpu
+
+
+def test_heap_local_view_roundtrip():
+    heap = SymmetricHeap(1 << 21)
+    assert heap.size >= 1 << 21
+    t = heap.tensor(4096, [1024], torch.float32)
+    t.copy_(torch.arange(1024, device="cuda", dtype=torch.float32))
+    assert heap.local_ptr == heap.peer_ptr(0)
+    assert torch.equal(heap.tensor(4096, [1024], torch.float32).cpu(), torch.arange(1024, dtype=torch.float32))
+    with pytest.raises(Exception):
+        heap.tensor(heap.size - 8, [16], torch.float32)
+
+
+@pytest.mark.parametrize("bytes_,n", [(64, 4), (1 << 20, 8)])
+def test_control_plane_copy_engine_puts(bytes_, n):
+    C = kiwi_b200.native()
+    heap = SymmetricHeap(32 << 20)
+    ctx = C.p2p.Context(heap.native, 1, 256)
+    src_off, dst_off, flag_off, counter_off = 1 << 20, 4 << 20, 0, 256
+    src = heap.tensor(src_off, [bytes_], torch.uint8)
+    src.copy_(torch.randint(0, 256, (bytes_,), device="cuda", dtype=torch.uint8))
+    heap.tensor(0, [512], torch.uint8).zero_()
+    status = torch.zeros(2, dtype=torch.int32, device="cuda")
+    torch.cuda.synchronize()
+    ctx.spawn_proxy_threads(1)
+    ctx.ce_put_selftest(0, src_off, dst_off, bytes_, n, flag_off, counter_off, status, 5_000_000_000)
+    torch.cuda.synchronize()
+    ctx.join_proxy_threads()
+    assert int(status[0].item()) == 0, status
+    assert ctx.copies_issued == n
+    for i in range(n):
+        assert torch.equal(heap.tensor(dst_off + i * bytes_, [bytes_], torch.uint8), src)
+    assert int(heap.tensor(flag_off, [1], torch.int64).item()) == n
+    assert int(heap.tensor(flag_off + 8, [1], torch.int64).item()) == 0xABCD
+
+
+def test_get_from_own_heap():
+    heap = SymmetricHeap(4 << 20)
+    n = 1 << 20
+    src = heap.tensor(0, [n], torch.uint8)
+    src.copy_(torch.randint(0, 256, (n,), device="cuda", dtype=torch.uint8))
+    lat = torch.zeros(3, dtype=torch.int64, device="cuda")
+    heap.native.get(0, n, 3, 0, 2 << 20, lat, 64)
+    torch.cuda.synchronize()
+    assert torch.equal(heap.tensor(2 << 20, [n], torch.uint8), src)
