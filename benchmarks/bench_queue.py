@@ -1,0 +1,48 @@
+"""Queue-level benchmarks on one B200 (reference: benchmarks/queue/*.hip.cpp and
+benchmarks/invoke/bench_{throughput,overhead}.hip.cpp of AMDResearch/kiwi).
+
+    python benchmarks/bench_queue.py
+
+* host_ring: two CPU threads ping-pong 1,000,000 seeded 8-byte payloads through
+  two 4096 x 64 B rings, p50 / p99 round trip ns, order and
+  checksum verified; plus a one-way streaming rate.
+* invoke_throughput: E producer warps x T progress threads, messages/s.
+* push_cost: SM cycles one warp spends per push (payload 8 .. 256 B).
+"""
+import json
+import os
+import sys
+
+sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+import numpy as np  # noqa: E402
+
+import kiwi_b200  # noqa: E402
+
+
+def emit(d):
+    print("RESULT " + json.dumps(d), flush=True)
+
+
+def main():
+    C = kiwi_b200.native()
+    cpus = C.topology.process_cpus()
+    a, b = (cpus[1], cpus[2]) if len(cpus) > 2 else (-1, -1)
+    r = C.bench.host_ring_pingpong(1_000_000, 10_000, 4096, 8, 0, a, b)
+    lat = np.asarray(r["latencies_ns"])
+    emit({"bench": "host_ring_pingpong", "ok": r["ok"], "messages": 1_000_000, "slots": 4096, "slot_bytes": 64,
+          "p50_ns": float(np.percentile(lat, 50)), "p99_ns": float(np.percentile(lat, 99)), "cpus": [a, b]})
+    s = C.bench.host_ring_stream(1_000_000, 4096, 8, 0, a, b)
+    emit({"bench": "host_ring_stream", "ok": s["ok"], "Mmsg_per_s": 1e3 / s["total_ns"] * 1e6})
+    if not C.cuda_device_available():
+        return
+    for e, t in [(1, 1), (4, 1), (8, 2), (16, 4), (64, 4)]:
+        r = C.bench.invoke_throughput(e, t, 20000, 8, 4096)
+        emit({"bench": "invoke_throughput", "endpoints": e, "threads": t, "ok": r["ok"],
+              "Mmsg_per_s": r["messages"] / max(r["device_ns"], 1) * 1e3})
+    for nbytes in [8, 32, 64, 128, 256]:
+        c = C.bench.push_cost(20000, nbytes)
+        emit({"bench": "push_cost", "payload_bytes": nbytes, "ok": c["ok"], "cycles": c["cycles_per_push"]})
+
+
+if __name__ == "__main__":
+    main()

@@ -437,6 +437,19 @@ PYBIND11_MODULE(_C, m) {
           },
           py::arg("slots") = 16, py::arg("slot_lines") = 2, py::arg("producers") = 2,
           py::arg("msgs_per_producer") = 100, py::arg("warps") = 4, py::arg("seed") = 5);
+    b.def("atomicity_test", [](uint32_t iters) {
+        bench::AtomicityResult r;
+        {
+            py::gil_scoped_release nogil;
+            r = bench::atomicity_test(iters);
+        }
+        py::dict d;
+        d["reads"] = r.reads;
+        d["torn8"] = r.torn8;
+        d["split16"] = r.split16;
+        d["final_ok"] = r.final_ok;
+        return d;
+    });
     b.def("invoke_throughput",
           [](uint32_t endpoints, uint32_t threads, uint32_t msgs, uint32_t bytes, uint64_t cap) {
               bench::ThroughputResult r;

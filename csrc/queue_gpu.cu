@@ -575,6 +575,54 @@ RttResult rtt_lab(uint64_t iters, uint64_t warmup, uint32_t pollers, uint32_t mi
 }
 
 
+
+// ---------------------------------------------------------------------------
+// Platform assumption the wire format relies on (reference category:
+// tests/queue/test_hardware_assumptions.hip.cpp): aligned 8-byte halves of a
+// GPU st.volatile.v4 into mapped host memory are never seen torn by host
+// 8-byte loads.  The GPU rewrites one 64-byte line `iters` times; in round i
+// every 8-byte half holds {i, ~i}; the host checks each half it reads.
+// ---------------------------------------------------------------------------
+
+__global__ void atomicity_writer_kernel(Chunk* line, uint32_t iters, volatile uint32_t* done) {
+    const uint32_t lane = ptx::lane_id();
+    for (uint32_t i = 1; i <= iters; ++i) {
+        if (lane < 4) ptx::st_volatile_v4(&line[lane], i, ~i, i, ~i);
+        __syncwarp();
+    }
+    if (lane == 0) {
+        ptx::fence_sys();
+        *done = 1;
+    }
+}
+
+AtomicityResult atomicity_test(uint32_t iters) {
+    detail::Block mem(128, MemKind::kMappedPinned);
+    PinnedFlag done;
+    Chunk* line = mem.as<Chunk>();
+    cudaStream_t stream;
+    KIWI_CUDA_CHECK(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking));
+    atomicity_writer_kernel<<<1, 32, 0, stream>>>(line, iters, done.p);
+    KIWI_CUDA_CHECK(cudaGetLastError());
+    AtomicityResult r;
+    uint64_t idle = 0;
+    while (!*done.p) {
+        for (int c = 0; c < 4; ++c) {
+            const uint64_t a = host::load_half(&line[c].lo);
+            const uint64_t b = host::load_half(&line[c].hi);
+            ++r.reads;
+            if (static_cast<uint32_t>(a >> 32) != ~static_cast<uint32_t>(a)) ++r.torn8;
+            if (static_cast<uint32_t>(b >> 32) != ~static_cast<uint32_t>(b)) ++r.torn8;
+            if (static_cast<uint32_t>(a) != static_cast<uint32_t>(b)) ++r.split16;
+        }
+        if ((++idle & 0xfffff) == 0 && cudaStreamQuery(stream) != cudaErrorNotReady) break;
+    }
+    KIWI_CUDA_CHECK(cudaStreamSynchronize(stream));
+    cudaStreamDestroy(stream);
+    r.final_ok = static_cast<uint32_t>(host::load_half(&line[3].hi)) == iters;
+    return r;
+}
+
 // ---------------------------------------------------------------------------
 // Invoke throughput and push cost (reference: benchmarks/invoke/
 // bench_throughput.hip.cpp:39, bench_overhead.hip.cpp:54-119)

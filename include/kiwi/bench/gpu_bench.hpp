@@ -48,6 +48,15 @@ RttResult pcie_floor(uint64_t iters, uint64_t warmup, int cpu, uint64_t timeout_
 RttResult rtt_lab(uint64_t iters, uint64_t warmup, uint32_t pollers, uint32_t mirrors, uint32_t stagger_ns,
                   uint32_t fence, uint32_t pipeline, int cpu, uint32_t initial_delay_ns = 0);
 
+struct AtomicityResult {
+    uint64_t reads = 0;    // 16-byte chunks the host read while the GPU wrote
+    uint64_t torn8 = 0;    // 8-byte halves seen torn (must be 0)
+    uint64_t split16 = 0;  // chunks whose two halves came from different rounds (allowed)
+    bool final_ok = false;
+};
+/// GPU rewrites one host line; a host thread checks every 8-byte half it reads.
+AtomicityResult atomicity_test(uint32_t iters);
+
 struct ThroughputResult {
     uint64_t messages = 0;
     uint64_t device_ns = 0;  // first push to last push (device %globaltimer)

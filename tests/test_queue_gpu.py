@@ -117,3 +117,22 @@ def test_invoke_roundtrip_small():
 def test_pcie_floor_small():
     r = _C().bench.pcie_floor(iters=2000, warmup=200)
     assert r["ok"], r
+
+
+def test_platform_8byte_atomicity_of_gpu_stores_to_host():
+    """The wire format's only hardware assumption (reference:
+    tests/queue/test_hardware_assumptions.hip.cpp): aligned 8-byte halves of a
+    GPU 16-byte store to mapped host memory are never seen torn by the host."""
+    r = _C().bench.atomicity_test(2_000_000)
+    assert r["final_ok"], r
+    assert r["reads"] > 1000, r
+    assert r["torn8"] == 0, r
+
+
+def test_invoke_throughput_and_push_cost():
+    C = _C()
+    r = C.bench.invoke_throughput(endpoints=8, threads=2, msgs_per_endpoint=20000, payload_bytes=8)
+    assert r["ok"], r
+    assert r["messages"] == 8 * 20000
+    c = C.bench.push_cost(20000, 8)
+    assert c["ok"] and c["cycles_per_push"] > 0, c
