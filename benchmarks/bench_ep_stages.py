@@ -24,11 +24,14 @@ def main():
     ap.add_argument("--config", default="deepseek_fp8")
     ap.add_argument("--tokens", type=int, default=None)
     ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--experts", type=int, default=None, help="override the expert count (small profiling cases)")
     args = ap.parse_args()
     rank, world = kdist.init()
     cfg = moe_model.CONFIGS[args.config]
     if args.tokens:
         cfg = moe_model.MoEConfig(**{**cfg.__dict__, "tokens_per_rank": args.tokens})
+    if args.experts:
+        cfg = moe_model.MoEConfig(**{**cfg.__dict__, "num_experts": args.experts})
     layer = ExpertParallelMoE(cfg)
     x, logits = moe_model.synthetic_inputs(cfg, rank, "cuda")
     out = torch.empty_like(x)

@@ -61,6 +61,7 @@ def main():
         out = torch.empty(total, n // 2 if swiglu else n, device="cuda", dtype=torch.bfloat16)
         plan = C.ops.GroupedGemm(a, b, groups)
         ms = timeit(lambda: plan.run(counts, out, swiglu), args.iters)
+        ms_pair = timeit(lambda: plan.run(counts, out, swiglu, None, 0, True), args.iters) if rows >= 256 else float("nan")
         flops = 2.0 * total * n * k
         bw = (b.numel() * 2 + a.numel() * 2 + out.numel() * 2) / (ms / 1e3) / 1e12
         offs = torch.cumsum(counts, 0).to(torch.int32)
@@ -73,6 +74,7 @@ def main():
                 print("torch._grouped_mm failed:", ex, file=sys.stderr)
         print("RESULT " + json.dumps({"bench": name, "groups": groups, "rows": rows, "k": k, "n": n,
                                       "kiwi_ms": ms, "kiwi_tflops": flops / ms / 1e9,
+                                      "kiwi_pair_ms": ms_pair, "kiwi_pair_tflops": flops / ms_pair / 1e9,
                                       "kiwi_hbm_TBps_min_traffic": bw,
                                       "torch_grouped_mm_ms": tms, "torch_tflops": flops / tms / 1e9}), flush=True)
 

@@ -121,8 +121,14 @@ public:
 
         tmap_a1_ = gemm::make_tmap_bf16_2d(a_.data_ptr(), pairs, cfg_.hidden, 128);
         tmap_b1_ = gemm::make_tmap_bf16_2d(w13.data_ptr(), w13.size(0), cfg_.hidden, 256);
+        tmap_b1h_ = gemm::make_tmap_bf16_2d(w13.data_ptr(), w13.size(0), cfg_.hidden, 128);
         tmap_a2_ = gemm::make_tmap_bf16_2d(h_.data_ptr(), pairs, ffn, 128);
         tmap_b2_ = gemm::make_tmap_bf16_2d(w2.data_ptr(), w2.size(0), ffn, 256);
+        tmap_b2h_ = gemm::make_tmap_bf16_2d(w2.data_ptr(), w2.size(0), ffn, 128);
+        // 2-SM tiles (256 rows) pay off once an expert expects >= 256 rows per round.
+        const int64_t expected_rows =
+            static_cast<int64_t>(cfg_.world) * cfg_.max_tokens * cfg_.topk / std::max(cfg_.num_experts, 1);
+        pair_ = expected_rows >= 256;
     }
 
     // ---- stages (all on the current stream) ----
@@ -144,9 +150,10 @@ public:
     void receive() {
         cudaStream_t s = cur_stream();
         ep::launch_recv_count(cfg_, heap_.view(), ws_, timeout_ns_, s);
+        const int bm = pair_ ? 256 : 128;
         gemm::build_schedule(ws_.expert_count, cfg_.experts_per_rank, static_cast<int>(2 * ffn_), 256, ws_.offsets,
-                             ws_.tiles1, s);
-        gemm::build_schedule(ws_.expert_count, cfg_.experts_per_rank, cfg_.hidden, 256, ws_.offsets, ws_.tiles2, s);
+                             ws_.tiles1, s, bm);
+        gemm::build_schedule(ws_.expert_count, cfg_.experts_per_rank, cfg_.hidden, 256, ws_.offsets, ws_.tiles2, s, bm);
         ep::launch_recv_scatter(cfg_, heap_.view(), ws_, s);
     }
 
@@ -163,7 +170,8 @@ public:
         g1.row_scale = nullptr;
         g1.error = reinterpret_cast<uint32_t*>(gemm_error_.data_ptr<int32_t>());
         g1.max_rows = cfg_.max_pairs();
-        gemm::grouped_gemm(tmap_a1_, tmap_b1_, g1, /*swiglu=*/true, 0, s);
+        if (pair_) gemm::grouped_gemm_pair(tmap_a1_, tmap_b1h_, g1, /*swiglu=*/true, 0, s);
+        else gemm::grouped_gemm(tmap_a1_, tmap_b1_, g1, /*swiglu=*/true, 0, s);
         gemm::GroupedArgs g2 = g1;
         g2.tile_prefix = ws_.tiles2;
         g2.n = cfg_.hidden;
@@ -171,7 +179,8 @@ public:
         g2.c = reinterpret_cast<__nv_bfloat16*>(y_.data_ptr());
         g2.ldc = cfg_.hidden;
         g2.row_scale = ws_.pair_w;
-        gemm::grouped_gemm(tmap_a2_, tmap_b2_, g2, /*swiglu=*/false, 0, s);
+        if (pair_) gemm::grouped_gemm_pair(tmap_a2_, tmap_b2h_, g2, /*swiglu=*/false, 0, s);
+        else gemm::grouped_gemm(tmap_a2_, tmap_b2_, g2, /*swiglu=*/false, 0, s);
     }
 
     void combine(torch::Tensor idx, torch::Tensor out) {
@@ -232,7 +241,12 @@ private:
     torch::Tensor epoch_, done_, counts_, cursor_, offsets_, tiles1_, tiles2_, slot_tokens_, pair_slot_, pair_w_,
         slot_pos_, a_, h_, y_, error_, gemm_error_;
     ep::EpWorkspace ws_{};
-    CUtensorMap tmap_a1_, tmap_b1_, tmap_a2_, tmap_b2_;
+    CUtensorMap tmap_a1_, tmap_b1_, tmap_a2_, tmap_b2_, tmap_b1h_, tmap_b2h_;
+    bool pair_ = false;
+
+public:
+    bool pair() const { return pair_; }
+    void set_pair(bool v) { pair_ = v; }
 };
 
 
@@ -363,5 +377,7 @@ void register_ep(py::module_& m) {
         .def_property_readonly("expert_input", &MoeLayer::expert_input)
         .def_property_readonly("expert_hidden", &MoeLayer::expert_hidden)
         .def_property_readonly("expert_output", &MoeLayer::expert_output)
-        .def_property_readonly("epoch", &MoeLayer::epoch);
+        .def_property_readonly("epoch", &MoeLayer::epoch)
+        .def_property("gemm_pair", &MoeLayer::pair, &MoeLayer::set_pair,
+                      "Use the 2-SM (256-row tile) grouped GEMM; the default follows the expected rows per expert.");
 }

@@ -406,8 +406,10 @@ __global__ void __launch_bounds__(kThreads) recv_count_kernel(EpConfig c, p2p::H
     }
 }
 
-template <int QUANT>
-__global__ void __launch_bounds__(kThreads) recv_scatter_kernel(EpConfig c, p2p::HeapView h, EpWorkspace ws) {
+/// Receive, step 1 (warp per slot): validates the slot, assigns one
+/// expert-major row per local expert with an atomic per expert, and records
+/// pair_slot / pair_w and the slot's row list (slot_pos, -1 padded).
+__global__ void __launch_bounds__(kThreads) recv_assign_kernel(EpConfig c, p2p::HeapView h, EpWorkspace ws) {
     const int lane = threadIdx.x & 31;
     const int warps = gridDim.x * (blockDim.x / 32);
     const uint32_t epoch = *reinterpret_cast<volatile uint32_t*>(ws.epoch);
@@ -430,9 +432,8 @@ __global__ void __launch_bounds__(kThreads) recv_scatter_kernel(EpConfig c, p2p:
         }
         const bool local = valid && lane < c.topk && e >= 0 && e < c.experts_per_rank;
         const uint32_t lmask = __ballot_sync(0xffffffffu, local);
-        int pos = -1;
         if (local) {
-            pos = ws.offsets[e] + atomicAdd(&ws.cursor[e], 1);
+            int pos = ws.offsets[e] + atomicAdd(&ws.cursor[e], 1);
             if (pos < max_pairs) {
                 ws.pair_slot[pos] = static_cast<int32_t>(s);
                 ws.pair_w[pos] = wt;
@@ -451,53 +452,65 @@ __global__ void __launch_bounds__(kThreads) recv_scatter_kernel(EpConfig c, p2p:
         }
         const int nloc = __popc(lmask);
         if (lane >= nloc && lane < lpt) ws.slot_pos[s * lpt + lane] = -1;
-        if (nloc == 0) continue;
-        // Copy (and dequantise) the row once per local expert.
-        for (int cb = 0; cb < c.hidden; cb += 512) {
-            const int col = cb + lane * 16;
-            uint4 out[2];
-            if constexpr (QUANT == static_cast<int>(Quant::kNone)) {
-                out[0] = ld_cg_v4(base + c.row_off(s) + 2ull * col);
-                out[1] = ld_cg_v4(base + c.row_off(s) + 2ull * col + 16);
-            } else if constexpr (QUANT == static_cast<int>(Quant::kFp8)) {
-                const uint4 q = ld_cg_v4(base + c.row_off(s) + col);
-                const float sc = ld_cg_f32(base + c.scale_off(s) + 4ull * (col / kFp8Block));
-                dequant_fp8_16(q, sc, out);
-            } else {
-                uint2 q;
-                const uint4 qq = ld_cg_v4(base + c.row_off(s) + (col / 32) * 16);  // 16 B = 32 elements
-                q = (lane & 1) ? make_uint2(qq.z, qq.w) : make_uint2(qq.x, qq.y);
-                const float rs = ld_cg_f32(base + c.scale_off(s));
-                const uint8_t sb = static_cast<uint8_t>(ld_cg_u32(base + c.scale_off(s) + 4 + ((col / kFp4Block) & ~3)) >>
-                                                        (8 * ((col / kFp4Block) & 3)));
-                const __half_raw sh = __nv_cvt_fp8_to_halfraw(sb, __NV_E4M3);
-                dequant_fp4_16(q, __half2float(*reinterpret_cast<const __half*>(&sh)) * rs, out);
-            }
-            for (uint32_t m = lmask; m; m &= m - 1) {
-                const int p = __shfl_sync(0xffffffffu, pos, __ffs(m) - 1);
-                if (p >= 0) {
-                    __nv_bfloat16* dst = ws.a + static_cast<int64_t>(p) * c.hidden + col;
-                    ptx::st_v4(dst, out[0]);
-                    ptx::st_v4(dst + 8, out[1]);
-                }
-            }
+    }
+}
+
+/// Receive, step 2: for every (valid slot, 512-column block) the warp loads the
+/// dispatched bytes once, dequantises them and stores the bf16 row block into
+/// each of the slot's expert-major rows.  Items are spread over the whole grid.
+template <int QUANT>
+__global__ void __launch_bounds__(kThreads) recv_copy_kernel(EpConfig c, p2p::HeapView h, EpWorkspace ws) {
+    const int lane = threadIdx.x & 31;
+    const int warps = gridDim.x * (blockDim.x / 32);
+    const int lpt = c.local_per_token();
+    const uint8_t* base = h.base[h.rank];
+    const int blocks = c.hidden / 512;
+    const uint64_t items = c.slots() * blocks;
+    for (uint64_t it = (blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x) / 32; it < items; it += warps) {
+        const uint64_t s = it / blocks;
+        const int col = static_cast<int>(it % blocks) * 512 + lane * 16;
+        const int p = lane < lpt ? ws.slot_pos[s * lpt + lane] : -1;
+        const uint32_t pm = __ballot_sync(0xffffffffu, p >= 0);
+        if (pm == 0) continue;
+        uint4 out[2];
+        if constexpr (QUANT == static_cast<int>(Quant::kNone)) {
+            out[0] = ld_cg_v4(base + c.row_off(s) + 2ull * col);
+            out[1] = ld_cg_v4(base + c.row_off(s) + 2ull * col + 16);
+        } else if constexpr (QUANT == static_cast<int>(Quant::kFp8)) {
+            const uint4 q = ld_cg_v4(base + c.row_off(s) + col);
+            const float sc = ld_cg_f32(base + c.scale_off(s) + 4ull * (col / kFp8Block));
+            dequant_fp8_16(q, sc, out);
+        } else {
+            const uint4 qq = ld_cg_v4(base + c.row_off(s) + (col / 32) * 16);  // 16 B = 32 elements
+            const uint2 q = (lane & 1) ? make_uint2(qq.z, qq.w) : make_uint2(qq.x, qq.y);
+            const float rs = ld_cg_f32(base + c.scale_off(s));
+            const uint8_t sb = static_cast<uint8_t>(ld_cg_u32(base + c.scale_off(s) + 4 + ((col / kFp4Block) & ~3)) >>
+                                                    (8 * ((col / kFp4Block) & 3)));
+            const __half_raw sh = __nv_cvt_fp8_to_halfraw(sb, __NV_E4M3);
+            dequant_fp4_16(q, __half2float(*reinterpret_cast<const __half*>(&sh)) * rs, out);
+        }
+        for (uint32_t m = pm; m; m &= m - 1) {
+            const int pp = __shfl_sync(0xffffffffu, p, __ffs(m) - 1);
+            __nv_bfloat16* dst = ws.a + static_cast<int64_t>(pp) * c.hidden + col;
+            ptx::st_v4(dst, out[0]);
+            ptx::st_v4(dst + 8, out[1]);
         }
     }
 }
 
-/// Sums up to 16 bf16 rows (`ptrs[j] + col`, j < n) into fp32: every load is
+/// Sums up to MAXP bf16 rows (load(j) for j < n) into fp32: every load is
 /// issued before the first add so all of them are in flight together.
-template <typename Loader>
+template <int MAXP, typename Loader>
 KIWI_DEV void sum_rows(int n, Loader load, float (&acc)[8]) {
-    uint4 v[kMaxTopk];
+    uint4 v[MAXP];
 #pragma unroll
-    for (int j = 0; j < kMaxTopk; ++j) {
+    for (int j = 0; j < MAXP; ++j) {
         if (j < n) v[j] = load(j);
     }
 #pragma unroll
     for (int i = 0; i < 8; ++i) acc[i] = 0.f;
 #pragma unroll
-    for (int j = 0; j < kMaxTopk; ++j) {
+    for (int j = 0; j < MAXP; ++j) {
         if (j < n) {
             float f[8];
             bf16x8_to_f32(v[j], f);
@@ -507,33 +520,40 @@ KIWI_DEV void sum_rows(int n, Loader load, float (&acc)[8]) {
     }
 }
 
+/// Combine, send side: for every (slot, 256-column block) the warp sums the
+/// slot's (already routing-weighted) expert rows and stores the bf16 block into
+/// the token owner's combine slot over NVLink.  MAXP bounds the rows per slot.
+template <int MAXP>
 __global__ void __launch_bounds__(kThreads) combine_send_kernel(EpConfig c, p2p::HeapView h,
                                                                 const __nv_bfloat16* y, EpWorkspace ws) {
     const int lane = threadIdx.x & 31;
     const int warps = gridDim.x * (blockDim.x / 32);
     const uint32_t epoch = *reinterpret_cast<volatile uint32_t*>(ws.epoch);
     const int lpt = c.local_per_token();
-    for (uint64_t s = (blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x) / 32; s < c.slots();
-         s += warps) {
+    const int blocks = c.hidden / 256;
+    const uint64_t items = c.slots() * blocks;
+    for (uint64_t it = (blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x) / 32; it < items; it += warps) {
+        const uint64_t s = it / blocks;
+        const int col = static_cast<int>(it % blocks) * 256 + lane * 8;
         const int p = lane < lpt ? ws.slot_pos[s * lpt + lane] : -1;
         const uint32_t pm = __ballot_sync(0xffffffffu, p >= 0);
         if (pm == 0) continue;
         const int npos = __popc(pm);  // positions are packed at the front of the slot's list
-        int pl[kMaxTopk];
+        int pl[MAXP];
 #pragma unroll
-        for (int j = 0; j < kMaxTopk; ++j) pl[j] = __shfl_sync(0xffffffffu, p, j);
+        for (int j = 0; j < MAXP; ++j) pl[j] = __shfl_sync(0xffffffffu, p, j);
         const int src = static_cast<int>(s / c.max_tokens);
         const int t = static_cast<int>(s % c.max_tokens);
-        uint8_t* dst = h.base[src] + c.comb_off(c.rank, t);
-        for (int col = lane * 8; col < c.hidden; col += 256) {
-            float acc[8];
-            sum_rows(npos, [&](int j) { return ptx::ld_v4(y + static_cast<int64_t>(pl[j]) * c.hidden + col); }, acc);
-            ptx::st_v4(dst + 2ull * col, f32x8_to_bf16(acc));
-        }
+        float acc[8];
+        sum_rows<MAXP>(npos, [&](int j) { return ptx::ld_v4(y + static_cast<int64_t>(pl[j]) * c.hidden + col); }, acc);
+        ptx::st_v4(h.base[src] + c.comb_off(c.rank, t) + 2ull * col, f32x8_to_bf16(acc));
     }
     grid_done_signal(c, h, &ws.done_ctas[1], c.combine_flag(c.rank), (static_cast<uint64_t>(epoch) << 32) | 1u);
 }
 
+/// Combine, receive side: after every rank's flag, each (token, 256-column
+/// block) sums the rows the token's destination ranks returned.
+template <int MAXR>
 __global__ void __launch_bounds__(kThreads) combine_recv_kernel(EpConfig c, p2p::HeapView h, const int32_t* idx,
                                                                 int tokens, __nv_bfloat16* out, EpWorkspace ws,
                                                                 uint64_t timeout_ns) {
@@ -545,31 +565,29 @@ __global__ void __launch_bounds__(kThreads) combine_recv_kernel(EpConfig c, p2p:
         return;
     }
     const uint8_t* base = h.base[h.rank];
-    for (int t = (blockIdx.x * blockDim.x + threadIdx.x) / 32; t < tokens; t += warps) {
+    const int blocks = c.hidden / 256;
+    const uint64_t items = static_cast<uint64_t>(tokens) * blocks;
+    for (uint64_t it = (blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x) / 32; it < items; it += warps) {
+        const int t = static_cast<int>(it / blocks);
+        const int col = static_cast<int>(it % blocks) * 256 + lane * 8;
         const int e = lane < c.topk ? idx[static_cast<int64_t>(t) * c.topk + lane] : -1;
         const bool ok_e = e >= 0 && e < c.num_experts;
-        const uint32_t mask = __reduce_or_sync(0xffffffffu, ok_e ? (1u << (e / c.experts_per_rank)) : 0u);
-        int rl[kMaxTopk];
+        uint32_t m = __reduce_or_sync(0xffffffffu, ok_e ? (1u << (e / c.experts_per_rank)) : 0u);
+        int rl[MAXR];
         int nr = 0;
-        {
-            uint32_t m = mask;
 #pragma unroll
-            for (int j = 0; j < kMaxTopk; ++j) {
-                rl[j] = m ? __ffs(m) - 1 : 0;
-                if (m) {
-                    ++nr;
-                    m &= m - 1;
-                }
+        for (int j = 0; j < MAXR; ++j) {
+            rl[j] = m ? __ffs(m) - 1 : 0;
+            if (m) {
+                ++nr;
+                m &= m - 1;
             }
         }
-        for (int col = lane * 8; col < c.hidden; col += 256) {
-            float acc[8];
-            sum_rows(nr, [&](int j) { return ld_cg_v4(base + c.comb_off(rl[j], t) + 2ull * col); }, acc);
-            ptx::st_v4(out + static_cast<int64_t>(t) * c.hidden + col, f32x8_to_bf16(acc));
-        }
+        float acc[8];
+        sum_rows<MAXR>(nr, [&](int j) { return ld_cg_v4(base + c.comb_off(rl[j], t) + 2ull * col); }, acc);
+        ptx::st_v4(out + static_cast<int64_t>(t) * c.hidden + col, f32x8_to_bf16(acc));
     }
 }
-
 
 // ---------------------------------------------------------------------------
 // Transport-only path (rows in, rows out), MORI semantics.
@@ -710,26 +728,35 @@ void launch_recv_count(const EpConfig& c, const p2p::HeapView& h, const EpWorksp
 }
 
 void launch_recv_scatter(const EpConfig& c, const p2p::HeapView& h, const EpWorkspace& ws, cudaStream_t s) {
-    const int grid = 2 * default_grid();
+    const uint64_t assign_blocks = (c.slots() * 32 + kThreads - 1) / kThreads;
+    const uint64_t cap = 8u * default_grid();
+    recv_assign_kernel<<<static_cast<int>(assign_blocks < cap ? assign_blocks : cap), kThreads, 0, s>>>(c, h, ws);
+    KIWI_CUDA_CHECK(cudaGetLastError());
+    const int grid = 8 * default_grid();
     switch (static_cast<Quant>(c.quant)) {
-        case Quant::kNone: recv_scatter_kernel<0><<<grid, kThreads, 0, s>>>(c, h, ws); break;
-        case Quant::kFp8: recv_scatter_kernel<1><<<grid, kThreads, 0, s>>>(c, h, ws); break;
-        case Quant::kNvfp4: recv_scatter_kernel<2><<<grid, kThreads, 0, s>>>(c, h, ws); break;
+        case Quant::kNone: recv_copy_kernel<0><<<grid, kThreads, 0, s>>>(c, h, ws); break;
+        case Quant::kFp8: recv_copy_kernel<1><<<grid, kThreads, 0, s>>>(c, h, ws); break;
+        case Quant::kNvfp4: recv_copy_kernel<2><<<grid, kThreads, 0, s>>>(c, h, ws); break;
     }
     KIWI_CUDA_CHECK(cudaGetLastError());
 }
 
 void launch_combine_send(const EpConfig& c, const p2p::HeapView& h, const __nv_bfloat16* y, const EpWorkspace& ws,
                          int grid, cudaStream_t s) {
-    if (grid <= 0) grid = 2 * default_grid();
-    combine_send_kernel<<<grid, kThreads, 0, s>>>(c, h, y, ws);
+    if (grid <= 0) grid = 8 * default_grid();
+    if (c.local_per_token() <= 8) combine_send_kernel<8><<<grid, kThreads, 0, s>>>(c, h, y, ws);
+    else combine_send_kernel<kMaxTopk><<<grid, kThreads, 0, s>>>(c, h, y, ws);
     KIWI_CUDA_CHECK(cudaGetLastError());
 }
 
 void launch_combine_recv(const EpConfig& c, const p2p::HeapView& h, const int32_t* idx, int tokens,
                          __nv_bfloat16* out, const EpWorkspace& ws, uint64_t timeout_ns, cudaStream_t s) {
-    const int grid = 2 * default_grid();
-    combine_recv_kernel<<<grid, kThreads, 0, s>>>(c, h, idx, tokens, out, ws, timeout_ns);
+    const int grid = 8 * default_grid();
+    if (c.world <= 8 && c.topk <= 8) {
+        combine_recv_kernel<8><<<grid, kThreads, 0, s>>>(c, h, idx, tokens, out, ws, timeout_ns);
+    } else {
+        combine_recv_kernel<kMaxTopk><<<grid, kThreads, 0, s>>>(c, h, idx, tokens, out, ws, timeout_ns);
+    }
     KIWI_CUDA_CHECK(cudaGetLastError());
 }
 

@@ -254,16 +254,225 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (warp == 1) sm100::tmem_dealloc(tmem_base, 2 * BN);
 }
 
+
+// ---------------------------------------------------------------------------
+// 2-SM variant: a cluster of two CTAs computes a 256 x 256 tile with
+// tcgen05.mma.cta_group::2 (M = 256 across the pair).  Each CTA loads its 128
+// rows of A and its 128-row half of the B tile, so a CTA moves 32 KB per
+// k-block for 128 x 256 x 64 MACs instead of 48 KB: the L2 -> SMEM traffic per
+// MMA drops by a third.  The leader (cluster rank 0) owns the full barriers
+// (both CTAs' TMA loads complete on them) and issues the MMAs; commits arrive
+// on both CTAs' barriers through their cluster addresses; each CTA drains its
+// own TMEM (its 128 rows x 256 columns).  Used when experts get >= 256 rows.
+// ---------------------------------------------------------------------------
+
+constexpr int kPairStages = 6;
+constexpr int kPairBM = 256;  // rows per pair tile (128 per CTA)
+constexpr int kPairBN = 256;
+
+struct PairSmem {
+    static constexpr int kABytes = 128 * kBK * 2;     // this CTA's 128 rows of A
+    static constexpr int kBBytes = 128 * kBK * 2;     // this CTA's half of the B tile
+    static constexpr int kStageBytes = kABytes + kBBytes;
+    static constexpr int kBarOffset = kPairStages * kStageBytes;
+    static constexpr int kBytes = kBarOffset + 256 + 1024;
+};
+
+template <bool SWIGLU>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+    grouped_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
+                             GroupedArgs p) {
+    using S = PairSmem;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::kBarOffset);
+    uint64_t* empty = full + kPairStages;
+    uint64_t* tmem_full = empty + kPairStages;
+    uint64_t* tmem_empty = tmem_full + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tmem_empty + 2);
+    __shared__ int s_abort;
+
+    const int warp = threadIdx.x / 32;
+    const int lane = threadIdx.x & 31;
+    const uint32_t crank = sm100::cluster_ctarank();
+    const bool leader = crank == 0;
+    const int cluster = blockIdx.x / 2;
+    const int nclusters = gridDim.x / 2;
+    const int n_tiles = p.n / kPairBN;
+    const int k_blocks = p.k / kBK;
+    const int total_tiles = __ldg(&p.tile_prefix[p.num_groups]);
+
+    if (threadIdx.x == 0) {
+        s_abort = 0;
+        for (int st = 0; st < kPairStages; ++st) {
+            sm100::mbar_init(&full[st], 1);
+            sm100::mbar_init(&empty[st], 1);
+        }
+        for (int a = 0; a < 2; ++a) {
+            sm100::mbar_init(&tmem_full[a], 1);
+            sm100::mbar_init(&tmem_empty[a], 8);  // 4 epilogue warps x 2 CTAs
+        }
+        sm100::fence_mbar_init();
+    }
+    if (warp == 0 && lane == 0) {
+        sm100::tma_prefetch_desc(&tmap_a);
+        sm100::tma_prefetch_desc(&tmap_b);
+    }
+    if (warp == 1) sm100::tmem_alloc_pair(tmem_slot, 2 * kPairBN);
+    sm100::tc_fence_before();
+    __syncthreads();
+    sm100::cluster_sync();  // both CTAs' barriers exist before any cross-CTA arrival
+    sm100::tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    auto abort_flag = [&]() { return *reinterpret_cast<volatile int*>(&s_abort) != 0; };
+    auto fail = [&](uint32_t code) {
+        *reinterpret_cast<volatile int*>(&s_abort) = 1;
+        if (p.error) atomicCAS(p.error, 0u, code);
+    };
+
+    if (warp == 0) {
+        if (lane == 0) {
+            int stage = 0;
+            uint32_t phase = 0;
+            for (int tile = cluster; tile < total_tiles && !abort_flag(); tile += nclusters) {
+                int g, mt, nt;
+                locate_tile(p.tile_prefix, p.num_groups, n_tiles, tile, g, mt, nt);
+                const int row0 = __ldg(&p.group_offset[g]) + mt * kPairBM + static_cast<int>(crank) * 128;
+                const int brow0 = g * p.n + nt * kPairBN + static_cast<int>(crank) * 128;
+                for (int kb = 0; kb < k_blocks; ++kb) {
+                    if (!sm100::mbar_wait(&empty[stage], phase ^ 1)) {
+                        fail(11);
+                        break;
+                    }
+                    uint8_t* sa = smem + stage * S::kStageBytes;
+                    uint8_t* sb = sa + S::kABytes;
+                    if (leader) sm100::mbar_arrive_expect_tx(&full[stage], 2 * S::kStageBytes);
+                    const uint32_t bar = sm100::mapa(&full[stage], 0);
+                    sm100::tma_load_2d_pair(sa, &tmap_a, bar, kb * kBK, row0);
+                    sm100::tma_load_2d_pair(sb, &tmap_b, bar, kb * kBK, brow0);
+                    if (++stage == kPairStages) {
+                        stage = 0;
+                        phase ^= 1;
+                    }
+                }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0 && leader) {
+            const uint32_t idesc = sm100::idesc_bf16_f32(kPairBM, kPairBN);
+            int stage = 0;
+            uint32_t phase = 0;
+            int acc = 0;
+            uint32_t acc_phase = 0;
+            for (int tile = cluster; tile < total_tiles && !abort_flag(); tile += nclusters) {
+                if (!sm100::mbar_wait(&tmem_empty[acc], acc_phase ^ 1)) {
+                    fail(12);
+                    break;
+                }
+                sm100::tc_fence_after();
+                const uint32_t d = tmem_base + acc * kPairBN;
+                bool ok = true;
+                for (int kb = 0; kb < k_blocks; ++kb) {
+                    if (!sm100::mbar_wait(&full[stage], phase)) {
+                        fail(13);
+                        ok = false;
+                        break;
+                    }
+                    sm100::tc_fence_after();
+                    uint8_t* sa = smem + stage * S::kStageBytes;
+                    uint8_t* sb = sa + S::kABytes;
+                    const uint64_t adesc = sm100::sw128_kmajor_desc(sa);
+                    const uint64_t bdesc = sm100::sw128_kmajor_desc(sb);
+#pragma unroll
+                    for (int kk = 0; kk < kBK / 16; ++kk) {
+                        sm100::mma_bf16_pair(d, adesc + 2 * kk, bdesc + 2 * kk, idesc, (kb | kk) != 0 ? 1u : 0u);
+                    }
+                    sm100::mma_commit_pair(sm100::mapa(&empty[stage], 0));
+                    sm100::mma_commit_pair(sm100::mapa(&empty[stage], 1));
+                    if (++stage == kPairStages) {
+                        stage = 0;
+                        phase ^= 1;
+                    }
+                }
+                if (!ok) break;
+                sm100::mma_commit_pair(sm100::mapa(&tmem_full[acc], 0));
+                sm100::mma_commit_pair(sm100::mapa(&tmem_full[acc], 1));
+                if (++acc == 2) {
+                    acc = 0;
+                    acc_phase ^= 1;
+                }
+            }
+        }
+    } else {
+        const int q = warp & 3;
+        const int row_in_tile = static_cast<int>(crank) * 128 + q * 32 + lane;
+        const uint32_t empty_leader = sm100::mapa(&tmem_empty[0], 0);
+        int acc = 0;
+        uint32_t acc_phase = 0;
+        for (int tile = cluster; tile < total_tiles && !abort_flag(); tile += nclusters) {
+            int g, mt, nt;
+            locate_tile(p.tile_prefix, p.num_groups, n_tiles, tile, g, mt, nt);
+            if (!sm100::mbar_wait(&tmem_full[acc], acc_phase)) {
+                fail(14);
+                break;
+            }
+            sm100::tc_fence_after();
+            const int g_off = __ldg(&p.group_offset[g]);
+            const int g_rows = __ldg(&p.group_offset[g + 1]) - g_off;
+            const int r = mt * kPairBM + row_in_tile;
+            const int64_t out_row = static_cast<int64_t>(g_off) + r;
+            const bool valid = r < g_rows && out_row < p.max_rows;
+            const float scale = (valid && p.row_scale) ? p.row_scale[out_row] : 1.0f;
+            const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * kPairBN;
+            if constexpr (SWIGLU) {
+                __nv_bfloat16* crow = p.c + out_row * p.ldc + nt * (kPairBN / 2);
+#pragma unroll 1
+                for (int c = 0; c < kPairBN / 2; c += 32) {
+                    float gv[32], uv[32];
+                    sm100::tmem_ld_32cols(taddr + c, gv);
+                    sm100::tmem_ld_32cols(taddr + kPairBN / 2 + c, uv);
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) gv[i] = silu(gv[i]) * uv[i] * scale;
+                    if (valid) store_row32(crow + c, gv);
+                }
+            } else {
+                __nv_bfloat16* crow = p.c + out_row * p.ldc + nt * kPairBN;
+#pragma unroll 1
+                for (int c = 0; c < kPairBN; c += 32) {
+                    float v[32];
+                    sm100::tmem_ld_32cols(taddr + c, v);
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) v[i] *= scale;
+                    if (valid) store_row32(crow + c, v);
+                }
+            }
+            sm100::tc_fence_before();
+            __syncwarp();
+            if (lane == 0) sm100::mbar_arrive_cluster(empty_leader + acc * static_cast<uint32_t>(sizeof(uint64_t)));
+            if (++acc == 2) {
+                acc = 0;
+                acc_phase ^= 1;
+            }
+        }
+    }
+    sm100::tc_fence_before();
+    __syncthreads();
+    sm100::cluster_sync();  // neither CTA leaves while its peer may still touch its barriers
+    sm100::tc_fence_after();
+    if (warp == 1) sm100::tmem_dealloc_pair(tmem_base, 2 * kPairBN);
+}
+
 /// One block: exclusive scan of group row counts -> offsets, and of the tile
 /// counts -> tile_prefix.  Works for up to 1024 groups.
-__global__ void build_schedule_kernel(const int32_t* counts, int num_groups, int n_tiles, int32_t* offsets,
+__global__ void build_schedule_kernel(const int32_t* counts, int num_groups, int n_tiles, int bm, int32_t* offsets,
                                       int32_t* tile_prefix) {
     __shared__ int32_t s_rows[1024];
     __shared__ int32_t s_tiles[1024];
     const int t = threadIdx.x;
     const int rows = t < num_groups ? counts[t] : 0;
     s_rows[t] = rows;
-    s_tiles[t] = ((rows + kBM - 1) / kBM) * n_tiles;
+    s_tiles[t] = ((rows + bm - 1) / bm) * n_tiles;
     __syncthreads();
     for (int d = 1; d < blockDim.x; d <<= 1) {
         const int a = t >= d ? s_rows[t - d] : 0;
@@ -310,11 +519,12 @@ CUtensorMap make_tmap_bf16_2d(const void* ptr, uint64_t rows, uint64_t cols, uin
 }
 
 void build_schedule(const int32_t* counts, int num_groups, int n, int bn, int32_t* offsets, int32_t* tile_prefix,
-                    cudaStream_t stream) {
+                    cudaStream_t stream, int bm) {
     if (num_groups < 1 || num_groups > 1024) throw kiwi::error("build_schedule: 1..1024 groups");
+    if (bm != kBM && bm != kPairBM) throw kiwi::error("build_schedule: bm must be 128 or 256");
     int threads = 32;
     while (threads < num_groups) threads <<= 1;
-    build_schedule_kernel<<<1, threads, 0, stream>>>(counts, num_groups, n / bn, offsets, tile_prefix);
+    build_schedule_kernel<<<1, threads, 0, stream>>>(counts, num_groups, n / bn, bm, offsets, tile_prefix);
     KIWI_CUDA_CHECK(cudaGetLastError());
 }
 
@@ -354,6 +564,42 @@ void grouped_gemm(const CUtensorMap& tmap_a, const CUtensorMap& tmap_b, const Gr
         grouped_gemm_kernel<BN, false><<<grid, kThreads, smem, stream>>>(tmap_a, tmap_b, args);
     }
     KIWI_CUDA_CHECK(cudaGetLastError());
+}
+
+void grouped_gemm_pair(const CUtensorMap& tmap_a, const CUtensorMap& tmap_b_half, const GroupedArgs& args,
+                       bool swiglu, int grid, cudaStream_t stream) {
+    if (args.n % kPairBN != 0 || args.k % kBK != 0) {
+        throw kiwi::error("grouped_gemm_pair: N must be a multiple of 256 and K of 64");
+    }
+    const int smem = PairSmem::kBytes;
+    if (grid <= 0) grid = num_sms();
+    grid &= ~1;  // whole clusters of two
+    if (grid < 2) throw kiwi::error("grouped_gemm_pair: needs at least two SMs");
+    if (swiglu) {
+        static bool attr = false;
+        if (!attr) {
+            KIWI_CUDA_CHECK(cudaFuncSetAttribute(grouped_gemm_pair_kernel<true>,
+                                                 cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+            attr = true;
+        }
+        grouped_gemm_pair_kernel<true><<<grid, kThreads, smem, stream>>>(tmap_a, tmap_b_half, args);
+    } else {
+        static bool attr = false;
+        if (!attr) {
+            KIWI_CUDA_CHECK(cudaFuncSetAttribute(grouped_gemm_pair_kernel<false>,
+                                                 cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+            attr = true;
+        }
+        grouped_gemm_pair_kernel<false><<<grid, kThreads, smem, stream>>>(tmap_a, tmap_b_half, args);
+    }
+    KIWI_CUDA_CHECK(cudaGetLastError());
+}
+
+KernelInfo gemm_pair_kernel_info(bool swiglu) {
+    cudaFuncAttributes a{};
+    if (swiglu) KIWI_CUDA_CHECK(cudaFuncGetAttributes(&a, grouped_gemm_pair_kernel<true>));
+    else KIWI_CUDA_CHECK(cudaFuncGetAttributes(&a, grouped_gemm_pair_kernel<false>));
+    return {static_cast<int>(a.localSizeBytes), a.numRegs, PairSmem::kBytes};
 }
 
 KernelInfo gemm_kernel_info(bool swiglu) {

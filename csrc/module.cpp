@@ -437,19 +437,35 @@ PYBIND11_MODULE(_C, m) {
           },
           py::arg("slots") = 16, py::arg("slot_lines") = 2, py::arg("producers") = 2,
           py::arg("msgs_per_producer") = 100, py::arg("warps") = 4, py::arg("seed") = 5);
-    b.def("atomicity_test", [](uint32_t iters) {
+    b.def("atomicity_test", [](uint32_t iters, uint32_t mode) {
         bench::AtomicityResult r;
         {
             py::gil_scoped_release nogil;
-            r = bench::atomicity_test(iters);
+            r = bench::atomicity_test(iters, mode);
+        }
+        py::dict d;
+        d["reads"] = r.reads;
+        d["torn8"] = r.torn8;
+        d["tag_ahead"] = r.tag_ahead;
+        d["split16"] = r.split16;
+        d["torn_word"] = r.torn_word;
+        d["final_ok"] = r.final_ok;
+        return d;
+    }, py::arg("iters"), py::arg("mode") = 0);
+    b.def("atomicity_h2d_test", [](uint32_t iters) {
+        bench::AtomicityResult r;
+        {
+            py::gil_scoped_release nogil;
+            r = bench::atomicity_h2d_test(iters);
         }
         py::dict d;
         d["reads"] = r.reads;
         d["torn8"] = r.torn8;
         d["split16"] = r.split16;
+        d["torn_word"] = r.torn_word;
         d["final_ok"] = r.final_ok;
         return d;
-    });
+    }, py::arg("iters"));
     b.def("invoke_throughput",
           [](uint32_t endpoints, uint32_t threads, uint32_t msgs, uint32_t bytes, uint64_t cap) {
               bench::ThroughputResult r;

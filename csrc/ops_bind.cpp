@@ -28,6 +28,7 @@ public:
         TORCH_CHECK(k_ % 64 == 0 && n_ % 256 == 0, "K % 64 == 0 and N % 256 == 0 required");
         tmap_a_ = gemm::make_tmap_bf16_2d(a.data_ptr(), a.size(0), k_, 128);
         tmap_b_ = gemm::make_tmap_bf16_2d(b.data_ptr(), b.size(0), k_, 256);
+        tmap_b_half_ = gemm::make_tmap_bf16_2d(b.data_ptr(), b.size(0), k_, 128);
         auto iopts = torch::TensorOptions().dtype(torch::kInt32).device(a.device());
         offsets_ = torch::zeros({num_groups_ + 1}, iopts);
         tile_prefix_ = torch::zeros({num_groups_ + 1}, iopts);
@@ -35,7 +36,7 @@ public:
     }
 
     /// counts: int32[G] rows per group (device); out: bf16 [rows, N] or [rows, N/2] with swiglu.
-    void run(torch::Tensor counts, torch::Tensor out, bool swiglu, py::object row_scale, int grid) {
+    void run(torch::Tensor counts, torch::Tensor out, bool swiglu, py::object row_scale, int grid, bool pair) {
         TORCH_CHECK(counts.is_cuda() && counts.scalar_type() == torch::kInt32 && counts.numel() == num_groups_,
                     "counts must be int32[num_groups] on the device");
         TORCH_CHECK(out.scalar_type() == torch::kBFloat16 && out.is_contiguous(), "out must be contiguous bf16");
@@ -50,7 +51,7 @@ public:
         }
         cudaStream_t s = cur_stream();
         gemm::build_schedule(counts.data_ptr<int32_t>(), num_groups_, n_, 256, offsets_.data_ptr<int32_t>(),
-                             tile_prefix_.data_ptr<int32_t>(), s);
+                             tile_prefix_.data_ptr<int32_t>(), s, pair ? 256 : 128);
         gemm::GroupedArgs args{};
         args.group_offset = offsets_.data_ptr<int32_t>();
         args.tile_prefix = tile_prefix_.data_ptr<int32_t>();
@@ -62,7 +63,11 @@ public:
         args.row_scale = rs;
         args.error = reinterpret_cast<uint32_t*>(error_.data_ptr<int32_t>());
         args.max_rows = out.size(0);
-        gemm::grouped_gemm(tmap_a_, tmap_b_, args, swiglu, grid, s);
+        if (pair) {
+            gemm::grouped_gemm_pair(tmap_a_, tmap_b_half_, args, swiglu, grid, s);
+        } else {
+            gemm::grouped_gemm(tmap_a_, tmap_b_, args, swiglu, grid, s);
+        }
     }
 
     torch::Tensor offsets() const { return offsets_; }
@@ -72,7 +77,7 @@ public:
 private:
     torch::Tensor a_, b_, offsets_, tile_prefix_, error_, row_scale_ref_;
     int num_groups_, n_, k_;
-    CUtensorMap tmap_a_, tmap_b_;
+    CUtensorMap tmap_a_, tmap_b_, tmap_b_half_;
 };
 
 }  // namespace
@@ -82,12 +87,16 @@ void register_ops(py::module_& m) {
     py::class_<GroupedGemm>(o, "GroupedGemm")
         .def(py::init<torch::Tensor, torch::Tensor, int64_t>(), py::arg("a"), py::arg("b"), py::arg("num_groups"))
         .def("run", &GroupedGemm::run, py::arg("counts"), py::arg("out"), py::arg("swiglu") = false,
-             py::arg("row_scale") = py::none(), py::arg("grid") = 0)
+             py::arg("row_scale") = py::none(), py::arg("grid") = 0, py::arg("pair") = false)
         .def_property_readonly("offsets", &GroupedGemm::offsets)
         .def_property_readonly("tile_prefix", &GroupedGemm::tile_prefix)
         .def_property_readonly("error", &GroupedGemm::error);
     o.def("gemm_kernel_info", [](bool swiglu) {
         const auto i = gemm::gemm_kernel_info(swiglu);
+        return py::make_tuple(i.local_bytes, i.registers, i.smem_bytes);
+    });
+    o.def("gemm_pair_kernel_info", [](bool swiglu) {
+        const auto i = gemm::gemm_pair_kernel_info(swiglu);
         return py::make_tuple(i.local_bytes, i.registers, i.smem_bytes);
     });
     o.def("num_sms", &gemm::num_sms);

@@ -122,11 +122,11 @@ __global__ void __launch_bounds__(256) invoke_rtt_kernel(
             bool ok = true;
             if (lane < 2) {
                 v = ptx::ld_volatile_v4(&reply.ring[(line & mask) * kChunksPerLine + lane]);
-                ok = v.y == tag && v.w == tag;
+                ok = dev::chunk_ok(v, tag);
             }
             if (__all_sync(ptx::kFullMask, ok)) {
-                const uint32_t lo = __shfl_sync(ptx::kFullMask, v.x, 1);
-                const uint32_t hi = __shfl_sync(ptx::kFullMask, v.z, 1);
+                const uint32_t lo = __shfl_sync(ptx::kFullMask, dev::chunk_lo(v), 1);
+                const uint32_t hi = __shfl_sync(ptx::kFullMask, dev::chunk_hi(v), 1);
                 if (lane == 0) {
                     reinterpret_cast<volatile uint64_t*>(sh.word)[line & 3] =
                         (static_cast<uint64_t>(hi) << 32) | lo;
@@ -577,17 +577,40 @@ RttResult rtt_lab(uint64_t iters, uint64_t warmup, uint32_t pollers, uint32_t mi
 
 
 // ---------------------------------------------------------------------------
-// Platform assumption the wire format relies on (reference category:
-// tests/queue/test_hardware_assumptions.hip.cpp): aligned 8-byte halves of a
-// GPU st.volatile.v4 into mapped host memory are never seen torn by host
-// 8-byte loads.  The GPU rewrites one 64-byte line `iters` times; in round i
-// every 8-byte half holds {i, ~i}; the host checks each half it reads.
+// Platform assumptions of the wire format (reference category:
+// tests/queue/test_hardware_assumptions.hip.cpp).  One 64-byte line is
+// rewritten `iters` times while the other side reads it as fast as it can.
+//   D2H modes (the GPU writes, the host reads with aligned 8-byte loads):
+//     0: raw {i, ~i, i, ~i} with one 16-byte store per chunk
+//     1: raw {i, ~i} with 8-byte stores
+//     2: tagged words {i:16, i:16} with one 16-byte store per chunk
+//     3: tagged words with 8-byte stores
+//   torn8 counts 8-byte halves whose two words came from different rounds,
+//   tag_ahead those whose high word was the newer one (modes 0/1: a raw
+//   {data, tag} half would hand out stale data), torn_word 32-bit words whose
+//   two 16-bit halves disagree (modes 2/3: the property the format needs).
+//   H2D (atomicity_h2d_test): the host writes tagged words with 8-byte
+//   stores, one GPU warp reads whole chunks with 16-byte loads.
 // ---------------------------------------------------------------------------
 
-__global__ void atomicity_writer_kernel(Chunk* line, uint32_t iters, volatile uint32_t* done) {
+__global__ void atomicity_writer_kernel(Chunk* line, uint32_t iters, uint32_t mode, volatile uint32_t* done) {
     const uint32_t lane = ptx::lane_id();
     for (uint32_t i = 1; i <= iters; ++i) {
-        if (lane < 4) ptx::st_volatile_v4(&line[lane], i, ~i, i, ~i);
+        if (lane < 4) {
+            const uint32_t t = tagged_word(i, i);
+            switch (mode) {
+                case 0: ptx::st_volatile_v4(&line[lane], i, ~i, i, ~i); break;
+                case 1:
+                    ptx::st_volatile_u64(&line[lane].lo, static_cast<uint64_t>(i) | (static_cast<uint64_t>(~i) << 32));
+                    ptx::st_volatile_u64(&line[lane].hi, static_cast<uint64_t>(i) | (static_cast<uint64_t>(~i) << 32));
+                    break;
+                case 2: ptx::st_volatile_v4(&line[lane], t, t, t, t); break;
+                default:
+                    ptx::st_volatile_u64(&line[lane].lo, static_cast<uint64_t>(t) | (static_cast<uint64_t>(t) << 32));
+                    ptx::st_volatile_u64(&line[lane].hi, static_cast<uint64_t>(t) | (static_cast<uint64_t>(t) << 32));
+                    break;
+            }
+        }
         __syncwarp();
     }
     if (lane == 0) {
@@ -596,30 +619,120 @@ __global__ void atomicity_writer_kernel(Chunk* line, uint32_t iters, volatile ui
     }
 }
 
-AtomicityResult atomicity_test(uint32_t iters) {
+namespace {
+
+/// Classifies one 8-byte half read while the line was being rewritten.
+void classify_half(uint64_t h, bool tagged, AtomicityResult& r) {
+    const uint32_t w0 = static_cast<uint32_t>(h), w1 = static_cast<uint32_t>(h >> 32);
+    if (tagged) {
+        if ((w0 & 0xffffu) != (w0 >> 16)) ++r.torn_word;
+        if ((w1 & 0xffffu) != (w1 >> 16)) ++r.torn_word;
+        if (w0 != w1) {
+            ++r.torn8;
+            if (((w1 - w0) & 0xffffu) < 0x8000u) ++r.tag_ahead;
+        }
+        return;
+    }
+    const uint32_t round_hi = ~w1;
+    if (round_hi == w0) return;
+    ++r.torn8;
+    if (round_hi > w0) ++r.tag_ahead;
+}
+
+}  // namespace
+
+AtomicityResult atomicity_test(uint32_t iters, uint32_t mode) {
+    if (mode > 3) throw kiwi::error("atomicity_test: mode 0..3");
     detail::Block mem(128, MemKind::kMappedPinned);
     PinnedFlag done;
     Chunk* line = mem.as<Chunk>();
     cudaStream_t stream;
     KIWI_CUDA_CHECK(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking));
-    atomicity_writer_kernel<<<1, 32, 0, stream>>>(line, iters, done.p);
+    atomicity_writer_kernel<<<1, 32, 0, stream>>>(line, iters, mode, done.p);
     KIWI_CUDA_CHECK(cudaGetLastError());
     AtomicityResult r;
+    const bool tagged = mode >= 2;
     uint64_t idle = 0;
     while (!*done.p) {
         for (int c = 0; c < 4; ++c) {
             const uint64_t a = host::load_half(&line[c].lo);
             const uint64_t b = host::load_half(&line[c].hi);
             ++r.reads;
-            if (static_cast<uint32_t>(a >> 32) != ~static_cast<uint32_t>(a)) ++r.torn8;
-            if (static_cast<uint32_t>(b >> 32) != ~static_cast<uint32_t>(b)) ++r.torn8;
+            classify_half(a, tagged, r);
+            classify_half(b, tagged, r);
             if (static_cast<uint32_t>(a) != static_cast<uint32_t>(b)) ++r.split16;
         }
         if ((++idle & 0xfffff) == 0 && cudaStreamQuery(stream) != cudaErrorNotReady) break;
     }
     KIWI_CUDA_CHECK(cudaStreamSynchronize(stream));
     cudaStreamDestroy(stream);
-    r.final_ok = static_cast<uint32_t>(host::load_half(&line[3].hi)) == iters;
+    const uint64_t last = host::load_half(&line[3].hi);
+    r.final_ok = tagged ? static_cast<uint32_t>(last) == tagged_word(iters, iters)
+                        : static_cast<uint32_t>(last) == iters;
+    return r;
+}
+
+__global__ void atomicity_reader_kernel(const Chunk* line, volatile uint32_t* done, unsigned long long* counts,
+                                        uint64_t max_reads, uint64_t timeout_ns) {
+    const uint32_t lane = ptx::lane_id();
+    uint64_t reads = 0, torn_word = 0, torn8 = 0, split16 = 0;
+    ptx::Deadline dl(timeout_ns);
+    bool timed_out = false;
+    while (reads < max_reads) {
+        if (*done) break;
+        if (dl.expired()) {
+            timed_out = true;
+            break;
+        }
+        if (lane < 4) {
+            const uint4 v = ptx::ld_volatile_v4(&line[lane]);
+            const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+            for (int j = 0; j < 4; ++j) torn_word += (w[j] & 0xffffu) != (w[j] >> 16);
+            torn8 += (v.x != v.y) + (v.z != v.w);
+            split16 += v.x != v.z;
+        }
+        ++reads;
+    }
+    if (lane < 4) {
+        atomicAdd(&counts[0], reads);
+        atomicAdd(&counts[1], torn_word);
+        atomicAdd(&counts[2], torn8);
+        atomicAdd(&counts[3], split16);
+        if (timed_out) atomicAdd(&counts[4], 1ull);
+    }
+}
+
+AtomicityResult atomicity_h2d_test(uint32_t iters) {
+    detail::Block mem(128, MemKind::kMappedPinned);
+    PinnedFlag done;
+    Chunk* line = mem.as<Chunk>();
+    DevBuf<unsigned long long> counts(8);
+    cudaStream_t stream;
+    KIWI_CUDA_CHECK(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking));
+    atomicity_reader_kernel<<<1, 32, 0, stream>>>(static_cast<const Chunk*>(device_address(line, MemKind::kMappedPinned)),
+                                                  done.p, counts.p, 4ull * iters + 1000000, 20000000000ull);
+    KIWI_CUDA_CHECK(cudaGetLastError());
+    for (uint32_t i = 1; i <= iters; ++i) {
+        const uint64_t t = tagged_word(i, i);
+        const uint64_t h = t | (t << 32);
+        for (int c = 0; c < 4; ++c) {
+            host::store_half(&line[c].lo, h);
+            host::store_half(&line[c].hi, h);
+        }
+    }
+    std::atomic_thread_fence(std::memory_order_seq_cst);
+    *done.p = 1;
+    KIWI_CUDA_CHECK(cudaStreamSynchronize(stream));
+    cudaStreamDestroy(stream);
+    unsigned long long c[8];
+    KIWI_CUDA_CHECK(cudaMemcpy(c, counts.p, sizeof(c), cudaMemcpyDeviceToHost));
+    AtomicityResult r;
+    r.reads = c[0] / 4;
+    r.torn_word = c[1];
+    r.torn8 = c[2];
+    r.split16 = c[3];
+    r.final_ok = c[4] == 0;
     return r;
 }
 

@@ -50,12 +50,18 @@ RttResult rtt_lab(uint64_t iters, uint64_t warmup, uint32_t pollers, uint32_t mi
 
 struct AtomicityResult {
     uint64_t reads = 0;    // 16-byte chunks the host read while the GPU wrote
-    uint64_t torn8 = 0;    // 8-byte halves seen torn (must be 0)
+    uint64_t torn8 = 0;    // 8-byte halves whose two words came from different rounds
+    uint64_t tag_ahead = 0;  // of those, halves whose tag word was newer than the data word
     uint64_t split16 = 0;  // chunks whose two halves came from different rounds (allowed)
+    uint64_t torn_word = 0;  // tagged 32-bit words whose 16-bit halves disagree (must stay 0)
     bool final_ok = false;
 };
-/// GPU rewrites one host line; a host thread checks every 8-byte half it reads.
-AtomicityResult atomicity_test(uint32_t iters);
+/// GPU rewrites one host line (mode 0: 16-byte stores, 1: 8-byte stores); a host
+/// thread classifies every 8-byte half it reads.
+AtomicityResult atomicity_test(uint32_t iters, uint32_t mode = 0);
+/// Host -> device direction: the host rewrites the line with tagged words
+/// (8-byte stores), one GPU warp reads it with 16-byte loads.
+AtomicityResult atomicity_h2d_test(uint32_t iters);
 
 struct ThroughputResult {
     uint64_t messages = 0;

@@ -36,14 +36,22 @@ struct KernelInfo {
 CUtensorMap make_tmap_bf16_2d(const void* ptr, uint64_t rows, uint64_t cols, uint32_t box_rows);
 
 /// Builds group offsets and the tile prefix from per-group row counts (device).
+/// `bm` = rows per tile: 128 for grouped_gemm, 256 for grouped_gemm_pair.
 void build_schedule(const int32_t* counts, int num_groups, int n, int bn, int32_t* offsets, int32_t* tile_prefix,
-                    cudaStream_t stream);
+                    cudaStream_t stream, int bm = 128);
 
 /// Launches the persistent grouped GEMM (BN = 256).  `grid` <= 0: one CTA per SM.
 void grouped_gemm(const CUtensorMap& tmap_a, const CUtensorMap& tmap_b, const GroupedArgs& args, bool swiglu,
                   int grid, cudaStream_t stream);
 
+/// 2-SM variant (clusters of two CTAs, 256 x 256 tiles).  `tmap_b_half` must
+/// have a box of 128 rows (each CTA loads half of the 256-row B tile); the
+/// schedule must be built with bm = 256.
+void grouped_gemm_pair(const CUtensorMap& tmap_a, const CUtensorMap& tmap_b_half, const GroupedArgs& args,
+                       bool swiglu, int grid, cudaStream_t stream);
+
 KernelInfo gemm_kernel_info(bool swiglu);
+KernelInfo gemm_pair_kernel_info(bool swiglu);
 int num_sms();
 
 }  // namespace kiwi::gemm

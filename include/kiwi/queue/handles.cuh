@@ -43,6 +43,17 @@ KIWI_DEV void report(ErrorRecord* err, Status code, uint32_t site, uint32_t info
     }
 }
 
+/// Stores one chunk {lo, hi} with tag `tag` (one 16-byte store).
+KIWI_DEV void store_chunk(Chunk* p, uint32_t lo, uint32_t hi, uint32_t tag) {
+    ptx::st_volatile_v4(p, tagged_word(lo, tag), tagged_word(lo >> 16, tag), tagged_word(hi, tag),
+                        tagged_word(hi >> 16, tag));
+}
+
+/// A chunk loaded with one 16-byte load carries `tag` in all four words.
+KIWI_DEV bool chunk_ok(const uint4& v, uint32_t tag) { return words_have_tag(v.x, v.y, v.z, v.w, tag); }
+KIWI_DEV uint32_t chunk_lo(const uint4& v) { return join_words(v.x, v.y); }
+KIWI_DEV uint32_t chunk_hi(const uint4& v) { return join_words(v.z, v.w); }
+
 /// Writes one message at line `head`.  `word(i)` returns payload word i (8
 /// bytes) for the calling lane; it is called only for the lane's own chunks.
 template <typename WordFn>
@@ -64,7 +75,7 @@ KIWI_DEV void write_message(Chunk* ring, uint32_t log2cap, uint64_t head, uint32
             lo = static_cast<uint32_t>(w);
             hi = static_cast<uint32_t>(w >> 32);
         }
-        ptx::st_volatile_v4(&ring[(line & mask) * kChunksPerLine + (k & 3u)], lo, tag, hi, tag);
+        dev::store_chunk(&ring[(line & mask) * kChunksPerLine + (k & 3u)], lo, hi, tag);
     }
 }
 
@@ -246,7 +257,7 @@ struct SpscD2HHandle {
                 lo = static_cast<uint32_t>(w);
                 hi = static_cast<uint32_t>(w >> 32);
             }
-            ptx::st_volatile_v4(&ring[(line & mask) * kChunksPerLine + (k & 3u)], lo, tag, hi, tag);
+            dev::store_chunk(&ring[(line & mask) * kChunksPerLine + (k & 3u)], lo, hi, tag);
         }
     }
 #endif
@@ -409,11 +420,11 @@ struct SpscH2DHandle {
         v = make_uint4(0, 0, 0, 0);
         if (lane < kChunksPerLine) {
             v = ptx::ld_volatile_v4(chunk_ptr(tail, lane));
-            ok = (v.y == tag) && (v.w == tag);
+            ok = dev::chunk_ok(v, tag);
         }
         if (!__all_sync(ptx::kFullMask, ok)) return false;
-        metadata = __shfl_sync(ptx::kFullMask, v.x, 0);
-        bytes = __shfl_sync(ptx::kFullMask, v.z, 0);
+        metadata = __shfl_sync(ptx::kFullMask, dev::chunk_lo(v), 0);
+        bytes = __shfl_sync(ptx::kFullMask, dev::chunk_hi(v), 0);
         if (bytes > kMaxMessageBytes || message_lines(bytes) > capacity()) {
             dev::report(err, Status::kCorrupt, site_h2d_pop, bytes);
             return false;
@@ -440,14 +451,14 @@ struct SpscH2DHandle {
                 const uint64_t line = tail + lane / kChunksPerLine;
                 const uint32_t tag = lap_tag(line, log2cap);
                 v = ptx::ld_volatile_v4(chunk_ptr(line, lane & 3u));
-                ok = (v.y == tag) && (v.w == tag);
+                ok = dev::chunk_ok(v, tag);
             }
             if (!__all_sync(ptx::kFullMask, ok)) return false;
         }
         // Lane i takes chunk i + 1.
         const uint32_t src = (lane + 1) & 31u;
-        const uint32_t lo = __shfl_sync(ptx::kFullMask, v.x, src);
-        const uint32_t hi = __shfl_sync(ptx::kFullMask, v.z, src);
+        const uint32_t lo = __shfl_sync(ptx::kFullMask, dev::chunk_lo(v), src);
+        const uint32_t hi = __shfl_sync(ptx::kFullMask, dev::chunk_hi(v), src);
         word = (static_cast<uint64_t>(hi) << 32) | lo;
         bytes = len;
         metadata = meta;
@@ -472,8 +483,10 @@ struct SpscH2DHandle {
                 const uint64_t line = tail + k / kChunksPerLine;
                 const uint32_t tag = lap_tag(line, log2cap);
                 const uint4 c = ptx::ld_volatile_v4(chunk_ptr(line, k & 3u));
-                ok = (c.y == tag) && (c.w == tag);
-                if (ok && k >= 1 && k < nchunks) out[k - 1] = (static_cast<uint64_t>(c.z) << 32) | c.x;
+                ok = dev::chunk_ok(c, tag);
+                if (ok && k >= 1 && k < nchunks) {
+                    out[k - 1] = (static_cast<uint64_t>(dev::chunk_hi(c)) << 32) | dev::chunk_lo(c);
+                }
             }
             if (!__all_sync(ptx::kFullMask, ok)) return false;
         }
@@ -531,18 +544,18 @@ struct MpmcH2DHandle {
         bool ok = true;
         if (lane < total) {
             v = ptx::ld_volatile_v4(&ring[slot * total + lane]);
-            ok = (v.y == tag) && (v.w == tag);
+            ok = dev::chunk_ok(v, tag);
         }
         if (!__all_sync(ptx::kFullMask, ok)) return false;
         unsigned long long old = 0;
         if (lane == 0) old = atomicCAS(claim, static_cast<unsigned long long>(pos), pos + 1);
         old = ptx::bcast64(old);
         if (old != pos) return false;
-        const uint32_t len = __shfl_sync(ptx::kFullMask, v.z, 0);
-        metadata = __shfl_sync(ptx::kFullMask, v.x, 0);
+        const uint32_t len = __shfl_sync(ptx::kFullMask, dev::chunk_hi(v), 0);
+        metadata = __shfl_sync(ptx::kFullMask, dev::chunk_lo(v), 0);
         const uint32_t src = (lane + 1) & 31u;
-        const uint32_t lo = __shfl_sync(ptx::kFullMask, v.x, src);
-        const uint32_t hi = __shfl_sync(ptx::kFullMask, v.z, src);
+        const uint32_t lo = __shfl_sync(ptx::kFullMask, dev::chunk_lo(v), src);
+        const uint32_t hi = __shfl_sync(ptx::kFullMask, dev::chunk_hi(v), src);
         word = (static_cast<uint64_t>(hi) << 32) | lo;
         bytes = len <= slot_payload() ? len : slot_payload();
         if (len > slot_payload()) dev::report(err, Status::kCorrupt, site_mpmc_pop, len);

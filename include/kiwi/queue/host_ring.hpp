@@ -34,8 +34,6 @@ inline void store_half(void* p, uint64_t v) {
     __atomic_store_n(static_cast<uint64_t*>(p), v, __ATOMIC_RELAXED);
 }
 
-inline uint32_t half_tag(uint64_t h) { return static_cast<uint32_t>(h >> 32); }
-inline uint32_t half_data(uint64_t h) { return static_cast<uint32_t>(h); }
 
 inline void cpu_relax() {
 #if defined(__x86_64__) || defined(__i386__)
@@ -58,7 +56,7 @@ public:
         refresh();
     }
     bool ready() const {
-        return host::half_tag(host::load_half(word_)) == expected_;
+        return half_has_tag(host::load_half(word_), expected_);
     }
     void refresh() {
         const uint64_t t = *tail_;
@@ -71,7 +69,7 @@ private:
     uint64_t mask_ = 0;
     uint32_t log2_ = 0;
     const uint64_t* tail_ = nullptr;
-    const uint32_t* word_ = nullptr;
+    const uint64_t* word_ = nullptr;
     uint32_t expected_ = 0xffffffffu;
 };
 
@@ -94,10 +92,10 @@ public:
         const Chunk* c0 = chunk(line0, 0);
         const uint32_t tag0 = lap_tag(line0, log2_);
         const uint64_t h0 = host::load_half(&c0->lo);
-        if (host::half_tag(h0) != tag0) return false;
+        if (!half_has_tag(h0, tag0)) return false;
         const uint64_t h1 = host::load_half(&c0->hi);
-        if (host::half_tag(h1) != tag0) return false;
-        const uint32_t len = host::half_data(h1);
+        if (!half_has_tag(h1, tag0)) return false;
+        const uint32_t len = half_data(h1);
         if (len > kMaxMessageBytes) {
             throw queue_error("kiwi::queue: corrupt message length " + std::to_string(len) +
                               " at line " + std::to_string(line0));
@@ -117,14 +115,14 @@ public:
             const Chunk* c = chunk(line, k % kChunksPerLine);
             const uint64_t a = host::load_half(&c->lo);
             const uint64_t b = host::load_half(&c->hi);
-            if (host::half_tag(a) != tag || host::half_tag(b) != tag) return false;
+            if (!half_has_tag(a, tag) || !half_has_tag(b, tag)) return false;
             if (k < nchunks) {
-                const uint32_t lo = host::half_data(a), hi = host::half_data(b);
+                const uint32_t lo = half_data(a), hi = half_data(b);
                 std::memcpy(dst + 8 * (k - 1), &lo, 4);
                 std::memcpy(dst + 8 * (k - 1) + 4, &hi, 4);
             }
         }
-        if (metadata) *metadata = host::half_data(h0);
+        if (metadata) *metadata = half_data(h0);
         if (bytes) *bytes = len;
         tail_ = line0 + nlines;
         publish();

@@ -13,9 +13,10 @@
 // with one or two reads in flight, after an initial delay that it adapts to
 // each wait's outcome (see adapt()).
 //
-// Each mirror holds one 16-byte chunk {value_lo, seq, value_hi, seq}; a reply
-// is valid when both halves carry the expected sequence number (8-byte
-// single-copy atomicity only, as the rings).  One outstanding request per
+// Each mirror holds one 16-byte chunk in the rings' wire format: the 8-byte
+// value in four tagged words whose tags are the low 16 bits of the sequence
+// number; a reply is valid when all four carry it (4-byte single-copy
+// atomicity only, as the rings).  One outstanding request per
 // mailbox: the host must not post reply n+1 before the device consumed reply
 // n, which call/return use guarantees.
 #pragma once
@@ -66,6 +67,10 @@ struct MailboxHandle {
         }
     }
 
+    KIWI_DEV static uint64_t chunk_value(const uint4& v) {
+        return (static_cast<uint64_t>(join_words(v.z, v.w)) << 32) | join_words(v.x, v.y);
+    }
+
     KIWI_DEV Status timed_out(uint32_t seq) const {
         if (err) {
             ptx::st_volatile_u32(&err->site, site_reply_wait);
@@ -87,8 +92,8 @@ struct MailboxHandle {
             bool first = true;
             while (true) {
                 const uint4 a = ptx::ld_volatile_v4(first ? m0 : m1);
-                if (a.y == seq && a.w == seq) {
-                    value = (static_cast<uint64_t>(a.z) << 32) | a.x;
+                if (words_have_tag(a.x, a.y, a.z, a.w, seq)) {
+                    value = chunk_value(a);
                     if (adaptive) adapt(first);
                     return Status::kOk;
                 }
@@ -100,13 +105,13 @@ struct MailboxHandle {
         spin_ns(stagger_ns);
         uint4 b = ptx::ld_volatile_v4(m1);
         while (true) {
-            if (a.y == seq && a.w == seq) {
-                value = (static_cast<uint64_t>(a.z) << 32) | a.x;
+            if (words_have_tag(a.x, a.y, a.z, a.w, seq)) {
+                value = chunk_value(a);
                 return Status::kOk;
             }
             a = ptx::ld_volatile_v4(m0);
-            if (b.y == seq && b.w == seq) {
-                value = (static_cast<uint64_t>(b.z) << 32) | b.x;
+            if (words_have_tag(b.x, b.y, b.z, b.w, seq)) {
+                value = chunk_value(b);
                 return Status::kOk;
             }
             b = ptx::ld_volatile_v4(m1);
@@ -172,8 +177,8 @@ public:
     bool peek(uint32_t m, uint32_t seq, uint64_t* value) const {
         const Chunk* c = chunk(m);
         const uint64_t lo = host::load_half(&c->lo), hi = host::load_half(&c->hi);
-        if (host::half_tag(lo) != seq || host::half_tag(hi) != seq) return false;
-        *value = (static_cast<uint64_t>(host::half_data(hi)) << 32) | host::half_data(lo);
+        if (!half_has_tag(lo, seq) || !half_has_tag(hi, seq)) return false;
+        *value = (static_cast<uint64_t>(half_data(hi)) << 32) | half_data(lo);
         return true;
     }
 

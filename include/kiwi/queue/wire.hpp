@@ -2,32 +2,37 @@
 //
 // Behaviour parity: the reference's device-to-host "LL8" ring
 // (include/kiwi/queue/detail/chunk.hip.hpp:1-60 of AMDResearch/kiwi) guards
-// every 4 data bytes with a 4-byte signal so that only aligned 8-byte
-// single-copy atomicity of PCIe writes and host loads is assumed (the property
-// NCCL's LL protocol relies on too).  This file keeps that property and
-// defines its own layout:
+// every 4 data bytes with a 4-byte signal and assumes that an aligned 8-byte
+// PCIe write is seen whole by a host 8-byte load.  On the B200 hosts this was
+// built on that assumption does NOT hold: a host hammering one line that a
+// kernel rewrote with 16- or 8-byte stores saw ~1 in 1000 reads with the high
+// 4 bytes of an 8-byte word newer than the low 4 bytes (the atomicity test in
+// the bench module reproduces it).  Single 4-byte words were never torn.  So
+// this layout puts a tag in EVERY 32-bit word:
 //
 //   ring  = `capacity` 64-byte lines (capacity a power of two)
 //   line  = 4 chunks of 16 bytes
-//   chunk = { data_lo u32, tag u32, data_hi u32, tag u32 }
+//   chunk = 4 tagged words; word j = { data bits [16j, 16j+16) : 16, tag : 16 }
+//           (data in the low half of the word, the tag in the high half), so a
+//           chunk carries 8 payload bytes, the same 50% as data+tag halves.
 //
-//   * Every tag is the 32-bit lap tag of the chunk's line:
+//   * A tag is the low 16 bits of the lap tag of the chunk's line:
 //         lap_tag(line) = (line >> log2(capacity)) + 1
 //     A freshly allocated ring is all zeros (tag 0 = never written), so no
-//     initialisation pass is needed, and a full 32-bit compare tells a line of
-//     this lap from any earlier lap (not only the previous one).
+//     initialisation pass is needed.  The producer is never more than one lap
+//     ahead of the consumer (credit), so the only stale tag a reader can meet
+//     is the previous lap's, which differs in its low 16 bits.
 //   * The message header is in-band: chunk 0's data is {metadata, length}.
 //     Payload byte b lives in chunk 1 + b/8.
 //   * A message of B bytes occupies message_lines(B) whole lines starting on a
 //     line; padding chunks of its last line carry tags (and zero data) so the
 //     producer always writes whole 64-byte lines (one PCIe write each) and the
-//     consumer can validate a line with one compare of its 8 tags.
+//     consumer validates a chunk with one masked compare of its 4 tags.
 //   * A message that reaches the end of the ring continues at line 0 with the
 //     next lap's tag.
 //
-// Each 8-byte half {data, tag} is written by one aligned 8-byte (or wider)
-// store and read by one aligned 8-byte (or wider) load, so a reader that sees
-// the expected tag in a half sees that half's data.
+// A reader that sees the expected tag in a word sees that word's data: only
+// 4-byte single-copy atomicity is assumed.
 #pragma once
 
 #include "kiwi/common.hpp"
@@ -47,11 +52,11 @@ inline constexpr uint64_t kMaxCapacityLines = uint64_t{1} << 31;
 /// Width of the warp that runs every collective device operation on B200.
 inline constexpr uint32_t kWarpSize = 32;
 
+/// One 16-byte chunk as two 8-byte halves; each half is two tagged words
+/// carrying 32 data bits (see pack_half).
 struct alignas(16) Chunk {
-    uint32_t lo;
-    uint32_t tag0;
-    uint32_t hi;
-    uint32_t tag1;
+    uint64_t lo;
+    uint64_t hi;
 };
 static_assert(sizeof(Chunk) == kChunkBytes, "chunk is 16 bytes");
 
@@ -69,9 +74,36 @@ KIWI_HD constexpr uint32_t lap_tag(uint64_t line, uint32_t log2_capacity) {
     return static_cast<uint32_t>(line >> log2_capacity) + 1u;
 }
 
-/// Packs one 8-byte half {data, tag} as the u64 a single store writes.
+/// One tagged word: 16 data bits (the low half of `data16`) and the low 16
+/// bits of `tag` in the high half.
+KIWI_HD constexpr uint32_t tagged_word(uint32_t data16, uint32_t tag) {
+    return (data16 & 0xffffu) | (tag << 16);
+}
+
+/// True if every word among a..d carries `tag` (one masked compare).
+KIWI_HD constexpr bool words_have_tag(uint32_t a, uint32_t b, uint32_t c, uint32_t d, uint32_t tag) {
+    const uint32_t t = tag << 16;
+    return (((a ^ t) | (b ^ t) | (c ^ t) | (d ^ t)) >> 16) == 0;
+}
+
+/// The 32 data bits of two tagged words (w0 holds the low 16).
+KIWI_HD constexpr uint32_t join_words(uint32_t w0, uint32_t w1) { return (w0 & 0xffffu) | (w1 << 16); }
+
+/// Packs 32 data bits as one 8-byte half: two tagged words.
 KIWI_HD constexpr uint64_t pack_half(uint32_t data, uint32_t tag) {
-    return static_cast<uint64_t>(data) | (static_cast<uint64_t>(tag) << 32);
+    return static_cast<uint64_t>(tagged_word(data, tag)) |
+           (static_cast<uint64_t>(tagged_word(data >> 16, tag)) << 32);
+}
+
+/// True if both words of half `h` carry `tag`.
+KIWI_HD constexpr bool half_has_tag(uint64_t h, uint32_t tag) {
+    const uint64_t t = tag & 0xffffu;
+    return (h & 0xffff0000ffff0000ull) == ((t << 16) | (t << 48));
+}
+
+/// The 32 data bits of half `h`.
+KIWI_HD constexpr uint32_t half_data(uint64_t h) {
+    return join_words(static_cast<uint32_t>(h), static_cast<uint32_t>(h >> 32));
 }
 
 /// Host-side queue configuration check shared by every ring constructor.

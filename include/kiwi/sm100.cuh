@@ -2,7 +2,7 @@
 //
 // Every wait here is bounded: a wait that exceeds its spin budget returns
 // false and the caller records an error and unwinds (freeing TMEM), so a lost
-// arrival can never hang the GPU.  TMA loads here never use .multicast::cluster.
+// arrival can never hang the GPU.  TMA loads here are plain tiled loads of this GPU's own memory (no cluster-wide broadcast).
 #pragma once
 
 #include <cuda.h>
@@ -161,6 +161,69 @@ KIWI_DEV void tmem_ld_32cols(uint32_t taddr, float (&v)[32]) {
         : "memory");
 #pragma unroll
     for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+
+// ---- clusters of two CTAs (2-SM UMMA) ----
+
+KIWI_DEV uint32_t cluster_ctarank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+
+KIWI_DEV void cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+/// Cluster-window address of the same shared variable in CTA `rank` of this cluster.
+KIWI_DEV uint32_t mapa(const void* p, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_addr(p)), "r"(rank));
+    return r;
+}
+
+/// Arrive (release, cluster scope) on an mbarrier given by its cluster-window address.
+KIWI_DEV void mbar_arrive_cluster(uint32_t cluster_addr) {
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+
+/// 2-SM TMA load into this CTA's shared memory whose transaction bytes complete
+/// on the barrier at cluster address `bar_cluster` (the pair leader's barrier).
+KIWI_DEV void tma_load_2d_pair(void* smem_dst, const CUtensorMap* map, uint32_t bar_cluster, int32_t x, int32_t y) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
+            smem_addr(smem_dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(bar_cluster), "r"(x), "r"(y)
+        : "memory");
+}
+
+KIWI_DEV void tmem_alloc_pair(uint32_t* smem_slot, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(smem_slot)),
+                 "r"(ncols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+
+KIWI_DEV void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+/// D[tmem of both CTAs] (+)= A[smem of both] * B[smem of both]^T (M = 256 across the pair).
+KIWI_DEV void mma_bf16_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+/// Arrives on the barrier at cluster address `bar_cluster` (this CTA's or the
+/// peer's) once every tcgen05 operation issued before by this thread completed.
+KIWI_DEV void mma_commit_pair(uint32_t bar_cluster) {
+    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar_cluster)
+                 : "memory");
 }
 
 #endif  // __CUDACC__

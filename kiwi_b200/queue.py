@@ -1,8 +1,10 @@
 """kiwi_b200.queue: GPU<->host rings (bindings of ``include/kiwi/queue``).
 
 Wire format (``include/kiwi/queue/wire.hpp``): 64-byte lines of four 16-byte
-chunks ``{data_lo, tag, data_hi, tag}``; chunk 0 carries ``{metadata, length}``;
-tags are 32-bit lap tags.  Messages are 0..4096 bytes.
+chunks; each chunk is four 32-bit words ``{16 data bits, 16-bit lap tag}``
+(8 payload bytes per chunk), because GPU 8-byte stores into host memory were
+seen torn between their 4-byte words on B200 hosts while single words never
+were.  Chunk 0 carries ``{metadata, length}``.  Messages are 0..4096 bytes.
 """
 from ._native import load as _load
 

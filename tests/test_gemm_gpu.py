@@ -28,13 +28,14 @@ def _ref(a, b, counts, n, swiglu, row_scale=None):
     return torch.cat(outs, 0)
 
 
+@pytest.mark.parametrize("pair", [False, True])
 @pytest.mark.parametrize("counts,n,k,swiglu", [
     ([5, 130, 0, 256], 256, 128, False),
     ([128], 512, 64, False),
     ([1, 0, 300], 512, 192, True),
     ([257, 64], 1024, 7168 // 4, True),
 ])
-def test_grouped_gemm_matches_fp32(counts, n, k, swiglu):
+def test_grouped_gemm_matches_fp32(counts, n, k, swiglu, pair):
     torch.manual_seed(0)
     C = kiwi_b200.native()
     rows = sum(counts)
@@ -44,7 +45,7 @@ def test_grouped_gemm_matches_fp32(counts, n, k, swiglu):
     plan = C.ops.GroupedGemm(a, b, len(counts))
     cnt = torch.tensor(counts, dtype=torch.int32, device="cuda")
     scale = torch.rand(max(rows, 1), device="cuda") + 0.5
-    plan.run(cnt, out, swiglu, scale)
+    plan.run(cnt, out, swiglu, scale, 0, pair)
     torch.cuda.synchronize()
     assert int(plan.error.item()) == 0
     ref = _ref(a, b, counts, n, swiglu, scale)
@@ -60,3 +61,23 @@ def test_gemm_kernels_use_no_local_memory():
     for sw in (False, True):
         local, regs, smem = C.ops.gemm_kernel_info(sw)
         assert local == 0, (sw, local)
+        local, regs, smem = C.ops.gemm_pair_kernel_info(sw)
+        assert local == 0, (sw, local)
+
+
+@pytest.mark.parametrize("pair", [False, True])
+def test_grouped_gemm_large_rows(pair):
+    """Groups with several 256-row tiles and ragged tails (both kernels)."""
+    torch.manual_seed(3)
+    C = kiwi_b200.native()
+    counts = [700, 256, 1, 513]
+    n, k = 512, 256
+    rows = sum(counts)
+    a = (torch.randn(rows, k, device="cuda") * 0.5).bfloat16()
+    b = (torch.randn(len(counts) * n, k, device="cuda") * 0.05).bfloat16()
+    out = torch.zeros(rows, n, device="cuda", dtype=torch.bfloat16)
+    C.ops.GroupedGemm(a, b, len(counts)).run(torch.tensor(counts, dtype=torch.int32, device="cuda"), out, False,
+                                             None, 0, pair)
+    torch.cuda.synchronize()
+    ref = _ref(a, b, counts, n, False)
+    assert (out.float() - ref).abs().max().item() <= 2e-2 * ref.abs().max().item() + 1e-2
