@@ -33,7 +33,7 @@ import torch  # noqa: E402
 
 METRIC = "p50 GPU→CPU→GPU invoke µs; EP dispatch+combine µs & tokens/s at 1/2/4/8 B200"
 BASELINE_INVOKE_P50_US = 1.92   # published reference number (MI300X)
-KERNELS_PER_STEP = 11           # begin, route, dispatch, recv_count, 2 schedules, scatter, 2 GEMMs, combine x2
+KERNELS_PER_STEP = 12           # route, begin, dispatch, recv_count, 2 schedules, recv assign+copy, 2 GEMMs, combine x2
 
 
 def parse():
@@ -68,11 +68,16 @@ def main():
     from kiwi_b200.models import moe as moe_model
     from kiwi_b200.utils import dist as kdist
     from kiwi_b200.utils.clocks import ClockSampler
+    from kiwi_b200.utils.pipeline import HostDevicePipeline
+    from kiwi_b200.utils.topology import bind_process_to_gpu
 
     rank, world = kdist.init()
     if world != args.gpus:
         raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
     dev = torch.device("cuda", torch.cuda.current_device())
+    # Host buffers and threads on the GPU's NUMA node (pinned pages are placed
+    # on the allocating thread's node).
+    bind_process_to_gpu(dev.index)
     cfg = moe_model.CONFIGS[args.config]
     if args.tokens:
         cfg = moe_model.MoEConfig(**{**cfg.__dict__, "tokens_per_rank": args.tokens})
@@ -117,32 +122,35 @@ def main():
         layer.check()
     clk = clocks.summary()
 
-    # ---- end to end through the public API: pinned H2D inputs, D2H result ----
+    # ---- end to end through the public API: every step copies its inputs from
+    # pinned host memory and its result back to pinned host memory; the copies of
+    # neighbouring steps overlap the compute (HostDevicePipeline, 2 slots). ----
     e2e = None
     if not args.no_e2e:
         x_h = x.cpu().pin_memory()
         l_h = logits.cpu().pin_memory()
-        out_h = torch.empty(T, cfg.hidden, dtype=torch.bfloat16).pin_memory()
-        xd = torch.empty_like(x)
-        ld = torch.empty_like(logits)
-        for _ in range(2):
-            xd.copy_(x_h, non_blocking=True)
-            ld.copy_(l_h, non_blocking=True)
-            out_h.copy_(step(xd, ld), non_blocking=True)
-        kdist.barrier()
-        torch.cuda.synchronize()
-        s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        s2.record()
-        for _ in range(args.steps):
-            xd.copy_(x_h, non_blocking=True)
-            ld.copy_(l_h, non_blocking=True)
-            out_h.copy_(step(xd, ld), non_blocking=True)
-        e2.record()
+        out_h = [torch.empty(T, cfg.hidden, dtype=torch.bfloat16).pin_memory() for _ in range(2)]
+        if args.impl == "kiwi":
+            def fn(xx, ll, out):
+                layer(xx, ll, out=out)
+        else:
+            def fn(xx, ll, out):
+                out.copy_(layer(xx, ll))
+        pipe = HostDevicePipeline(fn, [(tuple(x.shape), x.dtype), (tuple(logits.shape), logits.dtype)],
+                                  ((T, cfg.hidden), torch.bfloat16), depth=2)
+        pipe.run(3, lambda i: (x_h, l_h), lambda i: out_h[i % 2], timed=False)
         torch.cuda.synchronize()
         kdist.barrier()
-        e2e_ms = kdist.max_over_ranks(s2.elapsed_time(e2) / args.steps)
+        torch.cuda.synchronize()
+        e2e_ms = pipe.run(args.steps, lambda i: (x_h, l_h), lambda i: out_h[i % 2]) / args.steps
+        torch.cuda.synchronize()
+        kdist.barrier()
+        e2e_ms = kdist.max_over_ranks(e2e_ms)
         e2e = {"value": world * T / (e2e_ms / 1e3), "unit": "tokens/s", "ms_per_step": e2e_ms,
-               "h2d_bytes_per_step": x.numel() * 2 + logits.numel() * 4, "d2h_bytes_per_step": T * cfg.hidden * 2}
+               "h2d_bytes_per_step": x.numel() * x.element_size() + logits.numel() * logits.element_size(),
+               "d2h_bytes_per_step": T * cfg.hidden * 2,
+               "api": "kiwi_b200.utils.pipeline.HostDevicePipeline over ExpertParallelMoE.forward"
+               if args.impl == "kiwi" else "HostDevicePipeline over NcclMoEBaseline.forward"}
 
     # ---- latency mode (128 tokens per rank) on the same layer ----
     lat = None

@@ -11,6 +11,9 @@ Ranks pair up (0<->1, 2<->3, ...).  For each size 8 B .. max (powers of two):
     4 data bytes and the sequence number -- no fence, no separate flag.
   * kiwi_put_bw: back-to-back puts of `size` bytes, one signal at the end.
   * kiwi_get: reads of `size` bytes from the partner's heap.
+  Both rotate through a 256 MB region (larger than the 126 MB L2), one
+  4 KB-aligned slot per repetition, so no repetition finds its lines cached
+  (re-reading one address measured L1/L2 hits, ~0.1 us, not NVLink).
   * nccl_sendrecv: torch.distributed send/recv ping-pong of the same size,
     CUDA events, one-way = round trip / 2.
 Data: seeded uniform uint8.  Every number is the max over ranks.
@@ -40,15 +43,16 @@ def main():
     peer = rank ^ 1
     initiator = rank % 2 == 0
     maxb = args.max_bytes
+    region = max(maxb, 256 << 20)
     flag_off = 0
     src_off = 4096
-    dst_off = src_off + maxb
-    ll_base = dst_off + maxb + 4096
+    dst_off = src_off + region
+    ll_base = dst_off + region + 4096
     heap = SymmetricHeap(ll_base + 65536)
     h = heap.native
     g = torch.Generator(device="cuda").manual_seed(1234 + rank)
-    src = heap.tensor(src_off, [maxb], torch.uint8)
-    src.copy_(torch.randint(0, 256, (maxb,), generator=g, device="cuda", dtype=torch.uint8))
+    src = heap.tensor(src_off, [region], torch.uint8)
+    src.copy_(torch.randint(0, 256, (region,), generator=g, device="cuda", dtype=torch.uint8))
     flag = heap.tensor(flag_off, [8], torch.int64)
     status = torch.zeros(2, dtype=torch.int32, device="cuda")
     sizes = [1 << i for i in range(3, int(np.log2(maxb)) + 1)]
@@ -84,13 +88,13 @@ def main():
         reps = max(1, min(1000, (256 << 20) // size))
         torch.cuda.synchronize()
         kdist.barrier()
-        h.put_bw(peer, initiator, size, reps, src_off, dst_off, flag_off, 1, el, status, 132, 5_000_000_000)
+        h.put_bw(peer, initiator, size, reps, src_off, dst_off, flag_off, 1, el, status, 132, 5_000_000_000, region)
         torch.cuda.synchronize()
         kdist.barrier()
         bw = size * reps / (el.item() / 1e9) / 1e9 if initiator and el.item() else 0.0
         # get
         glat = torch.zeros(20, dtype=torch.int64, device="cuda")
-        h.get(peer, size, 20, src_off, dst_off, glat, 132)
+        h.get(peer, size, 20, src_off, dst_off, glat, 132, region)
         torch.cuda.synchronize()
         get_us = float(np.percentile(glat.cpu().numpy()[5:], 50)) / 1e3
         # NCCL send/recv ping-pong

@@ -452,11 +452,11 @@ PYBIND11_MODULE(_C, m) {
         d["final_ok"] = r.final_ok;
         return d;
     }, py::arg("iters"), py::arg("mode") = 0);
-    b.def("atomicity_h2d_test", [](uint32_t iters) {
+    b.def("atomicity_h2d_test", [](uint32_t duration_ms) {
         bench::AtomicityResult r;
         {
             py::gil_scoped_release nogil;
-            r = bench::atomicity_h2d_test(iters);
+            r = bench::atomicity_h2d_test(duration_ms);
         }
         py::dict d;
         d["reads"] = r.reads;
@@ -465,7 +465,7 @@ PYBIND11_MODULE(_C, m) {
         d["torn_word"] = r.torn_word;
         d["final_ok"] = r.final_ok;
         return d;
-    }, py::arg("iters"));
+    }, py::arg("duration_ms"));
     b.def("invoke_throughput",
           [](uint32_t endpoints, uint32_t threads, uint32_t msgs, uint32_t bytes, uint64_t cap) {
               bench::ThroughputResult r;

@@ -106,15 +106,21 @@ void register_p2p(py::module_& m) {
         .def("put_bw",
              [](SymmetricHeap& h, int peer, bool sender, uint64_t bytes, uint64_t reps, uint64_t src_off,
                 uint64_t dst_off, uint64_t flag_off, uint64_t round, torch::Tensor elapsed, torch::Tensor status,
-                uint32_t max_blocks, uint64_t timeout_ns) {
+                uint32_t max_blocks, uint64_t timeout_ns, uint64_t region) {
                  launch_put_bw(h.view(), peer, sender, bytes, reps, src_off, dst_off, flag_off, round,
-                               u64_ptr(elapsed), u32_ptr(status), max_blocks, timeout_ns, cur_stream());
-             })
+                               u64_ptr(elapsed), u32_ptr(status), max_blocks, timeout_ns, cur_stream(), region);
+             },
+             py::arg("peer"), py::arg("sender"), py::arg("bytes"), py::arg("reps"), py::arg("src_off"),
+             py::arg("dst_off"), py::arg("flag_off"), py::arg("round"), py::arg("elapsed"), py::arg("status"),
+             py::arg("max_blocks"), py::arg("timeout_ns"), py::arg("region") = 0)
         .def("get",
              [](SymmetricHeap& h, int peer, uint64_t bytes, uint64_t reps, uint64_t src_off, uint64_t dst_off,
-                torch::Tensor lat, uint32_t max_blocks) {
-                 launch_get(h.view(), peer, bytes, reps, src_off, dst_off, u64_ptr(lat), max_blocks, cur_stream());
-             })
+                torch::Tensor lat, uint32_t max_blocks, uint64_t region) {
+                 launch_get(h.view(), peer, bytes, reps, src_off, dst_off, u64_ptr(lat), max_blocks, cur_stream(),
+                            region);
+             },
+             py::arg("peer"), py::arg("bytes"), py::arg("reps"), py::arg("src_off"), py::arg("dst_off"),
+             py::arg("lat"), py::arg("max_blocks"), py::arg("region") = 0)
         .def("all_pairs",
              [](SymmetricHeap& h, uint64_t data_off, uint64_t flag_off, uint64_t words, uint32_t round,
                 torch::Tensor status, uint64_t timeout_ns) {

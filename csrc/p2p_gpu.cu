@@ -111,10 +111,19 @@ void launch_pingpong_ll8(const HeapView& h, int peer, bool initiator, uint32_t w
 
 /// One-directional put bandwidth: `reps` back-to-back puts of `bytes`, one
 /// signal per block at the end; the receiver answers with one signal.
+/// Offset of repetition r when `region` bytes are rotated through in slots of
+/// round_up(bytes, 4096) (region 0: no rotation).  Benchmarks rotate through
+/// more than the 126 MB L2 so that no repetition finds its lines cached.
+KIWI_DEV uint64_t rep_offset(uint64_t r, uint64_t bytes, uint64_t region) {
+    const uint64_t stride = round_up(bytes, 4096);
+    const uint64_t slots = region >= stride ? region / stride : 1;
+    return (r % slots) * stride;
+}
+
 __global__ void __launch_bounds__(512) put_bw_kernel(HeapView h, int peer, int sender, uint64_t bytes, uint64_t reps,
                                                      uint64_t src_off, uint64_t dst_off, uint64_t flag_off,
                                                      uint64_t round, uint64_t* elapsed_ns, uint32_t* status,
-                                                     uint64_t timeout_ns) {
+                                                     uint64_t timeout_ns, uint64_t region) {
     const uint32_t nb = gridDim.x;
     const uint64_t* my_flag = reinterpret_cast<const uint64_t*>(h.base[h.rank] + flag_off);
     if (!sender) {
@@ -132,8 +141,9 @@ __global__ void __launch_bounds__(512) put_bw_kernel(HeapView h, int peer, int s
     const uint64_t my_bytes = my_off >= bytes ? 0 : (bytes - my_off < slice ? bytes - my_off : slice);
     const uint64_t t0 = ptx::globaltimer();
     for (uint64_t r = 0; r < reps; ++r) {
-        coop_copy(h.base[peer] + dst_off + my_off, h.base[h.rank] + src_off + my_off, my_bytes, threadIdx.x,
-                  blockDim.x);
+        const uint64_t ro = rep_offset(r, bytes, region);
+        coop_copy(h.base[peer] + dst_off + ro + my_off, h.base[h.rank] + src_off + ro + my_off, my_bytes,
+                  threadIdx.x, blockDim.x);
     }
     __syncthreads();
     if (threadIdx.x == 0) signal(h, peer, flag_off, 1, SignalOp::kAdd);
@@ -148,15 +158,17 @@ __global__ void __launch_bounds__(512) put_bw_kernel(HeapView h, int peer, int s
 
 /// Get: `reps` reads of `bytes` from the peer's heap into local memory.
 __global__ void __launch_bounds__(512) get_kernel(HeapView h, int peer, uint64_t bytes, uint64_t reps,
-                                                  uint64_t src_off, uint64_t dst_off, uint64_t* lat_ns) {
+                                                  uint64_t src_off, uint64_t dst_off, uint64_t* lat_ns,
+                                                  uint64_t region) {
     const uint32_t nb = gridDim.x;
     const uint64_t slice = round_up((bytes + nb - 1) / nb, 16);
     const uint64_t my_off = slice * blockIdx.x;
     const uint64_t my_bytes = my_off >= bytes ? 0 : (bytes - my_off < slice ? bytes - my_off : slice);
     for (uint64_t r = 0; r < reps; ++r) {
+        const uint64_t ro = rep_offset(r, bytes, region);
         const uint64_t t0 = ptx::globaltimer();
-        coop_copy(h.base[h.rank] + dst_off + my_off, h.base[peer] + src_off + my_off, my_bytes, threadIdx.x,
-                  blockDim.x);
+        coop_copy(h.base[h.rank] + dst_off + ro + my_off, h.base[peer] + src_off + ro + my_off, my_bytes,
+                  threadIdx.x, blockDim.x);
         __syncthreads();
         if (blockIdx.x == 0 && threadIdx.x == 0) lat_ns[r] = ptx::globaltimer() - t0;
     }
@@ -265,17 +277,17 @@ void launch_pingpong(const HeapView& h, int peer, bool initiator, uint64_t bytes
 
 void launch_put_bw(const HeapView& h, int peer, bool sender, uint64_t bytes, uint64_t reps, uint64_t src_off,
                    uint64_t dst_off, uint64_t flag_off, uint64_t round, uint64_t* elapsed, uint32_t* status,
-                   uint32_t max_blocks, uint64_t timeout_ns, cudaStream_t s) {
+                   uint32_t max_blocks, uint64_t timeout_ns, cudaStream_t s, uint64_t region) {
     const uint32_t nb = sender ? blocks_for(bytes, max_blocks) : 1;
     put_bw_kernel<<<nb, 512, 0, s>>>(h, peer, sender ? 1 : 0, bytes, reps, src_off, dst_off, flag_off, round,
-                                     elapsed, status, timeout_ns);
+                                     elapsed, status, timeout_ns, region);
     KIWI_CUDA_CHECK(cudaGetLastError());
 }
 
 void launch_get(const HeapView& h, int peer, uint64_t bytes, uint64_t reps, uint64_t src_off, uint64_t dst_off,
-                uint64_t* lat_ns, uint32_t max_blocks, cudaStream_t s) {
+                uint64_t* lat_ns, uint32_t max_blocks, cudaStream_t s, uint64_t region) {
     const uint32_t nb = blocks_for(bytes, max_blocks);
-    get_kernel<<<nb, bytes <= 4096 ? 128 : 512, 0, s>>>(h, peer, bytes, reps, src_off, dst_off, lat_ns);
+    get_kernel<<<nb, bytes <= 4096 ? 128 : 512, 0, s>>>(h, peer, bytes, reps, src_off, dst_off, lat_ns, region);
     KIWI_CUDA_CHECK(cudaGetLastError());
 }
 

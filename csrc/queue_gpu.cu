@@ -580,35 +580,52 @@ RttResult rtt_lab(uint64_t iters, uint64_t warmup, uint32_t pollers, uint32_t mi
 // Platform assumptions of the wire format (reference category:
 // tests/queue/test_hardware_assumptions.hip.cpp).  One 64-byte line is
 // rewritten `iters` times while the other side reads it as fast as it can.
-//   D2H modes (the GPU writes, the host reads with aligned 8-byte loads):
-//     0: raw {i, ~i, i, ~i} with one 16-byte store per chunk
-//     1: raw {i, ~i} with 8-byte stores
-//     2: tagged words {i:16, i:16} with one 16-byte store per chunk
-//     3: tagged words with 8-byte stores
-//   torn8 counts 8-byte halves whose two words came from different rounds,
-//   tag_ahead those whose high word was the newer one (modes 0/1: a raw
-//   {data, tag} half would hand out stale data), torn_word 32-bit words whose
-//   two 16-bit halves disagree (modes 2/3: the property the format needs).
-//   H2D (atomicity_h2d_test): the host writes tagged words with 8-byte
-//   stores, one GPU warp reads whole chunks with 16-byte loads.
+// D2H modes (the GPU writes round i, the host reads with aligned 8-byte loads;
+// "v4" = one 16-byte store per chunk, "u64" = two 8-byte stores):
+//   0 v4 / 1 u64: raw words {i, ~i}       3-4: raw {~i, i} (v4 / u64)
+//   2 v4 / 5 u64: tagged {i:16 | i:16}    6-7: tagged {mix16(i) | i:16}
+//   8 v4:         {i:16 | ~i:16}          (every word self-checking)
+// torn8 counts 8-byte halves whose two words came from different rounds,
+// tag_ahead those whose high word was the newer one, torn_word 32-bit words
+// whose two 16-bit halves disagree (the property the wire format needs).
+// H2D (atomicity_h2d_test): the host rewrites tagged words with 8-byte
+// stores for a fixed time, one GPU warp reads whole chunks with 16-byte loads.
 // ---------------------------------------------------------------------------
+
+KIWI_HD uint32_t mix16(uint32_t x) {
+    x &= 0xffffu;
+    return ((x * 40503u) ^ (x >> 7) ^ 0x5bd1u) & 0xffffu;
+}
+
+/// The 32-bit word of round i in mode m, and whether mode m is raw.
+KIWI_HD uint32_t atom_word(uint32_t mode, uint32_t i, bool high) {
+    switch (mode) {
+        case 0:
+        case 1: return high ? ~i : i;
+        case 3:
+        case 4: return high ? i : ~i;
+        case 2:
+        case 5: return tagged_word(i, i);
+        case 6:
+        case 7: return tagged_word(mix16(i), i);
+        default: return (i & 0xffffu) | ((~i & 0xffffu) << 16);
+    }
+}
+
+KIWI_HD bool atom_v4(uint32_t mode) { return mode == 0 || mode == 2 || mode == 3 || mode == 6 || mode == 8; }
 
 __global__ void atomicity_writer_kernel(Chunk* line, uint32_t iters, uint32_t mode, volatile uint32_t* done) {
     const uint32_t lane = ptx::lane_id();
+    const bool v4 = atom_v4(mode);
     for (uint32_t i = 1; i <= iters; ++i) {
         if (lane < 4) {
-            const uint32_t t = tagged_word(i, i);
-            switch (mode) {
-                case 0: ptx::st_volatile_v4(&line[lane], i, ~i, i, ~i); break;
-                case 1:
-                    ptx::st_volatile_u64(&line[lane].lo, static_cast<uint64_t>(i) | (static_cast<uint64_t>(~i) << 32));
-                    ptx::st_volatile_u64(&line[lane].hi, static_cast<uint64_t>(i) | (static_cast<uint64_t>(~i) << 32));
-                    break;
-                case 2: ptx::st_volatile_v4(&line[lane], t, t, t, t); break;
-                default:
-                    ptx::st_volatile_u64(&line[lane].lo, static_cast<uint64_t>(t) | (static_cast<uint64_t>(t) << 32));
-                    ptx::st_volatile_u64(&line[lane].hi, static_cast<uint64_t>(t) | (static_cast<uint64_t>(t) << 32));
-                    break;
+            const uint32_t lo = atom_word(mode, i, false), hi = atom_word(mode, i, true);
+            if (v4) {
+                ptx::st_volatile_v4(&line[lane], lo, hi, lo, hi);
+            } else {
+                const uint64_t h = static_cast<uint64_t>(lo) | (static_cast<uint64_t>(hi) << 32);
+                ptx::st_volatile_u64(&line[lane].lo, h);
+                ptx::st_volatile_u64(&line[lane].hi, h);
             }
         }
         __syncwarp();
@@ -621,28 +638,45 @@ __global__ void atomicity_writer_kernel(Chunk* line, uint32_t iters, uint32_t mo
 
 namespace {
 
-/// Classifies one 8-byte half read while the line was being rewritten.
-void classify_half(uint64_t h, bool tagged, AtomicityResult& r) {
-    const uint32_t w0 = static_cast<uint32_t>(h), w1 = static_cast<uint32_t>(h >> 32);
-    if (tagged) {
-        if ((w0 & 0xffffu) != (w0 >> 16)) ++r.torn_word;
-        if ((w1 & 0xffffu) != (w1 >> 16)) ++r.torn_word;
-        if (w0 != w1) {
-            ++r.torn8;
-            if (((w1 - w0) & 0xffffu) < 0x8000u) ++r.tag_ahead;
-        }
-        return;
+/// Round (low 16 bits for tagged modes, full for raw) carried by a word.
+uint32_t word_round(uint32_t mode, uint32_t w, bool high) {
+    switch (mode) {
+        case 0:
+        case 1: return high ? ~w : w;
+        case 3:
+        case 4: return high ? w : ~w;
+        case 8: return w & 0xffffu;
+        default: return w >> 16;
     }
-    const uint32_t round_hi = ~w1;
-    if (round_hi == w0) return;
+}
+
+bool word_torn(uint32_t mode, uint32_t w) {
+    switch (mode) {
+        case 2:
+        case 5: return (w & 0xffffu) != (w >> 16);
+        case 6:
+        case 7: return (w & 0xffffu) != mix16(w >> 16);
+        case 8: return ((w ^ (w >> 16)) & 0xffffu) != 0xffffu;
+        default: return false;  // raw words carry no redundancy
+    }
+}
+
+/// Classifies one 8-byte half read while the line was being rewritten.
+void classify_half(uint32_t mode, uint64_t h, AtomicityResult& r) {
+    const uint32_t w0 = static_cast<uint32_t>(h), w1 = static_cast<uint32_t>(h >> 32);
+    r.torn_word += word_torn(mode, w0) + word_torn(mode, w1);
+    const bool raw = mode <= 1 || mode == 3 || mode == 4;
+    const uint32_t r0 = word_round(mode, w0, false), r1 = word_round(mode, w1, true);
+    if (r0 == r1) return;
     ++r.torn8;
-    if (round_hi > w0) ++r.tag_ahead;
+    const bool high_newer = raw ? r1 > r0 : ((r1 - r0) & 0xffffu) < 0x8000u;
+    if (high_newer) ++r.tag_ahead;
 }
 
 }  // namespace
 
 AtomicityResult atomicity_test(uint32_t iters, uint32_t mode) {
-    if (mode > 3) throw kiwi::error("atomicity_test: mode 0..3");
+    if (mode > 8) throw kiwi::error("atomicity_test: mode 0..8");
     detail::Block mem(128, MemKind::kMappedPinned);
     PinnedFlag done;
     Chunk* line = mem.as<Chunk>();
@@ -651,24 +685,23 @@ AtomicityResult atomicity_test(uint32_t iters, uint32_t mode) {
     atomicity_writer_kernel<<<1, 32, 0, stream>>>(line, iters, mode, done.p);
     KIWI_CUDA_CHECK(cudaGetLastError());
     AtomicityResult r;
-    const bool tagged = mode >= 2;
     uint64_t idle = 0;
     while (!*done.p) {
         for (int c = 0; c < 4; ++c) {
             const uint64_t a = host::load_half(&line[c].lo);
             const uint64_t b = host::load_half(&line[c].hi);
             ++r.reads;
-            classify_half(a, tagged, r);
-            classify_half(b, tagged, r);
-            if (static_cast<uint32_t>(a) != static_cast<uint32_t>(b)) ++r.split16;
+            classify_half(mode, a, r);
+            classify_half(mode, b, r);
+            if (a != b) ++r.split16;
         }
         if ((++idle & 0xfffff) == 0 && cudaStreamQuery(stream) != cudaErrorNotReady) break;
     }
     KIWI_CUDA_CHECK(cudaStreamSynchronize(stream));
     cudaStreamDestroy(stream);
     const uint64_t last = host::load_half(&line[3].hi);
-    r.final_ok = tagged ? static_cast<uint32_t>(last) == tagged_word(iters, iters)
-                        : static_cast<uint32_t>(last) == iters;
+    r.final_ok = static_cast<uint32_t>(last) == atom_word(mode, iters, false) &&
+                 static_cast<uint32_t>(last >> 32) == atom_word(mode, iters, true);
     return r;
 }
 
@@ -688,7 +721,7 @@ __global__ void atomicity_reader_kernel(const Chunk* line, volatile uint32_t* do
             const uint4 v = ptx::ld_volatile_v4(&line[lane]);
             const uint32_t w[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
-            for (int j = 0; j < 4; ++j) torn_word += (w[j] & 0xffffu) != (w[j] >> 16);
+            for (int j = 0; j < 4; ++j) torn_word += (w[j] & 0xffffu) != mix16(w[j] >> 16);
             torn8 += (v.x != v.y) + (v.z != v.w);
             split16 += v.x != v.z;
         }
@@ -703,23 +736,26 @@ __global__ void atomicity_reader_kernel(const Chunk* line, volatile uint32_t* do
     }
 }
 
-AtomicityResult atomicity_h2d_test(uint32_t iters) {
+AtomicityResult atomicity_h2d_test(uint32_t duration_ms) {
     detail::Block mem(128, MemKind::kMappedPinned);
     PinnedFlag done;
     Chunk* line = mem.as<Chunk>();
     DevBuf<unsigned long long> counts(8);
     cudaStream_t stream;
     KIWI_CUDA_CHECK(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking));
+    const uint64_t timeout_ns = (static_cast<uint64_t>(duration_ms) + 10000) * 1000000ull;
     atomicity_reader_kernel<<<1, 32, 0, stream>>>(static_cast<const Chunk*>(device_address(line, MemKind::kMappedPinned)),
-                                                  done.p, counts.p, 4ull * iters + 1000000, 20000000000ull);
+                                                  done.p, counts.p, ~0ull, timeout_ns);
     KIWI_CUDA_CHECK(cudaGetLastError());
-    for (uint32_t i = 1; i <= iters; ++i) {
-        const uint64_t t = tagged_word(i, i);
+    const auto t_end = std::chrono::steady_clock::now() + std::chrono::milliseconds(duration_ms);
+    for (uint32_t i = 1;; ++i) {
+        const uint64_t t = tagged_word(mix16(i), i);
         const uint64_t h = t | (t << 32);
         for (int c = 0; c < 4; ++c) {
             host::store_half(&line[c].lo, h);
             host::store_half(&line[c].hi, h);
         }
+        if ((i & 1023) == 0 && std::chrono::steady_clock::now() > t_end) break;
     }
     std::atomic_thread_fence(std::memory_order_seq_cst);
     *done.p = 1;

@@ -60,8 +60,8 @@ struct AtomicityResult {
 /// thread classifies every 8-byte half it reads.
 AtomicityResult atomicity_test(uint32_t iters, uint32_t mode = 0);
 /// Host -> device direction: the host rewrites the line with tagged words
-/// (8-byte stores), one GPU warp reads it with 16-byte loads.
-AtomicityResult atomicity_h2d_test(uint32_t iters);
+/// (8-byte stores) for `duration_ms`, one GPU warp reads it with 16-byte loads.
+AtomicityResult atomicity_h2d_test(uint32_t duration_ms);
 
 struct ThroughputResult {
     uint64_t messages = 0;

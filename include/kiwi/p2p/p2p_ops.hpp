@@ -18,10 +18,10 @@ void launch_pingpong_ll8(const HeapView& h, int peer, bool initiator, uint32_t w
 
 void launch_put_bw(const HeapView& h, int peer, bool sender, uint64_t bytes, uint64_t reps, uint64_t src_off,
                    uint64_t dst_off, uint64_t flag_off, uint64_t round, uint64_t* elapsed, uint32_t* status,
-                   uint32_t max_blocks, uint64_t timeout_ns, cudaStream_t s);
+                   uint32_t max_blocks, uint64_t timeout_ns, cudaStream_t s, uint64_t region = 0);
 
 void launch_get(const HeapView& h, int peer, uint64_t bytes, uint64_t reps, uint64_t src_off, uint64_t dst_off,
-                uint64_t* lat_ns, uint32_t max_blocks, cudaStream_t s);
+                uint64_t* lat_ns, uint32_t max_blocks, cudaStream_t s, uint64_t region = 0);
 
 void launch_all_pairs(const HeapView& h, uint64_t data_off, uint64_t flag_off, uint64_t words, uint32_t round,
                       uint32_t* status, uint64_t timeout_ns, cudaStream_t s);

@@ -119,14 +119,14 @@ def test_pcie_floor_small():
     assert r["ok"], r
 
 
-@pytest.mark.parametrize("mode", [2, 3])
+@pytest.mark.parametrize("mode", [2, 5, 6, 7, 8])
 def test_platform_word_atomicity_of_gpu_stores_to_host(mode):
     """The wire format's hardware assumption (reference category:
     tests/queue/test_hardware_assumptions.hip.cpp): a 32-bit word of a GPU
-    16-byte (mode 2) or 8-byte (mode 3) store into mapped host memory is never
-    seen torn by the host.  (Whole 8-byte halves DO tear on these hosts; see
+    16-byte or 8-byte store into mapped host memory is never seen torn by the
+    host, for several data patterns (modes listed in csrc/queue_gpu.cu).  (Whole 8-byte halves DO tear on these hosts; see
     test_platform_8byte_tearing_is_recorded.)"""
-    r = _C().bench.atomicity_test(2_000_000, mode)
+    r = _C().bench.atomicity_test(1_000_000, mode)
     assert r["final_ok"], r
     assert r["reads"] > 1000, r
     assert r["torn_word"] == 0, r
@@ -135,7 +135,7 @@ def test_platform_word_atomicity_of_gpu_stores_to_host(mode):
 def test_platform_word_atomicity_of_host_stores_to_gpu():
     """Host -> device direction: a GPU 16-byte load of host memory never sees a
     tagged word torn."""
-    r = _C().bench.atomicity_h2d_test(2_000_000)
+    r = _C().bench.atomicity_h2d_test(1500)
     assert r["final_ok"], r
     assert r["reads"] > 1000, r
     assert r["torn_word"] == 0, r
