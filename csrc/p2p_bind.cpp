@@ -7,6 +7,7 @@
 #include <torch/extension.h>
 #include <unistd.h>
 
+#include "kiwi/p2p/collectives.cuh"
 #include "kiwi/p2p/context.hpp"
 #include "kiwi/p2p/heap.hpp"
 #include "kiwi/p2p/p2p_ops.hpp"
@@ -46,6 +47,26 @@ void register_p2p(py::module_& m) {
     p.def("broadcast_fd", &broadcast_fd, py::arg("job"), py::arg("rank"), py::arg("world"), py::arg("root"),
           py::arg("fd"), py::arg("timeout_s") = 60.0, py::call_guard<py::gil_scoped_release>());
     p.def("multicast_supported", &SymmetricHeap::multicast_supported);
+    p.def("coll_ingress_bytes", [](int world) { return coll_ingress_bytes(world); });
+    p.def("grid_barrier_test",
+          [](uint32_t blocks, uint32_t rounds, uint64_t timeout_ns) {
+              auto opts = torch::TensorOptions().device(torch::kCUDA, c10::cuda::current_device());
+              auto word = torch::zeros({1}, opts.dtype(torch::kInt64));
+              auto data = torch::zeros({static_cast<int64_t>(blocks)}, opts.dtype(torch::kInt32));
+              auto status = torch::zeros({2}, opts.dtype(torch::kInt32));
+              auto el = torch::zeros({1}, opts.dtype(torch::kInt64));
+              launch_grid_barrier_test(reinterpret_cast<unsigned long long*>(word.data_ptr<int64_t>()),
+                                       u32_ptr(data), blocks, rounds, u32_ptr(status), timeout_ns, u64_ptr(el),
+                                       cur_stream());
+              KIWI_CUDA_CHECK(cudaStreamSynchronize(cur_stream()));
+              py::dict d;
+              d["status"] = status[0].item<int32_t>();
+              d["info"] = status[1].item<int32_t>();
+              d["elapsed_ns"] = el[0].item<int64_t>();
+              d["word"] = word[0].item<int64_t>();
+              return d;
+          },
+          py::arg("blocks"), py::arg("rounds"), py::arg("timeout_ns") = 2000000000ull);
 
     py::class_<Context>(p, "Context")
         .def(py::init<SymmetricHeap&, size_t, uint64_t>(), py::arg("heap"), py::arg("num_queues") = 1,
@@ -121,6 +142,28 @@ void register_p2p(py::module_& m) {
              },
              py::arg("peer"), py::arg("bytes"), py::arg("reps"), py::arg("src_off"), py::arg("dst_off"),
              py::arg("lat"), py::arg("max_blocks"), py::arg("region") = 0)
+        .def("all2all_rounds",
+             [](SymmetricHeap& h, uint64_t ingress_off, std::optional<torch::Tensor> send,
+                std::optional<torch::Tensor> recv, torch::Tensor epoch, torch::Tensor status, uint64_t timeout_ns,
+                uint32_t rounds, std::optional<torch::Tensor> lat) {
+                 if (send.has_value() != recv.has_value()) throw kiwi::error("all2all_rounds: send and recv together");
+                 if (send && (send->numel() < h.world() || recv->numel() < static_cast<int64_t>(rounds) * h.world())) {
+                     throw kiwi::error("all2all_rounds: send needs world values, recv rounds x world");
+                 }
+                 if (lat && lat->numel() < static_cast<int64_t>(rounds)) throw kiwi::error("all2all_rounds: lat too small");
+                 if (ingress_off + coll_ingress_bytes(h.world()) > h.size()) throw kiwi::error("all2all_rounds: ingress outside the heap");
+                 launch_all2all_rounds(h.view(), ingress_off, send ? u32_ptr(*send) : nullptr,
+                                       recv ? u32_ptr(*recv) : nullptr, u32_ptr(epoch), u32_ptr(status), timeout_ns,
+                                       rounds, lat ? u64_ptr(*lat) : nullptr, cur_stream());
+             },
+             py::arg("ingress_off"), py::arg("send"), py::arg("recv"), py::arg("epoch"), py::arg("status"),
+             py::arg("timeout_ns"), py::arg("rounds") = 1, py::arg("lat") = py::none())
+        .def("coll_wait_only",
+             [](SymmetricHeap& h, uint64_t ingress_off, uint32_t epoch, int src, torch::Tensor status,
+                uint64_t timeout_ns, torch::Tensor waited) {
+                 launch_coll_wait_only(h.view(), ingress_off, epoch, src, u32_ptr(status), timeout_ns, u64_ptr(waited),
+                                       cur_stream());
+             })
         .def("all_pairs",
              [](SymmetricHeap& h, uint64_t data_off, uint64_t flag_off, uint64_t words, uint32_t round,
                 torch::Tensor status, uint64_t timeout_ns) {

@@ -41,4 +41,20 @@ void launch_ce_put_selftest(const GContext& ctx, int dst, uint64_t src_off, uint
                             uint32_t n, uint64_t flag_off, uint64_t counter_off, uint32_t* status,
                             uint64_t timeout_ns, cudaStream_t s);
 
+// ---- device collectives (include/kiwi/p2p/collectives.cuh) ----
+
+/// `rounds` all-to-all rounds of one u32 per rank pair (send == nullptr: barrier
+/// rounds).  recv gets rounds x world values; lat_ns (optional) per-round time.
+void launch_all2all_rounds(const HeapView& h, uint64_t ingress_off, const uint32_t* send, uint32_t* recv,
+                           uint32_t* epoch_ctr, uint32_t* status, uint64_t timeout_ns, uint32_t rounds,
+                           uint64_t* lat_ns, cudaStream_t s);
+
+/// Waits (bounded) for a value nobody sends; records kTimeout in status.
+void launch_coll_wait_only(const HeapView& h, uint64_t ingress_off, uint32_t epoch, int src, uint32_t* status,
+                           uint64_t timeout_ns, uint64_t* waited_ns, cudaStream_t s);
+
+/// Cooperative launch of the grid-barrier self test.
+void launch_grid_barrier_test(unsigned long long* word, uint32_t* data, uint32_t blocks, uint32_t rounds,
+                              uint32_t* status, uint64_t timeout_ns, uint64_t* elapsed_ns, cudaStream_t s);
+
 }  // namespace kiwi::p2p

@@ -119,6 +119,12 @@ KIWI_DEV uint32_t ld_acquire_gpu_u32(const void* p) {
     return v;
 }
 
+KIWI_DEV uint64_t ld_acquire_gpu_u64(const void* p) {
+    uint64_t v;
+    asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+
 KIWI_DEV uint64_t ld_relaxed_sys_u64(const void* p) {
     uint64_t v;
     asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");

@@ -85,6 +85,21 @@ def _ep_layer(rank, world, quant):
         assert err <= rel * ref.abs().max().item() + 1e-3, (rank, step, err)
 
 
+def _collectives(rank, world):
+    from kiwi_b200.parallel.collectives import DeviceCollectives
+
+    coll = DeviceCollectives(timeout_s=5.0)
+    send = torch.tensor([rank * 100 + d for d in range(world)], dtype=torch.int32, device="cuda")
+    for call in range(3):
+        out = coll.all2all(send, rounds=64)
+        coll.barrier(rounds=16)
+        torch.cuda.synchronize()
+        coll.check()
+        expect = torch.tensor([[s * 100 + rank + r for s in range(world)] for r in range(64)], dtype=torch.int32)
+        assert torch.equal(out.cpu(), expect), (rank, call)
+    assert int(coll.epoch.item()) == 3 * 80
+
+
 def _nvls(rank, world):
     import kiwi_b200
     from kiwi_b200.parallel.p2p import SymmetricHeap
@@ -125,6 +140,16 @@ def test_ep_layer_world4():
     if _ngpu() < 4:
         pytest.skip("needs 4 GPUs")
     _run(_ep_layer, 4, "fp8")
+
+
+def test_device_collectives_2():
+    _run(_collectives, 2)
+
+
+def test_device_collectives_4():
+    if _ngpu() < 4:
+        pytest.skip("needs 4 GPUs")
+    _run(_collectives, 4)
 
 
 def test_nvls_allreduce_2():
