@@ -449,9 +449,26 @@ PYBIND11_MODULE(_C, m) {
         d["tag_ahead"] = r.tag_ahead;
         d["split16"] = r.split16;
         d["torn_word"] = r.torn_word;
+        d["torn_nonzero"] = r.torn_nonzero;
         d["final_ok"] = r.final_ok;
+        d["samples"] = r.samples;
         return d;
     }, py::arg("iters"), py::arg("mode") = 0);
+    b.def("atomicity_protocol_test", [](uint32_t iters, uint32_t format) {
+        bench::ProtocolResult r;
+        {
+            py::gil_scoped_release nogil;
+            r = bench::atomicity_protocol_test(iters, format);
+        }
+        py::dict d;
+        d["rounds"] = r.rounds;
+        d["reads"] = r.reads;
+        d["torn"] = r.torn;
+        d["accepted_bad"] = r.accepted_bad;
+        d["ok"] = r.ok;
+        d["samples"] = r.samples;
+        return d;
+    }, py::arg("iters"), py::arg("format") = 0);
     b.def("atomicity_h2d_test", [](uint32_t duration_ms) {
         bench::AtomicityResult r;
         {
@@ -463,7 +480,9 @@ PYBIND11_MODULE(_C, m) {
         d["torn8"] = r.torn8;
         d["split16"] = r.split16;
         d["torn_word"] = r.torn_word;
+        d["torn_nonzero"] = r.torn_nonzero;
         d["final_ok"] = r.final_ok;
+        d["samples"] = r.samples;
         return d;
     }, py::arg("duration_ms"));
     b.def("invoke_throughput",

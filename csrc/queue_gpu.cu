@@ -664,9 +664,18 @@ bool word_torn(uint32_t mode, uint32_t w) {
 /// Classifies one 8-byte half read while the line was being rewritten.
 void classify_half(uint32_t mode, uint64_t h, AtomicityResult& r) {
     const uint32_t w0 = static_cast<uint32_t>(h), w1 = static_cast<uint32_t>(h >> 32);
+    const bool bad_word = word_torn(mode, w0) || word_torn(mode, w1);
     r.torn_word += word_torn(mode, w0) + word_torn(mode, w1);
     const bool raw = mode <= 1 || mode == 3 || mode == 4;
     const uint32_t r0 = word_round(mode, w0, false), r1 = word_round(mode, w1, true);
+    if ((r0 != r1 || bad_word) && r.samples.size() < 64) r.samples.push_back(h);
+    // The wire format's assumption: a word being rewritten reads as its old
+    // value, its new value or zero.  Count reads that it does not explain.
+    if (raw) {
+        if (r0 != r1 && w0 != 0 && w1 != 0) ++r.torn_nonzero;
+    } else {
+        r.torn_nonzero += (word_torn(mode, w0) && w0 != 0) + (word_torn(mode, w1) && w1 != 0);
+    }
     if (r0 == r1) return;
     ++r.torn8;
     const bool high_newer = raw ? r1 > r0 : ((r1 - r0) & 0xffffu) < 0x8000u;
@@ -705,6 +714,93 @@ AtomicityResult atomicity_test(uint32_t iters, uint32_t mode) {
     return r;
 }
 
+// Protocol-level check, as a ring reader sees it: the GPU writes round i
+// (i = 1, 2, ...) into one line and waits (bounded) for the host to
+// acknowledge it before writing round i+1; the host polls for round i and, in
+// every 8-byte half whose tags read as round i, checks the data.  format 0 is
+// the wire format (16-bit tag in every word), format 1 a {data32, tag32} half.
+// accepted_bad must stay 0; torn counts halves that were neither round.
+
+KIWI_HD uint32_t proto_data(uint32_t i, uint32_t half) { return (i * 2654435761u) ^ (half * 0x9e3779b9u) ^ 0xa5a5a5a5u; }
+
+KIWI_HD uint64_t proto_half(uint32_t format, uint32_t i, uint32_t half) {
+    const uint32_t d = proto_data(i, half);
+    return format == 0 ? pack_half(d, i) : (static_cast<uint64_t>(d) | (static_cast<uint64_t>(i) << 32));
+}
+
+__global__ void protocol_writer_kernel(Chunk* line, const volatile uint32_t* ack, uint32_t iters, uint32_t format,
+                                       uint32_t* status, uint64_t timeout_ns) {
+    const uint32_t lane = ptx::lane_id();
+    for (uint32_t i = 1; i <= iters; ++i) {
+        if (lane < 4) {
+            const uint64_t a = proto_half(format, i, 2 * lane), b = proto_half(format, i, 2 * lane + 1);
+            ptx::st_volatile_v4(&line[lane], static_cast<uint32_t>(a), static_cast<uint32_t>(a >> 32),
+                                static_cast<uint32_t>(b), static_cast<uint32_t>(b >> 32));
+        }
+        __syncwarp();
+        if (lane == 0) {
+            ptx::Deadline dl(timeout_ns);
+            while (*ack != i) {
+                if (dl.expired()) {
+                    status[0] = 1;
+                    break;
+                }
+            }
+        }
+        if (__shfl_sync(ptx::kFullMask, lane == 0 ? status[0] : 0u, 0)) return;
+    }
+}
+
+ProtocolResult atomicity_protocol_test(uint32_t iters, uint32_t format) {
+    detail::Block mem(128, MemKind::kMappedPinned);
+    PinnedFlag ack;
+    DevBuf<uint32_t> status(2);
+    Chunk* line = mem.as<Chunk>();
+    cudaStream_t stream;
+    KIWI_CUDA_CHECK(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking));
+    protocol_writer_kernel<<<1, 32, 0, stream>>>(line, ack.p, iters, format, status.p, 2000000000ull);
+    KIWI_CUDA_CHECK(cudaGetLastError());
+    ProtocolResult r;
+    const auto tag_of = [&](uint64_t h, uint32_t i) {
+        return format == 0 ? half_has_tag(h, i) : static_cast<uint32_t>(h >> 32) == i;
+    };
+    const auto data_of = [&](uint64_t h) { return format == 0 ? half_data(h) : static_cast<uint32_t>(h); };
+    const auto give_up = std::chrono::steady_clock::now() + std::chrono::seconds(60);
+    for (uint32_t i = 1; i <= iters; ++i) {
+        uint32_t seen = 0;  // halves already accepted this round (bit mask)
+        uint64_t spins = 0;
+        while (seen != 0xffu) {
+            for (uint32_t c = 0; c < 4; ++c) {
+                for (uint32_t k = 0; k < 2; ++k) {
+                    const uint32_t half = 2 * c + k;
+                    if (seen & (1u << half)) continue;
+                    const uint64_t h = host::load_half(k ? &line[c].hi : &line[c].lo);
+                    ++r.reads;
+                    if (tag_of(h, i)) {
+                        seen |= 1u << half;
+                        if (data_of(h) != proto_data(i, half)) {
+                            ++r.accepted_bad;
+                            if (r.samples.size() < 32) r.samples.push_back(h);
+                        }
+                    } else if (h != proto_half(format, i - 1, half) && !(i == 1 && h == 0)) {
+                        ++r.torn;
+                    }
+                }
+            }
+            if ((++spins & 0xffff) == 0 && std::chrono::steady_clock::now() > give_up) break;
+        }
+        if (seen != 0xffu) break;
+        ++r.rounds;
+        *ack.p = i;
+    }
+    KIWI_CUDA_CHECK(cudaStreamSynchronize(stream));
+    uint32_t st[2];
+    KIWI_CUDA_CHECK(cudaMemcpy(st, status.p, sizeof(st), cudaMemcpyDeviceToHost));
+    cudaStreamDestroy(stream);
+    r.ok = st[0] == 0 && r.rounds == iters;
+    return r;
+}
+
 __global__ void atomicity_reader_kernel(const Chunk* line, volatile uint32_t* done, unsigned long long* counts,
                                         uint64_t max_reads, uint64_t timeout_ns) {
     const uint32_t lane = ptx::lane_id();
@@ -721,7 +817,14 @@ __global__ void atomicity_reader_kernel(const Chunk* line, volatile uint32_t* do
             const uint4 v = ptx::ld_volatile_v4(&line[lane]);
             const uint32_t w[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
-            for (int j = 0; j < 4; ++j) torn_word += (w[j] & 0xffffu) != mix16(w[j] >> 16);
+            for (int j = 0; j < 4; ++j) {
+                if ((w[j] & 0xffffu) != mix16(w[j] >> 16)) {
+                    const unsigned long long k = atomicAdd(&counts[5], 1ull);
+                    if (k < 32) counts[8 + k] = w[j];
+                    if (w[j] != 0) atomicAdd(&counts[6], 1ull);
+                    ++torn_word;
+                }
+            }
             torn8 += (v.x != v.y) + (v.z != v.w);
             split16 += v.x != v.z;
         }
@@ -740,7 +843,7 @@ AtomicityResult atomicity_h2d_test(uint32_t duration_ms) {
     detail::Block mem(128, MemKind::kMappedPinned);
     PinnedFlag done;
     Chunk* line = mem.as<Chunk>();
-    DevBuf<unsigned long long> counts(8);
+    DevBuf<unsigned long long> counts(40);
     cudaStream_t stream;
     KIWI_CUDA_CHECK(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking));
     const uint64_t timeout_ns = (static_cast<uint64_t>(duration_ms) + 10000) * 1000000ull;
@@ -761,11 +864,13 @@ AtomicityResult atomicity_h2d_test(uint32_t duration_ms) {
     *done.p = 1;
     KIWI_CUDA_CHECK(cudaStreamSynchronize(stream));
     cudaStreamDestroy(stream);
-    unsigned long long c[8];
+    unsigned long long c[40];
     KIWI_CUDA_CHECK(cudaMemcpy(c, counts.p, sizeof(c), cudaMemcpyDeviceToHost));
     AtomicityResult r;
+    for (unsigned long long k = 0; k < c[5] && k < 32; ++k) r.samples.push_back(c[8 + k]);
     r.reads = c[0] / 4;
     r.torn_word = c[1];
+    r.torn_nonzero = c[6];
     r.torn8 = c[2];
     r.split16 = c[3];
     r.final_ok = c[4] == 0;

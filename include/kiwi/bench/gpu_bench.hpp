@@ -53,12 +53,27 @@ struct AtomicityResult {
     uint64_t torn8 = 0;    // 8-byte halves whose two words came from different rounds
     uint64_t tag_ahead = 0;  // of those, halves whose tag word was newer than the data word
     uint64_t split16 = 0;  // chunks whose two halves came from different rounds (allowed)
-    uint64_t torn_word = 0;  // tagged 32-bit words whose 16-bit halves disagree (must stay 0)
+    uint64_t torn_word = 0;  // 32-bit words whose 16-bit halves disagree (self-checking modes)
+    uint64_t torn_nonzero = 0;  // reads that are neither old, new nor zero per word (must be 0)
     bool final_ok = false;
+    std::vector<uint64_t> samples;  // the first torn 8-byte halves (H2D: torn words) as read
 };
 /// GPU rewrites one host line (mode 0: 16-byte stores, 1: 8-byte stores); a host
 /// thread classifies every 8-byte half it reads.
 AtomicityResult atomicity_test(uint32_t iters, uint32_t mode = 0);
+struct ProtocolResult {
+    uint64_t rounds = 0;
+    uint64_t reads = 0;
+    uint64_t torn = 0;          // halves that were neither the old nor the new round
+    uint64_t accepted_bad = 0;  // halves with the expected tag but wrong data (must be 0)
+    bool ok = false;
+    std::vector<uint64_t> samples;
+};
+
+/// Ring-reader view of the wire format (format 0) or a {data32, tag32} half
+/// (format 1): GPU writes round i, the host waits for it and acknowledges.
+ProtocolResult atomicity_protocol_test(uint32_t iters, uint32_t format);
+
 /// Host -> device direction: the host rewrites the line with tagged words
 /// (8-byte stores) for `duration_ms`, one GPU warp reads it with 16-byte loads.
 AtomicityResult atomicity_h2d_test(uint32_t duration_ms);

@@ -538,7 +538,7 @@ struct MpmcH2DHandle {
         pos = ptx::bcast64(pos);
         const uint64_t slot = pos & ((uint64_t{1} << log2slots) - 1);
         const uint32_t lap = static_cast<uint32_t>(pos >> log2slots);
-        const uint32_t tag = lap + 1;
+        const uint32_t tag = wire_tag(lap);
         const uint32_t total = slot_lines * kChunksPerLine;
         uint4 v = make_uint4(0, 0, 0, 0);
         bool ok = true;

@@ -14,9 +14,9 @@
 // each wait's outcome (see adapt()).
 //
 // Each mirror holds one 16-byte chunk in the rings' wire format: the 8-byte
-// value in four tagged words whose tags are the low 16 bits of the sequence
-// number; a reply is valid when all four carry it (4-byte single-copy
-// atomicity only, as the rings).  One outstanding request per
+// value in four tagged words whose tags are wire_tag(seq); a reply is valid
+// when all four carry it (the rings' assumption: a word being rewritten reads
+// as old, new or zero).  One outstanding request per
 // mailbox: the host must not post reply n+1 before the device consumed reply
 // n, which call/return use guarantees.
 #pragma once
@@ -84,6 +84,7 @@ struct MailboxHandle {
     /// One thread: waits for reply `seq` and returns its 8-byte value.
     /// Returns kTimeout (recorded in the ErrorRecord) if it does not arrive.
     KIWI_DEV Status wait_thread(uint32_t seq, uint64_t& value, uint64_t timeout_ns) const {
+        const uint32_t tag = wire_tag(seq);
         const Chunk* m0 = mirror(0);
         const Chunk* m1 = mirror(1);
         spin_ns(initial_delay_ns);
@@ -92,7 +93,7 @@ struct MailboxHandle {
             bool first = true;
             while (true) {
                 const uint4 a = ptx::ld_volatile_v4(first ? m0 : m1);
-                if (words_have_tag(a.x, a.y, a.z, a.w, seq)) {
+                if (words_have_tag(a.x, a.y, a.z, a.w, tag)) {
                     value = chunk_value(a);
                     if (adaptive) adapt(first);
                     return Status::kOk;
@@ -105,12 +106,12 @@ struct MailboxHandle {
         spin_ns(stagger_ns);
         uint4 b = ptx::ld_volatile_v4(m1);
         while (true) {
-            if (words_have_tag(a.x, a.y, a.z, a.w, seq)) {
+            if (words_have_tag(a.x, a.y, a.z, a.w, tag)) {
                 value = chunk_value(a);
                 return Status::kOk;
             }
             a = ptx::ld_volatile_v4(m0);
-            if (words_have_tag(b.x, b.y, b.z, b.w, seq)) {
+            if (words_have_tag(b.x, b.y, b.z, b.w, tag)) {
                 value = chunk_value(b);
                 return Status::kOk;
             }
@@ -148,8 +149,8 @@ public:
 
     /// Publishes reply `seq` (seq != 0) carrying `value` to every mirror.
     void post(uint32_t seq, uint64_t value) {
-        const uint64_t lo = pack_half(static_cast<uint32_t>(value), seq);
-        const uint64_t hi = pack_half(static_cast<uint32_t>(value >> 32), seq);
+        const uint64_t lo = pack_half(static_cast<uint32_t>(value), wire_tag(seq));
+        const uint64_t hi = pack_half(static_cast<uint32_t>(value >> 32), wire_tag(seq));
         for (uint32_t m = 0; m < kMailboxMirrors; ++m) {
             Chunk* c = chunk(m);
             host::store_half(&c->lo, lo);
@@ -177,7 +178,7 @@ public:
     bool peek(uint32_t m, uint32_t seq, uint64_t* value) const {
         const Chunk* c = chunk(m);
         const uint64_t lo = host::load_half(&c->lo), hi = host::load_half(&c->hi);
-        if (!half_has_tag(lo, seq) || !half_has_tag(hi, seq)) return false;
+        if (!half_has_tag(lo, wire_tag(seq)) || !half_has_tag(hi, wire_tag(seq))) return false;
         *value = (static_cast<uint64_t>(half_data(hi)) << 32) | half_data(lo);
         return true;
     }

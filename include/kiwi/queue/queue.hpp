@@ -231,7 +231,7 @@ public:
             if (acked != lap) return false;
             if (__atomic_compare_exchange_n(&head_, &pos, pos + 1, false, __ATOMIC_ACQ_REL,
                                             __ATOMIC_RELAXED)) {
-                write_slot(slot, lap + 1, payload, bytes, metadata);
+                write_slot(slot, wire_tag(lap), payload, bytes, metadata);
                 return true;
             }
         }

@@ -16,12 +16,13 @@
 //           (data in the low half of the word, the tag in the high half), so a
 //           chunk carries 8 payload bytes, the same 50% as data+tag halves.
 //
-//   * A tag is the low 16 bits of the lap tag of the chunk's line:
-//         lap_tag(line) = (line >> log2(capacity)) + 1
+//   * A tag is the 16-bit wire tag of the chunk's lap:
+//         lap_tag(line) = wire_tag(line >> log2(capacity))
+//         wire_tag(n)   = n % 65535 + 1            (1 .. 65535, never 0)
 //     A freshly allocated ring is all zeros (tag 0 = never written), so no
 //     initialisation pass is needed.  The producer is never more than one lap
 //     ahead of the consumer (credit), so the only stale tag a reader can meet
-//     is the previous lap's, which differs in its low 16 bits.
+//     is the previous lap's, which differs from the expected one.
 //   * The message header is in-band: chunk 0's data is {metadata, length}.
 //     Payload byte b lives in chunk 1 + b/8.
 //   * A message of B bytes occupies message_lines(B) whole lines starting on a
@@ -31,8 +32,13 @@
 //   * A message that reaches the end of the ring continues at line 0 with the
 //     next lap's tag.
 //
-// A reader that sees the expected tag in a word sees that word's data: only
-// 4-byte single-copy atomicity is assumed.
+// Measured on B200 hosts (the atomicity tests of the bench module): while a
+// kernel rewrote one line back to back, host 8-byte loads sometimes returned
+// ZERO for a half (never a mix of the old and new values), and a host reading
+// a line that a kernel writes once per round (the ring pattern) saw only the
+// old or the new value.  So the format assumes that a 4-byte word being
+// rewritten reads as its old value, its new value or zero; since no tag is 0,
+// a reader that sees the expected tag in a word sees that word's data.
 #pragma once
 
 #include "kiwi/common.hpp"
@@ -70,8 +76,12 @@ KIWI_HD constexpr uint32_t message_lines(uint32_t bytes) {
 
 inline constexpr uint32_t kMaxMessageLines = message_lines(kMaxMessageBytes);
 
+/// 16-bit tag of round `n` (a lap or a reply sequence number): 1 .. 65535,
+/// so consecutive rounds differ and a zeroed word never matches.
+KIWI_HD constexpr uint32_t wire_tag(uint64_t n) { return static_cast<uint32_t>(n % 65535u) + 1u; }
+
 KIWI_HD constexpr uint32_t lap_tag(uint64_t line, uint32_t log2_capacity) {
-    return static_cast<uint32_t>(line >> log2_capacity) + 1u;
+    return wire_tag(line >> log2_capacity);
 }
 
 /// One tagged word: 16 data bits (the low half of `data16`) and the low 16

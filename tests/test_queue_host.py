@@ -24,6 +24,20 @@ def test_wire_constants():
     assert kq.message_lines(25) == 2 and kq.message_lines(56) == 2
     assert kq.message_lines(4096) == 129
     assert kq.lap_tag(0, 16) == 1 and kq.lap_tag(15, 16) == 1 and kq.lap_tag(16, 16) == 2
+    # 16-bit wire tags cycle through 1..65535: never 0 (a zeroed word never matches)
+    assert kq.lap_tag(65534 * 16, 16) == 65535 and kq.lap_tag(65535 * 16, 16) == 1
+
+
+def test_tag_cycle_wraps_in_a_tiny_ring():
+    """More than 65535 laps through a one-line ring: every lap's tag differs
+    from the previous lap's, across the 65535 -> 1 wrap."""
+    q = kq.SPSCD2HQueue(1, host_only=True)
+    w = q.host_writer()
+    for i in range(140_000):
+        payload = struct.pack("<Q", i * 0x9E3779B97F4A7C15 % (1 << 64))
+        assert w.try_push(payload, i & 0xFFFF)
+        assert q.try_pop() == (payload, i & 0xFFFF)
+        assert q.try_pop() is None
 
 
 @pytest.mark.parametrize("cap", [0, 3, 6, 100])
