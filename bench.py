@@ -33,7 +33,8 @@ import torch  # noqa: E402
 
 METRIC = "p50 GPU→CPU→GPU invoke µs; EP dispatch+combine µs & tokens/s at 1/2/4/8 B200"
 BASELINE_INVOKE_P50_US = 1.92   # published reference number (MI300X)
-KERNELS_PER_STEP = 12           # route, begin, dispatch, recv_count, 2 schedules, recv assign+copy, 2 GEMMs, combine x2
+# route, begin, dispatch, recv_count, 2 schedules, recv assign+copy, GEMM1, GEMM2 (+ combine send, unfused), combine recv
+KERNELS_PER_STEP = {True: 11, False: 12}
 
 
 def parse():
@@ -47,6 +48,8 @@ def parse():
     ap.add_argument("--latency-tokens", type=int, default=128)
     ap.add_argument("--invoke-iters", type=int, default=200000)
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--unfused-combine", action="store_true",
+                    help="GEMM2 to local memory + combine send/receive kernels (comparison only)")
     return ap.parse_args()
 
 
@@ -87,6 +90,7 @@ def main():
         from kiwi_b200.parallel.ep import ExpertParallelMoE
 
         layer = ExpertParallelMoE(cfg, max_tokens=max(T, args.latency_tokens))
+        layer.native.fused_combine = not args.unfused_combine
     else:
         from kiwi_b200.parallel.baseline import NcclMoEBaseline
 
@@ -203,7 +207,8 @@ def main():
             "tflops_per_gpu": flops / (ms / 1e3) / 1e12,
             "clocks": {"sm_mhz": clk["sm_mhz"], "sm_max_mhz": clk["sm_max_mhz"], "reasons": clk["reasons"],
                        "samples": clk["samples"]},
-            "e2e": e2e, "gpu_launches": KERNELS_PER_STEP * args.steps if args.impl == "kiwi" else None,
+            "e2e": e2e, "gpu_launches": KERNELS_PER_STEP[not args.unfused_combine] * args.steps if args.impl == "kiwi" else None,
+            "fused_combine": (not args.unfused_combine) if args.impl == "kiwi" else None,
             "latency_mode": lat, "invoke_rtt": invoke, "impl": args.impl,
         }
         emit(line)

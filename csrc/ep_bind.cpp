@@ -97,6 +97,7 @@ public:
         tiles2_ = torch::zeros({el + 1}, i32);
         slot_tokens_ = torch::zeros({ep::kMaxTopk}, i32);
         pair_slot_ = torch::zeros({pairs}, i32);
+        pair_dst_ = torch::full({pairs}, -1, torch::TensorOptions().dtype(torch::kInt64).device(dev));
         pair_w_ = torch::zeros({pairs}, f32);
         slot_pos_ = torch::full({static_cast<int64_t>(cfg_.slots()) * cfg_.local_per_token()}, -1, i32);
         a_ = torch::zeros({pairs, cfg_.hidden}, bf);
@@ -114,6 +115,7 @@ public:
         ws_.tiles2 = tiles2_.data_ptr<int32_t>();
         ws_.slot_tokens = slot_tokens_.data_ptr<int32_t>();
         ws_.pair_slot = pair_slot_.data_ptr<int32_t>();
+        ws_.pair_dst = pair_dst_.data_ptr<int64_t>();
         ws_.pair_w = pair_w_.data_ptr<float>();
         ws_.slot_pos = slot_pos_.data_ptr<int32_t>();
         ws_.a = reinterpret_cast<__nv_bfloat16*>(a_.data_ptr());
@@ -125,10 +127,10 @@ public:
         tmap_a2_ = gemm::make_tmap_bf16_2d(h_.data_ptr(), pairs, ffn, 128);
         tmap_b2_ = gemm::make_tmap_bf16_2d(w2.data_ptr(), w2.size(0), ffn, 256);
         tmap_b2h_ = gemm::make_tmap_bf16_2d(w2.data_ptr(), w2.size(0), ffn, 128);
-        // 2-SM tiles (256 rows) pay off once an expert expects >= 256 rows per round.
-        const int64_t expected_rows =
-            static_cast<int64_t>(cfg_.world) * cfg_.max_tokens * cfg_.topk / std::max(cfg_.num_experts, 1);
-        pair_ = expected_rows >= 256;
+        // The 2-SM (256-row tile) GEMM measured no faster than the 1-SM kernel
+        // at the EP shapes (1.39 vs 1.35 ms GEMM1, 0.76 vs 0.75 ms GEMM2 at
+        // 1024 rows per expert), so it is opt-in (gemm_pair).
+        pair_ = false;
     }
 
     // ---- stages (all on the current stream) ----
@@ -179,14 +181,33 @@ public:
         g2.c = reinterpret_cast<__nv_bfloat16*>(y_.data_ptr());
         g2.ldc = cfg_.hidden;
         g2.row_scale = ws_.pair_w;
-        if (pair_) gemm::grouped_gemm_pair(tmap_a2_, tmap_b2h_, g2, /*swiglu=*/false, 0, s);
-        else gemm::grouped_gemm(tmap_a2_, tmap_b2_, g2, /*swiglu=*/false, 0, s);
+        if (fused_) {
+            // Fused combine: the epilogue stores every weighted row straight into
+            // its token owner's combk slot over NVLink and the last CTA signals.
+            gemm::ScatterArgs sc{};
+            for (int r = 0; r < cfg_.world; ++r) sc.base[r] = heap_.view().base[r];
+            sc.row_dst = ws_.pair_dst;
+            sc.done_ctas = ws_.done_ctas + 2;
+            sc.epoch = ws_.epoch;
+            sc.flag_off = cfg_.combine_flag(cfg_.rank);
+            sc.world = cfg_.world;
+            gemm::grouped_gemm_scatter(tmap_a2_, tmap_b2_, g2, sc, 0, s);
+        } else if (pair_) {
+            gemm::grouped_gemm_pair(tmap_a2_, tmap_b2h_, g2, /*swiglu=*/false, 0, s);
+        } else {
+            gemm::grouped_gemm(tmap_a2_, tmap_b2_, g2, /*swiglu=*/false, 0, s);
+        }
     }
 
     void combine(torch::Tensor idx, torch::Tensor out) {
         cudaStream_t s = cur_stream();
         TORCH_CHECK(out.scalar_type() == torch::kBFloat16 && out.is_contiguous() && out.size(1) == cfg_.hidden,
                     "out must be contiguous bf16 [T, hidden]");
+        if (fused_) {
+            ep::launch_combine_recv_fused(cfg_, heap_.view(), idx.data_ptr<int32_t>(), static_cast<int>(out.size(0)),
+                                          reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), ws_, timeout_ns_, s);
+            return;
+        }
         ep::launch_combine_send(cfg_, heap_.view(), reinterpret_cast<const __nv_bfloat16*>(y_.data_ptr()), ws_, 0, s);
         ep::launch_combine_recv(cfg_, heap_.view(), idx.data_ptr<int32_t>(), static_cast<int>(out.size(0)),
                                 reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), ws_, timeout_ns_, s);
@@ -239,14 +260,17 @@ private:
     torch::Tensor w13_, w2_;
     uint64_t timeout_ns_;
     torch::Tensor epoch_, done_, counts_, cursor_, offsets_, tiles1_, tiles2_, slot_tokens_, pair_slot_, pair_w_,
-        slot_pos_, a_, h_, y_, error_, gemm_error_;
+        slot_pos_, a_, h_, y_, error_, gemm_error_, pair_dst_;
     ep::EpWorkspace ws_{};
     CUtensorMap tmap_a1_, tmap_b1_, tmap_a2_, tmap_b2_, tmap_b1h_, tmap_b2h_;
     bool pair_ = false;
+    bool fused_ = true;
 
 public:
     bool pair() const { return pair_; }
     void set_pair(bool v) { pair_ = v; }
+    bool fused() const { return fused_; }
+    void set_fused(bool v) { fused_ = v; }
 };
 
 
@@ -379,5 +403,8 @@ void register_ep(py::module_& m) {
         .def_property_readonly("expert_output", &MoeLayer::expert_output)
         .def_property_readonly("epoch", &MoeLayer::epoch)
         .def_property("gemm_pair", &MoeLayer::pair, &MoeLayer::set_pair,
-                      "Use the 2-SM (256-row tile) grouped GEMM; the default follows the expected rows per expert.");
+                      "Use the 2-SM (256-row tile) grouped GEMM (unfused combine only; off by default).")
+        .def_property("fused_combine", &MoeLayer::fused, &MoeLayer::set_fused,
+                      "GEMM2 epilogue stores rows over NVLink into the token owners' top-k slots (default); "
+                      "False: GEMM2 to local memory, then combine send + receive kernels.");
 }

@@ -437,6 +437,9 @@ __global__ void __launch_bounds__(kThreads) recv_assign_kernel(EpConfig c, p2p::
             if (pos < max_pairs) {
                 ws.pair_slot[pos] = static_cast<int32_t>(s);
                 ws.pair_w[pos] = wt;
+                if (ws.pair_dst) {
+                    ws.pair_dst[pos] = (static_cast<int64_t>(src) << 48) | static_cast<int64_t>(c.combk_off(t, lane));
+                }
             } else {
                 set_error(ws, static_cast<uint32_t>(Status::kBadArgument), kSiteCapacity, pos, c.rank);
                 pos = -1;
@@ -588,6 +591,44 @@ __global__ void __launch_bounds__(kThreads) combine_recv_kernel(EpConfig c, p2p:
         ptx::st_v4(out + static_cast<int64_t>(t) * c.hidden + col, f32x8_to_bf16(acc));
     }
 }
+
+/// Fused combine, receive side: (token, 256-column block) items sum the
+/// token's top-k combk rows (each written by the rank owning that expert).
+template <int MAXK>
+__global__ void __launch_bounds__(kThreads) combine_recv_fused_kernel(EpConfig c, p2p::HeapView h, const int32_t* idx,
+                                                                      int tokens, __nv_bfloat16* out, EpWorkspace ws,
+                                                                      uint64_t timeout_ns) {
+    const int lane = threadIdx.x & 31;
+    const int warps = gridDim.x * (blockDim.x / 32);
+    const uint32_t epoch = *reinterpret_cast<volatile uint32_t*>(ws.epoch);
+    if (!wait_all_flags(c, h, ws, epoch, [&](int src) { return c.combine_flag(src); }, kSiteCombineWait, timeout_ns,
+                        nullptr)) {
+        return;
+    }
+    const uint8_t* base = h.base[h.rank];
+    const int blocks = c.hidden / 256;
+    const uint64_t items = static_cast<uint64_t>(tokens) * blocks;
+    for (uint64_t it = (blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x) / 32; it < items; it += warps) {
+        const int t = static_cast<int>(it / blocks);
+        const int col = static_cast<int>(it % blocks) * 256 + lane * 8;
+        const int e = lane < c.topk ? idx[static_cast<int64_t>(t) * c.topk + lane] : -1;
+        uint32_t m = __ballot_sync(0xffffffffu, e >= 0 && e < c.num_experts);
+        int kl[MAXK];
+        int nk = 0;
+#pragma unroll
+        for (int j = 0; j < MAXK; ++j) {
+            kl[j] = m ? __ffs(m) - 1 : 0;
+            if (m) {
+                ++nk;
+                m &= m - 1;
+            }
+        }
+        float acc[8];
+        sum_rows<MAXK>(nk, [&](int j) { return ld_cg_v4(base + c.combk_off(t, kl[j]) + 2ull * col); }, acc);
+        ptx::st_v4(out + static_cast<int64_t>(t) * c.hidden + col, f32x8_to_bf16(acc));
+    }
+}
+
 
 // ---------------------------------------------------------------------------
 // Transport-only path (rows in, rows out), MORI semantics.
@@ -746,6 +787,17 @@ void launch_combine_send(const EpConfig& c, const p2p::HeapView& h, const __nv_b
     if (grid <= 0) grid = 8 * default_grid();
     if (c.local_per_token() <= 8) combine_send_kernel<8><<<grid, kThreads, 0, s>>>(c, h, y, ws);
     else combine_send_kernel<kMaxTopk><<<grid, kThreads, 0, s>>>(c, h, y, ws);
+    KIWI_CUDA_CHECK(cudaGetLastError());
+}
+
+void launch_combine_recv_fused(const EpConfig& c, const p2p::HeapView& h, const int32_t* idx, int tokens,
+                               __nv_bfloat16* out, const EpWorkspace& ws, uint64_t timeout_ns, cudaStream_t s) {
+    const int grid = 8 * default_grid();
+    if (c.topk <= 8) {
+        combine_recv_fused_kernel<8><<<grid, kThreads, 0, s>>>(c, h, idx, tokens, out, ws, timeout_ns);
+    } else {
+        combine_recv_fused_kernel<kMaxTopk><<<grid, kThreads, 0, s>>>(c, h, idx, tokens, out, ws, timeout_ns);
+    }
     KIWI_CUDA_CHECK(cudaGetLastError());
 }
 

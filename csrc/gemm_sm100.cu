@@ -26,6 +26,7 @@
 
 #include "kiwi/gemm/grouped_gemm.hpp"
 #include "kiwi/p2p/driver.hpp"
+#include "kiwi/p2p/heap.hpp"
 #include "kiwi/sm100.cuh"
 
 namespace kiwi::gemm {
@@ -35,14 +36,26 @@ namespace {
 constexpr int kBM = 128;
 constexpr int kBK = 64;
 constexpr int kStages = 4;
+constexpr int kScatterStages = 3;
 constexpr int kThreads = 192;
 
-template <int BN>
+enum Epi : int { kEpiStore = 0, kEpiSwiGLU = 1, kEpiScatter = 2 };
+
+static_assert(kScatterMaxRanks == p2p::kMaxRanks, "ScatterArgs holds one base per rank");
+
+/// Shared memory of one CTA: STAGES x (A tile + B tile), then (scatter
+/// epilogue only) a bf16 staging tile per epilogue warp, 32 rows of BN columns
+/// with a 16-byte pad per row (conflict-free 16-byte row-wise accesses), then
+/// the barriers.
+template <int BN, int STAGES = kStages, bool STAGING = false>
 struct Smem {
     static constexpr int kABytes = kBM * kBK * 2;
     static constexpr int kBBytes = BN * kBK * 2;
     static constexpr int kStageBytes = kABytes + kBBytes;
-    static constexpr int kBarOffset = kStages * kStageBytes;
+    static constexpr int kStgStride = BN * 2 + 16;
+    static constexpr int kStgOffset = STAGES * kStageBytes;
+    static constexpr int kStgBytes = STAGING ? 4 * 32 * kStgStride : 0;
+    static constexpr int kBarOffset = kStgOffset + kStgBytes;
     static constexpr int kBytes = kBarOffset + 256 + 1024;  // barriers + tmem slot + alignment slack
 };
 
@@ -79,11 +92,13 @@ __device__ __forceinline__ void store_row32(__nv_bfloat16* dst, const float (&v)
     for (int i = 0; i < 4; ++i) d[i] = out[i];
 }
 
-template <int BN, bool SWIGLU>
+template <int BN, int EPI, int STAGES>
 __global__ void __launch_bounds__(kThreads, 1)
     grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
-                        GroupedArgs p) {
-    using S = Smem<BN>;
+                        GroupedArgs p, const __grid_constant__ ScatterArgs sc) {
+    constexpr int kStages = STAGES;
+    using S = Smem<BN, STAGES, EPI == kEpiScatter>;
+    __shared__ uint8_t* s_base[kScatterMaxRanks];
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::kBarOffset);
@@ -99,6 +114,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int k_blocks = p.k / kBK;
     const int total_tiles = __ldg(&p.tile_prefix[p.num_groups]);
 
+    if constexpr (EPI == kEpiScatter) {
+        if (threadIdx.x < kScatterMaxRanks) s_base[threadIdx.x] = sc.base[threadIdx.x];
+    }
     if (threadIdx.x == 0) {
         s_abort = 0;
         for (int s = 0; s < kStages; ++s) {
@@ -218,7 +236,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const bool valid = r < g_rows && out_row < p.max_rows;
             const float scale = (valid && p.row_scale) ? p.row_scale[out_row] : 1.0f;
             const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN;
-            if constexpr (SWIGLU) {
+            if constexpr (EPI == kEpiSwiGLU) {
                 __nv_bfloat16* crow = p.c + out_row * p.ldc + nt * (BN / 2);
 #pragma unroll 1
                 for (int c = 0; c < BN / 2; c += 32) {
@@ -229,7 +247,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                     for (int i = 0; i < 32; ++i) gv[i] = silu(gv[i]) * uv[i] * scale;
                     if (valid) store_row32(crow + c, gv);
                 }
-            } else {
+                sm100::tc_fence_before();
+                sm100::mbar_arrive(&tmem_empty[acc]);
+            } else if constexpr (EPI == kEpiStore) {
                 __nv_bfloat16* crow = p.c + out_row * p.ldc + nt * BN;
 #pragma unroll 1
                 for (int c = 0; c < BN; c += 32) {
@@ -239,9 +259,42 @@ __global__ void __launch_bounds__(kThreads, 1)
                     for (int i = 0; i < 32; ++i) v[i] *= scale;
                     if (valid) store_row32(crow + c, v);
                 }
+                sm100::tc_fence_before();
+                sm100::mbar_arrive(&tmem_empty[acc]);
+            } else {
+                // Scatter: stage the warp's 32 rows in shared memory, free the
+                // accumulator, then store whole 512-byte rows (16 bytes per
+                // lane) straight into the destination ranks' heaps, so the
+                // NVLink traffic of tile i overlaps the MMAs of tile i+1.
+                uint8_t* stg = smem + S::kStgOffset + q * 32 * S::kStgStride;
+#pragma unroll 1
+                for (int c = 0; c < BN; c += 32) {
+                    float v[32];
+                    sm100::tmem_ld_32cols(taddr + c, v);
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) v[i] *= scale;
+                    store_row32(reinterpret_cast<__nv_bfloat16*>(stg + lane * S::kStgStride + c * 2), v);
+                }
+                sm100::tc_fence_before();
+                sm100::mbar_arrive(&tmem_empty[acc]);
+                const int64_t my_dst = valid ? __ldg(&sc.row_dst[out_row]) : -1;
+                __syncwarp();
+#pragma unroll 1
+                for (int rr = 0; rr < 32; ++rr) {
+                    const long long d = __shfl_sync(0xffffffffu, static_cast<long long>(my_dst), rr);
+                    if (d < 0) continue;
+                    const int rank = static_cast<int>(d >> 48);
+                    uint8_t* dst = s_base[rank] + (d & kScatterOffMask) + static_cast<int64_t>(nt) * BN * 2;
+#pragma unroll
+                    for (int b = lane * 16; b < BN * 2; b += 32 * 16) {
+                        const uint4 val = *reinterpret_cast<const uint4*>(stg + rr * S::kStgStride + b);
+                        asm volatile("st.global.v4.u32 [%0], {%1, %2, %3, %4};" ::"l"(dst + b), "r"(val.x),
+                                     "r"(val.y), "r"(val.z), "r"(val.w)
+                                     : "memory");
+                    }
+                }
+                __syncwarp();
             }
-            sm100::tc_fence_before();
-            sm100::mbar_arrive(&tmem_empty[acc]);
             if (++acc == 2) {
                 acc = 0;
                 acc_phase ^= 1;
@@ -252,6 +305,24 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
     sm100::tc_fence_after();
     if (warp == 1) sm100::tmem_dealloc(tmem_base, 2 * BN);
+    if constexpr (EPI == kEpiScatter) {
+        // Completion: every CTA releases its stores at system scope and counts
+        // itself; the last one publishes (epoch << 32) | 1 to every rank.  A CTA
+        // that aborted does not count, so the receivers' bounded waits report it.
+        if (threadIdx.x == 0 && !*reinterpret_cast<volatile int*>(&s_abort)) {
+            asm volatile("fence.sc.sys;" ::: "memory");
+            const uint32_t prev = atomicAdd(sc.done_ctas, 1u);
+            if (prev == gridDim.x - 1) {
+                asm volatile("fence.sc.sys;" ::: "memory");
+                const uint64_t v = (static_cast<uint64_t>(*reinterpret_cast<const volatile uint32_t*>(sc.epoch)) << 32) | 1u;
+                for (int r = 0; r < sc.world; ++r) {
+                    asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(s_base[r] + sc.flag_off), "l"(v)
+                                 : "memory");
+                }
+                *reinterpret_cast<volatile uint32_t*>(sc.done_ctas) = 0;
+            }
+        }
+    }
 }
 
 
@@ -538,32 +609,48 @@ int num_sms() {
     return n;
 }
 
-void grouped_gemm(const CUtensorMap& tmap_a, const CUtensorMap& tmap_b, const GroupedArgs& args, bool swiglu,
-                  int grid, cudaStream_t stream) {
+namespace {
+
+template <int EPI, int STAGES>
+void launch_grouped(const CUtensorMap& tmap_a, const CUtensorMap& tmap_b, const GroupedArgs& args,
+                    const ScatterArgs& sc, int grid, cudaStream_t stream) {
     constexpr int BN = 256;
-    if (args.n % BN != 0 || args.k % kBK != 0) {
+    const int smem = Smem<BN, STAGES, EPI == kEpiScatter>::kBytes;
+    static bool attr = false;
+    if (!attr) {
+        KIWI_CUDA_CHECK(cudaFuncSetAttribute(grouped_gemm_kernel<BN, EPI, STAGES>,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+        attr = true;
+    }
+    grouped_gemm_kernel<BN, EPI, STAGES><<<grid, kThreads, smem, stream>>>(tmap_a, tmap_b, args, sc);
+    KIWI_CUDA_CHECK(cudaGetLastError());
+}
+
+void check_shape(const GroupedArgs& args) {
+    if (args.n % 256 != 0 || args.k % kBK != 0) {
         throw kiwi::error("grouped_gemm: N must be a multiple of 256 and K of 64");
     }
-    const int smem = Smem<BN>::kBytes;
+}
+
+}  // namespace
+
+void grouped_gemm(const CUtensorMap& tmap_a, const CUtensorMap& tmap_b, const GroupedArgs& args, bool swiglu,
+                  int grid, cudaStream_t stream) {
+    check_shape(args);
     if (grid <= 0) grid = num_sms();
-    if (swiglu) {
-        static bool attr = false;
-        if (!attr) {
-            KIWI_CUDA_CHECK(cudaFuncSetAttribute(grouped_gemm_kernel<BN, true>,
-                                                 cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-            attr = true;
-        }
-        grouped_gemm_kernel<BN, true><<<grid, kThreads, smem, stream>>>(tmap_a, tmap_b, args);
-    } else {
-        static bool attr = false;
-        if (!attr) {
-            KIWI_CUDA_CHECK(cudaFuncSetAttribute(grouped_gemm_kernel<BN, false>,
-                                                 cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-            attr = true;
-        }
-        grouped_gemm_kernel<BN, false><<<grid, kThreads, smem, stream>>>(tmap_a, tmap_b, args);
-    }
-    KIWI_CUDA_CHECK(cudaGetLastError());
+    const ScatterArgs none{};
+    if (swiglu) launch_grouped<kEpiSwiGLU, kStages>(tmap_a, tmap_b, args, none, grid, stream);
+    else launch_grouped<kEpiStore, kStages>(tmap_a, tmap_b, args, none, grid, stream);
+}
+
+void grouped_gemm_scatter(const CUtensorMap& tmap_a, const CUtensorMap& tmap_b, const GroupedArgs& args,
+                          const ScatterArgs& sc, int grid, cudaStream_t stream) {
+    check_shape(args);
+    if (args.n * 2 % 512 != 0) throw kiwi::error("grouped_gemm_scatter: N must be a multiple of 256");
+    if (!sc.row_dst || !sc.done_ctas || !sc.epoch) throw kiwi::error("grouped_gemm_scatter: missing arguments");
+    if (sc.world < 1 || sc.world > kScatterMaxRanks) throw kiwi::error("grouped_gemm_scatter: world out of range");
+    if (grid <= 0) grid = num_sms();
+    launch_grouped<kEpiScatter, kScatterStages>(tmap_a, tmap_b, args, sc, grid, stream);
 }
 
 void grouped_gemm_pair(const CUtensorMap& tmap_a, const CUtensorMap& tmap_b_half, const GroupedArgs& args,
@@ -604,9 +691,15 @@ KernelInfo gemm_pair_kernel_info(bool swiglu) {
 
 KernelInfo gemm_kernel_info(bool swiglu) {
     cudaFuncAttributes a{};
-    if (swiglu) KIWI_CUDA_CHECK(cudaFuncGetAttributes(&a, grouped_gemm_kernel<256, true>));
-    else KIWI_CUDA_CHECK(cudaFuncGetAttributes(&a, grouped_gemm_kernel<256, false>));
+    if (swiglu) KIWI_CUDA_CHECK(cudaFuncGetAttributes(&a, grouped_gemm_kernel<256, kEpiSwiGLU, kStages>));
+    else KIWI_CUDA_CHECK(cudaFuncGetAttributes(&a, grouped_gemm_kernel<256, kEpiStore, kStages>));
     return {static_cast<int>(a.localSizeBytes), a.numRegs, Smem<256>::kBytes};
+}
+
+KernelInfo gemm_scatter_kernel_info() {
+    cudaFuncAttributes a{};
+    KIWI_CUDA_CHECK(cudaFuncGetAttributes(&a, grouped_gemm_kernel<256, kEpiScatter, kScatterStages>));
+    return {static_cast<int>(a.localSizeBytes), a.numRegs, Smem<256, kScatterStages, true>::kBytes};
 }
 
 }  // namespace kiwi::gemm

@@ -12,6 +12,9 @@
 //   recv_row    [src][token] the dispatched row (FP8 / NVFP4 / BF16 bytes)
 //   recv_scale  [src][token] block scales (FP8: fp32 per 128; NVFP4: e4m3 per 16 + fp32 row scale)
 //   comb        [expert_owner][token] bf16 rows returned by combine
+//   combk       [token][k] bf16 rows written by the fused GEMM2 epilogue of
+//               the rank that owns the token's k-th expert (routing weight
+//               applied), summed over k by the receive side
 //
 // A slot is valid for a round when its meta.epoch equals the round's epoch,
 // so nothing is cleared between rounds.
@@ -52,6 +55,7 @@ struct EpConfig {
     uint64_t off_row;
     uint64_t off_scale;
     uint64_t off_comb;
+    uint64_t off_combk;
     uint64_t heap_bytes;
 
     KIWI_HD uint64_t slots() const { return static_cast<uint64_t>(world) * max_tokens; }
@@ -65,6 +69,9 @@ struct EpConfig {
     KIWI_HD uint64_t scale_off(uint64_t slot) const { return off_scale + slot * scale_bytes; }
     KIWI_HD uint64_t comb_off(int owner, int token) const {
         return off_comb + (static_cast<uint64_t>(owner) * max_tokens + token) * static_cast<uint64_t>(hidden) * 2;
+    }
+    KIWI_HD uint64_t combk_off(int token, int k) const {
+        return off_combk + (static_cast<uint64_t>(token) * topk + k) * static_cast<uint64_t>(hidden) * 2;
     }
     /// Upper bound of (token, local expert) pairs a rank can receive.
     KIWI_HD int64_t max_pairs() const {

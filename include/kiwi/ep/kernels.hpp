@@ -22,6 +22,7 @@ struct EpWorkspace {
     int32_t* pair_slot;       // [max_pairs] source slot of each expert row
     float* pair_w;            // [max_pairs] routing weight of each expert row
     int32_t* slot_pos;        // [slots * local_per_token] expert rows of a slot (-1 = none)
+    int64_t* pair_dst;        // [max_pairs] (src rank << 48) | combk_off(token, k) of each expert row
     __nv_bfloat16* a;         // [max_pairs, hidden] dequantised expert-major rows
     uint32_t* error;          // [4] {code, site, info, rank}
 };
@@ -60,6 +61,12 @@ void launch_combine_send(const EpConfig& c, const p2p::HeapView& h, const __nv_b
 /// local token (over the ranks it was sent to) into out [T, hidden].
 void launch_combine_recv(const EpConfig& c, const p2p::HeapView& h, const int32_t* idx, int tokens,
                          __nv_bfloat16* out, const EpWorkspace& ws, uint64_t timeout_ns, cudaStream_t s);
+
+/// Fused combine, receive side: after every rank's combine flag (set by the
+/// last CTA of each rank's scatter GEMM2), sums each local token's top-k rows
+/// of combk (already routing-weighted) into out [T, hidden].
+void launch_combine_recv_fused(const EpConfig& c, const p2p::HeapView& h, const int32_t* idx, int tokens,
+                               __nv_bfloat16* out, const EpWorkspace& ws, uint64_t timeout_ns, cudaStream_t s);
 
 // ---- transport-only (MORI-compatible) path ----
 

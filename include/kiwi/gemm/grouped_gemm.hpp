@@ -25,6 +25,26 @@ struct GroupedArgs {
     int64_t max_rows;             // rows C holds: rows at or past it are never stored
 };
 
+/// Scatter epilogue of the fused MoE combine (grouped_gemm_scatter): result
+/// row r, scaled by row_scale[r] and converted to bf16, is stored at byte
+/// offset (row_dst[r] & kScatterOffMask) of rank (row_dst[r] >> 48)'s heap
+/// (base[rank], a peer mapping for other ranks); row_dst[r] < 0 drops the row.
+/// When every CTA has finished, the last one stores (epoch << 32) | 1 with
+/// release semantics at flag_off of every rank's heap.  done_ctas must be zero
+/// at launch (the last CTA leaves it zero again).
+inline constexpr int kScatterMaxRanks = 16;
+inline constexpr uint64_t kScatterOffMask = (uint64_t{1} << 48) - 1;
+
+struct ScatterArgs {
+    uint8_t* base[kScatterMaxRanks];
+    const int64_t* row_dst;
+    uint32_t* done_ctas;
+    const uint32_t* epoch;
+    uint64_t flag_off;
+    int32_t world;
+    int32_t pad_;
+};
+
 struct KernelInfo {
     int local_bytes;
     int registers;
@@ -50,7 +70,14 @@ void grouped_gemm(const CUtensorMap& tmap_a, const CUtensorMap& tmap_b, const Gr
 void grouped_gemm_pair(const CUtensorMap& tmap_a, const CUtensorMap& tmap_b_half, const GroupedArgs& args,
                        bool swiglu, int grid, cudaStream_t stream);
 
+/// Grouped GEMM whose epilogue scatters rows to (remote) heaps and signals
+/// completion (see ScatterArgs).  N must be a multiple of 256 (whole 512-byte
+/// rows per tile); 3 pipeline stages leave room for the staging tiles.
+void grouped_gemm_scatter(const CUtensorMap& tmap_a, const CUtensorMap& tmap_b, const GroupedArgs& args,
+                          const ScatterArgs& sc, int grid, cudaStream_t stream);
+
 KernelInfo gemm_kernel_info(bool swiglu);
+KernelInfo gemm_scatter_kernel_info();
 KernelInfo gemm_pair_kernel_info(bool swiglu);
 int num_sms();
 

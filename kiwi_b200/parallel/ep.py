@@ -11,10 +11,13 @@ stream and without host synchronisation:
    NVLink stores into every destination rank's receive slots, deduplicated
    per destination rank, one release flag per source rank;
 3. receive: per-expert counts, expert-major layout, dequantisation to bf16;
-4. experts: tcgen05 grouped GEMM (SwiGLU fused) then grouped GEMM (routing
-   weight fused), bf16 compute with fp32 accumulation;
-5. combine: each slot's weighted expert rows summed and stored back into the
-   token owner's combine slots over NVLink, then reduced per token.
+4. experts: tcgen05 grouped GEMM (SwiGLU fused) then grouped GEMM whose
+   epilogue multiplies by the routing weight and stores every row straight
+   into its token owner's top-k slot over NVLink (fused combine; the last CTA
+   signals every rank), bf16 compute with fp32 accumulation;
+5. combine: each token's top-k rows summed (fp32) into the output.
+   ``native.fused_combine = False`` selects the unfused path instead: GEMM2 to
+   local memory, per-slot sums sent over NVLink, reduced per token.
 
 ``stage(...)`` methods expose the phases separately for profiling, and
 :class:`EpDispatchCombine` gives the reference's transport-only
@@ -136,6 +139,9 @@ class EpDispatchCombine:
         w13 = torch.zeros(epr * 2 * cfg.ffn, hidden, dtype=torch.bfloat16, device=dev)
         w2 = torch.zeros(epr * hidden, cfg.ffn, dtype=torch.bfloat16, device=dev)
         self.moe = ExpertParallelMoE(cfg, group, max_tokens, weights=(w13, w2), timeout_s=timeout_s)
+        # The caller supplies expert outputs as rows: combine sends them with the
+        # combine-send kernel, not through the fused GEMM2 epilogue.
+        self.moe.native.fused_combine = False
         self._idx = None
 
     def dispatch(self, x, weights, indices):

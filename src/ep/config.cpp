@@ -46,6 +46,8 @@ EpConfig finalize(EpConfig c) {
     off += round_up(slots * static_cast<uint64_t>(c.scale_bytes), 256);
     c.off_comb = off;
     off += round_up(slots * static_cast<uint64_t>(c.hidden) * 2, 256);
+    c.off_combk = off;
+    off += round_up(static_cast<uint64_t>(c.max_tokens) * c.topk * static_cast<uint64_t>(c.hidden) * 2, 256);
     c.heap_bytes = off;
     return c;
 }

@@ -26,10 +26,14 @@ def _check(layer, cfg, x, logits, out, rel=2e-2):
     assert err <= rel * scale + 1e-3, (err, scale)
 
 
+@pytest.mark.parametrize("fused", [True, False])
 @pytest.mark.parametrize("quant", ["fp8", "nvfp4", "none"])
-def test_layer_matches_reference(quant):
+def test_layer_matches_reference(quant, fused):
+    """fused=True: GEMM2's epilogue stores the weighted rows into the token
+    owners' top-k slots (fused combine); False: GEMM2, combine send, receive."""
     cfg = small_cfg(quant)
     layer = ExpertParallelMoE(cfg)
+    layer.native.fused_combine = fused
     # NVFP4 keeps one mantissa bit: a single rounding disagreement between two
     # correct quantisers moves an output by a visible fraction of its range.
     rel = 5e-2 if quant == "nvfp4" else 2e-2

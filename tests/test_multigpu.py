@@ -66,13 +66,14 @@ def _all_pairs(rank, world):
     del heap
 
 
-def _ep_layer(rank, world, quant):
+def _ep_layer(rank, world, quant, fused=True):
     from kiwi_b200.models import moe
     from kiwi_b200.parallel.ep import ExpertParallelMoE
 
     cfg = moe.MoEConfig(hidden=1024, ffn=256, num_experts=8 * world, topk=4, tokens_per_rank=96, quant=quant,
                         name="t")
     layer = ExpertParallelMoE(cfg)
+    layer.native.fused_combine = fused
     for step in range(3):
         x, logits = moe.synthetic_inputs(cfg, rank, "cuda", step=step, tokens=96 - 16 * step)
         out = layer(x, logits).clone()
@@ -131,9 +132,9 @@ def test_all_pairs_puts_2():
     _run(_all_pairs, 2)
 
 
-@pytest.mark.parametrize("quant", ["fp8", "nvfp4"])
-def test_ep_layer_world2(quant):
-    _run(_ep_layer, 2, quant)
+@pytest.mark.parametrize("quant,fused", [("fp8", True), ("nvfp4", True), ("fp8", False)])
+def test_ep_layer_world2(quant, fused):
+    _run(_ep_layer, 2, quant, fused)
 
 
 def test_ep_layer_world4():
