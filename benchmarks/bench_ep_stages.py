@@ -3,8 +3,11 @@
     python benchmarks/bench_ep_stages.py [--config deepseek_fp8] [--tokens 4096] [--steps 10]
     torchrun --nproc-per-node N --master-addr 127.0.0.1 benchmarks/bench_ep_stages.py ...
 
-Stages: route, dispatch (+begin), receive (count, schedules, scatter), experts
-(two grouped GEMMs), combine (send + reduce).  Prints one RESULT JSON line.
+Stages: route, dispatch (+begin), receive (count, schedules, assign, copy),
+gemm1 (gate/up + SwiGLU), gemm2 (down projection; with the fused combine its
+epilogue also stores the rows over NVLink), combine (fused: wait + top-k sum;
+--unfused: send + reduce).  A stage that waits for other ranks includes their
+skew.  Prints one RESULT JSON line.
 """
 import argparse
 import json
@@ -25,6 +28,7 @@ def main():
     ap.add_argument("--tokens", type=int, default=None)
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--experts", type=int, default=None, help="override the expert count (small profiling cases)")
+    ap.add_argument("--unfused", action="store_true", help="GEMM2 to local memory + combine send/receive")
     args = ap.parse_args()
     rank, world = kdist.init()
     cfg = moe_model.CONFIGS[args.config]
@@ -33,9 +37,10 @@ def main():
     if args.experts:
         cfg = moe_model.MoEConfig(**{**cfg.__dict__, "num_experts": args.experts})
     layer = ExpertParallelMoE(cfg)
+    layer.native.fused_combine = not args.unfused
     x, logits = moe_model.synthetic_inputs(cfg, rank, "cuda")
     out = torch.empty_like(x)
-    names = ["route", "dispatch", "receive", "experts", "combine"]
+    names = ["route", "dispatch", "receive", "gemm1", "gemm2", "combine"]
     ev = [torch.cuda.Event(enable_timing=True) for _ in range(len(names) + 1)]
     acc = [0.0] * len(names)
     for it in range(args.steps + 3):
@@ -48,10 +53,12 @@ def main():
         ev[2].record()
         layer.stage_receive()
         ev[3].record()
-        layer.stage_experts()
+        layer.native.experts_gemm(1)
         ev[4].record()
-        layer.stage_combine(idx, out)
+        layer.native.experts_gemm(2)
         ev[5].record()
+        layer.stage_combine(idx, out)
+        ev[6].record()
         torch.cuda.synchronize()
         if it >= 3:
             for i in range(len(names)):
@@ -61,6 +68,7 @@ def main():
     counts = layer.expert_counts.float()
     if rank == 0:
         print("RESULT " + json.dumps({"bench": "ep_stages_us", "config": args.config, "world": world,
+                                      "fused_combine": not args.unfused,
                                       "tokens_per_rank": cfg.tokens_per_rank, **res,
                                       "total_us": sum(res.values()),
                                       "rows_per_expert_mean": float(counts.mean()),

@@ -160,6 +160,14 @@ public:
     }
 
     void experts() {
+        experts_gemm(1);
+        experts_gemm(2);
+    }
+
+    /// One of the two expert GEMMs (1: gate/up + SwiGLU, 2: down projection;
+    /// with fused_combine, GEMM2 also performs the combine's NVLink stores).
+    void experts_gemm(int which) {
+        TORCH_CHECK(which == 1 || which == 2, "experts_gemm: 1 or 2");
         cudaStream_t s = cur_stream();
         gemm::GroupedArgs g1{};
         g1.group_offset = ws_.offsets;
@@ -172,8 +180,11 @@ public:
         g1.row_scale = nullptr;
         g1.error = reinterpret_cast<uint32_t*>(gemm_error_.data_ptr<int32_t>());
         g1.max_rows = cfg_.max_pairs();
-        if (pair_) gemm::grouped_gemm_pair(tmap_a1_, tmap_b1h_, g1, /*swiglu=*/true, 0, s);
-        else gemm::grouped_gemm(tmap_a1_, tmap_b1_, g1, /*swiglu=*/true, 0, s);
+        if (which == 1) {
+            if (pair_) gemm::grouped_gemm_pair(tmap_a1_, tmap_b1h_, g1, /*swiglu=*/true, 0, s);
+            else gemm::grouped_gemm(tmap_a1_, tmap_b1_, g1, /*swiglu=*/true, 0, s);
+            return;
+        }
         gemm::GroupedArgs g2 = g1;
         g2.tile_prefix = ws_.tiles2;
         g2.n = cfg_.hidden;
@@ -389,6 +400,7 @@ void register_ep(py::module_& m) {
         .def("dispatch", &MoeLayer::dispatch)
         .def("receive", &MoeLayer::receive)
         .def("experts", &MoeLayer::experts)
+        .def("experts_gemm", &MoeLayer::experts_gemm, py::arg("which"))
         .def("combine", &MoeLayer::combine)
         .def("forward", &MoeLayer::forward)
         .def("error", &MoeLayer::error)
