@@ -20,6 +20,8 @@
 #include <cuda_fp8.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
+
 #include "kiwi/ep/kernels.hpp"
 #include "kiwi/ptx.cuh"
 
@@ -458,45 +460,85 @@ __global__ void __launch_bounds__(kThreads) recv_assign_kernel(EpConfig c, p2p::
     }
 }
 
+/// Raw bytes of one receive item (a slot's 512-column block) as loaded.
+struct RecvRaw {
+    uint4 q0, q1;
+    float s0;
+    uint32_t s1;
+};
+
+template <int QUANT>
+KIWI_DEV void recv_load(const EpConfig& c, const uint8_t* base, uint64_t s, int col, int lane, RecvRaw& r) {
+    if constexpr (QUANT == static_cast<int>(Quant::kNone)) {
+        r.q0 = ld_cg_v4(base + c.row_off(s) + 2ull * col);
+        r.q1 = ld_cg_v4(base + c.row_off(s) + 2ull * col + 16);
+    } else if constexpr (QUANT == static_cast<int>(Quant::kFp8)) {
+        r.q0 = ld_cg_v4(base + c.row_off(s) + col);
+        r.s0 = ld_cg_f32(base + c.scale_off(s) + 4ull * (col / kFp8Block));
+    } else {
+        r.q0 = ld_cg_v4(base + c.row_off(s) + (col / 32) * 16);  // 16 B = 32 elements (a lane pair)
+        r.s0 = ld_cg_f32(base + c.scale_off(s));
+        r.s1 = ld_cg_u32(base + c.scale_off(s) + 4 + ((col / kFp4Block) & ~3));
+    }
+}
+
+template <int QUANT>
+KIWI_DEV void recv_convert(int col, int lane, const RecvRaw& r, uint4 (&out)[2]) {
+    if constexpr (QUANT == static_cast<int>(Quant::kNone)) {
+        out[0] = r.q0;
+        out[1] = r.q1;
+    } else if constexpr (QUANT == static_cast<int>(Quant::kFp8)) {
+        dequant_fp8_16(r.q0, r.s0, out);
+    } else {
+        const uint2 q = (lane & 1) ? make_uint2(r.q0.z, r.q0.w) : make_uint2(r.q0.x, r.q0.y);
+        const uint8_t sb = static_cast<uint8_t>(r.s1 >> (8 * ((col / kFp4Block) & 3)));
+        const __half_raw sh = __nv_cvt_fp8_to_halfraw(sb, __NV_E4M3);
+        dequant_fp4_16(q, __half2float(*reinterpret_cast<const __half*>(&sh)) * r.s0, out);
+    }
+}
+
 /// Receive, step 2: for every (valid slot, 512-column block) the warp loads the
 /// dispatched bytes once, dequantises them and stores the bf16 row block into
-/// each of the slot's expert-major rows.  Items are spread over the whole grid.
+/// each of the slot's expert-major rows.  Items are spread over the whole grid
+/// and each warp keeps two items' loads in flight (the kernel is load-latency
+/// bound: ncu showed long-scoreboard stalls dominating at 79 % warp occupancy).
 template <int QUANT>
 __global__ void __launch_bounds__(kThreads) recv_copy_kernel(EpConfig c, p2p::HeapView h, EpWorkspace ws) {
     const int lane = threadIdx.x & 31;
-    const int warps = gridDim.x * (blockDim.x / 32);
+    const uint64_t warps = gridDim.x * (blockDim.x / 32);
     const int lpt = c.local_per_token();
     const uint8_t* base = h.base[h.rank];
     const int blocks = c.hidden / 512;
     const uint64_t items = c.slots() * blocks;
-    for (uint64_t it = (blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x) / 32; it < items; it += warps) {
-        const uint64_t s = it / blocks;
-        const int col = static_cast<int>(it % blocks) * 512 + lane * 16;
-        const int p = lane < lpt ? ws.slot_pos[s * lpt + lane] : -1;
-        const uint32_t pm = __ballot_sync(0xffffffffu, p >= 0);
-        if (pm == 0) continue;
-        uint4 out[2];
-        if constexpr (QUANT == static_cast<int>(Quant::kNone)) {
-            out[0] = ld_cg_v4(base + c.row_off(s) + 2ull * col);
-            out[1] = ld_cg_v4(base + c.row_off(s) + 2ull * col + 16);
-        } else if constexpr (QUANT == static_cast<int>(Quant::kFp8)) {
-            const uint4 q = ld_cg_v4(base + c.row_off(s) + col);
-            const float sc = ld_cg_f32(base + c.scale_off(s) + 4ull * (col / kFp8Block));
-            dequant_fp8_16(q, sc, out);
-        } else {
-            const uint4 qq = ld_cg_v4(base + c.row_off(s) + (col / 32) * 16);  // 16 B = 32 elements
-            const uint2 q = (lane & 1) ? make_uint2(qq.z, qq.w) : make_uint2(qq.x, qq.y);
-            const float rs = ld_cg_f32(base + c.scale_off(s));
-            const uint8_t sb = static_cast<uint8_t>(ld_cg_u32(base + c.scale_off(s) + 4 + ((col / kFp4Block) & ~3)) >>
-                                                    (8 * ((col / kFp4Block) & 3)));
-            const __half_raw sh = __nv_cvt_fp8_to_halfraw(sb, __NV_E4M3);
-            dequant_fp4_16(q, __half2float(*reinterpret_cast<const __half*>(&sh)) * rs, out);
+    for (uint64_t it = (blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x) / 32; it < items;
+         it += 2 * warps) {
+        uint64_t s[2];
+        int col[2], p[2];
+        uint32_t pm[2];
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+            const uint64_t i = it + u * warps;
+            s[u] = i / blocks;
+            col[u] = static_cast<int>(i % blocks) * 512 + lane * 16;
+            p[u] = (i < items && lane < lpt) ? ws.slot_pos[s[u] * lpt + lane] : -1;
         }
-        for (uint32_t m = pm; m; m &= m - 1) {
-            const int pp = __shfl_sync(0xffffffffu, p, __ffs(m) - 1);
-            __nv_bfloat16* dst = ws.a + static_cast<int64_t>(pp) * c.hidden + col;
-            ptx::st_v4(dst, out[0]);
-            ptx::st_v4(dst + 8, out[1]);
+        RecvRaw raw[2];
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+            pm[u] = __ballot_sync(0xffffffffu, p[u] >= 0);
+            if (pm[u]) recv_load<QUANT>(c, base, s[u], col[u], lane, raw[u]);
+        }
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+            if (pm[u] == 0) continue;
+            uint4 out[2];
+            recv_convert<QUANT>(col[u], lane, raw[u], out);
+            for (uint32_t m = pm[u]; m; m &= m - 1) {
+                const int pp = __shfl_sync(0xffffffffu, p[u], __ffs(m) - 1);
+                __nv_bfloat16* dst = ws.a + static_cast<int64_t>(pp) * c.hidden + col[u];
+                ptx::st_v4(dst, out[0]);
+                ptx::st_v4(dst + 8, out[1]);
+            }
         }
     }
 }
@@ -745,7 +787,12 @@ void launch_route(const float* logits, int tokens, int experts, int topk, int32_
 void launch_dispatch(const EpConfig& c, const p2p::HeapView& h, const __nv_bfloat16* x, const int32_t* idx,
                      const float* w, int tokens, const EpWorkspace& ws, int grid, cudaStream_t s) {
     if (tokens > c.max_tokens) throw kiwi::error("dispatch: more tokens than max_tokens");
-    if (grid <= 0) grid = default_grid();
+    if (grid <= 0) {
+        // One warp per token up to 8 blocks per SM: dispatch is load- and
+        // store-latency bound, so every token's loads should be in flight at once.
+        const int want = (tokens * 32 + kThreads - 1) / kThreads;
+        grid = std::max(1, std::min(want, 8 * default_grid()));
+    }
     switch (static_cast<Quant>(c.quant)) {
         case Quant::kNone:
             dispatch_kernel<0><<<grid, kThreads, 0, s>>>(c, h, x, idx, w, tokens, ws);

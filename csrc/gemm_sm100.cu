@@ -36,7 +36,7 @@ namespace {
 constexpr int kBM = 128;
 constexpr int kBK = 64;
 constexpr int kStages = 4;
-constexpr int kScatterStages = 3;
+constexpr int kScatterStages = 4;
 constexpr int kThreads = 192;
 
 enum Epi : int { kEpiStore = 0, kEpiSwiGLU = 1, kEpiScatter = 2 };
@@ -44,15 +44,16 @@ enum Epi : int { kEpiStore = 0, kEpiSwiGLU = 1, kEpiScatter = 2 };
 static_assert(kScatterMaxRanks == p2p::kMaxRanks, "ScatterArgs holds one base per rank");
 
 /// Shared memory of one CTA: STAGES x (A tile + B tile), then (scatter
-/// epilogue only) a bf16 staging tile per epilogue warp, 32 rows of BN columns
-/// with a 16-byte pad per row (conflict-free 16-byte row-wise accesses), then
-/// the barriers.
+/// epilogue only) a bf16 staging tile per epilogue warp holding 32 rows of
+/// BN/2 columns (256 bytes each, 16-byte chunks XOR-swizzled by row so that
+/// both the row-per-thread writes and the row-wise reads are conflict-free),
+/// then the barriers.
 template <int BN, int STAGES = kStages, bool STAGING = false>
 struct Smem {
     static constexpr int kABytes = kBM * kBK * 2;
     static constexpr int kBBytes = BN * kBK * 2;
     static constexpr int kStageBytes = kABytes + kBBytes;
-    static constexpr int kStgStride = BN * 2 + 16;
+    static constexpr int kStgStride = BN;  // BN/2 bf16 columns = BN bytes per staged row
     static constexpr int kStgOffset = STAGES * kStageBytes;
     static constexpr int kStgBytes = STAGING ? 4 * 32 * kStgStride : 0;
     static constexpr int kBarOffset = kStgOffset + kStgBytes;
@@ -262,38 +263,57 @@ __global__ void __launch_bounds__(kThreads, 1)
                 sm100::tc_fence_before();
                 sm100::mbar_arrive(&tmem_empty[acc]);
             } else {
-                // Scatter: stage the warp's 32 rows in shared memory, free the
-                // accumulator, then store whole 512-byte rows (16 bytes per
-                // lane) straight into the destination ranks' heaps, so the
-                // NVLink traffic of tile i overlaps the MMAs of tile i+1.
+                // Scatter: per half tile (BN/2 columns) stage the warp's 32
+                // rows in shared memory, then store them as 256-byte row
+                // segments (16 lanes per row, two rows per instruction) straight
+                // into the destination ranks' heaps, so the NVLink traffic of
+                // tile i overlaps the MMAs of tile i+1.  The accumulator is
+                // released as soon as its second half has been read.
+                static_assert(BN == 256, "scatter staging assumes 256-column tiles");
                 uint8_t* stg = smem + S::kStgOffset + q * 32 * S::kStgStride;
-#pragma unroll 1
-                for (int c = 0; c < BN; c += 32) {
-                    float v[32];
-                    sm100::tmem_ld_32cols(taddr + c, v);
-#pragma unroll
-                    for (int i = 0; i < 32; ++i) v[i] *= scale;
-                    store_row32(reinterpret_cast<__nv_bfloat16*>(stg + lane * S::kStgStride + c * 2), v);
-                }
-                sm100::tc_fence_before();
-                sm100::mbar_arrive(&tmem_empty[acc]);
                 const int64_t my_dst = valid ? __ldg(&sc.row_dst[out_row]) : -1;
-                __syncwarp();
+                const int half_lane = lane & 15;
 #pragma unroll 1
-                for (int rr = 0; rr < 32; ++rr) {
-                    const long long d = __shfl_sync(0xffffffffu, static_cast<long long>(my_dst), rr);
-                    if (d < 0) continue;
-                    const int rank = static_cast<int>(d >> 48);
-                    uint8_t* dst = s_base[rank] + (d & kScatterOffMask) + static_cast<int64_t>(nt) * BN * 2;
+                for (int half = 0; half < 2; ++half) {
+#pragma unroll 1
+                    for (int c = 0; c < BN / 2; c += 32) {
+                        float v[32];
+                        sm100::tmem_ld_32cols(taddr + half * (BN / 2) + c, v);
+                        uint32_t w[16];
 #pragma unroll
-                    for (int b = lane * 16; b < BN * 2; b += 32 * 16) {
-                        const uint4 val = *reinterpret_cast<const uint4*>(stg + rr * S::kStgStride + b);
-                        asm volatile("st.global.v4.u32 [%0], {%1, %2, %3, %4};" ::"l"(dst + b), "r"(val.x),
-                                     "r"(val.y), "r"(val.z), "r"(val.w)
-                                     : "memory");
+                        for (int i = 0; i < 16; ++i) {
+                            __nv_bfloat162 hv = __floats2bfloat162_rn(v[2 * i] * scale, v[2 * i + 1] * scale);
+                            w[i] = *reinterpret_cast<uint32_t*>(&hv);
+                        }
+#pragma unroll
+                        for (int j = 0; j < 4; ++j) {
+                            const int chunk = (c / 8 + j) ^ (lane & 15);
+                            *reinterpret_cast<uint4*>(stg + lane * S::kStgStride + chunk * 16) =
+                                make_uint4(w[4 * j], w[4 * j + 1], w[4 * j + 2], w[4 * j + 3]);
+                        }
                     }
+                    if (half == 1) {
+                        sm100::tc_fence_before();
+                        sm100::mbar_arrive(&tmem_empty[acc]);
+                    }
+                    __syncwarp();
+#pragma unroll 1
+                    for (int rr = 0; rr < 32; rr += 2) {
+                        const int row = rr + (lane >> 4);
+                        const long long d = __shfl_sync(0xffffffffu, static_cast<long long>(my_dst), row);
+                        if (d >= 0) {
+                            const int rank = static_cast<int>(d >> 48);
+                            uint8_t* dst = s_base[rank] + (d & kScatterOffMask) +
+                                           (static_cast<int64_t>(nt) * BN + half * (BN / 2)) * 2 + half_lane * 16;
+                            const uint4 val = *reinterpret_cast<const uint4*>(
+                                stg + row * S::kStgStride + ((half_lane ^ (row & 15)) * 16));
+                            asm volatile("st.global.v4.u32 [%0], {%1, %2, %3, %4};" ::"l"(dst), "r"(val.x),
+                                         "r"(val.y), "r"(val.z), "r"(val.w)
+                                         : "memory");
+                        }
+                    }
+                    __syncwarp();
                 }
-                __syncwarp();
             }
             if (++acc == 2) {
                 acc = 0;

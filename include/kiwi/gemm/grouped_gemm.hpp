@@ -72,7 +72,7 @@ void grouped_gemm_pair(const CUtensorMap& tmap_a, const CUtensorMap& tmap_b_half
 
 /// Grouped GEMM whose epilogue scatters rows to (remote) heaps and signals
 /// completion (see ScatterArgs).  N must be a multiple of 256 (whole 512-byte
-/// rows per tile); 3 pipeline stages leave room for the staging tiles.
+/// rows per tile); 4 pipeline stages plus 32 KB of half-row staging tiles.
 void grouped_gemm_scatter(const CUtensorMap& tmap_a, const CUtensorMap& tmap_b, const GroupedArgs& args,
                           const ScatterArgs& sc, int grid, cudaStream_t stream);
 
