@@ -33,8 +33,10 @@ import torch  # noqa: E402
 
 METRIC = "p50 GPU→CPU→GPU invoke µs; EP dispatch+combine µs & tokens/s at 1/2/4/8 B200"
 BASELINE_INVOKE_P50_US = 1.92   # published reference number (MI300X)
-# route, begin, dispatch, recv_count, 2 schedules, recv assign+copy, GEMM1, GEMM2 (+ combine send, unfused), combine recv
-KERNELS_PER_STEP = {True: 11, False: 12}
+# route, begin, dispatch, recv_count, 2 schedules, recv assign (+ copy without the GEMM1 gather), GEMM1,
+# GEMM2 (+ combine send when unfused), combine reduce
+def kernels_per_step(fused, gather):
+    return 10 + (0 if fused else 1) + (0 if gather else 1)
 
 
 def parse():
@@ -48,6 +50,8 @@ def parse():
     ap.add_argument("--latency-tokens", type=int, default=128)
     ap.add_argument("--invoke-iters", type=int, default=200000)
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-gather", action="store_true",
+                    help="receive kernel writes expert-major bf16 rows for GEMM1 (comparison only)")
     ap.add_argument("--unfused-combine", action="store_true",
                     help="GEMM2 to local memory + combine send/receive kernels (comparison only)")
     return ap.parse_args()
@@ -91,6 +95,7 @@ def main():
 
         layer = ExpertParallelMoE(cfg, max_tokens=max(T, args.latency_tokens))
         layer.native.fused_combine = not args.unfused_combine
+        layer.native.gather_a = not args.no_gather
     else:
         from kiwi_b200.parallel.baseline import NcclMoEBaseline
 
@@ -207,8 +212,10 @@ def main():
             "tflops_per_gpu": flops / (ms / 1e3) / 1e12,
             "clocks": {"sm_mhz": clk["sm_mhz"], "sm_max_mhz": clk["sm_max_mhz"], "reasons": clk["reasons"],
                        "samples": clk["samples"]},
-            "e2e": e2e, "gpu_launches": KERNELS_PER_STEP[not args.unfused_combine] * args.steps if args.impl == "kiwi" else None,
+            "e2e": e2e, "gpu_launches": kernels_per_step(not args.unfused_combine, not args.no_gather) * args.steps
+            if args.impl == "kiwi" else None,
             "fused_combine": (not args.unfused_combine) if args.impl == "kiwi" else None,
+            "gather_a": (not args.no_gather) if args.impl == "kiwi" else None,
             "latency_mode": lat, "invoke_rtt": invoke, "impl": args.impl,
         }
         emit(line)

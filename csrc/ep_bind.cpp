@@ -156,8 +156,13 @@ public:
         gemm::build_schedule(ws_.expert_count, cfg_.experts_per_rank, static_cast<int>(2 * ffn_), 256, ws_.offsets,
                              ws_.tiles1, s, bm);
         gemm::build_schedule(ws_.expert_count, cfg_.experts_per_rank, cfg_.hidden, 256, ws_.offsets, ws_.tiles2, s, bm);
-        ep::launch_recv_scatter(cfg_, heap_.view(), ws_, s);
+        ep::launch_recv_assign(cfg_, heap_.view(), ws_, s);
+        if (!gathers()) ep::launch_recv_copy(cfg_, heap_.view(), ws_, s);
     }
+
+    /// GEMM1 reads its A rows in place from the receive buffer (FP8 / NVFP4
+    /// dispatch), so the expert-major bf16 copy is skipped.
+    bool gathers() const { return gather_ && cfg_.quant != static_cast<int>(ep::Quant::kNone); }
 
     void experts() {
         experts_gemm(1);
@@ -181,8 +186,21 @@ public:
         g1.error = reinterpret_cast<uint32_t*>(gemm_error_.data_ptr<int32_t>());
         g1.max_rows = cfg_.max_pairs();
         if (which == 1) {
-            if (pair_) gemm::grouped_gemm_pair(tmap_a1_, tmap_b1h_, g1, /*swiglu=*/true, 0, s);
-            else gemm::grouped_gemm(tmap_a1_, tmap_b1_, g1, /*swiglu=*/true, 0, s);
+            if (gathers()) {
+                gemm::GatherArgs ga{};
+                ga.base = static_cast<const uint8_t*>(heap_.local());
+                ga.row_slot = ws_.pair_slot;
+                ga.off_row = cfg_.off_row;
+                ga.off_scale = cfg_.off_scale;
+                ga.row_bytes = cfg_.row_bytes;
+                ga.scale_bytes = cfg_.scale_bytes;
+                ga.quant = cfg_.quant;
+                gemm::grouped_gemm_gather(tmap_b1_, g1, ga, 0, s);
+            } else if (pair_) {
+                gemm::grouped_gemm_pair(tmap_a1_, tmap_b1h_, g1, /*swiglu=*/true, 0, s);
+            } else {
+                gemm::grouped_gemm(tmap_a1_, tmap_b1_, g1, /*swiglu=*/true, 0, s);
+            }
             return;
         }
         gemm::GroupedArgs g2 = g1;
@@ -276,8 +294,11 @@ private:
     CUtensorMap tmap_a1_, tmap_b1_, tmap_a2_, tmap_b2_, tmap_b1h_, tmap_b2h_;
     bool pair_ = false;
     bool fused_ = true;
+    bool gather_ = true;
 
 public:
+    bool gather() const { return gather_; }
+    void set_gather(bool v) { gather_ = v; }
     bool pair() const { return pair_; }
     void set_pair(bool v) { pair_ = v; }
     bool fused() const { return fused_; }
@@ -416,6 +437,9 @@ void register_ep(py::module_& m) {
         .def_property_readonly("epoch", &MoeLayer::epoch)
         .def_property("gemm_pair", &MoeLayer::pair, &MoeLayer::set_pair,
                       "Use the 2-SM (256-row tile) grouped GEMM (unfused combine only; off by default).")
+        .def_property("gather_a", &MoeLayer::gather, &MoeLayer::set_gather,
+                      "GEMM1 gathers and dequantises its A rows from the receive buffer (FP8 / NVFP4 dispatch; "
+                      "default); False: a receive kernel first writes expert-major bf16 rows.")
         .def_property("fused_combine", &MoeLayer::fused, &MoeLayer::set_fused,
                       "GEMM2 epilogue stores rows over NVLink into the token owners' top-k slots (default); "
                       "False: GEMM2 to local memory, then combine send + receive kernels.");

@@ -23,6 +23,7 @@
 #include <algorithm>
 
 #include "kiwi/ep/kernels.hpp"
+#include "kiwi/ep/quant.cuh"
 #include "kiwi/ptx.cuh"
 
 namespace kiwi::ep {
@@ -30,8 +31,6 @@ namespace kiwi::ep {
 namespace {
 
 constexpr int kThreads = 256;
-constexpr float kFp8Max = 448.0f;
-constexpr float kFp4Max = 6.0f;
 
 KIWI_DEV void set_error(const EpWorkspace& ws, uint32_t code, uint32_t site, uint32_t info, int rank) {
     if (atomicCAS(&ws.error[0], 0u, code) == 0u) {
@@ -60,27 +59,6 @@ KIWI_DEV uint32_t ld_cg_u32(const void* p) {
     return v;
 }
 KIWI_DEV float ld_cg_f32(const void* p) { return __uint_as_float(ld_cg_u32(p)); }
-
-KIWI_DEV void bf16x8_to_f32(uint4 u, float (&f)[8]) {
-    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        const float2 t = __bfloat1622float2(h[i]);
-        f[2 * i] = t.x;
-        f[2 * i + 1] = t.y;
-    }
-}
-
-KIWI_DEV uint4 f32x8_to_bf16(const float (&f)[8]) {
-    uint4 u;
-    uint32_t* w = reinterpret_cast<uint32_t*>(&u);
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        __nv_bfloat162 h = __floats2bfloat162_rn(f[2 * i], f[2 * i + 1]);
-        w[i] = *reinterpret_cast<uint32_t*>(&h);
-    }
-    return u;
-}
 
 /// Last-CTA completion: after every CTA has issued its stores, the last one
 /// to arrive publishes `value` to flag offset `flag_off` on every rank.
@@ -195,101 +173,6 @@ __global__ void __launch_bounds__(kThreads) route_kernel(const float* logits, in
             w[static_cast<int64_t>(t) * topk + r] = __expf(top_v[r] - top_v[0]) / sum;
         }
     }
-}
-
-/// FP8 1x128: lane covers 16 elements of a 512-element chunk; 8 lanes share a block scale.
-KIWI_DEV void quant_fp8_16(const uint4 (&in)[2], float& scale, uint4& out) {
-    float f[16];
-    float a[8];
-    bf16x8_to_f32(in[0], a);
-#pragma unroll
-    for (int i = 0; i < 8; ++i) f[i] = a[i];
-    bf16x8_to_f32(in[1], a);
-#pragma unroll
-    for (int i = 0; i < 8; ++i) f[8 + i] = a[i];
-    float amax = 0.f;
-#pragma unroll
-    for (int i = 0; i < 16; ++i) amax = fmaxf(amax, fabsf(f[i]));
-    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
-    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
-    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 4));
-    scale = amax > 0.f ? amax / kFp8Max : 1.0f;
-    const float inv = amax > 0.f ? kFp8Max / amax : 0.f;
-    uint16_t q[8];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-        q[i] = __nv_cvt_float2_to_fp8x2(make_float2(f[2 * i] * inv, f[2 * i + 1] * inv), __NV_SATFINITE, __NV_E4M3);
-    }
-    out = make_uint4(q[0] | (uint32_t(q[1]) << 16), q[2] | (uint32_t(q[3]) << 16), q[4] | (uint32_t(q[5]) << 16),
-                     q[6] | (uint32_t(q[7]) << 16));
-}
-
-KIWI_DEV void dequant_fp8_16(uint4 q, float scale, uint4 (&out)[2]) {
-    const uint16_t* p = reinterpret_cast<const uint16_t*>(&q);
-    float f[16];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-        const __half2_raw hr = __nv_cvt_fp8x2_to_halfraw2(static_cast<__nv_fp8x2_storage_t>(p[i]), __NV_E4M3);
-        const float2 t = __half22float2(*reinterpret_cast<const __half2*>(&hr));
-        f[2 * i] = t.x * scale;
-        f[2 * i + 1] = t.y * scale;
-    }
-    float a[8];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) a[i] = f[i];
-    out[0] = f32x8_to_bf16(a);
-#pragma unroll
-    for (int i = 0; i < 8; ++i) a[i] = f[8 + i];
-    out[1] = f32x8_to_bf16(a);
-}
-
-/// NVFP4: lane covers 16 elements = one 16-element block (e4m3 block scale,
-/// relative to a per-row fp32 scale so block scales stay in e4m3 range).
-KIWI_DEV void quant_fp4_16(const uint4 (&in)[2], float row_scale, uint8_t& sbyte, uint2& out) {
-    float f[16];
-    float a[8];
-    bf16x8_to_f32(in[0], a);
-#pragma unroll
-    for (int i = 0; i < 8; ++i) f[i] = a[i];
-    bf16x8_to_f32(in[1], a);
-#pragma unroll
-    for (int i = 0; i < 8; ++i) f[8 + i] = a[i];
-    float amax = 0.f;
-#pragma unroll
-    for (int i = 0; i < 16; ++i) amax = fmaxf(amax, fabsf(f[i]));
-    // block scale in e4m3 units of row_scale: s = amax / (6 * row_scale)
-    const float s = row_scale > 0.f ? amax / (kFp4Max * row_scale) : 0.f;
-    const __nv_fp8_storage_t sq = __nv_cvt_float_to_fp8(s, __NV_SATFINITE, __NV_E4M3);
-    const __half_raw sh = __nv_cvt_fp8_to_halfraw(sq, __NV_E4M3);
-    const float sdec = __half2float(*reinterpret_cast<const __half*>(&sh)) * row_scale;
-    const float inv = sdec > 0.f ? 1.0f / sdec : 0.f;
-    sbyte = sq;
-    uint8_t b[8];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-        b[i] = __nv_cvt_float2_to_fp4x2(make_float2(f[2 * i] * inv, f[2 * i + 1] * inv), __NV_E2M1, cudaRoundNearest);
-    }
-    out = make_uint2(b[0] | (uint32_t(b[1]) << 8) | (uint32_t(b[2]) << 16) | (uint32_t(b[3]) << 24),
-                     b[4] | (uint32_t(b[5]) << 8) | (uint32_t(b[6]) << 16) | (uint32_t(b[7]) << 24));
-}
-
-KIWI_DEV void dequant_fp4_16(uint2 q, float block_scale, uint4 (&out)[2]) {
-    const uint8_t* p = reinterpret_cast<const uint8_t*>(&q);
-    float f[16];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-        const __half2_raw hr = __nv_cvt_fp4x2_to_halfraw2(static_cast<__nv_fp4x2_storage_t>(p[i]), __NV_E2M1);
-        const float2 t = __half22float2(*reinterpret_cast<const __half2*>(&hr));
-        f[2 * i] = t.x * block_scale;
-        f[2 * i + 1] = t.y * block_scale;
-    }
-    float a[8];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) a[i] = f[i];
-    out[0] = f32x8_to_bf16(a);
-#pragma unroll
-    for (int i = 0; i < 8; ++i) a[i] = f[8 + i];
-    out[1] = f32x8_to_bf16(a);
 }
 
 template <int QUANT>
@@ -815,11 +698,14 @@ void launch_recv_count(const EpConfig& c, const p2p::HeapView& h, const EpWorksp
     KIWI_CUDA_CHECK(cudaGetLastError());
 }
 
-void launch_recv_scatter(const EpConfig& c, const p2p::HeapView& h, const EpWorkspace& ws, cudaStream_t s) {
+void launch_recv_assign(const EpConfig& c, const p2p::HeapView& h, const EpWorkspace& ws, cudaStream_t s) {
     const uint64_t assign_blocks = (c.slots() * 32 + kThreads - 1) / kThreads;
     const uint64_t cap = 8u * default_grid();
     recv_assign_kernel<<<static_cast<int>(assign_blocks < cap ? assign_blocks : cap), kThreads, 0, s>>>(c, h, ws);
     KIWI_CUDA_CHECK(cudaGetLastError());
+}
+
+void launch_recv_copy(const EpConfig& c, const p2p::HeapView& h, const EpWorkspace& ws, cudaStream_t s) {
     const int grid = 8 * default_grid();
     switch (static_cast<Quant>(c.quant)) {
         case Quant::kNone: recv_copy_kernel<0><<<grid, kThreads, 0, s>>>(c, h, ws); break;
@@ -827,6 +713,11 @@ void launch_recv_scatter(const EpConfig& c, const p2p::HeapView& h, const EpWork
         case Quant::kNvfp4: recv_copy_kernel<2><<<grid, kThreads, 0, s>>>(c, h, ws); break;
     }
     KIWI_CUDA_CHECK(cudaGetLastError());
+}
+
+void launch_recv_scatter(const EpConfig& c, const p2p::HeapView& h, const EpWorkspace& ws, cudaStream_t s) {
+    launch_recv_assign(c, h, ws, s);
+    launch_recv_copy(c, h, ws, s);
 }
 
 void launch_combine_send(const EpConfig& c, const p2p::HeapView& h, const __nv_bfloat16* y, const EpWorkspace& ws,

@@ -24,6 +24,7 @@
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
+#include "kiwi/ep/quant.cuh"
 #include "kiwi/gemm/grouped_gemm.hpp"
 #include "kiwi/p2p/driver.hpp"
 #include "kiwi/p2p/heap.hpp"
@@ -38,6 +39,13 @@ constexpr int kBK = 64;
 constexpr int kStages = 4;
 constexpr int kScatterStages = 4;
 constexpr int kThreads = 192;
+constexpr int kGatherThreads = 320;  // + 4 warps that gather and dequantise A
+constexpr int kGatherDepth = 3;      // cp.async staging entries per gathering thread
+
+/// Staged bytes per A row and k-block: FP8 64 data + 4 scale, NVFP4 32 data +
+/// 4 block scales (padded to 16-byte multiples for cp.async).
+template <int GQ>
+constexpr int gather_row_bytes() { return GQ == 1 ? 80 : (GQ == 2 ? 48 : 0); }
 
 enum Epi : int { kEpiStore = 0, kEpiSwiGLU = 1, kEpiScatter = 2 };
 
@@ -48,7 +56,7 @@ static_assert(kScatterMaxRanks == p2p::kMaxRanks, "ScatterArgs holds one base pe
 /// BN/2 columns (256 bytes each, 16-byte chunks XOR-swizzled by row so that
 /// both the row-per-thread writes and the row-wise reads are conflict-free),
 /// then the barriers.
-template <int BN, int STAGES = kStages, bool STAGING = false>
+template <int BN, int STAGES = kStages, bool STAGING = false, int GQ = -1>
 struct Smem {
     static constexpr int kABytes = kBM * kBK * 2;
     static constexpr int kBBytes = BN * kBK * 2;
@@ -56,7 +64,10 @@ struct Smem {
     static constexpr int kStgStride = BN;  // BN/2 bf16 columns = BN bytes per staged row
     static constexpr int kStgOffset = STAGES * kStageBytes;
     static constexpr int kStgBytes = STAGING ? 4 * 32 * kStgStride : 0;
-    static constexpr int kBarOffset = kStgOffset + kStgBytes;
+    static constexpr int kGRow = gather_row_bytes<GQ>();
+    static constexpr int kGStgOffset = kStgOffset + kStgBytes;
+    static constexpr int kGStgBytes = GQ >= 0 ? kGatherDepth * kBM * kGRow : 0;
+    static constexpr int kBarOffset = kGStgOffset + kGStgBytes;
     static constexpr int kBytes = kBarOffset + 256 + 1024;  // barriers + tmem slot + alignment slack
 };
 
@@ -93,12 +104,12 @@ __device__ __forceinline__ void store_row32(__nv_bfloat16* dst, const float (&v)
     for (int i = 0; i < 4; ++i) d[i] = out[i];
 }
 
-template <int BN, int EPI, int STAGES>
-__global__ void __launch_bounds__(kThreads, 1)
+template <int BN, int EPI, int STAGES, int GQ = -1>
+__global__ void __launch_bounds__(GQ >= 0 ? kGatherThreads : kThreads, 1)
     grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
-                        GroupedArgs p, const __grid_constant__ ScatterArgs sc) {
+                        GroupedArgs p, const __grid_constant__ ScatterArgs sc, const __grid_constant__ GatherArgs ga) {
     constexpr int kStages = STAGES;
-    using S = Smem<BN, STAGES, EPI == kEpiScatter>;
+    using S = Smem<BN, STAGES, EPI == kEpiScatter, GQ>;
     __shared__ uint8_t* s_base[kScatterMaxRanks];
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -121,7 +132,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (threadIdx.x == 0) {
         s_abort = 0;
         for (int s = 0; s < kStages; ++s) {
-            sm100::mbar_init(&full[s], 1);
+            // Gathered A: the TMA thread's arrival (B bytes) + one per A row.
+            sm100::mbar_init(&full[s], GQ >= 0 ? 1 + kBM : 1);
             sm100::mbar_init(&empty[s], 1);
         }
         for (int a = 0; a < 2; ++a) {
@@ -131,7 +143,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         sm100::fence_mbar_init();
     }
     if (warp == 0 && lane == 0) {
-        sm100::tma_prefetch_desc(&tmap_a);
+        if constexpr (GQ < 0) sm100::tma_prefetch_desc(&tmap_a);
         sm100::tma_prefetch_desc(&tmap_b);
     }
     if (warp == 1) sm100::tmem_alloc(tmem_slot, 2 * BN);
@@ -161,8 +173,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                     uint8_t* sa = smem + stage * S::kStageBytes;
                     uint8_t* sb = sa + S::kABytes;
-                    sm100::mbar_arrive_expect_tx(&full[stage], S::kStageBytes);
-                    sm100::tma_load_2d(sa, &tmap_a, &full[stage], kb * kBK, row0);
+                    if constexpr (GQ >= 0) {
+                        sm100::mbar_arrive_expect_tx(&full[stage], S::kBBytes);
+                    } else {
+                        sm100::mbar_arrive_expect_tx(&full[stage], S::kStageBytes);
+                        sm100::tma_load_2d(sa, &tmap_a, &full[stage], kb * kBK, row0);
+                    }
                     sm100::tma_load_2d(sb, &tmap_b, &full[stage], kb * kBK, brow0);
                     if (++stage == kStages) {
                         stage = 0;
@@ -215,6 +231,117 @@ __global__ void __launch_bounds__(kThreads, 1)
                     acc_phase ^= 1;
                 }
             }
+        }
+    } else if (warp >= 6) {
+        if constexpr (GQ >= 0) {
+            // Gathering A producer: thread r owns row r of every A tile.  Its
+            // cp.async copies of (row, k-block) run kGatherDepth - 1 items
+            // ahead of the dequantisation into the stage's swizzled A tile.
+            const int r = (warp - 6) * 32 + lane;
+            uint8_t* gstg = smem + S::kGStgOffset;
+            auto row_slot_of = [&](int tile) -> int64_t {
+                int g, mt, nt;
+                locate_tile(p.tile_prefix, p.num_groups, n_tiles, tile, g, mt, nt);
+                const int g_off = __ldg(&p.group_offset[g]);
+                const int rr = mt * kBM + r;
+                if (rr >= __ldg(&p.group_offset[g + 1]) - g_off || g_off + rr >= p.max_rows) return -1;
+                return __ldg(&ga.row_slot[g_off + rr]);
+            };
+            int i_tile = blockIdx.x, i_kb = 0;
+            int64_t i_slot = i_tile < total_tiles ? row_slot_of(i_tile) : -1;
+            uint32_t n_issued = 0;
+            auto issue = [&]() {
+                if (i_tile < total_tiles) {
+                    uint8_t* dst = gstg + (n_issued % kGatherDepth) * (kBM * S::kGRow) + r * S::kGRow;
+                    if (i_slot >= 0) {
+                        const uint8_t* row = ga.base + ga.off_row + static_cast<uint64_t>(i_slot) * ga.row_bytes;
+                        const uint8_t* scl = ga.base + ga.off_scale + static_cast<uint64_t>(i_slot) * ga.scale_bytes;
+                        if constexpr (GQ == 1) {
+#pragma unroll
+                            for (int j = 0; j < 4; ++j) sm100::cp_async_16(dst + 16 * j, row + i_kb * 64 + 16 * j);
+                            sm100::cp_async_4(dst + 64, scl + 4 * (i_kb / 2));
+                        } else {
+                            sm100::cp_async_16(dst, row + i_kb * 32);
+                            sm100::cp_async_16(dst + 16, row + i_kb * 32 + 16);
+                            sm100::cp_async_4(dst + 32, scl + 4 + 4 * i_kb);
+                        }
+                    }
+                    if (++i_kb == k_blocks) {
+                        i_kb = 0;
+                        i_tile += gridDim.x;
+                        i_slot = i_tile < total_tiles ? row_slot_of(i_tile) : -1;
+                    }
+                }
+                sm100::cp_async_commit();  // one group per item, empty at the tail
+                ++n_issued;
+            };
+#pragma unroll 1
+            for (int d = 0; d < kGatherDepth - 1; ++d) issue();
+            int stage = 0;
+            uint32_t phase = 0;
+            uint32_t n_done = 0;
+            bool ok = true;
+            for (int tile = blockIdx.x; ok && tile < total_tiles && !*reinterpret_cast<volatile int*>(&s_abort);
+                 tile += gridDim.x) {
+                const int64_t slot = row_slot_of(tile);
+                float row_scale = 1.0f;
+                if constexpr (GQ == 2) {
+                    if (slot >= 0) {
+                        row_scale = __ldg(reinterpret_cast<const float*>(
+                            ga.base + ga.off_scale + static_cast<uint64_t>(slot) * ga.scale_bytes));
+                    }
+                }
+#pragma unroll 1
+                for (int kb = 0; kb < k_blocks; ++kb) {
+                    issue();
+                    sm100::cp_async_wait<kGatherDepth - 1>();
+                    if (!sm100::mbar_wait(&empty[stage], phase ^ 1)) {
+                        fail(5);
+                        ok = false;
+                        break;
+                    }
+                    const uint8_t* src = gstg + (n_done % kGatherDepth) * (kBM * S::kGRow) + r * S::kGRow;
+                    uint4 out[8];
+                    if (slot < 0) {
+#pragma unroll
+                        for (int c = 0; c < 8; ++c) out[c] = make_uint4(0, 0, 0, 0);
+                    } else if constexpr (GQ == 1) {
+                        const float scl = *reinterpret_cast<const float*>(src + 64);
+#pragma unroll
+                        for (int j = 0; j < 4; ++j) {
+                            uint4 o[2];
+                            ep::dequant_fp8_16(*reinterpret_cast<const uint4*>(src + 16 * j), scl, o);
+                            out[2 * j] = o[0];
+                            out[2 * j + 1] = o[1];
+                        }
+                    } else {
+                        const uint32_t sbs = *reinterpret_cast<const uint32_t*>(src + 32);
+#pragma unroll
+                        for (int j = 0; j < 4; ++j) {
+                            const __half_raw sh =
+                                __nv_cvt_fp8_to_halfraw(static_cast<__nv_fp8_storage_t>((sbs >> (8 * j)) & 0xffu),
+                                                        __NV_E4M3);
+                            const float bs = __half2float(*reinterpret_cast<const __half*>(&sh)) * row_scale;
+                            uint4 o[2];
+                            ep::dequant_fp4_16(*reinterpret_cast<const uint2*>(src + 8 * j), bs, o);
+                            out[2 * j] = o[0];
+                            out[2 * j + 1] = o[1];
+                        }
+                    }
+                    // 128-byte swizzle: 16-byte chunk c of row r goes to chunk c ^ (r % 8).
+                    uint8_t* arow = smem + stage * S::kStageBytes + r * 128;
+#pragma unroll
+                    for (int c = 0; c < 8; ++c) *reinterpret_cast<uint4*>(arow + ((c ^ (r & 7)) * 16)) = out[c];
+                    sm100::fence_proxy_async_smem();
+                    sm100::mbar_arrive(&full[stage]);
+                    ++n_done;
+                    if (++stage == kStages) {
+                        stage = 0;
+                        phase ^= 1;
+                    }
+                }
+            }
+            sm100::cp_async_wait<0>();
         }
     } else {
         // Epilogue: warps 2..5; TMEM lane quadrant = warp % 4.
@@ -631,18 +758,19 @@ int num_sms() {
 
 namespace {
 
-template <int EPI, int STAGES>
+template <int EPI, int STAGES, int GQ = -1>
 void launch_grouped(const CUtensorMap& tmap_a, const CUtensorMap& tmap_b, const GroupedArgs& args,
-                    const ScatterArgs& sc, int grid, cudaStream_t stream) {
+                    const ScatterArgs& sc, int grid, cudaStream_t stream, const GatherArgs& ga = GatherArgs{}) {
     constexpr int BN = 256;
-    const int smem = Smem<BN, STAGES, EPI == kEpiScatter>::kBytes;
+    const int smem = Smem<BN, STAGES, EPI == kEpiScatter, GQ>::kBytes;
     static bool attr = false;
     if (!attr) {
-        KIWI_CUDA_CHECK(cudaFuncSetAttribute(grouped_gemm_kernel<BN, EPI, STAGES>,
+        KIWI_CUDA_CHECK(cudaFuncSetAttribute(grouped_gemm_kernel<BN, EPI, STAGES, GQ>,
                                              cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
         attr = true;
     }
-    grouped_gemm_kernel<BN, EPI, STAGES><<<grid, kThreads, smem, stream>>>(tmap_a, tmap_b, args, sc);
+    grouped_gemm_kernel<BN, EPI, STAGES, GQ>
+        <<<grid, GQ >= 0 ? kGatherThreads : kThreads, smem, stream>>>(tmap_a, tmap_b, args, sc, ga);
     KIWI_CUDA_CHECK(cudaGetLastError());
 }
 
@@ -661,6 +789,27 @@ void grouped_gemm(const CUtensorMap& tmap_a, const CUtensorMap& tmap_b, const Gr
     const ScatterArgs none{};
     if (swiglu) launch_grouped<kEpiSwiGLU, kStages>(tmap_a, tmap_b, args, none, grid, stream);
     else launch_grouped<kEpiStore, kStages>(tmap_a, tmap_b, args, none, grid, stream);
+}
+
+void grouped_gemm_gather(const CUtensorMap& tmap_b, const GroupedArgs& args, const GatherArgs& ga, int grid,
+                         cudaStream_t stream) {
+    check_shape(args);
+    if (!ga.base || !ga.row_slot) throw kiwi::error("grouped_gemm_gather: missing receive buffer or row slots");
+    if (ga.row_bytes % 16 || ga.off_row % 16 || ga.scale_bytes % 16 || ga.off_scale % 16) {
+        throw kiwi::error("grouped_gemm_gather: rows and scales must be 16-byte aligned");
+    }
+    if (grid <= 0) grid = num_sms();
+    const ScatterArgs none{};
+    // tmap_b stands in for the unused A map (the A tile is gathered).
+    if (ga.quant == 1) {
+        if (ga.row_bytes < args.k) throw kiwi::error("grouped_gemm_gather: FP8 rows shorter than K");
+        launch_grouped<kEpiSwiGLU, kStages, 1>(tmap_b, tmap_b, args, none, grid, stream, ga);
+    } else if (ga.quant == 2) {
+        if (ga.row_bytes * 2 < args.k) throw kiwi::error("grouped_gemm_gather: NVFP4 rows shorter than K");
+        launch_grouped<kEpiSwiGLU, kStages, 2>(tmap_b, tmap_b, args, none, grid, stream, ga);
+    } else {
+        throw kiwi::error("grouped_gemm_gather: quant must be 1 (FP8) or 2 (NVFP4)");
+    }
 }
 
 void grouped_gemm_scatter(const CUtensorMap& tmap_a, const CUtensorMap& tmap_b, const GroupedArgs& args,
@@ -714,6 +863,16 @@ KernelInfo gemm_kernel_info(bool swiglu) {
     if (swiglu) KIWI_CUDA_CHECK(cudaFuncGetAttributes(&a, grouped_gemm_kernel<256, kEpiSwiGLU, kStages>));
     else KIWI_CUDA_CHECK(cudaFuncGetAttributes(&a, grouped_gemm_kernel<256, kEpiStore, kStages>));
     return {static_cast<int>(a.localSizeBytes), a.numRegs, Smem<256>::kBytes};
+}
+
+KernelInfo gemm_gather_kernel_info(int quant) {
+    cudaFuncAttributes a{};
+    if (quant == 2) {
+        KIWI_CUDA_CHECK(cudaFuncGetAttributes(&a, grouped_gemm_kernel<256, kEpiSwiGLU, kStages, 2>));
+        return {static_cast<int>(a.localSizeBytes), a.numRegs, Smem<256, kStages, false, 2>::kBytes};
+    }
+    KIWI_CUDA_CHECK(cudaFuncGetAttributes(&a, grouped_gemm_kernel<256, kEpiSwiGLU, kStages, 1>));
+    return {static_cast<int>(a.localSizeBytes), a.numRegs, Smem<256, kStages, false, 1>::kBytes};
 }
 
 KernelInfo gemm_scatter_kernel_info() {

@@ -48,8 +48,15 @@ void launch_dispatch(const EpConfig& c, const p2p::HeapView& h, const __nv_bfloa
 void launch_recv_count(const EpConfig& c, const p2p::HeapView& h, const EpWorkspace& ws, uint64_t timeout_ns,
                        cudaStream_t s);
 
-/// Assigns expert-major rows, records the slot -> rows map and dequantises
-/// each received row into ws.a.
+/// Assigns expert-major rows: pair_slot / pair_w / pair_dst of every row and
+/// the slot -> rows map (slot_pos).
+void launch_recv_assign(const EpConfig& c, const p2p::HeapView& h, const EpWorkspace& ws, cudaStream_t s);
+
+/// Dequantises each received row into its expert-major rows of ws.a (not
+/// needed when GEMM1 gathers its A operand from the receive buffer).
+void launch_recv_copy(const EpConfig& c, const p2p::HeapView& h, const EpWorkspace& ws, cudaStream_t s);
+
+/// launch_recv_assign then launch_recv_copy.
 void launch_recv_scatter(const EpConfig& c, const p2p::HeapView& h, const EpWorkspace& ws, cudaStream_t s);
 
 /// Sums each slot's (already weighted) expert outputs y and stores the bf16

@@ -45,6 +45,23 @@ struct ScatterArgs {
     int32_t pad_;
 };
 
+/// Gathering A producer (fused EP receive -> GEMM1): expert-major row i of A is
+/// the dispatched row of slot row_slot[i], read in place from the receive
+/// buffer and dequantised to bf16 in shared memory.  quant 1: FP8 e4m3 rows
+/// of row_bytes at base + off_row + slot * row_bytes with fp32 scales per 128
+/// columns at base + off_scale + slot * scale_bytes; quant 2: NVFP4 (e2m1
+/// pairs per byte, an fp32 row scale then one e4m3 scale per 16 columns).
+struct GatherArgs {
+    const uint8_t* base;
+    const int32_t* row_slot;
+    uint64_t off_row;
+    uint64_t off_scale;
+    int32_t row_bytes;
+    int32_t scale_bytes;
+    int32_t quant;
+    int32_t pad_;
+};
+
 struct KernelInfo {
     int local_bytes;
     int registers;
@@ -76,7 +93,13 @@ void grouped_gemm_pair(const CUtensorMap& tmap_a, const CUtensorMap& tmap_b_half
 void grouped_gemm_scatter(const CUtensorMap& tmap_a, const CUtensorMap& tmap_b, const GroupedArgs& args,
                           const ScatterArgs& sc, int grid, cudaStream_t stream);
 
+/// GEMM1 with the SwiGLU epilogue whose A operand is gathered from the receive
+/// buffer (GatherArgs) instead of a dense bf16 matrix; tmap_b as grouped_gemm.
+void grouped_gemm_gather(const CUtensorMap& tmap_b, const GroupedArgs& args, const GatherArgs& ga, int grid,
+                         cudaStream_t stream);
+
 KernelInfo gemm_kernel_info(bool swiglu);
+KernelInfo gemm_gather_kernel_info(int quant);
 KernelInfo gemm_scatter_kernel_info();
 KernelInfo gemm_pair_kernel_info(bool swiglu);
 int num_sms();

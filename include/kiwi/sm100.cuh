@@ -82,6 +82,28 @@ KIWI_DEV void tma_load_2d(void* smem_dst, const CUtensorMap* map, uint64_t* bar,
         : "memory");
 }
 
+// ---- cp.async (LDGSTS): per-thread asynchronous global -> shared copies ----
+
+KIWI_DEV void cp_async_16(void* smem_dst, const void* gmem_src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(smem_dst)), "l"(gmem_src) : "memory");
+}
+
+KIWI_DEV void cp_async_4(void* smem_dst, const void* gmem_src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_addr(smem_dst)), "l"(gmem_src) : "memory");
+}
+
+KIWI_DEV void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+
+/// Waits until at most N of this thread's committed cp.async groups are pending.
+template <int N>
+KIWI_DEV void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+/// Makes this thread's generic-proxy shared-memory writes visible to the async
+/// proxy (tcgen05.mma operand reads) before it signals an mbarrier.
+KIWI_DEV void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
 // ---- tcgen05 / TMEM ----
 
 /// Allocates `ncols` TMEM columns (power of two >= 32); the address lands in *smem_slot.

@@ -10,8 +10,11 @@ stream and without host synchronisation:
 2. dispatch: 1x128 FP8 (or NVFP4 / bf16) quantisation fused with 16-byte
    NVLink stores into every destination rank's receive slots, deduplicated
    per destination rank, one release flag per source rank;
-3. receive: per-expert counts, expert-major layout, dequantisation to bf16;
-4. experts: tcgen05 grouped GEMM (SwiGLU fused) then grouped GEMM whose
+3. receive: per-expert counts and the expert-major row assignment;
+4. experts: tcgen05 grouped GEMM (SwiGLU fused) whose A tiles are gathered
+   from the receive slots and dequantised to bf16 in shared memory by
+   producer warps (``native.gather_a = False``: a receive kernel writes
+   expert-major bf16 rows first and TMA loads them), then grouped GEMM whose
    epilogue multiplies by the routing weight and stores every row straight
    into its token owner's top-k slot over NVLink (fused combine; the last CTA
    signals every rank), bf16 compute with fp32 accumulation;
@@ -142,6 +145,9 @@ class EpDispatchCombine:
         # The caller supplies expert outputs as rows: combine sends them with the
         # combine-send kernel, not through the fused GEMM2 epilogue.
         self.moe.native.fused_combine = False
+        # dispatch() returns the expert-major bf16 rows, so the receive side
+        # must materialise them (GEMM1's in-place gather skips that copy).
+        self.moe.native.gather_a = False
         self._idx = None
 
     def dispatch(self, x, weights, indices):

@@ -26,14 +26,17 @@ def _check(layer, cfg, x, logits, out, rel=2e-2):
     assert err <= rel * scale + 1e-3, (err, scale)
 
 
-@pytest.mark.parametrize("fused", [True, False])
+@pytest.mark.parametrize("fused,gather", [(True, True), (False, True), (True, False), (False, False)])
 @pytest.mark.parametrize("quant", ["fp8", "nvfp4", "none"])
-def test_layer_matches_reference(quant, fused):
+def test_layer_matches_reference(quant, fused, gather):
     """fused=True: GEMM2's epilogue stores the weighted rows into the token
-    owners' top-k slots (fused combine); False: GEMM2, combine send, receive."""
+    owners' top-k slots (fused combine); False: GEMM2, combine send, receive.
+    gather=True: GEMM1 gathers and dequantises its A rows from the receive
+    slots; False: expert-major bf16 rows are written first, TMA loads them."""
     cfg = small_cfg(quant)
     layer = ExpertParallelMoE(cfg)
     layer.native.fused_combine = fused
+    layer.native.gather_a = gather
     # NVFP4 keeps one mantissa bit: a single rounding disagreement between two
     # correct quantisers moves an output by a visible fraction of its range.
     rel = 5e-2 if quant == "nvfp4" else 2e-2
@@ -43,12 +46,43 @@ def test_layer_matches_reference(quant, fused):
         _check(layer, cfg, x, logits, out, rel)
 
 
+def _hidden_by_row(layer, cfg):
+    """GEMM1 output rows keyed by (local expert, source slot), sorted: row
+    order inside an expert follows atomics and may differ between rounds."""
+    n = int(layer.expert_counts.sum().item())
+    offs = layer.native.expert_offsets.long()
+    pos = torch.arange(n, device=offs.device)
+    expert = torch.searchsorted(offs[1:], pos, right=True)
+    key = expert * (1 << 32) + layer.native.pair_slot[:n].long()
+    order = torch.argsort(key)
+    return key[order], layer.native.expert_hidden[:n][order].clone()
+
+
+@pytest.mark.parametrize("quant", ["fp8", "nvfp4"])
+def test_gathered_gemm1_equals_materialised_rows(quant):
+    """GEMM1 fed by the gathering producer (dequantised in shared memory)
+    gives bit-identical rows to GEMM1 over the receive kernel's bf16 rows."""
+    cfg = small_cfg(quant, tokens=200, zipf=1.2)
+    layer = ExpertParallelMoE(cfg)
+    x, logits = moe.synthetic_inputs(cfg, 0, "cuda")
+    out = {}
+    for gather in (False, True):
+        layer.native.gather_a = gather
+        layer(x, logits)
+        torch.cuda.synchronize()
+        layer.check()
+        out[gather] = _hidden_by_row(layer, cfg)
+    assert torch.equal(out[False][0], out[True][0])
+    assert torch.equal(out[False][1], out[True][1])
+
+
 @pytest.mark.parametrize("quant", ["fp8", "nvfp4", "none"])
 def test_dispatched_rows_match_reference_quantisation(quant):
     """Each expert-major row the receive side produced equals the reference
     quantise-dequantise of its source token (bf16-rounded)."""
     cfg = small_cfg(quant, tokens=64)
     layer = ExpertParallelMoE(cfg)
+    layer.native.gather_a = False  # materialise the expert-major rows
     x, logits = moe.synthetic_inputs(cfg, 0, "cuda")
     layer(x, logits)
     torch.cuda.synchronize()
