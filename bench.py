@@ -50,8 +50,8 @@ def parse():
     ap.add_argument("--latency-tokens", type=int, default=128)
     ap.add_argument("--invoke-iters", type=int, default=200000)
     ap.add_argument("--no-e2e", action="store_true")
-    ap.add_argument("--no-gather", action="store_true",
-                    help="receive kernel writes expert-major bf16 rows for GEMM1 (comparison only)")
+    ap.add_argument("--gather", action="store_true",
+                    help="GEMM1 gathers its A rows from the receive slots (opt-in, comparison only)")
     ap.add_argument("--unfused-combine", action="store_true",
                     help="GEMM2 to local memory + combine send/receive kernels (comparison only)")
     return ap.parse_args()
@@ -95,7 +95,7 @@ def main():
 
         layer = ExpertParallelMoE(cfg, max_tokens=max(T, args.latency_tokens))
         layer.native.fused_combine = not args.unfused_combine
-        layer.native.gather_a = not args.no_gather
+        layer.native.gather_a = args.gather
     else:
         from kiwi_b200.parallel.baseline import NcclMoEBaseline
 
@@ -212,10 +212,10 @@ def main():
             "tflops_per_gpu": flops / (ms / 1e3) / 1e12,
             "clocks": {"sm_mhz": clk["sm_mhz"], "sm_max_mhz": clk["sm_max_mhz"], "reasons": clk["reasons"],
                        "samples": clk["samples"]},
-            "e2e": e2e, "gpu_launches": kernels_per_step(not args.unfused_combine, not args.no_gather) * args.steps
+            "e2e": e2e, "gpu_launches": kernels_per_step(not args.unfused_combine, args.gather) * args.steps
             if args.impl == "kiwi" else None,
             "fused_combine": (not args.unfused_combine) if args.impl == "kiwi" else None,
-            "gather_a": (not args.no_gather) if args.impl == "kiwi" else None,
+            "gather_a": args.gather if args.impl == "kiwi" else None,
             "latency_mode": lat, "invoke_rtt": invoke, "impl": args.impl,
         }
         emit(line)

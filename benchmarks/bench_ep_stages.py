@@ -3,9 +3,9 @@
     python benchmarks/bench_ep_stages.py [--config deepseek_fp8] [--tokens 4096] [--steps 10]
     torchrun --nproc-per-node N --master-addr 127.0.0.1 benchmarks/bench_ep_stages.py ...
 
-Stages: route, dispatch (+begin), receive (count, schedules, assign; + copy
-with --no-gather), gemm1 (gate/up + SwiGLU; by default its A rows are gathered
-and dequantised from the receive slots), gemm2 (down projection; with the fused combine its
+Stages: route, dispatch (+begin), receive (count, schedules, assign, copy;
+no copy with --gather), gemm1 (gate/up + SwiGLU; with --gather its A rows are
+gathered and dequantised from the receive slots), gemm2 (down projection; with the fused combine its
 epilogue also stores the rows over NVLink), combine (fused: wait + top-k sum;
 --unfused: send + reduce).  A stage that waits for other ranks includes their
 skew.  Prints one RESULT JSON line.
@@ -30,7 +30,7 @@ def main():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--experts", type=int, default=None, help="override the expert count (small profiling cases)")
     ap.add_argument("--unfused", action="store_true", help="GEMM2 to local memory + combine send/receive")
-    ap.add_argument("--no-gather", action="store_true", help="receive kernel writes bf16 rows; GEMM1 loads them by TMA")
+    ap.add_argument("--gather", action="store_true", help="GEMM1 gathers its A rows from the receive slots")
     args = ap.parse_args()
     rank, world = kdist.init()
     cfg = moe_model.CONFIGS[args.config]
@@ -40,7 +40,7 @@ def main():
         cfg = moe_model.MoEConfig(**{**cfg.__dict__, "num_experts": args.experts})
     layer = ExpertParallelMoE(cfg)
     layer.native.fused_combine = not args.unfused
-    layer.native.gather_a = not args.no_gather
+    layer.native.gather_a = args.gather
     x, logits = moe_model.synthetic_inputs(cfg, rank, "cuda")
     out = torch.empty_like(x)
     names = ["route", "dispatch", "receive", "gemm1", "gemm2", "combine"]
@@ -71,7 +71,7 @@ def main():
     counts = layer.expert_counts.float()
     if rank == 0:
         print("RESULT " + json.dumps({"bench": "ep_stages_us", "config": args.config, "world": world,
-                                      "fused_combine": not args.unfused, "gather_a": not args.no_gather,
+                                      "fused_combine": not args.unfused, "gather_a": args.gather,
                                       "tokens_per_rank": cfg.tokens_per_rank, **res,
                                       "total_us": sum(res.values()),
                                       "rows_per_expert_mean": float(counts.mean()),

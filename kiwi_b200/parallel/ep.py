@@ -10,11 +10,12 @@ stream and without host synchronisation:
 2. dispatch: 1x128 FP8 (or NVFP4 / bf16) quantisation fused with 16-byte
    NVLink stores into every destination rank's receive slots, deduplicated
    per destination rank, one release flag per source rank;
-3. receive: per-expert counts and the expert-major row assignment;
-4. experts: tcgen05 grouped GEMM (SwiGLU fused) whose A tiles are gathered
-   from the receive slots and dequantised to bf16 in shared memory by
-   producer warps (``native.gather_a = False``: a receive kernel writes
-   expert-major bf16 rows first and TMA loads them), then grouped GEMM whose
+3. receive: per-expert counts, the expert-major row assignment and the
+   dequantised bf16 expert-major rows;
+4. experts: tcgen05 grouped GEMM (SwiGLU fused) over the expert-major rows
+   (TMA-fed; ``native.gather_a = True`` instead gathers and dequantises the A
+   tiles straight from the receive slots in producer warps, which skips the
+   copy but measured slower), then grouped GEMM whose
    epilogue multiplies by the routing weight and stores every row straight
    into its token owner's top-k slot over NVLink (fused combine; the last CTA
    signals every rank), bf16 compute with fp32 accumulation;
