@@ -75,6 +75,14 @@ void register_p2p(py::module_& m) {
              py::arg("cpus") = std::vector<int>{})
         .def("join_proxy_threads", &Context::join_proxy_threads, py::call_guard<py::gil_scoped_release>())
         .def_property_readonly("copies_issued", &Context::copies_issued)
+        .def("ce_pingpong",
+             [](Context& c, int peer, bool initiator, uint64_t bytes, uint32_t iters, uint32_t warmup,
+                uint64_t src_off, uint64_t dst_off, uint64_t flag_off, torch::Tensor lat, torch::Tensor status,
+                uint64_t timeout_ns) {
+                 if (lat.numel() < iters) throw kiwi::error("ce_pingpong: lat needs iters entries");
+                 launch_ce_pingpong(c.device_context(), peer, initiator, bytes, iters, warmup, src_off, dst_off,
+                                    flag_off, u64_ptr(lat), u32_ptr(status), timeout_ns, cur_stream());
+             })
         .def("ce_put_selftest",
              [](Context& c, int dst, uint64_t src_off, uint64_t dst_off, uint64_t bytes, uint32_t n,
                 uint64_t flag_off, uint64_t counter_off, torch::Tensor status, uint64_t timeout_ns) {
@@ -142,6 +150,9 @@ void register_p2p(py::module_& m) {
              },
              py::arg("peer"), py::arg("bytes"), py::arg("reps"), py::arg("src_off"), py::arg("dst_off"),
              py::arg("lat"), py::arg("max_blocks"), py::arg("region") = 0)
+        .def("host_ce_pingpong", &host_ce_pingpong, py::arg("peer"), py::arg("initiator"), py::arg("bytes"),
+             py::arg("iters"), py::arg("warmup"), py::arg("src_off"), py::arg("dst_off"), py::arg("flag_off"),
+             py::arg("timeout_s") = 10.0, py::call_guard<py::gil_scoped_release>())
         .def("all2all_rounds",
              [](SymmetricHeap& h, uint64_t ingress_off, std::optional<torch::Tensor> send,
                 std::optional<torch::Tensor> recv, torch::Tensor epoch, torch::Tensor status, uint64_t timeout_ns,

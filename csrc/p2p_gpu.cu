@@ -374,6 +374,64 @@ __global__ void ce_put_selftest_kernel(GContext ctx, int dst, uint64_t src_off, 
     }
 }
 
+/// Copy-engine ping-pong (the B200 counterpart of the reference's invoke ->
+/// host SDMA ping-pong, examples/invoke/invoke_sdma_ping_pong.hip.cpp:501-553):
+/// in round i the initiator's warp posts a copy-engine put of `bytes` to the
+/// peer with flag value i (a proxy thread issues cudaMemcpyAsync and the flag
+/// write on its copy stream), then waits for the peer's put back; the
+/// responder waits for round i and answers the same way.  lat_ns[i - warmup]
+/// = the initiator's round trip (device %globaltimer).
+__global__ void ce_pingpong_kernel(GContext ctx, int peer, int initiator, uint64_t bytes, uint32_t iters,
+                                   uint32_t warmup, uint64_t src_off, uint64_t dst_off, uint64_t flag_off,
+                                   uint64_t* lat_ns, uint32_t* status, uint64_t timeout_ns) {
+    GHandle g(ctx, 0);
+    auto put_back = [&](uint32_t i) {
+        CePutDesc d{};
+        d.dst_rank = static_cast<uint32_t>(peer);
+        d.flag_rank = static_cast<uint32_t>(peer);
+        d.dst_off = dst_off;
+        d.src_off = src_off;
+        d.bytes = bytes;
+        d.flag_off = flag_off;
+        d.flag_value = i;
+        d.counter_off = flag_off + 8;  // local completion counter (unused by the ping-pong)
+        d.counter_value = 0;
+        return g.post_ce_put(d, timeout_ns);
+    };
+    for (uint32_t i = 1; i <= iters + warmup; ++i) {
+        const uint64_t t0 = ptx::globaltimer();
+        if (initiator) {
+            if (put_back(i) != Status::kOk) {
+                if (ptx::lane_id() == 0) status[0] = 1;
+                return;
+            }
+        }
+        if (g.wait_local(flag_off, Cmp::kGe, i, timeout_ns) != Status::kOk) {
+            if (ptx::lane_id() == 0) {
+                status[0] = 2;
+                status[1] = i;
+            }
+            return;
+        }
+        if (!initiator) {
+            if (put_back(i) != Status::kOk) {
+                if (ptx::lane_id() == 0) status[0] = 3;
+                return;
+            }
+        } else if (i > warmup && ptx::lane_id() == 0) {
+            lat_ns[i - 1 - warmup] = ptx::globaltimer() - t0;
+        }
+    }
+}
+
+void launch_ce_pingpong(const GContext& ctx, int peer, bool initiator, uint64_t bytes, uint32_t iters,
+                        uint32_t warmup, uint64_t src_off, uint64_t dst_off, uint64_t flag_off, uint64_t* lat_ns,
+                        uint32_t* status, uint64_t timeout_ns, cudaStream_t s) {
+    ce_pingpong_kernel<<<1, 32, 0, s>>>(ctx, peer, initiator ? 1 : 0, bytes, iters, warmup, src_off, dst_off,
+                                        flag_off, lat_ns, status, timeout_ns);
+    KIWI_CUDA_CHECK(cudaGetLastError());
+}
+
 void launch_ce_put_selftest(const GContext& ctx, int dst, uint64_t src_off, uint64_t dst_off, uint64_t bytes,
                             uint32_t n, uint64_t flag_off, uint64_t counter_off, uint32_t* status,
                             uint64_t timeout_ns, cudaStream_t s) {

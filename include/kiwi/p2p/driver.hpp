@@ -29,6 +29,7 @@ struct Driver {
     PFN_cuGetErrorString_v6000 cuGetErrorString = nullptr;
     PFN_cuCtxGetCurrent_v4000 cuCtxGetCurrent = nullptr;
     PFN_cuStreamWriteValue64_v11070 cuStreamWriteValue64 = nullptr;
+    PFN_cuStreamWaitValue64_v11070 cuStreamWaitValue64 = nullptr;
 };
 
 /// Loads the entry points once (throws kiwi::error if the driver lacks one).

@@ -1,6 +1,8 @@
 // Host launchers for the kiwi::p2p kernels (csrc/p2p_gpu.cu).
 #pragma once
 
+#include <vector>
+
 #include <cuda_runtime.h>
 
 #include "kiwi/p2p/context.hpp"
@@ -56,5 +58,18 @@ void launch_coll_wait_only(const HeapView& h, uint64_t ingress_off, uint32_t epo
 /// Cooperative launch of the grid-barrier self test.
 void launch_grid_barrier_test(unsigned long long* word, uint32_t* data, uint32_t blocks, uint32_t rounds,
                               uint32_t* status, uint64_t timeout_ns, uint64_t* elapsed_ns, cudaStream_t s);
+
+/// Copy-engine ping-pong through the control plane (see csrc/p2p_gpu.cu).
+void launch_ce_pingpong(const GContext& ctx, int peer, bool initiator, uint64_t bytes, uint32_t iters,
+                        uint32_t warmup, uint64_t src_off, uint64_t dst_off, uint64_t flag_off, uint64_t* lat_ns,
+                        uint32_t* status, uint64_t timeout_ns, cudaStream_t s);
+
+/// Host-initiated copy-engine ping-pong (no kernel): a CPU thread issues
+/// cudaMemcpyAsync into the peer's heap and the peer flag write, then a
+/// stream wait on its own flag; returns per-round CPU round-trip ns
+/// (initiator) and throws on a timeout.
+std::vector<uint64_t> host_ce_pingpong(SymmetricHeap& heap, int peer, bool initiator, uint64_t bytes, uint32_t iters,
+                                       uint32_t warmup, uint64_t src_off, uint64_t dst_off, uint64_t flag_off,
+                                       double timeout_s);
 
 }  // namespace kiwi::p2p

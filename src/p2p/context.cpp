@@ -86,3 +86,82 @@ GContext Context::device_context() const {
 }
 
 }  // namespace kiwi::p2p
+
+// ---------------------------------------------------------------------------
+// Host-initiated copy-engine ping-pong (the "host" mode of the reference's
+// SDMA ping-pong example, examples/invoke/README.md): no kernel; the CPU
+// thread of each rank issues the copy and the peer's flag write on its own
+// stream and makes the stream wait (cuStreamWaitValue64) for its own flag.
+// ---------------------------------------------------------------------------
+#include <chrono>
+
+#include "kiwi/p2p/p2p_ops.hpp"
+
+namespace kiwi::p2p {
+
+std::vector<uint64_t> host_ce_pingpong(SymmetricHeap& heap, int peer, bool initiator, uint64_t bytes, uint32_t iters,
+                                       uint32_t warmup, uint64_t src_off, uint64_t dst_off, uint64_t flag_off,
+                                       double timeout_s) {
+    const HeapView& v = heap.view();
+    if (peer < 0 || peer >= v.world || src_off + bytes > v.size || dst_off + bytes > v.size || flag_off + 8 > v.size) {
+        throw kiwi::error("host_ce_pingpong: arguments outside the heap");
+    }
+    const Driver& drv = driver();
+    cudaStream_t st;
+    KIWI_CUDA_CHECK(cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking));
+    auto cs = reinterpret_cast<CUstream>(st);
+    auto put = [&](uint64_t value) {
+        if (bytes) {
+            KIWI_CUDA_CHECK(cudaMemcpyAsync(v.base[peer] + dst_off, v.base[v.rank] + src_off, bytes,
+                                            cudaMemcpyDeviceToDevice, st));
+        }
+        check_cu(drv.cuStreamWriteValue64(cs, reinterpret_cast<CUdeviceptr>(v.base[peer] + flag_off), value,
+                                          CU_STREAM_WRITE_VALUE_DEFAULT),
+                 "cuStreamWriteValue64");
+    };
+    auto wait_own = [&](uint64_t value) {
+        check_cu(drv.cuStreamWaitValue64(cs, reinterpret_cast<CUdeviceptr>(v.base[v.rank] + flag_off), value,
+                                         CU_STREAM_WAIT_VALUE_GEQ),
+                 "cuStreamWaitValue64");
+        // Bounded host wait: poll the stream instead of blocking forever.
+        const auto end = std::chrono::steady_clock::now() + std::chrono::duration<double>(timeout_s);
+        while (true) {
+            const cudaError_t q = cudaStreamQuery(st);
+            if (q == cudaSuccess) return;
+            if (q != cudaErrorNotReady) KIWI_CUDA_CHECK(q);
+            if (std::chrono::steady_clock::now() > end) {
+                // Release the stream's wait ourselves so nothing stays queued
+                // behind it, then report.
+                cudaStream_t rel;
+                KIWI_CUDA_CHECK(cudaStreamCreateWithFlags(&rel, cudaStreamNonBlocking));
+                check_cu(drv.cuStreamWriteValue64(reinterpret_cast<CUstream>(rel),
+                                                  reinterpret_cast<CUdeviceptr>(v.base[v.rank] + flag_off), value,
+                                                  CU_STREAM_WRITE_VALUE_DEFAULT),
+                         "cuStreamWriteValue64(release)");
+                KIWI_CUDA_CHECK(cudaStreamSynchronize(rel));
+                KIWI_CUDA_CHECK(cudaStreamSynchronize(st));
+                cudaStreamDestroy(rel);
+                cudaStreamDestroy(st);
+                throw kiwi::error("host_ce_pingpong: the peer's flag did not arrive in time");
+            }
+        }
+    };
+    std::vector<uint64_t> lat;
+    lat.reserve(iters);
+    for (uint32_t i = 1; i <= iters + warmup; ++i) {
+        const auto t0 = std::chrono::steady_clock::now();
+        if (initiator) put(i);
+        wait_own(i);
+        if (!initiator) {
+            put(i);
+        } else if (i > warmup) {
+            lat.push_back(static_cast<uint64_t>(
+                std::chrono::duration_cast<std::chrono::nanoseconds>(std::chrono::steady_clock::now() - t0).count()));
+        }
+    }
+    KIWI_CUDA_CHECK(cudaStreamSynchronize(st));
+    KIWI_CUDA_CHECK(cudaStreamDestroy(st));
+    return lat;
+}
+
+}  // namespace kiwi::p2p

@@ -48,6 +48,7 @@ const Driver& driver() {
         load(d.cuGetErrorString, "cuGetErrorString", 6000);
         load(d.cuCtxGetCurrent, "cuCtxGetCurrent", 4000);
         load(d.cuStreamWriteValue64, "cuStreamWriteValue64", 11070);
+        load(d.cuStreamWaitValue64, "cuStreamWaitValue64", 11070);
     });
     return d;
 }

@@ -101,6 +101,21 @@ def _collectives(rank, world):
     assert int(coll.epoch.item()) == 3 * 80
 
 
+def _ce_pingpong_example(rank, world):
+    import importlib.util
+    import pathlib
+
+    path = pathlib.Path(__file__).resolve().parent.parent / "examples" / "python" / "ce_pingpong.py"
+    spec = importlib.util.spec_from_file_location("ce_pingpong_example", path)
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    rows = mod.run([8, 4096, 1 << 20], iters=20, warmup=3)
+    for r in rows:
+        assert r["device_ok"] and r["invoke_ok"] and r["host_ok"], r
+        if rank == 0:
+            assert r["device_oneway_us"] > 0 and r["invoke_oneway_us"] > 0 and r["host_oneway_us"] > 0, r
+
+
 def _nvls(rank, world):
     import kiwi_b200
     from kiwi_b200.parallel.p2p import SymmetricHeap
@@ -151,6 +166,12 @@ def test_device_collectives_4():
     if _ngpu() < 4:
         pytest.skip("needs 4 GPUs")
     _run(_collectives, 4)
+
+
+def test_ce_pingpong_example_2():
+    """examples/python/ce_pingpong.py: device NVLink, invoke -> copy engine and
+    host copy-engine ping-pongs, data checked in both directions."""
+    _run(_ce_pingpong_example, 2)
 
 
 def test_nvls_allreduce_2():
