@@ -531,6 +531,7 @@ PYBIND11_MODULE(_C, m) {
     t.def("parse_cpulist", &topology::parse_cpulist);
     t.def("gpu_local_cpus", &topology::gpu_local_cpus, py::arg("device"), py::arg("sysfs_root") = "/sys");
     t.def("process_cpus", &topology::process_cpus);
+    t.def("poller_cpus", &topology::poller_cpus, py::arg("device"), py::arg("n"), py::arg("sysfs_root") = "/sys");
     t.def("bind_current_thread", &topology::bind_current_thread);
     t.def("gpu_numa_node", &topology::gpu_numa_node, py::arg("device"), py::arg("sysfs_root") = "/sys");
 

@@ -74,9 +74,7 @@ int pick_cpu(int cpu) {
     if (cpu >= 0) return cpu;
     int dev = 0;
     cudaGetDevice(&dev);
-    const auto cpus = topology::gpu_local_cpus(dev);
-    // Avoid core 0 (interrupts); take the second local core when there is one.
-    if (cpus.size() > 1) return cpus[1];
+    const auto cpus = topology::poller_cpus(dev, 1);
     return cpus.empty() ? -1 : cpus[0];
 }
 
@@ -917,9 +915,7 @@ ThroughputResult invoke_throughput(uint32_t endpoints, uint32_t threads, uint32_
     kiwi::invoke::ProgressThreads<SPSCD2HQueue> pt(ctx);
     int dev = 0;
     cudaGetDevice(&dev);
-    auto cpus = topology::gpu_local_cpus(dev);
-    if (cpus.size() > 1) cpus.erase(cpus.begin());
-    pt.start(threads, cpus);
+    pt.start(threads, topology::poller_cpus(dev, threads));
     invoke_throughput_kernel<<<endpoints, 32>>>(ctx.device_context(), cb, msgs_per_endpoint, payload_bytes / 8, t.p,
                                                 status.p, 2000000000ull);
     KIWI_CUDA_CHECK(cudaGetLastError());

@@ -23,6 +23,14 @@ std::vector<int> parse_cpulist(const std::string& s);
 /// whole process mask when sysfs gives nothing.  `sysfs_root` is for tests.
 std::vector<int> gpu_local_cpus(int device, const std::string& sysfs_root = "/sys");
 
+/// Cores for `n` busy-polling host threads (progress / proxy threads) that
+/// serve `device`: the GPU's local CPUs without core 0 (left to the OS) when
+/// there are others, starting at offset device * n.  Processes that drive
+/// different GPUs sharing one CPU list (a single-node VM reports the same list
+/// for every GPU) then pin their pollers to different cores: two spinning
+/// pollers on one core time-share it in scheduler slices of milliseconds.
+std::vector<int> poller_cpus(int device, size_t n, const std::string& sysfs_root = "/sys");
+
 /// CPUs in this process's affinity mask.
 std::vector<int> process_cpus();
 

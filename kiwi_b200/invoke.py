@@ -60,8 +60,7 @@ class Context:
             if not self._ctx.host_only:
                 import torch
 
-                local = _C.topology.gpu_local_cpus(torch.cuda.current_device())
-                cpus = local[1:] + local[:1] if len(local) > 1 else local
+                cpus = _C.topology.poller_cpus(torch.cuda.current_device(), num_threads)
         self._ctx.start_progress_threads(num_threads, list(cpus))
         return self
 

@@ -80,6 +80,16 @@ std::vector<int> gpu_local_cpus(int device, const std::string& sysfs_root) {
     return out.empty() ? allowed : out;
 }
 
+std::vector<int> poller_cpus(int device, size_t n, const std::string& sysfs_root) {
+    std::vector<int> local = gpu_local_cpus(device, sysfs_root);
+    if (local.size() > 1 && local.front() == 0) local.erase(local.begin());
+    std::vector<int> out;
+    if (local.empty() || n == 0) return out;
+    const size_t start = (static_cast<size_t>(device < 0 ? 0 : device) * n) % local.size();
+    for (size_t t = 0; t < n; ++t) out.push_back(local[(start + t) % local.size()]);
+    return out;
+}
+
 bool bind_current_thread(const std::vector<int>& cpus) {
     if (cpus.empty()) return false;
     cpu_set_t set;

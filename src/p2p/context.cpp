@@ -63,10 +63,7 @@ void Context::host_signal(const HostSignalDesc& d) {
 }
 
 void Context::spawn_proxy_threads(size_t n, std::vector<int> cpus) {
-    if (cpus.empty()) {
-        cpus = topology::gpu_local_cpus(device_);
-        if (cpus.size() > 1) cpus.erase(cpus.begin());  // keep core 0 for the OS
-    }
+    if (cpus.empty()) cpus = topology::poller_cpus(device_, n);
     threads_->start(n, cpus);
 }
 
