@@ -13,6 +13,7 @@
 
 #include "kiwi/ep/config.hpp"
 #include "kiwi/ep/kernels.hpp"
+#include "kiwi/ep/tuning.hpp"
 #include "kiwi/gemm/grouped_gemm.hpp"
 #include "kiwi/p2p/heap.hpp"
 
@@ -61,9 +62,22 @@ py::dict config_to_dict(const ep::EpConfig& c) {
     d["off_row"] = c.off_row;
     d["off_scale"] = c.off_scale;
     d["off_comb"] = c.off_comb;
+    d["off_combk"] = c.off_combk;
     d["heap_bytes"] = c.heap_bytes;
     d["max_pairs"] = c.max_pairs();
     d["local_per_token"] = c.local_per_token();
+    return d;
+}
+
+py::dict tuning_dict(const ep::EpTuning& t) {
+    py::dict d;
+    d["dispatch_blocks"] = t.dispatch_blocks;
+    d["recv_blocks"] = t.recv_blocks;
+    d["combine_blocks"] = t.combine_blocks;
+    d["fused_combine"] = t.fused_combine;
+    d["gather_a"] = t.gather_a;
+    d["gemm_pair"] = t.gemm_pair;
+    d["source"] = t.source;
     return d;
 }
 
@@ -127,10 +141,10 @@ public:
         tmap_a2_ = gemm::make_tmap_bf16_2d(h_.data_ptr(), pairs, ffn, 128);
         tmap_b2_ = gemm::make_tmap_bf16_2d(w2.data_ptr(), w2.size(0), ffn, 256);
         tmap_b2h_ = gemm::make_tmap_bf16_2d(w2.data_ptr(), w2.size(0), ffn, 128);
-        // The 2-SM (256-row tile) GEMM measured no faster than the 1-SM kernel
-        // at the EP shapes (1.39 vs 1.35 ms GEMM1, 0.76 vs 0.75 ms GEMM2 at
-        // 1024 rows per expert), so it is opt-in (gemm_pair).
-        pair_ = false;
+        tuning_ = ep::tune(cfg_, gemm::num_sms());
+        pair_ = tuning_.gemm_pair;
+        fused_ = tuning_.fused_combine;
+        gather_ = tuning_.gather_a;
     }
 
     // ---- stages (all on the current stream) ----
@@ -146,7 +160,8 @@ public:
         cudaStream_t s = cur_stream();
         ep::launch_begin(cfg_, ws_, s);
         ep::launch_dispatch(cfg_, heap_.view(), reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()),
-                            idx.data_ptr<int32_t>(), w.data_ptr<float>(), static_cast<int>(x.size(0)), ws_, 0, s);
+                            idx.data_ptr<int32_t>(), w.data_ptr<float>(), static_cast<int>(x.size(0)), ws_,
+                            tuning_.dispatch_blocks, s);
     }
 
     void receive() {
@@ -156,8 +171,8 @@ public:
         gemm::build_schedule(ws_.expert_count, cfg_.experts_per_rank, static_cast<int>(2 * ffn_), 256, ws_.offsets,
                              ws_.tiles1, s, bm);
         gemm::build_schedule(ws_.expert_count, cfg_.experts_per_rank, cfg_.hidden, 256, ws_.offsets, ws_.tiles2, s, bm);
-        ep::launch_recv_assign(cfg_, heap_.view(), ws_, s);
-        if (!gathers()) ep::launch_recv_copy(cfg_, heap_.view(), ws_, s);
+        ep::launch_recv_assign(cfg_, heap_.view(), ws_, s, tuning_.recv_blocks);
+        if (!gathers()) ep::launch_recv_copy(cfg_, heap_.view(), ws_, s, tuning_.recv_blocks);
     }
 
     /// GEMM1 reads its A rows in place from the receive buffer (FP8 / NVFP4
@@ -234,12 +249,15 @@ public:
                     "out must be contiguous bf16 [T, hidden]");
         if (fused_) {
             ep::launch_combine_recv_fused(cfg_, heap_.view(), idx.data_ptr<int32_t>(), static_cast<int>(out.size(0)),
-                                          reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), ws_, timeout_ns_, s);
+                                          reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), ws_, timeout_ns_, s,
+                                          tuning_.combine_blocks);
             return;
         }
-        ep::launch_combine_send(cfg_, heap_.view(), reinterpret_cast<const __nv_bfloat16*>(y_.data_ptr()), ws_, 0, s);
+        ep::launch_combine_send(cfg_, heap_.view(), reinterpret_cast<const __nv_bfloat16*>(y_.data_ptr()), ws_,
+                                tuning_.combine_blocks, s);
         ep::launch_combine_recv(cfg_, heap_.view(), idx.data_ptr<int32_t>(), static_cast<int>(out.size(0)),
-                                reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), ws_, timeout_ns_, s);
+                                reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), ws_, timeout_ns_, s,
+                                tuning_.combine_blocks);
     }
 
     /// The whole layer: x [T, hidden] bf16, idx [T, topk] int32, w [T, topk] fp32 -> out [T, hidden] bf16.
@@ -294,10 +312,8 @@ private:
     CUtensorMap tmap_a1_, tmap_b1_, tmap_a2_, tmap_b2_, tmap_b1h_, tmap_b2h_;
     bool pair_ = false;
     bool fused_ = true;
-    // Measured on B200 at one EP8 rank's shape (32 experts x 1024 rows):
-    // GEMM1 with the gathering producer 2605 us vs 1483 us TMA-fed (+105 us
-    // receive copy), so the gather is opt-in.
     bool gather_ = false;
+    ep::EpTuning tuning_{};
 
 public:
     bool gather() const { return gather_; }
@@ -305,6 +321,7 @@ public:
     bool pair() const { return pair_; }
     void set_pair(bool v) { pair_ = v; }
     bool fused() const { return fused_; }
+    py::dict tuning() const { return tuning_dict(tuning_); }
     void set_fused(bool v) { fused_ = v; }
 };
 
@@ -401,6 +418,13 @@ void register_ep(py::module_& m) {
     auto e = m.def_submodule("ep", "kiwi::ep (expert-parallel MoE)");
     e.attr("MAX_TOPK") = ep::kMaxTopk;
     e.def("finalize_config", [](const py::dict& d) { return config_to_dict(config_from_dict(d)); });
+    e.def("tune", [](const py::dict& d, int sms, py::object env) {
+              std::string ev;
+              if (!env.is_none()) ev = env.cast<std::string>();
+              return tuning_dict(ep::tune(config_from_dict(d), sms, env.is_none() ? nullptr : ev.c_str()));
+          },
+          py::arg("config"), py::arg("sms"), py::arg("env") = py::none(),
+          "B200 launch tuning of an EP configuration (env: a KIWI_EP_TUNING override string).");
     e.def("route",
           [](torch::Tensor logits, int topk, torch::Tensor idx, torch::Tensor w) {
               ep::launch_route(logits.data_ptr<float>(), static_cast<int>(logits.size(0)),
@@ -440,6 +464,7 @@ void register_ep(py::module_& m) {
         .def_property_readonly("epoch", &MoeLayer::epoch)
         .def_property("gemm_pair", &MoeLayer::pair, &MoeLayer::set_pair,
                       "Use the 2-SM (256-row tile) grouped GEMM (unfused combine only; off by default).")
+        .def_property_readonly("tuning", &MoeLayer::tuning, "Launch tuning in effect (B200 table + KIWI_EP_TUNING).")
         .def_property("gather_a", &MoeLayer::gather, &MoeLayer::set_gather,
                       "GEMM1 gathers and dequantises its A rows from the receive buffer (FP8 / NVFP4 dispatch; "
                       "opt-in: measured slower than the default, where a receive kernel first writes "

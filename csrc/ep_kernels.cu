@@ -698,15 +698,15 @@ void launch_recv_count(const EpConfig& c, const p2p::HeapView& h, const EpWorksp
     KIWI_CUDA_CHECK(cudaGetLastError());
 }
 
-void launch_recv_assign(const EpConfig& c, const p2p::HeapView& h, const EpWorkspace& ws, cudaStream_t s) {
+void launch_recv_assign(const EpConfig& c, const p2p::HeapView& h, const EpWorkspace& ws, cudaStream_t s, int grid) {
     const uint64_t assign_blocks = (c.slots() * 32 + kThreads - 1) / kThreads;
-    const uint64_t cap = 8u * default_grid();
+    const uint64_t cap = grid > 0 ? static_cast<uint64_t>(grid) : 8u * default_grid();
     recv_assign_kernel<<<static_cast<int>(assign_blocks < cap ? assign_blocks : cap), kThreads, 0, s>>>(c, h, ws);
     KIWI_CUDA_CHECK(cudaGetLastError());
 }
 
-void launch_recv_copy(const EpConfig& c, const p2p::HeapView& h, const EpWorkspace& ws, cudaStream_t s) {
-    const int grid = 8 * default_grid();
+void launch_recv_copy(const EpConfig& c, const p2p::HeapView& h, const EpWorkspace& ws, cudaStream_t s, int grid) {
+    if (grid <= 0) grid = 8 * default_grid();
     switch (static_cast<Quant>(c.quant)) {
         case Quant::kNone: recv_copy_kernel<0><<<grid, kThreads, 0, s>>>(c, h, ws); break;
         case Quant::kFp8: recv_copy_kernel<1><<<grid, kThreads, 0, s>>>(c, h, ws); break;
@@ -716,8 +716,8 @@ void launch_recv_copy(const EpConfig& c, const p2p::HeapView& h, const EpWorkspa
 }
 
 void launch_recv_scatter(const EpConfig& c, const p2p::HeapView& h, const EpWorkspace& ws, cudaStream_t s) {
-    launch_recv_assign(c, h, ws, s);
-    launch_recv_copy(c, h, ws, s);
+    launch_recv_assign(c, h, ws, s, 0);
+    launch_recv_copy(c, h, ws, s, 0);
 }
 
 void launch_combine_send(const EpConfig& c, const p2p::HeapView& h, const __nv_bfloat16* y, const EpWorkspace& ws,
@@ -729,8 +729,9 @@ void launch_combine_send(const EpConfig& c, const p2p::HeapView& h, const __nv_b
 }
 
 void launch_combine_recv_fused(const EpConfig& c, const p2p::HeapView& h, const int32_t* idx, int tokens,
-                               __nv_bfloat16* out, const EpWorkspace& ws, uint64_t timeout_ns, cudaStream_t s) {
-    const int grid = 8 * default_grid();
+                               __nv_bfloat16* out, const EpWorkspace& ws, uint64_t timeout_ns, cudaStream_t s,
+                               int grid) {
+    if (grid <= 0) grid = 8 * default_grid();
     if (c.topk <= 8) {
         combine_recv_fused_kernel<8><<<grid, kThreads, 0, s>>>(c, h, idx, tokens, out, ws, timeout_ns);
     } else {
@@ -740,8 +741,8 @@ void launch_combine_recv_fused(const EpConfig& c, const p2p::HeapView& h, const 
 }
 
 void launch_combine_recv(const EpConfig& c, const p2p::HeapView& h, const int32_t* idx, int tokens,
-                         __nv_bfloat16* out, const EpWorkspace& ws, uint64_t timeout_ns, cudaStream_t s) {
-    const int grid = 8 * default_grid();
+                         __nv_bfloat16* out, const EpWorkspace& ws, uint64_t timeout_ns, cudaStream_t s, int grid) {
+    if (grid <= 0) grid = 8 * default_grid();
     if (c.world <= 8 && c.topk <= 8) {
         combine_recv_kernel<8><<<grid, kThreads, 0, s>>>(c, h, idx, tokens, out, ws, timeout_ns);
     } else {

@@ -50,11 +50,13 @@ void launch_recv_count(const EpConfig& c, const p2p::HeapView& h, const EpWorksp
 
 /// Assigns expert-major rows: pair_slot / pair_w / pair_dst of every row and
 /// the slot -> rows map (slot_pos).
-void launch_recv_assign(const EpConfig& c, const p2p::HeapView& h, const EpWorkspace& ws, cudaStream_t s);
+void launch_recv_assign(const EpConfig& c, const p2p::HeapView& h, const EpWorkspace& ws, cudaStream_t s,
+                        int grid = 0);
 
 /// Dequantises each received row into its expert-major rows of ws.a (not
 /// needed when GEMM1 gathers its A operand from the receive buffer).
-void launch_recv_copy(const EpConfig& c, const p2p::HeapView& h, const EpWorkspace& ws, cudaStream_t s);
+void launch_recv_copy(const EpConfig& c, const p2p::HeapView& h, const EpWorkspace& ws, cudaStream_t s,
+                      int grid = 0);
 
 /// launch_recv_assign then launch_recv_copy.
 void launch_recv_scatter(const EpConfig& c, const p2p::HeapView& h, const EpWorkspace& ws, cudaStream_t s);
@@ -67,13 +69,15 @@ void launch_combine_send(const EpConfig& c, const p2p::HeapView& h, const __nv_b
 /// Waits for every rank's combine flag and reduces the returned rows of each
 /// local token (over the ranks it was sent to) into out [T, hidden].
 void launch_combine_recv(const EpConfig& c, const p2p::HeapView& h, const int32_t* idx, int tokens,
-                         __nv_bfloat16* out, const EpWorkspace& ws, uint64_t timeout_ns, cudaStream_t s);
+                         __nv_bfloat16* out, const EpWorkspace& ws, uint64_t timeout_ns, cudaStream_t s,
+                         int grid = 0);
 
 /// Fused combine, receive side: after every rank's combine flag (set by the
 /// last CTA of each rank's scatter GEMM2), sums each local token's top-k rows
 /// of combk (already routing-weighted) into out [T, hidden].
 void launch_combine_recv_fused(const EpConfig& c, const p2p::HeapView& h, const int32_t* idx, int tokens,
-                               __nv_bfloat16* out, const EpWorkspace& ws, uint64_t timeout_ns, cudaStream_t s);
+                               __nv_bfloat16* out, const EpWorkspace& ws, uint64_t timeout_ns, cudaStream_t s,
+                               int grid = 0);
 
 // ---- transport-only (MORI-compatible) path ----
 

@@ -27,7 +27,7 @@ def test_fp8_layout_of_the_benchmark_config():
     slots = 8 * 4096
     regions = [("off_flags", 2 * 16 * 128), ("off_meta", slots * c["meta_bytes"]),
                ("off_row", slots * c["row_bytes"]), ("off_scale", slots * c["scale_bytes"]),
-               ("off_comb", slots * 7168 * 2)]
+               ("off_comb", slots * 7168 * 2), ("off_combk", 4096 * 8 * 7168 * 2)]
     ends = []
     for name, size in regions:
         assert c[name] % 256 == 0, name
@@ -43,7 +43,7 @@ def test_fp8_layout_of_the_benchmark_config():
 @pytest.mark.parametrize("quant", ["fp8", "nvfp4", "none"])
 def test_layout_alignment(world, quant):
     c = cfg(world=world, rank=world - 1, num_experts=256 if world <= 16 else 256, quant=quant)
-    for k in ("off_meta", "off_row", "off_scale", "off_comb"):
+    for k in ("off_meta", "off_row", "off_scale", "off_comb", "off_combk"):
         assert c[k] % 256 == 0
     assert c["row_bytes"] % 16 == 0 and c["scale_bytes"] % 16 == 0 and c["meta_bytes"] % 16 == 0
     if quant == "nvfp4":
@@ -121,3 +121,24 @@ def test_zipf_skews_routing():
     counts = torch.bincount(idx.flatten().long(), minlength=64).float()
     assert counts.max() / counts.mean() > 3.0
     assert c.quant == "nvfp4" and c.topk == 6
+
+
+def test_tuning_table_and_overrides():
+    """B200 tuning table (reference: apps/ep/ep_tuning.hpp runtime tables):
+    latency vs throughput entries, and KIWI_EP_TUNING overrides."""
+    from kiwi_b200._native import load
+
+    ep = load().ep
+    cfg = dict(world=8, rank=0, hidden=7168, num_experts=256, topk=8, max_tokens=4096, quant="fp8")
+    t = ep.tune(cfg, 148, "")
+    assert t["fused_combine"] and not t["gather_a"] and not t["gemm_pair"]
+    assert t["recv_blocks"] == 8 * 148 and t["combine_blocks"] == 8 * 148 and t["dispatch_blocks"] == 0
+    assert "throughput" in t["source"]
+    lat = ep.tune({**cfg, "max_tokens": 128}, 148, "")
+    assert lat["recv_blocks"] == 4 * 148 and "latency" in lat["source"]
+    o = ep.tune(cfg, 148, "gather_a=1,dispatch_blocks=296,fused_combine=off")
+    assert o["gather_a"] and o["dispatch_blocks"] == 296 and not o["fused_combine"]
+    assert o["source"].endswith("KIWI_EP_TUNING")
+    for bad in ("nope=1", "gather_a=maybe", "recv_blocks=0", "dispatch_blocks"):
+        with pytest.raises(Exception):
+            ep.tune(cfg, 148, bad)
