@@ -68,6 +68,24 @@ void register_p2p(py::module_& m) {
           },
           py::arg("blocks"), py::arg("rounds"), py::arg("timeout_ns") = 2000000000ull);
 
+    py::class_<CompletionCounter>(p, "CompletionCounter",
+                                  "64-bit counter in mapped pinned memory: host signal(), kernel poll.")
+        .def(py::init([](bool host_only) {
+                 return std::make_unique<CompletionCounter>(host_only ? queue::MemKind::kHost
+                                                                      : queue::MemKind::kMappedPinned);
+             }),
+             py::arg("host_only") = false)
+        .def("signal", &CompletionCounter::signal, py::arg("n") = 1)
+        .def("get", &CompletionCounter::get)
+        .def("set", &CompletionCounter::set)
+        .def("wait_kernel",
+             [](CompletionCounter& c, uint32_t steps, torch::Tensor seen, torch::Tensor status, uint64_t timeout_ns) {
+                 if (seen.numel() < steps) throw kiwi::error("wait_kernel: seen needs steps entries");
+                 launch_counter_wait(c.device_view(), steps, u64_ptr(seen), u32_ptr(status), timeout_ns,
+                                     cur_stream());
+             },
+             "Launches a one-thread kernel that polls the counter for 1..steps (bounded).");
+
     py::class_<Context>(p, "Context")
         .def(py::init<SymmetricHeap&, size_t, uint64_t>(), py::arg("heap"), py::arg("num_queues") = 1,
              py::arg("queue_capacity") = 2048, py::keep_alive<1, 2>())

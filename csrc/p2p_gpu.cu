@@ -331,6 +331,7 @@ void launch_heap_barrier(const HeapView& h, uint64_t flag_off, uint64_t round, u
 // (src_off -> dst_off + i*bytes on rank `dst`), each followed by a flag the
 // proxy writes; the warp waits (bounded) for every flag and the local counter.
 // ---------------------------------------------------------------------------
+#include "kiwi/p2p/counter.hpp"
 #include "kiwi/p2p/ghandle.cuh"
 
 namespace kiwi::p2p {
@@ -429,6 +430,26 @@ void launch_ce_pingpong(const GContext& ctx, int peer, bool initiator, uint64_t 
                         uint32_t* status, uint64_t timeout_ns, cudaStream_t s) {
     ce_pingpong_kernel<<<1, 32, 0, s>>>(ctx, peer, initiator ? 1 : 0, bytes, iters, warmup, src_off, dst_off,
                                         flag_off, lat_ns, status, timeout_ns);
+    KIWI_CUDA_CHECK(cudaGetLastError());
+}
+
+/// Completion-counter test kernel: one thread waits (bounded) for the counter
+/// to reach 1, 2, ..., steps, recording when each value was seen.
+__global__ void counter_wait_kernel(CounterView c, uint32_t steps, uint64_t* seen_ns, uint32_t* status,
+                                    uint64_t timeout_ns) {
+    for (uint32_t i = 1; i <= steps; ++i) {
+        if (c.poll(i, timeout_ns) != Status::kOk) {
+            status[0] = static_cast<uint32_t>(Status::kTimeout);
+            status[1] = i;
+            return;
+        }
+        seen_ns[i - 1] = ptx::globaltimer();
+    }
+}
+
+void launch_counter_wait(const CounterView& c, uint32_t steps, uint64_t* seen_ns, uint32_t* status,
+                         uint64_t timeout_ns, cudaStream_t s) {
+    counter_wait_kernel<<<1, 1, 0, s>>>(c, steps, seen_ns, status, timeout_ns);
     KIWI_CUDA_CHECK(cudaGetLastError());
 }
 

@@ -6,6 +6,7 @@
 #include <cuda_runtime.h>
 
 #include "kiwi/p2p/context.hpp"
+#include "kiwi/p2p/counter.hpp"
 #include "kiwi/p2p/heap.hpp"
 
 namespace kiwi::p2p {
@@ -71,5 +72,9 @@ void launch_ce_pingpong(const GContext& ctx, int peer, bool initiator, uint64_t 
 std::vector<uint64_t> host_ce_pingpong(SymmetricHeap& heap, int peer, bool initiator, uint64_t bytes, uint32_t iters,
                                        uint32_t warmup, uint64_t src_off, uint64_t dst_off, uint64_t flag_off,
                                        double timeout_s);
+
+/// Waits (one thread, bounded) for a completion counter to reach 1..steps.
+void launch_counter_wait(const CounterView& c, uint32_t steps, uint64_t* seen_ns, uint32_t* status,
+                         uint64_t timeout_ns, cudaStream_t s);
 
 }  // namespace kiwi::p2p

@@ -62,3 +62,22 @@ def test_missing_peer_times_out():
     msg = q.get(timeout=60)
     p.join(timeout=30)
     assert "timed out" in msg
+
+
+def test_completion_counter_host_only():
+    """Completion counter (reference: apps/p2p/comp_counter.hip.hpp): host
+    threads signal with release fetch_add, the value is monotonic."""
+    import threading
+
+    from kiwi_b200._native import load
+
+    c = load().p2p.CompletionCounter(host_only=True)
+    assert c.get() == 0
+    ths = [threading.Thread(target=lambda: [c.signal() for _ in range(10000)]) for _ in range(4)]
+    for t in ths:
+        t.start()
+    for t in ths:
+        t.join()
+    assert c.get() == 40000
+    c.set(7)
+    assert c.signal(3) == 10

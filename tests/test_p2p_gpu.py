@@ -52,3 +52,44 @@ def test_get_from_own_heap():
     heap.native.get(0, n, 3, 0, 2 << 20, lat, 64)
     torch.cuda.synchronize()
     assert torch.equal(heap.tensor(2 << 20, [n], torch.uint8), src)
+
+
+def test_completion_counter_host_signals_kernel():
+    """A kernel polls a completion counter (bounded) while a host thread bumps
+    it; every value is seen, in order."""
+    import threading
+    import time
+
+    C = kiwi_b200.native()
+    c = C.p2p.CompletionCounter()
+    steps = 200
+    seen = torch.zeros(steps, dtype=torch.int64, device="cuda")
+    status = torch.zeros(2, dtype=torch.int32, device="cuda")
+    c.wait_kernel(steps, seen, status, 5_000_000_000)
+
+    def bump():
+        for _ in range(steps):
+            c.signal()
+            time.sleep(20e-6)
+
+    t = threading.Thread(target=bump)
+    t.start()
+    t.join()
+    torch.cuda.synchronize()
+    assert int(status[0].item()) == 0, status
+    s = seen.cpu()
+    assert bool((s[1:] >= s[:-1]).all())
+    assert c.get() == steps
+
+
+def test_completion_counter_wait_times_out():
+    """Nobody signals: the kernel's wait returns kTimeout after its deadline
+    and the context stays usable."""
+    C = kiwi_b200.native()
+    c = C.p2p.CompletionCounter()
+    seen = torch.zeros(1, dtype=torch.int64, device="cuda")
+    status = torch.zeros(2, dtype=torch.int32, device="cuda")
+    c.wait_kernel(1, seen, status, 50_000_000)
+    torch.cuda.synchronize()
+    assert int(status[0].item()) != 0
+    assert torch.ones(1, device="cuda").item() == 1.0
