@@ -69,6 +69,10 @@ public:
     virtual bool poll_ready(size_t ep) = 0;
     virtual void upload_handles() = 0;
     virtual bool host_only() const = 0;
+    /// A native callback (any payload) that only counts its calls: lets a
+    /// benchmark measure the queue / frontend without Python in the loop.
+    virtual uint8_t register_native_counter() = 0;
+    virtual uint64_t native_count() const = 0;
 };
 
 template <typename Q>
@@ -85,6 +89,12 @@ public:
         const uint32_t exp = nbytes < 0 ? invoke::CallbackBase::kAnySize : static_cast<uint32_t>(nbytes);
         return ctx_.register_raw_callback(PyFn(std::move(fn)), exp);
     }
+    uint8_t register_native_counter() override {
+        return ctx_.register_raw_callback(
+            [this](const uint8_t*, uint32_t) { count_.fetch_add(1, std::memory_order_relaxed); },
+            invoke::CallbackBase::kAnySize);
+    }
+    uint64_t native_count() const override { return count_.load(std::memory_order_relaxed); }
     size_t progress(size_t ep, int max) override { return ctx_.progress(ep, max); }
     size_t progress_all(int max) override { return ctx_.progress_all(max); }
     void start_threads(size_t n, std::vector<int> cpus) override { threads_.start(n, std::move(cpus)); }
@@ -116,6 +126,7 @@ public:
     bool host_only() const override { return host_only_; }
 
 private:
+    std::atomic<uint64_t> count_{0};
     invoke::Context<Q> ctx_;
     invoke::ProgressThreads<Q> threads_;
     bool host_only_;
@@ -287,7 +298,9 @@ PYBIND11_MODULE(_C, m) {
         .def("poll_ready", &KiwiContextBase::poll_ready)
         .def("upload_handles", &KiwiContextBase::upload_handles)
         .def("check_device_errors", &KiwiContextBase::check_device_errors)
-        .def("rethrow_progress_errors", &KiwiContextBase::rethrow);
+        .def("rethrow_progress_errors", &KiwiContextBase::rethrow)
+        .def("register_native_counter", &KiwiContextBase::register_native_counter)
+        .def_property_readonly("native_count", &KiwiContextBase::native_count);
 
     // ---------------- bench ----------------
     auto b = m.def_submodule("bench", "native benchmark loops");
