@@ -10,8 +10,9 @@ kernels).
                 through kiwi_b200.utils.build.load_inline (the PyTorch-level
                 frontend), pushing to a native counting callback
 * python_cb:    the load_inline kernel with a Python callback (GIL in the loop)
-Each row: messages/s over the device time from the first push to the last
-(%globaltimer), 8-byte payloads, one warp per endpoint, native progress threads.
+Each row: messages/s over the longer of the device push time (first push to
+last, %globaltimer) and the host time until the callback has seen every
+message, 8-byte payloads, one warp per endpoint, native progress threads.
 """
 import argparse
 import json
@@ -79,18 +80,22 @@ def frontend_run(mod, endpoints, msgs, threads, python_cb=False, timeout_s=30.0)
     ctx.start(num_threads=threads)
     t = torch.zeros(2, dtype=torch.int64, device="cuda")
     status = torch.zeros(1, dtype=torch.int32, device="cuda")
-    mod.push(ctx.device_context_ptr, cb, endpoints, msgs, t, status)
     torch.cuda.synchronize()
+    h0 = time.perf_counter()
+    mod.push(ctx.device_context_ptr, cb, endpoints, msgs, t, status)
     want = endpoints * msgs
     end = time.time() + timeout_s
     while count() < want and time.time() < end:
-        time.sleep(1e-3)
+        time.sleep(1e-4)
+    host_s = time.perf_counter() - h0
+    torch.cuda.synchronize()
     got = count()
     ctx.stop()
     ctx.check_device_errors()
-    ns = int(t[1].item() - t[0].item())
+    dev_s = int(t[1].item() - t[0].item()) / 1e9
+    span = max(dev_s, host_s)
     return {"messages": got, "ok": got == want and int(status.item()) == 0,
-            "msgs_per_s": got / (ns / 1e9) if ns > 0 else 0.0}
+            "msgs_per_s": got / span if span > 0 else 0.0, "device_s": dev_s, "host_s": host_s}
 
 
 def main():
@@ -107,7 +112,7 @@ def main():
                  "msgs_per_s": r["messages"] / (r["device_ns"] / 1e9) if r["device_ns"] else 0.0})
     mod = load_inline("kiwi_bench_frontends", [CUDA], ["push"], cpp_sources=[CPP])
     rows.append({"frontend": "torch_inline", **frontend_run(mod, args.endpoints, args.msgs, args.threads)})
-    rows.append({"frontend": "python_cb", **frontend_run(mod, args.endpoints, max(1, args.msgs // 20), args.threads,
+    rows.append({"frontend": "python_cb", **frontend_run(mod, args.endpoints, max(1, args.msgs // 4), args.threads,
                                                          python_cb=True)})
     for row in rows:
         print("RESULT " + json.dumps({"bench": "invoke_frontends", "endpoints": args.endpoints, **row}), flush=True)
