@@ -4,7 +4,7 @@ the GPU->CPU->GPU invoke round trip.
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl kiwi|reference|nccl]
     torchrun --nnodes=1 --nproc-per-node N --master-addr 127.0.0.1 bench.py --gpus N ...
 
-Config (throughput mode): hidden 7168, expert FFN
+Config (the headline MoE EP benchmark, throughput mode): hidden 7168, expert FFN
 7168 -> 2048 -> 7168 SwiGLU (bf16 compute, fp32 accumulate), 256 experts sharded
 evenly over the N GPUs, top-8 routing (softmax over the top-k) from N(0,1)
 router logits, 4096 tokens per rank of N(0,1) bf16 activations, 1x128
@@ -63,7 +63,7 @@ def emit(obj):
 
 def reference_unavailable(args):
     emit({"impl": "reference", "unavailable": "AMDResearch/kiwi is ROCm/HIP-only (gfx90a/942/950, CMake + HIP, "
-          "no setup.py/pyproject; pip install of /root/reference fails: not installable) and has no CUDA path "
+          "no setup.py/pyproject; pip install of the reference checkout fails: not installable) and has no CUDA path "
           "to run on B200", "metric": METRIC, "n_gpus": args.gpus})
 
 

@@ -1,4 +1,4 @@
-"""GPU -> CPU -> GPU invoke round trip and the raw PCIe floor.
+"""GPU -> CPU -> GPU invoke round trip (one persistent block, 8-byte payload, payload sweep) and the raw PCIe floor.
 
     python benchmarks/bench_invoke.py [--iters 1000000] [--warmup 10000] [--sweep]
 

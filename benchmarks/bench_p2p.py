@@ -1,5 +1,5 @@
 """Kernel-initiated P2P put / get / signal over NVLink vs NCCL send/recv
-(BASELINE config 3).
+(the P2P latency and bandwidth sweep, 8 B - 64 MB, pairs of GPUs).
 
     torchrun --nproc-per-node N --master-addr 127.0.0.1 benchmarks/bench_p2p.py [--max-bytes 67108864]
 

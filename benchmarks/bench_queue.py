@@ -4,7 +4,7 @@ benchmarks/invoke/bench_{throughput,overhead}.hip.cpp of AMDResearch/kiwi).
     python benchmarks/bench_queue.py
 
 * host_ring: two CPU threads ping-pong 1,000,000 seeded 8-byte payloads through
-  two 4096 x 64 B rings, p50 / p99 round trip ns, order and
+  two 4096 x 64 B rings (the host-only ring benchmark), p50 / p99 round trip ns, order and
   checksum verified; plus a one-way streaming rate.
 * invoke_throughput: E producer warps x T progress threads, messages/s.
 * push_cost: SM cycles one warp spends per push (payload 8 .. 256 B).
