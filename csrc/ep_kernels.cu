@@ -175,31 +175,49 @@ __global__ void __launch_bounds__(kThreads) route_kernel(const float* logits, in
     }
 }
 
+/// Copies `bytes` (a multiple of 16) from this warp's shared staging to a
+/// (possibly remote) slot, 16 bytes per lane per instruction.
+KIWI_DEV void warp_copy_out(uint8_t* dst, const uint8_t* src, int bytes, int lane) {
+    for (int o = lane * 16; o < bytes; o += 32 * 16) {
+        ptx::st_v4(dst + o, *reinterpret_cast<const uint4*>(src + o));
+    }
+}
+
+/// Dispatch: one warp per token.  The row is quantised 512 columns at a time
+/// and each 16-byte lane chunk is stored straight into every destination
+/// rank's receive slot over NVLink; the token's metadata (epoch, token, top-k
+/// ids and weights) and its scales are first assembled in the warp's shared
+/// staging in the slot's own layout and then stored with 16-byte vector
+/// stores, so no destination sees a stream of 1- or 4-byte remote writes.
 template <int QUANT>
 __global__ void __launch_bounds__(kThreads) dispatch_kernel(EpConfig c, p2p::HeapView h, const __nv_bfloat16* x,
                                                             const int32_t* idx, const float* w, int tokens,
                                                             EpWorkspace ws) {
+    extern __shared__ __align__(16) uint8_t dyn_smem[];
     const int lane = threadIdx.x & 31;
+    const int warp_in_block = threadIdx.x / 32;
     const int warps = gridDim.x * (blockDim.x / 32);
     const uint32_t epoch = *reinterpret_cast<volatile uint32_t*>(ws.epoch);
     const int me = c.rank;
+    // Per-warp staging: [meta_bytes][scale_bytes], both 16-byte multiples.
+    uint8_t* stage = dyn_smem + warp_in_block * (c.meta_bytes + c.scale_bytes);
+    uint8_t* s_meta = stage;
+    uint8_t* s_scale = stage + c.meta_bytes;
     for (int t = (blockIdx.x * blockDim.x + threadIdx.x) / 32; t < tokens; t += warps) {
         const int e = lane < c.topk ? idx[static_cast<int64_t>(t) * c.topk + lane] : -1;
         const float wt = lane < c.topk ? w[static_cast<int64_t>(t) * c.topk + lane] : 0.f;
         const bool ok_e = e >= 0 && e < c.num_experts;
         const uint32_t mask = __reduce_or_sync(0xffffffffu, ok_e ? (1u << (e / c.experts_per_rank)) : 0u);
         const uint64_t slot = c.slot_index(me, t);
-        // Metadata (header, ids, weights) to every destination.
-        for (uint32_t m = mask; m; m &= m - 1) {
-            const int r = __ffs(m) - 1;
-            uint8_t* mp = h.base[r] + c.meta_off(slot);
-            if (lane < c.topk) {
-                reinterpret_cast<int32_t*>(mp + sizeof(DispatchMetaHeader))[lane] = e;
-                reinterpret_cast<float*>(mp + sizeof(DispatchMetaHeader) + 4 * c.topk)[lane] = wt;
-            }
-            if (lane == 0) {
-                ptx::st_v4(mp, make_uint4(epoch, static_cast<uint32_t>(t), 0, 0));
-            }
+        __syncwarp();  // the previous token's staging has been stored
+        if (lane < c.topk) {
+            reinterpret_cast<int32_t*>(s_meta + sizeof(DispatchMetaHeader))[lane] = e;
+            reinterpret_cast<float*>(s_meta + sizeof(DispatchMetaHeader) + 4 * c.topk)[lane] = wt;
+        }
+        if (lane == 0) *reinterpret_cast<uint4*>(s_meta) = make_uint4(epoch, static_cast<uint32_t>(t), 0, 0);
+        const int meta_pad_from = static_cast<int>(sizeof(DispatchMetaHeader)) + 8 * c.topk;
+        for (int o = meta_pad_from + lane * 4; o < c.meta_bytes; o += 32 * 4) {
+            *reinterpret_cast<uint32_t*>(s_meta + o) = 0;
         }
         const __nv_bfloat16* xr = x + static_cast<int64_t>(t) * c.hidden;
         if constexpr (QUANT == static_cast<int>(Quant::kNone)) {
@@ -219,12 +237,10 @@ __global__ void __launch_bounds__(kThreads) dispatch_kernel(EpConfig c, p2p::Hea
                 float scale;
                 uint4 q;
                 quant_fp8_16(in, scale, q);
+                if ((lane & 7) == 0) reinterpret_cast<float*>(s_scale)[col / kFp8Block] = scale;
                 for (uint32_t m = mask; m; m &= m - 1) {
                     const int r = __ffs(m) - 1;
                     ptx::st_v4(h.base[r] + c.row_off(slot) + col, q);
-                    if ((lane & 7) == 0) {
-                        reinterpret_cast<float*>(h.base[r] + c.scale_off(slot))[col / kFp8Block] = scale;
-                    }
                 }
             }
         } else {
@@ -239,6 +255,7 @@ __global__ void __launch_bounds__(kThreads) dispatch_kernel(EpConfig c, p2p::Hea
 #pragma unroll
             for (int d = 16; d > 0; d >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, d));
             const float row_scale = amax > 0.f ? amax / (kFp8Max * kFp4Max) : 0.f;
+            if (lane == 0) reinterpret_cast<float*>(s_scale)[0] = row_scale;
             for (int base = 0; base < c.hidden; base += 512) {
                 const int col = base + lane * 16;
                 uint4 in[2];
@@ -247,18 +264,20 @@ __global__ void __launch_bounds__(kThreads) dispatch_kernel(EpConfig c, p2p::Hea
                 uint8_t sb;
                 uint2 q;
                 quant_fp4_16(in, row_scale, sb, q);
+                s_scale[4 + col / kFp4Block] = sb;
                 for (uint32_t m = mask; m; m &= m - 1) {
                     const int r = __ffs(m) - 1;
                     *reinterpret_cast<uint2*>(h.base[r] + c.row_off(slot) + col / 2) = q;
-                    h.base[r][c.scale_off(slot) + 4 + col / kFp4Block] = sb;
                 }
             }
-            if (lane == 0) {
-                for (uint32_t m = mask; m; m &= m - 1) {
-                    const int r = __ffs(m) - 1;
-                    reinterpret_cast<float*>(h.base[r] + c.scale_off(slot))[0] = row_scale;
-                }
-            }
+            // Zero the staging tail past the last block scale (the slot layout pads to 16 bytes).
+            for (int o = 4 + c.hidden / kFp4Block + lane; o < c.scale_bytes; o += 32) s_scale[o] = 0;
+        }
+        __syncwarp();
+        for (uint32_t m = mask; m; m &= m - 1) {
+            const int r = __ffs(m) - 1;
+            warp_copy_out(h.base[r] + c.meta_off(slot), s_meta, c.meta_bytes, lane);
+            if (c.scale_bytes) warp_copy_out(h.base[r] + c.scale_off(slot), s_scale, c.scale_bytes, lane);
         }
     }
     grid_done_signal(c, h, &ws.done_ctas[0], c.dispatch_flag(me),
@@ -676,15 +695,17 @@ void launch_dispatch(const EpConfig& c, const p2p::HeapView& h, const __nv_bfloa
         const int want = (tokens * 32 + kThreads - 1) / kThreads;
         grid = std::max(1, std::min(want, 8 * default_grid()));
     }
+    const size_t smem = static_cast<size_t>(kThreads / 32) * (c.meta_bytes + c.scale_bytes);
+    if (smem > 48 * 1024) throw kiwi::error("dispatch: per-token staging exceeds 48 KB per block (hidden too large)");
     switch (static_cast<Quant>(c.quant)) {
         case Quant::kNone:
-            dispatch_kernel<0><<<grid, kThreads, 0, s>>>(c, h, x, idx, w, tokens, ws);
+            dispatch_kernel<0><<<grid, kThreads, smem, s>>>(c, h, x, idx, w, tokens, ws);
             break;
         case Quant::kFp8:
-            dispatch_kernel<1><<<grid, kThreads, 0, s>>>(c, h, x, idx, w, tokens, ws);
+            dispatch_kernel<1><<<grid, kThreads, smem, s>>>(c, h, x, idx, w, tokens, ws);
             break;
         case Quant::kNvfp4:
-            dispatch_kernel<2><<<grid, kThreads, 0, s>>>(c, h, x, idx, w, tokens, ws);
+            dispatch_kernel<2><<<grid, kThreads, smem, s>>>(c, h, x, idx, w, tokens, ws);
             break;
     }
     KIWI_CUDA_CHECK(cudaGetLastError());
