@@ -49,14 +49,20 @@ def main():
     ap.add_argument("--warmup", type=int, default=10_000)
     ap.add_argument("--sweep", action="store_true", help="payload sweep 8 B .. 4 KB")
     ap.add_argument("--poll-warps", type=int, nargs="*", default=[0, 2])
-    ap.add_argument("--stagger", type=int, nargs="*", default=[150, 200, 250, 300])
+    ap.add_argument("--stagger", type=int, nargs="*", default=[100, 150, 200],
+                    help="two-reads-in-flight mailbox mode: delay between the two reads (ns)")
     ap.add_argument("--cpu", type=int, default=-1)
     args = ap.parse_args()
     C = kiwi_b200.native()
     summarize("pcie_floor", C.bench.pcie_floor(args.iters, args.warmup, args.cpu))
+    # Mailbox replies: one adaptive read in flight (the default), then two reads in flight a stagger apart.
+    r = C.bench.invoke_rtt(iters=args.iters, warmup=args.warmup, cpu=args.cpu, mailbox=True, pipeline=1)
+    summarize("invoke_rtt", r, {"payload_bytes": 8, "reply": "mailbox", "pipeline": 1, "queue": "spsc"})
     for st in args.stagger:
-        r = C.bench.invoke_rtt(args.iters, args.warmup, 8, 1, args.cpu, 4096, False, 0, 2_000_000_000, True, st)
-        summarize("invoke_rtt", r, {"payload_bytes": 8, "reply": "mailbox", "stagger_ns": st, "queue": "spsc"})
+        r = C.bench.invoke_rtt(iters=args.iters, warmup=args.warmup, cpu=args.cpu, mailbox=True, pipeline=2,
+                               stagger_ns=st)
+        summarize("invoke_rtt", r, {"payload_bytes": 8, "reply": "mailbox", "pipeline": 2, "stagger_ns": st,
+                                    "queue": "spsc"})
     for pw in args.poll_warps:
         r = C.bench.invoke_rtt(args.iters // 4, args.warmup, 8, 1, args.cpu, 4096, False, pw)
         summarize("invoke_rtt", r, {"payload_bytes": 8, "reply": "ring", "poll_warps": pw, "queue": "spsc"})

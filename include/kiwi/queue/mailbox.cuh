@@ -56,6 +56,16 @@ struct MailboxHandle {
             d += kAdaptUp;
         }
     }
+    /// Two-read variant: outcome 0 = the first read hit, 1 = the staggered
+    /// second read hit, 2 = a later read.
+    KIWI_DEV void adapt2(int outcome) const {
+        uint32_t& d = const_cast<uint32_t&>(initial_delay_ns);
+        if (outcome == 0) {
+            d = d > kAdaptDown ? d - kAdaptDown : 0;
+        } else if (d < kAdaptMax) {
+            d += outcome == 1 ? kAdaptUp / 3 : kAdaptUp;
+        }
+    }
     static constexpr uint32_t kAdaptDown = 8;
     static constexpr uint32_t kAdaptUp = 48;
     static constexpr uint32_t kAdaptMax = 4000;
@@ -102,17 +112,23 @@ struct MailboxHandle {
                 if (dl.expired()) return timed_out(seq);
             }
         }
+        // Two reads in flight on the two mirrors, `stagger_ns` apart: a first
+        // read that leaves a little early costs only the stagger, not a
+        // whole extra PCIe read.  Adaptive: first read hit -> delay - 8 ns,
+        // second read hit -> + 16 ns, later -> + 48 ns.
         uint4 a = ptx::ld_volatile_v4(m0);
         spin_ns(stagger_ns);
         uint4 b = ptx::ld_volatile_v4(m1);
-        while (true) {
+        for (int round = 0;; ++round) {
             if (words_have_tag(a.x, a.y, a.z, a.w, tag)) {
                 value = chunk_value(a);
+                if (adaptive) adapt2(round == 0 ? 0 : 2);
                 return Status::kOk;
             }
             a = ptx::ld_volatile_v4(m0);
             if (words_have_tag(b.x, b.y, b.z, b.w, tag)) {
                 value = chunk_value(b);
+                if (adaptive) adapt2(round == 0 ? 1 : 2);
                 return Status::kOk;
             }
             b = ptx::ld_volatile_v4(m1);
