@@ -16,6 +16,21 @@ import torch.multiprocessing as mp
 pytestmark = [pytest.mark.gpu, pytest.mark.multigpu]
 
 
+def _ngpu():
+    return torch.cuda.device_count() if torch.cuda.is_available() else 0
+
+
+@pytest.fixture(autouse=True)
+def _one_gpu_per_rank(request):
+    """Every rank needs its own GPU: ranks whose kernels wait on one another
+    must never share a GPU (they would run as separate launches that nothing
+    schedules together).  Each test names its world size in its node id."""
+    name = request.node.name
+    world = 4 if "world4" in name or name.endswith("_4") else 2
+    if _ngpu() < world:
+        pytest.skip(f"needs {world} GPUs, one per rank")
+
+
 def _free_port():
     s = socket.socket()
     s.bind(("127.0.0.1", 0))
@@ -137,10 +152,6 @@ def _nvls(rank, world):
     expect = torch.arange(n, device="cuda", dtype=torch.float32) * (world * (world + 1) / 2)
     assert torch.allclose(data, expect), (data[:4], expect[:4])
     assert int(status[0].item()) == 0
-
-
-def _ngpu():
-    return torch.cuda.device_count() if torch.cuda.is_available() else 0
 
 
 def test_all_pairs_puts_2():
