@@ -351,7 +351,7 @@ PYBIND11_MODULE(_C, m) {
     b.def("invoke_rtt",
           [rtt_to_dict](uint64_t iters, uint64_t warmup, uint32_t bytes, uint64_t seed, int cpu, uint64_t cap,
                         bool mpsc, uint32_t poll_warps, uint64_t timeout_ns, bool mailbox, uint32_t stagger_ns,
-                        uint32_t initial_delay_ns, uint32_t pipeline, bool adaptive) {
+                        uint32_t initial_delay_ns, uint32_t pipeline, bool adaptive, bool demote) {
               bench::RttConfig c;
               c.iters = iters;
               c.warmup = warmup;
@@ -367,6 +367,7 @@ PYBIND11_MODULE(_C, m) {
               c.initial_delay_ns = initial_delay_ns;
               c.pipeline = pipeline;
               c.adaptive = adaptive;
+              c.demote = demote;
               bench::RttResult r;
               {
                   py::gil_scoped_release nogil;
@@ -377,7 +378,8 @@ PYBIND11_MODULE(_C, m) {
           py::arg("iters") = 100000, py::arg("warmup") = 10000, py::arg("payload_bytes") = 8, py::arg("seed") = 1,
           py::arg("cpu") = -1, py::arg("capacity") = 4096, py::arg("mpsc") = false, py::arg("poll_warps") = 0,
           py::arg("timeout_ns") = 2000000000ull, py::arg("mailbox") = false, py::arg("stagger_ns") = 200,
-          py::arg("initial_delay_ns") = 300, py::arg("pipeline") = 1, py::arg("adaptive") = true);
+          py::arg("initial_delay_ns") = 300, py::arg("pipeline") = 1, py::arg("adaptive") = true,
+          py::arg("demote") = false);
     b.def("pcie_floor",
           [rtt_to_dict](uint64_t iters, uint64_t warmup, int cpu, uint64_t timeout_ns) {
               bench::RttResult r;

@@ -243,7 +243,8 @@ static RttResult run_invoke_rtt(const RttConfig& cfg) {
     if (cfg.poll_warps > 7) throw kiwi::error("invoke_rtt: poll_warps must be <= 7");
     kiwi::invoke::Context<Q> ctx(1, cfg.capacity, MemKind::kMappedPinned);
     SPSCH2DQueue reply(64, MemKind::kMappedPinned);
-    ReplyMailbox mailbox(MemKind::kMappedPinned, cfg.stagger_ns, cfg.initial_delay_ns, cfg.pipeline, cfg.adaptive);
+    ReplyMailbox mailbox(MemKind::kMappedPinned, cfg.stagger_ns, cfg.initial_delay_ns, cfg.pipeline, cfg.adaptive,
+                         cfg.demote);
     uint64_t callbacks = 0;
     if (cfg.mailbox && cfg.payload_bytes != 8) throw kiwi::error("invoke_rtt: the mailbox path sends 8-byte payloads");
     const uint8_t cb = cfg.mailbox ? ctx.register_call(std::function<uint64_t(uint64_t)>([&](uint64_t v) {

@@ -34,6 +34,17 @@ inline void store_half(void* p, uint64_t v) {
     __atomic_store_n(static_cast<uint64_t*>(p), v, __ATOMIC_RELAXED);
 }
 
+/// Hints the core to move the cache line holding `p` to the shared last-level
+/// cache (x86 CLDEMOTE), so a device read of it over PCIe does not have to
+/// snoop this core's private caches.  Executes as a no-op on CPUs without it.
+inline void demote_line(const void* p) {
+#if defined(__x86_64__)
+    asm volatile("cldemote %0" ::"m"(*static_cast<const volatile char*>(p)));
+#else
+    (void)p;
+#endif
+}
+
 
 inline void cpu_relax() {
 #if defined(__x86_64__) || defined(__i386__)

@@ -156,8 +156,10 @@ public:
     /// Defaults: one poll in flight, first poll after an adaptive delay that
     /// starts at 300 ns (the fastest configuration measured on B200).
     explicit ReplyMailbox(MemKind kind = default_host_kind(), uint32_t stagger_ns = 200,
-                          uint32_t initial_delay_ns = 300, uint32_t pipeline = 1, bool adaptive = true)
+                          uint32_t initial_delay_ns = 300, uint32_t pipeline = 1, bool adaptive = true,
+                          bool demote = false)
         : kind_(kind), stagger_(stagger_ns), delay_(initial_delay_ns), pipeline_(pipeline), adaptive_(adaptive),
+          demote_(demote),
           mem_(alloc_zeroed(kMailboxMirrors * kMailboxStride + sizeof(ErrorRecord), kind)) {}
     ~ReplyMailbox() { free_memory(mem_, kind_); }
     ReplyMailbox(const ReplyMailbox&) = delete;
@@ -171,6 +173,7 @@ public:
             Chunk* c = chunk(m);
             host::store_half(&c->lo, lo);
             host::store_half(&c->hi, hi);
+            if (demote_) host::demote_line(c);
         }
     }
 
@@ -208,6 +211,7 @@ private:
     uint32_t delay_;
     uint32_t pipeline_;
     bool adaptive_;
+    bool demote_;
     void* mem_;
 };
 
