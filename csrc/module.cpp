@@ -379,7 +379,7 @@ PYBIND11_MODULE(_C, m) {
           py::arg("cpu") = -1, py::arg("capacity") = 4096, py::arg("mpsc") = false, py::arg("poll_warps") = 0,
           py::arg("timeout_ns") = 2000000000ull, py::arg("mailbox") = false, py::arg("stagger_ns") = 200,
           py::arg("initial_delay_ns") = 300, py::arg("pipeline") = 1, py::arg("adaptive") = true,
-          py::arg("demote") = false);
+          py::arg("demote") = true);
     b.def("pcie_floor",
           [rtt_to_dict](uint64_t iters, uint64_t warmup, int cpu, uint64_t timeout_ns) {
               bench::RttResult r;

@@ -22,7 +22,7 @@ struct RttConfig {
     uint32_t stagger_ns = 200;     // mailbox: delay between the two in-flight polls
     uint32_t initial_delay_ns = 300; // mailbox: (starting) delay before the first poll
     uint32_t pipeline = 1;           // mailbox: polls in flight (1 or 2)
-    bool demote = false;             // mailbox: CLDEMOTE each reply line after writing it
+    bool demote = true;              // mailbox: CLDEMOTE each reply line after writing it
     bool adaptive = true;            // mailbox: adapt the delay
     uint64_t timeout_ns = 2000000000ull;
 };

@@ -150,14 +150,17 @@ struct MailboxHandle {
 #endif
 };
 
-/// Host side: owns the mirrors in mapped pinned memory.
+/// Host side: owns the mirrors in mapped pinned memory.  `demote` (default)
+/// CLDEMOTEs each mirror line after writing it: measured p50 1.499 vs
+/// 1.518 us and p99 2.48 vs 2.54 us through invoke on B200 (three
+/// alternating runs of 200 k round trips each).
 class ReplyMailbox {
 public:
     /// Defaults: one poll in flight, first poll after an adaptive delay that
     /// starts at 300 ns (the fastest configuration measured on B200).
     explicit ReplyMailbox(MemKind kind = default_host_kind(), uint32_t stagger_ns = 200,
                           uint32_t initial_delay_ns = 300, uint32_t pipeline = 1, bool adaptive = true,
-                          bool demote = false)
+                          bool demote = true)
         : kind_(kind), stagger_(stagger_ns), delay_(initial_delay_ns), pipeline_(pipeline), adaptive_(adaptive),
           demote_(demote),
           mem_(alloc_zeroed(kMailboxMirrors * kMailboxStride + sizeof(ErrorRecord), kind)) {}
