@@ -239,6 +239,9 @@ private:
         write_chunks(payload, bytes, metadata, 1, nlines * kChunksPerLine);
         std::atomic_thread_fence(std::memory_order_release);
         write_chunks(payload, bytes, metadata, 0, 1);
+        // The device polls these lines over PCIe: move them to the shared LLC
+        // so its reads need not snoop this core's caches (as the reply mailbox).
+        for (uint32_t l = 0; l < nlines; ++l) host::demote_line(&ring_[((head_ + l) & mask_) * kChunksPerLine]);
         head_ += nlines;
     }
 

@@ -264,6 +264,7 @@ private:
             host::store_half(&base[k].hi, pack_half(hi, tag));
             if (k == 1) std::atomic_thread_fence(std::memory_order_release);
         }
+        for (uint32_t l = 0; l < slot_lines_; ++l) host::demote_line(&base[l * kChunksPerLine]);
     }
 
     uint64_t slots_;
