@@ -69,6 +69,7 @@ public:
 
 private:
     void map_range(CUmemGenericAllocationHandle h, void** va);
+    void release() noexcept;
 
     int device_;
     HeapView view_{};

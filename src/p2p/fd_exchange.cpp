@@ -2,9 +2,11 @@
 // abstract-namespace Unix sockets (no files on disk, nothing to clean up).
 #include <poll.h>
 #include <sys/socket.h>
+#include <sys/time.h>
 #include <sys/un.h>
 #include <unistd.h>
 
+#include <algorithm>
 #include <chrono>
 #include <cstring>
 #include <string>
@@ -142,12 +144,26 @@ int fetch_from(const std::string& name, int32_t my_rank, double timeout_s) {
         socklen_t len;
         sockaddr_un a = make_addr(name, &len);
         if (connect(s, reinterpret_cast<sockaddr*>(&a), len) == 0) {
+            // Bound the reply wait by what is left of the timeout (a server that
+            // accepted but stalled must not block this rank forever).
+            const auto left = std::chrono::duration_cast<std::chrono::microseconds>(end - std::chrono::steady_clock::now());
+            const long long us = std::max<long long>(left.count(), 1000);
+            timeval tv{};
+            tv.tv_sec = static_cast<time_t>(us / 1000000);
+            tv.tv_usec = static_cast<suseconds_t>(us % 1000000);
+            setsockopt(s, SOL_SOCKET, SO_RCVTIMEO, &tv, sizeof(tv));
             if (write(s, &my_rank, sizeof(my_rank)) != sizeof(my_rank)) {
                 close(s);
                 throw kiwi::error("kiwi::p2p: write to " + name + " failed");
             }
             int32_t tag = -1;
-            const int fd = recv_fd(s, &tag);
+            int fd = -1;
+            try {
+                fd = recv_fd(s, &tag);
+            } catch (...) {
+                close(s);
+                throw;
+            }
             close(s);
             return fd;
         }
