@@ -245,8 +245,12 @@ public:
 
     void combine(torch::Tensor idx, torch::Tensor out) {
         cudaStream_t s = cur_stream();
-        TORCH_CHECK(out.scalar_type() == torch::kBFloat16 && out.is_contiguous() && out.size(1) == cfg_.hidden,
-                    "out must be contiguous bf16 [T, hidden]");
+        TORCH_CHECK(out.scalar_type() == torch::kBFloat16 && out.is_contiguous() && out.dim() == 2 &&
+                        out.size(1) == cfg_.hidden && out.device() == w13_.device(),
+                    "out must be contiguous bf16 [T, hidden] on the layer's GPU");
+        TORCH_CHECK(idx.scalar_type() == torch::kInt32 && idx.is_contiguous() && idx.dim() == 2 &&
+                        idx.size(1) == cfg_.topk && idx.size(0) == out.size(0) && out.size(0) <= cfg_.max_tokens,
+                    "idx must be the round's contiguous int32 [T, topk] with T = out rows <= max_tokens");
         if (fused_) {
             ep::launch_combine_recv_fused(cfg_, heap_.view(), idx.data_ptr<int32_t>(), static_cast<int>(out.size(0)),
                                           reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), ws_, timeout_ns_, s,
@@ -290,6 +294,9 @@ public:
 
 private:
     void check_tokens(const torch::Tensor& x, const torch::Tensor& idx, const torch::Tensor& w) {
+        TORCH_CHECK(x.is_cuda() && x.device() == w13_.device() && idx.device() == x.device() && w.device() == x.device(),
+                    "x, idx and w must live on the layer's GPU");
+        TORCH_CHECK(x.dim() == 2 && idx.dim() == 2 && w.dim() == 2, "x, idx and w must be 2-D");
         TORCH_CHECK(x.scalar_type() == torch::kBFloat16 && x.is_contiguous() && x.size(1) == cfg_.hidden,
                     "x must be contiguous bf16 [T, hidden]");
         TORCH_CHECK(x.size(0) <= cfg_.max_tokens, "more tokens than max_tokens");
