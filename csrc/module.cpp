@@ -320,6 +320,28 @@ PYBIND11_MODULE(_C, m) {
           },
           py::arg("iters"), py::arg("warmup"), py::arg("capacity") = 4096, py::arg("payload_bytes") = 8,
           py::arg("seed") = 0, py::arg("cpu_a") = -1, py::arg("cpu_b") = -1);
+    b.def("queue_baselines",
+          [](uint64_t iters, uint64_t warmup, uint64_t messages, uint32_t bytes, uint64_t cap, int a, int c) {
+              std::vector<bench::BaselineResult> rs;
+              {
+                  py::gil_scoped_release nogil;
+                  rs = bench::queue_baselines(iters, warmup, messages, bytes, cap, a, c);
+              }
+              py::list out;
+              for (const auto& r : rs) {
+                  py::dict d;
+                  d["name"] = r.name;
+                  d["p50_ns"] = r.p50_ns;
+                  d["p99_ns"] = r.p99_ns;
+                  d["msgs_per_s"] = r.msgs_per_s;
+                  d["ok"] = r.ok;
+                  out.append(d);
+              }
+              return out;
+          },
+          py::arg("iters") = 100000, py::arg("warmup") = 10000, py::arg("messages") = 1000000,
+          py::arg("payload_bytes") = 8, py::arg("capacity") = 4096, py::arg("cpu_a") = -1, py::arg("cpu_b") = -1,
+          "Host-only queue baselines (kiwi ring, head/tail ring, per-slot sequence ring, raw word).");
     b.def("host_ring_stream",
           [](uint64_t n, uint64_t cap, uint32_t bytes, uint64_t seed, int a, int c) {
               bench::HostRingResult r;

@@ -2,6 +2,7 @@
 #pragma once
 
 #include <cstdint>
+#include <string>
 #include <vector>
 
 namespace kiwi::bench {
@@ -24,5 +25,22 @@ HostRingResult host_ring_pingpong(uint64_t iters, uint64_t warmup, uint64_t capa
 /// Thread A streams `messages` seeded payloads; B pops and checks order and sum.
 HostRingResult host_ring_stream(uint64_t messages, uint64_t capacity, uint32_t payload_bytes,
                                 uint64_t seed, int cpu_a, int cpu_b);
+
+/// One queue design measured by queue_baselines().
+struct BaselineResult {
+    std::string name;
+    double p50_ns = 0;           // ping-pong round trip
+    double p99_ns = 0;
+    double msgs_per_s = 0;       // one-way streaming
+    bool ok = false;             // order and checksum verified in both runs
+};
+
+/// Host-only queue baselines through one adapter contract (the reference's
+/// benchmarks/queue_baselines harness without a GPU): the kiwi ring (this
+/// wire format), a head/tail-counter ring of 64-byte slots, a per-slot
+/// sequence ring, and a single-word store floor.  Two CPU threads; ping-pong
+/// of `iters` round trips (after `warmup`) and a stream of `messages`.
+std::vector<BaselineResult> queue_baselines(uint64_t iters, uint64_t warmup, uint64_t messages, uint32_t payload_bytes,
+                                            uint64_t capacity, int cpu_a, int cpu_b);
 
 }  // namespace kiwi::bench

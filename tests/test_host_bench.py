@@ -26,3 +26,17 @@ def test_xorshift_reference_values():
     s ^= s >> 7
     s ^= (s << 17) & (2**64 - 1)
     assert C.bench.xorshift64(1) == s
+
+
+def test_queue_baselines_all_designs_deliver_in_order():
+    """Host-only queue baselines through one adapter contract (reference:
+    benchmarks/queue_baselines): every design delivers in order with the
+    right checksum, and reports latency and throughput."""
+    from kiwi_b200._native import load
+
+    rs = load().bench.queue_baselines(iters=2000, warmup=200, messages=20000, payload_bytes=8, capacity=64)
+    names = [r["name"] for r in rs]
+    assert names == ["kiwi_ring", "head_tail", "seq_slot", "raw_word"]
+    for r in rs:
+        assert r["ok"], r
+        assert r["p50_ns"] > 0 and r["p99_ns"] >= r["p50_ns"] and r["msgs_per_s"] > 0, r
