@@ -119,19 +119,19 @@ public:
                               " lines");
         }
         uint8_t* dst = static_cast<uint8_t*>(out);
-        const uint32_t total = nlines * kChunksPerLine;
-        for (uint32_t k = 1; k < total; ++k) {
+        // Only chunks that carry payload are read: every word is tagged on its
+        // own, and the padding after the last payload chunk carries no data
+        // (the next message starts on the next line).
+        for (uint32_t k = 1; k < nchunks; ++k) {
             const uint64_t line = line0 + k / kChunksPerLine;
             const uint32_t tag = lap_tag(line, log2_);
             const Chunk* c = chunk(line, k % kChunksPerLine);
             const uint64_t a = host::load_half(&c->lo);
             const uint64_t b = host::load_half(&c->hi);
             if (!half_has_tag(a, tag) || !half_has_tag(b, tag)) return false;
-            if (k < nchunks) {
-                const uint32_t lo = half_data(a), hi = half_data(b);
-                std::memcpy(dst + 8 * (k - 1), &lo, 4);
-                std::memcpy(dst + 8 * (k - 1) + 4, &hi, 4);
-            }
+            const uint32_t lo = half_data(a), hi = half_data(b);
+            std::memcpy(dst + 8 * (k - 1), &lo, 4);
+            std::memcpy(dst + 8 * (k - 1) + 4, &hi, 4);
         }
         if (metadata) *metadata = half_data(h0);
         if (bytes) *bytes = len;

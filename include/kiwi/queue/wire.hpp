@@ -27,8 +27,9 @@
 //     Payload byte b lives in chunk 1 + b/8.
 //   * A message of B bytes occupies message_lines(B) whole lines starting on a
 //     line; padding chunks of its last line carry tags (and zero data) so the
-//     producer always writes whole 64-byte lines (one PCIe write each) and the
-//     consumer validates a chunk with one masked compare of its 4 tags.
+//     producer always writes whole 64-byte lines (one PCIe write each).  The
+//     consumer validates the header and payload chunks (one masked compare of
+//     a chunk's 4 tags) and never reads the padding.
 //   * A message that reaches the end of the ring continues at line 0 with the
 //     next lap's tag.
 //

@@ -145,13 +145,24 @@ def test_corrupt_length_raises():
         q.try_pop()
 
 
-def test_wrong_tag_in_padding_blocks_pop():
+def test_padding_chunks_are_not_read():
+    """Only chunks that carry payload are validated: a message whose padding
+    chunks were never written pops (the next message starts on the next line)."""
+    q = kq.SPSCD2HQueue(4, host_only=True)
+    w = q.host_writer()
+    w.write_chunks(b"12345678", 3, 0, 2)  # header + the one payload chunk
+    w.advance(1)
+    assert q.try_pop() == (b"12345678", 3)
+    assert q.try_pop() is None
+
+
+def test_wrong_tag_in_payload_chunk_blocks_pop():
     q = kq.SPSCD2HQueue(4, host_only=True)
     w = q.host_writer()
     w.write_chunks(b"12345678", 3, 0, 4)
-    q.corrupt_line(0, 3, 0, 0, 0, 0)  # padding chunk never written
+    q.corrupt_line(0, 1, 0, 0, 0, 0)  # the payload chunk reads as never written
     assert q.try_pop() is None
-    w.write_chunks(b"12345678", 3, 3, 4)
+    w.write_chunks(b"12345678", 3, 1, 2)
     w.advance(1)
     assert q.try_pop() == (b"12345678", 3)
 
