@@ -1,0 +1,105 @@
+"""Property-based tests (hypothesis) of the host-side logic: any message
+stream through a host-only ring arrives intact and in order across
+wrap-around and tag cycles; any payload reaches its callback byte for byte;
+any valid EP configuration lays out aligned, non-overlapping heap regions.
+(Reference test categories: the queue basic/chunk tests, the invoke
+serializer tests and the EP layout tests of AMDResearch/kiwi.)"""
+import struct
+
+import pytest
+from hypothesis import HealthCheck, given, settings
+from hypothesis import strategies as st
+
+from kiwi_b200 import invoke
+from kiwi_b200 import queue as kq
+from kiwi_b200._native import load
+
+SETTINGS = dict(max_examples=60, deadline=None, suppress_health_check=[HealthCheck.too_slow])
+
+
+@settings(**SETTINGS)
+@given(log2cap=st.integers(min_value=0, max_value=6),
+       sizes=st.lists(st.integers(min_value=0, max_value=600), min_size=1, max_size=80),
+       seed=st.integers(min_value=0, max_value=2**32 - 1))
+def test_ring_delivers_any_stream_in_order(log2cap, sizes, seed):
+    cap = 1 << log2cap
+    max_bytes = min(kq.MAX_MESSAGE_BYTES, (cap * 4 - 1) * 8)
+    q = kq.SPSCD2HQueue(cap, host_only=True)
+    w = q.host_writer()
+    sent, got = [], []
+    x = seed | 1
+    for i, n in enumerate(sizes):
+        n = min(n, max_bytes)
+        payload = bytes(((x >> (8 * (j % 8))) + j) & 0xFF for j in range(n))
+        x = (x * 6364136223846793005 + 1442695040888963407) & (2**64 - 1)
+        while not w.try_push(payload, i & 0xFFFF):
+            r = q.try_pop()
+            assert r is not None, "a full ring must hold a message"
+            got.append(r)
+        sent.append((payload, i & 0xFFFF))
+    while (r := q.try_pop()) is not None:
+        got.append(r)
+    assert got == sent
+
+
+@settings(**SETTINGS)
+@given(payloads=st.lists(st.binary(min_size=0, max_size=512), min_size=1, max_size=40))
+def test_raw_callbacks_receive_every_payload(payloads):
+    ctx = invoke.Context(1, 128, host_only=True)
+    seen = []
+    cb = ctx.register_callback(lambda p: seen.append(bytes(p)))
+    for p in payloads:
+        try:
+            ctx.emulate_invoke(0, cb, p)
+        except Exception:
+            ctx.progress(0)
+            ctx.emulate_invoke(0, cb, p)
+    ctx.progress(0)
+    assert seen == payloads
+
+
+@settings(**SETTINGS)
+@given(vals=st.lists(st.tuples(st.integers(0, 2**64 - 1), st.integers(-2**31, 2**31 - 1),
+                               st.floats(allow_nan=False, width=32)), min_size=1, max_size=30))
+def test_typed_callbacks_unpack_packed_little_endian(vals):
+    ctx = invoke.Context(1, 64, host_only=True)
+    got = []
+    cb = ctx.register_callback(lambda a, b, c: got.append((a, b, c)), "<Qif")
+    for v in vals:
+        ctx.emulate_invoke(0, cb, struct.pack("<Qif", *v))
+        ctx.progress(0)
+    assert got == [(a, b, struct.unpack("<f", struct.pack("<f", c))[0]) for a, b, c in vals]
+
+
+@settings(**SETTINGS)
+@given(world=st.sampled_from([1, 2, 4, 8, 16]), hidden_blocks=st.integers(1, 32),
+       experts_per_rank=st.integers(1, 64), topk=st.integers(1, 16), max_tokens=st.integers(1, 8192),
+       quant=st.sampled_from(["none", "fp8", "nvfp4"]))
+def test_ep_layout_regions_aligned_and_disjoint(world, hidden_blocks, experts_per_rank, topk, max_tokens, quant):
+    ep = load().ep
+    experts = world * experts_per_rank
+    if topk > experts:
+        topk = experts
+    c = ep.finalize_config(dict(world=world, rank=world - 1, hidden=512 * hidden_blocks, num_experts=experts,
+                                topk=topk, max_tokens=max_tokens, quant=quant))
+    slots = world * max_tokens
+    hidden = 512 * hidden_blocks
+    regions = [("off_flags", 2 * 16 * 128), ("off_meta", slots * c["meta_bytes"]),
+               ("off_row", slots * c["row_bytes"]), ("off_scale", slots * c["scale_bytes"]),
+               ("off_comb", slots * hidden * 2), ("off_combk", max_tokens * topk * hidden * 2)]
+    spans = []
+    for name, size in regions:
+        assert c[name] % 256 == 0, name
+        spans.append((c[name], c[name] + size))
+    for (a0, a1), (b0, b1) in zip(spans, spans[1:]):
+        assert a1 <= b0
+    assert c["heap_bytes"] >= spans[-1][1]
+    assert c["meta_bytes"] % 16 == 0 and c["scale_bytes"] % 16 == 0 and c["row_bytes"] % 16 == 0
+    assert c["local_per_token"] == min(topk, experts_per_rank)
+
+
+def test_tag_cycle_never_zero_and_changes_every_lap():
+    for lap in list(range(0, 70000, 997)) + [65533, 65534, 65535, 65536, 131070, 131071]:
+        t0 = kq.lap_tag(lap * 16, 16)
+        t1 = kq.lap_tag((lap + 1) * 16, 16)
+        assert 1 <= t0 <= 65535 and t0 != t1
