@@ -161,16 +161,23 @@ __global__ void __launch_bounds__(GQ >= 0 ? kGatherThreads : kThreads, 1)
         if (lane == 0) {
             int stage = 0;
             uint32_t phase = 0;
+            int64_t n_prod = 0;
             for (int tile = blockIdx.x; tile < total_tiles && !*reinterpret_cast<volatile int*>(&s_abort); tile += gridDim.x) {
                 int g, mt, nt;
                 locate_tile(p.tile_prefix, p.num_groups, n_tiles, tile, g, mt, nt);
                 const int row0 = __ldg(&p.group_offset[g]) + mt * kBM;
                 const int brow0 = g * p.n + nt * BN;
                 for (int kb = 0; kb < k_blocks; ++kb) {
+                    const uint64_t tw0 = p.trace ? clock64() : 0;
                     if (!sm100::mbar_wait(&empty[stage], phase ^ 1)) {
                         fail(1);
                         break;
                     }
+                    if (p.trace && blockIdx.x == 0 && n_prod < p.trace_capacity) {
+                        p.trace[n_prod * kTraceSlots + 2] = tw0;
+                        p.trace[n_prod * kTraceSlots + 3] = clock64();
+                    }
+                    ++n_prod;
                     uint8_t* sa = smem + stage * S::kStageBytes;
                     uint8_t* sb = sa + S::kABytes;
                     if constexpr (GQ >= 0) {
@@ -194,6 +201,7 @@ __global__ void __launch_bounds__(GQ >= 0 ? kGatherThreads : kThreads, 1)
             uint32_t phase = 0;
             int acc = 0;
             uint32_t acc_phase = 0;
+            int64_t n_mma = 0;
             for (int tile = blockIdx.x; tile < total_tiles && !*reinterpret_cast<volatile int*>(&s_abort); tile += gridDim.x) {
                 if (!sm100::mbar_wait(&tmem_empty[acc], acc_phase ^ 1)) {
                     fail(2);
@@ -203,11 +211,17 @@ __global__ void __launch_bounds__(GQ >= 0 ? kGatherThreads : kThreads, 1)
                 const uint32_t d = tmem_base + acc * BN;
                 bool ok = true;
                 for (int kb = 0; kb < k_blocks; ++kb) {
+                    const uint64_t tw0 = p.trace ? clock64() : 0;
                     if (!sm100::mbar_wait(&full[stage], phase)) {
                         fail(3);
                         ok = false;
                         break;
                     }
+                    if (p.trace && blockIdx.x == 0 && n_mma < p.trace_capacity) {
+                        p.trace[n_mma * kTraceSlots + 0] = tw0;
+                        p.trace[n_mma * kTraceSlots + 1] = clock64();
+                    }
+                    ++n_mma;
                     sm100::tc_fence_after();
                     uint8_t* sa = smem + stage * S::kStageBytes;
                     uint8_t* sb = sa + S::kABytes;

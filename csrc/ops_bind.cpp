@@ -36,7 +36,8 @@ public:
     }
 
     /// counts: int32[G] rows per group (device); out: bf16 [rows, N] or [rows, N/2] with swiglu.
-    void run(torch::Tensor counts, torch::Tensor out, bool swiglu, py::object row_scale, int grid, bool pair) {
+    void run(torch::Tensor counts, torch::Tensor out, bool swiglu, py::object row_scale, int grid, bool pair,
+             py::object trace) {
         TORCH_CHECK(counts.is_cuda() && counts.scalar_type() == torch::kInt32 && counts.numel() == num_groups_,
                     "counts must be int32[num_groups] on the device");
         TORCH_CHECK(out.scalar_type() == torch::kBFloat16 && out.is_contiguous(), "out must be contiguous bf16");
@@ -63,6 +64,14 @@ public:
         args.row_scale = rs;
         args.error = reinterpret_cast<uint32_t*>(error_.data_ptr<int32_t>());
         args.max_rows = out.size(0);
+        if (!trace.is_none()) {
+            torch::Tensor t = trace.cast<torch::Tensor>();
+            TORCH_CHECK(t.is_cuda() && t.scalar_type() == torch::kInt64 && t.is_contiguous() && !pair,
+                        "trace must be a contiguous int64 CUDA tensor (1-SM kernel only)");
+            args.trace = reinterpret_cast<uint64_t*>(t.data_ptr<int64_t>());
+            args.trace_capacity = t.numel() / gemm::kTraceSlots;
+            trace_ref_ = t;
+        }
         if (pair) {
             gemm::grouped_gemm_pair(tmap_a_, tmap_b_half_, args, swiglu, grid, s);
         } else {
@@ -75,7 +84,7 @@ public:
     torch::Tensor error() const { return error_; }
 
 private:
-    torch::Tensor a_, b_, offsets_, tile_prefix_, error_, row_scale_ref_;
+    torch::Tensor a_, b_, offsets_, tile_prefix_, error_, row_scale_ref_, trace_ref_;
     int num_groups_, n_, k_;
     CUtensorMap tmap_a_, tmap_b_, tmap_b_half_;
 };
@@ -87,7 +96,8 @@ void register_ops(py::module_& m) {
     py::class_<GroupedGemm>(o, "GroupedGemm")
         .def(py::init<torch::Tensor, torch::Tensor, int64_t>(), py::arg("a"), py::arg("b"), py::arg("num_groups"))
         .def("run", &GroupedGemm::run, py::arg("counts"), py::arg("out"), py::arg("swiglu") = false,
-             py::arg("row_scale") = py::none(), py::arg("grid") = 0, py::arg("pair") = false)
+             py::arg("row_scale") = py::none(), py::arg("grid") = 0, py::arg("pair") = false,
+             py::arg("trace") = py::none())
         .def_property_readonly("offsets", &GroupedGemm::offsets)
         .def_property_readonly("tile_prefix", &GroupedGemm::tile_prefix)
         .def_property_readonly("error", &GroupedGemm::error);

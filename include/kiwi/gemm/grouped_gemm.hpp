@@ -23,7 +23,15 @@ struct GroupedArgs {
     const float* row_scale;       // optional per-row factor applied in the epilogue
     uint32_t* error;              // device word: non-zero if a bounded wait ran out
     int64_t max_rows;             // rows C holds: rows at or past it are never stored
+    // Optional pipeline trace of CTA 0 (null: off).  trace[0..n) of
+    // kTraceSlots each: {mma_wait_full_start, mma_wait_full_end,
+    // producer_wait_empty_start, producer_wait_empty_end} in SM clock cycles,
+    // one slot per k-block in issue order; trace_capacity slots at most.
+    uint64_t* trace;
+    int64_t trace_capacity;
 };
+
+inline constexpr int kTraceSlots = 4;
 
 /// Scatter epilogue of the fused MoE combine (grouped_gemm_scatter): result
 /// row r, scaled by row_scale[r] and converted to bf16, is stored at byte
