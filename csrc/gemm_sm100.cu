@@ -56,10 +56,10 @@ static_assert(kScatterMaxRanks == p2p::kMaxRanks, "ScatterArgs holds one base pe
 /// BN/2 columns (256 bytes each, 16-byte chunks XOR-swizzled by row so that
 /// both the row-per-thread writes and the row-wise reads are conflict-free),
 /// then the barriers.
-template <int BN, int STAGES = kStages, bool STAGING = false, int GQ = -1>
+template <int BN, int STAGES = kStages, bool STAGING = false, int GQ = -1, int BKT = kBK>
 struct Smem {
-    static constexpr int kABytes = kBM * kBK * 2;
-    static constexpr int kBBytes = BN * kBK * 2;
+    static constexpr int kABytes = kBM * BKT * 2;
+    static constexpr int kBBytes = BN * BKT * 2;
     static constexpr int kStageBytes = kABytes + kBBytes;
     static constexpr int kStgStride = BN;  // BN/2 bf16 columns = BN bytes per staged row
     static constexpr int kStgOffset = STAGES * kStageBytes;
@@ -104,12 +104,14 @@ __device__ __forceinline__ void store_row32(__nv_bfloat16* dst, const float (&v)
     for (int i = 0; i < 4; ++i) d[i] = out[i];
 }
 
-template <int BN, int EPI, int STAGES, int GQ = -1>
+template <int BN, int EPI, int STAGES, int GQ = -1, int BKT = kBK>
 __global__ void __launch_bounds__(GQ >= 0 ? kGatherThreads : kThreads, 1)
     grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                         GroupedArgs p, const __grid_constant__ ScatterArgs sc, const __grid_constant__ GatherArgs ga) {
     constexpr int kStages = STAGES;
-    using S = Smem<BN, STAGES, EPI == kEpiScatter, GQ>;
+    constexpr int kBK = BKT;  // K per stage (64: 128-byte swizzle, 32: 64-byte swizzle)
+    static_assert(GQ < 0 || BKT == 64, "the gathering producer writes 128-byte rows");
+    using S = Smem<BN, STAGES, EPI == kEpiScatter, GQ, BKT>;
     __shared__ uint8_t* s_base[kScatterMaxRanks];
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -225,11 +227,11 @@ __global__ void __launch_bounds__(GQ >= 0 ? kGatherThreads : kThreads, 1)
                     sm100::tc_fence_after();
                     uint8_t* sa = smem + stage * S::kStageBytes;
                     uint8_t* sb = sa + S::kABytes;
-                    const uint64_t adesc = sm100::sw128_kmajor_desc(sa);
-                    const uint64_t bdesc = sm100::sw128_kmajor_desc(sb);
+                    const uint64_t adesc = sm100::kmajor_desc<BKT>(sa);
+                    const uint64_t bdesc = sm100::kmajor_desc<BKT>(sb);
 #pragma unroll
                     for (int kk = 0; kk < kBK / 16; ++kk) {
-                        // +32 bytes of K per step inside the 128-byte swizzle atom.
+                        // +32 bytes of K per step inside the swizzle atom.
                         sm100::mma_bf16(d, adesc + 2 * kk, bdesc + 2 * kk, idesc, (kb | kk) != 0 ? 1u : 0u);
                     }
                     sm100::mma_commit(&empty[stage]);
@@ -726,7 +728,7 @@ __global__ void build_schedule_kernel(const int32_t* counts, int num_groups, int
 
 }  // namespace
 
-CUtensorMap make_tmap_bf16_2d(const void* ptr, uint64_t rows, uint64_t cols, uint32_t box_rows) {
+CUtensorMap make_tmap_bf16_2d(const void* ptr, uint64_t rows, uint64_t cols, uint32_t box_rows, uint32_t box_k) {
     static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
     if (!encode) {
         void* fn = nullptr;
@@ -741,10 +743,12 @@ CUtensorMap make_tmap_bf16_2d(const void* ptr, uint64_t rows, uint64_t cols, uin
     CUtensorMap m;
     const cuuint64_t dims[2] = {cols, rows};
     const cuuint64_t strides[1] = {cols * 2};
-    const cuuint32_t box[2] = {static_cast<cuuint32_t>(kBK), box_rows};
+    if (box_k != 64 && box_k != 32) throw kiwi::error("make_tmap_bf16_2d: box_k must be 64 or 32");
+    const cuuint32_t box[2] = {box_k, box_rows};
     const cuuint32_t estr[2] = {1, 1};
     const CUresult r = encode(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, estr,
-                              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                              CU_TENSOR_MAP_INTERLEAVE_NONE,
+                              box_k == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
                               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     p2p::check_cu(r, "cuTensorMapEncodeTiled");
     return m;
@@ -772,18 +776,18 @@ int num_sms() {
 
 namespace {
 
-template <int EPI, int STAGES, int GQ = -1>
+template <int EPI, int STAGES, int GQ = -1, int BKT = kBK>
 void launch_grouped(const CUtensorMap& tmap_a, const CUtensorMap& tmap_b, const GroupedArgs& args,
                     const ScatterArgs& sc, int grid, cudaStream_t stream, const GatherArgs& ga = GatherArgs{}) {
     constexpr int BN = 256;
-    const int smem = Smem<BN, STAGES, EPI == kEpiScatter, GQ>::kBytes;
+    const int smem = Smem<BN, STAGES, EPI == kEpiScatter, GQ, BKT>::kBytes;
     static bool attr = false;
     if (!attr) {
-        KIWI_CUDA_CHECK(cudaFuncSetAttribute(grouped_gemm_kernel<BN, EPI, STAGES, GQ>,
+        KIWI_CUDA_CHECK(cudaFuncSetAttribute(grouped_gemm_kernel<BN, EPI, STAGES, GQ, BKT>,
                                              cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
         attr = true;
     }
-    grouped_gemm_kernel<BN, EPI, STAGES, GQ>
+    grouped_gemm_kernel<BN, EPI, STAGES, GQ, BKT>
         <<<grid, GQ >= 0 ? kGatherThreads : kThreads, smem, stream>>>(tmap_a, tmap_b, args, sc, ga);
     KIWI_CUDA_CHECK(cudaGetLastError());
 }
@@ -803,6 +807,19 @@ void grouped_gemm(const CUtensorMap& tmap_a, const CUtensorMap& tmap_b, const Gr
     const ScatterArgs none{};
     if (swiglu) launch_grouped<kEpiSwiGLU, kStages>(tmap_a, tmap_b, args, none, grid, stream);
     else launch_grouped<kEpiStore, kStages>(tmap_a, tmap_b, args, none, grid, stream);
+}
+
+constexpr int kBk32Stages = 9;  // 9 x 24 KB stages
+
+void grouped_gemm_bk32(const CUtensorMap& tmap_a32, const CUtensorMap& tmap_b32, const GroupedArgs& args,
+                       bool swiglu, int grid, cudaStream_t stream) {
+    if (args.n % 256 != 0 || args.k % 32 != 0) {
+        throw kiwi::error("grouped_gemm_bk32: N must be a multiple of 256 and K of 32");
+    }
+    if (grid <= 0) grid = num_sms();
+    const ScatterArgs none{};
+    if (swiglu) launch_grouped<kEpiSwiGLU, kBk32Stages, -1, 32>(tmap_a32, tmap_b32, args, none, grid, stream);
+    else launch_grouped<kEpiStore, kBk32Stages, -1, 32>(tmap_a32, tmap_b32, args, none, grid, stream);
 }
 
 void grouped_gemm_gather(const CUtensorMap& tmap_b, const GroupedArgs& args, const GatherArgs& ga, int grid,

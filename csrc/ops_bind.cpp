@@ -29,6 +29,10 @@ public:
         tmap_a_ = gemm::make_tmap_bf16_2d(a.data_ptr(), a.size(0), k_, 128);
         tmap_b_ = gemm::make_tmap_bf16_2d(b.data_ptr(), b.size(0), k_, 256);
         tmap_b_half_ = gemm::make_tmap_bf16_2d(b.data_ptr(), b.size(0), k_, 128);
+        if (k_ % 32 == 0) {
+            tmap_a32_ = gemm::make_tmap_bf16_2d(a.data_ptr(), a.size(0), k_, 128, 32);
+            tmap_b32_ = gemm::make_tmap_bf16_2d(b.data_ptr(), b.size(0), k_, 256, 32);
+        }
         auto iopts = torch::TensorOptions().dtype(torch::kInt32).device(a.device());
         offsets_ = torch::zeros({num_groups_ + 1}, iopts);
         tile_prefix_ = torch::zeros({num_groups_ + 1}, iopts);
@@ -37,7 +41,9 @@ public:
 
     /// counts: int32[G] rows per group (device); out: bf16 [rows, N] or [rows, N/2] with swiglu.
     void run(torch::Tensor counts, torch::Tensor out, bool swiglu, py::object row_scale, int grid, bool pair,
-             py::object trace) {
+             py::object trace, int bk) {
+        TORCH_CHECK(bk == 64 || bk == 32, "bk must be 64 or 32");
+        TORCH_CHECK(bk == 64 || (!pair && trace.is_none()), "bk = 32 is a 1-SM variant without trace");
         TORCH_CHECK(counts.is_cuda() && counts.scalar_type() == torch::kInt32 && counts.numel() == num_groups_,
                     "counts must be int32[num_groups] on the device");
         TORCH_CHECK(out.scalar_type() == torch::kBFloat16 && out.is_contiguous(), "out must be contiguous bf16");
@@ -72,7 +78,9 @@ public:
             args.trace_capacity = t.numel() / gemm::kTraceSlots;
             trace_ref_ = t;
         }
-        if (pair) {
+        if (bk == 32) {
+            gemm::grouped_gemm_bk32(tmap_a32_, tmap_b32_, args, swiglu, grid, s);
+        } else if (pair) {
             gemm::grouped_gemm_pair(tmap_a_, tmap_b_half_, args, swiglu, grid, s);
         } else {
             gemm::grouped_gemm(tmap_a_, tmap_b_, args, swiglu, grid, s);
@@ -86,7 +94,7 @@ public:
 private:
     torch::Tensor a_, b_, offsets_, tile_prefix_, error_, row_scale_ref_, trace_ref_;
     int num_groups_, n_, k_;
-    CUtensorMap tmap_a_, tmap_b_, tmap_b_half_;
+    CUtensorMap tmap_a_, tmap_b_, tmap_b_half_, tmap_a32_, tmap_b32_;
 };
 
 }  // namespace
@@ -97,7 +105,7 @@ void register_ops(py::module_& m) {
         .def(py::init<torch::Tensor, torch::Tensor, int64_t>(), py::arg("a"), py::arg("b"), py::arg("num_groups"))
         .def("run", &GroupedGemm::run, py::arg("counts"), py::arg("out"), py::arg("swiglu") = false,
              py::arg("row_scale") = py::none(), py::arg("grid") = 0, py::arg("pair") = false,
-             py::arg("trace") = py::none())
+             py::arg("trace") = py::none(), py::arg("bk") = 64)
         .def_property_readonly("offsets", &GroupedGemm::offsets)
         .def_property_readonly("tile_prefix", &GroupedGemm::tile_prefix)
         .def_property_readonly("error", &GroupedGemm::error);

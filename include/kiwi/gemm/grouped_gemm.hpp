@@ -76,9 +76,12 @@ struct KernelInfo {
     int smem_bytes;
 };
 
-/// Tensor map of a row-major [rows, cols] bf16 matrix, box [box_rows, 64],
-/// 128-byte swizzle (the layout the kernel's shared-memory descriptors expect).
-CUtensorMap make_tmap_bf16_2d(const void* ptr, uint64_t rows, uint64_t cols, uint32_t box_rows);
+/// Tensor map of a row-major [rows, cols] bf16 matrix, box [box_rows, box_k]:
+/// box_k 64 with the 128-byte swizzle (grouped_gemm and friends) or 32 with
+/// the 64-byte swizzle (grouped_gemm_bk32), the layouts the kernels'
+/// shared-memory descriptors expect.
+CUtensorMap make_tmap_bf16_2d(const void* ptr, uint64_t rows, uint64_t cols, uint32_t box_rows,
+                              uint32_t box_k = 64);
 
 /// Builds group offsets and the tile prefix from per-group row counts (device).
 /// `bm` = rows per tile: 128 for grouped_gemm, 256 for grouped_gemm_pair.
@@ -88,6 +91,14 @@ void build_schedule(const int32_t* counts, int num_groups, int n, int bn, int32_
 /// Launches the persistent grouped GEMM (BN = 256).  `grid` <= 0: one CTA per SM.
 void grouped_gemm(const CUtensorMap& tmap_a, const CUtensorMap& tmap_b, const GroupedArgs& args, bool swiglu,
                   int grid, cudaStream_t stream);
+
+/// Variant with 32-column K stages (64-byte swizzle, 9 stages of 24 KB): more
+/// lookahead per byte of shared memory for operand loads whose latency the
+/// 4 x 48 KB stages of grouped_gemm do not cover.  Tensor maps from
+/// make_tmap_bf16_2d(..., box_k = 32).  Same results as grouped_gemm (the
+/// same K = 16 MMA sequence).
+void grouped_gemm_bk32(const CUtensorMap& tmap_a32, const CUtensorMap& tmap_b32, const GroupedArgs& args,
+                       bool swiglu, int grid, cudaStream_t stream);
 
 /// 2-SM variant (clusters of two CTAs, 256 x 256 tiles).  `tmap_b_half` must
 /// have a box of 128 rows (each CTA loads half of the 256-row B tile); the

@@ -138,6 +138,30 @@ KIWI_DEV uint64_t sw128_kmajor_desc(const void* smem_tile) {
     return d;
 }
 
+/// Same for a K-major tile of 64-byte rows (32 bf16 of K) as a TMA load with
+/// CU_TENSOR_MAP_SWIZZLE_64B writes it: 8-row groups 512 B apart, layout
+/// SWIZZLE_64B = 4 (the canonical K-major B64 layout
+/// Swizzle<2,4,3> o ((8,m),2):((4,SBO),1) in 16-byte units).
+KIWI_DEV uint64_t sw64_kmajor_desc(const void* smem_tile) {
+    const uint64_t addr = smem_addr(smem_tile);
+    uint64_t d = 0;
+    d |= (addr >> 4) & 0x3FFFull;
+    d |= static_cast<uint64_t>(1) << 16;           // LBO (16 B)
+    d |= static_cast<uint64_t>(512 >> 4) << 32;    // SBO = 512 B between 8-row groups
+    d |= static_cast<uint64_t>(1) << 46;           // descriptor version (sm100)
+    d |= static_cast<uint64_t>(4) << 61;           // SWIZZLE_64B
+    return d;
+}
+
+/// Descriptor of a K-major tile whose rows hold BK bf16 (64: 128-byte swizzle,
+/// 32: 64-byte swizzle).
+template <int BK>
+KIWI_DEV uint64_t kmajor_desc(const void* smem_tile) {
+    static_assert(BK == 64 || BK == 32, "BK must be 64 or 32");
+    if constexpr (BK == 64) return sw128_kmajor_desc(smem_tile);
+    else return sw64_kmajor_desc(smem_tile);
+}
+
 /// Instruction descriptor, kind::f16 with BF16 A/B, FP32 accumulate, both K-major.
 KIWI_HD constexpr uint32_t idesc_bf16_f32(uint32_t m, uint32_t n) {
     return (1u << 4)            // D format: F32
