@@ -47,6 +47,9 @@ def main():
     ap.add_argument("--groups", type=int, default=None, help="override the group count")
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--no-torch", action="store_true")
+    ap.add_argument("--no-pair", action="store_true", help="skip the 2-SM (cta_group::2) kernel")
+    ap.add_argument("--bk", type=int, default=64, choices=(64, 32),
+                    help="K columns per pipeline stage of the 1-SM kernel (32: 64-byte swizzle, 9 stages)")
     args = ap.parse_args()
     C = kiwi_b200.native()
     torch.manual_seed(0)
@@ -60,8 +63,10 @@ def main():
         counts = torch.full((groups,), rows, dtype=torch.int32, device="cuda")
         out = torch.empty(total, n // 2 if swiglu else n, device="cuda", dtype=torch.bfloat16)
         plan = C.ops.GroupedGemm(a, b, groups)
-        ms = timeit(lambda: plan.run(counts, out, swiglu), args.iters)
-        ms_pair = timeit(lambda: plan.run(counts, out, swiglu, None, 0, True), args.iters) if rows >= 256 else float("nan")
+        ms = timeit(lambda: plan.run(counts, out, swiglu, None, 0, False, None, args.bk), args.iters)
+        ms_pair = float("nan")
+        if rows >= 256 and not args.no_pair:
+            ms_pair = timeit(lambda: plan.run(counts, out, swiglu, None, 0, True), args.iters)
         flops = 2.0 * total * n * k
         bw = (b.numel() * 2 + a.numel() * 2 + out.numel() * 2) / (ms / 1e3) / 1e12
         offs = torch.cumsum(counts, 0).to(torch.int32)
@@ -72,7 +77,7 @@ def main():
                 tms = timeit(lambda: torch._grouped_mm(a, bt, offs=offs, out_dtype=torch.bfloat16), args.iters)
             except Exception as ex:  # pragma: no cover
                 print("torch._grouped_mm failed:", ex, file=sys.stderr)
-        print("RESULT " + json.dumps({"bench": name, "groups": groups, "rows": rows, "k": k, "n": n,
+        print("RESULT " + json.dumps({"bench": name, "groups": groups, "rows": rows, "k": k, "n": n, "bk": args.bk,
                                       "kiwi_ms": ms, "kiwi_tflops": flops / ms / 1e9,
                                       "kiwi_pair_ms": ms_pair, "kiwi_pair_tflops": flops / ms_pair / 1e9,
                                       "kiwi_hbm_TBps_min_traffic": bw,

@@ -43,7 +43,7 @@ public:
     void run(torch::Tensor counts, torch::Tensor out, bool swiglu, py::object row_scale, int grid, bool pair,
              py::object trace, int bk) {
         TORCH_CHECK(bk == 64 || bk == 32, "bk must be 64 or 32");
-        TORCH_CHECK(bk == 64 || (!pair && trace.is_none()), "bk = 32 is a 1-SM variant without trace");
+        TORCH_CHECK(bk == 64 || !pair, "bk = 32 is a 1-SM variant");
         TORCH_CHECK(counts.is_cuda() && counts.scalar_type() == torch::kInt32 && counts.numel() == num_groups_,
                     "counts must be int32[num_groups] on the device");
         TORCH_CHECK(out.scalar_type() == torch::kBFloat16 && out.is_contiguous(), "out must be contiguous bf16");
