@@ -31,6 +31,9 @@ def main():
     ap.add_argument("--experts", type=int, default=None, help="override the expert count (small profiling cases)")
     ap.add_argument("--unfused", action="store_true", help="GEMM2 to local memory + combine send/receive")
     ap.add_argument("--gather", action="store_true", help="GEMM1 gathers its A rows from the receive slots")
+    ap.add_argument("--debug-timing", action="store_true",
+                    help="after the timed loop, run one round with device phase timing and print every rank's "
+                         "per-kernel spans (first block start to last warp end, flag waits)")
     args = ap.parse_args()
     rank, world = kdist.init()
     cfg = moe_model.CONFIGS[args.config]
@@ -67,6 +70,19 @@ def main():
             for i in range(len(names)):
                 acc[i] += ev[i].elapsed_time(ev[i + 1])
     layer.check()
+    if args.debug_timing:
+        # Outside the timed loop: one more round with the stamps on.
+        from kiwi_b200.parallel.ep import format_debug_timing
+
+        layer.set_debug_timing_enabled(True)
+        kdist.barrier()
+        layer(x, logits, out)
+        snap = layer.get_debug_timing_snapshot()
+        layer.set_debug_timing_enabled(False)
+        for r in range(world):
+            if r == rank:
+                print(format_debug_timing(snap, f"ep-{args.config}"), flush=True)
+            kdist.barrier()
     res = {n: kdist.max_over_ranks(a / args.steps * 1e3) for n, a in zip(names, acc)}
     counts = layer.expert_counts.float()
     if rank == 0:

@@ -7,11 +7,15 @@
 // weight into the second), combine over NVLink and the final reduction, all
 // enqueued on the current torch stream with no host synchronisation.
 #include <ATen/cuda/CUDAContext.h>
+#include <array>
+#include <cstring>
+#include <vector>
 #include <pybind11/pybind11.h>
 #include <pybind11/stl.h>
 #include <torch/extension.h>
 
 #include "kiwi/ep/config.hpp"
+#include "kiwi/ep/debug_timing.hpp"
 #include "kiwi/ep/kernels.hpp"
 #include "kiwi/ep/tuning.hpp"
 #include "kiwi/gemm/grouped_gemm.hpp"
@@ -79,6 +83,68 @@ py::dict tuning_dict(const ep::EpTuning& t) {
     d["gemm_pair"] = t.gemm_pair;
     d["source"] = t.source;
     return d;
+}
+
+/// Device phase-timing buffer of one EP op (allocated on first enable).
+/// Rounds reset it with one memset; a snapshot synchronises the stream.
+class DebugTiming {
+public:
+    uint64_t* enable(bool on, torch::Device dev) {
+        if (on && !buf_.defined()) {
+            buf_ = torch::zeros({ep::kDebugTimeWords}, torch::TensorOptions().dtype(torch::kInt64).device(dev));
+        }
+        on_ = on;
+        if (on) buf_.zero_();
+        return ptr();
+    }
+    bool on() const { return on_; }
+    uint64_t* ptr() const { return on_ ? reinterpret_cast<uint64_t*>(buf_.data_ptr<int64_t>()) : nullptr; }
+    /// Zeroes every slot on `s` (a memset node when captured in a graph).
+    void reset(cudaStream_t s) const {
+        if (on_) {
+            KIWI_CUDA_CHECK(cudaMemsetAsync(buf_.data_ptr(), 0, ep::kDebugTimeWords * sizeof(uint64_t), s));
+        }
+    }
+    /// {"enabled", "clock", "wall_clock_rate_khz", "time_ticks" (absolute ns, 0 = not recorded),
+    ///  "meta", "phase_names", "meta_names"}.
+    py::dict snapshot(const std::vector<int32_t>& meta) const {
+        cudaStreamCaptureStatus st = cudaStreamCaptureStatusNone;
+        KIWI_CUDA_CHECK(cudaStreamIsCapturing(cur_stream(), &st));
+        TORCH_CHECK(st == cudaStreamCaptureStatusNone, "get_debug_timing_snapshot: not allowed during graph capture");
+        std::vector<uint64_t> raw(ep::kDebugTimeWords, 0), ticks(ep::kDebugTimeWords, 0);
+        if (buf_.defined()) {
+            auto h = buf_.cpu();  // ordered after the round's kernels on the current stream
+            std::memcpy(raw.data(), h.data_ptr<int64_t>(), raw.size() * sizeof(uint64_t));
+            ep::decode_debug_words(raw.data(), ticks.data(), ep::kDebugTimeWords);
+        }
+        std::vector<int32_t> m(ep::kDebugMetaWords, 0);
+        for (size_t i = 0; i < meta.size() && i < m.size(); ++i) m[i] = meta[i];
+        py::dict d;
+        d["enabled"] = on_;
+        d["clock"] = "globaltimer_ns";
+        d["wall_clock_rate_khz"] = 1000000;
+        d["time_ticks"] = py::cast(ticks);
+        d["meta"] = py::cast(m);
+        py::list pn, mn;
+        for (int i = 0; i < ep::kNumDebugPhases; ++i) pn.append(ep::debug_phase_name(i));
+        for (int i = 0; i < ep::kNumDebugMeta; ++i) mn.append(ep::debug_meta_name(i));
+        d["phase_names"] = pn;
+        d["meta_names"] = mn;
+        return d;
+    }
+
+private:
+    torch::Tensor buf_;
+    bool on_ = false;
+};
+
+/// Per-source token counts of the last round (ws.slot_tokens) as {received, remote, self}.
+std::array<int32_t, 3> recv_token_meta(const torch::Tensor& slot_tokens, const ep::EpConfig& c) {
+    auto t = slot_tokens.cpu();
+    int32_t all = 0;
+    for (int r = 0; r < c.world && r < t.size(0); ++r) all += t[r].item<int32_t>();
+    const int32_t self = c.rank < t.size(0) ? t[c.rank].item<int32_t>() : 0;
+    return {all, all - self, self};
 }
 
 class MoeLayer {
@@ -151,13 +217,19 @@ public:
     void route(torch::Tensor logits, torch::Tensor idx, torch::Tensor w) {
         TORCH_CHECK(logits.scalar_type() == torch::kFloat32 && logits.is_contiguous(), "logits must be fp32");
         TORCH_CHECK(logits.size(1) == cfg_.num_experts, "logits must be [T, num_experts]");
+        cudaStream_t s = cur_stream();
+        debug_.reset(s);
+        routed_ = true;
         ep::launch_route(logits.data_ptr<float>(), static_cast<int>(logits.size(0)), cfg_.num_experts, cfg_.topk,
-                         idx.data_ptr<int32_t>(), w.data_ptr<float>(), cur_stream());
+                         idx.data_ptr<int32_t>(), w.data_ptr<float>(), s, ws_.debug_time);
     }
 
     void dispatch(torch::Tensor x, torch::Tensor idx, torch::Tensor w) {
         check_tokens(x, idx, w);
         cudaStream_t s = cur_stream();
+        if (!routed_) debug_.reset(s);  // a round starts at route() when the layer routes
+        routed_ = false;
+        tokens_ = static_cast<int>(x.size(0));
         ep::launch_begin(cfg_, ws_, s);
         ep::launch_dispatch(cfg_, heap_.view(), reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()),
                             idx.data_ptr<int32_t>(), w.data_ptr<float>(), static_cast<int>(x.size(0)), ws_,
@@ -200,6 +272,7 @@ public:
         g1.row_scale = nullptr;
         g1.error = reinterpret_cast<uint32_t*>(gemm_error_.data_ptr<int32_t>());
         g1.max_rows = cfg_.max_pairs();
+        g1.span = debug_.on() ? ws_.debug_time + ep::kDebugWordsPerPhase * ep::kPhaseGemm1 : nullptr;
         if (which == 1) {
             if (gathers()) {
                 gemm::GatherArgs ga{};
@@ -225,6 +298,7 @@ public:
         g2.c = reinterpret_cast<__nv_bfloat16*>(y_.data_ptr());
         g2.ldc = cfg_.hidden;
         g2.row_scale = ws_.pair_w;
+        g2.span = debug_.on() ? ws_.debug_time + ep::kDebugWordsPerPhase * ep::kPhaseGemm2 : nullptr;
         if (fused_) {
             // Fused combine: the epilogue stores every weighted row straight into
             // its token owner's combk slot over NVLink and the last CTA signals.
@@ -282,6 +356,31 @@ public:
         gemm_error_.zero_();
     }
 
+    void set_debug_timing_enabled(bool on) { ws_.debug_time = debug_.enable(on, w13_.device()); }
+    bool debug_timing_enabled() const { return debug_.on(); }
+    py::dict debug_timing_snapshot() const {
+        std::vector<int32_t> m(ep::kNumDebugMeta, 0);
+        const auto rt = recv_token_meta(slot_tokens_, cfg_);
+        m[ep::kMetaRank] = cfg_.rank;
+        m[ep::kMetaWorld] = cfg_.world;
+        m[ep::kMetaTokens] = tokens_;
+        m[ep::kMetaRecvTokens] = rt[0];
+        m[ep::kMetaRecvRemote] = rt[1];
+        m[ep::kMetaRecvSelf] = rt[2];
+        m[ep::kMetaExpertRows] = offsets_[cfg_.experts_per_rank].item<int32_t>();
+        m[ep::kMetaDispatchBlocks] = tuning_.dispatch_blocks;
+        m[ep::kMetaRecvBlocks] = tuning_.recv_blocks;
+        m[ep::kMetaCombineBlocks] = tuning_.combine_blocks;
+        m[ep::kMetaHidden] = cfg_.hidden;
+        m[ep::kMetaTopk] = cfg_.topk;
+        m[ep::kMetaExpertsPerRank] = cfg_.experts_per_rank;
+        m[ep::kMetaQuant] = cfg_.quant;
+        m[ep::kMetaFusedCombine] = fused_;
+        m[ep::kMetaGatherA] = gathers();
+        m[ep::kMetaGemmPair] = pair_;
+        return debug_.snapshot(m);
+    }
+
     py::dict config() const { return config_to_dict(cfg_); }
     torch::Tensor expert_counts() const { return counts_; }
     torch::Tensor expert_offsets() const { return offsets_; }
@@ -321,6 +420,9 @@ private:
     bool fused_ = true;
     bool gather_ = false;
     ep::EpTuning tuning_{};
+    DebugTiming debug_;
+    bool routed_ = false;
+    int tokens_ = 0;
 
 public:
     bool gather() const { return gather_; }
@@ -375,6 +477,7 @@ public:
         cudaStream_t s = cur_stream();
         idx_in_ = idx;
         tokens_ = static_cast<int>(x.size(0));
+        debug_.reset(s);
         ep::launch_begin(cfg_, ws_, s);
         ep::launch_dispatch(cfg_, heap_.view(), reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()),
                             idx.data_ptr<int32_t>(), w.data_ptr<float>(), tokens_, ws_, 0, s);
@@ -409,6 +512,25 @@ public:
     torch::Tensor src_token_pos() const { return src_pos_; }
     py::dict config() const { return config_to_dict(cfg_); }
 
+    void set_debug_timing_enabled(bool on) { ws_.debug_time = debug_.enable(on, epoch_.device()); }
+    bool debug_timing_enabled() const { return debug_.on(); }
+    py::dict debug_timing_snapshot() const {
+        std::vector<int32_t> m(ep::kNumDebugMeta, 0);
+        const auto rt = recv_token_meta(slot_tokens_, cfg_);
+        m[ep::kMetaRank] = cfg_.rank;
+        m[ep::kMetaWorld] = cfg_.world;
+        m[ep::kMetaTokens] = tokens_;
+        m[ep::kMetaRecvTokens] = rt[0];
+        m[ep::kMetaRecvRemote] = rt[1];
+        m[ep::kMetaRecvSelf] = rt[2];
+        m[ep::kMetaExpertRows] = recv_count_.cpu()[0].item<int32_t>();
+        m[ep::kMetaHidden] = cfg_.hidden;
+        m[ep::kMetaTopk] = cfg_.topk;
+        m[ep::kMetaExpertsPerRank] = cfg_.experts_per_rank;
+        m[ep::kMetaQuant] = cfg_.quant;
+        return debug_.snapshot(m);
+    }
+
 private:
     p2p::SymmetricHeap& heap_;
     ep::EpConfig cfg_;
@@ -417,6 +539,7 @@ private:
     torch::Tensor epoch_, done_, counts_, cursor_, slot_tokens_, error_, slot_compact_, recv_count_, rows_, scales_,
         idx_, w_, src_pos_, idx_in_;
     ep::EpWorkspace ws_{};
+    DebugTiming debug_;
 };
 
 }  // namespace
@@ -424,6 +547,22 @@ private:
 void register_ep(py::module_& m) {
     auto e = m.def_submodule("ep", "kiwi::ep (expert-parallel MoE)");
     e.attr("MAX_TOPK") = ep::kMaxTopk;
+    e.attr("DEBUG_TIME_WORDS") = ep::kDebugTimeWords;
+    e.attr("DEBUG_WORDS_PER_PHASE") = ep::kDebugWordsPerPhase;
+    {
+        py::list pn, mn;
+        for (int i = 0; i < ep::kNumDebugPhases; ++i) pn.append(ep::debug_phase_name(i));
+        for (int i = 0; i < ep::kNumDebugMeta; ++i) mn.append(ep::debug_meta_name(i));
+        e.attr("DEBUG_PHASES") = pn;
+        e.attr("DEBUG_META") = mn;
+    }
+    e.def("decode_debug_words",
+          [](const std::vector<uint64_t>& raw) {
+              std::vector<uint64_t> out(raw.size(), 0);
+              ep::decode_debug_words(raw.data(), out.data(), static_cast<int>(raw.size()));
+              return out;
+          },
+          "Raw phase words (start slots hold ~t) -> absolute ns, 0 = not recorded.");
     e.def("finalize_config", [](const py::dict& d) { return config_to_dict(config_from_dict(d)); });
     e.def("tune", [](const py::dict& d, int sms, py::object env) {
               std::string ev;
@@ -445,6 +584,9 @@ void register_ep(py::module_& m) {
         .def("dispatch", &Transport::dispatch)
         .def("combine", &Transport::combine)
         .def("error", &Transport::error)
+        .def("set_debug_timing_enabled", &Transport::set_debug_timing_enabled, py::arg("enabled"))
+        .def_property_readonly("debug_timing_enabled", &Transport::debug_timing_enabled)
+        .def("get_debug_timing_snapshot", &Transport::debug_timing_snapshot)
         .def_property_readonly("src_token_pos", &Transport::src_token_pos)
         .def_property_readonly("config", &Transport::config);
     py::class_<MoeLayer>(e, "MoeLayer")
@@ -460,6 +602,11 @@ void register_ep(py::module_& m) {
         .def("forward", &MoeLayer::forward)
         .def("error", &MoeLayer::error)
         .def("clear_error", &MoeLayer::clear_error)
+        .def("set_debug_timing_enabled", &MoeLayer::set_debug_timing_enabled, py::arg("enabled"),
+             "Per-kernel %globaltimer spans of every round (first block start, last warp end, flag waits).")
+        .def_property_readonly("debug_timing_enabled", &MoeLayer::debug_timing_enabled)
+        .def("get_debug_timing_snapshot", &MoeLayer::debug_timing_snapshot,
+             "Synchronises the current stream and returns the last round's phase stamps.")
         .def_property_readonly("config", &MoeLayer::config)
         .def_property_readonly("expert_counts", &MoeLayer::expert_counts)
         .def_property_readonly("expert_offsets", &MoeLayer::expert_offsets)

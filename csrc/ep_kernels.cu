@@ -22,6 +22,7 @@
 
 #include <algorithm>
 
+#include "kiwi/ep/debug_timing.hpp"
 #include "kiwi/ep/kernels.hpp"
 #include "kiwi/ep/quant.cuh"
 #include "kiwi/ptx.cuh"
@@ -80,12 +81,14 @@ KIWI_DEV void grid_done_signal(const EpConfig& c, const p2p::HeapView& h, uint32
 /// `epoch`; returns false (error recorded) on timeout.  Block-collective.
 template <typename FlagOf>
 KIWI_DEV bool wait_all_flags(const EpConfig& c, const p2p::HeapView& h, const EpWorkspace& ws, uint32_t epoch,
-                             FlagOf flag_of, uint32_t site, uint64_t timeout_ns, uint32_t* tokens_out) {
+                             FlagOf flag_of, uint32_t site, uint64_t timeout_ns, uint32_t* tokens_out,
+                             const PhaseScope& ps) {
     __shared__ int s_fail;
     if (threadIdx.x == 0) s_fail = 0;
     __syncthreads();
     if (threadIdx.x < static_cast<unsigned>(c.world)) {
         const uint64_t* f = reinterpret_cast<const uint64_t*>(h.base[h.rank] + flag_of(threadIdx.x));
+        ps.wait_begin();
         ptx::Deadline dl(timeout_ns);
         uint64_t v = ptx::ld_acquire_sys_u64(f);
         while (static_cast<uint32_t>(v >> 32) != epoch) {
@@ -96,6 +99,7 @@ KIWI_DEV bool wait_all_flags(const EpConfig& c, const p2p::HeapView& h, const Ep
             }
             v = ptx::ld_acquire_sys_u64(f);
         }
+        ps.wait_end();
         if (tokens_out) tokens_out[threadIdx.x] = static_cast<uint32_t>(v);
     }
     __syncthreads();
@@ -105,6 +109,7 @@ KIWI_DEV bool wait_all_flags(const EpConfig& c, const p2p::HeapView& h, const Ep
 // ---------------------------------------------------------------------------
 
 __global__ void begin_kernel(EpConfig c, EpWorkspace ws) {
+    PhaseScope ps_(ws.debug_time, kPhaseBegin);
     if (threadIdx.x == 0 && blockIdx.x == 0) {
         *ws.epoch += 1;
         if (*reinterpret_cast<volatile uint32_t*>(ws.error) != 0) {
@@ -119,7 +124,8 @@ __global__ void begin_kernel(EpConfig c, EpWorkspace ws) {
 
 template <int MAXV>
 __global__ void __launch_bounds__(kThreads) route_kernel(const float* logits, int tokens, int experts, int topk,
-                                                         int32_t* idx, float* w) {
+                                                         int32_t* idx, float* w, uint64_t* dbg) {
+    PhaseScope ps_(dbg, kPhaseRoute);
     const int lane = threadIdx.x & 31;
     const int t = (blockIdx.x * blockDim.x + threadIdx.x) / 32;
     if (t >= tokens) return;
@@ -193,6 +199,7 @@ template <int QUANT>
 __global__ void __launch_bounds__(kThreads) dispatch_kernel(EpConfig c, p2p::HeapView h, const __nv_bfloat16* x,
                                                             const int32_t* idx, const float* w, int tokens,
                                                             EpWorkspace ws) {
+    PhaseScope ps_(ws.debug_time, kPhaseDispatch);
     extern __shared__ __align__(16) uint8_t dyn_smem[];
     const int lane = threadIdx.x & 31;
     const int warp_in_block = threadIdx.x / 32;
@@ -286,10 +293,11 @@ __global__ void __launch_bounds__(kThreads) dispatch_kernel(EpConfig c, p2p::Hea
 
 __global__ void __launch_bounds__(kThreads) recv_count_kernel(EpConfig c, p2p::HeapView h, EpWorkspace ws,
                                                               uint64_t timeout_ns) {
+    PhaseScope ps_(ws.debug_time, kPhaseRecvCount);
     __shared__ uint32_t s_tokens[kMaxRanks];
     const uint32_t epoch = *reinterpret_cast<volatile uint32_t*>(ws.epoch);
     if (!wait_all_flags(c, h, ws, epoch, [&](int src) { return c.dispatch_flag(src); }, kSiteDispatchWait,
-                        timeout_ns, s_tokens)) {
+                        timeout_ns, s_tokens, ps_)) {
         return;
     }
     if (blockIdx.x == 0 && threadIdx.x < static_cast<unsigned>(c.world)) ws.slot_tokens[threadIdx.x] = s_tokens[threadIdx.x];
@@ -314,6 +322,7 @@ __global__ void __launch_bounds__(kThreads) recv_count_kernel(EpConfig c, p2p::H
 /// expert-major row per local expert with an atomic per expert, and records
 /// pair_slot / pair_w and the slot's row list (slot_pos, -1 padded).
 __global__ void __launch_bounds__(kThreads) recv_assign_kernel(EpConfig c, p2p::HeapView h, EpWorkspace ws) {
+    PhaseScope ps_(ws.debug_time, kPhaseRecvAssign);
     const int lane = threadIdx.x & 31;
     const int warps = gridDim.x * (blockDim.x / 32);
     const uint32_t epoch = *reinterpret_cast<volatile uint32_t*>(ws.epoch);
@@ -406,6 +415,7 @@ KIWI_DEV void recv_convert(int col, int lane, const RecvRaw& r, uint4 (&out)[2])
 /// bound: ncu showed long-scoreboard stalls dominating at 79 % warp occupancy).
 template <int QUANT>
 __global__ void __launch_bounds__(kThreads) recv_copy_kernel(EpConfig c, p2p::HeapView h, EpWorkspace ws) {
+    PhaseScope ps_(ws.debug_time, kPhaseRecvCopy);
     const int lane = threadIdx.x & 31;
     const uint64_t warps = gridDim.x * (blockDim.x / 32);
     const int lpt = c.local_per_token();
@@ -473,6 +483,7 @@ KIWI_DEV void sum_rows(int n, Loader load, float (&acc)[8]) {
 template <int MAXP>
 __global__ void __launch_bounds__(kThreads) combine_send_kernel(EpConfig c, p2p::HeapView h,
                                                                 const __nv_bfloat16* y, EpWorkspace ws) {
+    PhaseScope ps_(ws.debug_time, kPhaseCombineSend);
     const int lane = threadIdx.x & 31;
     const int warps = gridDim.x * (blockDim.x / 32);
     const uint32_t epoch = *reinterpret_cast<volatile uint32_t*>(ws.epoch);
@@ -504,11 +515,12 @@ template <int MAXR>
 __global__ void __launch_bounds__(kThreads) combine_recv_kernel(EpConfig c, p2p::HeapView h, const int32_t* idx,
                                                                 int tokens, __nv_bfloat16* out, EpWorkspace ws,
                                                                 uint64_t timeout_ns) {
+    PhaseScope ps_(ws.debug_time, kPhaseCombineRecv);
     const int lane = threadIdx.x & 31;
     const int warps = gridDim.x * (blockDim.x / 32);
     const uint32_t epoch = *reinterpret_cast<volatile uint32_t*>(ws.epoch);
     if (!wait_all_flags(c, h, ws, epoch, [&](int src) { return c.combine_flag(src); }, kSiteCombineWait, timeout_ns,
-                        nullptr)) {
+                        nullptr, ps_)) {
         return;
     }
     const uint8_t* base = h.base[h.rank];
@@ -542,11 +554,12 @@ template <int MAXK>
 __global__ void __launch_bounds__(kThreads) combine_recv_fused_kernel(EpConfig c, p2p::HeapView h, const int32_t* idx,
                                                                       int tokens, __nv_bfloat16* out, EpWorkspace ws,
                                                                       uint64_t timeout_ns) {
+    PhaseScope ps_(ws.debug_time, kPhaseCombineRecv);
     const int lane = threadIdx.x & 31;
     const int warps = gridDim.x * (blockDim.x / 32);
     const uint32_t epoch = *reinterpret_cast<volatile uint32_t*>(ws.epoch);
     if (!wait_all_flags(c, h, ws, epoch, [&](int src) { return c.combine_flag(src); }, kSiteCombineWait, timeout_ns,
-                        nullptr)) {
+                        nullptr, ps_)) {
         return;
     }
     const uint8_t* base = h.base[h.rank];
@@ -580,6 +593,7 @@ __global__ void __launch_bounds__(kThreads) combine_recv_fused_kernel(EpConfig c
 
 __global__ void __launch_bounds__(1024) recv_compact_kernel(EpConfig c, p2p::HeapView h, EpWorkspace ws,
                                                             int32_t* slot_compact, int32_t* recv_count) {
+    PhaseScope ps_(ws.debug_time, kPhaseRecvCompact);
     __shared__ int32_t s_scan[1024];
     __shared__ int32_t s_base;
     const uint32_t epoch = *reinterpret_cast<volatile uint32_t*>(ws.epoch);
@@ -614,6 +628,7 @@ __global__ void __launch_bounds__(kThreads) gather_rows_kernel(EpConfig c, p2p::
                                                                const int32_t* slot_compact, uint8_t* out_rows,
                                                                uint8_t* out_scales, int32_t* out_idx, float* out_w,
                                                                int32_t* out_src_pos) {
+    PhaseScope ps_(ws.debug_time, kPhaseGatherRows);
     const int lane = threadIdx.x & 31;
     const int warps = gridDim.x * (blockDim.x / 32);
     const uint8_t* base = h.base[h.rank];
@@ -643,6 +658,7 @@ __global__ void __launch_bounds__(kThreads) gather_rows_kernel(EpConfig c, p2p::
 __global__ void __launch_bounds__(kThreads) combine_rows_kernel(EpConfig c, p2p::HeapView h,
                                                                 const __nv_bfloat16* rows, const int32_t* src_pos,
                                                                 const int32_t* recv_count, EpWorkspace ws) {
+    PhaseScope ps_(ws.debug_time, kPhaseCombineRows);
     const int lane = threadIdx.x & 31;
     const int warps = gridDim.x * (blockDim.x / 32);
     const uint32_t epoch = *reinterpret_cast<volatile uint32_t*>(ws.epoch);
@@ -675,13 +691,14 @@ void launch_begin(const EpConfig& c, const EpWorkspace& ws, cudaStream_t s) {
     KIWI_CUDA_CHECK(cudaGetLastError());
 }
 
-void launch_route(const float* logits, int tokens, int experts, int topk, int32_t* idx, float* w, cudaStream_t s) {
+void launch_route(const float* logits, int tokens, int experts, int topk, int32_t* idx, float* w, cudaStream_t s,
+                  uint64_t* debug_time) {
     if (topk < 1 || topk > kMaxTopk) throw kiwi::error("route: topk must be in [1, 16]");
     if (tokens == 0) return;
     const int blocks = (tokens * 32 + kThreads - 1) / kThreads;
-    if (experts <= 64) route_kernel<2><<<blocks, kThreads, 0, s>>>(logits, tokens, experts, topk, idx, w);
-    else if (experts <= 256) route_kernel<8><<<blocks, kThreads, 0, s>>>(logits, tokens, experts, topk, idx, w);
-    else if (experts <= 1024) route_kernel<32><<<blocks, kThreads, 0, s>>>(logits, tokens, experts, topk, idx, w);
+    if (experts <= 64) route_kernel<2><<<blocks, kThreads, 0, s>>>(logits, tokens, experts, topk, idx, w, debug_time);
+    else if (experts <= 256) route_kernel<8><<<blocks, kThreads, 0, s>>>(logits, tokens, experts, topk, idx, w, debug_time);
+    else if (experts <= 1024) route_kernel<32><<<blocks, kThreads, 0, s>>>(logits, tokens, experts, topk, idx, w, debug_time);
     else throw kiwi::error("route: at most 1024 experts");
     KIWI_CUDA_CHECK(cudaGetLastError());
 }

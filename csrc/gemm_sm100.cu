@@ -25,6 +25,7 @@
 #include <cuda_runtime.h>
 
 #include "kiwi/ep/quant.cuh"
+#include "kiwi/ep/debug_timing.hpp"
 #include "kiwi/gemm/grouped_gemm.hpp"
 #include "kiwi/p2p/driver.hpp"
 #include "kiwi/p2p/heap.hpp"
@@ -153,6 +154,7 @@ __global__ void __launch_bounds__(GQ >= 0 ? kGatherThreads : kThreads, 1)
     __syncthreads();
     sm100::tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
+    if (threadIdx.x == 0) ep::span_start(p.span);
 
     auto fail = [&](uint32_t code) {
         *reinterpret_cast<volatile int*>(&s_abort) = 1;
@@ -486,6 +488,7 @@ __global__ void __launch_bounds__(GQ >= 0 ? kGatherThreads : kThreads, 1)
             }
         }
     }
+    if (threadIdx.x == 0) ep::span_end(p.span);
 }
 
 
@@ -558,6 +561,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     sm100::cluster_sync();  // both CTAs' barriers exist before any cross-CTA arrival
     sm100::tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
+    if (threadIdx.x == 0) ep::span_start(p.span);
 
     auto abort_flag = [&]() { return *reinterpret_cast<volatile int*>(&s_abort) != 0; };
     auto fail = [&](uint32_t code) {
@@ -695,6 +699,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     sm100::cluster_sync();  // neither CTA leaves while its peer may still touch its barriers
     sm100::tc_fence_after();
     if (warp == 1) sm100::tmem_dealloc_pair(tmem_base, 2 * kPairBN);
+    if (threadIdx.x == 0) ep::span_end(p.span);
 }
 
 /// One block: exclusive scan of group row counts -> offsets, and of the tile

@@ -25,6 +25,7 @@ struct EpWorkspace {
     int64_t* pair_dst;        // [max_pairs] (src rank << 48) | combk_off(token, k) of each expert row
     __nv_bfloat16* a;         // [max_pairs, hidden] dequantised expert-major rows
     uint32_t* error;          // [4] {code, site, info, rank}
+    uint64_t* debug_time;     // [kDebugTimeWords] phase stamps (null: timing off)
 };
 
 /// Error sites recorded in EpWorkspace::error[1].
@@ -37,7 +38,8 @@ enum EpSite : uint32_t {
 void launch_begin(const EpConfig& c, const EpWorkspace& ws, cudaStream_t s);
 
 /// Top-k routing with softmax over the selected logits (logits fp32 [T, E]).
-void launch_route(const float* logits, int tokens, int experts, int topk, int32_t* idx, float* w, cudaStream_t s);
+void launch_route(const float* logits, int tokens, int experts, int topk, int32_t* idx, float* w, cudaStream_t s,
+                  uint64_t* debug_time = nullptr);
 
 /// Quantises (per cfg.quant) and stores each token's row, scales and metadata
 /// into every destination rank's receive slot; the last CTA signals all ranks.

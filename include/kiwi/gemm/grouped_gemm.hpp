@@ -29,6 +29,10 @@ struct GroupedArgs {
     // one slot per k-block in issue order; trace_capacity slots at most.
     uint64_t* trace;
     int64_t trace_capacity;
+    // Optional kernel span (null: off): span[0] = ~(first CTA start) and
+    // span[1] = last CTA end, %globaltimer ns, both updated with atomicMax
+    // (the layout of one phase of kiwi::ep's debug timing buffer).
+    uint64_t* span;
 };
 
 inline constexpr int kTraceSlots = 4;

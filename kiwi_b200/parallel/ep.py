@@ -23,10 +23,15 @@ stream and without host synchronisation:
    ``native.fused_combine = False`` selects the unfused path instead: GEMM2 to
    local memory, per-slot sums sent over NVLink, reduced per token.
 
-``stage(...)`` methods expose the phases separately for profiling, and
+``stage(...)`` methods expose the phases separately for profiling,
+``set_debug_timing_enabled`` / ``get_debug_timing_snapshot`` record every
+kernel's device span per round (:func:`debug_phases` turns a snapshot into a
+per-phase table), and
 :class:`EpDispatchCombine` gives the reference's transport-only
 dispatch/combine contract (rows in, rows out).
 """
+import os
+
 import torch
 
 from .._native import load as _load
@@ -38,6 +43,89 @@ _C = _load()
 
 QUANTS = ("fp8", "nvfp4", "none")
 
+_NVTX = os.environ.get("KIWI_NVTX", "0") not in ("", "0")
+
+
+class _nvtx_range:
+    """An NVTX range around a host call when KIWI_NVTX=1 (no-op otherwise)."""
+
+    __slots__ = ("name",)
+
+    def __init__(self, name):
+        self.name = name
+
+    def __enter__(self):
+        if _NVTX:
+            torch.cuda.nvtx.range_push(self.name)
+
+    def __exit__(self, *exc):
+        if _NVTX:
+            torch.cuda.nvtx.range_pop()
+        return False
+
+
+def debug_phases(snapshot):
+    """Per-kernel device spans of a debug-timing snapshot.
+
+    Returns ``{phase: {"start_us", "end_us", "us"[, "wait_start_us", "wait_end_us", "wait_us"]}}``
+    in microseconds relative to the round's earliest stamp, for the phases that
+    ran in the round.  ``start`` is the first block's start and ``end`` the last
+    warp's exit over the whole grid; the wait entries are block 0's flag wait
+    in the receive-side kernels (from its first poll until every source rank's
+    flag was seen).  Phase
+    words follow the native layout: four per phase, {start, end, wait start,
+    wait end}, absolute %globaltimer nanoseconds, 0 = not recorded.
+    """
+    ticks = list(snapshot["time_ticks"])
+    names = list(snapshot["phase_names"])
+    t0 = min((t for t in ticks if t), default=0)
+    out = {}
+    for p, name in enumerate(names):
+        w = ticks[4 * p:4 * p + 4]
+        if len(w) < 4 or not w[0] or not w[1]:
+            continue
+        d = {"start_us": (w[0] - t0) / 1e3, "end_us": (w[1] - t0) / 1e3, "us": (w[1] - w[0]) / 1e3}
+        if w[2] and w[3]:
+            d.update(wait_start_us=(w[2] - t0) / 1e3, wait_end_us=(w[3] - t0) / 1e3, wait_us=(w[3] - w[2]) / 1e3)
+        out[name] = d
+    return out
+
+
+def format_debug_timing(snapshot, label="ep"):
+    """Human-readable lines of :func:`debug_phases` (one per phase, in start order)."""
+    meta = dict(zip(snapshot.get("meta_names", []), snapshot.get("meta", [])))
+    head = f"# {label} debug timing rank={meta.get('rank', '?')} world={meta.get('world', '?')} " \
+           f"tokens={meta.get('tokens', '?')} recv_tokens={meta.get('recv_tokens', '?')} " \
+           f"expert_rows={meta.get('expert_rows', '?')}"
+    lines = [head]
+    phases = sorted(debug_phases(snapshot).items(), key=lambda kv: kv[1]["start_us"])
+    for name, d in phases:
+        wait = f" wait={d['wait_us']:.2f}us" if "wait_us" in d else ""
+        lines.append(f"#   {name:<13} start={d['start_us']:9.2f}us end={d['end_us']:9.2f}us dur={d['us']:8.2f}us{wait}")
+    return "\n".join(lines)
+
+
+class _DebugTimingMixin:
+    """set_debug_timing_enabled / get_debug_timing_snapshot of the reference's
+    KiwiEpOp (apps/ep/python/kiwi_ep_bindings.hip.cpp:471-506 of AMDResearch/kiwi),
+    backed by the native op's per-kernel %globaltimer spans."""
+
+    def _debug_native(self):
+        raise NotImplementedError
+
+    def set_debug_timing_enabled(self, enabled=True):
+        self._debug_native().set_debug_timing_enabled(bool(enabled))
+
+    @property
+    def debug_timing_enabled(self):
+        return self._debug_native().debug_timing_enabled
+
+    def get_debug_timing_snapshot(self):
+        """Synchronises the current stream; refused while a CUDA graph is being captured."""
+        snap = self._debug_native().get_debug_timing_snapshot()
+        snap["phases"] = debug_phases(snap)
+        return snap
+
 
 def layer_config(cfg, rank, world, max_tokens=None):
     """The native EpConfig (dict) of a MoEConfig on `world` ranks."""
@@ -46,7 +134,7 @@ def layer_config(cfg, rank, world, max_tokens=None):
     return _C.ep.finalize_config(d)
 
 
-class ExpertParallelMoE:
+class ExpertParallelMoE(_DebugTimingMixin):
     """One rank's expert-parallel MoE layer (collective constructor)."""
 
     def __init__(self, cfg, group=None, max_tokens=None, weights=None, timeout_s=5.0, heap=None):
@@ -83,9 +171,10 @@ class ExpertParallelMoE:
         """x [T, hidden] bf16, router_logits [T, num_experts] fp32 -> [T, hidden] bf16.
         The returned tensor is operator-owned unless `out` is given."""
         t = x.shape[0]
-        idx, w = self.route(router_logits)
-        out = self._out[:t] if out is None else out
-        self._layer.forward(x.contiguous(), idx, w, out)
+        with _nvtx_range("kiwi.ep.forward"):
+            idx, w = self.route(router_logits)
+            out = self._out[:t] if out is None else out
+            self._layer.forward(x.contiguous(), idx, w, out)
         return out
 
     __call__ = forward
@@ -124,8 +213,11 @@ class ExpertParallelMoE:
     def native(self):
         return self._layer
 
+    def _debug_native(self):
+        return self._layer
 
-class EpDispatchCombine:
+
+class EpDispatchCombine(_DebugTimingMixin):
     """Transport-only dispatch / combine with the reference's contract
     (apps/ep/python/kiwi_ep_bindings.hip.cpp:289-373 of AMDResearch/kiwi):
     ``dispatch(x, weights, indices)`` returns the rows received on this rank
@@ -170,8 +262,11 @@ class EpDispatchCombine:
         self.moe.stage_combine(self._idx, out)
         return out
 
+    def _debug_native(self):
+        return self.moe.native
 
-class KiwiEpOp:
+
+class KiwiEpOp(_DebugTimingMixin):
     """Expert-parallel dispatch/combine with the reference's operator contract
     (``KiwiEpOp`` of apps/ep/python/kiwi_ep_bindings.hip.cpp:123-574 of
     AMDResearch/kiwi, MORI ``EpDispatchCombineOp`` compatible):
@@ -259,10 +354,14 @@ class KiwiEpOp:
         """Encoded source position (src_rank * max_tokens + token) of each received row."""
         return self._op.src_token_pos
 
+    def _debug_native(self):
+        return self._op
+
     def check(self):
         code, site, info, rank = self._op.error()
         if code:
             raise RuntimeError(f"kiwi ep error: code={code} site={site} info={info} rank={rank}")
 
 
-__all__ = ["ExpertParallelMoE", "EpDispatchCombine", "KiwiEpOp", "layer_config"]
+__all__ = ["ExpertParallelMoE", "EpDispatchCombine", "KiwiEpOp", "layer_config", "debug_phases",
+           "format_debug_timing"]

@@ -142,3 +142,43 @@ def test_tuning_table_and_overrides():
     for bad in ("nope=1", "gather_a=maybe", "recv_blocks=0", "dispatch_blocks"):
         with pytest.raises(Exception):
             ep.tune(cfg, 148, bad)
+
+
+# ---- device phase timing: layout and decoding (the kernels' side is a GPU test) ----
+
+def test_debug_timing_layout_and_names():
+    names = list(C.ep.DEBUG_PHASES)
+    assert names[:3] == ["route", "begin", "dispatch"]
+    for n in ("recv_count", "recv_assign", "recv_copy", "gemm1", "gemm2", "combine_send", "combine_recv",
+              "recv_compact", "gather_rows", "combine_rows"):
+        assert n in names
+    assert len(set(names)) == len(names)
+    assert C.ep.DEBUG_WORDS_PER_PHASE == 4
+    assert C.ep.DEBUG_TIME_WORDS >= 4 * len(names)
+    assert list(C.ep.DEBUG_META)[:3] == ["rank", "world", "tokens"]
+
+
+def test_debug_words_decode_start_slots_from_complement():
+    mask = (1 << 64) - 1
+    raw = [~1000 & mask, 2500, ~1200 & mask, 2000, 0, 0, 0, 0, ~3000 & mask, 3400, 0, 0]
+    assert C.ep.decode_debug_words(raw) == [1000, 2500, 1200, 2000, 0, 0, 0, 0, 3000, 3400, 0, 0]
+
+
+def test_debug_phases_table_relative_to_first_stamp():
+    from kiwi_b200.parallel.ep import debug_phases, format_debug_timing
+
+    names = list(C.ep.DEBUG_PHASES)
+    ticks = [0] * C.ep.DEBUG_TIME_WORDS
+    d, rc = names.index("dispatch"), names.index("recv_count")
+    ticks[4 * d:4 * d + 2] = [10_000, 14_000]
+    ticks[4 * rc:4 * rc + 4] = [14_500, 30_000, 14_600, 29_000]
+    snap = {"time_ticks": ticks, "phase_names": names, "meta": [3, 8, 128] + [0] * 29,
+            "meta_names": list(C.ep.DEBUG_META)}
+    ph = debug_phases(snap)
+    assert set(ph) == {"dispatch", "recv_count"}
+    assert ph["dispatch"] == {"start_us": 0.0, "end_us": 4.0, "us": 4.0}
+    assert ph["recv_count"]["start_us"] == 4.5 and ph["recv_count"]["us"] == 15.5
+    assert ph["recv_count"]["wait_us"] == 14.4
+    text = format_debug_timing(snap)
+    assert "rank=3" in text and "tokens=128" in text
+    assert text.index("dispatch") < text.index("recv_count")

@@ -199,3 +199,66 @@ def test_kiwi_ep_op_contract(dtype):
     torch.cuda.synchronize()
     op.check()
     assert torch.equal(out, deq.bfloat16())
+
+
+@pytest.mark.filterwarnings("ignore:The CUDA Graph is empty")
+@pytest.mark.parametrize("fused", [True, False])
+def test_debug_timing_spans_every_kernel_of_a_round(fused):
+    """Opt-in phase timing: each kernel's span (first block start, last warp
+    end) is recorded per round, in stream order, and the receive-side flag
+    waits sit inside their kernels."""
+    cfg = small_cfg("fp8", tokens=128)
+    layer = ExpertParallelMoE(cfg)
+    layer.native.fused_combine = fused
+    x, logits = moe.synthetic_inputs(cfg, 0, "cuda")
+    layer(x, logits)
+    snap = layer.get_debug_timing_snapshot()
+    assert not snap["enabled"] and not any(snap["time_ticks"])
+    layer.set_debug_timing_enabled(True)
+    for step in range(2):  # the second round must not keep the first round's stamps
+        x, logits = moe.synthetic_inputs(cfg, 0, "cuda", step=step)
+        out = layer(x, logits).clone()
+        snap = layer.get_debug_timing_snapshot()
+    _check(layer, cfg, x, logits, out)
+    ph = snap["phases"]
+    order = ["route", "begin", "dispatch", "recv_count", "recv_assign", "recv_copy", "gemm1", "gemm2"]
+    order += ["combine_recv"] if fused else ["combine_send", "combine_recv"]
+    assert set(order) <= set(ph), sorted(ph)
+    slack = 2.0  # us: %globaltimer granularity
+    for a, b in zip(order, order[1:]):
+        assert ph[a]["end_us"] <= ph[b]["start_us"] + slack, (a, b, ph[a], ph[b])
+    for name in order:
+        assert ph[name]["us"] >= 0
+    for name in ("recv_count", "combine_recv"):
+        assert "wait_us" in ph[name]
+        assert ph[name]["start_us"] - slack <= ph[name]["wait_start_us"] <= ph[name]["wait_end_us"] + slack
+        assert ph[name]["wait_end_us"] <= ph[name]["end_us"] + slack
+    span = ph[order[-1]]["end_us"] - ph["route"]["start_us"]
+    assert 0 < span < 1e6
+    meta = dict(zip(snap["meta_names"], snap["meta"]))
+    assert meta["world"] == 1 and meta["tokens"] == 128 and meta["recv_tokens"] == 128
+    assert meta["expert_rows"] == 128 * cfg.topk and meta["fused_combine"] == int(fused)
+    # a graph capture must not read the buffer
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        with pytest.raises(RuntimeError):
+            layer.get_debug_timing_snapshot()
+    layer.set_debug_timing_enabled(False)
+    assert not layer.debug_timing_enabled
+
+
+def test_debug_timing_of_the_transport_op():
+    from kiwi_b200.parallel.ep import KiwiEpOp
+
+    op = KiwiEpOp(hidden_dim=512, topk=2, num_experts_per_rank=8, max_num_inp_token_per_rank=32)
+    op.set_debug_timing_enabled(True)
+    x = torch.randn(32, 512, device="cuda").bfloat16()
+    idx, w = moe.route_reference(torch.randn(32, 8, device="cuda"), 2)
+    rows, _, _, _, cnt = op.dispatch(x, w, None, idx)
+    op.combine(rows[:32].clone(), None, idx)
+    snap = op.get_debug_timing_snapshot()
+    op.check()
+    ph = snap["phases"]
+    for name in ("dispatch", "recv_count", "recv_compact", "gather_rows", "combine_rows", "combine_recv"):
+        assert name in ph, sorted(ph)
+    assert ph["dispatch"]["end_us"] <= ph["combine_recv"]["start_us"] + 2.0
