@@ -60,6 +60,7 @@ public:
     virtual void start_threads(size_t n, std::vector<int> cpus) = 0;
     virtual void stop_threads() = 0;
     virtual uint64_t callbacks_run() const = 0;
+    virtual invoke::ProgressStats stats() const = 0;
     virtual uintptr_t device_context_ptr() const = 0;
     virtual size_t num_endpoints() const = 0;
     virtual size_t num_callbacks() const = 0;
@@ -103,6 +104,7 @@ public:
         threads_.stop();
     }
     uint64_t callbacks_run() const override { return threads_.callbacks_run(); }
+    invoke::ProgressStats stats() const override { return threads_.stats(); }
     uintptr_t device_context_ptr() const override {
         return reinterpret_cast<uintptr_t>(ctx_.device_context());
     }
@@ -289,6 +291,18 @@ PYBIND11_MODULE(_C, m) {
              py::arg("cpus") = std::vector<int>{})
         .def("stop_progress_threads", &KiwiContextBase::stop_threads)
         .def_property_readonly("callbacks_run", &KiwiContextBase::callbacks_run)
+        .def_property_readonly(
+            "stats",
+            [](const KiwiContextBase& c) {
+                const auto st = c.stats();
+                py::dict d;
+                d["callbacks"] = st.callbacks;
+                d["sweeps"] = st.sweeps;
+                d["empty_polls"] = st.empty_polls;
+                d["threads"] = st.threads;
+                return d;
+            },
+            "Progress-thread totals: callbacks, sweeps, endpoint polls that found nothing, threads running.")
         .def_property_readonly("device_context_ptr", &KiwiContextBase::device_context_ptr)
         .def_property_readonly("num_endpoints", &KiwiContextBase::num_endpoints)
         .def_property_readonly("num_callbacks", &KiwiContextBase::num_callbacks)
@@ -570,6 +584,7 @@ PYBIND11_MODULE(_C, m) {
     t.def("process_cpus", &topology::process_cpus);
     t.def("poller_cpus", &topology::poller_cpus, py::arg("device"), py::arg("n"), py::arg("sysfs_root") = "/sys");
     t.def("bind_current_thread", &topology::bind_current_thread);
+    t.def("current_thread_cpus", &topology::current_thread_cpus);
     t.def("gpu_numa_node", &topology::gpu_numa_node, py::arg("device"), py::arg("sysfs_root") = "/sys");
 
     register_p2p(m);

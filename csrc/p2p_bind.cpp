@@ -92,6 +92,19 @@ void register_p2p(py::module_& m) {
         .def("spawn_proxy_threads", &Context::spawn_proxy_threads, py::arg("num_threads") = 1,
              py::arg("cpus") = std::vector<int>{})
         .def("join_proxy_threads", &Context::join_proxy_threads, py::call_guard<py::gil_scoped_release>())
+        .def_property_readonly(
+            "proxy_stats",
+            [](const Context& c) {
+                const auto st = c.proxy_stats();
+                py::dict d;
+                d["messages"] = st.callbacks;
+                d["sweeps"] = st.sweeps;
+                d["empty_polls"] = st.empty_polls;
+                d["threads"] = st.threads;
+                d["copies_issued"] = c.copies_issued();
+                return d;
+            },
+            "Proxy totals: control messages served, sweeps, empty endpoint polls, threads, copy-engine puts.")
         .def_property_readonly("copies_issued", &Context::copies_issued)
         .def("ce_pingpong",
              [](Context& c, int peer, bool initiator, uint64_t bytes, uint32_t iters, uint32_t warmup,

@@ -5,12 +5,20 @@
 // each owned endpoint with its HostPollState (one load) and only then runs
 // progress() and refreshes the state; an optional hook runs once per endpoint
 // per sweep; threads are pinned to GPU-local CPUs; stop() drains.
+// Counters (callbacks run, sweeps, polls that found nothing) are flushed from
+// thread-local tallies every 1024 sweeps and at stop(), so the polling loop
+// itself takes no shared atomics.  KIWI_PROXY_AFFINITY_DEBUG=1 logs each
+// thread's requested and actual CPUs and its endpoints to stderr (the
+// reference's variable of the same name, apps/README.md:297-300).
 #pragma once
 
 #include <atomic>
+#include <cstdio>
+#include <cstdlib>
 #include <exception>
 #include <functional>
 #include <mutex>
+#include <string>
 #include <thread>
 #include <vector>
 
@@ -18,6 +26,26 @@
 #include "kiwi/topology.hpp"
 
 namespace kiwi::invoke {
+
+/// Totals of a ProgressThreads instance since its construction.
+struct ProgressStats {
+    uint64_t callbacks = 0;    // callbacks dispatched
+    uint64_t sweeps = 0;       // passes over a thread's endpoints
+    uint64_t empty_polls = 0;  // endpoint checks that found nothing to do
+    uint64_t threads = 0;      // threads running now
+};
+
+/// True when KIWI_PROXY_AFFINITY_DEBUG is set to anything but "" or "0".
+inline bool affinity_debug_enabled() {
+    const char* v = std::getenv("KIWI_PROXY_AFFINITY_DEBUG");
+    return v && *v && std::string(v) != "0";
+}
+
+inline std::string join_ints(const std::vector<int>& v) {
+    std::string s;
+    for (size_t i = 0; i < v.size(); ++i) s += (i ? "," : "") + std::to_string(v[i]);
+    return s.empty() ? "-" : s;
+}
 
 template <typename Queue>
 class ProgressThreads {
@@ -56,6 +84,15 @@ public:
     bool running() const { return !threads_.empty(); }
     uint64_t callbacks_run() const { return callbacks_.load(std::memory_order_relaxed); }
     uint64_t sweeps() const { return sweeps_.load(std::memory_order_relaxed); }
+    uint64_t empty_polls() const { return empty_.load(std::memory_order_relaxed); }
+    ProgressStats stats() const {
+        ProgressStats st;
+        st.callbacks = callbacks_run();
+        st.sweeps = sweeps();
+        st.empty_polls = empty_polls();
+        st.threads = threads_.size();
+        return st;
+    }
 
     /// Rethrows the first exception a callback raised on a progress thread.
     void rethrow_if_failed() {
@@ -69,25 +106,41 @@ public:
 
 private:
     void run(size_t tid, size_t nthreads, std::vector<int> cpus) {
-        if (!cpus.empty()) topology::bind_current_thread(cpus);
+        const bool pinned = !cpus.empty() && topology::bind_current_thread(cpus);
         std::vector<size_t> mine;
         for (size_t e = tid; e < ctx_.num_endpoints(); e += nthreads) mine.push_back(e);
+        if (affinity_debug_enabled()) {
+            std::vector<int> eps(mine.begin(), mine.end());
+            std::fprintf(stderr, "[kiwi] progress thread %zu/%zu: requested cpus %s, pinned %d, running on %s, "
+                                 "endpoints %s\n",
+                         tid, nthreads, join_ints(cpus).c_str(), pinned ? 1 : 0,
+                         join_ints(topology::current_thread_cpus()).c_str(), join_ints(eps).c_str());
+        }
         std::vector<queue::HostPollState> polls;
         for (size_t e : mine) polls.push_back(ctx_.poll_state(e));
-        uint64_t local_sweeps = 0;
+        uint64_t local_sweeps = 0, local_empty = 0;
+        auto flush = [&] {
+            sweeps_.fetch_add(local_sweeps, std::memory_order_relaxed);
+            empty_.fetch_add(local_empty, std::memory_order_relaxed);
+            local_sweeps = local_empty = 0;
+        };
         try {
             while (!stop_.load(std::memory_order_relaxed)) {
                 for (size_t i = 0; i < mine.size(); ++i) {
                     if (polls[i].ready()) {
                         callbacks_.fetch_add(ctx_.progress(mine[i]), std::memory_order_relaxed);
                         polls[i].refresh();
+                    } else {
+                        ++local_empty;
                     }
                     if (hook_) hook_(mine[i]);
                 }
-                if ((++local_sweeps & 1023u) == 0) sweeps_.fetch_add(1024, std::memory_order_relaxed);
+                if (++local_sweeps == 1024) flush();
             }
+            flush();
             for (size_t e : mine) callbacks_.fetch_add(ctx_.progress(e), std::memory_order_relaxed);
         } catch (...) {
+            flush();
             std::lock_guard<std::mutex> g(mu_);
             if (!error_) error_ = std::current_exception();
         }
@@ -99,6 +152,7 @@ private:
     std::atomic<bool> stop_{false};
     std::atomic<uint64_t> callbacks_{0};
     std::atomic<uint64_t> sweeps_{0};
+    std::atomic<uint64_t> empty_{0};
     std::mutex mu_;
     std::exception_ptr error_;
 };

@@ -86,6 +86,8 @@ public:
     invoke::Context<ControlQueue>& invoke_context() { return *ictx_; }
     SymmetricHeap& heap() { return heap_; }
     uint64_t copies_issued() const { return copies_; }
+    /// Proxy-thread totals (callbacks = control messages served).
+    invoke::ProgressStats proxy_stats() const { return threads_->stats(); }
 
 private:
     void ce_put(const CePutDesc& d);

@@ -34,6 +34,9 @@ std::vector<int> poller_cpus(int device, size_t n, const std::string& sysfs_root
 /// CPUs in this process's affinity mask.
 std::vector<int> process_cpus();
 
+/// CPUs in the calling thread's affinity mask.
+std::vector<int> current_thread_cpus();
+
 /// Pins the calling thread to `cpus`; returns false if the kernel refused.
 bool bind_current_thread(const std::vector<int>& cpus);
 

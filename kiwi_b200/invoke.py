@@ -94,6 +94,12 @@ class Context:
         return self._ctx.callbacks_run
 
     @property
+    def stats(self):
+        """Progress-thread totals: ``callbacks``, ``sweeps``, ``empty_polls``
+        (endpoint checks that found nothing) and ``threads`` running now."""
+        return self._ctx.stats
+
+    @property
     def host_only(self):
         return self._ctx.host_only
 

@@ -11,21 +11,41 @@ import torch
 import torch.distributed as dist
 
 
-def env_rank():
-    return int(os.environ.get("RANK", "0"))
+# Launcher variables, first match wins.  torchrun's come first: under torchrun
+# inside a SLURM allocation every child shares SLURM_LOCALID but has its own
+# LOCAL_RANK.  The MPI and SLURM names are the ones the reference's launch
+# discovery reads (apps/README.md:297-300 of AMDResearch/kiwi).
+RANK_VARS = ("RANK", "OMPI_COMM_WORLD_RANK", "PMI_RANK", "SLURM_PROCID")
+WORLD_VARS = ("WORLD_SIZE", "OMPI_COMM_WORLD_SIZE", "PMI_SIZE", "SLURM_NTASKS")
+LOCAL_RANK_VARS = ("LOCAL_RANK", "OMPI_COMM_WORLD_LOCAL_RANK", "MPI_LOCALRANKID", "SLURM_LOCALID")
 
 
-def env_world():
-    return int(os.environ.get("WORLD_SIZE", "1"))
+def _first_env(names, default, env=None):
+    env = os.environ if env is None else env
+    for n in names:
+        v = env.get(n)
+        if v not in (None, ""):
+            return int(v)
+    return default
 
 
-def env_local_rank():
-    return int(os.environ.get("LOCAL_RANK", "0"))
+def env_rank(env=None):
+    return _first_env(RANK_VARS, 0, env)
+
+
+def env_world(env=None):
+    return _first_env(WORLD_VARS, 1, env)
+
+
+def env_local_rank(env=None):
+    return _first_env(LOCAL_RANK_VARS, 0, env)
 
 
 def init(backend=None, timeout_s=120.0, device=True):
-    """Initialises the default process group from torchrun's environment (no-op
-    for a world of 1 unless MASTER_ADDR is set).  Returns (rank, world)."""
+    """Initialises the default process group from the launcher's environment
+    (torchrun, or mpirun / srun through RANK_VARS, WORLD_VARS and
+    LOCAL_RANK_VARS; MASTER_ADDR defaults to 127.0.0.1 and MASTER_PORT to 29500
+    when the launcher sets neither).  No-op for a world of 1.  Returns (rank, world)."""
     world = env_world()
     if device and torch.cuda.is_available():
         torch.cuda.set_device(env_local_rank() % max(torch.cuda.device_count(), 1))
@@ -33,7 +53,9 @@ def init(backend=None, timeout_s=120.0, device=True):
         if backend is None:
             backend = "nccl" if torch.cuda.is_available() else "gloo"
         os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
-        kwargs = dict(backend=backend, timeout=datetime.timedelta(seconds=timeout_s))
+        os.environ.setdefault("MASTER_PORT", "29500")
+        kwargs = dict(backend=backend, timeout=datetime.timedelta(seconds=timeout_s),
+                      rank=env_rank(), world_size=world)
         if backend == "nccl" and torch.cuda.is_available():
             kwargs["device_id"] = torch.device("cuda", torch.cuda.current_device())
         dist.init_process_group(**kwargs)

@@ -90,6 +90,17 @@ std::vector<int> poller_cpus(int device, size_t n, const std::string& sysfs_root
     return out;
 }
 
+std::vector<int> current_thread_cpus() {
+    std::vector<int> out;
+    cpu_set_t set;
+    CPU_ZERO(&set);
+    if (pthread_getaffinity_np(pthread_self(), sizeof(set), &set) != 0) return out;
+    for (int c = 0; c < CPU_SETSIZE; ++c) {
+        if (CPU_ISSET(c, &set)) out.push_back(c);
+    }
+    return out;
+}
+
 bool bind_current_thread(const std::vector<int>& cpus) {
     if (cpus.empty()) return false;
     cpu_set_t set;

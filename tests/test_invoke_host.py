@@ -7,6 +7,7 @@ import time
 
 import pytest
 
+import kiwi_b200
 from kiwi_b200 import invoke
 
 
@@ -120,3 +121,31 @@ def test_mpsc_context_host_only():
     cb = ctx.register_callback(lambda v: got.append(v), "<d")
     ctx.emulate_invoke(0, cb, struct.pack("<d", 3.25))
     assert ctx.progress(0) == 1 and got == [3.25]
+
+
+def test_progress_stats_and_affinity_log(capfd, monkeypatch):
+    """Proxy counters (callbacks, sweeps, empty polls) and the
+    KIWI_PROXY_AFFINITY_DEBUG log of each thread's CPUs and endpoints."""
+    monkeypatch.setenv("KIWI_PROXY_AFFINITY_DEBUG", "1")
+    ctx = invoke.Context(num_endpoints=3, capacity=64, host_only=True)
+    got = []
+    cb = ctx.register_callback(lambda i: got.append(i), "<I")
+    cpus = kiwi_b200.native().topology.current_thread_cpus()
+    ctx.start(num_threads=2, cpus=cpus[:1])
+    for i in range(10):
+        ctx.emulate_invoke(i % 3, cb, struct.pack("<I", i))
+    deadline = time.time() + 10
+    while len(got) < 10 and time.time() < deadline:
+        time.sleep(0.01)
+    st = ctx.stats
+    assert st["threads"] == 2
+    ctx.stop()
+    st = ctx.stats
+    assert sorted(got) == list(range(10))
+    assert st["callbacks"] == 10 and st["threads"] == 0
+    assert st["sweeps"] > 0 and st["empty_polls"] > 0
+    err = capfd.readouterr().err
+    lines = [ln for ln in err.splitlines() if ln.startswith("[kiwi] progress thread")]
+    assert len(lines) == 2, err
+    assert f"requested cpus {cpus[0]}, pinned 1, running on {cpus[0]}" in lines[0]
+    assert "endpoints 0,2" in "".join(lines) and "endpoints 1" in "".join(lines)
