@@ -53,7 +53,8 @@ public:
     }
     HostPollState host_poll_state() const { return reader_.poll_state(); }
     uint64_t capacity() const { return capacity_; }
-    uint64_t consumer_position() const { return reader_.tail(); }
+    /// The consumer's published position (safe to read from any thread).
+    uint64_t consumer_position() const { return __atomic_load_n(pos_.as<const uint64_t>(), __ATOMIC_ACQUIRE); }
     MemKind memory_kind() const { return kind_; }
 
     /// Error recorded by device code (code 0 = none).
@@ -69,8 +70,11 @@ public:
     void clear_error() { *err_.as<volatile uint32_t>() = 0; }
 
     /// CPU stand-in producer positioned at the consumer (host-only tests).
+    /// Reads the position the consumer publishes (not its private cursor), so
+    /// it may be called while progress threads pop; call it when no other
+    /// producer has messages in flight, since it starts where they would be.
     RingWriter host_writer_any() const {
-        return RingWriter(ring_.as<Chunk>(), capacity_, pos_.as<const uint64_t>(), reader_.tail());
+        return RingWriter(ring_.as<Chunk>(), capacity_, pos_.as<const uint64_t>(), consumer_position());
     }
 
     /// Host pointers, for CPU stand-in producers in tests and benchmarks.

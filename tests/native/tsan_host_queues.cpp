@@ -1,0 +1,171 @@
+// Host-side race check of kiwi::queue and kiwi::invoke, compiled with
+// -fsanitize=thread by tests/test_tsan_host.py (CPU only, no GPU).
+//
+// Each case runs real producer and consumer threads over the host-only rings
+// (plain memory instead of mapped pinned memory, same code paths):
+//   spsc_d2h  - a producer thread and the consumer over an 8-line ring, so
+//               every message wraps and the producer waits for credit;
+//   spsc_h2d  - the host producer of an H2D ring and a CPU stand-in for the
+//               device consumer that publishes its position;
+//   mpmc_push - four threads claim slots of one MPMC H2D ring concurrently;
+//   invoke    - four producer threads (one per endpoint) feed an invoke
+//               Context served by two progress threads, then stop() drains.
+// Exit status 0 and no ThreadSanitizer report mean the case passed.
+#include <atomic>
+#include <chrono>
+#include <cstdio>
+#include <cstring>
+#include <thread>
+#include <vector>
+
+#include "kiwi/invoke/invoke.hpp"
+#include "kiwi/invoke/progress.hpp"
+#include "kiwi/queue/queue.hpp"
+
+using namespace kiwi;
+using namespace kiwi::queue;
+
+namespace {
+
+int fail(const char* what, long a, long b) {
+    std::fprintf(stderr, "FAIL %s: %ld vs %ld\n", what, a, b);
+    return 1;
+}
+
+void fill(uint8_t* p, uint32_t n, uint32_t seed) {
+    for (uint32_t i = 0; i < n; ++i) p[i] = static_cast<uint8_t>(seed * 31u + i);
+}
+
+bool check(const uint8_t* p, uint32_t n, uint32_t seed) {
+    for (uint32_t i = 0; i < n; ++i) {
+        if (p[i] != static_cast<uint8_t>(seed * 31u + i)) return false;
+    }
+    return true;
+}
+
+int spsc_d2h() {
+    SPSCD2HQueue q(8, MemKind::kHost);
+    RingWriter w = q.host_writer();
+    const uint32_t n = 20000;
+    std::thread producer([&] {
+        alignas(16) uint8_t buf[kMaxMessageBytes];
+        for (uint32_t i = 0; i < n; ++i) {
+            const uint32_t bytes = (i * 7) % 121;
+            fill(buf, bytes, i);
+            while (!w.try_push(buf, bytes, i)) std::this_thread::yield();
+        }
+    });
+    alignas(16) uint8_t buf[kMaxMessageBytes];
+    for (uint32_t got = 0; got < n;) {
+        uint32_t meta = 0, bytes = 0;
+        if (!q.try_pop(buf, &meta, &bytes)) {
+            std::this_thread::yield();
+            continue;
+        }
+        if (meta != got) return fail("spsc_d2h order", meta, got);
+        if (bytes != (got * 7) % 121 || !check(buf, bytes, got)) return fail("spsc_d2h payload", got, bytes);
+        ++got;
+    }
+    producer.join();
+    return 0;
+}
+
+int spsc_h2d() {
+    SPSCH2DQueue q(16, MemKind::kHost);
+    const uint32_t n = 20000;
+    std::atomic<int> bad{0};
+    std::thread consumer([&] {
+        RingReader r(q.ring_host(), q.capacity(), q.consumer_pos_host());
+        alignas(16) uint8_t buf[kMaxMessageBytes];
+        for (uint32_t got = 0; got < n;) {
+            uint32_t meta = 0, bytes = 0;
+            if (!r.try_pop(buf, &meta, &bytes)) {
+                std::this_thread::yield();
+                continue;
+            }
+            if (meta != got || bytes != (got * 5) % 97 || !check(buf, bytes, got)) bad.store(1);
+            ++got;
+        }
+    });
+    alignas(16) uint8_t buf[kMaxMessageBytes];
+    for (uint32_t i = 0; i < n; ++i) {
+        const uint32_t bytes = (i * 5) % 97;
+        fill(buf, bytes, i);
+        while (!q.try_push(buf, bytes, i)) std::this_thread::yield();
+    }
+    consumer.join();
+    return bad.load() ? fail("spsc_h2d payload", 1, 0) : 0;
+}
+
+int mpmc_push() {
+    MPMCH2DQueue q(64, 2, MemKind::kHost);
+    std::atomic<int> pushed{0};
+    std::vector<std::thread> ts;
+    for (int t = 0; t < 4; ++t) {
+        ts.emplace_back([&, t] {
+            uint64_t v = static_cast<uint64_t>(t);
+            for (int i = 0; i < 16; ++i) {
+                if (q.try_push(&v, sizeof(v), static_cast<uint32_t>(t))) pushed.fetch_add(1);
+            }
+        });
+    }
+    for (auto& th : ts) th.join();
+    // 64 free slots, 64 attempts: every push lands in its own slot.
+    if (pushed.load() != 64) return fail("mpmc_push count", pushed.load(), 64);
+    if (q.producer_position() != 64) return fail("mpmc_push head", static_cast<long>(q.producer_position()), 64);
+    return 0;
+}
+
+int invoke_threads() {
+    invoke::Context<SPSCD2HQueue> ctx(4, 16, MemKind::kHost);
+    std::atomic<uint64_t> sum{0};
+    std::atomic<uint32_t> calls{0};
+    const uint8_t cb = ctx.register_callback(std::function<void(uint32_t, uint64_t)>([&](uint32_t ep, uint64_t v) {
+        sum.fetch_add(v + ep, std::memory_order_relaxed);
+        calls.fetch_add(1, std::memory_order_relaxed);
+    }));
+    invoke::ProgressThreads<SPSCD2HQueue> threads(ctx);
+    threads.start(2);
+    const uint32_t per = 3000;
+    std::vector<std::thread> producers;
+    for (uint32_t ep = 0; ep < 4; ++ep) {
+        producers.emplace_back([&, ep] {
+            RingWriter w = ctx.raw_queue(ep)->host_writer_any();
+            for (uint32_t i = 0; i < per; ++i) {
+                uint8_t msg[12];  // the serializer's packed image of (uint32_t, uint64_t)
+                const uint64_t v = i;
+                std::memcpy(msg, &ep, 4);
+                std::memcpy(msg + 4, &v, 8);
+                while (!w.try_push(msg, sizeof(msg), cb)) std::this_thread::yield();
+            }
+        });
+    }
+    for (auto& p : producers) p.join();
+    const auto deadline = std::chrono::steady_clock::now() + std::chrono::seconds(60);
+    while (calls.load() < 4 * per && std::chrono::steady_clock::now() < deadline) std::this_thread::yield();
+    threads.stop();
+    threads.rethrow_if_failed();
+    if (calls.load() != 4 * per) return fail("invoke calls", calls.load(), 4 * per);
+    const uint64_t want = 4ull * per * (per - 1) / 2 + per * (0 + 1 + 2 + 3);
+    if (sum.load() != want) return fail("invoke sum", static_cast<long>(sum.load()), static_cast<long>(want));
+    const auto st = threads.stats();
+    if (st.callbacks != 4ull * per) return fail("invoke stats", static_cast<long>(st.callbacks), 4 * per);
+    return 0;
+}
+
+}  // namespace
+
+int main(int argc, char** argv) {
+    struct Case {
+        const char* name;
+        int (*fn)();
+    } cases[] = {{"spsc_d2h", spsc_d2h}, {"spsc_h2d", spsc_h2d}, {"mpmc_push", mpmc_push}, {"invoke", invoke_threads}};
+    int rc = 0;
+    for (const auto& c : cases) {
+        if (argc > 1 && std::strcmp(argv[1], c.name) != 0) continue;
+        const int r = c.fn();
+        std::printf("%s %s\n", c.name, r ? "FAIL" : "ok");
+        rc |= r;
+    }
+    return rc;
+}
