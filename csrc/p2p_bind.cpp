@@ -48,6 +48,14 @@ void register_p2p(py::module_& m) {
           py::arg("fd"), py::arg("timeout_s") = 60.0, py::call_guard<py::gil_scoped_release>());
     p.def("multicast_supported", &SymmetricHeap::multicast_supported);
     p.def("coll_ingress_bytes", [](int world) { return coll_ingress_bytes(world); });
+    p.def("heap_range_ok", &heap_range_ok, py::arg("world"), py::arg("limit"), py::arg("rank"), py::arg("off"),
+          py::arg("bytes"), "The checked mode's range rule: rank in [0, world), [off, off + bytes) in [0, limit).");
+    py::enum_<CheckSite>(p, "CheckSite")
+        .value("PUT", kCheckPut)
+        .value("GET", kCheckGet)
+        .value("SIGNAL", kCheckSignal)
+        .value("LL8", kCheckLl8)
+        .value("MULTICAST", kCheckMulticast);
     p.def("grid_barrier_test",
           [](uint32_t blocks, uint32_t rounds, uint64_t timeout_ns) {
               auto opts = torch::TensorOptions().device(torch::kCUDA, c10::cuda::current_device());
@@ -143,6 +151,29 @@ void register_p2p(py::module_& m) {
         .def_property_readonly("local_ptr", [](SymmetricHeap& h) { return reinterpret_cast<uintptr_t>(h.local()); })
         .def_property_readonly("mc_ptr", [](SymmetricHeap& h) { return reinterpret_cast<uintptr_t>(h.multicast()); })
         .def("peer_ptr", [](SymmetricHeap& h, int r) { return reinterpret_cast<uintptr_t>(h.peer(r)); })
+        .def(
+            "set_checks",
+            [](SymmetricHeap& h, py::object record, uint64_t limit) {
+                if (record.is_none()) {
+                    h.set_checks(nullptr, 0);
+                    return;
+                }
+                torch::Tensor t = record.cast<torch::Tensor>();
+                TORCH_CHECK(t.is_cuda() && t.scalar_type() == torch::kInt32 && t.numel() >= 4 && t.is_contiguous(),
+                            "check record must be a contiguous int32 CUDA tensor of 4 words");
+                h.set_checks(u32_ptr(t), limit);
+            },
+            py::arg("record"), py::arg("limit") = 0,
+            "Checked mode of the device API: ranges validated against [0, limit) (0: the heap size), the first "
+            "violation recorded in `record` as {1, site, rank, offset}, bad accesses skipped.  None: off.  Applies "
+            "to views taken after the call.")
+        .def_property_readonly("check_limit", [](SymmetricHeap& h) { return h.view().check_limit; })
+        .def("checked_ops",
+             [](SymmetricHeap& h, int peer, uint64_t off, uint64_t bytes, uint64_t flag_off) {
+                 launch_checked_ops(h.view(), peer, off, bytes, flag_off, cur_stream());
+             },
+             py::arg("peer"), py::arg("off"), py::arg("bytes"), py::arg("flag_off"),
+             "One block: put_block, get_block and signal on the given ranges (checked-mode tests).")
         .def("tensor",
              [](SymmetricHeap& h, uint64_t offset, std::vector<int64_t> shape, torch::Dtype dtype) {
                  int dev = 0;

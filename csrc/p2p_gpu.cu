@@ -174,6 +174,14 @@ __global__ void __launch_bounds__(512) get_kernel(HeapView h, int peer, uint64_t
     }
 }
 
+__global__ void checked_ops_kernel(HeapView h, int peer, uint64_t off, uint64_t bytes, uint64_t flag_off) {
+    put_block(h, peer, off, h.base[h.rank], bytes);
+    __syncthreads();
+    get_block(h, peer, off, h.base[h.rank] + bytes, bytes);
+    __syncthreads();
+    if (threadIdx.x == 0) signal(h, peer, flag_off, 1, SignalOp::kAdd);
+}
+
 /// Every rank stores (rank+1) * (i+1) into its slot of every peer, signals them,
 /// then waits for all peers and checks what arrived (all-pairs put test).
 __global__ void all_pairs_kernel(HeapView h, uint64_t data_off, uint64_t flag_off, uint64_t words, uint32_t round,
@@ -288,6 +296,11 @@ void launch_get(const HeapView& h, int peer, uint64_t bytes, uint64_t reps, uint
                 uint64_t* lat_ns, uint32_t max_blocks, cudaStream_t s, uint64_t region) {
     const uint32_t nb = blocks_for(bytes, max_blocks);
     get_kernel<<<nb, bytes <= 4096 ? 128 : 512, 0, s>>>(h, peer, bytes, reps, src_off, dst_off, lat_ns, region);
+    KIWI_CUDA_CHECK(cudaGetLastError());
+}
+
+void launch_checked_ops(const HeapView& h, int peer, uint64_t off, uint64_t bytes, uint64_t flag_off, cudaStream_t s) {
+    checked_ops_kernel<<<1, 256, 0, s>>>(h, peer, off, bytes, flag_off);
     KIWI_CUDA_CHECK(cudaGetLastError());
 }
 

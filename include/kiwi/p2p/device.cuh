@@ -11,6 +11,8 @@
 //   wait     = ld.acquire.sys polling with a deadline (never unbounded)
 //   put_ll8  = small messages whose 8-byte words carry data + sequence (no fence)
 //   get      = 16-byte loads from the peer mapping
+// Checked mode (HeapView::check set by SymmetricHeap::set_checks): each call
+// validates its range first and records and skips a bad one, never traps.
 // Ordering: a signal issued after __syncwarp()/__syncthreads() releases every
 // store the warp/block made before it (PTX release is cumulative over writes
 // the releasing thread has observed through the barrier).
@@ -27,6 +29,22 @@ enum class Cmp : int { kEq = 0, kGe = 1, kNe = 2 };
 #if defined(__CUDACC__)
 
 KIWI_DEV uint8_t* remote(const HeapView& h, int rank, uint64_t off) { return h.base[rank] + off; }
+
+/// Checked mode (HeapView::check non-null): false, with the first violation
+/// recorded, when the access leaves [0, check_limit) of a valid rank's heap.
+/// Every lane of a cooperative call computes the same answer, so a rejected
+/// put or get is skipped by the whole warp or block.
+KIWI_DEV bool access_ok(const HeapView& h, int rank, uint64_t off, uint64_t bytes, CheckSite site) {
+    if (h.check == nullptr) return true;
+    if (heap_range_ok(h.world, h.check_limit, rank, off, bytes)) return true;
+    if (atomicCAS(h.check, 0u, 1u) == 0u) {
+        h.check[1] = static_cast<uint32_t>(site);
+        h.check[2] = static_cast<uint32_t>(rank);
+        h.check[3] = static_cast<uint32_t>(off);
+        __threadfence_system();
+    }
+    return false;
+}
 
 /// Copies `bytes` from src to dst with `nthreads` cooperating threads
 /// (thread index `tid`).  Both addresses 16-byte aligned for the vector part;
@@ -56,26 +74,31 @@ KIWI_DEV void coop_copy(void* dst, const void* src, uint64_t bytes, uint32_t tid
 
 /// Warp-cooperative put of `bytes` from local `src` into rank's heap at `dst_off`.
 KIWI_DEV void put_warp(const HeapView& h, int rank, uint64_t dst_off, const void* src, uint64_t bytes) {
+    if (!access_ok(h, rank, dst_off, bytes, kCheckPut)) return;
     coop_copy(remote(h, rank, dst_off), src, bytes, ptx::lane_id(), 32);
 }
 
 /// Block-cooperative put.
 KIWI_DEV void put_block(const HeapView& h, int rank, uint64_t dst_off, const void* src, uint64_t bytes) {
+    if (!access_ok(h, rank, dst_off, bytes, kCheckPut)) return;
     coop_copy(remote(h, rank, dst_off), src, bytes, threadIdx.x, blockDim.x);
 }
 
 /// Warp-cooperative get of `bytes` from rank's heap at `src_off` into local `dst`.
 KIWI_DEV void get_warp(const HeapView& h, int rank, uint64_t src_off, void* dst, uint64_t bytes) {
+    if (!access_ok(h, rank, src_off, bytes, kCheckGet)) return;
     coop_copy(dst, remote(h, rank, src_off), bytes, ptx::lane_id(), 32);
 }
 
 KIWI_DEV void get_block(const HeapView& h, int rank, uint64_t src_off, void* dst, uint64_t bytes) {
+    if (!access_ok(h, rank, src_off, bytes, kCheckGet)) return;
     coop_copy(dst, remote(h, rank, src_off), bytes, threadIdx.x, blockDim.x);
 }
 
 /// Signals a 64-bit flag in rank's heap with release semantics (system scope).
 /// Call from one thread after a warp/block barrier that follows the puts.
 KIWI_DEV void signal(const HeapView& h, int rank, uint64_t flag_off, uint64_t value, SignalOp op) {
+    if (!access_ok(h, rank, flag_off, sizeof(uint64_t), kCheckSignal)) return;
     void* f = remote(h, rank, flag_off);
     if (op == SignalOp::kSet) {
         ptx::st_release_sys_u64(f, value);
@@ -115,6 +138,7 @@ KIWI_DEV Status wait(const uint64_t* flag, Cmp c, uint64_t want, uint64_t timeou
 /// (8 bytes per word on the wire).
 KIWI_DEV void put_ll8_warp(const HeapView& h, int rank, uint64_t dst_off, const uint32_t* src, uint32_t nwords,
                            uint32_t seq) {
+    if (!access_ok(h, rank, dst_off, 8ull * nwords, kCheckLl8)) return;
     uint64_t* dst = reinterpret_cast<uint64_t*>(h.base[rank] + dst_off);
     for (uint32_t i = ptx::lane_id(); i < nwords; i += 32) {
         ptx::st_volatile_u64(dst + i, static_cast<uint64_t>(src[i]) | (static_cast<uint64_t>(seq) << 32));
@@ -179,6 +203,7 @@ KIWI_DEV void mc_red_add_u64(void* mc_addr, uint64_t v) {
 /// Block-cooperative broadcast of `bytes` (16-byte multiple) from local src to
 /// every rank's heap at mc_off.
 KIWI_DEV void mc_broadcast_block(const HeapView& h, uint64_t mc_off, const void* src, uint64_t bytes) {
+    if (!access_ok(h, h.rank, mc_off, bytes, kCheckMulticast)) return;
     const uint4* s = static_cast<const uint4*>(src);
     uint4* d = reinterpret_cast<uint4*>(h.mc + mc_off);
     for (uint64_t i = threadIdx.x; i < bytes / 16; i += blockDim.x) mc_store_v4(d + i, ptx::ld_v4(s + i));

@@ -31,7 +31,27 @@ struct HeapView {
     uint64_t size;
     int32_t rank;
     int32_t world;
+    // Checked mode (null: off).  Every put / get / signal of the device API
+    // validates (rank, offset, bytes) against [0, check_limit); the first bad
+    // access is recorded as check[0..3] = {1, site, rank, offset low 32 bits}
+    // and every bad access is skipped instead of touching memory.
+    uint32_t* check;
+    uint64_t check_limit;
 };
+
+/// Sites recorded by the checked mode (HeapView::check[1]).
+enum CheckSite : uint32_t {
+    kCheckPut = 1,
+    kCheckGet = 2,
+    kCheckSignal = 3,
+    kCheckLl8 = 4,
+    kCheckMulticast = 5,
+};
+
+/// True when [off, off + bytes) of rank's heap lies inside [0, limit).
+KIWI_HD constexpr bool heap_range_ok(int world, uint64_t limit, int rank, uint64_t off, uint64_t bytes) {
+    return rank >= 0 && rank < world && off <= limit && bytes <= limit - off;
+}
 
 /// Exchanges one file descriptor per rank through abstract Unix sockets named
 /// "kiwi.<job>.<rank>".  Returns fds[r] = a descriptor for rank r's object in
@@ -63,6 +83,12 @@ public:
     int rank() const { return view_.rank; }
     int world() const { return view_.world; }
     const HeapView& view() const { return view_; }
+    /// Checked mode: `record` = 4 device uint32 words (null: off); accesses
+    /// must stay below `limit` (0 or more than the size: the whole heap).
+    void set_checks(uint32_t* record, uint64_t limit) {
+        view_.check = record;
+        view_.check_limit = (limit == 0 || limit > view_.size) ? view_.size : limit;
+    }
 
     /// True when the device supports NVLS multicast objects.
     static bool multicast_supported(int device);

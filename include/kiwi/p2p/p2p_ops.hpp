@@ -26,6 +26,12 @@ void launch_put_bw(const HeapView& h, int peer, bool sender, uint64_t bytes, uin
 void launch_get(const HeapView& h, int peer, uint64_t bytes, uint64_t reps, uint64_t src_off, uint64_t dst_off,
                 uint64_t* lat_ns, uint32_t max_blocks, cudaStream_t s, uint64_t region = 0);
 
+/// One block exercises the device API on caller-chosen ranges: put_block of
+/// `bytes` from local offset 0 to (peer, off), get_block back from (peer, off)
+/// into local offset `bytes`, and a signal on (peer, flag_off).  Exists for the
+/// checked-mode tests; the caller keeps every range inside the mapped heap.
+void launch_checked_ops(const HeapView& h, int peer, uint64_t off, uint64_t bytes, uint64_t flag_off, cudaStream_t s);
+
 void launch_all_pairs(const HeapView& h, uint64_t data_off, uint64_t flag_off, uint64_t words, uint32_t round,
                       uint32_t* status, uint64_t timeout_ns, cudaStream_t s);
 

@@ -60,6 +60,36 @@ class SymmetricHeap:
             shape = [shape]
         return self._h.tensor(int(offset), list(shape), dtype)
 
+    # -- checked mode ------------------------------------------------------------
+    def enable_checks(self, limit=None):
+        """Validate every put / get / signal of the device API against
+        [0, limit) of a valid rank's heap (default: the whole heap).  A bad
+        access is skipped and the first one recorded (see :meth:`check_error`);
+        nothing traps.  Applies to kernels launched with views taken after the
+        call, i.e. every launch from here on."""
+        dev = torch.device("cuda", torch.cuda.current_device())
+        self._check = torch.zeros(4, dtype=torch.int32, device=dev)
+        self._h.set_checks(self._check, int(limit or 0))
+
+    def disable_checks(self):
+        self._h.set_checks(None)
+        self._check = None
+
+    def check_error(self):
+        """None, or {"site", "rank", "offset"} of the first rejected access
+        (offset: low 32 bits).  Synchronises the current stream."""
+        rec = getattr(self, "_check", None)
+        if rec is None:
+            return None
+        code, site, rank, off = (int(v) for v in rec.cpu().tolist())
+        if code == 0:
+            return None
+        return {"site": _C.p2p.CheckSite(site).name.lower(), "rank": rank, "offset": off & 0xFFFFFFFF}
+
+    def clear_check_error(self):
+        if getattr(self, "_check", None) is not None:
+            self._check.zero_()
+
     def barrier(self, flag_offset, round_, status):
         """Device-side barrier over the heap: flag words at flag_offset + 8*rank."""
         self._h.barrier(int(flag_offset), int(round_), status, 2_000_000_000)

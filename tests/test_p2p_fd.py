@@ -81,3 +81,22 @@ def test_completion_counter_host_only():
     assert c.get() == 40000
     c.set(7)
     assert c.signal(3) == 10
+
+
+def test_checked_mode_range_rule():
+    """The device API's checked mode rejects an access unless the rank exists
+    and [off, off + bytes) stays inside the checked limit (overflow included)."""
+    from kiwi_b200._native import load
+
+    ok = load().p2p.heap_range_ok
+    lim = 1 << 20
+    assert ok(2, lim, 0, 0, lim)
+    assert ok(2, lim, 1, lim - 96, 96)
+    assert ok(2, lim, 1, lim, 0)
+    assert not ok(2, lim, 1, lim - 96, 97)
+    assert not ok(2, lim, 2, 0, 8)
+    assert not ok(2, lim, -1, 0, 8)
+    assert not ok(2, lim, 0, lim + 1, 0)
+    assert not ok(2, lim, 0, 8, (1 << 64) - 4)  # off + bytes would wrap
+    sites = load().p2p.CheckSite
+    assert [sites.PUT.value, sites.GET.value, sites.SIGNAL.value] == [1, 2, 3]

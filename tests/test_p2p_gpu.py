@@ -93,3 +93,47 @@ def test_completion_counter_wait_times_out():
     torch.cuda.synchronize()
     assert int(status[0].item()) != 0
     assert torch.ones(1, device="cuda").item() == 1.0
+
+
+def test_checked_mode_records_and_skips_out_of_range_accesses():
+    """Checked mode: every rejected range lies past the checked limit but
+    inside the mapped heap, so even a broken check could not leave the
+    mapping.  Rejected puts, gets and signals leave memory untouched and the
+    first violation is reported; valid ones run unchanged."""
+    heap = SymmetricHeap(4 << 20)
+    limit = 1 << 20
+    heap.enable_checks(limit)
+    assert heap.native.check_limit == limit
+    n = 4096
+    src = heap.tensor(0, [n], torch.uint8)
+    src.copy_(torch.randint(1, 256, (n,), device="cuda", dtype=torch.uint8))
+    flag = heap.tensor(512 << 10, [1], torch.int64)
+    flag.zero_()
+    # valid: put to 64 KiB, get back to [n, 2n), signal the flag
+    heap.native.checked_ops(0, 64 << 10, n, 512 << 10)
+    torch.cuda.synchronize()
+    assert heap.check_error() is None
+    assert torch.equal(heap.tensor(64 << 10, [n], torch.uint8), src)
+    assert torch.equal(heap.tensor(n, [n], torch.uint8), src)
+    assert flag.item() == 1
+    # put / get crossing the limit: skipped, recorded as a put at that offset
+    edge = limit - 1024
+    beyond = heap.tensor(edge, [n], torch.uint8)
+    beyond.zero_()
+    heap.tensor(n, [n], torch.uint8).zero_()
+    heap.native.checked_ops(0, edge, n, 512 << 10)
+    torch.cuda.synchronize()
+    assert heap.check_error() == {"site": "put", "rank": 0, "offset": edge}
+    assert int(beyond.count_nonzero()) == 0
+    assert int(heap.tensor(n, [n], torch.uint8).count_nonzero()) == 0  # the get was skipped too
+    assert flag.item() == 2  # the valid signal still ran
+    # signal past the limit: skipped and recorded
+    heap.clear_check_error()
+    far = heap.tensor(2 << 20, [1], torch.int64)
+    far.zero_()
+    heap.native.checked_ops(0, 64 << 10, 0, 2 << 20)
+    torch.cuda.synchronize()
+    assert heap.check_error() == {"site": "signal", "rank": 0, "offset": 2 << 20}
+    assert far.item() == 0
+    heap.disable_checks()
+    assert heap.check_error() is None
