@@ -17,6 +17,7 @@
 #include "kiwi/bench/gpu_bench.hpp"
 #include "kiwi/bench/host_bench.hpp"
 #include "kiwi/invoke/invoke.hpp"
+#include "kiwi/invoke/printer.hpp"
 #include "kiwi/invoke/progress.hpp"
 #include "kiwi/topology.hpp"
 
@@ -74,6 +75,8 @@ public:
     /// benchmark measure the queue / frontend without Python in the loop.
     virtual uint8_t register_native_counter() = 0;
     virtual uint64_t native_count() const = 0;
+    /// A native callback that prints its arguments with a printf-style format.
+    virtual uint8_t register_native_print(const std::string& fmt, const std::string& codes, bool to_stderr) = 0;
 };
 
 template <typename Q>
@@ -96,6 +99,12 @@ public:
             invoke::CallbackBase::kAnySize);
     }
     uint64_t native_count() const override { return count_.load(std::memory_order_relaxed); }
+    uint8_t register_native_print(const std::string& fmt, const std::string& codes, bool to_stderr) override {
+        invoke::PrintFormat pf(fmt, codes);  // throws on a bad format, at registration
+        const uint32_t bytes = pf.payload_bytes();
+        return ctx_.register_raw_callback(
+            [pf, to_stderr](const uint8_t* p, uint32_t n) { pf.print(p, n, to_stderr ? stderr : stdout); }, bytes);
+    }
     size_t progress(size_t ep, int max) override { return ctx_.progress(ep, max); }
     size_t progress_all(int max) override { return ctx_.progress_all(max); }
     void start_threads(size_t n, std::vector<int> cpus) override { threads_.start(n, std::move(cpus)); }
@@ -314,7 +323,21 @@ PYBIND11_MODULE(_C, m) {
         .def("check_device_errors", &KiwiContextBase::check_device_errors)
         .def("rethrow_progress_errors", &KiwiContextBase::rethrow)
         .def("register_native_counter", &KiwiContextBase::register_native_counter)
+        .def("register_native_print", &KiwiContextBase::register_native_print, py::arg("fmt"), py::arg("codes"),
+             py::arg("to_stderr") = false,
+             "Native callback printing its packed arguments (struct codes b B h H i I l L q Q f d) with a "
+             "printf-style format; the format is checked against the codes here.")
         .def_property_readonly("native_count", &KiwiContextBase::native_count);
+
+    m.def_submodule("print_format").def(
+        "format",
+        [](const std::string& fmt, const std::string& codes, py::bytes payload) {
+            invoke::PrintFormat pf(fmt, codes);
+            const std::string b = payload;
+            return pf.format(reinterpret_cast<const uint8_t*>(b.data()), static_cast<uint32_t>(b.size()));
+        },
+        py::arg("fmt"), py::arg("codes"), py::arg("payload"),
+        "What register_native_print would print for one payload (no newline).");
 
     // ---------------- bench ----------------
     auto b = m.def_submodule("bench", "native benchmark loops");

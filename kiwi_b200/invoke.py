@@ -46,6 +46,17 @@ class Context:
 
         return self._ctx.register_callback(thunk, st.size)
 
+    def register_native_print(self, fmt, struct_format, stream="stdout"):
+        """Register a native (C++, no GIL) callback that prints each invoke's
+        arguments: ``struct_format`` gives their packed layout (codes
+        b B h H i I l L q Q f d, little-endian) and ``fmt`` a printf-style line
+        with one conversion per argument, e.g.
+        ``register_native_print("step=%d value=%.2f tag=0x%llx", "<ifQ")``.
+        The format is checked against the codes now; returns the callback id."""
+        if stream not in ("stdout", "stderr"):
+            raise ValueError("stream must be 'stdout' or 'stderr'")
+        return self._ctx.register_native_print(fmt, struct_format, stream == "stderr")
+
     # -- progress ------------------------------------------------------------
     def progress(self, endpoint=0, max_callbacks=-1):
         return self._ctx.progress(endpoint, max_callbacks)

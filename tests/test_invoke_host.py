@@ -149,3 +149,34 @@ def test_progress_stats_and_affinity_log(capfd, monkeypatch):
     assert len(lines) == 2, err
     assert f"requested cpus {cpus[0]}, pinned 1, running on {cpus[0]}" in lines[0]
     assert "endpoints 0,2" in "".join(lines) and "endpoints 1" in "".join(lines)
+
+
+def test_native_print_formats_packed_arguments():
+    """Native print callback (reference: examples/common/kiwi_print_ext.hip.cpp):
+    printf-style conversions over the packed argument image."""
+    fmt = kiwi_b200.native().print_format.format
+    pay = struct.pack("<ifQ", -3, 1.5, 0xC0FFEE03)
+    assert fmt("step=%d value=%.2f tag=0x%llx", "<ifQ", pay) == "step=-3 value=1.50 tag=0xc0ffee03"
+    assert fmt("%5u|%-4x|%c|%e", "IBbd", struct.pack("<IBbd", 7, 255, 65, 0.25)) == "    7|ff  |A|2.500000e-01"
+    assert fmt("100%% of %hd and %lld", "hq", struct.pack("<hq", -2, 1 << 40)) == "100% of -2 and 1099511627776"
+    assert fmt("unsigned %u", "Q", struct.pack("<Q", (1 << 64) - 1)) == "unsigned 18446744073709551615"
+    assert fmt("no args %%", "", b"") == "no args %"
+    for bad_fmt, codes in [("%s", "i"), ("%d", "f"), ("%f", "i"), ("%d %d", "i"), ("%d", "ii"), ("%*d", "i"),
+                           ("%n", "i"), ("%d", "z"), ("tail %", "")]:
+        with pytest.raises(Exception):
+            fmt(bad_fmt, codes, b"\0" * 8)
+    with pytest.raises(Exception):
+        fmt("%d", "i", b"\0" * 3)  # wrong payload size
+
+
+def test_native_print_callback_prints_each_invoke(capfd):
+    ctx = invoke.Context(num_endpoints=1, capacity=64, host_only=True)
+    cb = ctx.register_native_print("[kernel] step=%d value=%.2f tag=0x%llx", "<ifQ")
+    for i in range(3):
+        ctx.emulate_invoke(0, cb, struct.pack("<ifQ", i, i * 0.5, 0xC0FFEE00 + i))
+    assert ctx.progress(0) == 3
+    out = capfd.readouterr().out.splitlines()
+    assert out[-3:] == ["[kernel] step=0 value=0.00 tag=0xc0ffee00", "[kernel] step=1 value=0.50 tag=0xc0ffee01",
+                        "[kernel] step=2 value=1.00 tag=0xc0ffee02"]
+    with pytest.raises(Exception):
+        ctx.register_native_print("%s", "<i")
