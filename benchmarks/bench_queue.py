@@ -8,7 +8,8 @@ benchmarks/invoke/bench_{throughput,overhead}.hip.cpp of AMDResearch/kiwi).
   checksum verified; plus a one-way streaming rate.
 * queue_baselines: the same two-thread ping-pong and stream through four queue
   designs behind one adapter contract (kiwi ring, head/tail-counter ring,
-  per-slot sequence ring, single-word floor); reference:
+  per-slot sequence ring, single-word floor), plus the cost of one poll of an
+  empty queue and the ping-pong under a concurrent stream; reference:
   benchmarks/queue_baselines.
 * invoke_throughput: E producer warps x T progress threads, messages/s.
 * push_cost: SM cycles one warp spends per push (payload 8 .. 256 B).
@@ -37,10 +38,15 @@ def main():
           "p50_ns": float(np.percentile(lat, 50)), "p99_ns": float(np.percentile(lat, 99)), "cpus": [a, b]})
     s = C.bench.host_ring_stream(1_000_000, 4096, 8, 0, a, b)
     emit({"bench": "host_ring_stream", "ok": s["ok"], "Mmsg_per_s": 1e3 / s["total_ns"] * 1e6})
+    # The loaded mode's background pair takes the two cores after the ping-pong's, when there are any.
+    c_bg, d_bg = (cpus[3], cpus[4]) if len(cpus) > 4 else (-1, -1)
     for q in C.bench.queue_baselines(iters=200_000, warmup=20_000, messages=1_000_000, payload_bytes=8,
-                                     capacity=4096, cpu_a=a, cpu_b=b):
+                                     capacity=4096, cpu_a=a, cpu_b=b, idle_polls=10_000_000, loaded=True,
+                                     cpu_c=c_bg, cpu_d=d_bg):
         emit({"bench": "queue_baseline", "design": q["name"], "ok": q["ok"], "p50_ns": q["p50_ns"],
-              "p99_ns": q["p99_ns"], "Mmsg_per_s": q["msgs_per_s"] / 1e6})
+              "p99_ns": q["p99_ns"], "Mmsg_per_s": q["msgs_per_s"] / 1e6, "idle_poll_ns": q["idle_poll_ns"],
+              "loaded_p50_ns": q["loaded_p50_ns"], "loaded_p99_ns": q["loaded_p99_ns"],
+              "loaded_bg_Mmsg_per_s": q["loaded_bg_msgs_per_s"] / 1e6})
     if not C.cuda_device_available():
         return
     for e, t in [(1, 1), (4, 1), (8, 2), (16, 4), (64, 4)]:

@@ -358,11 +358,24 @@ PYBIND11_MODULE(_C, m) {
           py::arg("iters"), py::arg("warmup"), py::arg("capacity") = 4096, py::arg("payload_bytes") = 8,
           py::arg("seed") = 0, py::arg("cpu_a") = -1, py::arg("cpu_b") = -1);
     b.def("queue_baselines",
-          [](uint64_t iters, uint64_t warmup, uint64_t messages, uint32_t bytes, uint64_t cap, int a, int c) {
+          [](uint64_t iters, uint64_t warmup, uint64_t messages, uint32_t bytes, uint64_t cap, int a, int c,
+             uint64_t idle_polls, bool loaded, int cpu_c, int cpu_d) {
+              bench::BaselineOptions o;
+              o.iters = iters;
+              o.warmup = warmup;
+              o.messages = messages;
+              o.payload_bytes = bytes;
+              o.capacity = cap;
+              o.cpu_a = a;
+              o.cpu_b = c;
+              o.idle_polls = idle_polls;
+              o.loaded = loaded;
+              o.cpu_c = cpu_c;
+              o.cpu_d = cpu_d;
               std::vector<bench::BaselineResult> rs;
               {
                   py::gil_scoped_release nogil;
-                  rs = bench::queue_baselines(iters, warmup, messages, bytes, cap, a, c);
+                  rs = bench::queue_baselines(o);
               }
               py::list out;
               for (const auto& r : rs) {
@@ -371,6 +384,12 @@ PYBIND11_MODULE(_C, m) {
                   d["p50_ns"] = r.p50_ns;
                   d["p99_ns"] = r.p99_ns;
                   d["msgs_per_s"] = r.msgs_per_s;
+                  if (idle_polls) d["idle_poll_ns"] = r.idle_poll_ns;
+                  if (loaded) {
+                      d["loaded_p50_ns"] = r.loaded_p50_ns;
+                      d["loaded_p99_ns"] = r.loaded_p99_ns;
+                      d["loaded_bg_msgs_per_s"] = r.loaded_bg_msgs_per_s;
+                  }
                   d["ok"] = r.ok;
                   out.append(d);
               }
@@ -378,7 +397,9 @@ PYBIND11_MODULE(_C, m) {
           },
           py::arg("iters") = 100000, py::arg("warmup") = 10000, py::arg("messages") = 1000000,
           py::arg("payload_bytes") = 8, py::arg("capacity") = 4096, py::arg("cpu_a") = -1, py::arg("cpu_b") = -1,
-          "Host-only queue baselines (kiwi ring, head/tail ring, per-slot sequence ring, raw word).");
+          py::arg("idle_polls") = 0, py::arg("loaded") = false, py::arg("cpu_c") = -1, py::arg("cpu_d") = -1,
+          "Host-only queue baselines (kiwi ring, head/tail ring, per-slot sequence ring, raw word): ping-pong, "
+          "stream, and optionally the idle-poll cost and the loaded ping-pong.");
     b.def("host_ring_stream",
           [](uint64_t n, uint64_t cap, uint32_t bytes, uint64_t seed, int a, int c) {
               bench::HostRingResult r;

@@ -32,7 +32,21 @@ struct BaselineResult {
     double p50_ns = 0;           // ping-pong round trip
     double p99_ns = 0;
     double msgs_per_s = 0;       // one-way streaming
-    bool ok = false;             // order and checksum verified in both runs
+    double idle_poll_ns = 0;     // one poll of an empty queue (0: not run)
+    double loaded_p50_ns = 0;    // ping-pong while another pair streams (0: not run)
+    double loaded_p99_ns = 0;
+    double loaded_bg_msgs_per_s = 0;  // the background stream's rate meanwhile
+    bool ok = false;             // order and checksums verified in every run
+};
+
+struct BaselineOptions {
+    uint64_t iters = 10000, warmup = 1000, messages = 200000;
+    uint32_t payload_bytes = 8;
+    uint64_t capacity = 1024;
+    int cpu_a = -1, cpu_b = -1;  // ping-pong / stream threads (-1: unpinned)
+    uint64_t idle_polls = 0;     // 0: skip the idle-poll mode
+    bool loaded = false;         // run the loaded-latency mode
+    int cpu_c = -1, cpu_d = -1;  // background producer / consumer of the loaded mode
 };
 
 /// Host-only queue baselines through one adapter contract (the reference's
@@ -42,5 +56,7 @@ struct BaselineResult {
 /// of `iters` round trips (after `warmup`) and a stream of `messages`.
 std::vector<BaselineResult> queue_baselines(uint64_t iters, uint64_t warmup, uint64_t messages, uint32_t payload_bytes,
                                             uint64_t capacity, int cpu_a, int cpu_b);
+/// The same with every mode's options (idle-poll and loaded-latency included).
+std::vector<BaselineResult> queue_baselines(const BaselineOptions& options);
 
 }  // namespace kiwi::bench

@@ -14,12 +14,18 @@
 //               producer release-stores after the payload (Vyukov SPSC)
 //   raw_word    one 8-byte word per direction holding a counter: the floor
 //               of any queue (payload limited to the counter itself)
+//
+// Modes (the reference's latency, throughput, idle-poll and loaded-latency,
+// benchmarks/queue_baselines/README.md:96-104): ping-pong round trip, one-way
+// stream, the cost of polling an empty queue, and the ping-pong again while a
+// second pair of threads streams through another instance of the same queue.
 #include <algorithm>
 #include <atomic>
 #include <chrono>
 #include <cstring>
 #include <memory>
 #include <thread>
+#include <vector>
 
 #include "kiwi/bench/host_bench.hpp"
 #include "kiwi/queue/host_ring.hpp"
@@ -170,64 +176,70 @@ private:
     alignas(64) uint64_t seen_ = 0;
 };
 
+/// Ping-pong of `iters` round trips (after `warmup`) over two A queues between
+/// the calling thread (cpu_a) and a second thread (cpu_b).  Returns whether
+/// order and payloads checked out; fills p50 / p99 in ns.
 template <typename A>
-BaselineResult run_one(uint64_t iters, uint64_t warmup, uint64_t messages, uint32_t payload, uint64_t cap, int cpu_a,
-                       int cpu_b) {
+bool pingpong(uint64_t iters, uint64_t warmup, uint32_t n, uint64_t cap, int cpu_a, int cpu_b, double* p50,
+              double* p99) {
+    const bool raw = std::strcmp(A::name(), "raw_word") == 0;
+    A a2b(cap), b2a(cap);
+    const uint64_t total = iters + warmup;
+    std::vector<uint64_t> lat(iters);
+    std::atomic<bool> b_ok{true};
+    std::thread tb([&] {
+        if (cpu_b >= 0) topology::bind_current_thread({cpu_b});
+        alignas(64) uint8_t buf[queue::kMaxMessageBytes];
+        for (uint64_t i = 0; i < total; ++i) {
+            uint32_t meta = 0, bytes = 0;
+            while (!a2b.try_pop(buf, &meta, &bytes)) queue::host::cpu_relax();
+            if (meta != static_cast<uint32_t>(i)) b_ok = false;
+            while (!b2a.try_push(buf, bytes, meta)) queue::host::cpu_relax();
+        }
+    });
+    if (cpu_a >= 0) topology::bind_current_thread({cpu_a});
+    alignas(64) uint8_t msg[queue::kMaxMessageBytes] = {0};
+    alignas(64) uint8_t buf[queue::kMaxMessageBytes];
+    uint64_t state = 0x9E3779B97F4A7C15ull;
+    bool ok = true;
+    for (uint64_t i = 0; i < total; ++i) {
+        const uint64_t v = xorshift64(state);
+        std::memcpy(msg, &v, 8);
+        const uint64_t t0 = now_ns();
+        while (!a2b.try_push(msg, n, static_cast<uint32_t>(i))) queue::host::cpu_relax();
+        uint32_t meta = 0, bytes = 0;
+        while (!b2a.try_pop(buf, &meta, &bytes)) queue::host::cpu_relax();
+        const uint64_t t1 = now_ns();
+        uint64_t back;
+        std::memcpy(&back, buf, 8);
+        if (meta != static_cast<uint32_t>(i) || (!raw && back != v)) ok = false;
+        if (i >= warmup) lat[i - warmup] = t1 - t0;
+    }
+    tb.join();
+    std::sort(lat.begin(), lat.end());
+    if (!lat.empty()) {
+        *p50 = static_cast<double>(lat[lat.size() / 2]);
+        *p99 = static_cast<double>(lat[std::min(lat.size() - 1, lat.size() * 99 / 100)]);
+    }
+    return ok && b_ok;
+}
+
+template <typename A>
+BaselineResult run_one(const BaselineOptions& o) {
     BaselineResult r;
     r.name = A::name();
-    const uint32_t n = std::min<uint32_t>(std::max<uint32_t>(payload, 8), A::max_payload());
+    const uint32_t n = std::min<uint32_t>(std::max<uint32_t>(o.payload_bytes, 8), A::max_payload());
     const bool raw = std::strcmp(A::name(), "raw_word") == 0;
-    // Ping-pong over two queues.
-    {
-        A a2b(cap), b2a(cap);
-        const uint64_t total = iters + warmup;
-        std::vector<uint64_t> lat(iters);
-        std::atomic<bool> b_ok{true};
-        std::thread tb([&] {
-            if (cpu_b >= 0) topology::bind_current_thread({cpu_b});
-            alignas(64) uint8_t buf[queue::kMaxMessageBytes];
-            for (uint64_t i = 0; i < total; ++i) {
-                uint32_t meta = 0, bytes = 0;
-                while (!a2b.try_pop(buf, &meta, &bytes)) queue::host::cpu_relax();
-                if (meta != static_cast<uint32_t>(i)) b_ok = false;
-                while (!b2a.try_push(buf, bytes, meta)) queue::host::cpu_relax();
-            }
-        });
-        if (cpu_a >= 0) topology::bind_current_thread({cpu_a});
-        alignas(64) uint8_t msg[queue::kMaxMessageBytes] = {0};
-        alignas(64) uint8_t buf[queue::kMaxMessageBytes];
-        uint64_t state = 0x9E3779B97F4A7C15ull;
-        bool ok = true;
-        for (uint64_t i = 0; i < total; ++i) {
-            const uint64_t v = xorshift64(state);
-            std::memcpy(msg, &v, 8);
-            const uint64_t t0 = now_ns();
-            while (!a2b.try_push(msg, n, static_cast<uint32_t>(i))) queue::host::cpu_relax();
-            uint32_t meta = 0, bytes = 0;
-            while (!b2a.try_pop(buf, &meta, &bytes)) queue::host::cpu_relax();
-            const uint64_t t1 = now_ns();
-            uint64_t back;
-            std::memcpy(&back, buf, 8);
-            if (meta != static_cast<uint32_t>(i) || (!raw && back != v)) ok = false;
-            if (i >= warmup) lat[i - warmup] = t1 - t0;
-        }
-        tb.join();
-        std::sort(lat.begin(), lat.end());
-        if (!lat.empty()) {
-            r.p50_ns = static_cast<double>(lat[lat.size() / 2]);
-            r.p99_ns = static_cast<double>(lat[std::min(lat.size() - 1, lat.size() * 99 / 100)]);
-        }
-        r.ok = ok && b_ok;
-    }
+    r.ok = pingpong<A>(o.iters, o.warmup, n, o.capacity, o.cpu_a, o.cpu_b, &r.p50_ns, &r.p99_ns);
     // One-way stream.
     {
-        A q(cap);
+        A q(o.capacity);
         uint64_t got_sum = 0;
         bool order = true;
         std::thread tb([&] {
-            if (cpu_b >= 0) topology::bind_current_thread({cpu_b});
+            if (o.cpu_b >= 0) topology::bind_current_thread({o.cpu_b});
             alignas(64) uint8_t buf[queue::kMaxMessageBytes];
-            for (uint64_t i = 0; i < messages; ++i) {
+            for (uint64_t i = 0; i < o.messages; ++i) {
                 uint32_t meta = 0, bytes = 0;
                 while (!q.try_pop(buf, &meta, &bytes)) queue::host::cpu_relax();
                 uint64_t v;
@@ -236,11 +248,11 @@ BaselineResult run_one(uint64_t iters, uint64_t warmup, uint64_t messages, uint3
                 if (meta != static_cast<uint32_t>(i)) order = false;
             }
         });
-        if (cpu_a >= 0) topology::bind_current_thread({cpu_a});
+        if (o.cpu_a >= 0) topology::bind_current_thread({o.cpu_a});
         alignas(64) uint8_t msg[queue::kMaxMessageBytes] = {0};
         uint64_t state = 0x243F6A8885A308D3ull, sum = 0;
         const uint64_t t0 = now_ns();
-        for (uint64_t i = 0; i < messages; ++i) {
+        for (uint64_t i = 0; i < o.messages; ++i) {
             const uint64_t v = raw ? i + 1 : xorshift64(state);
             std::memcpy(msg, &v, 8);
             sum += v;
@@ -248,23 +260,83 @@ BaselineResult run_one(uint64_t iters, uint64_t warmup, uint64_t messages, uint3
         }
         tb.join();
         const uint64_t dt = now_ns() - t0;
-        r.msgs_per_s = dt ? static_cast<double>(messages) / (static_cast<double>(dt) / 1e9) : 0.0;
+        r.msgs_per_s = dt ? static_cast<double>(o.messages) / (static_cast<double>(dt) / 1e9) : 0.0;
         r.ok = r.ok && order && got_sum == sum;
+    }
+    // Idle poll: what one check of an empty queue costs the consumer.
+    if (o.idle_polls) {
+        A q(o.capacity);
+        alignas(64) uint8_t buf[queue::kMaxMessageBytes];
+        uint32_t meta = 0, bytes = 0;
+        uint64_t hits = 0;
+        const uint64_t t0 = now_ns();
+        for (uint64_t i = 0; i < o.idle_polls; ++i) hits += q.try_pop(buf, &meta, &bytes) ? 1 : 0;
+        r.idle_poll_ns = static_cast<double>(now_ns() - t0) / static_cast<double>(o.idle_polls);
+        r.ok = r.ok && hits == 0;
+    }
+    // Loaded latency: the ping-pong again while two more threads stream
+    // through another instance of the same queue (cpu_c produces, cpu_d
+    // consumes), sharing caches, memory bandwidth and the scheduler with it.
+    if (o.loaded) {
+        A bg(o.capacity);
+        std::atomic<bool> stop{false};
+        std::atomic<uint64_t> streamed{0};
+        std::thread prod([&] {
+            if (o.cpu_c >= 0) topology::bind_current_thread({o.cpu_c});
+            alignas(64) uint8_t msg[queue::kMaxMessageBytes] = {0};
+            uint32_t i = 0;
+            while (!stop.load(std::memory_order_relaxed)) {
+                if (bg.try_push(msg, n, i)) ++i;
+                else queue::host::cpu_relax();
+            }
+        });
+        std::thread cons([&] {
+            if (o.cpu_d >= 0) topology::bind_current_thread({o.cpu_d});
+            alignas(64) uint8_t buf[queue::kMaxMessageBytes];
+            uint64_t got = 0;
+            while (!stop.load(std::memory_order_relaxed)) {
+                uint32_t meta = 0, bytes = 0;
+                if (bg.try_pop(buf, &meta, &bytes)) ++got;
+                else queue::host::cpu_relax();
+            }
+            streamed.store(got);
+        });
+        const uint64_t t0 = now_ns();
+        const bool ok = pingpong<A>(o.iters, o.warmup, n, o.capacity, o.cpu_a, o.cpu_b, &r.loaded_p50_ns,
+                                    &r.loaded_p99_ns);
+        const uint64_t dt = now_ns() - t0;
+        stop.store(true);
+        prod.join();
+        cons.join();
+        r.loaded_bg_msgs_per_s = dt ? static_cast<double>(streamed.load()) / (static_cast<double>(dt) / 1e9) : 0.0;
+        r.ok = r.ok && ok;
     }
     return r;
 }
 
 }  // namespace
 
+std::vector<BaselineResult> queue_baselines(const BaselineOptions& o) {
+    if (!is_pow2(o.capacity)) throw kiwi::error("queue_baselines: capacity must be a power of two");
+    std::vector<BaselineResult> out;
+    out.push_back(run_one<KiwiRing>(o));
+    out.push_back(run_one<HeadTail>(o));
+    out.push_back(run_one<SeqSlot>(o));
+    out.push_back(run_one<RawWord>(o));
+    return out;
+}
+
 std::vector<BaselineResult> queue_baselines(uint64_t iters, uint64_t warmup, uint64_t messages, uint32_t payload_bytes,
                                             uint64_t capacity, int cpu_a, int cpu_b) {
-    if (!is_pow2(capacity)) throw kiwi::error("queue_baselines: capacity must be a power of two");
-    std::vector<BaselineResult> out;
-    out.push_back(run_one<KiwiRing>(iters, warmup, messages, payload_bytes, capacity, cpu_a, cpu_b));
-    out.push_back(run_one<HeadTail>(iters, warmup, messages, payload_bytes, capacity, cpu_a, cpu_b));
-    out.push_back(run_one<SeqSlot>(iters, warmup, messages, payload_bytes, capacity, cpu_a, cpu_b));
-    out.push_back(run_one<RawWord>(iters, warmup, messages, payload_bytes, capacity, cpu_a, cpu_b));
-    return out;
+    BaselineOptions o;
+    o.iters = iters;
+    o.warmup = warmup;
+    o.messages = messages;
+    o.payload_bytes = payload_bytes;
+    o.capacity = capacity;
+    o.cpu_a = cpu_a;
+    o.cpu_b = cpu_b;
+    return queue_baselines(o);
 }
 
 }  // namespace kiwi::bench

@@ -34,9 +34,16 @@ def test_queue_baselines_all_designs_deliver_in_order():
     right checksum, and reports latency and throughput."""
     from kiwi_b200._native import load
 
-    rs = load().bench.queue_baselines(iters=2000, warmup=200, messages=20000, payload_bytes=8, capacity=64)
+    rs = load().bench.queue_baselines(iters=2000, warmup=200, messages=20000, payload_bytes=8, capacity=64,
+                                      idle_polls=100000, loaded=True)
     names = [r["name"] for r in rs]
     assert names == ["kiwi_ring", "head_tail", "seq_slot", "raw_word"]
     for r in rs:
         assert r["ok"], r
         assert r["p50_ns"] > 0 and r["p99_ns"] >= r["p50_ns"] and r["msgs_per_s"] > 0, r
+        # idle poll and loaded ping-pong (reference modes idle-poll and loaded-latency)
+        assert 0 < r["idle_poll_ns"] < 1e5, r
+        assert r["loaded_p50_ns"] > 0 and r["loaded_p99_ns"] >= r["loaded_p50_ns"], r
+        assert r["loaded_bg_msgs_per_s"] > 0, r
+    plain = load().bench.queue_baselines(iters=200, warmup=20, messages=2000, capacity=64)
+    assert "idle_poll_ns" not in plain[0] and "loaded_p50_ns" not in plain[0]
