@@ -27,8 +27,10 @@ import kiwi_b200  # noqa: E402
 from kiwi_b200 import invoke  # noqa: E402
 from kiwi_b200.utils.build import load_inline  # noqa: E402
 
+# The CUDA source takes raw device addresses, so nvcc never parses the torch
+# headers (the generated C++ wrapper is the only torch-dependent part).
 CUDA = r"""
-#include <torch/extension.h>
+#include <cstdint>
 #include <kiwi/invoke/device_context.cuh>
 #include <kiwi/queue/queue.hpp>
 #include <kiwi/ptx.cuh>
@@ -54,14 +56,13 @@ __global__ void push_kernel(Ctx* ctx, uint8_t cb, uint32_t msgs, unsigned long l
     if (threadIdx.x == 0) atomicMax(&t[1], static_cast<unsigned long long>(kiwi::ptx::globaltimer()));
 }
 
-void push(int64_t ctx_ptr, int64_t cb, int64_t endpoints, int64_t msgs, torch::Tensor t, torch::Tensor status) {
+void push(int64_t ctx_ptr, int64_t cb, int64_t endpoints, int64_t msgs, int64_t t_ptr, int64_t status_ptr) {
     push_kernel<<<endpoints, 32>>>(reinterpret_cast<Ctx*>(ctx_ptr), static_cast<uint8_t>(cb),
-                                   static_cast<uint32_t>(msgs),
-                                   reinterpret_cast<unsigned long long*>(t.data_ptr<int64_t>()),
-                                   reinterpret_cast<uint32_t*>(status.data_ptr<int32_t>()));
+                                   static_cast<uint32_t>(msgs), reinterpret_cast<unsigned long long*>(t_ptr),
+                                   reinterpret_cast<uint32_t*>(status_ptr));
 }
 """
-CPP = "void push(int64_t ctx_ptr, int64_t cb, int64_t endpoints, int64_t msgs, torch::Tensor t, torch::Tensor status);"
+CPP = "void push(int64_t ctx_ptr, int64_t cb, int64_t endpoints, int64_t msgs, int64_t t_ptr, int64_t status_ptr);"
 
 
 def frontend_run(mod, endpoints, msgs, threads, python_cb=False, timeout_s=30.0):
@@ -82,7 +83,7 @@ def frontend_run(mod, endpoints, msgs, threads, python_cb=False, timeout_s=30.0)
     status = torch.zeros(1, dtype=torch.int32, device="cuda")
     torch.cuda.synchronize()
     h0 = time.perf_counter()
-    mod.push(ctx.device_context_ptr, cb, endpoints, msgs, t, status)
+    mod.push(ctx.device_context_ptr, cb, endpoints, msgs, t.data_ptr(), status.data_ptr())
     want = endpoints * msgs
     end = time.time() + timeout_s
     while count() < want and time.time() < end:

@@ -20,7 +20,7 @@ from kiwi_b200 import invoke  # noqa: E402
 from kiwi_b200.utils.build import load_inline  # noqa: E402
 
 CUDA = r"""
-#include <torch/extension.h>
+#include <cstdint>
 #include <kiwi/invoke/device_context.cuh>
 #include <kiwi/queue/queue.hpp>
 
