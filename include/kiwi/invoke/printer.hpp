@@ -18,8 +18,11 @@
 // bytes as in Python's standard sizes); e E f F g G a A take f or d.  Flags,
 // width and precision are kept; length modifiers written by the user are
 // replaced by the argument's own; `*` widths, %s, %p and %n are rejected.
+// %d / %i of an unsigned 64-bit value past INT64_MAX prints the value through
+// %u, where the + and space flags have no effect.
 #pragma once
 
+#include <climits>
 #include <cstdint>
 #include <cstdio>
 #include <cstring>
@@ -73,8 +76,11 @@ public:
             } else {
                 throw kiwi::error(std::string("print format: conversion %") + conv + " is not supported");
             }
+            // An unsigned 64-bit value past INT64_MAX prints through the %u form
+            // of the same spec (its value, not a negative reinterpretation).
+            const std::string spec_u = (conv == 'd' || conv == 'i') ? literal + spec + 'u' : std::string();
             spec += conv;
-            pieces_.push_back({literal + spec, code, conv, off});
+            pieces_.push_back({literal + spec, spec_u, code, conv, off});
             literal.clear();
             off += size;
             i = j;
@@ -110,8 +116,13 @@ public:
             } else if (is_signed(pc.code)) {
                 w = std::snprintf(buf, sizeof(buf), pc.spec.c_str(), static_cast<long long>(read_int(p, pc)));
             } else {
-                w = std::snprintf(buf, sizeof(buf), pc.spec.c_str(),
-                                  static_cast<unsigned long long>(read_uint(p, pc)));
+                const unsigned long long v = read_uint(p, pc);
+                const bool signed_conv = pc.conv == 'd' || pc.conv == 'i';
+                if (signed_conv && v <= static_cast<unsigned long long>(INT64_MAX)) {
+                    w = std::snprintf(buf, sizeof(buf), pc.spec.c_str(), static_cast<long long>(v));
+                } else {
+                    w = std::snprintf(buf, sizeof(buf), (signed_conv ? pc.spec_u : pc.spec).c_str(), v);
+                }
             }
             if (w > 0) out.append(buf, static_cast<size_t>(w) < sizeof(buf) ? static_cast<size_t>(w) : sizeof(buf) - 1);
         }
@@ -134,7 +145,8 @@ public:
 
 private:
     struct Piece {
-        std::string spec;  // literal text before the conversion + the conversion itself
+        std::string spec;    // literal text before the conversion + the conversion itself
+        std::string spec_u;  // the same with %u, for %d / %i of unsigned values past INT64_MAX
         char code;
         char conv;
         uint32_t offset;

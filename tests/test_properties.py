@@ -4,6 +4,7 @@ wrap-around and tag cycles; any payload reaches its callback byte for byte;
 any valid EP configuration lays out aligned, non-overlapping heap regions.
 (Reference test categories: the queue basic/chunk tests, the invoke
 serializer tests and the EP layout tests of AMDResearch/kiwi.)"""
+import os
 import struct
 
 import pytest
@@ -103,3 +104,59 @@ def test_tag_cycle_never_zero_and_changes_every_lap():
         t0 = kq.lap_tag(lap * 16, 16)
         t1 = kq.lap_tag((lap + 1) * 16, 16)
         assert 1 <= t0 <= 65535 and t0 != t1
+
+
+# ---- native print formatter vs Python's printf-compatible % operator ----
+
+_INT_CODES = {"b": (-128, 127), "B": (0, 255), "h": (-(1 << 15), (1 << 15) - 1), "H": (0, (1 << 16) - 1),
+              "i": (-(1 << 31), (1 << 31) - 1), "I": (0, (1 << 32) - 1), "q": (-(1 << 63), (1 << 63) - 1),
+              "Q": (0, (1 << 64) - 1)}
+
+
+@st.composite
+def _print_case(draw):
+    """(C format, the same format for Python's %, struct codes, values).  The
+    generator avoids the combinations where Python's % differs from C's printf:
+    the 0 flag with an integer precision, +/space with x, X, o, and a zero
+    printed with precision 0."""
+    fmt, py_fmt, codes, values = "", "", "", []
+    for _ in range(draw(st.integers(0, 4))):
+        lit = draw(st.text(alphabet="ab =:|-", max_size=4))
+        width = draw(st.sampled_from(["", "3", "12"]))
+        if draw(st.booleans()):
+            conv = draw(st.sampled_from("dixXo"))
+            code = draw(st.sampled_from("BHIQ" if conv in "xXo" else sorted(_INT_CODES)))
+            lo, hi = _INT_CODES[code]
+            v = draw(st.integers(lo, hi))
+            prec = draw(st.sampled_from(["", ".0", ".3"])) if conv in "di" else ""
+            if prec == ".0" and v == 0:  # C prints nothing here, Python's % prints 0
+                prec = ""
+            flag_set = "-" if conv in "xXo" else ("-+ " if prec else "-+ 0")
+            if v > (1 << 63) - 1:  # printed through %u: no sign flags (documented in printer.hpp)
+                flag_set = flag_set.replace("+", "").replace(" ", "")
+            flags = "".join(sorted(set(draw(st.text(alphabet=flag_set, max_size=2)))))
+            length = draw(st.sampled_from(["", "l", "ll", "h"]))  # replaced by the argument's own
+            fmt += lit + "%" + flags + width + prec + length + conv
+            py_fmt += lit + "%" + flags + width + prec + conv
+        else:
+            code = draw(st.sampled_from("fd"))
+            v = draw(st.floats(-1e6, 1e6, allow_nan=False, width=32 if code == "f" else 64))
+            conv = draw(st.sampled_from("efgEG"))
+            prec = draw(st.sampled_from(["", ".0", ".3"]))
+            flags = "".join(sorted(set(draw(st.text(alphabet="-+ 0", max_size=2)))))
+            fmt += lit + "%" + flags + width + prec + conv
+            py_fmt += lit + "%" + flags + width + prec + conv
+        codes += code
+        values.append(v)
+    tail = draw(st.text(alphabet="xyz ", max_size=3)) + draw(st.sampled_from(["", "%%"]))
+    return fmt + tail, py_fmt + tail, codes, values
+
+
+@settings(max_examples=int(os.environ.get("KIWI_PROPERTY_EXAMPLES", "400")), deadline=None)
+@given(_print_case())
+def test_native_print_matches_printf_semantics(case):
+    fmt, py_fmt, codes, values = case
+    payload = struct.pack("<" + codes, *values)
+    got = load().print_format.format(fmt, "<" + codes, payload)
+    vals = struct.unpack("<" + codes, payload)  # float32 rounding as the device would send it
+    assert got == py_fmt % tuple(vals)
