@@ -160,3 +160,27 @@ def test_native_print_matches_printf_semantics(case):
     got = load().print_format.format(fmt, "<" + codes, payload)
     vals = struct.unpack("<" + codes, payload)  # float32 rounding as the device would send it
     assert got == py_fmt % tuple(vals)
+
+
+_U64 = st.integers(0, (1 << 64) - 1)
+
+
+@settings(max_examples=int(os.environ.get("KIWI_PROPERTY_EXAMPLES", "400")), deadline=None)
+@given(st.integers(1, 16), _U64, st.integers(-2, 18), _U64, _U64)
+def test_checked_mode_rule_matches_interval_model(world, limit, rank, off, nbytes):
+    """The P2P checked mode admits exactly the accesses whose byte interval
+    lies inside [0, limit) of an existing rank, with no wrap-around."""
+    want = 0 <= rank < world and off + nbytes <= limit
+    assert load().p2p.heap_range_ok(world, limit, rank, off, nbytes) == want
+
+
+@settings(max_examples=int(os.environ.get("KIWI_PROPERTY_EXAMPLES", "400")), deadline=None)
+@given(st.lists(st.integers(1, (1 << 63) - 1), min_size=4, max_size=64))
+def test_debug_words_decode_inverts_the_device_encoding(times):
+    """Start words (0 and 2 of each phase) are stored as ~t, end words as t;
+    0 stays 'not recorded'."""
+    mask = (1 << 64) - 1
+    raw = [(~t & mask) if (i % 4) % 2 == 0 else t for i, t in enumerate(times)]
+    raw[0] = 0
+    got = load().ep.decode_debug_words(raw)
+    assert got[0] == 0 and got[1:] == times[1:]
