@@ -266,6 +266,12 @@ class EpDispatchCombine(_DebugTimingMixin):
         return self.moe.native
 
 
+def _to_send_flat_idx(pos, max_tokens, world):
+    """Receive-slot positions (src_rank * max_tokens + token, as the receive
+    kernels record them) -> src_rank * (world * max_tokens) + token."""
+    return (pos // max_tokens) * (world * max_tokens) + pos % max_tokens
+
+
 class KiwiEpOp(_DebugTimingMixin):
     """Expert-parallel dispatch/combine with the reference's operator contract
     (``KiwiEpOp`` of apps/ep/python/kiwi_ep_bindings.hip.cpp:123-574 of
@@ -312,6 +318,7 @@ class KiwiEpOp(_DebugTimingMixin):
         rows, w, sc, idx, count = self._op.dispatch(input.contiguous(), indices.to(torch.int32).contiguous(),
                                                     weights.float().contiguous())
         self._last_tokens = input.shape[0]
+        self._count = count
         if self._quant == "none":
             rows = rows.view(torch.bfloat16)
         elif self._quant == "fp8":
@@ -339,10 +346,21 @@ class KiwiEpOp(_DebugTimingMixin):
         return self._out[:self._last_tokens] if self._out is not None else None, None
 
     def reset(self):
-        """Nothing to clear: slots are epoch-tagged (kept for call-shape parity)."""
+        """Ends the current round on the host.  Device slots are epoch-tagged,
+        so nothing on the GPU needs clearing; like the reference, the call is
+        refused while the current stream is being captured into a graph and
+        otherwise waits for the stream."""
+        if torch.cuda.is_current_stream_capturing():
+            raise RuntimeError("KiwiEpOp.reset() is not supported during graph capture; dispatch and combine "
+                               "already carry their per-round state on the device")
+        torch.cuda.current_stream().synchronize()
+        self._last_tokens = 0
 
     def max_num_tokens_to_recv(self):
         return self.world_size * self.max_tokens
+
+    def max_num_tokens_to_recv_per_rank(self):
+        return self.max_tokens
 
     def max_num_tokens_to_send(self):
         return self.world_size * self.max_tokens
@@ -350,9 +368,43 @@ class KiwiEpOp(_DebugTimingMixin):
     def max_num_tokens_to_send_per_rank(self):
         return self.max_tokens
 
+    def launch_policy(self, num_tokens):
+        """The launch configuration dispatch / combine use (the B200 tuning
+        table with KIWI_EP_TUNING applied): grid sizes of the EP kernels, the
+        transport and the table's source.  ``num_tokens`` is accepted for call
+        compatibility; the table is keyed by the op's configuration."""
+        sms = torch.cuda.get_device_properties(torch.cuda.current_device()).multi_processor_count
+        t = dict(_C.ep.tune(self.layout, sms, os.environ.get("KIWI_EP_TUNING")))
+        t.update(num_tokens=int(num_tokens), num_blocks=t["dispatch_blocks"], transport="nvlink",
+                 gpu_arch="sm_100a")
+        return t
+
+    def decode_send_flat_idx(self, flat_idx):
+        """(source rank, source token) of a position from get_dispatch_src_token_pos()."""
+        stride = self.max_num_tokens_to_send()
+        return int(flat_idx) // stride, int(flat_idx) % stride
+
     def get_dispatch_src_token_pos(self):
-        """Encoded source position (src_rank * max_tokens + token) of each received row."""
-        return self._op.src_token_pos
+        """Source position of each row received by the last dispatch, encoded as
+        ``src_rank * max_num_tokens_to_send() + src_token`` (the reference's
+        encoding; decode_send_flat_idx inverts it).  Reads the received count,
+        so it synchronises the current stream."""
+        n = int(self._count.item()) if getattr(self, "_count", None) is not None else 0
+        return _to_send_flat_idx(self._op.src_token_pos[:n], self.max_tokens, self.world_size)
+
+    def get_registered_combine_input_buffer(self, combine_dtype=torch.bfloat16, hidden_dim=-1):
+        """Operator-owned [max_num_tokens_to_recv(), hidden] buffer a caller can
+        write expert outputs into and pass to combine() without a copy."""
+        if combine_dtype != torch.bfloat16:
+            raise ValueError("combine_dtype must be torch.bfloat16")
+        if hidden_dim > 0 and hidden_dim != self.hidden_dim:
+            raise ValueError("get_registered_combine_input_buffer hidden_dim must match the configured hidden_dim")
+        buf = getattr(self, "_combine_in", None)
+        if buf is None:
+            dev = torch.device("cuda", torch.cuda.current_device())
+            buf = self._combine_in = torch.empty(self.max_num_tokens_to_recv(), self.hidden_dim,
+                                                 dtype=torch.bfloat16, device=dev)
+        return buf
 
     def _debug_native(self):
         return self._op

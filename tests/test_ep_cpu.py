@@ -182,3 +182,22 @@ def test_debug_phases_table_relative_to_first_stamp():
     text = format_debug_timing(snap)
     assert "rank=3" in text and "tokens=128" in text
     assert text.index("dispatch") < text.index("recv_count")
+
+
+def test_kiwi_ep_op_source_position_encoding_round_trips():
+    """get_dispatch_src_token_pos uses the reference's encoding
+    src_rank * (world * max_tokens) + token, and decode_send_flat_idx inverts it."""
+    from kiwi_b200.parallel.ep import KiwiEpOp, _to_send_flat_idx
+
+    world, max_tokens = 4, 10
+    slots = torch.arange(world * max_tokens)  # receive-slot order: src_rank * max_tokens + token
+    enc = _to_send_flat_idx(slots, max_tokens, world)
+    op = KiwiEpOp.__new__(KiwiEpOp)
+    op.world_size, op.max_tokens, op.hidden_dim = world, max_tokens, 64
+    assert op.max_num_tokens_to_send() == 40 and op.max_num_tokens_to_recv_per_rank() == 10
+    for s, e in zip(slots.tolist(), enc.tolist()):
+        assert op.decode_send_flat_idx(e) == (s // max_tokens, s % max_tokens)
+    with pytest.raises(ValueError):
+        op.get_registered_combine_input_buffer(torch.float32)
+    with pytest.raises(ValueError):
+        op.get_registered_combine_input_buffer(torch.bfloat16, hidden_dim=32)

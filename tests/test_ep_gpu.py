@@ -262,3 +262,33 @@ def test_debug_timing_of_the_transport_op():
     for name in ("dispatch", "recv_count", "recv_compact", "gather_rows", "combine_rows", "combine_recv"):
         assert name in ph, sorted(ph)
     assert ph["dispatch"]["end_us"] <= ph["combine_recv"]["start_us"] + 2.0
+
+
+@pytest.mark.filterwarnings("ignore:The CUDA Graph is empty")
+def test_kiwi_ep_op_reference_accessors():
+    """launch_policy, the registered combine-input buffer (combine straight
+    from it), source positions and reset() refused during graph capture."""
+    from kiwi_b200.parallel.ep import KiwiEpOp
+
+    op = KiwiEpOp(hidden_dim=256, topk=2, num_experts_per_rank=4, max_num_inp_token_per_rank=16)
+    pol = op.launch_policy(16)
+    assert pol["num_blocks"] > 0 and pol["transport"] == "nvlink" and pol["num_tokens"] == 16
+    buf = op.get_registered_combine_input_buffer(torch.bfloat16)
+    assert tuple(buf.shape) == (16, 256) and buf.data_ptr() == op.get_registered_combine_input_buffer().data_ptr()
+    x = torch.randn(16, 256, device="cuda").bfloat16()
+    idx, w = moe.route_reference(torch.randn(16, 4, device="cuda"), 2)
+    rows, _, _, _, cnt = op.dispatch(x, w, None, idx)
+    n = int(cnt.item())
+    assert n == 16
+    pos = op.get_dispatch_src_token_pos()
+    assert [op.decode_send_flat_idx(p) for p in pos.tolist()] == [(0, t) for t in range(16)]
+    buf[:n].copy_(rows[:n])
+    out, _ = op.combine(buf, None, idx)
+    torch.cuda.synchronize()
+    op.check()
+    assert torch.equal(out, x)  # world of 1: one row per token comes back unchanged
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        with pytest.raises(RuntimeError):
+            op.reset()
+    op.reset()
