@@ -556,6 +556,8 @@ void register_ep(py::module_& m) {
         e.attr("DEBUG_PHASES") = pn;
         e.attr("DEBUG_META") = mn;
     }
+    e.def("dispatch_grid", &ep::dispatch_grid, py::arg("tokens"), py::arg("tuned"), py::arg("sms"),
+          "Blocks the dispatch kernel launches for `tokens` tokens (tuned > 0: that many).");
     e.def("decode_debug_words",
           [](const std::vector<uint64_t>& raw) {
               std::vector<uint64_t> out(raw.size(), 0);

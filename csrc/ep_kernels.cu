@@ -703,15 +703,18 @@ void launch_route(const float* logits, int tokens, int experts, int topk, int32_
     KIWI_CUDA_CHECK(cudaGetLastError());
 }
 
+int dispatch_grid(int tokens, int tuned, int sms) {
+    if (tuned > 0) return tuned;
+    // One warp per token up to 8 blocks per SM: dispatch is load- and
+    // store-latency bound, so every token's loads should be in flight at once.
+    const int want = (tokens * 32 + kThreads - 1) / kThreads;
+    return std::max(1, std::min(want, 8 * std::max(1, sms)));
+}
+
 void launch_dispatch(const EpConfig& c, const p2p::HeapView& h, const __nv_bfloat16* x, const int32_t* idx,
                      const float* w, int tokens, const EpWorkspace& ws, int grid, cudaStream_t s) {
     if (tokens > c.max_tokens) throw kiwi::error("dispatch: more tokens than max_tokens");
-    if (grid <= 0) {
-        // One warp per token up to 8 blocks per SM: dispatch is load- and
-        // store-latency bound, so every token's loads should be in flight at once.
-        const int want = (tokens * 32 + kThreads - 1) / kThreads;
-        grid = std::max(1, std::min(want, 8 * default_grid()));
-    }
+    grid = dispatch_grid(tokens, grid, default_grid());
     const size_t smem = static_cast<size_t>(kThreads / 32) * (c.meta_bytes + c.scale_bytes);
     if (smem > 48 * 1024) throw kiwi::error("dispatch: per-token staging exceeds 48 KB per block (hidden too large)");
     switch (static_cast<Quant>(c.quant)) {

@@ -37,6 +37,10 @@ enum EpSite : uint32_t {
 
 void launch_begin(const EpConfig& c, const EpWorkspace& ws, cudaStream_t s);
 
+/// Blocks launch_dispatch runs for `tokens` tokens: `tuned` when positive,
+/// else one warp per token capped at 8 blocks per SM.
+int dispatch_grid(int tokens, int tuned, int sms);
+
 /// Top-k routing with softmax over the selected logits (logits fp32 [T, E]).
 void launch_route(const float* logits, int tokens, int experts, int topk, int32_t* idx, float* w, cudaStream_t s,
                   uint64_t* debug_time = nullptr);

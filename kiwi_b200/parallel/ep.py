@@ -292,16 +292,40 @@ class KiwiEpOp(_DebugTimingMixin):
 
     _DTYPES = {torch.bfloat16: "none", torch.float8_e4m3fn: "fp8", "fp8": "fp8", "nvfp4": "nvfp4", "none": "none"}
 
-    def __init__(self, hidden_dim, topk, num_experts_per_rank, max_num_inp_token_per_rank,
-                 dispatch_dtype=torch.bfloat16, combine_dtype=torch.bfloat16, group=None, timeout_s=5.0, **_ignored):
-        if combine_dtype != torch.bfloat16:
-            raise ValueError("combine_dtype must be torch.bfloat16")
-        quant = self._DTYPES.get(dispatch_dtype)
+    _QUANT_FORMATS = {"none": None, "fp8": "fp8", "fp4": "nvfp4"}
+
+    def __init__(self, device_id=None, world_size=None, hidden_dim=None, topk=None, num_experts_per_rank=None,
+                 max_num_inp_token_per_rank=None, dispatch_dtype=torch.bfloat16, combine_dtype=torch.bfloat16,
+                 *_launch_args, group=None, timeout_s=5.0, dispatch_quant_format="none", combine_quant_format="none",
+                 **_ignored):
+        """Arguments in the reference's order and names (device_id, world_size,
+        hidden_dim, topk, num_experts_per_rank, max_num_inp_token_per_rank,
+        dispatch_dtype, combine_dtype, ...); its launch arguments (num_blocks,
+        num_proxy_threads, scale sizes, queue_capacity, rcomp_backend, ...) are
+        accepted and ignored.  ``device_id`` selects the CUDA device and
+        ``world_size`` must equal the size of ``group``.  The wire format is
+        ``dispatch_quant_format`` ("fp8" / "fp4") when given, else follows
+        ``dispatch_dtype``; dispatch always takes bf16 rows and quantises them."""
+        missing = [n for n, v in (("hidden_dim", hidden_dim), ("topk", topk),
+                                  ("num_experts_per_rank", num_experts_per_rank),
+                                  ("max_num_inp_token_per_rank", max_num_inp_token_per_rank)) if v is None]
+        if missing:
+            raise TypeError("KiwiEpOp missing required arguments: " + ", ".join(missing))
+        if combine_dtype != torch.bfloat16 or str(combine_quant_format).lower() != "none":
+            raise ValueError("combine_dtype must be torch.bfloat16 (combine_quant_format 'none')")
+        fmt = str(dispatch_quant_format).lower()
+        if fmt not in self._QUANT_FORMATS:
+            raise ValueError(f"unsupported dispatch_quant_format {dispatch_quant_format!r} (none, fp8 or fp4)")
+        quant = self._QUANT_FORMATS[fmt] or self._DTYPES.get(dispatch_dtype)
         if quant is None:
             raise ValueError(f"unsupported dispatch_dtype {dispatch_dtype}")
+        if device_id is not None:
+            torch.cuda.set_device(int(device_id))
         self.group = group
         self.rank = kdist.rank(group)
         self.world_size = kdist.world_size(group)
+        if world_size is not None and int(world_size) != self.world_size:
+            raise ValueError(f"world_size {world_size} differs from the process group's {self.world_size}")
         self.hidden_dim = hidden_dim
         self.topk = topk
         self.max_tokens = max_num_inp_token_per_rank
@@ -373,10 +397,10 @@ class KiwiEpOp(_DebugTimingMixin):
         table with KIWI_EP_TUNING applied): grid sizes of the EP kernels, the
         transport and the table's source.  ``num_tokens`` is accepted for call
         compatibility; the table is keyed by the op's configuration."""
-        sms = torch.cuda.get_device_properties(torch.cuda.current_device()).multi_processor_count
+        sms = _default_sms()
         t = dict(_C.ep.tune(self.layout, sms, os.environ.get("KIWI_EP_TUNING")))
-        t.update(num_tokens=int(num_tokens), num_blocks=t["dispatch_blocks"], transport="nvlink",
-                 gpu_arch="sm_100a")
+        t.update(num_tokens=int(num_tokens), num_blocks=_C.ep.dispatch_grid(int(num_tokens), 0, sms),
+                 transport="nvlink", gpu_arch="sm_100a")
         return t
 
     def decode_send_flat_idx(self, flat_idx):
@@ -415,5 +439,57 @@ class KiwiEpOp(_DebugTimingMixin):
             raise RuntimeError(f"kiwi ep error: code={code} site={site} info={info} rank={rank}")
 
 
+# ---- module-level helpers of the reference's extension (kiwi_ep_ext) ----
+
+def barrier(group=None):
+    """Host barrier over the process group (the reference's LCI barrier)."""
+    kdist.barrier(group)
+
+
+def get_rank(group=None):
+    return kdist.rank(group)
+
+
+def get_nranks(group=None):
+    return kdist.world_size(group)
+
+
+def get_hca_name_for_gpu(device=None):
+    """Always "": every peer is reached over NVLink, no NIC is selected."""
+    return ""
+
+
+def get_hca_name_for_current_gpu():
+    return ""
+
+
+def _default_sms():
+    try:
+        if torch.cuda.is_available():
+            return torch.cuda.get_device_properties(torch.cuda.current_device()).multi_processor_count
+    except Exception:  # noqa: BLE001
+        pass
+    return 148  # B200
+
+
+def recommended_runtime_defaults(num_tokens, world_size, gpu_arch="", nic_family="", hidden_dim=7168,
+                                 num_experts=256, topk=8, quant="fp8"):
+    """Launch defaults the B200 tuning table gives an op of `num_tokens` tokens
+    per rank on `world_size` ranks (KIWI_EP_TUNING applied).  gpu_arch and
+    nic_family are accepted for call compatibility: the table is keyed by the
+    configuration and this GPU's SM count."""
+    cfg = dict(world=int(world_size), rank=0, hidden=hidden_dim, num_experts=num_experts, topk=topk,
+               max_tokens=max(1, int(num_tokens)), quant=quant)
+    sms = _default_sms()
+    t = dict(_C.ep.tune(cfg, sms, os.environ.get("KIWI_EP_TUNING")))
+    t.update(num_blocks=_C.ep.dispatch_grid(int(num_tokens), t["dispatch_blocks"], sms), rcomp_backend="nvlink")
+    return t
+
+
+def recommended_num_blocks(num_tokens, world_size, gpu_arch="", nic_family=""):
+    return recommended_runtime_defaults(num_tokens, world_size, gpu_arch, nic_family)["num_blocks"]
+
+
 __all__ = ["ExpertParallelMoE", "EpDispatchCombine", "KiwiEpOp", "layer_config", "debug_phases",
-           "format_debug_timing"]
+           "format_debug_timing", "barrier", "get_rank", "get_nranks", "get_hca_name_for_gpu",
+           "get_hca_name_for_current_gpu", "recommended_num_blocks", "recommended_runtime_defaults"]

@@ -201,3 +201,23 @@ def test_kiwi_ep_op_source_position_encoding_round_trips():
         op.get_registered_combine_input_buffer(torch.float32)
     with pytest.raises(ValueError):
         op.get_registered_combine_input_buffer(torch.bfloat16, hidden_dim=32)
+
+
+def test_kiwi_ep_ext_module_surface():
+    """The reference extension's module-level API under its own name."""
+    from kiwi_b200.parallel import kiwi_ep_ext as ext
+
+    assert ext.get_rank() == 0 and ext.get_nranks() == 1
+    ext.barrier()
+    assert ext.get_hca_name_for_gpu(0) == "" and ext.get_hca_name_for_current_gpu() == ""
+    d = ext.recommended_runtime_defaults(128, 8)
+    assert d["num_blocks"] > 0 and d["rcomp_backend"] == "nvlink"
+    assert ext.recommended_num_blocks(4096, 8) >= ext.recommended_num_blocks(8, 8) > 0
+    with ext.LciContext("") as ctx:
+        assert ctx.nranks == 1
+    with pytest.raises(TypeError):
+        ext.KiwiEpOp(0, 1, 512)  # topk, experts per rank and max tokens missing
+    with pytest.raises(ValueError):
+        ext.KiwiEpOp(0, 1, 512, 2, 8, 16, torch.bfloat16, torch.float32)
+    with pytest.raises(ValueError):
+        ext.KiwiEpOp(0, 1, 512, 2, 8, 16, torch.bfloat16, torch.bfloat16, dispatch_quant_format="int4")
