@@ -118,4 +118,22 @@ void register_ops(py::module_& m) {
         return py::make_tuple(i.local_bytes, i.registers, i.smem_bytes);
     });
     o.def("num_sms", &gemm::num_sms);
+    o.def(
+        "tma_load_rate",
+        [](torch::Tensor t, int box_rows, int box_k, int stages, int64_t iters, int grid, bool shared_rows) {
+            TORCH_CHECK(t.is_cuda() && t.scalar_type() == torch::kBFloat16 && t.dim() == 2 && t.is_contiguous(),
+                        "tma_load_rate: a contiguous 2-D bf16 CUDA tensor");
+            if (grid <= 0) grid = gemm::num_sms();
+            auto opts = torch::TensorOptions().device(t.device());
+            torch::Tensor cycles = torch::zeros({grid}, opts.dtype(torch::kInt64));
+            torch::Tensor error = torch::zeros({1}, opts.dtype(torch::kInt32));
+            gemm::tma_load_rate(t.data_ptr(), t.size(0), t.size(1), box_rows, box_k, stages, iters, grid, shared_rows,
+                                reinterpret_cast<uint64_t*>(cycles.data_ptr<int64_t>()),
+                                reinterpret_cast<uint32_t*>(error.data_ptr<int32_t>()),
+                                at::cuda::getCurrentCUDAStream().stream());
+            return py::make_tuple(cycles, error);
+        },
+        py::arg("tensor"), py::arg("box_rows"), py::arg("box_k"), py::arg("stages"), py::arg("iters"),
+        py::arg("grid") = 0, py::arg("shared_rows") = false,
+        "TMA operand-feed probe (no MMAs): (cycles per CTA, error word), enqueued on the current stream.");
 }
