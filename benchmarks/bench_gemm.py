@@ -48,8 +48,9 @@ def main():
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--no-torch", action="store_true")
     ap.add_argument("--no-pair", action="store_true", help="skip the 2-SM (cta_group::2) kernel")
-    ap.add_argument("--bk", type=int, default=64, choices=(64, 32),
-                    help="K columns per pipeline stage of the 1-SM kernel (32: 64-byte swizzle, 9 stages)")
+    ap.add_argument("--bk", type=int, default=64, choices=(64, 32, 128),
+                    help="K columns per pipeline stage of the 1-SM kernel (32: 64-byte swizzle, 9 stages; "
+                         "128: two 64-column boxes per operand, 2 stages)")
     args = ap.parse_args()
     C = kiwi_b200.native()
     torch.manual_seed(0)

@@ -61,6 +61,10 @@ template <int BN, int STAGES = kStages, bool STAGING = false, int GQ = -1, int B
 struct Smem {
     static constexpr int kABytes = kBM * BKT * 2;
     static constexpr int kBBytes = BN * BKT * 2;
+    // BKT = 128: each operand's stage holds two 64-column, 128-byte-swizzled
+    // sub-tiles back to back (one TMA box each).
+    static constexpr int kASub = kBM * 64 * 2;
+    static constexpr int kBSub = BN * 64 * 2;
     static constexpr int kStageBytes = kABytes + kBBytes;
     static constexpr int kStgStride = BN;  // BN/2 bf16 columns = BN bytes per staged row
     static constexpr int kStgOffset = STAGES * kStageBytes;
@@ -110,7 +114,7 @@ __global__ void __launch_bounds__(GQ >= 0 ? kGatherThreads : kThreads, 1)
     grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                         GroupedArgs p, const __grid_constant__ ScatterArgs sc, const __grid_constant__ GatherArgs ga) {
     constexpr int kStages = STAGES;
-    constexpr int kBK = BKT;  // K per stage (64: 128-byte swizzle, 32: 64-byte swizzle)
+    constexpr int kBK = BKT;  // K per stage (64: 128-byte swizzle, 32: 64-byte swizzle, 128: two 64-column boxes)
     static_assert(GQ < 0 || BKT == 64, "the gathering producer writes 128-byte rows");
     using S = Smem<BN, STAGES, EPI == kEpiScatter, GQ, BKT>;
     __shared__ uint8_t* s_base[kScatterMaxRanks];
@@ -189,8 +193,14 @@ __global__ void __launch_bounds__(GQ >= 0 ? kGatherThreads : kThreads, 1)
                     } else {
                         sm100::mbar_arrive_expect_tx(&full[stage], S::kStageBytes);
                         sm100::tma_load_2d(sa, &tmap_a, &full[stage], kb * kBK, row0);
+                        if constexpr (BKT == 128) {
+                            sm100::tma_load_2d(sa + S::kASub, &tmap_a, &full[stage], kb * kBK + 64, row0);
+                        }
                     }
                     sm100::tma_load_2d(sb, &tmap_b, &full[stage], kb * kBK, brow0);
+                    if constexpr (BKT == 128) {
+                        sm100::tma_load_2d(sb + S::kBSub, &tmap_b, &full[stage], kb * kBK + 64, brow0);
+                    }
                     if (++stage == kStages) {
                         stage = 0;
                         phase ^= 1;
@@ -233,8 +243,14 @@ __global__ void __launch_bounds__(GQ >= 0 ? kGatherThreads : kThreads, 1)
                     const uint64_t bdesc = sm100::kmajor_desc<BKT>(sb);
 #pragma unroll
                     for (int kk = 0; kk < kBK / 16; ++kk) {
-                        // +32 bytes of K per step inside the swizzle atom.
-                        sm100::mma_bf16(d, adesc + 2 * kk, bdesc + 2 * kk, idesc, (kb | kk) != 0 ? 1u : 0u);
+                        // +32 bytes of K per step inside the swizzle atom; with
+                        // BKT = 128, steps 4..7 move to the second sub-tile (the
+                        // descriptor's start address is in 16-byte units).
+                        const int sub = BKT == 128 ? kk >> 2 : 0;
+                        const int w = BKT == 128 ? kk & 3 : kk;
+                        const uint64_t ad = adesc + static_cast<uint64_t>(sub * (S::kASub >> 4) + 2 * w);
+                        const uint64_t bd = bdesc + static_cast<uint64_t>(sub * (S::kBSub >> 4) + 2 * w);
+                        sm100::mma_bf16(d, ad, bd, idesc, (kb | kk) != 0 ? 1u : 0u);
                     }
                     sm100::mma_commit(&empty[stage]);
                     if (++stage == kStages) {
@@ -905,7 +921,8 @@ void grouped_gemm(const CUtensorMap& tmap_a, const CUtensorMap& tmap_b, const Gr
     else launch_grouped<kEpiStore, kStages>(tmap_a, tmap_b, args, none, grid, stream);
 }
 
-constexpr int kBk32Stages = 9;  // 9 x 24 KB stages
+constexpr int kBk32Stages = 9;   // 9 x 24 KB stages
+constexpr int kBk128Stages = 2;  // 2 x 96 KB stages (half the stage hand-offs of BK 64 per FLOP)
 
 void tma_load_rate(const void* ptr, int64_t rows, int64_t k, int box_rows, int box_k, int stages, int64_t iters,
                    int grid, bool shared_rows, uint64_t* cycles, uint32_t* error, cudaStream_t stream) {
@@ -926,6 +943,17 @@ void tma_load_rate(const void* ptr, int64_t rows, int64_t k, int box_rows, int b
     tma_rate_kernel<<<grid, 64, smem, stream>>>(m, box_rows, box_k, stages, iters, static_cast<int>(rows),
                                                 static_cast<int>(k), shared_rows ? 1 : 0, cycles, error);
     KIWI_CUDA_CHECK(cudaGetLastError());
+}
+
+void grouped_gemm_bk128(const CUtensorMap& tmap_a, const CUtensorMap& tmap_b, const GroupedArgs& args, bool swiglu,
+                        int grid, cudaStream_t stream) {
+    if (args.n % 256 != 0 || args.k % 128 != 0) {
+        throw kiwi::error("grouped_gemm_bk128: N must be a multiple of 256 and K of 128");
+    }
+    if (grid <= 0) grid = num_sms();
+    const ScatterArgs none{};
+    if (swiglu) launch_grouped<kEpiSwiGLU, kBk128Stages, -1, 128>(tmap_a, tmap_b, args, none, grid, stream);
+    else launch_grouped<kEpiStore, kBk128Stages, -1, 128>(tmap_a, tmap_b, args, none, grid, stream);
 }
 
 void grouped_gemm_bk32(const CUtensorMap& tmap_a32, const CUtensorMap& tmap_b32, const GroupedArgs& args,

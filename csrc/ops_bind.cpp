@@ -42,8 +42,9 @@ public:
     /// counts: int32[G] rows per group (device); out: bf16 [rows, N] or [rows, N/2] with swiglu.
     void run(torch::Tensor counts, torch::Tensor out, bool swiglu, py::object row_scale, int grid, bool pair,
              py::object trace, int bk) {
-        TORCH_CHECK(bk == 64 || bk == 32, "bk must be 64 or 32");
-        TORCH_CHECK(bk == 64 || !pair, "bk = 32 is a 1-SM variant");
+        TORCH_CHECK(bk == 64 || bk == 32 || bk == 128, "bk must be 64, 32 or 128");
+        TORCH_CHECK(bk == 64 || !pair, "bk = 32 and 128 are 1-SM variants");
+        TORCH_CHECK(bk != 128 || k_ % 128 == 0, "bk = 128 needs K a multiple of 128");
         TORCH_CHECK(counts.is_cuda() && counts.scalar_type() == torch::kInt32 && counts.numel() == num_groups_,
                     "counts must be int32[num_groups] on the device");
         TORCH_CHECK(out.scalar_type() == torch::kBFloat16 && out.is_contiguous(), "out must be contiguous bf16");
@@ -80,6 +81,8 @@ public:
         }
         if (bk == 32) {
             gemm::grouped_gemm_bk32(tmap_a32_, tmap_b32_, args, swiglu, grid, s);
+        } else if (bk == 128) {
+            gemm::grouped_gemm_bk128(tmap_a_, tmap_b_, args, swiglu, grid, s);
         } else if (pair) {
             gemm::grouped_gemm_pair(tmap_a_, tmap_b_half_, args, swiglu, grid, s);
         } else {
@@ -105,7 +108,10 @@ void register_ops(py::module_& m) {
         .def(py::init<torch::Tensor, torch::Tensor, int64_t>(), py::arg("a"), py::arg("b"), py::arg("num_groups"))
         .def("run", &GroupedGemm::run, py::arg("counts"), py::arg("out"), py::arg("swiglu") = false,
              py::arg("row_scale") = py::none(), py::arg("grid") = 0, py::arg("pair") = false,
-             py::arg("trace") = py::none(), py::arg("bk") = 64)
+             py::arg("trace") = py::none(), py::arg("bk") = 64,
+             "Grouped GEMM on the current stream.  bk: K columns per pipeline stage of the 1-SM kernel (64: "
+             "4 x 48 KB stages, the default; 32: 64-byte swizzle, 9 stages; 128: two 64-column boxes per operand, "
+             "2 x 96 KB stages).  All three issue the same K = 16 MMAs in the same order.")
         .def_property_readonly("offsets", &GroupedGemm::offsets)
         .def_property_readonly("tile_prefix", &GroupedGemm::tile_prefix)
         .def_property_readonly("error", &GroupedGemm::error);

@@ -109,6 +109,12 @@ void grouped_gemm(const CUtensorMap& tmap_a, const CUtensorMap& tmap_b, const Gr
 void tma_load_rate(const void* ptr, int64_t rows, int64_t k, int box_rows, int box_k, int stages, int64_t iters,
                    int grid, bool shared_rows, uint64_t* cycles, uint32_t* error, cudaStream_t stream);
 
+/// The 1-SM kernel with 128 columns of K per stage: two 64-column boxes per
+/// operand (the default 128-byte-swizzled maps), 2 stages of 96 KB, the same
+/// MMA order as grouped_gemm.  K must be a multiple of 128.
+void grouped_gemm_bk128(const CUtensorMap& tmap_a, const CUtensorMap& tmap_b, const GroupedArgs& args, bool swiglu,
+                        int grid, cudaStream_t stream);
+
 void grouped_gemm_bk32(const CUtensorMap& tmap_a32, const CUtensorMap& tmap_b32, const GroupedArgs& args,
                        bool swiglu, int grid, cudaStream_t stream);
 

@@ -154,12 +154,13 @@ KIWI_DEV uint64_t sw64_kmajor_desc(const void* smem_tile) {
 }
 
 /// Descriptor of a K-major tile whose rows hold BK bf16 (64: 128-byte swizzle,
-/// 32: 64-byte swizzle).
+/// 32: 64-byte swizzle; 128: two 128-byte-swizzled 64-column sub-tiles one after
+/// the other, the descriptor of the first).
 template <int BK>
 KIWI_DEV uint64_t kmajor_desc(const void* smem_tile) {
-    static_assert(BK == 64 || BK == 32, "BK must be 64 or 32");
-    if constexpr (BK == 64) return sw128_kmajor_desc(smem_tile);
-    else return sw64_kmajor_desc(smem_tile);
+    static_assert(BK == 128 || BK == 64 || BK == 32, "BK must be 128, 64 or 32");
+    if constexpr (BK == 32) return sw64_kmajor_desc(smem_tile);
+    else return sw128_kmajor_desc(smem_tile);  // 128: the first of two 64-column sub-tiles
 }
 
 /// Instruction descriptor, kind::f16 with BF16 A/B, FP32 accumulate, both K-major.
