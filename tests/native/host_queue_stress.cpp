@@ -1,5 +1,6 @@
-// Host-side race check of kiwi::queue and kiwi::invoke, compiled with
-// -fsanitize=thread by tests/test_tsan_host.py (CPU only, no GPU).
+// Host-side stress of kiwi::queue and kiwi::invoke, compiled with
+// -fsanitize=thread and with -fsanitize=address,undefined by
+// tests/test_sanitizers_host.py (CPU only, no GPU).
 //
 // Each case runs real producer and consumer threads over the host-only rings
 // (plain memory instead of mapped pinned memory, same code paths):
@@ -9,8 +10,10 @@
 //               device consumer that publishes its position;
 //   mpmc_push - four threads claim slots of one MPMC H2D ring concurrently;
 //   invoke    - four producer threads (one per endpoint) feed an invoke
-//               Context served by two progress threads, then stop() drains.
-// Exit status 0 and no ThreadSanitizer report mean the case passed.
+//               Context served by two progress threads, then stop() drains;
+//   print     - the native print formatter over many formats and payloads,
+//               from two threads at once (buffer and integer handling).
+// Exit status 0 and no sanitizer report mean the case passed.
 #include <atomic>
 #include <chrono>
 #include <cstdio>
@@ -19,6 +22,7 @@
 #include <vector>
 
 #include "kiwi/invoke/invoke.hpp"
+#include "kiwi/invoke/printer.hpp"
 #include "kiwi/invoke/progress.hpp"
 #include "kiwi/queue/queue.hpp"
 
@@ -153,13 +157,46 @@ int invoke_threads() {
     return 0;
 }
 
+int print_formats() {
+    struct F {
+        const char* fmt;
+        const char* codes;
+    } formats[] = {{"step=%d value=%.2f tag=0x%llx", "ifQ"}, {"%-12u|%+08.3e|%c", "IdB"},
+                   {"%llu %lld %x %o", "QqHb"}, {"%%%5.1g%% of %hhd", "fb"}, {"plain text", ""},
+                   {"%300.200f", "d"}};
+    std::atomic<int> bad{0};
+    auto work = [&](uint64_t seed) {
+        uint8_t payload[64];
+        for (int it = 0; it < 2000; ++it) {
+            for (const auto& f : formats) {
+                kiwi::invoke::PrintFormat pf(f.fmt, f.codes);
+                for (uint32_t i = 0; i < pf.payload_bytes(); ++i) {
+                    seed = seed * 6364136223846793005ull + 1442695040888963407ull;
+                    payload[i] = static_cast<uint8_t>(seed >> 56);
+                }
+                if (pf.payload_bytes() >= 8 && std::strcmp(f.codes, "d") == 0) {
+                    const double v = 1e300;  // the widest %f output
+                    std::memcpy(payload, &v, 8);
+                }
+                const std::string out = pf.format(payload, pf.payload_bytes());
+                if (out.size() > 4096) bad.store(1);
+            }
+        }
+    };
+    std::thread t1(work, 1), t2(work, 2);
+    t1.join();
+    t2.join();
+    return bad.load() ? fail("print length", 1, 0) : 0;
+}
+
 }  // namespace
 
 int main(int argc, char** argv) {
     struct Case {
         const char* name;
         int (*fn)();
-    } cases[] = {{"spsc_d2h", spsc_d2h}, {"spsc_h2d", spsc_h2d}, {"mpmc_push", mpmc_push}, {"invoke", invoke_threads}};
+    } cases[] = {{"spsc_d2h", spsc_d2h}, {"spsc_h2d", spsc_h2d}, {"mpmc_push", mpmc_push}, {"invoke", invoke_threads},
+                 {"print", print_formats}};
     int rc = 0;
     for (const auto& c : cases) {
         if (argc > 1 && std::strcmp(argv[1], c.name) != 0) continue;
