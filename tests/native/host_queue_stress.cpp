@@ -12,7 +12,10 @@
 //   invoke    - four producer threads (one per endpoint) feed an invoke
 //               Context served by two progress threads, then stop() drains;
 //   print     - the native print formatter over many formats and payloads,
-//               from two threads at once (buffer and integer handling).
+//               from two threads at once (buffer and integer handling);
+//   fds       - four "ranks" (threads) exchange pipe descriptors with
+//               SCM_RIGHTS over abstract sockets, then a broadcast; every
+//               received descriptor must reach its sender's pipe.
 // Exit status 0 and no sanitizer report mean the case passed.
 #include <atomic>
 #include <chrono>
@@ -24,7 +27,10 @@
 #include "kiwi/invoke/invoke.hpp"
 #include "kiwi/invoke/printer.hpp"
 #include "kiwi/invoke/progress.hpp"
+#include "kiwi/p2p/heap.hpp"
 #include "kiwi/queue/queue.hpp"
+
+#include <unistd.h>
 
 using namespace kiwi;
 using namespace kiwi::queue;
@@ -189,6 +195,70 @@ int print_formats() {
     return bad.load() ? fail("print length", 1, 0) : 0;
 }
 
+int fd_exchange() {
+    const int world = 4;
+    int pipes[world][2];
+    for (auto& p : pipes) {
+        if (pipe(p) != 0) return fail("pipe", 0, 0);
+    }
+    const std::string job = "stress" + std::to_string(getpid());
+    std::vector<std::vector<int>> got(world);
+    std::vector<int> bcast(world, -1);
+    std::atomic<int> bad{0};
+    std::vector<std::thread> ts;
+    for (int r = 0; r < world; ++r) {
+        ts.emplace_back([&, r] {
+            try {
+                got[r] = kiwi::p2p::exchange_fds(job, r, world, pipes[r][1], 20.0);
+                bcast[r] = kiwi::p2p::broadcast_fd(job + "b", r, world, 0, r == 0 ? pipes[0][1] : -1, 20.0);
+            } catch (const std::exception& e) {
+                std::fprintf(stderr, "rank %d: %s\n", r, e.what());
+                bad.store(1);
+            }
+        });
+    }
+    for (auto& t : ts) t.join();
+    if (bad.load()) return fail("fd exchange threw", 1, 0);
+    // rank r writes (r, q) through its copy of q's descriptor; q's pipe must hold it.
+    for (int r = 0; r < world; ++r) {
+        if (static_cast<int>(got[r].size()) != world) return fail("fd count", static_cast<long>(got[r].size()), world);
+        for (int q = 0; q < world; ++q) {
+            const uint8_t msg[2] = {static_cast<uint8_t>(r), static_cast<uint8_t>(q)};
+            if (write(got[r][q], msg, 2) != 2) return fail("write", r, q);
+        }
+    }
+    for (int q = 0; q < world; ++q) {
+        uint8_t buf[2 * world];
+        ssize_t n = 0;
+        while (n < 2 * world) {
+            const ssize_t k = read(pipes[q][0], buf + n, sizeof(buf) - n);
+            if (k <= 0) return fail("read", q, static_cast<long>(k));
+            n += k;
+        }
+        for (int i = 0; i < world; ++i) {
+            if (buf[2 * i + 1] != q) return fail("fd routed to the wrong pipe", buf[2 * i + 1], q);
+        }
+    }
+    for (int r = 0; r < world; ++r) {
+        const uint8_t m = 0xB0;
+        if (write(bcast[r], &m, 1) != 1) return fail("broadcast write", r, 0);
+    }
+    uint8_t b[world];
+    ssize_t n = 0;
+    while (n < world) {
+        const ssize_t k = read(pipes[0][0], b + n, sizeof(b) - n);
+        if (k <= 0) return fail("broadcast read", static_cast<long>(k), 0);
+        n += k;
+    }
+    for (int r = 0; r < world; ++r) {
+        for (int q = 0; q < world; ++q) close(got[r][q]);
+        close(bcast[r]);
+        close(pipes[r][0]);
+        close(pipes[r][1]);
+    }
+    return 0;
+}
+
 }  // namespace
 
 int main(int argc, char** argv) {
@@ -196,7 +266,7 @@ int main(int argc, char** argv) {
         const char* name;
         int (*fn)();
     } cases[] = {{"spsc_d2h", spsc_d2h}, {"spsc_h2d", spsc_h2d}, {"mpmc_push", mpmc_push}, {"invoke", invoke_threads},
-                 {"print", print_formats}};
+                 {"print", print_formats}, {"fds", fd_exchange}};
     int rc = 0;
     for (const auto& c : cases) {
         if (argc > 1 && std::strcmp(argv[1], c.name) != 0) continue;

@@ -4,7 +4,8 @@ Builds tests/native/host_queue_stress.cpp twice, with -fsanitize=thread and
 with -fsanitize=address,undefined, and runs each case (SPSC D2H with
 wrap-around and back-pressure, SPSC H2D with a CPU stand-in consumer,
 concurrent MPMC producers, an invoke Context served by progress threads while
-four producers push, the native print formatter from two threads).  Ring words
+four producers push, the native print formatter from two threads, descriptor
+exchange between four thread "ranks").  Ring words
 are atomic accesses and the writer's release fence is not modelled by TSan
 (-Wno-tsan); what TSan checks is every other piece of shared state: cursors,
 positions, registries, counters, thread start/stop.  ASan / UBSan check every
@@ -18,7 +19,7 @@ import pytest
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 CUDA = os.environ.get("CUDA_HOME", "/usr/local/cuda")
-CASES = ["spsc_d2h", "spsc_h2d", "mpmc_push", "invoke", "print"]
+CASES = ["spsc_d2h", "spsc_h2d", "mpmc_push", "invoke", "print", "fds"]
 SANITIZERS = {"thread": ["-fsanitize=thread", "-Wno-tsan"],
               "address,undefined": ["-fsanitize=address,undefined", "-fno-omit-frame-pointer",
                                     "-fno-sanitize-recover=undefined"]}
@@ -32,6 +33,7 @@ def _build(tmp_path_factory, name):
     cmd = [cxx, "-std=c++17", "-O1", "-g", *SANITIZERS[name], "-I" + os.path.join(ROOT, "include"),
            "-I" + os.path.join(CUDA, "include"), os.path.join(ROOT, "tests/native/host_queue_stress.cpp"),
            os.path.join(ROOT, "src/queue/host_memory.cpp"), os.path.join(ROOT, "src/common/topology.cpp"),
+           os.path.join(ROOT, "src/p2p/fd_exchange.cpp"),
            "-L" + os.path.join(CUDA, "lib64"), "-lcudart", "-lpthread", "-o", out]
     r = subprocess.run(cmd, capture_output=True, text=True, timeout=300)
     if r.returncode != 0 and "cannot find" in r.stderr.lower() and "san" in r.stderr.lower():
