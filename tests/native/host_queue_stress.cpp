@@ -13,6 +13,10 @@
 //               Context served by two progress threads, then stop() drains;
 //   print     - the native print formatter over many formats and payloads,
 //               from two threads at once (buffer and integer handling);
+//   fuzz      - the host reader over random ring contents in which about
+//               half the words carry the right lap tag: every pop returns,
+//               consumes a whole message or throws queue_error, and never
+//               reads outside the ring (ASan) or its output buffer;
 //   fds       - four "ranks" (threads) exchange pipe descriptors with
 //               SCM_RIGHTS over abstract sockets, then a broadcast; every
 //               received descriptor must reach its sender's pipe.
@@ -195,6 +199,59 @@ int print_formats() {
     return bad.load() ? fail("print length", 1, 0) : 0;
 }
 
+int fuzz_reader() {
+    uint64_t seed = 0x2545F4914F6CDD1Dull;
+    auto rnd = [&] {
+        seed ^= seed << 13;
+        seed ^= seed >> 7;
+        seed ^= seed << 17;
+        return seed;
+    };
+    uint64_t pops = 0, errors = 0;
+    for (int round = 0; round < 4000; ++round) {
+        const uint64_t cap = 1ull << (rnd() % 8);  // 1 .. 128 lines
+        SPSCD2HQueue q(cap, MemKind::kHost);
+        Chunk* ring = q.ring_host();
+        const uint32_t log2cap = static_cast<uint32_t>(__builtin_ctzll(cap));
+        for (uint64_t line = 0; line < cap; ++line) {
+            const uint32_t tag = lap_tag(line, log2cap);
+            for (uint32_t c = 0; c < kChunksPerLine; ++c) {
+                uint32_t w[4];
+                if (c == 0 && (rnd() & 1)) {
+                    // a well-formed header: metadata and a length, half of them short,
+                    // the rest up to 1.2x the maximum
+                    const uint32_t len = (rnd() & 1) ? static_cast<uint32_t>(rnd() % 64)
+                                                     : static_cast<uint32_t>(rnd() % (kMaxMessageBytes + kMaxMessageBytes / 5));
+                    const uint64_t h0 = pack_half(static_cast<uint32_t>(rnd()), tag), h1 = pack_half(len, tag);
+                    std::memcpy(w, &h0, 8);
+                    std::memcpy(w + 2, &h1, 8);
+                } else {
+                    for (auto& x : w) {
+                        const uint32_t data = static_cast<uint32_t>(rnd());
+                        x = (rnd() % 10) ? tagged_word(data, tag) : static_cast<uint32_t>(rnd());
+                    }
+                }
+                std::memcpy(&ring[line * kChunksPerLine + c], w, sizeof(w));
+            }
+        }
+        alignas(16) uint8_t out[kMaxMessageBytes + 64];
+        for (int k = 0; k < 64; ++k) {
+            uint32_t meta = 0, bytes = 0;
+            try {
+                if (!q.try_pop(out, &meta, &bytes)) break;
+                if (bytes > kMaxMessageBytes) return fail("fuzz length", bytes, kMaxMessageBytes);
+                ++pops;
+            } catch (const queue_error&) {
+                ++errors;
+                break;
+            }
+        }
+    }
+    std::printf("fuzz: %llu pops, %llu rejected rings\n", static_cast<unsigned long long>(pops),
+                static_cast<unsigned long long>(errors));
+    return 0;
+}
+
 int fd_exchange() {
     const int world = 4;
     int pipes[world][2];
@@ -266,7 +323,7 @@ int main(int argc, char** argv) {
         const char* name;
         int (*fn)();
     } cases[] = {{"spsc_d2h", spsc_d2h}, {"spsc_h2d", spsc_h2d}, {"mpmc_push", mpmc_push}, {"invoke", invoke_threads},
-                 {"print", print_formats}, {"fds", fd_exchange}};
+                 {"print", print_formats}, {"fuzz", fuzz_reader}, {"fds", fd_exchange}};
     int rc = 0;
     for (const auto& c : cases) {
         if (argc > 1 && std::strcmp(argv[1], c.name) != 0) continue;
