@@ -17,6 +17,10 @@
 //               half the words carry the right lap tag: every pop returns,
 //               consumes a whole message or throws queue_error, and never
 //               reads outside the ring (ASan) or its output buffer;
+//   fuzz_invoke - random callback ids (some unregistered) and payload sizes
+//               (mostly wrong) through an invoke Context: every message
+//               either runs its callback or raises invoke_error once, and
+//               progress continues after each error;
 //   fds       - four "ranks" (threads) exchange pipe descriptors with
 //               SCM_RIGHTS over abstract sockets, then a broadcast; every
 //               received descriptor must reach its sender's pipe.
@@ -252,6 +256,48 @@ int fuzz_reader() {
     return 0;
 }
 
+int fuzz_invoke() {
+    invoke::Context<SPSCD2HQueue> ctx(1, 64, MemKind::kHost);
+    std::atomic<uint64_t> called{0};
+    ctx.register_callback(std::function<void(uint32_t)>([&](uint32_t) { called.fetch_add(1); }));
+    ctx.register_callback(std::function<void(uint64_t, float, uint8_t)>(
+        [&](uint64_t, float, uint8_t) { called.fetch_add(1); }));
+    ctx.register_raw_callback([&](const uint8_t*, uint32_t) { called.fetch_add(1); },
+                              invoke::CallbackBase::kAnySize);
+    RingWriter w = ctx.raw_queue(0)->host_writer_any();
+    uint64_t seed = 88172645463325252ull, errors = 0, sent = 0;
+    auto rnd = [&] {
+        seed ^= seed << 13;
+        seed ^= seed >> 7;
+        seed ^= seed << 17;
+        return seed;
+    };
+    auto drain_once = [&]() -> size_t {
+        try {
+            return ctx.progress(0);
+        } catch (const std::exception&) {
+            ++errors;
+            return 1;
+        }
+    };
+    uint8_t payload[128];
+    for (int i = 0; i < 20000; ++i) {
+        for (auto& b : payload) b = static_cast<uint8_t>(rnd());
+        const uint32_t bytes = static_cast<uint32_t>(rnd() % 97);
+        const uint32_t meta = static_cast<uint32_t>(rnd() % 6);  // ids 3..5 are not registered
+        while (!w.try_push(payload, bytes, meta)) drain_once();
+        ++sent;
+    }
+    while (drain_once() != 0) {
+    }
+    if (called.load() + errors != sent) {
+        return fail("invoke fuzz accounting", static_cast<long>(called.load() + errors), static_cast<long>(sent));
+    }
+    std::printf("fuzz_invoke: %llu calls, %llu rejected\n", static_cast<unsigned long long>(called.load()),
+                static_cast<unsigned long long>(errors));
+    return 0;
+}
+
 int fd_exchange() {
     const int world = 4;
     int pipes[world][2];
@@ -323,7 +369,8 @@ int main(int argc, char** argv) {
         const char* name;
         int (*fn)();
     } cases[] = {{"spsc_d2h", spsc_d2h}, {"spsc_h2d", spsc_h2d}, {"mpmc_push", mpmc_push}, {"invoke", invoke_threads},
-                 {"print", print_formats}, {"fuzz", fuzz_reader}, {"fds", fd_exchange}};
+                 {"print", print_formats}, {"fuzz", fuzz_reader}, {"fuzz_invoke", fuzz_invoke},
+                 {"fds", fd_exchange}};
     int rc = 0;
     for (const auto& c : cases) {
         if (argc > 1 && std::strcmp(argv[1], c.name) != 0) continue;

@@ -5,8 +5,8 @@ with -fsanitize=address,undefined, and runs each case (SPSC D2H with
 wrap-around and back-pressure, SPSC H2D with a CPU stand-in consumer,
 concurrent MPMC producers, an invoke Context served by progress threads while
 four producers push, the native print formatter from two threads, the host
-reader over random ring contents, descriptor exchange between four thread
-"ranks").  Ring words
+reader over random ring contents, random callback ids and sizes through the
+dispatcher, descriptor exchange between four thread "ranks").  Ring words
 are atomic accesses and the writer's release fence is not modelled by TSan
 (-Wno-tsan); what TSan checks is every other piece of shared state: cursors,
 positions, registries, counters, thread start/stop.  ASan / UBSan check every
@@ -20,7 +20,7 @@ import pytest
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 CUDA = os.environ.get("CUDA_HOME", "/usr/local/cuda")
-CASES = ["spsc_d2h", "spsc_h2d", "mpmc_push", "invoke", "print", "fuzz", "fds"]
+CASES = ["spsc_d2h", "spsc_h2d", "mpmc_push", "invoke", "print", "fuzz", "fuzz_invoke", "fds"]
 SANITIZERS = {"thread": ["-fsanitize=thread", "-Wno-tsan"],
               "address,undefined": ["-fsanitize=address,undefined", "-fno-omit-frame-pointer",
                                     "-fno-sanitize-recover=undefined"]}
