@@ -23,3 +23,26 @@ def test_env_cli_writes_json(tmp_path):
     env.main(["--output", str(out)])
     d = json.loads(out.read_text())
     assert d["python"] and "repo" in d
+
+
+def test_installation_check_cli():
+    """python -m kiwi_b200: the extension loads; without a GPU, --smoke reports
+    itself skipped and exits non-zero instead of pretending to pass."""
+    import os
+    import subprocess
+    import sys
+
+    import torch
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    r = subprocess.run([sys.executable, "-m", "kiwi_b200", "--json"], capture_output=True, text=True, timeout=300,
+                       cwd=root)
+    assert r.returncode == 0, r.stderr[-2000:]
+    d = json.loads(r.stdout)
+    assert d["extension"]["loaded"] and d["ok"]
+    if not torch.cuda.is_available():
+        assert d["gpus"] == []
+        r = subprocess.run([sys.executable, "-m", "kiwi_b200", "--smoke", "--json"], capture_output=True, text=True,
+                           timeout=300, cwd=root)
+        assert r.returncode == 1
+        assert "skipped" in json.loads(r.stdout)["smoke"]
