@@ -1,13 +1,17 @@
 """A user CUDA kernel calls Python from the GPU through kiwi_b200.invoke.
 
-    python examples/python/invoke_from_kernel.py
+    python examples/python/invoke_from_kernel.py [--fast-build]
 
 Each block of the kernel reports (block id, reading) to a Python callback
 through its own invoke endpoint while it runs; a native progress thread pinned
 near the GPU dispatches the messages.  (Reference counterpart:
 examples/invoke/invoke_example.hip.cpp and the Triton/FlyDSL print examples of
-AMDResearch/kiwi.)
+AMDResearch/kiwi.)  ``--fast-build`` compiles the kernel with nvcc alone and
+loads it with ctypes (``kiwi_b200.utils.build.load_cuda``) instead of building a
+PyTorch extension, which takes seconds instead of about a minute.
 """
+import argparse
+import ctypes
 import os
 import sys
 import threading
@@ -16,7 +20,7 @@ sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspa
 import torch  # noqa: E402
 
 from kiwi_b200 import invoke  # noqa: E402
-from kiwi_b200.utils.build import load_inline  # noqa: E402
+from kiwi_b200.utils.build import load_cuda, load_inline  # noqa: E402
 
 CUDA = r"""
 #include <cstdint>
@@ -38,12 +42,27 @@ void run_sensors(int64_t ctx_ptr, int64_t cb, int64_t blocks, int64_t readings) 
     sensor_kernel<<<blocks, 32>>>(reinterpret_cast<Ctx*>(ctx_ptr), static_cast<uint8_t>(cb),
                                   static_cast<int>(readings));
 }
+
+// The same entry point with C linkage, for the ctypes build.
+extern "C" void kiwi_run_sensors(int64_t ctx_ptr, int64_t cb, int64_t blocks, int64_t readings) {
+    run_sensors(ctx_ptr, cb, blocks, readings);
+}
 """
 CPP = "void run_sensors(int64_t ctx_ptr, int64_t cb, int64_t blocks, int64_t readings);"
 
 
-def main(blocks=4, readings=8):
-    mod = load_inline("kiwi_example_sensors", [CUDA], ["run_sensors"], cpp_sources=[CPP])
+def build(fast=False):
+    """A callable run_sensors(ctx_ptr, cb, blocks, readings)."""
+    if fast:
+        lib = load_cuda("kiwi_example_sensors_c", CUDA)
+        lib.kiwi_run_sensors.argtypes = [ctypes.c_int64] * 4
+        lib.kiwi_run_sensors.restype = None
+        return lib.kiwi_run_sensors
+    return load_inline("kiwi_example_sensors", [CUDA], ["run_sensors"], cpp_sources=[CPP]).run_sensors
+
+
+def main(blocks=4, readings=8, fast=False):
+    run_sensors = build(fast)
     ctx = invoke.Context(num_endpoints=blocks, capacity=256)
     got = []
     lock = threading.Lock()
@@ -54,7 +73,7 @@ def main(blocks=4, readings=8):
 
     cb = ctx.register_callback(on_reading, "<If")
     ctx.start(num_threads=1)
-    mod.run_sensors(ctx.device_context_ptr, cb, blocks, readings)
+    run_sensors(ctx.device_context_ptr, cb, blocks, readings)
     torch.cuda.synchronize()
     ctx.stop()
     ctx.check_device_errors()
@@ -62,5 +81,7 @@ def main(blocks=4, readings=8):
 
 
 if __name__ == "__main__":
-    readings = main()
+    ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    ap.add_argument("--fast-build", action="store_true", help="nvcc + ctypes instead of a PyTorch extension")
+    readings = main(fast=ap.parse_args().fast_build)
     print(f"{len(readings)} readings from the GPU, e.g. {sorted(readings)[:3]}")

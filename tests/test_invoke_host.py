@@ -180,3 +180,29 @@ def test_native_print_callback_prints_each_invoke(capfd):
                         "[kernel] step=2 value=1.00 tag=0xc0ffee02"]
     with pytest.raises(Exception):
         ctx.register_native_print("%s", "<i")
+
+
+def test_load_cuda_builds_and_caches_a_kiwi_kernel_library(tmp_path):
+    """kiwi_b200.utils.build.load_cuda: nvcc-only build of a source that uses
+    the kiwi headers, loaded with ctypes (no GPU needed to build or call a host
+    function); an unchanged source is not rebuilt."""
+    import ctypes
+
+    from kiwi_b200.utils.build import load_cuda
+
+    src = r"""
+#include <cstdint>
+#include <kiwi/queue/wire.hpp>
+__global__ void never_launched(uint32_t* out) { out[0] = kiwi::queue::wire_tag(threadIdx.x); }
+extern "C" uint32_t kiwi_jit_tag(uint64_t n) { return kiwi::queue::wire_tag(n); }
+"""
+    lib = load_cuda("kiwi_jit_test", src, build_directory=str(tmp_path))
+    lib.kiwi_jit_tag.argtypes = [ctypes.c_uint64]
+    lib.kiwi_jit_tag.restype = ctypes.c_uint32
+    assert lib.kiwi_jit_tag(0) == 1 and lib.kiwi_jit_tag(65535) == 1 and lib.kiwi_jit_tag(65534) == 65535
+    so = tmp_path / "libkiwi_jit_test.so"
+    mtime = so.stat().st_mtime_ns
+    load_cuda("kiwi_jit_test", src, build_directory=str(tmp_path))
+    assert so.stat().st_mtime_ns == mtime  # cached
+    with pytest.raises(RuntimeError, match="nvcc failed"):
+        load_cuda("kiwi_jit_bad", "this is not C++", build_directory=str(tmp_path / "bad"))
