@@ -279,6 +279,15 @@ PYBIND11_MODULE(_C, m) {
                  return s.try_push(b.data(), static_cast<uint32_t>(b.size()), meta);
              },
              py::arg("payload"), py::arg("metadata") = 0)
+        .def(
+            "host_try_pop",
+            [](queue::MPMCH2DQueue& s) -> py::object {
+                uint8_t buf[queue::kMaxMessageBytes];
+                uint32_t meta = 0, bytes = 0;
+                if (!s.host_try_pop(buf, &meta, &bytes)) return py::none();
+                return py::make_tuple(py::bytes(reinterpret_cast<const char*>(buf), bytes), meta);
+            },
+            "CPU stand-in for the device consumers (host_only queues): (payload, metadata) or None.")
         .def_property_readonly("slot_payload_bytes", &queue::MPMCH2DQueue::slot_payload_bytes)
         .def_property_readonly("producer_position", &queue::MPMCH2DQueue::producer_position);
 

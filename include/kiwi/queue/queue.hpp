@@ -241,6 +241,52 @@ public:
         }
     }
 
+    /// CPU stand-in for the device consumers (host-only queues: tests and
+    /// host-side stress).  The same protocol as MpmcH2DHandle::try_pop: read
+    /// the claimed position's slot, check every word's lap tag, take the slot
+    /// with a CAS on the claim counter, copy the payload, then ack the slot so
+    /// producers can reuse it.  Thread-safe; false when the next slot is empty
+    /// or another consumer took it first.
+    bool host_try_pop(void* out, uint32_t* metadata, uint32_t* bytes) {
+        if (ring_.kind != MemKind::kHost) throw kiwi::error("host_try_pop needs a host-only (MemKind::kHost) queue");
+        auto* claim = claim_.as<unsigned long long>();
+        const uint64_t pos = __atomic_load_n(claim, __ATOMIC_ACQUIRE);
+        const uint64_t slot = pos & (slots_ - 1);
+        const uint32_t lap = static_cast<uint32_t>(pos >> log2_);
+        const uint32_t tag = wire_tag(lap);
+        const uint32_t total = slot_lines_ * kChunksPerLine;
+        const Chunk* base = ring_.as<Chunk>() + slot * total;
+        uint32_t lo[kChunksPerLine * 8], hi[kChunksPerLine * 8];
+        for (uint32_t k = 0; k < total; ++k) {
+            const uint64_t a = host::load_half(&base[k].lo);
+            const uint64_t b = host::load_half(&base[k].hi);
+            if (!half_has_tag(a, tag) || !half_has_tag(b, tag)) return false;
+            lo[k] = half_data(a);
+            hi[k] = half_data(b);
+        }
+        unsigned long long expect = pos;
+        if (!__atomic_compare_exchange_n(claim, &expect, pos + 1, false, __ATOMIC_ACQ_REL, __ATOMIC_RELAXED)) {
+            return false;
+        }
+        const uint32_t len = hi[0];
+        if (metadata) *metadata = lo[0];
+        if (len > slot_payload_bytes()) {
+            __atomic_store_n(&acks_.as<uint32_t>()[slot], lap + 1, __ATOMIC_RELEASE);
+            throw queue_error("kiwi::queue: MPMC slot holds a length of " + std::to_string(len) + " bytes");
+        }
+        uint8_t* dst = static_cast<uint8_t*>(out);
+        for (uint32_t k = 1; 8 * (k - 1) < len; ++k) {
+            uint8_t w[8];
+            std::memcpy(w, &lo[k], 4);
+            std::memcpy(w + 4, &hi[k], 4);
+            const uint32_t off = 8 * (k - 1);
+            std::memcpy(dst + off, w, len - off < 8 ? len - off : 8);
+        }
+        if (bytes) *bytes = len;
+        __atomic_store_n(&acks_.as<uint32_t>()[slot], lap + 1, __ATOMIC_RELEASE);
+        return true;
+    }
+
     uint64_t slots() const { return slots_; }
     uint64_t producer_position() const { return __atomic_load_n(&head_, __ATOMIC_RELAXED); }
     ErrorRecord error() const { return *err_.as<ErrorRecord>(); }

@@ -9,6 +9,9 @@
 //   spsc_h2d  - the host producer of an H2D ring and a CPU stand-in for the
 //               device consumer that publishes its position;
 //   mpmc_push - four threads claim slots of one MPMC H2D ring concurrently;
+//   mpmc      - three producers and two CPU stand-in consumers (the device
+//               consumers' claim / tag / ack protocol) through a 16-slot MPMC
+//               ring: every message arrives exactly once, payload intact;
 //   invoke    - four producer threads (one per endpoint) feed an invoke
 //               Context served by two progress threads, then stop() drains;
 //   print     - the native print formatter over many formats and payloads,
@@ -25,6 +28,7 @@
 //               SCM_RIGHTS over abstract sockets, then a broadcast; every
 //               received descriptor must reach its sender's pipe.
 // Exit status 0 and no sanitizer report mean the case passed.
+#include <algorithm>
 #include <atomic>
 #include <chrono>
 #include <cstdio>
@@ -131,6 +135,58 @@ int mpmc_push() {
     // 64 free slots, 64 attempts: every push lands in its own slot.
     if (pushed.load() != 64) return fail("mpmc_push count", pushed.load(), 64);
     if (q.producer_position() != 64) return fail("mpmc_push head", static_cast<long>(q.producer_position()), 64);
+    return 0;
+}
+
+int mpmc_full() {
+    MPMCH2DQueue q(16, 2, MemKind::kHost);
+    const uint32_t producers = 3, per = 4000, total = producers * per;
+    std::atomic<uint32_t> got{0};
+    std::atomic<int> bad{0};
+    std::vector<std::vector<uint64_t>> seen(2);
+    std::vector<std::thread> ts;
+    for (uint32_t p = 0; p < producers; ++p) {
+        ts.emplace_back([&, p] {
+            uint8_t msg[56];
+            for (uint32_t i = 0; i < per; ++i) {
+                const uint32_t bytes = 8 + (i * 7 + p) % 49;  // 8 .. 56
+                std::memcpy(msg, &p, 4);
+                std::memcpy(msg + 4, &i, 4);
+                fill(msg + 8, bytes - 8, p * per + i);
+                while (!q.try_push(msg, bytes, p)) std::this_thread::yield();
+            }
+        });
+    }
+    for (int c = 0; c < 2; ++c) {
+        ts.emplace_back([&, c] {
+            uint8_t buf[64];
+            while (got.load() < total) {
+                uint32_t meta = 0, bytes = 0;
+                if (!q.host_try_pop(buf, &meta, &bytes)) {
+                    std::this_thread::yield();
+                    continue;
+                }
+                got.fetch_add(1);
+                uint32_t p, i;
+                std::memcpy(&p, buf, 4);
+                std::memcpy(&i, buf + 4, 4);
+                if (p != meta || p >= producers || i >= per || bytes != 8 + (i * 7 + p) % 49 ||
+                    !check(buf + 8, bytes - 8, p * per + i)) {
+                    bad.store(1);
+                }
+                seen[c].push_back(static_cast<uint64_t>(p) * per + i);
+            }
+        });
+    }
+    for (auto& t : ts) t.join();
+    if (bad.load()) return fail("mpmc payload", 1, 0);
+    std::vector<uint64_t> all(seen[0]);
+    all.insert(all.end(), seen[1].begin(), seen[1].end());
+    std::sort(all.begin(), all.end());
+    if (all.size() != total) return fail("mpmc count", static_cast<long>(all.size()), total);
+    for (uint32_t k = 0; k < total; ++k) {
+        if (all[k] != k) return fail("mpmc exactly once", static_cast<long>(all[k]), k);
+    }
     return 0;
 }
 
@@ -368,7 +424,8 @@ int main(int argc, char** argv) {
     struct Case {
         const char* name;
         int (*fn)();
-    } cases[] = {{"spsc_d2h", spsc_d2h}, {"spsc_h2d", spsc_h2d}, {"mpmc_push", mpmc_push}, {"invoke", invoke_threads},
+    } cases[] = {{"spsc_d2h", spsc_d2h}, {"spsc_h2d", spsc_h2d}, {"mpmc_push", mpmc_push}, {"mpmc", mpmc_full},
+                 {"invoke", invoke_threads},
                  {"print", print_formats}, {"fuzz", fuzz_reader}, {"fuzz_invoke", fuzz_invoke},
                  {"fds", fd_exchange}};
     int rc = 0;

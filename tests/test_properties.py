@@ -184,3 +184,33 @@ def test_debug_words_decode_inverts_the_device_encoding(times):
     raw[0] = 0
     got = load().ep.decode_debug_words(raw)
     assert got[0] == 0 and got[1:] == times[1:]
+
+
+@settings(max_examples=int(os.environ.get("KIWI_PROPERTY_EXAMPLES", "200")), deadline=None)
+@given(st.integers(0, 4), st.integers(1, 3), st.lists(st.one_of(st.binary(max_size=56), st.none()), max_size=120))
+def test_mpmc_h2d_fifo_and_full_with_stand_in_consumer(log2slots, slot_lines, ops):
+    """MPMC host-to-device queue against a deque model, with the CPU stand-in
+    for the device consumers: bytes = push (False exactly when every slot
+    holds an unconsumed message), None = pop (FIFO; None when empty)."""
+    import collections
+
+    slots = 1 << log2slots
+    q = kq.MPMCH2DQueue(slots, slot_lines, host_only=True)
+    payload_max = q.slot_payload_bytes
+    model = collections.deque()
+    for i, op in enumerate(ops):
+        if op is None:
+            got = q.host_try_pop()
+            if model:
+                assert got == model.popleft()
+            else:
+                assert got is None
+        else:
+            data = op[:payload_max]
+            ok = q.try_push(data, i % 251)
+            assert ok == (len(model) < slots)
+            if ok:
+                model.append((data, i % 251))
+    while model:
+        assert q.host_try_pop() == model.popleft()
+    assert q.host_try_pop() is None
