@@ -159,7 +159,10 @@ private:
     uint64_t* published_ = nullptr;
 };
 
-/// Host producer.  Credit comes from the consumer's published position.
+/// Host producer.  Credit comes from the consumer's published position.  A
+/// writer starts with credit for `capacity` lines from `start`, i.e. it assumes
+/// the consumer is at `start`; a producer that begins elsewhere checks the
+/// consumer's position first (MPSCD2HQueue::host_push).
 class RingWriter {
 public:
     RingWriter() = default;

@@ -9,6 +9,8 @@
 // Capacities are in 64-byte lines (slots for MPMC) and must be powers of two.
 #pragma once
 
+#include <chrono>
+
 #include <memory>
 #include <mutex>
 
@@ -134,6 +136,32 @@ public:
         h.timeout_ns = timeout_ns;
         h.log2cap = log2_pow2(capacity_);
         return h;
+    }
+
+    /// CPU stand-in for the device producers (host-only queues: tests and
+    /// host-side stress).  The same protocol as MpscD2HHandle: claim the
+    /// message's lines with a fetch-add on the producer counter, wait for the
+    /// consumer's credit, then write the message there (header last).
+    /// Thread-safe.  A claimed range must be written or the consumer stalls at
+    /// it, so a credit wait that runs out throws instead of returning.
+    void host_push(const void* payload, uint32_t bytes, uint32_t metadata, double timeout_s = 10.0) {
+        if (ring_.kind != MemKind::kHost) throw kiwi::error("host_push needs a host-only (MemKind::kHost) queue");
+        if (bytes > kMaxMessageBytes || message_lines(bytes) > capacity_) {
+            throw kiwi::error("kiwi::queue: host_push of " + std::to_string(bytes) + " bytes does not fit");
+        }
+        const uint32_t nlines = message_lines(bytes);
+        const uint64_t base = __atomic_fetch_add(claim_.as<unsigned long long>(), nlines, __ATOMIC_RELAXED);
+        // Credit from the consumer's published position (a writer constructed at
+        // `base` would assume the ring is empty there).
+        const auto deadline = std::chrono::steady_clock::now() + std::chrono::duration<double>(timeout_s);
+        while (base + nlines > consumer_position() + capacity_) {
+            if (std::chrono::steady_clock::now() > deadline) {
+                throw kiwi::error("kiwi::queue: host_push waited too long for consumer credit");
+            }
+            host::cpu_relax();
+        }
+        RingWriter w(ring_.as<Chunk>(), capacity_, pos_.as<const uint64_t>(), base);
+        if (!w.try_push(payload, bytes, metadata)) throw kiwi::error("kiwi::queue: host_push lost its credit");
     }
 
 private:

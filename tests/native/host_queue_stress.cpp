@@ -6,6 +6,9 @@
 // (plain memory instead of mapped pinned memory, same code paths):
 //   spsc_d2h  - a producer thread and the consumer over an 8-line ring, so
 //               every message wraps and the producer waits for credit;
+//   mpsc      - four CPU stand-ins for the device producers (fetch-add line
+//               claims, credit waits, out-of-order completion) and the host
+//               consumer: every message once, each producer's in its order;
 //   spsc_h2d  - the host producer of an H2D ring and a CPU stand-in for the
 //               device consumer that publishes its position;
 //   mpmc_push - four threads claim slots of one MPMC H2D ring concurrently;
@@ -90,6 +93,53 @@ int spsc_d2h() {
     }
     producer.join();
     return 0;
+}
+
+int mpsc_d2h() {
+    MPSCD2HQueue q(16, MemKind::kHost);
+    const uint32_t producers = 4, per = 5000, total = producers * per;
+    std::atomic<int> bad{0};
+    std::vector<std::thread> ts;
+    for (uint32_t p = 0; p < producers; ++p) {
+        ts.emplace_back([&, p] {
+            uint8_t msg[kMaxMessageBytes];
+            try {
+                for (uint32_t i = 0; i < per; ++i) {
+                    const uint32_t bytes = 8 + (i * 13 + p * 5) % 200;  // 1 to 4 lines
+                    std::memcpy(msg, &i, 4);
+                    std::memcpy(msg + 4, &p, 4);
+                    fill(msg + 8, bytes - 8, p * per + i);
+                    q.host_push(msg, bytes, p, 60.0);
+                }
+            } catch (const std::exception& e) {
+                std::fprintf(stderr, "producer %u: %s\n", p, e.what());
+                bad.store(1);
+            }
+        });
+    }
+    std::vector<uint32_t> next(producers, 0);
+    alignas(16) uint8_t buf[kMaxMessageBytes];
+    const auto deadline = std::chrono::steady_clock::now() + std::chrono::seconds(120);
+    for (uint32_t got = 0; got < total && !bad.load();) {
+        uint32_t meta = 0, bytes = 0;
+        if (!q.try_pop(buf, &meta, &bytes)) {
+            if (std::chrono::steady_clock::now() > deadline) return fail("mpsc stalled", got, total);
+            std::this_thread::yield();
+            continue;
+        }
+        uint32_t i, p;
+        std::memcpy(&i, buf, 4);
+        std::memcpy(&p, buf + 4, 4);
+        if (p != meta || p >= producers || i != next[p] || bytes != 8 + (i * 13 + p * 5) % 200 ||
+            !check(buf + 8, bytes - 8, p * per + i)) {
+            bad.store(1);
+            break;
+        }
+        ++next[p];
+        ++got;
+    }
+    for (auto& t : ts) t.join();
+    return bad.load() ? fail("mpsc order or payload", 1, 0) : 0;
 }
 
 int spsc_h2d() {
@@ -424,7 +474,7 @@ int main(int argc, char** argv) {
     struct Case {
         const char* name;
         int (*fn)();
-    } cases[] = {{"spsc_d2h", spsc_d2h}, {"spsc_h2d", spsc_h2d}, {"mpmc_push", mpmc_push}, {"mpmc", mpmc_full},
+    } cases[] = {{"spsc_d2h", spsc_d2h}, {"mpsc", mpsc_d2h}, {"spsc_h2d", spsc_h2d}, {"mpmc_push", mpmc_push}, {"mpmc", mpmc_full},
                  {"invoke", invoke_threads},
                  {"print", print_formats}, {"fuzz", fuzz_reader}, {"fuzz_invoke", fuzz_invoke},
                  {"fds", fd_exchange}};

@@ -2,7 +2,8 @@
 
 Builds tests/native/host_queue_stress.cpp twice, with -fsanitize=thread and
 with -fsanitize=address,undefined, and runs each case (SPSC D2H with
-wrap-around and back-pressure, SPSC H2D with a CPU stand-in consumer,
+wrap-around and back-pressure, MPSC D2H with four CPU stand-ins for the
+device producers, SPSC H2D with a CPU stand-in consumer,
 concurrent MPMC producers, MPMC producers and CPU stand-in consumers, an invoke Context served by progress threads while
 four producers push, the native print formatter from two threads, the host
 reader over random ring contents, random callback ids and sizes through the
@@ -20,7 +21,7 @@ import pytest
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 CUDA = os.environ.get("CUDA_HOME", "/usr/local/cuda")
-CASES = ["spsc_d2h", "spsc_h2d", "mpmc_push", "mpmc", "invoke", "print", "fuzz", "fuzz_invoke", "fds"]
+CASES = ["spsc_d2h", "mpsc", "spsc_h2d", "mpmc_push", "mpmc", "invoke", "print", "fuzz", "fuzz_invoke", "fds"]
 SANITIZERS = {"thread": ["-fsanitize=thread", "-Wno-tsan"],
               "address,undefined": ["-fsanitize=address,undefined", "-fno-omit-frame-pointer",
                                     "-fno-sanitize-recover=undefined"]}
