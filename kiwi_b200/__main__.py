@@ -16,6 +16,7 @@ import sys
 
 
 def gpu_checks(C):
+    """Per visible GPU: generation, SMs, memory, P2P peers, NVLS support."""
     import torch
 
     out = []
@@ -36,6 +37,7 @@ def gpu_checks(C):
 
 
 def main(argv=None):
+    """Command-line entry; returns the exit status."""
     ap = argparse.ArgumentParser(prog="python -m kiwi_b200", description=__doc__.splitlines()[0])
     ap.add_argument("--smoke", action="store_true", help="run the end-to-end smoke pass on cuda:0")
     ap.add_argument("--json", action="store_true", help="print one JSON document instead of text")

@@ -10,6 +10,7 @@ _C = None
 
 
 def load():
+    """The extension module kiwi_b200._C (imported once; ImportError if not built)."""
     global _C
     if _C is None:
         import torch  # noqa: F401  (loads libc10/libtorch the extension links against)

@@ -24,6 +24,11 @@ FP4_VALUES = torch.tensor([0.0, 0.5, 1.0, 1.5, 2.0, 3.0, 4.0, 6.0])
 
 @dataclass
 class MoEConfig:
+    """Shape of one MoE layer and its synthetic workload: hidden size, expert FFN
+    width, expert count, top-k, tokens per rank, dispatch wire format
+    ("fp8" 1x128 blocks, "nvfp4" 16-element blocks, "none" = bf16), router skew
+    (Zipf exponent; 0 = N(0, 1) logits) and seed.  CONFIGS holds the benchmark
+    configurations."""
     hidden: int = 7168
     ffn: int = 2048
     num_experts: int = 256
@@ -143,6 +148,8 @@ def quant_nvfp4_reference(x, block=16):
 
 
 def dispatch_reference(x, quant):
+    """What the dispatch kernel delivers for rows `x` in wire format `quant`,
+    dequantised to fp32 (the reference the receive-side tests compare with)."""
     if quant == "fp8":
         return quant_fp8_reference(x)
     if quant in ("nvfp4", "fp4"):

@@ -44,6 +44,11 @@ def _grouped_mm(a, w, offs):
 
 
 class NcclMoEBaseline:
+    """The same MoE layer built from library calls, for the on-box baseline:
+    torch top-k routing and FP8 quantisation, NCCL all-to-all
+    (``all_to_all_single``) of rows, scales, ids and weights, ``torch._grouped_mm``
+    for both expert GEMMs, all-to-all back and a per-token sum.  Not product
+    code: ``bench.py --impl nccl`` times it."""
     def __init__(self, cfg, group=None):
         self.cfg = cfg
         self.group = group

@@ -21,6 +21,11 @@ _C = _load()
 
 
 class DeviceCollectives:
+    """Device-side count all-to-all and cross-rank barrier over NVLink
+    (``include/kiwi/p2p/collectives.cuh``): one u32 per (source, destination)
+    pair per round, epoch-tagged ingress cells in a symmetric heap (its own
+    2 MB heap unless `heap` and a 64-byte aligned `offset` are given), every wait
+    bounded by `timeout_s`.  Collective constructor."""
     def __init__(self, group=None, heap=None, offset=0, timeout_s=5.0):
         self.group = group
         self.rank = kdist.rank(group)

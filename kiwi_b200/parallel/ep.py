@@ -447,10 +447,12 @@ def barrier(group=None):
 
 
 def get_rank(group=None):
+    """This process's rank in `group`."""
     return kdist.rank(group)
 
 
 def get_nranks(group=None):
+    """Number of ranks in `group`."""
     return kdist.world_size(group)
 
 
@@ -460,6 +462,7 @@ def get_hca_name_for_gpu(device=None):
 
 
 def get_hca_name_for_current_gpu():
+    """Always "": every peer is reached over NVLink."""
     return ""
 
 
@@ -487,6 +490,7 @@ def recommended_runtime_defaults(num_tokens, world_size, gpu_arch="", nic_family
 
 
 def recommended_num_blocks(num_tokens, world_size, gpu_arch="", nic_family=""):
+    """Dispatch grid size of recommended_runtime_defaults."""
     return recommended_runtime_defaults(num_tokens, world_size, gpu_arch, nic_family)["num_blocks"]
 
 

@@ -20,6 +20,11 @@ _C = _load()
 
 
 class SymmetricHeap:
+    """`nbytes` of device memory on every rank of `group`, mapped into every
+    rank's address space over NVLink (collective constructor).  ``native.view()``
+    is the by-value ``HeapView`` kernels take; ``tensor(offset, shape, dtype)`` a
+    torch view of this rank's part; ``enable_checks(limit)`` the checked mode of
+    the device put / get / signal API."""
     def __init__(self, nbytes, group=None, multicast=False, timeout_s=60.0):
         self.group = group
         self.rank = kdist.rank(group)
@@ -96,6 +101,8 @@ class SymmetricHeap:
 
 
 def exchange_fds(job, rank, world, fd, timeout_s=60.0):
+    """Every rank passes one file descriptor and receives every rank's (in
+    rank order), over abstract Unix sockets named after `job`."""
     return _C.p2p.exchange_fds(job, rank, world, fd, timeout_s)
 
 

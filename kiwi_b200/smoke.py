@@ -5,6 +5,7 @@ NVLink-path combine on a world of one) checked against the fp32 reference."""
 
 
 def run():
+    """Runs the smoke pass on the current CUDA device; raises on any mismatch."""
     import torch
 
     import kiwi_b200

@@ -28,6 +28,8 @@ ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a", "-lineinfo", "-O3", 
 
 def load_inline(name, cuda_sources, functions, cpp_sources="", build_directory=None, verbose=False,
                 extra_cuda_cflags=()):
+    """torch.utils.cpp_extension.load_inline with the kiwi headers on the
+    include path and sm_100a code generation; builds under build/jit/<name>."""
     from torch.utils.cpp_extension import load_inline as _load_inline
 
     if build_directory is None:

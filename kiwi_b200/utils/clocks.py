@@ -17,6 +17,9 @@ QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowd
 
 
 class ClockSampler:
+    """Samples SM clocks, power and throttle reasons with nvidia-smi (read
+    only) in a background process while the ``with`` block runs; ``summary()``
+    reports the samples between ``mark_start()`` and ``mark_end()``."""
     def __init__(self, device_index=0, period_ms=50):
         self.device_index = device_index
         self.period_ms = period_ms

@@ -30,14 +30,17 @@ def _first_env(names, default, env=None):
 
 
 def env_rank(env=None):
+    """Global rank from the launcher's variables (RANK_VARS), 0 if none is set."""
     return _first_env(RANK_VARS, 0, env)
 
 
 def env_world(env=None):
+    """World size from the launcher's variables (WORLD_VARS), 1 if none is set."""
     return _first_env(WORLD_VARS, 1, env)
 
 
 def env_local_rank(env=None):
+    """Rank within the node (LOCAL_RANK_VARS), 0 if none is set."""
     return _first_env(LOCAL_RANK_VARS, 0, env)
 
 
@@ -63,14 +66,17 @@ def init(backend=None, timeout_s=120.0, device=True):
 
 
 def rank(group=None):
+    """This process's rank in `group` (0 without a process group)."""
     return dist.get_rank(group) if dist.is_initialized() else 0
 
 
 def world_size(group=None):
+    """Size of `group` (1 without a process group)."""
     return dist.get_world_size(group) if dist.is_initialized() else 1
 
 
 def barrier(group=None):
+    """Host barrier over `group` (a no-op for a world of 1)."""
     if dist.is_initialized() and world_size(group) > 1:
         if dist.get_backend(group) == "nccl":
             dist.barrier(group=group, device_ids=[torch.cuda.current_device()])
@@ -79,6 +85,7 @@ def barrier(group=None):
 
 
 def broadcast_object(obj, src=0, group=None):
+    """`obj` from rank `src` of `group` on every rank."""
     if not dist.is_initialized() or world_size(group) == 1:
         return obj
     lst = [obj]
@@ -102,6 +109,7 @@ def max_over_ranks(value, group=None):
 
 
 def all_gather_objects(obj, group=None):
+    """Every rank's `obj`, in rank order."""
     if not dist.is_initialized() or world_size(group) == 1:
         return [obj]
     out = [None] * world_size(group)

@@ -154,6 +154,7 @@ def collect_env():
 
 
 def main(argv=None):
+    """Command-line entry: prints (or writes) collect_env() as JSON."""
     import argparse
 
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])

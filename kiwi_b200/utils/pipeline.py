@@ -22,6 +22,10 @@ import torch
 
 
 class HostDevicePipeline:
+    """End-to-end step loop: every step copies its inputs from pinned host
+    memory to the device, runs the step, and copies the result back, with `depth`
+    device slots and separate host-to-device and device-to-host streams so the
+    copies of neighbouring steps overlap the compute."""
     def __init__(self, fn, inputs, output, depth=2, device=None):
         """fn(*device_inputs, out=device_output) runs one step on the current
         stream.  `inputs`: list of (shape, dtype) of the device inputs;

@@ -3,6 +3,8 @@ import torch
 
 
 class EventTimer:
+    """CUDA-event timer of a region on the current stream:
+    ``with EventTimer() as t: ...`` then ``t.ms()`` after a synchronize."""
     def __init__(self):
         self.start = torch.cuda.Event(enable_timing=True)
         self.end = torch.cuda.Event(enable_timing=True)
