@@ -31,6 +31,37 @@ def timeit(fn, iters=20):
     return s.elapsed_time(e) / iters
 
 
+def trace_stats(plan, counts, out, swiglu, groups, rows, k, n, bk):
+    """One launch with the kernel's pipeline trace of CTA 0 (GroupedArgs::trace:
+    per k-block, when the MMA warp started / ended its wait for a full stage and
+    when the TMA producer started / ended its wait for a free stage, SM cycles),
+    reduced to per-k-block statistics."""
+    import numpy as np
+
+    kb = k // bk
+    tiles = groups * (rows // 128) * (n // 256)
+    cap = kb * ((tiles + 147) // 148)
+    tr = torch.zeros(cap * 4, dtype=torch.int64, device="cuda")
+    plan.run(counts, out, swiglu, None, 0, False, tr, bk)
+    torch.cuda.synchronize()
+    t = tr.view(-1, 4).cpu().numpy().astype(np.int64)
+    t = t[t[:, 1] > 0]
+    mma_wait = t[:, 1] - t[:, 0]
+    prod_wait = t[:, 3] - t[:, 2]
+    span = t[-1, 1] - t[0, 0]
+    per_kb = np.diff(t[:, 1])
+    issue = t[1:, 0] - t[:-1, 1]        # MMA warp: stage ready -> next wait (issue + commit)
+    lat = (t[:, 1] - t[:, 3])[t[:, 3] > 0]  # producer issue -> stage full seen by the MMA warp
+    pct = lambda a, q: float(np.percentile(a, q))  # noqa: E731
+    return {"kblocks_traced": int(len(t)), "span_cycles": int(span),
+            "cycles_per_kblock_p50": pct(per_kb, 50), "cycles_per_kblock_mean": float(per_kb.mean()),
+            "ideal_cycles_per_kblock": 128 * 256 * bk * 2 / 8192,
+            "mma_wait_full_p50": pct(mma_wait, 50), "mma_wait_full_p90": pct(mma_wait, 90),
+            "mma_wait_full_frac": float(mma_wait.sum() / span), "mma_issue_p50": pct(issue, 50),
+            "producer_wait_empty_frac": float(prod_wait.sum() / span),
+            "issue_to_full_p10": pct(lat, 10), "issue_to_full_p50": pct(lat, 50), "issue_to_full_p90": pct(lat, 90)}
+
+
 SHAPES = [
     ("gemm1_ep8", 32, 1024, 7168, 4096, True),
     ("gemm2_ep8", 32, 1024, 2048, 7168, False),
@@ -48,6 +79,9 @@ def main():
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--no-torch", action="store_true")
     ap.add_argument("--no-pair", action="store_true", help="skip the 2-SM (cta_group::2) kernel")
+    ap.add_argument("--trace", action="store_true",
+                    help="after timing, run one launch with the kernel's pipeline trace of CTA 0 and print its "
+                         "per-k-block statistics (1-SM kernel)")
     ap.add_argument("--bk", type=int, default=64, choices=(64, 32, 128),
                     help="K columns per pipeline stage of the 1-SM kernel (32: 64-byte swizzle, 9 stages; "
                          "128: two 64-column boxes per operand, 2 stages)")
@@ -78,6 +112,10 @@ def main():
                 tms = timeit(lambda: torch._grouped_mm(a, bt, offs=offs, out_dtype=torch.bfloat16), args.iters)
             except Exception as ex:  # pragma: no cover
                 print("torch._grouped_mm failed:", ex, file=sys.stderr)
+        if args.trace:
+            print("RESULT " + json.dumps({"bench": name + "_trace", "bk": args.bk,
+                                          **trace_stats(plan, counts, out, swiglu, groups, rows, k, n, args.bk)}),
+                  flush=True)
         print("RESULT " + json.dumps({"bench": name, "groups": groups, "rows": rows, "k": k, "n": n, "bk": args.bk,
                                       "kiwi_ms": ms, "kiwi_tflops": flops / ms / 1e9,
                                       "kiwi_pair_ms": ms_pair, "kiwi_pair_tflops": flops / ms_pair / 1e9,
