@@ -1,5 +1,6 @@
 #include "kiwi/ep/tuning.hpp"
 
+#include <cctype>
 #include <cstdlib>
 #include <sstream>
 
@@ -30,6 +31,18 @@ bool parse_bool(const std::string& v) {
     if (v == "1" || v == "true" || v == "on") return true;
     if (v == "0" || v == "false" || v == "off") return false;
     throw kiwi::error("KIWI_EP_TUNING: expected a boolean, got '" + v + "'");
+}
+
+/// A block count: the whole value must be a decimal integer in [0, 2^20].
+int parse_blocks(const std::string& v) {
+    if (v.empty() || !(std::isdigit(static_cast<unsigned char>(v[0])) || v[0] == '-')) {
+        throw kiwi::error("KIWI_EP_TUNING: expected a number, got '" + v + "'");
+    }
+    size_t used = 0;
+    const long n = std::stol(v, &used, 10);  // invalid_argument / out_of_range handled by the caller
+    if (used != v.size()) throw kiwi::error("KIWI_EP_TUNING: trailing characters in '" + v + "'");
+    if (n < 0 || n > (1L << 20)) throw kiwi::error("KIWI_EP_TUNING: block count " + v + " outside [0, 2^20]");
+    return static_cast<int>(n);
 }
 
 }  // namespace
@@ -66,9 +79,9 @@ EpTuning tune(const EpConfig& c, int sms, const char* env) {
             if (eq == std::string::npos) throw kiwi::error("KIWI_EP_TUNING: expected key=value, got '" + item + "'");
             const std::string k = item.substr(0, eq), v = item.substr(eq + 1);
             try {
-                if (k == "dispatch_blocks") t.dispatch_blocks = std::stoi(v);
-                else if (k == "recv_blocks") t.recv_blocks = std::stoi(v);
-                else if (k == "combine_blocks") t.combine_blocks = std::stoi(v);
+                if (k == "dispatch_blocks") t.dispatch_blocks = parse_blocks(v);
+                else if (k == "recv_blocks") t.recv_blocks = parse_blocks(v);
+                else if (k == "combine_blocks") t.combine_blocks = parse_blocks(v);
                 else if (k == "fused_combine") t.fused_combine = parse_bool(v);
                 else if (k == "gather_a") t.gather_a = parse_bool(v);
                 else if (k == "gemm_pair") t.gemm_pair = parse_bool(v);

@@ -139,9 +139,11 @@ def test_tuning_table_and_overrides():
     o = ep.tune(cfg, 148, "gather_a=1,dispatch_blocks=296,fused_combine=off")
     assert o["gather_a"] and o["dispatch_blocks"] == 296 and not o["fused_combine"]
     assert o["source"].endswith("KIWI_EP_TUNING")
-    for bad in ("nope=1", "gather_a=maybe", "recv_blocks=0", "dispatch_blocks"):
+    for bad in ("nope=1", "gather_a=maybe", "recv_blocks=0", "dispatch_blocks", "dispatch_blocks=12abc",
+                "recv_blocks=99999999999", "combine_blocks=2000000", "dispatch_blocks=-1", "recv_blocks= 5"):
         with pytest.raises(Exception):
             ep.tune(cfg, 148, bad)
+    assert ep.tune(cfg, 148, "recv_blocks=1048576,,combine_blocks=1")["recv_blocks"] == 1 << 20
 
 
 # ---- device phase timing: layout and decoding (the kernels' side is a GPU test) ----
