@@ -68,6 +68,14 @@ def main():
         summarize("invoke_rtt", r, {"payload_bytes": 8, "reply": "ring", "poll_warps": pw, "queue": "spsc"})
     r = C.bench.invoke_rtt(args.iters // 4, args.warmup, 8, 1, args.cpu, 4096, True, 0, 2_000_000_000, True, 200)
     summarize("invoke_rtt", r, {"payload_bytes": 8, "reply": "mailbox", "stagger_ns": 200, "queue": "mpsc"})
+    # Device-side overhead of one invoke (reference: benchmarks/invoke/bench_overhead): SM cycles per call.
+    for lm in (False, True):
+        c = C.bench.invoke_cost(calls=100_000, lane_masked=lm)
+        print("RESULT " + json.dumps({"bench": "invoke_cost", "lane_masked": lm, "args_bytes": 16,
+                                      "messages_per_call": 16 if lm else 1, **c}), flush=True)
+    for b in (8, 64, 256):
+        c = C.bench.push_cost(msgs=100_000, payload_bytes=b)
+        print("RESULT " + json.dumps({"bench": "push_cost", "payload_bytes": b, **c}), flush=True)
     if args.sweep:
         for b in [8, 16, 32, 64, 128, 256, 512, 1024, 2048, 4096]:
             r = C.bench.invoke_rtt(max(args.iters // 20, 1000), args.warmup // 10, b, 1, args.cpu, 4096, False,

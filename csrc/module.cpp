@@ -617,6 +617,21 @@ PYBIND11_MODULE(_C, m) {
               return d;
           },
           py::arg("msgs") = 10000, py::arg("payload_bytes") = 8);
+    b.def("invoke_cost",
+          [](uint32_t calls, bool lane_masked) {
+              bench::InvokeCostResult r;
+              {
+                  py::gil_scoped_release nogil;
+                  r = bench::invoke_cost(calls, lane_masked);
+              }
+              py::dict d;
+              d["cycles_per_call"] = r.cycles_per_call;
+              d["messages"] = r.messages;
+              d["ok"] = r.ok;
+              return d;
+          },
+          py::arg("calls") = 10000, py::arg("lane_masked") = false,
+          "SM cycles per device invoke (16-byte arguments), or per lane-masked invoke of 16 lanes.");
     b.def("h2d_timeout_test", [](uint64_t ns) {
         py::gil_scoped_release nogil;
         return bench::h2d_timeout_test(ns);

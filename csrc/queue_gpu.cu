@@ -989,6 +989,77 @@ PushCostResult push_cost(uint32_t msgs, uint32_t bytes) {
     return r;
 }
 
+/// SM cycles one warp spends per invoke (reference: bench_overhead.hip.cpp:54-119):
+/// mode 0 = invoke(cb, int32, float, uint64), a 16-byte argument image
+/// serialised in registers; mode 1 = invoke_lane_masked with the even lanes
+/// active (16 messages per call).  Calls that find the ring full are retried
+/// without counting the wait.
+__global__ void invoke_cost_kernel(DeviceContext<SPSCD2HQueue>* ctx, uint8_t cb, uint32_t calls, int mode,
+                                   uint64_t* cycles, uint32_t* status) {
+    auto h = ctx->get_device_handle(0);
+    const uint32_t lane = ptx::lane_id();
+    uint64_t total = 0;
+    for (uint32_t i = 0; i < calls; ++i) {
+        const int32_t a = static_cast<int32_t>(i);
+        const float b = 0.5f * static_cast<float>(i);
+        // invoke takes warp-uniform arguments; the lane-masked form sends each lane's own
+        const uint64_t c = mode == 0 ? i : ((static_cast<uint64_t>(lane) << 32) | i);
+        auto once = [&]() { return mode == 0 ? h.invoke(cb, a, b, c) : h.invoke_lane_masked(cb, (lane & 1) == 0, a, b, c); };
+        const uint64_t c0 = ptx::clock64();
+        const bool ok = once();
+        const uint64_t c1 = ptx::clock64();
+        if (ok) {
+            total += c1 - c0;
+            continue;
+        }
+        ptx::Deadline dl(2000000000ull);
+        while (!once()) {
+            if (dl.expired()) {
+                if (lane == 0) status[0] = 1;
+                ctx->save_device_handle(0, h);
+                return;
+            }
+        }
+    }
+    ctx->save_device_handle(0, h);
+    if (lane == 0) cycles[0] = total;
+}
+
+InvokeCostResult invoke_cost(uint32_t calls, bool lane_masked) {
+    kiwi::invoke::Context<SPSCD2HQueue> ctx(1, 1 << 16, MemKind::kMappedPinned);
+    std::atomic<uint64_t> count{0};
+    const uint8_t cb = ctx.register_raw_callback(
+        [&](const uint8_t*, uint32_t n) {
+            if (n == 16) count.fetch_add(1, std::memory_order_relaxed);
+        },
+        kiwi::invoke::CallbackBase::kAnySize);
+    DevBuf<uint64_t> cyc(1);
+    DevBuf<uint32_t> status(1);
+    cudaStream_t stream;
+    KIWI_CUDA_CHECK(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking));
+    invoke_cost_kernel<<<1, 32, 0, stream>>>(ctx.device_context(), cb, calls, lane_masked ? 1 : 0, cyc.p, status.p);
+    KIWI_CUDA_CHECK(cudaGetLastError());
+    const uint64_t want = static_cast<uint64_t>(calls) * (lane_masked ? 16 : 1);
+    uint64_t idle = 0;
+    while (count.load() < want) {
+        if (ctx.progress(0) == 0 && (++idle & 0xfffff) == 0 && cudaStreamQuery(stream) != cudaErrorNotReady) {
+            ctx.progress(0);
+            break;
+        }
+    }
+    KIWI_CUDA_CHECK(cudaStreamSynchronize(stream));
+    cudaStreamDestroy(stream);
+    uint64_t c = 0;
+    uint32_t st = 0;
+    KIWI_CUDA_CHECK(cudaMemcpy(&c, cyc.p, 8, cudaMemcpyDeviceToHost));
+    KIWI_CUDA_CHECK(cudaMemcpy(&st, status.p, 4, cudaMemcpyDeviceToHost));
+    InvokeCostResult r;
+    r.cycles_per_call = calls ? static_cast<double>(c) / calls : 0;
+    r.messages = count.load();
+    r.ok = st == 0 && r.messages == want;
+    return r;
+}
+
 // ---------------------------------------------------------------------------
 // Device-to-host push correctness
 // ---------------------------------------------------------------------------

@@ -96,6 +96,15 @@ struct PushCostResult {
 /// SM cycles one warp spends in push_lanes (ring never full: host drains).
 PushCostResult push_cost(uint32_t msgs, uint32_t bytes);
 
+struct InvokeCostResult {
+    double cycles_per_call = 0;  // SM cycles per invoke call (lane-masked: per call of 16 messages)
+    uint64_t messages = 0;       // messages the host received
+    bool ok = false;
+};
+/// SM cycles one warp spends per invoke(cb, int32, float, uint64), or per
+/// invoke_lane_masked with 16 active lanes; the host drains concurrently.
+InvokeCostResult invoke_cost(uint32_t calls, bool lane_masked);
+
 struct PushTestResult {
     uint64_t popped = 0;
     uint64_t mismatches = 0;     // payload / length / metadata errors
