@@ -68,6 +68,12 @@ def main():
         summarize("invoke_rtt", r, {"payload_bytes": 8, "reply": "ring", "poll_warps": pw, "queue": "spsc"})
     r = C.bench.invoke_rtt(args.iters // 4, args.warmup, 8, 1, args.cpu, 4096, True, 0, 2_000_000_000, True, 200)
     summarize("invoke_rtt", r, {"payload_bytes": 8, "reply": "mailbox", "stagger_ns": 200, "queue": "mpsc"})
+    # Host-mapped grid polling (reference: benchmarks/hardware/bench_host_mapped_grid_poll): block 0 publishes
+    # through host memory, the other blocks' warps poll it, then ack back.
+    sms = C.ops.num_sms()
+    for blocks in (2, 16, min(64, sms), sms):
+        g = C.bench.grid_poll(blocks=blocks, threads=256, rounds=2000, delay_ns=10_000)
+        print("RESULT " + json.dumps({"bench": "grid_poll", "threads": 256, **g}), flush=True)
     # Device-side overhead of one invoke (reference: benchmarks/invoke/bench_overhead): SM cycles per call.
     for lm in (False, True):
         c = C.bench.invoke_cost(calls=100_000, lane_masked=lm)

@@ -617,6 +617,28 @@ PYBIND11_MODULE(_C, m) {
               return d;
           },
           py::arg("msgs") = 10000, py::arg("payload_bytes") = 8);
+    b.def("grid_poll",
+          [](uint32_t blocks, uint32_t threads, uint32_t rounds, uint64_t delay_ns, uint64_t timeout_ns) {
+              bench::GridPollResult r;
+              {
+                  py::gil_scoped_release nogil;
+                  r = bench::grid_poll(blocks, threads, rounds, delay_ns, timeout_ns);
+              }
+              py::dict d;
+              d["blocks"] = r.blocks;
+              d["pollers"] = r.pollers;
+              d["first_observe_p50_ns"] = r.first_observe_p50_ns;
+              d["last_observe_p50_ns"] = r.last_observe_p50_ns;
+              d["last_observe_p99_ns"] = r.last_observe_p99_ns;
+              d["ack_p50_ns"] = r.ack_p50_ns;
+              d["ack_p99_ns"] = r.ack_p99_ns;
+              d["status"] = r.status;
+              d["ok"] = r.ok;
+              return d;
+          },
+          py::arg("blocks") = 16, py::arg("threads") = 256, py::arg("rounds") = 1000, py::arg("delay_ns") = 10000,
+          py::arg("timeout_ns") = 2000000000ull,
+          "Host-mapped grid polling: block 0 publishes, every other block's warps poll, blocks ack back.");
     b.def("invoke_cost",
           [](uint32_t calls, bool lane_masked) {
               bench::InvokeCostResult r;

@@ -8,6 +8,7 @@
 //   h2d_*_test      tests/queue/test_host_to_device_concurrent, test_mpmc_h2d_concurrent
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <atomic>
 #include <chrono>
 
@@ -413,6 +414,133 @@ RttResult pcie_floor(uint64_t iters, uint64_t warmup, int cpu, uint64_t timeout_
     return r;
 }
 
+
+// ---------------------------------------------------------------------------
+// Grid polling of mapped host memory (reference:
+// benchmarks/hardware/bench_host_mapped_grid_poll.hip.cpp): per round, block 0
+// publishes the round number into a host-mapped count slot after `delay_ns`;
+// lane 0 of every warp of the other blocks polls it; each of those blocks then
+// stores its own ack line (host-mapped, 64 bytes apart, plain release stores:
+// no host-memory atomics) and block 0 waits for every ack.  One GPU clock
+// (%globaltimer) times publish -> each warp's observation and publish -> last
+// ack.  Cooperative launch: every block is resident, so no poller waits on a
+// publisher that is not running.  Every wait is bounded.
+// ---------------------------------------------------------------------------
+
+__global__ void grid_poll_kernel(uint64_t* count_slot, uint64_t* acks, uint32_t rounds, uint64_t delay_ns,
+                                 uint64_t* pub_ns, uint64_t* obs_ns, uint64_t* ack_ns, uint32_t* status,
+                                 uint64_t timeout_ns) {
+    const uint32_t warps = blockDim.x / 32;
+    const uint32_t warp = threadIdx.x / 32;
+    const uint32_t lane = ptx::lane_id();
+    __shared__ int s_fail;
+    if (threadIdx.x == 0) s_fail = 0;
+    __syncthreads();
+    for (uint32_t r = 1; r <= rounds; ++r) {
+        if (blockIdx.x == 0) {
+            if (threadIdx.x == 0) {
+                const uint64_t t_start = ptx::globaltimer();
+                while (ptx::globaltimer() - t_start < delay_ns) {
+                }
+                const uint64_t t_pub = ptx::globaltimer();
+                ptx::st_release_sys_u64(count_slot, r);
+                pub_ns[r - 1] = t_pub;
+                for (uint32_t b = 1; b < gridDim.x; ++b) {
+                    ptx::Deadline dl(timeout_ns);
+                    while (ptx::ld_acquire_sys_u64(acks + 8 * b) != r) {
+                        if (dl.expired()) {
+                            status[0] = static_cast<uint32_t>(Status::kTimeout);
+                            s_fail = 1;
+                            break;
+                        }
+                    }
+                    if (s_fail) break;
+                }
+                ack_ns[r - 1] = ptx::globaltimer() - t_pub;
+            }
+        } else {
+            if (lane == 0) {
+                ptx::Deadline dl(timeout_ns);
+                uint64_t v = ptx::ld_acquire_sys_u64(count_slot);
+                while (v < r) {
+                    if (dl.expired()) {
+                        status[0] = static_cast<uint32_t>(Status::kTimeout);
+                        s_fail = 1;
+                        break;
+                    }
+                    v = ptx::ld_acquire_sys_u64(count_slot);
+                }
+                obs_ns[(static_cast<uint64_t>(r) - 1) * (gridDim.x - 1) * warps + (blockIdx.x - 1) * warps + warp] =
+                    ptx::globaltimer();
+            }
+            __syncthreads();
+            if (threadIdx.x == 0 && !s_fail) ptx::st_release_sys_u64(acks + 8 * blockIdx.x, r);
+        }
+        __syncthreads();
+        if (*reinterpret_cast<volatile int*>(&s_fail) || *reinterpret_cast<volatile uint32_t*>(status) != 0) return;
+    }
+}
+
+GridPollResult grid_poll(uint32_t blocks, uint32_t threads, uint32_t rounds, uint64_t delay_ns, uint64_t timeout_ns) {
+    if (blocks < 2 || threads < 32 || threads % 32 || threads > 1024 || rounds < 1) {
+        throw kiwi::error("grid_poll: blocks >= 2, threads a multiple of 32 in [32, 1024], rounds >= 1");
+    }
+    if (delay_ns > 1000000000ull || timeout_ns > 60000000000ull) {
+        throw kiwi::error("grid_poll: delay_ns at most 1 s and timeout_ns at most 60 s");
+    }
+    int dev = 0, per_sm = 0, sms = 0, coop = 0;
+    KIWI_CUDA_CHECK(cudaGetDevice(&dev));
+    KIWI_CUDA_CHECK(cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, dev));
+    KIWI_CUDA_CHECK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+    KIWI_CUDA_CHECK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, grid_poll_kernel, static_cast<int>(threads), 0));
+    if (!coop || static_cast<int64_t>(blocks) > static_cast<int64_t>(per_sm) * sms) {
+        throw kiwi::error("grid_poll: the grid must fit on the GPU at once (cooperative launch)");
+    }
+    detail::Block slots(64 * (blocks + 1), MemKind::kMappedPinned);  // count line, then one ack line per block
+    uint64_t* count_slot = slots.as<uint64_t>();
+    uint64_t* acks = slots.as<uint64_t>() + 8;
+    const uint32_t pollers = (blocks - 1) * (threads / 32);
+    DevBuf<uint64_t> pub(rounds), obs(static_cast<uint64_t>(rounds) * pollers), ackt(rounds);
+    DevBuf<uint32_t> status(1);
+    void* args[] = {&count_slot, &acks, &rounds, &delay_ns, &pub.p, &obs.p, &ackt.p, &status.p, &timeout_ns};
+    KIWI_CUDA_CHECK(cudaLaunchCooperativeKernel(reinterpret_cast<void*>(grid_poll_kernel), dim3(blocks), dim3(threads),
+                                                args, 0, nullptr));
+    KIWI_CUDA_CHECK(cudaDeviceSynchronize());
+    std::vector<uint64_t> p(rounds), o(static_cast<size_t>(rounds) * pollers), a(rounds);
+    uint32_t st = 0;
+    KIWI_CUDA_CHECK(cudaMemcpy(p.data(), pub.p, rounds * 8, cudaMemcpyDeviceToHost));
+    KIWI_CUDA_CHECK(cudaMemcpy(o.data(), obs.p, o.size() * 8, cudaMemcpyDeviceToHost));
+    KIWI_CUDA_CHECK(cudaMemcpy(a.data(), ackt.p, rounds * 8, cudaMemcpyDeviceToHost));
+    KIWI_CUDA_CHECK(cudaMemcpy(&st, status.p, 4, cudaMemcpyDeviceToHost));
+    GridPollResult r;
+    r.blocks = blocks;
+    r.pollers = pollers;
+    r.status = st;
+    r.ok = st == 0;
+    if (!r.ok) return r;
+    std::vector<double> first, last, acklat;
+    for (uint32_t k = 0; k < rounds; ++k) {
+        uint64_t lo = ~0ull, hi = 0;
+        for (uint32_t w = 0; w < pollers; ++w) {
+            const uint64_t t = o[static_cast<size_t>(k) * pollers + w];
+            lo = std::min(lo, t);
+            hi = std::max(hi, t);
+        }
+        first.push_back(static_cast<double>(lo > p[k] ? lo - p[k] : 0));
+        last.push_back(static_cast<double>(hi > p[k] ? hi - p[k] : 0));
+        acklat.push_back(static_cast<double>(a[k]));
+    }
+    auto pct = [](std::vector<double> v, double q) {
+        std::sort(v.begin(), v.end());
+        return v[std::min(v.size() - 1, static_cast<size_t>(q * (v.size() - 1) + 0.5))];
+    };
+    r.first_observe_p50_ns = pct(first, 0.5);
+    r.last_observe_p50_ns = pct(last, 0.5);
+    r.last_observe_p99_ns = pct(last, 0.99);
+    r.ack_p50_ns = pct(acklat, 0.5);
+    r.ack_p99_ns = pct(acklat, 0.99);
+    return r;
+}
 
 // ---------------------------------------------------------------------------
 // Round-trip protocol lab: measures store-and-poll variants so the invoke

@@ -96,6 +96,21 @@ struct PushCostResult {
 /// SM cycles one warp spends in push_lanes (ring never full: host drains).
 PushCostResult push_cost(uint32_t msgs, uint32_t bytes);
 
+struct GridPollResult {
+    uint32_t blocks = 0, pollers = 0;   // pollers = warps of blocks 1.. (lane 0 of each polls)
+    double first_observe_p50_ns = 0;    // publish -> first warp saw it (p50 over rounds)
+    double last_observe_p50_ns = 0;     // publish -> last warp saw it
+    double last_observe_p99_ns = 0;
+    double ack_p50_ns = 0;              // publish -> block 0 saw every block's ack
+    double ack_p99_ns = 0;
+    uint32_t status = 0;
+    bool ok = false;
+};
+/// A grid polling one host-mapped slot that block 0 publishes, then acking
+/// through host-mapped lines (the reference's host-mapped grid-poll
+/// reproducer); `blocks` must fit on the GPU at once.
+GridPollResult grid_poll(uint32_t blocks, uint32_t threads, uint32_t rounds, uint64_t delay_ns, uint64_t timeout_ns);
+
 struct InvokeCostResult {
     double cycles_per_call = 0;  // SM cycles per invoke call (lane-masked: per call of 16 messages)
     uint64_t messages = 0;       // messages the host received
