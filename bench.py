@@ -22,9 +22,7 @@ with cold weights.  `value` is the whole-job aggregate tokens/s.
 import argparse
 import json
 import os
-import subprocess
 import sys
-import threading
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)

@@ -7,7 +7,6 @@ serializer tests and the EP layout tests of AMDResearch/kiwi.)"""
 import os
 import struct
 
-import pytest
 from hypothesis import HealthCheck, given, settings
 from hypothesis import strategies as st
 
