@@ -32,8 +32,9 @@ NVCC_FLAGS = ARCH + [
     "--expt-relaxed-constexpr",
     "-DNDEBUG",
     "-Xcompiler=-fPIC",
+    "-Xcompiler=-fvisibility=hidden",
 ]
-CXX_FLAGS = ["-O3", "-std=c++17", "-DNDEBUG", "-fPIC"]
+CXX_FLAGS = ["-O3", "-std=c++17", "-DNDEBUG", "-fPIC", "-fvisibility=hidden"]
 
 
 def sources():
