@@ -5,10 +5,8 @@
 //
 // Who needs it: callers that must not allocate device memory while they run.
 // Typical cases are a serving engine that reserves all GPU memory for its own
-// pool at start-up (any cudaMalloc later fails or fragments that pool), C or
-// C++ hosts that cannot reach PyTorch's caching allocator, and code that issues
-// work while another component is capturing the stream into a CUDA graph,
-// where cudaMalloc is not permitted.  The regular entry point
+// pool at start-up (any cudaMalloc later fails or fragments that pool), and C
+// or C++ hosts that cannot reach PyTorch's caching allocator.  The regular entry point
 // (kiwi_b200._C.ops.GroupedGemm) allocates its schedule buffers with torch;
 // this one keeps them in a fixed device array instead.
 //

@@ -3,8 +3,8 @@ symbol, against the regular entry point (kiwi_b200._C.ops.GroupedGemm).
 
 The C entry point exists for callers that may not allocate device memory
 while running (engines that pre-reserve the whole GPU for their own pool,
-hosts without PyTorch's allocator, code running under another component's
-stream capture); it keeps its scratch in a fixed device array.  This file is
+hosts without PyTorch's allocator); it keeps its scratch in a fixed device
+array.  This file is
 named to be collected last.
 """
 import ctypes
