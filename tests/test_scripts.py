@@ -34,3 +34,31 @@ def test_script_help(path, capsys, monkeypatch):
         runpy.run_path(path, run_name="__main__")
     assert e.value.code in (0, None)
     assert "usage" in capsys.readouterr().out.lower()
+
+
+def test_run_suite_dry_run_lists_every_benchmark(capsys):
+    sys.path.insert(0, os.path.join(ROOT, "benchmarks"))
+    import run_suite
+
+    assert run_suite.main(["--dry-run", "--gpus", "4"]) == 0
+    out = capsys.readouterr().out.splitlines()
+    assert [ln.split(":")[0] for ln in out] == [n for n, _, _ in run_suite.suite(4, False)]
+    for name, multi, argv in run_suite.suite(4, False):
+        assert os.path.exists(os.path.join(ROOT, argv[0])), argv[0]
+        line = next(ln for ln in out if ln.startswith(name + ":"))
+        assert ("--nproc-per-node=4" in line) == multi
+    assert run_suite.main(["--dry-run", "--only", "gemm,invoke"]) == 0
+    with pytest.raises(SystemExit):
+        run_suite.main(["--dry-run", "--only", "nope"])
+
+
+def test_run_suite_ends_its_process_group_on_timeout():
+    sys.path.insert(0, os.path.join(ROOT, "benchmarks"))
+    import run_suite
+
+    slow = "import time; print('started', flush=True); time.sleep(60)"
+    rc, out = run_suite.run_group([sys.executable, "-c", slow], timeout_s=2, grace_s=2)
+    assert rc == -1 and "timed out" in out
+    code = "import json; print('RESULT ' + json.dumps({'x': 1}))"
+    rc, out = run_suite.run_group([sys.executable, "-c", code], timeout_s=60)
+    assert rc == 0 and run_suite.parse_results(out) == [{"x": 1}]
