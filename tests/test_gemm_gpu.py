@@ -56,6 +56,30 @@ def test_grouped_gemm_matches_fp32(counts, n, k, swiglu, pair):
     assert err <= tol, (err, tol)
 
 
+@pytest.mark.parametrize("swiglu", [False, True])
+def test_bk32_stages_match_bk64_bitwise(swiglu):
+    """The opt-in 32-column-stage kernel (64-byte swizzle, 9 stages) issues the
+    same K = 16 MMAs in the same order as the default 64-column one, so the
+    outputs are identical, ragged and empty groups included."""
+    torch.manual_seed(1)
+    C = kiwi_b200.native()
+    counts, n, k = [200, 0, 256, 77], 512, 1024
+    rows = sum(counts)
+    a = (torch.randn(rows, k, device="cuda") * 0.5).bfloat16()
+    b = (torch.randn(len(counts) * n, k, device="cuda") * 0.05).bfloat16()
+    cols = n // 2 if swiglu else n
+    o64 = torch.full((rows, cols), float("nan"), device="cuda", dtype=torch.bfloat16)
+    o32 = torch.full_like(o64, float("nan"))
+    plan = C.ops.GroupedGemm(a, b, len(counts))
+    cnt = torch.tensor(counts, dtype=torch.int32, device="cuda")
+    plan.run(cnt, o64, swiglu)
+    plan.run(cnt, o32, swiglu, None, 0, False, None, 32)
+    torch.cuda.synchronize()
+    assert int(plan.error.item()) == 0
+    assert torch.isfinite(o64.float()).all()
+    assert torch.equal(o64, o32)
+
+
 def test_gemm_kernels_use_no_local_memory():
     C = kiwi_b200.native()
     for sw in (False, True):
