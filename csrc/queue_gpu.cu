@@ -48,6 +48,10 @@ KIWI_DEV uint64_t dev_xorshift(uint64_t& s) {
     return s;
 }
 
+/// Upper bound on helper warps that poll until their block's main warp sets a
+/// stop flag (10 minutes: far above any benchmark run).
+constexpr uint64_t kHelperGuardNs = 600ull * 1000000000ull;
+
 template <typename T>
 struct DevBuf {
     T* p = nullptr;
@@ -113,8 +117,12 @@ __global__ void __launch_bounds__(256) invoke_rtt_kernel(
         // staggered so their reads reach host memory evenly spaced.
         __nanosleep(static_cast<uint32_t>(stagger_ns * (warp - 1)));
         const uint64_t mask = reply.capacity() - 1;
+        // The main warp sets sh.stop on every exit path; the guard bounds the
+        // loop regardless (far above any run's length).
+        ptx::Deadline guard(kHelperGuardNs);
         while (true) {
-            if (*reinterpret_cast<volatile uint32_t*>(&sh.stop)) break;
+            const bool quit = *reinterpret_cast<volatile uint32_t*>(&sh.stop) != 0 || guard.expired();
+            if (__any_sync(ptx::kFullMask, quit)) break;  // warp-uniform: the loop body uses full-warp collectives
             const uint64_t line = *reinterpret_cast<volatile uint64_t*>(&sh.line);
             const uint32_t tag = lap_tag(line, reply.log2cap);
             uint4 v = make_uint4(0, 0, 0, 0);
@@ -578,7 +586,8 @@ __global__ void __launch_bounds__(288) rtt_lab_kernel(uint64_t* d2h, const uint6
         const uint64_t t_start = ptx::globaltimer() + static_cast<uint64_t>(stagger_ns) * p;
         while (ptx::globaltimer() < t_start) {
         }
-        while (!*reinterpret_cast<volatile uint32_t*>(&sh.stop)) {
+        ptx::Deadline guard(kHelperGuardNs);  // sh.stop ends the loop; the guard bounds it regardless
+        while (!*reinterpret_cast<volatile uint32_t*>(&sh.stop) && !guard.expired()) {
             const uint64_t v = ptx::ld_volatile_u64(a);
             if (v > *reinterpret_cast<volatile unsigned long long*>(&sh.found)) atomicMax(&sh.found, v);
         }
