@@ -109,15 +109,24 @@ def route_reference(logits, topk):
 # ---------------------------------------------------------------- quantisation
 
 
-def quant_fp8_reference(x, block=128):
-    """1 x `block` FP8 e4m3 quantise-dequantise of rows of x (fp32 scale = amax / 448)."""
+def quant_fp8_codes(x, block=128):
+    """1 x `block` FP8 e4m3 quantisation of rows of x, the dispatch wire format:
+    (codes float8_e4m3fn [t, h], fp32 scales [t, h / block]) with scale =
+    amax / 448 per block (1 for an all-zero block)."""
     t, h = x.shape
     xf = x.float().view(t, h // block, block)
     amax = xf.abs().amax(-1, keepdim=True)
     scale = torch.where(amax > 0, amax / FP8_MAX, torch.ones_like(amax))
     inv = torch.where(amax > 0, FP8_MAX / amax, torch.zeros_like(amax))  # multiply by the reciprocal, as on the device
     q = (xf * inv).clamp(-FP8_MAX, FP8_MAX).to(torch.float8_e4m3fn)
-    return (q.float() * scale).view(t, h)
+    return q.view(t, h), scale.view(t, h // block)
+
+
+def quant_fp8_reference(x, block=128):
+    """1 x `block` FP8 e4m3 quantise-dequantise of rows of x (fp32 scale = amax / 448)."""
+    t, h = x.shape
+    q, scale = quant_fp8_codes(x, block)
+    return (q.float().view(t, h // block, block) * scale.unsqueeze(-1)).view(t, h)
 
 
 def _round_fp4(v):

@@ -1,0 +1,209 @@
+"""KiwiEpOp's dispatch / combine contract over torch.distributed all-to-all.
+
+``CollectiveEpOp`` has the same constructor arguments, methods and return
+values as :class:`kiwi_b200.parallel.ep.KiwiEpOp`, but moves the rows with
+``all_to_all_single`` (NCCL between GPUs, gloo between CPU processes) instead
+of NVLink stores into a symmetric heap.  It is the way to run the transport on
+ranks that do not share one NVSwitch domain (several nodes), which
+:class:`~kiwi_b200.parallel.ep.KiwiEpOp` does not span, and it runs on CPU
+processes too.  The caller chooses it explicitly; nothing switches between the
+two.  (The reference spans nodes with LCI RDMA through CPU proxies,
+apps/ep/dispatch.hip.cpp and apps/ep/comm of AMDResearch/kiwi.)
+
+Semantics, as KiwiEpOp:
+
+* ``dispatch(input, weights, scales, indices)`` returns ``(out, out_weights,
+  out_scales, out_indices, recv_count)``: one row per (source rank, token) that
+  routes at least one of its top-k experts to this rank, in (source rank,
+  token) order; ``out`` in the wire format (bf16, or float8_e4m3fn with fp32
+  1x128 scales in ``out_scales``), ``out_weights`` / ``out_indices`` the token's
+  full top-k weights and global expert ids.  Quantisation happens here, so
+  ``scales`` is accepted and ignored.
+* ``combine(input, weights, indices, out)`` returns ``(out, None)``: row i of
+  ``input`` goes back to the rank and token it came from, and each token's rows
+  are summed (no routing weights, as MORI); tokens routed nowhere get zeros.
+* ``get_dispatch_src_token_pos()`` encodes each received row's source as
+  ``src_rank * (world * max_tokens) + token`` and ``decode_send_flat_idx``
+  inverts it.
+
+Per call there are four small all-to-alls (counts) plus one per payload
+tensor; every rank must call dispatch and combine in the same order.
+"""
+import torch
+import torch.distributed as dist
+
+from ..models import moe as moe_model
+from ..utils import dist as kdist
+
+_FORMATS = {"none": "none", "fp8": "fp8"}
+_DTYPES = {torch.bfloat16: "none", torch.float8_e4m3fn: "fp8"}
+
+
+class CollectiveEpOp:
+    """KiwiEpOp's transport contract over torch.distributed all-to-all (see the module docstring)."""
+
+    def __init__(self, device_id=None, world_size=None, hidden_dim=None, topk=None, num_experts_per_rank=None,
+                 max_num_inp_token_per_rank=None, dispatch_dtype=torch.bfloat16, combine_dtype=torch.bfloat16,
+                 *_launch_args, group=None, dispatch_quant_format="none", combine_quant_format="none", device=None,
+                 **_ignored):
+        missing = [n for n, v in (("hidden_dim", hidden_dim), ("topk", topk),
+                                  ("num_experts_per_rank", num_experts_per_rank),
+                                  ("max_num_inp_token_per_rank", max_num_inp_token_per_rank)) if v is None]
+        if missing:
+            raise TypeError("CollectiveEpOp missing required arguments: " + ", ".join(missing))
+        if combine_dtype != torch.bfloat16 or str(combine_quant_format).lower() != "none":
+            raise ValueError("combine_dtype must be torch.bfloat16 (combine_quant_format 'none')")
+        fmt = str(dispatch_quant_format).lower()
+        if fmt not in _FORMATS:
+            raise ValueError(f"unsupported dispatch_quant_format {dispatch_quant_format!r}: CollectiveEpOp carries "
+                             "bf16 or FP8 rows (NVFP4 is the NVLink op's)")
+        quant = "fp8" if fmt == "fp8" else _DTYPES.get(dispatch_dtype)
+        if quant is None:
+            raise ValueError(f"unsupported dispatch_dtype {dispatch_dtype}")
+        if hidden_dim % 128 and quant == "fp8":
+            raise ValueError("FP8 dispatch needs hidden_dim to be a multiple of 128")
+        self.group = group
+        self.rank = kdist.rank(group)
+        self.world_size = kdist.world_size(group)
+        if world_size is not None and int(world_size) != self.world_size:
+            raise ValueError(f"world_size {world_size} differs from the process group's {self.world_size}")
+        if device is None:
+            if device_id is not None:
+                torch.cuda.set_device(int(device_id))
+                device = torch.device("cuda", int(device_id))
+            elif torch.cuda.is_available() and (not dist.is_initialized() or dist.get_backend(group) == "nccl"):
+                device = torch.device("cuda", torch.cuda.current_device())
+            else:
+                device = torch.device("cpu")
+        self.device = torch.device(device)
+        self.hidden_dim = int(hidden_dim)
+        self.topk = int(topk)
+        self.experts_per_rank = int(num_experts_per_rank)
+        self.max_tokens = int(max_num_inp_token_per_rank)
+        self._quant = quant
+        self._send_counts = None
+        self._recv_counts = None
+        self._send_tokens = None
+        self._src_pos = None
+        self._last_tokens = 0
+        self._out = None
+
+    # -- helpers ------------------------------------------------------------------
+    def _a2a(self, send, send_counts, recv_counts):
+        """all_to_all_single of the rows of `send` (first dimension split by rank)."""
+        shape = (int(sum(recv_counts)),) + tuple(send.shape[1:])
+        recv = torch.empty(shape, dtype=send.dtype, device=send.device)
+        if self.world_size == 1:
+            recv.copy_(send)
+            return recv
+        dist.all_to_all_single(recv, send.contiguous(), output_split_sizes=list(recv_counts),
+                               input_split_sizes=list(send_counts), group=self.group)
+        return recv
+
+    def _wire(self, t):
+        """A payload tensor as bytes (all_to_all needs types every backend carries)."""
+        return t.contiguous().view(torch.uint8).view(t.shape[0], -1)
+
+    # -- the contract ---------------------------------------------------------------
+    def dispatch(self, input, weights, scales=None, indices=None, **_launch_kwargs):
+        """See the module docstring; collective over the group."""
+        x = input.to(self.device)
+        t = x.shape[0]
+        if t > self.max_tokens:
+            raise ValueError("more tokens than max_num_inp_token_per_rank")
+        idx = indices.to(self.device, torch.int64)
+        w = weights.to(self.device, torch.float32)
+        dest = idx // self.experts_per_rank                                           # [T, k]
+        onehot = torch.zeros(t, self.world_size, dtype=torch.bool, device=self.device)
+        if t:
+            onehot.scatter_(1, dest.clamp(0, self.world_size - 1), True)
+        pairs = onehot.t().nonzero()                                                   # (dest, token), dest-major
+        order_dest, order_tok = pairs[:, 0], pairs[:, 1]
+        send_counts = torch.bincount(order_dest, minlength=self.world_size)
+        recv_counts = self._a2a(send_counts.view(-1, 1), [1] * self.world_size, [1] * self.world_size).view(-1)
+        send_counts, recv_counts = send_counts.tolist(), recv_counts.tolist()
+        if self._quant == "fp8":
+            codes, sc = moe_model.quant_fp8_codes(x)
+            rows, row_scales = codes[order_tok], sc[order_tok]
+        else:
+            rows, row_scales = x.to(torch.bfloat16)[order_tok], None
+        out_rows = self._a2a(self._wire(rows), send_counts, recv_counts)
+        out_w = self._a2a(w[order_tok], send_counts, recv_counts)
+        out_idx = self._a2a(idx.to(torch.int32)[order_tok], send_counts, recv_counts)
+        src_tok = self._a2a(order_tok.to(torch.int32).view(-1, 1), send_counts, recv_counts).view(-1)
+        out_sc = None
+        if row_scales is not None:
+            out_sc = self._a2a(row_scales.contiguous(), send_counts, recv_counts)
+        n = int(sum(recv_counts))
+        rows_dtype = torch.float8_e4m3fn if self._quant == "fp8" else torch.bfloat16
+        out_rows = out_rows.view(rows_dtype).view(n, self.hidden_dim)
+        src_rank = torch.repeat_interleave(torch.arange(self.world_size, device=self.device),
+                                           torch.tensor(recv_counts, device=self.device))
+        self._src_pos = src_rank.to(torch.int64) * self.max_num_tokens_to_send() + src_tok.to(torch.int64)
+        self._send_counts, self._recv_counts, self._send_tokens = send_counts, recv_counts, order_tok
+        self._last_tokens = t
+        count = torch.tensor([n], dtype=torch.int32, device=self.device)
+        return out_rows, out_w, out_sc, out_idx, count
+
+    dispatch_send = dispatch
+
+    def dispatch_recv(self, **_kwargs):
+        """dispatch() already completes the receive (kept for call-shape parity)."""
+
+    def combine(self, input, weights=None, indices=None, out=None, **_launch_kwargs):
+        """See the module docstring; collective over the group."""
+        if self._send_counts is None:
+            raise RuntimeError("combine needs a prior dispatch")
+        n = int(sum(self._recv_counts))
+        rows = input[:n].to(self.device, torch.bfloat16)
+        back = self._a2a(rows, self._recv_counts, self._send_counts)                   # (dest, token) order
+        t = self._last_tokens
+        acc = torch.zeros(t, self.hidden_dim, dtype=torch.float32, device=self.device)
+        if back.shape[0]:
+            acc.index_add_(0, self._send_tokens, back.float())
+        if out is None:
+            out = torch.empty(t, self.hidden_dim, dtype=torch.bfloat16, device=self.device)
+        out[:t].copy_(acc)
+        self._out = out
+        return out, None
+
+    combine_send = combine
+
+    def combine_recv(self, **_kwargs):
+        return (self._out[:self._last_tokens] if self._out is not None else None), None
+
+    def reset(self):
+        """Ends the current round (nothing to clear between rounds)."""
+        self._last_tokens = 0
+
+    # -- accessors of the reference op -------------------------------------------
+    def max_num_tokens_to_recv(self):
+        return self.world_size * self.max_tokens
+
+    def max_num_tokens_to_recv_per_rank(self):
+        return self.max_tokens
+
+    def max_num_tokens_to_send(self):
+        return self.world_size * self.max_tokens
+
+    def max_num_tokens_to_send_per_rank(self):
+        return self.max_tokens
+
+    def decode_send_flat_idx(self, flat_idx):
+        """(source rank, source token) of a position from get_dispatch_src_token_pos()."""
+        stride = self.max_num_tokens_to_send()
+        return int(flat_idx) // stride, int(flat_idx) % stride
+
+    def get_dispatch_src_token_pos(self):
+        """Source position of each row the last dispatch received (see decode_send_flat_idx)."""
+        return self._src_pos if self._src_pos is not None else torch.empty(0, dtype=torch.int64)
+
+    def launch_policy(self, num_tokens):
+        return {"num_tokens": int(num_tokens), "transport": "torch.distributed all_to_all",
+                "backend": dist.get_backend(self.group) if dist.is_initialized() else "none"}
+
+    def check(self):
+        """Nothing to check: errors surface as exceptions of the collectives."""
+
+
+__all__ = ["CollectiveEpOp"]

@@ -1,0 +1,123 @@
+"""CollectiveEpOp: KiwiEpOp's dispatch / combine contract over all-to-all,
+checked on CPU (world of 1 in-process, two gloo ranks as processes) against
+the contract computed directly from every rank's inputs."""
+import multiprocessing as mp
+import os
+import socket
+
+import pytest
+import torch
+
+from kiwi_b200.models import moe
+from kiwi_b200.parallel.ep_collective import CollectiveEpOp
+
+HIDDEN, TOPK, EPR, TOKENS = 256, 3, 4, 24
+
+
+def inputs(rank, world, tokens=TOKENS):
+    """Seeded per-rank inputs every process can regenerate."""
+    g = torch.Generator().manual_seed(100 + rank)
+    x = torch.randn(tokens, HIDDEN, generator=g).bfloat16()
+    logits = torch.randn(tokens, EPR * world, generator=g)
+    idx, w = moe.route_reference(logits, TOPK)
+    return x, idx.to(torch.int32), w.float()
+
+
+def expected(rank, world, quant):
+    """(rows, weights, indices, positions) rank `rank` must receive, in (source, token) order."""
+    rows, ws, ids, pos = [], [], [], []
+    for s in range(world):
+        x, idx, w = inputs(s, world)
+        for t in range(x.shape[0]):
+            if bool(((idx[t].long() // EPR) == rank).any()):
+                rows.append(x[t])
+                ws.append(w[t])
+                ids.append(idx[t])
+                pos.append(s * world * TOKENS + t)
+    rows = torch.stack(rows) if rows else torch.empty(0, HIDDEN, dtype=torch.bfloat16)
+    return rows, torch.stack(ws), torch.stack(ids), pos
+
+
+def check_rank(op, rank, world, quant):
+    x, idx, w = inputs(rank, world)
+    out, ow, sc, oidx, cnt = op.dispatch(x, w, None, idx)
+    rows, ws, ids, pos = expected(rank, world, quant)
+    n = int(cnt.item())
+    assert n == rows.shape[0]
+    assert torch.equal(oidx[:n], ids) and torch.equal(ow[:n], ws)
+    assert op.get_dispatch_src_token_pos().tolist() == pos
+    assert [op.decode_send_flat_idx(p) for p in pos] == [(p // (world * TOKENS), p % (world * TOKENS)) for p in pos]
+    if quant == "fp8":
+        codes, scales = moe.quant_fp8_codes(rows)
+        assert out.dtype == torch.float8_e4m3fn
+        assert torch.equal(out[:n].view(torch.uint8), codes.view(torch.uint8)) and torch.equal(sc[:n], scales)
+        back = moe.quant_fp8_reference(rows).bfloat16()
+    else:
+        assert sc is None and torch.equal(out[:n], rows)
+        back = out[:n].clone()
+    # combine: every destination returns the token's (dequantised) row; the source sums them
+    res, _ = op.combine(back, None, oidx)
+    dests = (idx.long() // EPR)
+    want = torch.zeros(x.shape[0], HIDDEN)
+    ref_rows = moe.quant_fp8_reference(x) if quant == "fp8" else x.float()
+    for t in range(x.shape[0]):
+        k = len(set(dests[t].tolist()))
+        want[t] = ref_rows[t].bfloat16().float() * k
+    assert (res.float() - want).abs().max().item() <= 2e-2 * want.abs().max().item() + 1e-3
+
+
+@pytest.mark.parametrize("quant", ["none", "fp8"])
+def test_world_of_one(quant):
+    op = CollectiveEpOp(hidden_dim=HIDDEN, topk=TOPK, num_experts_per_rank=EPR, max_num_inp_token_per_rank=TOKENS,
+                        dispatch_quant_format=quant, device="cpu")
+    for _ in range(2):  # rounds are independent
+        check_rank(op, 0, 1, quant)
+
+
+def _member(rank, port, quant, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE="2",
+                      LOCAL_RANK=str(rank))
+    try:
+        from kiwi_b200.utils import dist as kdist
+
+        kdist.init(backend="gloo", timeout_s=30.0, device=False)
+        op = CollectiveEpOp(hidden_dim=HIDDEN, topk=TOPK, num_experts_per_rank=EPR,
+                            max_num_inp_token_per_rank=TOKENS, dispatch_quant_format=quant, device="cpu")
+        for _ in range(2):
+            check_rank(op, rank, 2, quant)
+        kdist.dist.destroy_process_group()
+        q.put((rank, "ok"))
+    except Exception as e:  # noqa: BLE001 - reported to the parent
+        import traceback
+
+        q.put((rank, f"{type(e).__name__}: {e}\n{traceback.format_exc()[-2000:]}"))
+
+
+@pytest.mark.parametrize("quant", ["none", "fp8"])
+def test_two_gloo_ranks(quant):
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    ps = [ctx.Process(target=_member, args=(r, port, quant, q)) for r in range(2)]
+    for p in ps:
+        p.start()
+    got = dict(q.get(timeout=180) for _ in ps)
+    for p in ps:
+        p.join(timeout=30)
+    assert got == {0: "ok", 1: "ok"}, got
+
+
+def test_constructor_checks():
+    with pytest.raises(TypeError):
+        CollectiveEpOp(0, 1, 256)
+    with pytest.raises(ValueError):
+        CollectiveEpOp(hidden_dim=256, topk=2, num_experts_per_rank=4, max_num_inp_token_per_rank=8,
+                       dispatch_quant_format="fp4", device="cpu")
+    with pytest.raises(ValueError):
+        CollectiveEpOp(hidden_dim=200, topk=2, num_experts_per_rank=4, max_num_inp_token_per_rank=8,
+                       dispatch_quant_format="fp8", device="cpu")
+    op = CollectiveEpOp(hidden_dim=256, topk=2, num_experts_per_rank=4, max_num_inp_token_per_rank=8, device="cpu")
+    with pytest.raises(RuntimeError):
+        op.combine(torch.zeros(1, 256).bfloat16())

@@ -292,3 +292,28 @@ def test_kiwi_ep_op_reference_accessors():
         with pytest.raises(RuntimeError):
             op.reset()
     op.reset()
+
+
+def test_collective_op_matches_the_nvlink_op():
+    """CollectiveEpOp (all-to-all transport, for ranks across nodes) and
+    KiwiEpOp (NVLink stores) deliver the same rows, ids, weights and source
+    positions, and combine to the same sums, on one GPU."""
+    from kiwi_b200.parallel.ep import KiwiEpOp
+    from kiwi_b200.parallel.ep_collective import CollectiveEpOp
+
+    kw = dict(hidden_dim=512, topk=2, num_experts_per_rank=8, max_num_inp_token_per_rank=32)
+    a, b = KiwiEpOp(**kw), CollectiveEpOp(**kw)
+    torch.manual_seed(3)
+    x = torch.randn(32, 512, device="cuda").bfloat16()
+    idx, w = moe.route_reference(torch.randn(32, 8, device="cuda"), 2)
+    ra, wa, _, ia, ca = a.dispatch(x, w, None, idx)
+    rb, wb, _, ib, cb = b.dispatch(x, w, None, idx)
+    n = int(ca.item())
+    assert n == int(cb.item()) == 32
+    assert torch.equal(ra[:n], rb[:n]) and torch.equal(ia[:n], ib[:n]) and torch.allclose(wa[:n], wb[:n])
+    assert a.get_dispatch_src_token_pos().tolist() == b.get_dispatch_src_token_pos().tolist()
+    oa, _ = a.combine(ra[:n].clone(), None, idx)
+    ob, _ = b.combine(rb[:n].clone(), None, idx)
+    torch.cuda.synchronize()
+    a.check()
+    assert torch.equal(oa, ob) and torch.equal(oa, x)
