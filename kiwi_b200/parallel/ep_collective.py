@@ -21,7 +21,9 @@ Semantics, as KiwiEpOp:
   ``scales`` is accepted and ignored.
 * ``combine(input, weights, indices, out)`` returns ``(out, None)``: row i of
   ``input`` goes back to the rank and token it came from, and each token's rows
-  are summed (no routing weights, as MORI); tokens routed nowhere get zeros.
+  are summed in fp32 (no routing weights, as MORI); tokens routed nowhere get
+  zeros.  Rows travel and the result is returned in ``combine_dtype``: bf16,
+  or float32 as the reference also accepts (the NVLink op combines bf16 only).
 * ``get_dispatch_src_token_pos()`` encodes each received row's source as
   ``src_rank * (world * max_tokens) + token`` and ``decode_send_flat_idx``
   inverts it.
@@ -51,8 +53,9 @@ class CollectiveEpOp:
                                   ("max_num_inp_token_per_rank", max_num_inp_token_per_rank)) if v is None]
         if missing:
             raise TypeError("CollectiveEpOp missing required arguments: " + ", ".join(missing))
-        if combine_dtype != torch.bfloat16 or str(combine_quant_format).lower() != "none":
-            raise ValueError("combine_dtype must be torch.bfloat16 (combine_quant_format 'none')")
+        if combine_dtype not in (torch.bfloat16, torch.float32) or str(combine_quant_format).lower() != "none":
+            raise ValueError("combine_dtype must be torch.bfloat16 or torch.float32 (combine_quant_format 'none')")
+        self._combine_dtype = combine_dtype
         fmt = str(dispatch_quant_format).lower()
         if fmt not in _FORMATS:
             raise ValueError(f"unsupported dispatch_quant_format {dispatch_quant_format!r}: CollectiveEpOp carries "
@@ -155,14 +158,14 @@ class CollectiveEpOp:
         if self._send_counts is None:
             raise RuntimeError("combine needs a prior dispatch")
         n = int(sum(self._recv_counts))
-        rows = input[:n].to(self.device, torch.bfloat16)
+        rows = input[:n].to(self.device, self._combine_dtype)
         back = self._a2a(rows, self._recv_counts, self._send_counts)                   # (dest, token) order
         t = self._last_tokens
         acc = torch.zeros(t, self.hidden_dim, dtype=torch.float32, device=self.device)
         if back.shape[0]:
             acc.index_add_(0, self._send_tokens, back.float())
         if out is None:
-            out = torch.empty(t, self.hidden_dim, dtype=torch.bfloat16, device=self.device)
+            out = torch.empty(t, self.hidden_dim, dtype=self._combine_dtype, device=self.device)
         out[:t].copy_(acc)
         self._out = out
         return out, None

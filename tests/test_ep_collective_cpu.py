@@ -109,9 +109,23 @@ def test_two_gloo_ranks(quant):
     assert got == {0: "ok", 1: "ok"}, got
 
 
+def test_float32_combine_sums_exactly():
+    op = CollectiveEpOp(hidden_dim=HIDDEN, topk=TOPK, num_experts_per_rank=EPR, max_num_inp_token_per_rank=TOKENS,
+                        combine_dtype=torch.float32, device="cpu")
+    x, idx, w = inputs(0, 1)
+    out, _, _, _, cnt = op.dispatch(x, w, None, idx)
+    n = int(cnt.item())
+    rows = torch.randn(n, HIDDEN)  # fp32 expert outputs, one per received row
+    res, _ = op.combine(rows)
+    assert res.dtype == torch.float32 and torch.equal(res, rows)  # world of 1: one row per token
+
+
 def test_constructor_checks():
     with pytest.raises(TypeError):
         CollectiveEpOp(0, 1, 256)
+    with pytest.raises(ValueError):
+        CollectiveEpOp(hidden_dim=256, topk=2, num_experts_per_rank=4, max_num_inp_token_per_rank=8,
+                       combine_dtype=torch.float16, device="cpu")
     with pytest.raises(ValueError):
         CollectiveEpOp(hidden_dim=256, topk=2, num_experts_per_rank=4, max_num_inp_token_per_rank=8,
                        dispatch_quant_format="fp4", device="cpu")
