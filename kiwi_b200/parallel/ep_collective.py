@@ -17,8 +17,9 @@ Semantics, as KiwiEpOp:
   routes at least one of its top-k experts to this rank, in (source rank,
   token) order; ``out`` in the wire format (bf16, or float8_e4m3fn with fp32
   1x128 scales in ``out_scales``), ``out_weights`` / ``out_indices`` the token's
-  full top-k weights and global expert ids.  Quantisation happens here, so
-  ``scales`` is accepted and ignored.
+  full top-k weights and global expert ids.  bf16 input is quantised here
+  (``scales`` ignored); float8_e4m3fn input with per-token fp32 ``scales``
+  [T, S] (the reference's pre-quantised contract) travels unchanged.
 * ``combine(input, weights, indices, out)`` returns ``(out, None)``: row i of
   ``input`` goes back to the rank and token it came from, and each token's rows
   are summed in fp32 (no routing weights, as MORI); tokens routed nowhere get
@@ -125,7 +126,13 @@ class CollectiveEpOp:
         send_counts = torch.bincount(order_dest, minlength=self.world_size)
         recv_counts = self._a2a(send_counts.view(-1, 1), [1] * self.world_size, [1] * self.world_size).view(-1)
         send_counts, recv_counts = send_counts.tolist(), recv_counts.tolist()
-        if self._quant == "fp8":
+        if x.dtype == torch.float8_e4m3fn:
+            # Pre-quantised by the caller (the reference's dispatch contract): codes
+            # and the caller's per-token scales travel unchanged.
+            if self._quant != "fp8" or scales is None or scales.shape[0] != t:
+                raise ValueError("FP8 input needs an FP8 op and per-token scales [T, S]")
+            rows, row_scales = x[order_tok], scales.to(self.device, torch.float32).reshape(t, -1)[order_tok]
+        elif self._quant == "fp8":
             codes, sc = moe_model.quant_fp8_codes(x)
             rows, row_scales = codes[order_tok], sc[order_tok]
         else:

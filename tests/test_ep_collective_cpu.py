@@ -120,6 +120,23 @@ def test_float32_combine_sums_exactly():
     assert res.dtype == torch.float32 and torch.equal(res, rows)  # world of 1: one row per token
 
 
+def test_prequantised_fp8_input_travels_unchanged():
+    op = CollectiveEpOp(hidden_dim=HIDDEN, topk=TOPK, num_experts_per_rank=EPR, max_num_inp_token_per_rank=TOKENS,
+                        dispatch_quant_format="fp8", device="cpu")
+    x, idx, w = inputs(0, 1)
+    codes = (torch.randn(TOKENS, HIDDEN) * 50).to(torch.float8_e4m3fn)
+    scales = torch.rand(TOKENS, 4) + 0.1  # the caller's own scale layout (4 per row here)
+    out, _, sc, _, cnt = op.dispatch(codes, w, scales, idx)
+    n = int(cnt.item())
+    assert torch.equal(out[:n].view(torch.uint8), codes.view(torch.uint8)) and torch.equal(sc[:n], scales)
+    with pytest.raises(ValueError):
+        op.dispatch(codes, w, None, idx)
+    bf16_op = CollectiveEpOp(hidden_dim=HIDDEN, topk=TOPK, num_experts_per_rank=EPR,
+                             max_num_inp_token_per_rank=TOKENS, device="cpu")
+    with pytest.raises(ValueError):
+        bf16_op.dispatch(codes, w, scales, idx)
+
+
 def test_constructor_checks():
     with pytest.raises(TypeError):
         CollectiveEpOp(0, 1, 256)
