@@ -11,11 +11,13 @@ Exposes the module-level API of the reference's ``kiwi_ep_ext``
 ``recommended_num_blocks``, ``recommended_runtime_defaults``.  The
 reference's ``LciContext`` runtime guard becomes a no-op context manager that
 initialises the process group from the launcher's environment (torchrun,
-mpirun or srun variables).
+mpirun or srun variables).  ``CollectiveEpOp`` is the same operator contract
+over NCCL all-to-all, for ranks that span nodes.
 """
 from ..utils import dist as _dist
 from .ep import (KiwiEpOp, barrier, get_hca_name_for_current_gpu, get_hca_name_for_gpu, get_nranks, get_rank,
                  recommended_num_blocks, recommended_runtime_defaults)
+from .ep_collective import CollectiveEpOp
 
 
 class LciContext:
@@ -33,5 +35,5 @@ class LciContext:
         return False
 
 
-__all__ = ["KiwiEpOp", "LciContext", "barrier", "get_rank", "get_nranks", "get_hca_name_for_gpu",
+__all__ = ["KiwiEpOp", "CollectiveEpOp", "LciContext", "barrier", "get_rank", "get_nranks", "get_hca_name_for_gpu",
            "get_hca_name_for_current_gpu", "recommended_num_blocks", "recommended_runtime_defaults"]
