@@ -208,6 +208,20 @@ class CollectiveEpOp:
         """Source position of each row the last dispatch received (see decode_send_flat_idx)."""
         return self._src_pos if self._src_pos is not None else torch.empty(0, dtype=torch.int64)
 
+    def get_registered_combine_input_buffer(self, combine_dtype=None, hidden_dim=-1):
+        """Operator-owned [max_num_tokens_to_recv(), hidden] buffer in the
+        combine dtype, for expert outputs handed to combine() without a copy."""
+        dt = self._combine_dtype if combine_dtype is None else combine_dtype
+        if dt != self._combine_dtype:
+            raise ValueError("combine_dtype must be the op's combine dtype")
+        if hidden_dim > 0 and hidden_dim != self.hidden_dim:
+            raise ValueError("get_registered_combine_input_buffer hidden_dim must match the configured hidden_dim")
+        buf = getattr(self, "_combine_in", None)
+        if buf is None:
+            buf = self._combine_in = torch.empty(self.max_num_tokens_to_recv(), self.hidden_dim, dtype=dt,
+                                                 device=self.device)
+        return buf
+
     def launch_policy(self, num_tokens):
         return {"num_tokens": int(num_tokens), "transport": "torch.distributed all_to_all",
                 "backend": dist.get_backend(self.group) if dist.is_initialized() else "none"}

@@ -137,6 +137,21 @@ def test_prequantised_fp8_input_travels_unchanged():
         bf16_op.dispatch(codes, w, scales, idx)
 
 
+def test_registered_combine_buffer():
+    op = CollectiveEpOp(hidden_dim=HIDDEN, topk=TOPK, num_experts_per_rank=EPR, max_num_inp_token_per_rank=TOKENS,
+                        device="cpu")
+    buf = op.get_registered_combine_input_buffer(torch.bfloat16)
+    assert tuple(buf.shape) == (TOKENS, HIDDEN) and buf is op.get_registered_combine_input_buffer()
+    x, idx, w = inputs(0, 1)
+    out, _, _, _, cnt = op.dispatch(x, w, None, idx)
+    n = int(cnt.item())
+    buf[:n].copy_(out[:n])
+    res, _ = op.combine(buf)
+    assert torch.equal(res, x)
+    with pytest.raises(ValueError):
+        op.get_registered_combine_input_buffer(torch.float32)
+
+
 def test_constructor_checks():
     with pytest.raises(TypeError):
         CollectiveEpOp(0, 1, 256)
