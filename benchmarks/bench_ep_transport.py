@@ -29,6 +29,7 @@ sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
 import torch  # noqa: E402
 
 from kiwi_b200.parallel.ep import KiwiEpOp  # noqa: E402
+from kiwi_b200.parallel.ep_collective import CollectiveEpOp  # noqa: E402
 from kiwi_b200.utils import dist as kdist  # noqa: E402
 
 
@@ -51,6 +52,35 @@ def time_graph(g, iters):
     return kdist.max_over_ranks(s.elapsed_time(e) * 1e3 / iters)
 
 
+def eager_and_report(op, dispatch, combine, args, rank, world):
+    """CollectiveEpOp: dispatch and combine timed eagerly, events around each call, max over ranks."""
+    s_d, e_d = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s_c, e_c = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    d_ms = c_ms = 0.0
+    kdist.barrier()
+    torch.cuda.synchronize()
+    for _ in range(args.iters):
+        s_d.record()
+        cnt = dispatch()[4]
+        e_d.record()
+        s_c.record()
+        combine()
+        e_c.record()
+        torch.cuda.synchronize()
+        d_ms += s_d.elapsed_time(e_d)
+        c_ms += s_c.elapsed_time(e_c)
+    res = {"dispatch_us": kdist.max_over_ranks(d_ms * 1e3 / args.iters),
+           "combine_us": kdist.max_over_ranks(c_ms * 1e3 / args.iters)}
+    if rank == 0:
+        print("RESULT " + json.dumps({"bench": "ep_transport", "transport": "collective", "world": world,
+                                      "dtype": args.dtype, "hidden": args.hidden, "tokens_per_rank": args.tokens,
+                                      "experts_per_rank": args.experts_per_rank, "topk": args.topk,
+                                      "iters": args.iters, "recv_tokens_rank0": int(cnt.item()), **res,
+                                      "split_e2e_us": res["dispatch_us"] + res["combine_us"],
+                                      "timing": "eager, CUDA events, max over ranks"}), flush=True)
+    kdist.barrier()
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     ap.add_argument("--hidden", type=int, default=7168)
@@ -60,13 +90,17 @@ def main():
     ap.add_argument("--dtype", default="bf16", choices=("bf16", "fp8"))
     ap.add_argument("--iters", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--transport", default="nvlink", choices=("nvlink", "collective"),
+                    help="KiwiEpOp (NVLink stores, CUDA graphs) or CollectiveEpOp (NCCL all-to-all, timed eagerly: "
+                         "it reads the exchanged counts on the host)")
     args = ap.parse_args()
 
     rank, world = kdist.init()
     dev = torch.device("cuda", torch.cuda.current_device())
     dtype = torch.bfloat16 if args.dtype == "bf16" else torch.float8_e4m3fn
-    op = KiwiEpOp(hidden_dim=args.hidden, topk=args.topk, num_experts_per_rank=args.experts_per_rank,
-                  max_num_inp_token_per_rank=args.tokens, dispatch_dtype=dtype)
+    op_cls = KiwiEpOp if args.transport == "nvlink" else CollectiveEpOp
+    op = op_cls(hidden_dim=args.hidden, topk=args.topk, num_experts_per_rank=args.experts_per_rank,
+                max_num_inp_token_per_rank=args.tokens, dispatch_dtype=dtype)
     gen = torch.Generator().manual_seed(1234 + rank)
     experts = args.experts_per_rank * world
     idx, w = random_topk(args.tokens, experts, args.topk, gen, dev)
@@ -86,6 +120,10 @@ def main():
     torch.cuda.synchronize()
     op.check()
     kdist.barrier()
+
+    if args.transport == "collective":
+        eager_and_report(op, dispatch, combine, args, rank, world)
+        return
 
     side = torch.cuda.Stream()
     side.wait_stream(torch.cuda.current_stream())
