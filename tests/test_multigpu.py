@@ -101,6 +101,35 @@ def _ep_layer(rank, world, quant, fused=True):
         assert err <= rel * ref.abs().max().item() + 1e-3, (rank, step, err)
 
 
+def _collective_vs_nvlink(rank, world):
+    """CollectiveEpOp over NCCL and KiwiEpOp over NVLink deliver the same rows,
+    in the same (source rank, token) order, and combine to the same sums."""
+    from kiwi_b200.models import moe
+    from kiwi_b200.parallel.ep import KiwiEpOp
+    from kiwi_b200.parallel.ep_collective import CollectiveEpOp
+
+    kw = dict(hidden_dim=512, topk=3, num_experts_per_rank=4, max_num_inp_token_per_rank=48)
+    a, b = KiwiEpOp(**kw), CollectiveEpOp(**kw)
+    for step in range(2):
+        g = torch.Generator(device="cuda").manual_seed(10 * rank + step)
+        t = 48 - 8 * step
+        x = torch.randn(t, 512, device="cuda", generator=g).bfloat16()
+        idx, w = moe.route_reference(torch.randn(t, 4 * world, device="cuda", generator=g), 3)
+        ra, wa, _, ia, ca = a.dispatch(x, w, None, idx)
+        rb, wb, _, ib, cb = b.dispatch(x, w, None, idx)
+        n = int(ca.item())
+        assert n == int(cb.item()), (rank, step, n, int(cb.item()))
+        assert torch.equal(ra[:n], rb[:n]) and torch.equal(ia[:n], ib[:n]) and torch.allclose(wa[:n], wb[:n])
+        assert a.get_dispatch_src_token_pos().tolist() == b.get_dispatch_src_token_pos().tolist()
+        oa, _ = a.combine(ra[:n].clone(), None, idx)
+        ob, _ = b.combine(rb[:n].clone(), None, idx)
+        torch.cuda.synchronize()
+        a.check()
+        assert torch.equal(oa[:t], ob[:t]), (rank, step)
+        a.reset()
+        b.reset()
+
+
 def _collectives(rank, world):
     from kiwi_b200.parallel.collectives import DeviceCollectives
 
@@ -167,6 +196,10 @@ def test_ep_layer_world4():
     if _ngpu() < 4:
         pytest.skip("needs 4 GPUs")
     _run(_ep_layer, 4, "fp8")
+
+
+def test_collective_ep_op_matches_the_nvlink_op_2():
+    _run(_collective_vs_nvlink, 2)
 
 
 def test_device_collectives_2():
