@@ -36,6 +36,7 @@ import torch
 import torch.distributed as dist
 
 from ..models import moe as moe_model
+from ..ops import ExpertFFN
 from ..utils import dist as kdist
 
 _FORMATS = {"none": "none", "fp8": "fp8"}
@@ -230,4 +231,71 @@ class CollectiveEpOp:
         """Nothing to check: errors surface as exceptions of the collectives."""
 
 
-__all__ = ["CollectiveEpOp"]
+class CollectiveMoE:
+    """One rank's expert-parallel MoE layer over :class:`CollectiveEpOp`.
+
+    The same layer as :class:`kiwi_b200.parallel.ep.ExpertParallelMoE` (top-k
+    softmax routing, dispatch in ``cfg.quant`` = "none" or "fp8", each local
+    expert's SwiGLU FFN, routing-weighted sum over the top-k experts), for ranks
+    that do not share one NVSwitch domain: rows move with all-to-all, and each
+    rank sums the contributions of its own experts to a received token before
+    the token goes back, so one row per (token, destination rank) travels each
+    way.  The experts run :class:`kiwi_b200.ops.ExpertFFN` (the tcgen05 grouped
+    GEMM on CUDA tensors, its fp32 reference in CPU processes).  Collective:
+    every rank of the group calls forward in the same order."""
+
+    def __init__(self, cfg, group=None, max_tokens=None, weights=None, device=None, combine_dtype=torch.bfloat16):
+        if cfg.quant not in ("none", "fp8"):
+            raise ValueError("CollectiveMoE carries bf16 ('none') or FP8 rows")
+        world = kdist.world_size(group)
+        if cfg.num_experts % world:
+            raise ValueError("num_experts must be divisible by the world size")
+        self.cfg = cfg
+        self.max_tokens = int(max_tokens or cfg.tokens_per_rank)
+        self.experts_per_rank = cfg.num_experts // world
+        self.op = CollectiveEpOp(hidden_dim=cfg.hidden, topk=cfg.topk, num_experts_per_rank=self.experts_per_rank,
+                                 max_num_inp_token_per_rank=self.max_tokens, combine_dtype=combine_dtype,
+                                 group=group, dispatch_quant_format=cfg.quant, device=device)
+        self.device, self.rank, self.world = self.op.device, self.op.rank, self.op.world_size
+        if weights is None:
+            weights = moe_model.local_expert_weights(cfg, self.rank, self.world, self.device)
+        self.w13, self.w2 = weights
+        max_pairs = self.world * self.max_tokens * min(cfg.topk, self.experts_per_rank)
+        self.experts = ExpertFFN(self.w13, self.w2, self.experts_per_rank, max_pairs)
+        self._scale = torch.zeros(max(max_pairs, 1), dtype=torch.float32, device=self.device)
+
+    def forward(self, x, router_logits):
+        """x [T, hidden] bf16, router_logits [T, num_experts] -> [T, hidden] (combine dtype)."""
+        idx, w = moe_model.route_reference(router_logits.to(self.device), self.cfg.topk)
+        return self.forward_routed(x, idx, w)
+
+    __call__ = forward
+
+    def forward_routed(self, x, idx, w):
+        """Same layer with precomputed routing (idx [T, k] global expert ids, w [T, k])."""
+        rows, rw, scales, ridx, _ = self.op.dispatch(x, w, None, idx)
+        n, h = rows.shape
+        if scales is not None:  # FP8 codes x 1x128 scales -> bf16 operand rows
+            rows = (rows.float().view(n, h // 128, 128) * scales.view(n, -1, 1)).view(n, h)
+        local = ridx.long() - self.rank * self.experts_per_rank
+        r, s = ((local >= 0) & (local < self.experts_per_rank)).nonzero(as_tuple=True)
+        e = local[r, s]
+        order = torch.argsort(e, stable=True)
+        r, s, e = r[order], s[order], e[order]
+        p = r.numel()
+        counts = torch.bincount(e, minlength=self.experts_per_rank).to(torch.int32)
+        self.experts.input_buffer()[:p].copy_(rows[r])
+        self._scale[:p].copy_(rw[r, s])
+        y = self.experts(counts, self._scale)
+        partial = torch.zeros(n, h, dtype=torch.float32, device=self.device)
+        if p:
+            partial.index_add_(0, r, y[:p].float())
+        out, _ = self.op.combine(partial)
+        return out
+
+    def check(self):
+        """Raises if an expert GEMM reported an error (synchronises)."""
+        self.experts.check()
+
+
+__all__ = ["CollectiveEpOp", "CollectiveMoE"]

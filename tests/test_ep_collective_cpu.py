@@ -167,3 +167,67 @@ def test_constructor_checks():
     op = CollectiveEpOp(hidden_dim=256, topk=2, num_experts_per_rank=4, max_num_inp_token_per_rank=8, device="cpu")
     with pytest.raises(RuntimeError):
         op.combine(torch.zeros(1, 256).bfloat16())
+
+
+# -- CollectiveMoE: the whole layer over the all-to-all transport ---------------------------------
+
+def _moe_cfg(world, quant):
+    return moe.MoEConfig(hidden=256, ffn=128, num_experts=3 * world, topk=2, tokens_per_rank=20, quant=quant,
+                         name="t")
+
+
+def check_moe(rank, world, quant):
+    from kiwi_b200.parallel.ep_collective import CollectiveMoE
+
+    cfg = _moe_cfg(world, quant)
+    layer = CollectiveMoE(cfg, device="cpu")
+    for step in range(2):
+        x, logits = moe.synthetic_inputs(cfg, rank, "cpu", tokens=20 - 6 * step, step=step)
+        out = layer(x, logits)
+        idx, w = moe.route_reference(logits, cfg.topk)
+        ref = moe.moe_reference(cfg, x, idx, w, device="cpu")
+        err = (out.float() - ref).abs().max().item()
+        assert out.shape == ref.shape and err <= 2e-2 * ref.abs().max().item() + 1e-3, (rank, step, err)
+
+
+@pytest.mark.parametrize("quant", ["none", "fp8"])
+def test_moe_layer_world_of_one(quant):
+    check_moe(0, 1, quant)
+
+
+def _moe_member(rank, port, quant, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE="2",
+                      LOCAL_RANK=str(rank))
+    try:
+        from kiwi_b200.utils import dist as kdist
+
+        kdist.init(backend="gloo", timeout_s=30.0, device=False)
+        check_moe(rank, 2, quant)
+        kdist.dist.destroy_process_group()
+        q.put((rank, "ok"))
+    except Exception as e:  # noqa: BLE001 - reported to the parent
+        import traceback
+
+        q.put((rank, f"{type(e).__name__}: {e}\n{traceback.format_exc()[-2000:]}"))
+
+
+def test_moe_layer_two_gloo_ranks():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    ps = [ctx.Process(target=_moe_member, args=(r, port, "fp8", q)) for r in range(2)]
+    for p in ps:
+        p.start()
+    got = dict(q.get(timeout=180) for _ in ps)
+    for p in ps:
+        p.join(timeout=30)
+    assert got == {0: "ok", 1: "ok"}, got
+
+
+def test_moe_layer_rejects_nvfp4():
+    from kiwi_b200.parallel.ep_collective import CollectiveMoE
+
+    with pytest.raises(ValueError):
+        CollectiveMoE(_moe_cfg(1, "nvfp4"), device="cpu")

@@ -317,3 +317,22 @@ def test_collective_op_matches_the_nvlink_op():
     torch.cuda.synchronize()
     a.check()
     assert torch.equal(oa, ob) and torch.equal(oa, x)
+
+
+@pytest.mark.parametrize("quant", ["none", "fp8"])
+def test_collective_moe_layer_on_one_gpu(quant):
+    """CollectiveMoE (all-to-all transport + the tcgen05 expert FFN) against the
+    fp32 layer reference."""
+    from kiwi_b200.parallel.ep_collective import CollectiveMoE
+
+    cfg = moe.MoEConfig(hidden=512, ffn=256, num_experts=8, topk=2, tokens_per_rank=64, quant=quant, name="t")
+    layer = CollectiveMoE(cfg)
+    assert layer.device.type == "cuda"
+    for step in range(2):
+        x, logits = moe.synthetic_inputs(cfg, 0, "cuda", tokens=64 - 20 * step, step=step)
+        out = layer(x, logits)
+        torch.cuda.synchronize()
+        layer.check()
+        idx, w = moe.route_reference(logits, cfg.topk)
+        ref = moe.moe_reference(cfg, x, idx, w, device=x.device)
+        assert (out.float() - ref).abs().max().item() <= 2e-2 * ref.abs().max().item() + 1e-3

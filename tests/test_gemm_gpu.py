@@ -105,3 +105,24 @@ def test_grouped_gemm_large_rows(pair):
     torch.cuda.synchronize()
     ref = _ref(a, b, counts, n, False)
     assert (out.float() - ref).abs().max().item() <= 2e-2 * ref.abs().max().item() + 1e-2
+
+
+@pytest.mark.parametrize("swiglu", [False, True])
+def test_ops_plan_runs_the_kernel_and_matches_its_reference(swiglu):
+    """kiwi_b200.ops.GroupedGemm on CUDA tensors (the tcgen05 kernel) against
+    kiwi_b200.ops.grouped_gemm_reference, the fp32 path CPU tensors take."""
+    from kiwi_b200.ops import GroupedGemm, grouped_gemm_reference
+
+    torch.manual_seed(5)
+    counts, n, k = [64, 0, 130], 512, 256
+    rows = sum(counts)
+    a = (torch.randn(rows, k, device="cuda") * 0.5).bfloat16()
+    b = (torch.randn(len(counts) * n, k, device="cuda") * 0.05).bfloat16()
+    scale = torch.rand(rows, device="cuda") + 0.5
+    plan = GroupedGemm(a, b, len(counts))
+    assert plan._plan is not None  # the native kernel, not the reference
+    out = plan(counts, swiglu=swiglu, row_scale=scale)
+    torch.cuda.synchronize()
+    plan.check()
+    ref = grouped_gemm_reference(a, b, counts, swiglu, scale)
+    assert (out[:rows].float() - ref).abs().max().item() <= 2e-2 * ref.abs().max().item() + 1e-2

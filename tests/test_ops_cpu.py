@@ -1,0 +1,74 @@
+"""kiwi_b200.ops on CPU tensors: the grouped GEMM's fp32 restatement against a
+plain per-group matmul, and the expert FFN against the MoE reference's math."""
+import pytest
+import torch
+import torch.nn.functional as F
+
+from kiwi_b200.models import moe
+from kiwi_b200.ops import ExpertFFN, GroupedGemm, grouped_gemm, grouped_gemm_reference
+
+
+def _plain(a, b, counts, swiglu, row_scale):
+    n = b.shape[0] // len(counts)
+    outs, off = [], 0
+    for g, c in enumerate(counts):
+        y = a[off:off + c].double() @ b[g * n:(g + 1) * n].double().t()
+        if swiglu:
+            y = torch.cat([F.silu(y[:, t:t + 128]) * y[:, t + 128:t + 256] for t in range(0, n, 256)], 1)
+        if row_scale is not None:
+            y = y * row_scale[off:off + c].double()[:, None]
+        outs.append(y)
+        off += c
+    return torch.cat(outs)
+
+
+@pytest.mark.parametrize("swiglu", [False, True])
+@pytest.mark.parametrize("counts", [[5, 0, 17], [0, 0], [33]])
+def test_reference_matches_per_group_matmul(counts, swiglu):
+    torch.manual_seed(0)
+    rows, k, n = sum(counts), 64, 512
+    a = torch.randn(max(rows, 1), k).bfloat16()
+    b = (torch.randn(len(counts) * n, k) * 0.1).bfloat16()
+    scale = torch.rand(max(rows, 1)) + 0.5
+    got = grouped_gemm_reference(a, b, counts, swiglu, scale)
+    assert got.shape == (rows, n // 2 if swiglu else n)
+    if rows:
+        assert torch.allclose(got.double(), _plain(a, b, counts, swiglu, scale), rtol=1e-5, atol=1e-5)
+
+
+def test_plan_on_cpu_tensors_writes_only_the_counted_rows():
+    torch.manual_seed(1)
+    a = torch.randn(12, 64).bfloat16()
+    b = (torch.randn(2 * 256, 64) * 0.1).bfloat16()
+    out = torch.full((12, 256), 7.0).bfloat16()
+    GroupedGemm(a, b, 2)([3, 4], out)
+    ref = grouped_gemm_reference(a[:7], b, [3, 4]).bfloat16()
+    assert torch.equal(out[:7], ref) and (out[7:] == 7).all()
+    one = grouped_gemm(a, b, torch.tensor([3, 4]))
+    assert torch.equal(one[:7], ref)
+    with pytest.raises(ValueError):
+        GroupedGemm(a, b[:-1], 2)
+
+
+def test_expert_ffn_matches_the_moe_reference():
+    cfg = moe.MoEConfig(hidden=256, ffn=128, num_experts=3, topk=1, tokens_per_rank=8, quant="none", name="t")
+    w13, w2 = moe.local_expert_weights(cfg, 0, 1, "cpu")
+    ffn = ExpertFFN(w13, w2, 3, 16)
+    torch.manual_seed(2)
+    x = torch.randn(10, 256).bfloat16()
+    counts = [4, 0, 6]
+    scale = torch.rand(16)
+    ffn.input_buffer()[:10].copy_(x)
+    y = ffn(torch.tensor(counts), scale)[:10].float()
+    off = 0
+    for e, c in enumerate(counts):
+        if c == 0:
+            continue
+        g, u, d = moe.expert_weights(cfg, e, "cpu")
+        a = x[off:off + c].float()
+        hid = (F.silu(a @ g.float().t()) * (a @ u.float().t())).bfloat16().float()
+        want = (hid @ d.float().t()) * scale[off:off + c, None]
+        assert (y[off:off + c] - want).abs().max().item() <= 1e-2 * want.abs().max().item() + 1e-4
+        off += c
+    with pytest.raises(ValueError):
+        ExpertFFN(w13, w2[:-1], 3, 4)
