@@ -1,10 +1,13 @@
 // Python bindings of the sm_100a compute ops (kiwi_b200._C.ops).
 #include <ATen/cuda/CUDAContext.h>
+#include <algorithm>
+#include <c10/cuda/CUDAGuard.h>
 #include <pybind11/pybind11.h>
 #include <pybind11/stl.h>
 #include <torch/extension.h>
 
 #include "kiwi/gemm/grouped_gemm.hpp"
+#include "kiwi/ops/rows.hpp"
 
 namespace py = pybind11;
 using namespace kiwi;
@@ -100,6 +103,62 @@ private:
     CUtensorMap tmap_a_, tmap_b_, tmap_b_half_, tmap_a32_, tmap_b32_;
 };
 
+void check_rows_tensor(const torch::Tensor& t, const char* what) {
+    TORCH_CHECK(t.is_cuda() && t.dim() == 2 && t.is_contiguous(), what, " must be a contiguous 2-D CUDA tensor");
+    TORCH_CHECK(reinterpret_cast<uintptr_t>(t.data_ptr()) % 16 == 0, what, " must start on a 16-byte boundary");
+}
+
+const int32_t* index_ptr(const py::object& idx, int64_t rows, const torch::Device& dev, const char* what) {
+    if (idx.is_none()) return nullptr;
+    torch::Tensor t = idx.cast<torch::Tensor>();
+    TORCH_CHECK(t.device() == dev && t.scalar_type() == torch::kInt32 && t.is_contiguous() && t.numel() >= rows,
+                what, " must be a contiguous int32 tensor on the rows' device with at least `rows` entries");
+    return t.data_ptr<int32_t>();
+}
+
+void check_error_word(const torch::Tensor& e, const torch::Device& dev) {
+    TORCH_CHECK(e.device() == dev && e.scalar_type() == torch::kInt32 && e.numel() >= 1,
+                "error must be an int32 tensor on the rows' device");
+}
+
+void rows_copy_py(torch::Tensor src, torch::Tensor dst, py::object src_idx, py::object dst_idx, int64_t rows,
+                  torch::Tensor error, int grid) {
+    check_rows_tensor(src, "src");
+    check_rows_tensor(dst, "dst");
+    TORCH_CHECK(src.device() == dst.device(), "src and dst must be on one device");
+    const int64_t row_bytes = src.size(1) * src.element_size();
+    TORCH_CHECK(row_bytes == dst.size(1) * dst.element_size() && row_bytes % 16 == 0,
+                "src and dst rows must have the same size, a multiple of 16 bytes");
+    if (rows < 0) {
+        if (!src_idx.is_none()) rows = src_idx.cast<torch::Tensor>().numel();
+        else if (!dst_idx.is_none()) rows = dst_idx.cast<torch::Tensor>().numel();
+        else rows = std::min(src.size(0), dst.size(0));
+    }
+    TORCH_CHECK(!src_idx.is_none() || rows <= src.size(0), "rows exceeds src without a source index");
+    TORCH_CHECK(!dst_idx.is_none() || rows <= dst.size(0), "rows exceeds dst without a destination index");
+    const c10::cuda::CUDAGuard guard(src.device());
+    check_error_word(error, src.device());
+    ops::rows_copy(src.data_ptr(), dst.data_ptr(), index_ptr(src_idx, rows, src.device(), "src_idx"),
+                   index_ptr(dst_idx, rows, src.device(), "dst_idx"), rows, row_bytes, src.size(0), dst.size(0),
+                   reinterpret_cast<uint32_t*>(error.data_ptr<int32_t>()), grid, cur_stream());
+}
+
+void rows_accumulate_py(torch::Tensor src, torch::Tensor out, torch::Tensor map, torch::Tensor error, int grid) {
+    check_rows_tensor(src, "src");
+    check_rows_tensor(out, "out");
+    TORCH_CHECK(src.scalar_type() == torch::kBFloat16 && out.scalar_type() == torch::kBFloat16, "bf16 rows only");
+    TORCH_CHECK(src.size(1) == out.size(1) && src.size(1) % 8 == 0, "src and out share hidden, a multiple of 8");
+    TORCH_CHECK(map.device() == src.device() && out.device() == src.device() && map.scalar_type() == torch::kInt32 &&
+                    map.dim() == 2 && map.is_contiguous() && map.size(0) <= out.size(0),
+                "map must be a contiguous int32 [tokens, k] tensor on src's device, tokens <= out rows");
+    TORCH_CHECK(map.size(1) >= 1 && map.size(1) <= ops::kRowsMaxK, "k must be in [1, ", ops::kRowsMaxK, "]");
+    const c10::cuda::CUDAGuard guard(src.device());
+    check_error_word(error, src.device());
+    ops::rows_accumulate_bf16(src.data_ptr(), out.data_ptr(), map.data_ptr<int32_t>(), map.size(0),
+                              static_cast<int>(map.size(1)), src.size(1), src.size(0),
+                              reinterpret_cast<uint32_t*>(error.data_ptr<int32_t>()), grid, cur_stream());
+}
+
 }  // namespace
 
 void register_ops(py::module_& m) {
@@ -124,6 +183,13 @@ void register_ops(py::module_& m) {
         return py::make_tuple(i.local_bytes, i.registers, i.smem_bytes);
     });
     o.def("num_sms", &gemm::num_sms);
+    o.def("rows_copy", &rows_copy_py, py::arg("src"), py::arg("dst"), py::arg("src_idx") = py::none(),
+          py::arg("dst_idx") = py::none(), py::arg("rows") = -1, py::arg("error"), py::arg("grid") = 0,
+          "dst[dst_idx[i]] = src[src_idx[i]] (identity where an index is None), i < rows; negative indices skip "
+          "the row, out-of-range ones set bits of `error` (int32[1]) and skip it.  Current stream.");
+    o.def("rows_accumulate", &rows_accumulate_py, py::arg("src"), py::arg("out"), py::arg("map"), py::arg("error"),
+          py::arg("grid") = 0,
+          "out[t] = sum_j src[map[t, j]] (bf16 rows, fp32 sums); negative entries are skipped.  Current stream.");
     o.def(
         "tma_load_rate",
         [](torch::Tensor t, int box_rows, int box_k, int stages, int64_t iters, int grid, bool shared_rows) {

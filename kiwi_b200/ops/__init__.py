@@ -5,11 +5,16 @@
   fused SwiGLU and per-row-scale epilogues.
 * :class:`ExpertFFN`: the local experts' SwiGLU FFN on expert-sorted rows.
 * :func:`grouped_gemm_reference`: the fp32 restatement the kernel is tested against.
+* :func:`copy_rows` / :func:`accumulate_rows`: the pack / unpack / copy and
+  top-k accumulate row patterns of EP dispatch and combine as stand-alone
+  kernels (``benchmarks/bench_ep_copy.py`` measures them against HBM).
 
 Routing and FP8 / NVFP4 quantisation run fused into the EP dispatch kernel
 (:mod:`kiwi_b200.parallel.ep`); their fp32 references are in
 :mod:`kiwi_b200.models.moe`.
 """
 from .grouped_gemm import ExpertFFN, GroupedGemm, grouped_gemm, grouped_gemm_reference
+from .rows import accumulate_rows, check_error, copy_rows
 
-__all__ = ["ExpertFFN", "GroupedGemm", "grouped_gemm", "grouped_gemm_reference"]
+__all__ = ["ExpertFFN", "GroupedGemm", "grouped_gemm", "grouped_gemm_reference", "accumulate_rows", "check_error",
+           "copy_rows"]

@@ -72,3 +72,39 @@ def test_expert_ffn_matches_the_moe_reference():
         off += c
     with pytest.raises(ValueError):
         ExpertFFN(w13, w2[:-1], 3, 4)
+
+
+def test_row_copies_on_cpu_follow_the_index_rules():
+    from kiwi_b200.ops import accumulate_rows, check_error, copy_rows
+
+    src = torch.arange(5 * 8, dtype=torch.float32).view(5, 8).bfloat16()
+    dst = torch.zeros(4, 8).bfloat16()
+    err = copy_rows(src, dst, torch.tensor([4, -1, 9, 0]), torch.tensor([0, 1, 2, 7]))
+    assert err == 1 | 2  # index 9 past src, 7 past dst: both rows skipped
+    assert torch.equal(dst[0], src[4]) and (dst[1:] == 0).all()
+    with pytest.raises(RuntimeError):
+        check_error(err)
+    check_error(0)
+    out, err = accumulate_rows(src, torch.tensor([[0, 1], [-1, -1], [2, 7]]))
+    assert err == 1 and torch.equal(out[0], (src[0].float() + src[1].float()).bfloat16())
+    assert (out[1] == 0).all() and torch.equal(out[2], src[2])
+
+
+def test_ep_copy_bench_accounting():
+    import importlib.util
+    import pathlib
+
+    path = pathlib.Path(__file__).resolve().parent.parent / "benchmarks" / "bench_ep_copy.py"
+    spec = importlib.util.spec_from_file_location("bench_ep_copy", path)
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    assert mod.algorithmic_bytes("copy", 16384, 7168, 8) == 2 * 16384 * 7168 * 2
+    assert mod.algorithmic_bytes("accumulate", 16384, 7168, 8) == (16384 + 2048) * 7168 * 2
+    src, dst, idx = mod.build("accumulate", 64, 16, 8, "cpu")
+    assert tuple(idx.shape) == (8, 8) and sorted(idx.view(-1).tolist()) == list(range(64))
+    src, dst, idx = mod.build("copy", 64, 16, 8, "cpu")
+    assert idx is None and dst.shape == src.shape
+    peak, how = mod.hbm_peak("/nonexistent/peaks.json")
+    assert (peak, how) == (mod.FALLBACK_HBM_GBS, "fallback")
+    assert mod.agree("accumulate", torch.ones(2, 2), torch.ones(2, 2) * 1.001)
+    assert not mod.agree("pack", torch.ones(2, 2), torch.ones(2, 2) * 1.001)

@@ -1,0 +1,47 @@
+"""Row-copy kernels (kiwi_b200.ops.copy_rows / accumulate_rows on CUDA tensors)
+against plain PyTorch: gather, scatter, skipped and out-of-range indices, and
+the fp32 top-k sum."""
+import pytest
+import torch
+
+from kiwi_b200 import ops
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.parametrize("hidden", [8, 7168, 7176])
+def test_gather_and_scatter_match_torch(hidden):
+    torch.manual_seed(0)
+    src = torch.randn(300, hidden, device="cuda").bfloat16()
+    perm = torch.randperm(300, device="cuda").to(torch.int32)
+    dst = torch.zeros_like(src)
+    ops.check_error(ops.copy_rows(src, dst, perm))
+    assert torch.equal(dst, src[perm.long()])
+    dst.zero_()
+    ops.check_error(ops.copy_rows(src, dst, None, perm))
+    want = torch.zeros_like(src)
+    want[perm.long()] = src
+    assert torch.equal(dst, want)
+
+
+def test_skipped_and_out_of_range_rows_are_not_written():
+    src = torch.randn(4, 64, device="cuda").bfloat16()
+    dst = torch.zeros(4, 64, device="cuda").bfloat16()
+    err = ops.copy_rows(src, dst, torch.tensor([3, -1, 4, 1], device="cuda"), torch.tensor([0, 1, 2, 9]))
+    assert int(err.item()) == 3  # source index 4 and destination index 9 are past the end
+    assert torch.equal(dst[0], src[3]) and (dst[1:] == 0).all()
+
+
+@pytest.mark.parametrize("k", [1, 3, 8])
+def test_accumulate_matches_fp32_sum(k):
+    torch.manual_seed(1)
+    src = torch.randn(97, 7168, device="cuda").bfloat16()
+    idx = torch.randint(-1, 97, (40, k), device="cuda", dtype=torch.int32)
+    out, err = ops.accumulate_rows(src, idx)
+    ops.check_error(err)
+    want = torch.zeros(40, 7168, device="cuda")
+    for j in range(k):
+        col = idx[:, j].long()
+        ok = col >= 0
+        want[ok] += src[col[ok]].float()
+    assert (out.float() - want).abs().max().item() <= 1e-2 * want.abs().max().item()
