@@ -32,6 +32,8 @@ Semantics, as KiwiEpOp:
 Per call there are four small all-to-alls (counts) plus one per payload
 tensor; every rank must call dispatch and combine in the same order.
 """
+import math
+
 import torch
 import torch.distributed as dist
 
@@ -107,7 +109,8 @@ class CollectiveEpOp:
 
     def _wire(self, t):
         """A payload tensor as bytes (all_to_all needs types every backend carries)."""
-        return t.contiguous().view(torch.uint8).view(t.shape[0], -1)
+        row_bytes = t.element_size() * math.prod(t.shape[1:])
+        return t.contiguous().view(torch.uint8).view(t.shape[0], row_bytes)
 
     # -- the contract ---------------------------------------------------------------
     def dispatch(self, input, weights, scales=None, indices=None, **_launch_kwargs):

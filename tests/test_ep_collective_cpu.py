@@ -231,3 +231,19 @@ def test_moe_layer_rejects_nvfp4():
 
     with pytest.raises(ValueError):
         CollectiveMoE(_moe_cfg(1, "nvfp4"), device="cpu")
+
+
+def test_token_sweep_including_zero():
+    """Rounds of 0 to max tokens in a row on one op (world of one)."""
+    op = CollectiveEpOp(hidden_dim=HIDDEN, topk=TOPK, num_experts_per_rank=EPR, max_num_inp_token_per_rank=TOKENS,
+                        device="cpu")
+    for t in (0, 1, 2, 13, TOKENS, 0, 5):
+        x, idx, w = inputs(t, 1, tokens=t)
+        out, ow, _, oidx, cnt = op.dispatch(x, w, None, idx)
+        assert int(cnt.item()) == t and torch.equal(out, x) and torch.equal(oidx, idx)
+        assert op.get_dispatch_src_token_pos().tolist() == list(range(t))
+        res, _ = op.combine(out)
+        assert res.shape == (t, HIDDEN) and torch.equal(res, x)
+    x, idx, w = inputs(0, 1, tokens=TOKENS + 1)
+    with pytest.raises(ValueError):
+        op.dispatch(x, w, None, idx)  # more than max_num_inp_token_per_rank

@@ -201,6 +201,29 @@ def test_kiwi_ep_op_contract(dtype):
     assert torch.equal(out, deq.bfloat16())
 
 
+def test_kiwi_ep_op_token_sweep():
+    """One op, rounds of 1 to max_num_inp_token_per_rank tokens in a row (the
+    reference's 1..256 token sweeps): every round delivers exactly its own
+    tokens, in order, and combines them back, so no round reads a stale slot."""
+    from kiwi_b200.parallel.ep import KiwiEpOp
+
+    op = KiwiEpOp(hidden_dim=256, topk=2, num_experts_per_rank=4, max_num_inp_token_per_rank=256)
+    for i, t in enumerate((1, 2, 31, 128, 255, 256, 7)):
+        g = torch.Generator(device="cuda").manual_seed(i)
+        x = torch.randn(t, 256, device="cuda", generator=g).bfloat16()
+        idx, w = moe.route_reference(torch.randn(t, 4, device="cuda", generator=g), 2)
+        rows, ow, _, oidx, cnt = op.dispatch(x, w, None, idx)
+        torch.cuda.synchronize()
+        op.check()
+        n = int(cnt.item())
+        assert n == t and torch.equal(rows[:n], x) and torch.equal(oidx[:n], idx), (t, n)
+        out, _ = op.combine(rows[:n].clone(), None, idx)
+        torch.cuda.synchronize()
+        op.check()
+        assert torch.equal(out[:t], x), t
+        op.reset()
+
+
 @pytest.mark.filterwarnings("ignore:The CUDA Graph is empty")
 @pytest.mark.parametrize("fused", [True, False])
 def test_debug_timing_spans_every_kernel_of_a_round(fused):
