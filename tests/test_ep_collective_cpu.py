@@ -247,3 +247,44 @@ def test_token_sweep_including_zero():
     x, idx, w = inputs(0, 1, tokens=TOKENS + 1)
     with pytest.raises(ValueError):
         op.dispatch(x, w, None, idx)  # more than max_num_inp_token_per_rank
+
+
+def _uneven_member(rank, port, q):
+    """Rank 0 has no tokens; rank 1 routes every token to its own experts."""
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE="2",
+                      LOCAL_RANK=str(rank))
+    try:
+        from kiwi_b200.utils import dist as kdist
+
+        kdist.init(backend="gloo", timeout_s=30.0, device=False)
+        op = CollectiveEpOp(hidden_dim=HIDDEN, topk=TOPK, num_experts_per_rank=EPR,
+                            max_num_inp_token_per_rank=TOKENS, device="cpu")
+        t = 0 if rank == 0 else 9
+        x = torch.randn(t, HIDDEN).bfloat16()
+        idx = (EPR + torch.arange(t * TOPK) % EPR).view(t, TOPK).to(torch.int32)
+        w = torch.full((t, TOPK), 1.0 / TOPK)
+        out, _, _, _, cnt = op.dispatch(x, w, None, idx)
+        assert int(cnt.item()) == (0 if rank == 0 else 9)
+        res, _ = op.combine(out)
+        assert res.shape == (t, HIDDEN) and torch.equal(res, x)
+        kdist.dist.destroy_process_group()
+        q.put((rank, "ok"))
+    except Exception as e:  # noqa: BLE001 - reported to the parent
+        import traceback
+
+        q.put((rank, f"{type(e).__name__}: {e}\n{traceback.format_exc()[-2000:]}"))
+
+
+def test_two_gloo_ranks_with_empty_sends():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    ps = [ctx.Process(target=_uneven_member, args=(r, port, q)) for r in range(2)]
+    for p in ps:
+        p.start()
+    got = dict(q.get(timeout=180) for _ in ps)
+    for p in ps:
+        p.join(timeout=30)
+    assert got == {0: "ok", 1: "ok"}, got
