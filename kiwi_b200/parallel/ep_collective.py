@@ -121,10 +121,12 @@ class CollectiveEpOp:
             raise ValueError("more tokens than max_num_inp_token_per_rank")
         idx = indices.to(self.device, torch.int64)
         w = weights.to(self.device, torch.float32)
+        if t and (int(idx.min()) < 0 or int(idx.max()) >= self.world_size * self.experts_per_rank):
+            raise ValueError("expert indices must lie in [0, world_size * num_experts_per_rank)")
         dest = idx // self.experts_per_rank                                           # [T, k]
         onehot = torch.zeros(t, self.world_size, dtype=torch.bool, device=self.device)
         if t:
-            onehot.scatter_(1, dest.clamp(0, self.world_size - 1), True)
+            onehot.scatter_(1, dest, True)
         pairs = onehot.t().nonzero()                                                   # (dest, token), dest-major
         order_dest, order_tok = pairs[:, 0], pairs[:, 1]
         send_counts = torch.bincount(order_dest, minlength=self.world_size)

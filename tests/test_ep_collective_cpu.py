@@ -288,3 +288,14 @@ def test_two_gloo_ranks_with_empty_sends():
     for p in ps:
         p.join(timeout=30)
     assert got == {0: "ok", 1: "ok"}, got
+
+
+def test_out_of_range_expert_ids_are_rejected():
+    op = CollectiveEpOp(hidden_dim=HIDDEN, topk=TOPK, num_experts_per_rank=EPR, max_num_inp_token_per_rank=TOKENS,
+                        device="cpu")
+    x, idx, w = inputs(0, 1)
+    for bad in (EPR, -1):
+        idx2 = idx.clone()
+        idx2[3, 1] = bad
+        with pytest.raises(ValueError):
+            op.dispatch(x, w, None, idx2)
