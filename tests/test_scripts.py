@@ -62,3 +62,23 @@ def test_run_suite_ends_its_process_group_on_timeout():
     code = "import json; print('RESULT ' + json.dumps({'x': 1}))"
     rc, out = run_suite.run_group([sys.executable, "-c", code], timeout_s=60)
     assert rc == 0 and run_suite.parse_results(out) == [{"x": 1}]
+
+
+def test_moe_multinode_example_on_two_gloo_ranks():
+    """examples/python/moe_multinode.py under torchrun, two CPU processes."""
+    import json
+    import socket
+    import subprocess
+
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2",
+           "--master-addr=127.0.0.1", f"--master-port={port}", "examples/python/moe_multinode.py", "--cpu",
+           "--hidden", "256", "--ffn", "128", "--tokens", "24", "--steps", "2"]
+    env = dict(os.environ, CUDA_VISIBLE_DEVICES="")
+    r = subprocess.run(cmd, cwd=ROOT, capture_output=True, text=True, timeout=300, env=env)
+    assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-2000:]
+    line = next(ln for ln in r.stdout.splitlines() if ln.startswith("RESULT "))
+    res = json.loads(line[len("RESULT "):])
+    assert res["ok"] and res["world"] == 2 and res["device"] == "cpu", res
