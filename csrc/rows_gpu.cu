@@ -12,6 +12,7 @@
 
 #include <cstdint>
 
+#include "kiwi/common.hpp"
 #include "kiwi/ops/rows.hpp"
 
 namespace kiwi::ops {
@@ -106,8 +107,8 @@ __global__ void __launch_bounds__(kThreads) rows_accumulate_kernel(const uint4* 
 int default_grid(int64_t rows, int grid) {
     if (grid > 0) return grid;
     int dev = 0, sms = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    KIWI_CUDA_CHECK(cudaGetDevice(&dev));
+    KIWI_CUDA_CHECK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
     const int64_t g = 4LL * sms;
     return static_cast<int>(rows < g ? (rows > 0 ? rows : 1) : g);
 }
@@ -120,6 +121,7 @@ void rows_copy(const void* src, void* dst, const int32_t* src_idx, const int32_t
     rows_copy_kernel<<<default_grid(rows, grid), kThreads, 0, s>>>(
         static_cast<const uint4*>(src), static_cast<uint4*>(dst), src_idx, dst_idx, rows,
         static_cast<int32_t>(row_bytes / 16), src_rows, dst_rows, error);
+    KIWI_CUDA_CHECK(cudaGetLastError());
 }
 
 void rows_accumulate_bf16(const void* src, void* out, const int32_t* map, int64_t tokens, int k, int64_t hidden,
@@ -128,6 +130,7 @@ void rows_accumulate_bf16(const void* src, void* out, const int32_t* map, int64_
     rows_accumulate_kernel<<<default_grid(tokens, grid), kThreads, 0, s>>>(
         static_cast<const uint4*>(src), static_cast<uint4*>(out), map, tokens, k, static_cast<int32_t>(hidden / 8),
         src_rows, error);
+    KIWI_CUDA_CHECK(cudaGetLastError());
 }
 
 }  // namespace kiwi::ops
