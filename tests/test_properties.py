@@ -213,3 +213,51 @@ def test_mpmc_h2d_fifo_and_full_with_stand_in_consumer(log2slots, slot_lines, op
     while model:
         assert q.host_try_pop() == model.popleft()
     assert q.host_try_pop() is None
+
+
+@settings(max_examples=40, deadline=None, suppress_health_check=[HealthCheck.too_slow])
+@given(tokens=st.integers(min_value=0, max_value=24), topk=st.integers(min_value=1, max_value=4),
+       epr=st.integers(min_value=1, max_value=6), seed=st.integers(min_value=0, max_value=2**31 - 1))
+def test_collective_ep_op_round_trips_any_routing(tokens, topk, epr, seed):
+    """World of one: any routing delivers every token once, in order, with its
+    ids and weights, and combine returns it unchanged."""
+    import torch
+
+    from kiwi_b200.parallel.ep_collective import CollectiveEpOp
+
+    topk = min(topk, epr)
+    g = torch.Generator().manual_seed(seed)
+    x = torch.randn(tokens, 128, generator=g).bfloat16()
+    idx = torch.stack([torch.randperm(epr, generator=g)[:topk] for _ in range(tokens)]) if tokens else \
+        torch.empty(0, topk, dtype=torch.int64)
+    w = torch.rand(tokens, topk, generator=g)
+    op = CollectiveEpOp(hidden_dim=128, topk=topk, num_experts_per_rank=epr, max_num_inp_token_per_rank=24,
+                        device="cpu")
+    out, ow, _, oidx, cnt = op.dispatch(x, w, None, idx)
+    assert int(cnt.item()) == tokens
+    assert torch.equal(out, x) and torch.equal(oidx, idx.to(torch.int32)) and torch.equal(ow, w)
+    res, _ = op.combine(out)
+    assert torch.equal(res, x)
+
+
+@settings(max_examples=40, deadline=None, suppress_health_check=[HealthCheck.too_slow])
+@given(counts=st.lists(st.integers(min_value=0, max_value=9), min_size=1, max_size=5), swiglu=st.booleans(),
+       seed=st.integers(min_value=0, max_value=2**31 - 1))
+def test_grouped_gemm_reference_is_a_per_group_matmul(counts, swiglu, seed):
+    import torch
+
+    from kiwi_b200.ops import grouped_gemm_reference
+
+    g = torch.Generator().manual_seed(seed)
+    rows, n, k = sum(counts), 256, 32
+    a = torch.randn(rows, k, generator=g)
+    b = torch.randn(len(counts) * n, k, generator=g)
+    got = grouped_gemm_reference(a, b, counts, swiglu)
+    off = 0
+    for e, c in enumerate(counts):
+        y = a[off:off + c] @ b[e * n:(e + 1) * n].t()
+        if swiglu:
+            y = torch.nn.functional.silu(y[:, :128]) * y[:, 128:]
+        assert torch.allclose(got[off:off + c], y, rtol=1e-5, atol=1e-4)
+        off += c
+    assert got.shape[0] == rows
