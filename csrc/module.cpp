@@ -60,6 +60,9 @@ public:
     virtual size_t progress_all(int max) = 0;
     virtual void start_threads(size_t n, std::vector<int> cpus) = 0;
     virtual void stop_threads() = 0;
+    virtual uint32_t set_active_endpoints(size_t n) = 0;
+    virtual size_t active_endpoints() const = 0;
+    virtual bool active_applied(uint32_t generation) const = 0;
     virtual uint64_t callbacks_run() const = 0;
     virtual invoke::ProgressStats stats() const = 0;
     virtual uintptr_t device_context_ptr() const = 0;
@@ -112,6 +115,9 @@ public:
         py::gil_scoped_release nogil;
         threads_.stop();
     }
+    uint32_t set_active_endpoints(size_t n) override { return threads_.set_active_endpoints(n); }
+    size_t active_endpoints() const override { return threads_.active_endpoints(); }
+    bool active_applied(uint32_t generation) const override { return threads_.active_applied(generation); }
     uint64_t callbacks_run() const override { return threads_.callbacks_run(); }
     invoke::ProgressStats stats() const override { return threads_.stats(); }
     uintptr_t device_context_ptr() const override {
@@ -308,6 +314,11 @@ PYBIND11_MODULE(_C, m) {
         .def("start_progress_threads", &KiwiContextBase::start_threads, py::arg("num_threads") = 1,
              py::arg("cpus") = std::vector<int>{})
         .def("stop_progress_threads", &KiwiContextBase::stop_threads)
+        .def("set_active_endpoints", &KiwiContextBase::set_active_endpoints, py::arg("n"),
+             "Progress threads poll endpoints [0, n) only (0 = all); a shrink drains the dropped endpoints once. "
+             "Returns the request's generation.")
+        .def_property_readonly("active_endpoints", &KiwiContextBase::active_endpoints)
+        .def("active_applied", &KiwiContextBase::active_applied, py::arg("generation"))
         .def_property_readonly("callbacks_run", &KiwiContextBase::callbacks_run)
         .def_property_readonly(
             "stats",

@@ -12,11 +12,13 @@
 // reference's variable of the same name, apps/README.md:297-300).
 #pragma once
 
+#include <algorithm>
 #include <atomic>
 #include <cstdio>
 #include <cstdlib>
 #include <exception>
 #include <functional>
+#include <memory>
 #include <mutex>
 #include <string>
 #include <thread>
@@ -67,6 +69,12 @@ public:
         hook_ = std::move(hook);
         stop_.store(false);
         error_ = nullptr;
+        {
+            std::lock_guard<std::mutex> g(seen_mu_);
+            seen_.reset(new std::atomic<uint32_t>[num_threads]);
+            for (size_t t = 0; t < num_threads; ++t) seen_[t].store(0, std::memory_order_relaxed);
+            seen_count_ = num_threads;
+        }
         for (size_t t = 0; t < num_threads; ++t) {
             std::vector<int> mine;
             if (!cpus.empty()) mine.push_back(cpus[t % cpus.size()]);
@@ -79,6 +87,43 @@ public:
         stop_.store(true);
         for (auto& th : threads_) th.join();
         threads_.clear();
+        std::lock_guard<std::mutex> g(seen_mu_);
+        seen_count_ = 0;
+    }
+
+    /// Restricts polling to the active prefix [0, n) of the endpoints (0 = all,
+    /// the default): a kernel launched with fewer blocks than the context has
+    /// endpoints leaves the rest idle, and polling them only adds latency to
+    /// the ones in use.  A larger prefix takes effect at each thread's next
+    /// sweep.  For a smaller one, each thread drains its endpoints in
+    /// [n, old prefix) once when it sees the request and then stops polling
+    /// them, so every message pushed before the call is delivered; shrink only
+    /// after the kernels pushing to those endpoints have finished.  Returns the
+    /// request's generation (see active_applied).  stop() drains every
+    /// endpoint whatever the prefix.  Counterpart of the reference's
+    /// active-queue state (apps/ep/comm/active_queue_state.hpp of
+    /// AMDResearch/kiwi: immediate grow, deferred shrink).
+    uint32_t set_active_endpoints(size_t n) {
+        const uint64_t count = std::min<uint64_t>(n, 0xffffffffull);
+        uint64_t cur = active_.load(std::memory_order_relaxed);
+        uint64_t next;
+        do {
+            next = (((cur >> 32) + 1) << 32) | count;
+        } while (!active_.compare_exchange_weak(cur, next, std::memory_order_acq_rel, std::memory_order_relaxed));
+        return static_cast<uint32_t>(next >> 32);
+    }
+
+    /// The active prefix requested last (0 = all endpoints).
+    size_t active_endpoints() const { return static_cast<size_t>(active_.load(std::memory_order_acquire) & 0xffffffffull); }
+
+    /// True once every running thread has applied request `generation` (its
+    /// drain included), or when no thread runs.
+    bool active_applied(uint32_t generation) const {
+        std::lock_guard<std::mutex> g(seen_mu_);
+        for (size_t t = 0; t < seen_count_; ++t) {
+            if (static_cast<int32_t>(seen_[t].load(std::memory_order_acquire) - generation) < 0) return false;
+        }
+        return true;
     }
 
     bool running() const { return !threads_.empty(); }
@@ -124,9 +169,30 @@ private:
             empty_.fetch_add(local_empty, std::memory_order_relaxed);
             local_sweeps = local_empty = 0;
         };
+        const size_t all = ctx_.num_endpoints();
+        auto prefix_of = [all](uint64_t word) {
+            const size_t n = static_cast<size_t>(word & 0xffffffffull);
+            return n == 0 ? all : std::min(n, all);
+        };
+        uint64_t word = active_.load(std::memory_order_acquire);
+        size_t active = prefix_of(word);
+        seen_[tid].store(static_cast<uint32_t>(word >> 32), std::memory_order_release);
         try {
             while (!stop_.load(std::memory_order_relaxed)) {
-                for (size_t i = 0; i < mine.size(); ++i) {
+                const uint64_t now = active_.load(std::memory_order_acquire);
+                if (now != word) {
+                    const size_t next = prefix_of(now);
+                    for (size_t i = 0; i < mine.size(); ++i) {  // shrink: drain what leaves the prefix
+                        if (mine[i] >= next && mine[i] < active) {
+                            callbacks_.fetch_add(ctx_.progress(mine[i]), std::memory_order_relaxed);
+                            polls[i].refresh();
+                        }
+                    }
+                    word = now;
+                    active = next;
+                    seen_[tid].store(static_cast<uint32_t>(word >> 32), std::memory_order_release);
+                }
+                for (size_t i = 0; i < mine.size() && mine[i] < active; ++i) {
                     if (polls[i].ready()) {
                         callbacks_.fetch_add(ctx_.progress(mine[i]), std::memory_order_relaxed);
                         polls[i].refresh();
@@ -153,6 +219,10 @@ private:
     std::atomic<uint64_t> callbacks_{0};
     std::atomic<uint64_t> sweeps_{0};
     std::atomic<uint64_t> empty_{0};
+    std::atomic<uint64_t> active_{0};  // (generation << 32) | prefix length (0 = all)
+    mutable std::mutex seen_mu_;
+    std::unique_ptr<std::atomic<uint32_t>[]> seen_;  // per thread: the last generation applied
+    size_t seen_count_ = 0;
     std::mutex mu_;
     std::exception_ptr error_;
 };

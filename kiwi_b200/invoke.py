@@ -79,6 +79,30 @@ class Context:
         self._ctx.stop_progress_threads()
         self._ctx.rethrow_progress_errors()
 
+    def set_active_endpoints(self, n, wait_s=None):
+        """Progress threads poll only endpoints [0, n) (0 = all, the default),
+        e.g. the endpoints of the blocks a kernel actually launches.  Growing
+        applies at the threads' next sweep; shrinking first drains the dropped
+        endpoints once (shrink only after the kernels pushing to them have
+        finished).  With ``wait_s``, waits up to that long until every running
+        thread has applied the request and raises TimeoutError otherwise.
+        Returns the request's generation."""
+        import time
+
+        gen = self._ctx.set_active_endpoints(int(n))
+        if wait_s is not None:
+            deadline = time.monotonic() + wait_s
+            while not self._ctx.active_applied(gen):
+                if time.monotonic() > deadline:
+                    raise TimeoutError("progress threads did not apply the active-endpoint request")
+                time.sleep(1e-4)
+        return gen
+
+    @property
+    def active_endpoints(self):
+        """The active prefix requested last (0 = all endpoints)."""
+        return self._ctx.active_endpoints
+
     def __enter__(self):
         return self
 

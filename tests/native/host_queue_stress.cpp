@@ -277,6 +277,53 @@ int invoke_threads() {
     return 0;
 }
 
+int invoke_active_prefix() {
+    // Producers push to every endpoint while a controller grows and shrinks the
+    // active prefix; every message must still run exactly once (a dropped
+    // endpoint keeps its messages until the prefix covers it again or stop()).
+    invoke::Context<SPSCD2HQueue> ctx(8, 16, MemKind::kHost);
+    std::vector<std::atomic<uint32_t>> next(8);
+    for (auto& n : next) n.store(0);
+    std::atomic<int> bad{0};
+    const uint8_t cb = ctx.register_callback(std::function<void(uint32_t, uint32_t)>([&](uint32_t ep, uint32_t i) {
+        if (ep >= 8 || next[ep].fetch_add(1, std::memory_order_relaxed) != i) bad.store(1);
+    }));
+    invoke::ProgressThreads<SPSCD2HQueue> threads(ctx);
+    threads.start(3);
+    const uint32_t per = 2000;
+    std::atomic<bool> done{false};
+    std::thread controller([&] {
+        const size_t cycle[] = {2, 8, 1, 5, 0, 3};
+        for (size_t k = 0; !done.load(); ++k) {
+            const uint32_t gen = threads.set_active_endpoints(cycle[k % 6]);
+            while (!threads.active_applied(gen) && !done.load()) std::this_thread::yield();
+        }
+        threads.set_active_endpoints(0);
+    });
+    std::vector<std::thread> producers;
+    for (uint32_t ep = 0; ep < 8; ++ep) {
+        producers.emplace_back([&, ep] {
+            RingWriter w = ctx.raw_queue(ep)->host_writer_any();
+            for (uint32_t i = 0; i < per; ++i) {
+                uint8_t msg[8];
+                std::memcpy(msg, &ep, 4);
+                std::memcpy(msg + 4, &i, 4);
+                while (!w.try_push(msg, sizeof(msg), cb)) std::this_thread::yield();
+            }
+        });
+    }
+    for (auto& p : producers) p.join();
+    done.store(true);
+    controller.join();
+    threads.stop();
+    threads.rethrow_if_failed();
+    if (bad.load()) return fail("active prefix order", 1, 0);
+    for (uint32_t ep = 0; ep < 8; ++ep) {
+        if (next[ep].load() != per) return fail("active prefix count", next[ep].load(), per);
+    }
+    return 0;
+}
+
 int print_formats() {
     struct F {
         const char* fmt;
@@ -475,7 +522,7 @@ int main(int argc, char** argv) {
         const char* name;
         int (*fn)();
     } cases[] = {{"spsc_d2h", spsc_d2h}, {"mpsc", mpsc_d2h}, {"spsc_h2d", spsc_h2d}, {"mpmc_push", mpmc_push}, {"mpmc", mpmc_full},
-                 {"invoke", invoke_threads},
+                 {"invoke", invoke_threads}, {"invoke_active", invoke_active_prefix},
                  {"print", print_formats}, {"fuzz", fuzz_reader}, {"fuzz_invoke", fuzz_invoke},
                  {"fds", fd_exchange}};
     int rc = 0;

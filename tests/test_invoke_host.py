@@ -206,3 +206,42 @@ extern "C" uint32_t kiwi_jit_tag(uint64_t n) { return kiwi::queue::wire_tag(n); 
     assert so.stat().st_mtime_ns == mtime  # cached
     with pytest.raises(RuntimeError, match="nvcc failed"):
         load_cuda("kiwi_jit_bad", "this is not C++", build_directory=str(tmp_path / "bad"))
+
+
+def test_progress_threads_poll_only_the_active_prefix():
+    """Endpoints past the active prefix are not polled; growing the prefix
+    reaches them; shrinking delivers what was already queued; stop() drains
+    everything (the reference's active-queue state)."""
+    import time
+
+    ctx = invoke.Context(8, 16, host_only=True)
+    got = []
+    cb = ctx.register_callback(lambda p: got.append(p[0]))
+
+    def wait_for(n):
+        deadline = time.monotonic() + 10
+        while len(got) < n and time.monotonic() < deadline:
+            time.sleep(1e-3)
+
+    ctx.set_active_endpoints(2)
+    assert ctx.active_endpoints == 2
+    ctx.start(num_threads=3, cpus=[])
+    try:
+        ctx.emulate_invoke(1, cb, b"\x01")
+        ctx.emulate_invoke(5, cb, b"\x05")  # outside the prefix
+        wait_for(1)
+        time.sleep(0.05)
+        assert got == [1]
+        ctx.set_active_endpoints(0, wait_s=10)  # all endpoints
+        wait_for(2)
+        assert got == [1, 5]
+        for ep in (3, 6, 7):
+            ctx.emulate_invoke(ep, cb, bytes([ep]))
+        ctx.set_active_endpoints(1, wait_s=10)  # shrink: the three queued messages arrive first
+        assert sorted(got) == [1, 3, 5, 6, 7]
+        ctx.emulate_invoke(4, cb, b"\x04")
+        time.sleep(0.05)
+        assert len(got) == 5
+    finally:
+        ctx.stop()
+    assert sorted(got) == [1, 3, 4, 5, 6, 7]  # the final drain covers every endpoint

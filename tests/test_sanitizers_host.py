@@ -21,7 +21,7 @@ import pytest
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 CUDA = os.environ.get("CUDA_HOME", "/usr/local/cuda")
-CASES = ["spsc_d2h", "mpsc", "spsc_h2d", "mpmc_push", "mpmc", "invoke", "print", "fuzz", "fuzz_invoke", "fds"]
+CASES = ["spsc_d2h", "mpsc", "spsc_h2d", "mpmc_push", "mpmc", "invoke", "invoke_active", "print", "fuzz", "fuzz_invoke", "fds"]
 SANITIZERS = {"thread": ["-fsanitize=thread", "-Wno-tsan"],
               "address,undefined": ["-fsanitize=address,undefined", "-fno-omit-frame-pointer",
                                     "-fno-sanitize-recover=undefined"]}
