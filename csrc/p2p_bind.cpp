@@ -114,6 +114,9 @@ void register_p2p(py::module_& m) {
             },
             "Proxy totals: control messages served, sweeps, empty endpoint polls, threads, copy-engine puts.")
         .def_property_readonly("copies_issued", &Context::copies_issued)
+        .def("set_active_queues", &Context::set_active_queues, py::arg("n"),
+             "Proxy threads serve only control queues [0, n) (0 = all); returns the request's generation.")
+        .def("active_applied", &Context::active_applied, py::arg("generation"))
         .def("ce_pingpong",
              [](Context& c, int peer, bool initiator, uint64_t bytes, uint32_t iters, uint32_t warmup,
                 uint64_t src_off, uint64_t dst_off, uint64_t flag_off, torch::Tensor lat, torch::Tensor status,

@@ -88,6 +88,10 @@ public:
     uint64_t copies_issued() const { return copies_; }
     /// Proxy-thread totals (callbacks = control messages served).
     invoke::ProgressStats proxy_stats() const { return threads_->stats(); }
+    /// Proxy threads serve only queues [0, n) (0 = all); a shrink drains the
+    /// dropped queues once (invoke::ProgressThreads::set_active_endpoints).
+    uint32_t set_active_queues(size_t n) { return threads_->set_active_endpoints(n); }
+    bool active_applied(uint32_t generation) const { return threads_->active_applied(generation); }
 
 private:
     void ce_put(const CePutDesc& d);
