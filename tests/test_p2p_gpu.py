@@ -43,6 +43,28 @@ def test_control_plane_copy_engine_puts(bytes_, n):
     assert int(heap.tensor(flag_off + 8, [1], torch.int64).item()) == 0xABCD
 
 
+def test_proxy_threads_serve_the_active_queue_prefix():
+    """Four control queues, proxies restricted to queue 0 (the one the
+    self-test kernel's single block posts on): every put is still served."""
+    C = kiwi_b200.native()
+    heap = SymmetricHeap(8 << 20)
+    ctx = C.p2p.Context(heap.native, 4, 256)
+    gen = ctx.set_active_queues(1)
+    src_off, dst_off = 1 << 20, 2 << 20
+    heap.tensor(src_off, [4096], torch.uint8).fill_(7)
+    heap.tensor(0, [512], torch.uint8).zero_()
+    status = torch.zeros(2, dtype=torch.int32, device="cuda")
+    torch.cuda.synchronize()
+    ctx.spawn_proxy_threads(2)
+    ctx.ce_put_selftest(0, src_off, dst_off, 4096, 3, 0, 256, status, 5_000_000_000)
+    torch.cuda.synchronize()
+    assert ctx.active_applied(gen)
+    ctx.join_proxy_threads()
+    assert int(status[0].item()) == 0, status
+    assert ctx.copies_issued == 3
+    assert bool((heap.tensor(dst_off, [3 * 4096], torch.uint8) == 7).all())
+
+
 def test_get_from_own_heap():
     heap = SymmetricHeap(4 << 20)
     n = 1 << 20
