@@ -24,7 +24,9 @@ Semantics, as KiwiEpOp:
   ``input`` goes back to the rank and token it came from, and each token's rows
   are summed in fp32 (no routing weights, as MORI); tokens routed nowhere get
   zeros.  Rows travel and the result is returned in ``combine_dtype``: bf16,
-  or float32 as the reference also accepts (the NVLink op combines bf16 only).
+  float32, or float8_e4m3fn (codes without scales, the sum re-quantised by a
+  saturating cast), as the reference also accepts (the NVLink op combines bf16
+  only).
 * ``get_dispatch_src_token_pos()`` encodes each received row's source as
   ``src_rank * (world * max_tokens) + token`` and ``decode_send_flat_idx``
   inverts it.
@@ -43,6 +45,15 @@ from ..utils import dist as kdist
 
 _FORMATS = {"none": "none", "fp8": "fp8"}
 _DTYPES = {torch.bfloat16: "none", torch.float8_e4m3fn: "fp8"}
+_COMBINE_DTYPES = (torch.bfloat16, torch.float32, torch.float8_e4m3fn)
+_FP8_MAX = 448.0
+
+
+def _to_combine_dtype(x, dtype):
+    """x in `dtype`; FP8 saturates at +-448 (e4m3fn has no infinity)."""
+    if dtype == torch.float8_e4m3fn and x.dtype != dtype:
+        return x.float().clamp(-_FP8_MAX, _FP8_MAX).to(dtype)
+    return x.to(dtype)
 
 
 class CollectiveEpOp:
@@ -57,8 +68,9 @@ class CollectiveEpOp:
                                   ("max_num_inp_token_per_rank", max_num_inp_token_per_rank)) if v is None]
         if missing:
             raise TypeError("CollectiveEpOp missing required arguments: " + ", ".join(missing))
-        if combine_dtype not in (torch.bfloat16, torch.float32) or str(combine_quant_format).lower() != "none":
-            raise ValueError("combine_dtype must be torch.bfloat16 or torch.float32 (combine_quant_format 'none')")
+        if combine_dtype not in _COMBINE_DTYPES or str(combine_quant_format).lower() != "none":
+            raise ValueError("combine_dtype must be torch.bfloat16, torch.float32 or torch.float8_e4m3fn "
+                             "(combine_quant_format 'none')")
         self._combine_dtype = combine_dtype
         fmt = str(dispatch_quant_format).lower()
         if fmt not in _FORMATS:
@@ -171,15 +183,16 @@ class CollectiveEpOp:
         if self._send_counts is None:
             raise RuntimeError("combine needs a prior dispatch")
         n = int(sum(self._recv_counts))
-        rows = input[:n].to(self.device, self._combine_dtype)
-        back = self._a2a(rows, self._recv_counts, self._send_counts)                   # (dest, token) order
+        rows = _to_combine_dtype(input[:n].to(self.device), self._combine_dtype)
+        back = self._a2a(self._wire(rows), self._recv_counts, self._send_counts)       # (dest, token) order
+        back = back.view(self._combine_dtype).view(back.shape[0], self.hidden_dim)
         t = self._last_tokens
         acc = torch.zeros(t, self.hidden_dim, dtype=torch.float32, device=self.device)
         if back.shape[0]:
             acc.index_add_(0, self._send_tokens, back.float())
         if out is None:
             out = torch.empty(t, self.hidden_dim, dtype=self._combine_dtype, device=self.device)
-        out[:t].copy_(acc)
+        out[:t].copy_(_to_combine_dtype(acc, out.dtype))
         self._out = out
         return out, None
 

@@ -299,3 +299,20 @@ def test_out_of_range_expert_ids_are_rejected():
         idx2[3, 1] = bad
         with pytest.raises(ValueError):
             op.dispatch(x, w, None, idx2)
+
+
+def test_fp8_combine_sums_codes_and_saturates():
+    op = CollectiveEpOp(hidden_dim=HIDDEN, topk=TOPK, num_experts_per_rank=EPR, max_num_inp_token_per_rank=TOKENS,
+                        combine_dtype=torch.float8_e4m3fn, device="cpu")
+    x, idx, w = inputs(0, 1)
+    _, _, _, _, cnt = op.dispatch(x, w, None, idx)
+    n = int(cnt.item())
+    rows = (torch.randn(n, HIDDEN) * 30).to(torch.float8_e4m3fn)
+    res, _ = op.combine(rows)
+    assert res.dtype == torch.float8_e4m3fn
+    assert torch.equal(res.view(torch.uint8), rows.view(torch.uint8))  # one row per token at world 1
+    big = torch.full((n, HIDDEN), 1000.0)  # bf16 / fp32 rows past the FP8 range saturate, never NaN
+    res, _ = op.combine(big)
+    assert (res.float() == 448.0).all()
+    buf = op.get_registered_combine_input_buffer()
+    assert buf.dtype == torch.float8_e4m3fn
