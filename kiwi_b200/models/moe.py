@@ -131,13 +131,33 @@ def quant_fp8_reference(x, block=128):
 
 def _round_fp4(v):
     """Round-to-nearest-even onto the e2m1 grid (saturating at 6)."""
-    sign = torch.sign(v)
-    a = v.abs().clamp(max=FP4_MAX)
+    codes = fp4_codes(v).long()
+    mag = FP4_VALUES.to(v.device)[codes & 7]
+    return torch.where(codes >= 8, -mag, mag)
+
+
+def fp4_codes(v):
+    """e2m1 codes (uint8, 0..15: sign in bit 3, the index into FP4_VALUES below
+    it) of v rounded to nearest-even on the e2m1 grid, saturating at +-6."""
     grid = FP4_VALUES.to(v.device)
+    a = v.float().abs().clamp(max=FP4_MAX)
     d = (a.unsqueeze(-1) - grid).abs()
-    # ties: prefer the even mantissa (grid index parity as e2m1 encodes it)
     idx = torch.argmin(d + (torch.arange(len(grid), device=v.device) % 2) * 1e-6, dim=-1)
-    return sign * grid[idx]
+    return (idx | ((v < 0).to(idx.dtype) << 3)).to(torch.uint8)
+
+
+def fp4_pack(codes):
+    """[..., 2m] e2m1 codes -> [..., m] bytes, element 2i in the low nibble."""
+    c = codes.to(torch.uint8)
+    return c[..., 0::2] | (c[..., 1::2] << 4)
+
+
+def fp4_unpack(packed):
+    """[..., m] packed e2m1 bytes -> [..., 2m] fp32 values (inverse of fp4_pack)."""
+    b = packed.view(torch.uint8)
+    codes = torch.stack([b & 0xF, b >> 4], dim=-1).flatten(-2).long()
+    mag = FP4_VALUES.to(b.device)[codes & 7]
+    return torch.where(codes >= 8, -mag, mag)
 
 
 def quant_nvfp4_reference(x, block=16):

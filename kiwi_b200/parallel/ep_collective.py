@@ -24,8 +24,9 @@ Semantics, as KiwiEpOp:
   ``input`` goes back to the rank and token it came from, and each token's rows
   are summed in fp32 (no routing weights, as MORI); tokens routed nowhere get
   zeros.  Rows travel and the result is returned in ``combine_dtype``: bf16,
-  float32, or float8_e4m3fn (codes without scales, the sum re-quantised by a
-  saturating cast), as the reference also accepts (the NVLink op combines bf16
+  float32, float8_e4m3fn or float4_e2m1fn_x2 (codes without scales, the sum
+  re-quantised with saturation; FP4 rows are hidden / 2 bytes, element 2i in
+  the low nibble), as the reference also accepts (the NVLink op combines bf16
   only).
 * ``get_dispatch_src_token_pos()`` encodes each received row's source as
   ``src_rank * (world * max_tokens) + token`` and ``decode_send_flat_idx``
@@ -45,15 +46,26 @@ from ..utils import dist as kdist
 
 _FORMATS = {"none": "none", "fp8": "fp8"}
 _DTYPES = {torch.bfloat16: "none", torch.float8_e4m3fn: "fp8"}
-_COMBINE_DTYPES = (torch.bfloat16, torch.float32, torch.float8_e4m3fn)
+_FP4 = torch.float4_e2m1fn_x2
+_COMBINE_DTYPES = (torch.bfloat16, torch.float32, torch.float8_e4m3fn, _FP4)
 _FP8_MAX = 448.0
 
 
 def _to_combine_dtype(x, dtype):
-    """x in `dtype`; FP8 saturates at +-448 (e4m3fn has no infinity)."""
+    """x in `dtype`; FP8 saturates at +-448 (e4m3fn has no infinity); FP4
+    (e2m1, two per byte, so [rows, hidden / 2]) rounds to nearest-even and
+    saturates at +-6.  FP4 input already packed passes through."""
+    if dtype == _FP4:
+        if x.dtype in (_FP4, torch.uint8):
+            return x.view(_FP4)
+        return moe_model.fp4_pack(moe_model.fp4_codes(x)).view(_FP4)
     if dtype == torch.float8_e4m3fn and x.dtype != dtype:
         return x.float().clamp(-_FP8_MAX, _FP8_MAX).to(dtype)
     return x.to(dtype)
+
+
+def _to_float(x):
+    return moe_model.fp4_unpack(x) if x.dtype == _FP4 else x.float()
 
 
 class CollectiveEpOp:
@@ -69,9 +81,11 @@ class CollectiveEpOp:
         if missing:
             raise TypeError("CollectiveEpOp missing required arguments: " + ", ".join(missing))
         if combine_dtype not in _COMBINE_DTYPES or str(combine_quant_format).lower() != "none":
-            raise ValueError("combine_dtype must be torch.bfloat16, torch.float32 or torch.float8_e4m3fn "
-                             "(combine_quant_format 'none')")
+            raise ValueError("combine_dtype must be torch.bfloat16, torch.float32, torch.float8_e4m3fn or "
+                             "torch.float4_e2m1fn_x2 (combine_quant_format 'none')")
         self._combine_dtype = combine_dtype
+        if combine_dtype == _FP4 and hidden_dim % 2:
+            raise ValueError("FP4 combine needs an even hidden_dim (two elements per byte)")
         fmt = str(dispatch_quant_format).lower()
         if fmt not in _FORMATS:
             raise ValueError(f"unsupported dispatch_quant_format {dispatch_quant_format!r}: CollectiveEpOp carries "
@@ -185,18 +199,26 @@ class CollectiveEpOp:
         n = int(sum(self._recv_counts))
         rows = _to_combine_dtype(input[:n].to(self.device), self._combine_dtype)
         back = self._a2a(self._wire(rows), self._recv_counts, self._send_counts)       # (dest, token) order
-        back = back.view(self._combine_dtype).view(back.shape[0], self.hidden_dim)
+        back = back.view(self._combine_dtype).view(back.shape[0], self._combine_cols())
         t = self._last_tokens
         acc = torch.zeros(t, self.hidden_dim, dtype=torch.float32, device=self.device)
         if back.shape[0]:
-            acc.index_add_(0, self._send_tokens, back.float())
+            acc.index_add_(0, self._send_tokens, _to_float(back))
         if out is None:
-            out = torch.empty(t, self.hidden_dim, dtype=self._combine_dtype, device=self.device)
-        out[:t].copy_(_to_combine_dtype(acc, out.dtype))
+            out = torch.empty(t, self._combine_cols(), dtype=self._combine_dtype, device=self.device)
+        res = _to_combine_dtype(acc, out.dtype)
+        if out.dtype == _FP4:  # copy_ has no FP4 kernel: move the bytes
+            out[:t].view(torch.uint8).copy_(res.view(torch.uint8))
+        else:
+            out[:t].copy_(res)
         self._out = out
         return out, None
 
     combine_send = combine
+
+    def _combine_cols(self):
+        """Columns of a combine row: hidden, or hidden / 2 bytes for FP4."""
+        return self.hidden_dim // 2 if self._combine_dtype == _FP4 else self.hidden_dim
 
     def combine_recv(self, **_kwargs):
         return (self._out[:self._last_tokens] if self._out is not None else None), None
@@ -237,7 +259,7 @@ class CollectiveEpOp:
             raise ValueError("get_registered_combine_input_buffer hidden_dim must match the configured hidden_dim")
         buf = getattr(self, "_combine_in", None)
         if buf is None:
-            buf = self._combine_in = torch.empty(self.max_num_tokens_to_recv(), self.hidden_dim, dtype=dt,
+            buf = self._combine_in = torch.empty(self.max_num_tokens_to_recv(), self._combine_cols(), dtype=dt,
                                                  device=self.device)
         return buf
 

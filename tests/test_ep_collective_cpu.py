@@ -316,3 +316,31 @@ def test_fp8_combine_sums_codes_and_saturates():
     assert (res.float() == 448.0).all()
     buf = op.get_registered_combine_input_buffer()
     assert buf.dtype == torch.float8_e4m3fn
+
+
+def test_fp4_codes_round_trip_and_pack_low_nibble_first():
+    vals = torch.tensor([0.0, 0.5, 1.0, 1.5, 2.0, 3.0, 4.0, 6.0, -0.5, -6.0, 7.0, -100.0, 0.74, 0.76, 2.5, 5.0])
+    codes = moe.fp4_codes(vals)
+    back = moe.fp4_unpack(moe.fp4_pack(codes))
+    want = torch.tensor([0.0, 0.5, 1.0, 1.5, 2.0, 3.0, 4.0, 6.0, -0.5, -6.0, 6.0, -6.0, 0.5, 1.0, 2.0, 4.0])
+    assert torch.equal(back, want)  # 0.75 -> 0.5 / 1.0 by distance; ties 2.5 -> 2, 5 -> 4 (even mantissa)
+    assert int(moe.fp4_pack(moe.fp4_codes(torch.tensor([1.0, -2.0])))[0]) == 0x2 | (0xC << 4)
+
+
+def test_fp4_combine_sums_and_requantises():
+    op = CollectiveEpOp(hidden_dim=HIDDEN, topk=TOPK, num_experts_per_rank=EPR, max_num_inp_token_per_rank=TOKENS,
+                        combine_dtype=torch.float4_e2m1fn_x2, device="cpu")
+    x, idx, w = inputs(0, 1)
+    _, _, _, _, cnt = op.dispatch(x, w, None, idx)
+    n = int(cnt.item())
+    vals = moe.FP4_VALUES[torch.randint(0, 8, (n, HIDDEN))] * torch.where(torch.rand(n, HIDDEN) < 0.5, -1.0, 1.0)
+    packed = moe.fp4_pack(moe.fp4_codes(vals)).view(torch.float4_e2m1fn_x2)
+    res, _ = op.combine(packed)
+    assert res.dtype == torch.float4_e2m1fn_x2 and tuple(res.shape) == (TOKENS, HIDDEN // 2)
+    assert torch.equal(moe.fp4_unpack(res), vals)  # world of one: one row per token
+    res, _ = op.combine(torch.full((n, HIDDEN), 9.0))  # float rows are quantised, saturating at 6
+    assert (moe.fp4_unpack(res) == 6.0).all()
+    assert tuple(op.get_registered_combine_input_buffer().shape) == (TOKENS * 1, HIDDEN // 2)
+    with pytest.raises(ValueError):
+        CollectiveEpOp(hidden_dim=255, topk=1, num_experts_per_rank=1, max_num_inp_token_per_rank=1,
+                       combine_dtype=torch.float4_e2m1fn_x2, device="cpu")
