@@ -32,8 +32,10 @@ Semantics, as KiwiEpOp:
   ``src_rank * (world * max_tokens) + token`` and ``decode_send_flat_idx``
   inverts it.
 
-Per call there are four small all-to-alls (counts) plus one per payload
-tensor; every rank must call dispatch and combine in the same order.
+Per dispatch there are two all-to-alls (the per-rank row counts, then one
+record per row holding the row, its weights, ids, source token and scales),
+and one per combine; every rank must call dispatch and combine in the same
+order.
 """
 import math
 
@@ -138,6 +140,16 @@ class CollectiveEpOp:
         row_bytes = t.element_size() * math.prod(t.shape[1:])
         return t.contiguous().view(torch.uint8).view(t.shape[0], row_bytes)
 
+    @staticmethod
+    def _unwire(recv, like):
+        """Splits received records back into tensors of the dtypes and widths of `like`."""
+        out, off, n = [], 0, recv.shape[0]
+        for f in like:
+            nb = f.element_size() * math.prod(f.shape[1:])
+            out.append(recv[:, off:off + nb].contiguous().view(f.dtype).view(n, *f.shape[1:]))
+            off += nb
+        return out
+
     # -- the contract ---------------------------------------------------------------
     def dispatch(self, input, weights, scales=None, indices=None, **_launch_kwargs):
         """See the module docstring; collective over the group."""
@@ -169,16 +181,16 @@ class CollectiveEpOp:
             rows, row_scales = codes[order_tok], sc[order_tok]
         else:
             rows, row_scales = x.to(torch.bfloat16)[order_tok], None
-        out_rows = self._a2a(self._wire(rows), send_counts, recv_counts)
-        out_w = self._a2a(w[order_tok], send_counts, recv_counts)
-        out_idx = self._a2a(idx.to(torch.int32)[order_tok], send_counts, recv_counts)
-        src_tok = self._a2a(order_tok.to(torch.int32).view(-1, 1), send_counts, recv_counts).view(-1)
-        out_sc = None
+        # One record per row, [row | weights | ids | source token | scales], so
+        # the payload crosses in a single all-to-all.
+        fields = [rows, w[order_tok], idx.to(torch.int32)[order_tok], order_tok.to(torch.int32).view(-1, 1)]
         if row_scales is not None:
-            out_sc = self._a2a(row_scales.contiguous(), send_counts, recv_counts)
+            fields.append(row_scales)
+        recv = self._a2a(torch.cat([self._wire(f) for f in fields], dim=1), send_counts, recv_counts)
+        out_rows, out_w, out_idx, src_tok, *rest = self._unwire(recv, fields)
+        out_sc = rest[0] if rest else None
+        src_tok = src_tok.view(-1)
         n = int(sum(recv_counts))
-        rows_dtype = torch.float8_e4m3fn if self._quant == "fp8" else torch.bfloat16
-        out_rows = out_rows.view(rows_dtype).view(n, self.hidden_dim)
         src_rank = torch.repeat_interleave(torch.arange(self.world_size, device=self.device),
                                            torch.tensor(recv_counts, device=self.device))
         self._src_pos = src_rank.to(torch.int64) * self.max_num_tokens_to_send() + src_tok.to(torch.int64)
