@@ -77,6 +77,9 @@ public:
     /// A native callback (any payload) that only counts its calls: lets a
     /// benchmark measure the queue / frontend without Python in the loop.
     virtual uint8_t register_native_counter() = 0;
+    /// A native callback taking one uint32 n that sets the progress threads'
+    /// active prefix (0 = all): how a kernel publishes the endpoints it uses.
+    virtual uint8_t register_active_endpoints_callback() = 0;
     virtual uint64_t native_count() const = 0;
     /// A native callback that prints its arguments with a printf-style format.
     virtual uint8_t register_native_print(const std::string& fmt, const std::string& codes, bool to_stderr) = 0;
@@ -100,6 +103,10 @@ public:
         return ctx_.register_raw_callback(
             [this](const uint8_t*, uint32_t) { count_.fetch_add(1, std::memory_order_relaxed); },
             invoke::CallbackBase::kAnySize);
+    }
+    uint8_t register_active_endpoints_callback() override {
+        return ctx_.register_callback(
+            std::function<void(uint32_t)>([this](uint32_t n) { threads_.set_active_endpoints(n); }));
     }
     uint64_t native_count() const override { return count_.load(std::memory_order_relaxed); }
     uint8_t register_native_print(const std::string& fmt, const std::string& codes, bool to_stderr) override {
@@ -343,6 +350,8 @@ PYBIND11_MODULE(_C, m) {
         .def("check_device_errors", &KiwiContextBase::check_device_errors)
         .def("rethrow_progress_errors", &KiwiContextBase::rethrow)
         .def("register_native_counter", &KiwiContextBase::register_native_counter)
+        .def("register_active_endpoints_callback", &KiwiContextBase::register_active_endpoints_callback,
+             "Registers a callback (one uint32 argument) that sets the active endpoint prefix; returns its id.")
         .def("register_native_print", &KiwiContextBase::register_native_print, py::arg("fmt"), py::arg("codes"),
              py::arg("to_stderr") = false,
              "Native callback printing its packed arguments (struct codes b B h H i I l L q Q f d) with a "

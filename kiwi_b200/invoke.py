@@ -98,6 +98,12 @@ class Context:
                 time.sleep(1e-4)
         return gen
 
+    def register_active_endpoints_callback(self):
+        """Registers a native callback taking one uint32 ``n`` that applies
+        ``set_active_endpoints(n)``, so a kernel can publish how many endpoints
+        it uses with ``invoke(cb, n)``.  Returns the callback id."""
+        return self._ctx.register_active_endpoints_callback()
+
     @property
     def active_endpoints(self):
         """The active prefix requested last (0 = all endpoints)."""

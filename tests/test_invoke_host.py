@@ -245,3 +245,15 @@ def test_progress_threads_poll_only_the_active_prefix():
     finally:
         ctx.stop()
     assert sorted(got) == [1, 3, 4, 5, 6, 7]  # the final drain covers every endpoint
+
+
+def test_a_kernel_can_publish_its_active_endpoints():
+    """The active-prefix callback (what a kernel invokes with the number of
+    endpoints it uses) sets the prefix the progress threads poll."""
+    ctx = invoke.Context(4, 16, host_only=True)
+    cb = ctx.register_active_endpoints_callback()
+    ctx.emulate_invoke(0, cb, struct.pack("<I", 2))
+    assert ctx.progress(0) == 1
+    assert ctx.active_endpoints == 2
+    ctx.emulate_invoke(1, cb, struct.pack("<I", 0))
+    assert ctx.progress(1) == 1 and ctx.active_endpoints == 0
