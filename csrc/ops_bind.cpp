@@ -6,6 +6,7 @@
 #include <pybind11/stl.h>
 #include <torch/extension.h>
 
+#include "kiwi/ep/kernels.hpp"
 #include "kiwi/gemm/grouped_gemm.hpp"
 #include "kiwi/ops/rows.hpp"
 
@@ -183,6 +184,25 @@ void register_ops(py::module_& m) {
         return py::make_tuple(i.local_bytes, i.registers, i.smem_bytes);
     });
     o.def("num_sms", &gemm::num_sms);
+    o.def(
+        "route_topk",
+        [](torch::Tensor logits, int64_t topk) {
+            TORCH_CHECK(logits.is_cuda() && logits.scalar_type() == torch::kFloat32 && logits.dim() == 2 &&
+                            logits.is_contiguous(),
+                        "logits must be a contiguous fp32 [tokens, experts] CUDA tensor");
+            TORCH_CHECK(topk >= 1 && topk <= logits.size(1), "topk must be in [1, experts]");
+            const c10::cuda::CUDAGuard guard(logits.device());
+            auto opts = torch::TensorOptions().device(logits.device());
+            torch::Tensor idx = torch::empty({logits.size(0), topk}, opts.dtype(torch::kInt32));
+            torch::Tensor w = torch::empty({logits.size(0), topk}, opts.dtype(torch::kFloat32));
+            ep::launch_route(logits.data_ptr<float>(), static_cast<int>(logits.size(0)),
+                             static_cast<int>(logits.size(1)), static_cast<int>(topk), idx.data_ptr<int32_t>(),
+                             w.data_ptr<float>(), cur_stream());
+            return py::make_tuple(idx, w);
+        },
+        py::arg("logits"), py::arg("topk"),
+        "Top-k experts per token and the softmax over their logits (the EP layer's routing kernel): "
+        "(idx int32 [T, k], weights fp32 [T, k]) on the current stream.");
     o.def("rows_copy", &rows_copy_py, py::arg("src"), py::arg("dst"), py::arg("src_idx") = py::none(),
           py::arg("dst_idx") = py::none(), py::arg("rows") = -1, py::arg("error"), py::arg("grid") = 0,
           "dst[dst_idx[i]] = src[src_idx[i]] (identity where an index is None), i < rows; negative indices skip "

@@ -9,12 +9,16 @@
   top-k accumulate row patterns of EP dispatch and combine as stand-alone
   kernels (``benchmarks/bench_ep_copy.py`` measures them against HBM).
 
-Routing and FP8 / NVFP4 quantisation run fused into the EP dispatch kernel
-(:mod:`kiwi_b200.parallel.ep`); their fp32 references are in
+* :func:`route_topk`: top-k routing with the softmax over the selected logits
+  (the EP layer's routing kernel).
+
+FP8 / NVFP4 quantisation runs fused into the EP dispatch kernel
+(:mod:`kiwi_b200.parallel.ep`); its fp32 references are in
 :mod:`kiwi_b200.models.moe`.
 """
 from .grouped_gemm import ExpertFFN, GroupedGemm, grouped_gemm, grouped_gemm_reference
+from .routing import route_topk
 from .rows import accumulate_rows, check_error, copy_rows
 
 __all__ = ["ExpertFFN", "GroupedGemm", "grouped_gemm", "grouped_gemm_reference", "accumulate_rows", "check_error",
-           "copy_rows"]
+           "copy_rows", "route_topk"]

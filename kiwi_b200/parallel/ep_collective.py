@@ -43,7 +43,7 @@ import torch
 import torch.distributed as dist
 
 from ..models import moe as moe_model
-from ..ops import ExpertFFN
+from ..ops import ExpertFFN, route_topk
 from ..utils import dist as kdist
 
 _FORMATS = {"none": "none", "fp8": "fp8"}
@@ -318,7 +318,7 @@ class CollectiveMoE:
 
     def forward(self, x, router_logits):
         """x [T, hidden] bf16, router_logits [T, num_experts] -> [T, hidden] (combine dtype)."""
-        idx, w = moe_model.route_reference(router_logits.to(self.device), self.cfg.topk)
+        idx, w = route_topk(router_logits.to(self.device), self.cfg.topk)
         return self.forward_routed(x, idx, w)
 
     __call__ = forward

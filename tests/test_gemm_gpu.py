@@ -126,3 +126,18 @@ def test_ops_plan_runs_the_kernel_and_matches_its_reference(swiglu):
     plan.check()
     ref = grouped_gemm_reference(a, b, counts, swiglu, scale)
     assert (out[:rows].float() - ref).abs().max().item() <= 2e-2 * ref.abs().max().item() + 1e-2
+
+
+@pytest.mark.parametrize("experts,topk", [(8, 2), (64, 6), (256, 8)])
+def test_ops_route_topk_matches_the_reference(experts, topk):
+    """kiwi_b200.ops.route_topk (the EP layer's routing kernel) against
+    torch.topk + softmax in fp32."""
+    from kiwi_b200.models import moe
+    from kiwi_b200.ops import route_topk
+
+    torch.manual_seed(experts)
+    logits = torch.randn(300, experts, device="cuda")
+    idx, w = route_topk(logits, topk)
+    ridx, rw = moe.route_reference(logits, topk)
+    assert torch.equal(idx, ridx)
+    assert torch.allclose(w, rw, atol=1e-6)

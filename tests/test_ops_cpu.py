@@ -108,3 +108,13 @@ def test_ep_copy_bench_accounting():
     assert (peak, how) == (mod.FALLBACK_HBM_GBS, "fallback")
     assert mod.agree("accumulate", torch.ones(2, 2), torch.ones(2, 2) * 1.001)
     assert not mod.agree("pack", torch.ones(2, 2), torch.ones(2, 2) * 1.001)
+
+
+def test_route_topk_on_cpu_is_the_reference():
+    from kiwi_b200.ops import route_topk
+
+    logits = torch.randn(9, 16)
+    idx, w = route_topk(logits, 4)
+    ridx, rw = moe.route_reference(logits, 4)
+    assert torch.equal(idx, ridx) and torch.equal(w, rw)
+    assert idx.dtype == torch.int32 and torch.allclose(w.sum(-1), torch.ones(9))
