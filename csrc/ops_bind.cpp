@@ -8,6 +8,7 @@
 
 #include "kiwi/ep/kernels.hpp"
 #include "kiwi/gemm/grouped_gemm.hpp"
+#include "kiwi/ops/quant.hpp"
 #include "kiwi/ops/rows.hpp"
 
 namespace py = pybind11;
@@ -184,6 +185,23 @@ void register_ops(py::module_& m) {
         return py::make_tuple(i.local_bytes, i.registers, i.smem_bytes);
     });
     o.def("num_sms", &gemm::num_sms);
+    o.def(
+        "quant_fp8",
+        [](torch::Tensor x) {
+            TORCH_CHECK(x.is_cuda() && x.scalar_type() == torch::kBFloat16 && x.dim() == 2 && x.is_contiguous(),
+                        "x must be a contiguous bf16 [rows, hidden] CUDA tensor");
+            TORCH_CHECK(x.size(1) % 128 == 0, "hidden must be a multiple of 128");
+            TORCH_CHECK(reinterpret_cast<uintptr_t>(x.data_ptr()) % 16 == 0, "x must start on a 16-byte boundary");
+            const c10::cuda::CUDAGuard guard(x.device());
+            auto opts = torch::TensorOptions().device(x.device());
+            torch::Tensor codes = torch::empty({x.size(0), x.size(1)}, opts.dtype(torch::kFloat8_e4m3fn));
+            torch::Tensor scales = torch::empty({x.size(0), x.size(1) / 128}, opts.dtype(torch::kFloat32));
+            ops::quant_fp8_rows(x.data_ptr(), codes.data_ptr(), scales.data_ptr<float>(), x.size(0),
+                                static_cast<int>(x.size(1)), cur_stream());
+            return py::make_tuple(codes, scales);
+        },
+        py::arg("x"),
+        "1x128 FP8 e4m3 quantisation of bf16 rows with the dispatch kernel's arithmetic: (codes, fp32 scales).");
     o.def(
         "route_topk",
         [](torch::Tensor logits, int64_t topk) {

@@ -43,7 +43,7 @@ import torch
 import torch.distributed as dist
 
 from ..models import moe as moe_model
-from ..ops import ExpertFFN, route_topk
+from ..ops import ExpertFFN, quant_fp8, route_topk
 from ..utils import dist as kdist
 
 _FORMATS = {"none": "none", "fp8": "fp8"}
@@ -177,7 +177,7 @@ class CollectiveEpOp:
                 raise ValueError("FP8 input needs an FP8 op and per-token scales [T, S]")
             rows, row_scales = x[order_tok], scales.to(self.device, torch.float32).reshape(t, -1)[order_tok]
         elif self._quant == "fp8":
-            codes, sc = moe_model.quant_fp8_codes(x)
+            codes, sc = quant_fp8(x)  # the dispatch kernel's arithmetic on CUDA tensors
             rows, row_scales = codes[order_tok], sc[order_tok]
         else:
             rows, row_scales = x.to(torch.bfloat16)[order_tok], None

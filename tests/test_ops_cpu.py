@@ -118,3 +118,12 @@ def test_route_topk_on_cpu_is_the_reference():
     ridx, rw = moe.route_reference(logits, 4)
     assert torch.equal(idx, ridx) and torch.equal(w, rw)
     assert idx.dtype == torch.int32 and torch.allclose(w.sum(-1), torch.ones(9))
+
+
+def test_quant_fp8_on_cpu_is_the_reference():
+    from kiwi_b200.ops import quant_fp8
+
+    x = torch.randn(4, 256).bfloat16()
+    codes, scales = quant_fp8(x)
+    rc, rs = moe.quant_fp8_codes(x)
+    assert torch.equal(codes.view(torch.uint8), rc.view(torch.uint8)) and torch.equal(scales, rs)

@@ -45,3 +45,22 @@ def test_accumulate_matches_fp32_sum(k):
         ok = col >= 0
         want[ok] += src[col[ok]].float()
     assert (out.float() - want).abs().max().item() <= 1e-2 * want.abs().max().item()
+
+
+@pytest.mark.parametrize("hidden", [128, 384, 7168])
+def test_quant_fp8_matches_the_reference(hidden):
+    """kiwi_b200.ops.quant_fp8 (the dispatch kernel's arithmetic in a kernel of
+    its own) against the fp32 reference: equal scales; codes equal except where
+    a value lies exactly between two e4m3 codes; all-zero blocks get scale 1."""
+    from kiwi_b200.models import moe
+
+    torch.manual_seed(hidden)
+    x = (torch.randn(37, hidden, device="cuda") * 3).bfloat16()
+    x[5] = 0
+    codes, scales = ops.quant_fp8(x)
+    rc, rs = moe.quant_fp8_codes(x)
+    assert codes.dtype == torch.float8_e4m3fn and tuple(scales.shape) == (37, hidden // 128)
+    assert torch.allclose(scales, rs, rtol=1e-6, atol=0) and bool((scales[5] == 1).all())
+    diff = (codes.float() - rc.float()).abs()
+    assert (diff > 0).float().mean().item() < 5e-3
+    assert (diff <= torch.maximum(rc.float().abs(), codes.float().abs()) * 0.125 + 2.0 ** -9).all()  # one code
