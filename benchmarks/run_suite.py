@@ -41,6 +41,8 @@ def suite(gpus, quick):
         ("collectives", True, ["benchmarks/bench_collectives.py"]),
         ("ep_stages", True, ["benchmarks/bench_ep_stages.py", "--steps", str(it(10, 3))]),
         ("ep_transport", True, ["benchmarks/bench_ep_transport.py", "--iters", str(it(50, 10))]),
+        ("ep_transport_collective", True, ["benchmarks/bench_ep_transport.py", "--transport", "collective",
+                                           "--iters", str(it(50, 10))]),
         ("bench", True, ["bench.py", "--gpus", str(gpus), "--steps", str(it(40, 5)), "--warmup", str(it(5, 3))]),
     ]
 
