@@ -160,9 +160,14 @@ def fp4_unpack(packed):
     return torch.where(codes >= 8, -mag, mag)
 
 
-def quant_nvfp4_reference(x, block=16):
-    """NVFP4 quantise-dequantise: per-row fp32 scale amax/(448*6), e4m3 block
-    scales per `block` elements, e2m1 values."""
+def nvfp4_scale_bytes(hidden, block=16):
+    """Scale bytes of one NVFP4 row on the wire: fp32 row scale + one e4m3 byte
+    per block, padded to 16 bytes."""
+    return (4 + hidden // block + 15) // 16 * 16
+
+
+def _nvfp4_parts(x, block=16):
+    """(row_scale [t, 1], e4m3 block scales [t, h/block, 1], per-element scale, e2m1 codes [t, h])."""
     t, h = x.shape
     xf = x.float()
     row_amax = xf.abs().amax(-1, keepdim=True)
@@ -170,10 +175,40 @@ def quant_nvfp4_reference(x, block=16):
     xb = xf.view(t, h // block, block)
     bamax = xb.abs().amax(-1, keepdim=True)
     s = torch.where(row_scale[:, :, None] > 0, bamax / (FP4_MAX * row_scale[:, :, None]), torch.zeros_like(bamax))
-    s = s.clamp(max=FP8_MAX).to(torch.float8_e4m3fn).float() * row_scale[:, :, None]
-    inv = torch.where(s > 0, 1.0 / s, torch.zeros_like(s))
-    q = _round_fp4(xb * inv)
-    return (q * s).view(t, h)
+    s8 = s.clamp(max=FP8_MAX).to(torch.float8_e4m3fn)
+    sdec = s8.float() * row_scale[:, :, None]
+    inv = torch.where(sdec > 0, 1.0 / sdec, torch.zeros_like(sdec))
+    return row_scale, s8, sdec, fp4_codes(xb * inv).view(t, h)
+
+
+def quant_nvfp4_codes(x, block=16):
+    """NVFP4 wire format of rows x [t, h]: (packed e2m1 codes uint8 [t, h / 2],
+    element 2i in the low nibble; scale bytes uint8 [t, nvfp4_scale_bytes(h)] =
+    fp32 row scale amax / (448 * 6), then one e4m3 block scale per `block`
+    elements relative to it, zero padding)."""
+    t, h = x.shape
+    row_scale, s8, _, codes = _nvfp4_parts(x, block)
+    sc = torch.zeros(t, nvfp4_scale_bytes(h, block), dtype=torch.uint8, device=x.device)
+    sc[:, :4] = row_scale.contiguous().view(torch.uint8).view(t, 4)
+    sc[:, 4:4 + h // block] = s8.view(t, h // block).view(torch.uint8)
+    return fp4_pack(codes), sc
+
+
+def dequant_nvfp4(codes, scales, block=16):
+    """fp32 rows [t, h] of the NVFP4 wire format (inverse of quant_nvfp4_codes)."""
+    t, h = codes.shape[0], codes.shape[1] * 2
+    row_scale = scales[:, :4].contiguous().view(torch.float32)                    # [t, 1]
+    s = scales[:, 4:4 + h // block].contiguous().view(torch.float8_e4m3fn).float() * row_scale
+    return (fp4_unpack(codes).view(t, h // block, block) * s[:, :, None]).view(t, h)
+
+
+def quant_nvfp4_reference(x, block=16):
+    """NVFP4 quantise-dequantise: per-row fp32 scale amax/(448*6), e4m3 block
+    scales per `block` elements, e2m1 values."""
+    t, h = x.shape
+    _, _, sdec, codes = _nvfp4_parts(x, block)
+    q = fp4_unpack(fp4_pack(codes)).view(t, h // block, block)
+    return (q * sdec).view(t, h)
 
 
 def dispatch_reference(x, quant):

@@ -15,8 +15,11 @@ Semantics, as KiwiEpOp:
 * ``dispatch(input, weights, scales, indices)`` returns ``(out, out_weights,
   out_scales, out_indices, recv_count)``: one row per (source rank, token) that
   routes at least one of its top-k experts to this rank, in (source rank,
-  token) order; ``out`` in the wire format (bf16, or float8_e4m3fn with fp32
-  1x128 scales in ``out_scales``), ``out_weights`` / ``out_indices`` the token's
+  token) order; ``out`` in the wire format (bf16; float8_e4m3fn with fp32
+  1x128 scales in ``out_scales``; or NVFP4 as the NVLink op carries it: packed
+  e2m1 bytes [n, hidden / 2] and, in ``out_scales``, an fp32 row scale then
+  e4m3 block scales per 16 elements, padded to 16 bytes), ``out_weights`` /
+  ``out_indices`` the token's
   full top-k weights and global expert ids.  bf16 input is quantised here
   (``scales`` ignored); float8_e4m3fn input with per-token fp32 ``scales``
   [T, S] (the reference's pre-quantised contract) travels unchanged.
@@ -46,7 +49,7 @@ from ..models import moe as moe_model
 from ..ops import ExpertFFN, quant_fp8, route_topk
 from ..utils import dist as kdist
 
-_FORMATS = {"none": "none", "fp8": "fp8"}
+_FORMATS = {"none": "none", "fp8": "fp8", "fp4": "nvfp4", "nvfp4": "nvfp4"}
 _DTYPES = {torch.bfloat16: "none", torch.float8_e4m3fn: "fp8"}
 _FP4 = torch.float4_e2m1fn_x2
 _COMBINE_DTYPES = (torch.bfloat16, torch.float32, torch.float8_e4m3fn, _FP4)
@@ -90,13 +93,14 @@ class CollectiveEpOp:
             raise ValueError("FP4 combine needs an even hidden_dim (two elements per byte)")
         fmt = str(dispatch_quant_format).lower()
         if fmt not in _FORMATS:
-            raise ValueError(f"unsupported dispatch_quant_format {dispatch_quant_format!r}: CollectiveEpOp carries "
-                             "bf16 or FP8 rows (NVFP4 is the NVLink op's)")
-        quant = "fp8" if fmt == "fp8" else _DTYPES.get(dispatch_dtype)
+            raise ValueError(f"unsupported dispatch_quant_format {dispatch_quant_format!r} (none, fp8 or fp4)")
+        quant = _FORMATS[fmt] if fmt != "none" else _DTYPES.get(dispatch_dtype)
         if quant is None:
             raise ValueError(f"unsupported dispatch_dtype {dispatch_dtype}")
         if hidden_dim % 128 and quant == "fp8":
             raise ValueError("FP8 dispatch needs hidden_dim to be a multiple of 128")
+        if hidden_dim % 16 and quant == "nvfp4":
+            raise ValueError("NVFP4 dispatch needs hidden_dim to be a multiple of 16")
         self.group = group
         self.rank = kdist.rank(group)
         self.world_size = kdist.world_size(group)
@@ -178,6 +182,9 @@ class CollectiveEpOp:
             rows, row_scales = x[order_tok], scales.to(self.device, torch.float32).reshape(t, -1)[order_tok]
         elif self._quant == "fp8":
             codes, sc = quant_fp8(x)  # the dispatch kernel's arithmetic on CUDA tensors
+            rows, row_scales = codes[order_tok], sc[order_tok]
+        elif self._quant == "nvfp4":
+            codes, sc = moe_model.quant_nvfp4_codes(x)  # the NVLink op's wire bytes
             rows, row_scales = codes[order_tok], sc[order_tok]
         else:
             rows, row_scales = x.to(torch.bfloat16)[order_tok], None
@@ -287,7 +294,7 @@ class CollectiveMoE:
     """One rank's expert-parallel MoE layer over :class:`CollectiveEpOp`.
 
     The same layer as :class:`kiwi_b200.parallel.ep.ExpertParallelMoE` (top-k
-    softmax routing, dispatch in ``cfg.quant`` = "none" or "fp8", each local
+    softmax routing, dispatch in ``cfg.quant`` = "none", "fp8" or "nvfp4", each local
     expert's SwiGLU FFN, routing-weighted sum over the top-k experts), for ranks
     that do not share one NVSwitch domain: rows move with all-to-all, and each
     rank sums the contributions of its own experts to a received token before
@@ -297,8 +304,8 @@ class CollectiveMoE:
     every rank of the group calls forward in the same order."""
 
     def __init__(self, cfg, group=None, max_tokens=None, weights=None, device=None, combine_dtype=torch.bfloat16):
-        if cfg.quant not in ("none", "fp8"):
-            raise ValueError("CollectiveMoE carries bf16 ('none') or FP8 rows")
+        if cfg.quant not in ("none", "fp8", "nvfp4"):
+            raise ValueError("CollectiveMoE carries bf16 ('none'), FP8 or NVFP4 rows")
         world = kdist.world_size(group)
         if cfg.num_experts % world:
             raise ValueError("num_experts must be divisible by the world size")
@@ -327,7 +334,10 @@ class CollectiveMoE:
         """Same layer with precomputed routing (idx [T, k] global expert ids, w [T, k])."""
         rows, rw, scales, ridx, _ = self.op.dispatch(x, w, None, idx)
         n, h = rows.shape
-        if scales is not None:  # FP8 codes x 1x128 scales -> bf16 operand rows
+        if self.cfg.quant == "nvfp4":  # e2m1 codes x block scales -> operand rows
+            h = self.cfg.hidden
+            rows = moe_model.dequant_nvfp4(rows, scales)
+        elif scales is not None:  # FP8 codes x 1x128 scales -> operand rows
             rows = (rows.float().view(n, h // 128, 128) * scales.view(n, -1, 1)).view(n, h)
         local = ridx.long() - self.rank * self.experts_per_rank
         r, s = ((local >= 0) & (local < self.experts_per_rank)).nonzero(as_tuple=True)

@@ -52,6 +52,11 @@ def check_rank(op, rank, world, quant):
         assert out.dtype == torch.float8_e4m3fn
         assert torch.equal(out[:n].view(torch.uint8), codes.view(torch.uint8)) and torch.equal(sc[:n], scales)
         back = moe.quant_fp8_reference(rows).bfloat16()
+    elif quant == "fp4":
+        codes, scales = moe.quant_nvfp4_codes(rows)
+        assert out.dtype == torch.uint8 and tuple(out.shape[1:]) == (HIDDEN // 2,)
+        assert torch.equal(out[:n], codes) and torch.equal(sc[:n], scales)
+        back = moe.dequant_nvfp4(out[:n], sc[:n]).bfloat16()
     else:
         assert sc is None and torch.equal(out[:n], rows)
         back = out[:n].clone()
@@ -59,14 +64,14 @@ def check_rank(op, rank, world, quant):
     res, _ = op.combine(back, None, oidx)
     dests = (idx.long() // EPR)
     want = torch.zeros(x.shape[0], HIDDEN)
-    ref_rows = moe.quant_fp8_reference(x) if quant == "fp8" else x.float()
+    ref_rows = {"fp8": moe.quant_fp8_reference, "fp4": moe.quant_nvfp4_reference}.get(quant, lambda v: v.float())(x)
     for t in range(x.shape[0]):
         k = len(set(dests[t].tolist()))
         want[t] = ref_rows[t].bfloat16().float() * k
     assert (res.float() - want).abs().max().item() <= 2e-2 * want.abs().max().item() + 1e-3
 
 
-@pytest.mark.parametrize("quant", ["none", "fp8"])
+@pytest.mark.parametrize("quant", ["none", "fp8", "fp4"])
 def test_world_of_one(quant):
     op = CollectiveEpOp(hidden_dim=HIDDEN, topk=TOPK, num_experts_per_rank=EPR, max_num_inp_token_per_rank=TOKENS,
                         dispatch_quant_format=quant, device="cpu")
@@ -93,7 +98,7 @@ def _member(rank, port, quant, q):
         q.put((rank, f"{type(e).__name__}: {e}\n{traceback.format_exc()[-2000:]}"))
 
 
-@pytest.mark.parametrize("quant", ["none", "fp8"])
+@pytest.mark.parametrize("quant", ["none", "fp8", "fp4"])
 def test_two_gloo_ranks(quant):
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
@@ -160,6 +165,9 @@ def test_constructor_checks():
                        combine_dtype=torch.float16, device="cpu")
     with pytest.raises(ValueError):
         CollectiveEpOp(hidden_dim=256, topk=2, num_experts_per_rank=4, max_num_inp_token_per_rank=8,
+                       dispatch_quant_format="int4", device="cpu")
+    with pytest.raises(ValueError):
+        CollectiveEpOp(hidden_dim=200, topk=2, num_experts_per_rank=4, max_num_inp_token_per_rank=8,
                        dispatch_quant_format="fp4", device="cpu")
     with pytest.raises(ValueError):
         CollectiveEpOp(hidden_dim=200, topk=2, num_experts_per_rank=4, max_num_inp_token_per_rank=8,
@@ -190,7 +198,7 @@ def check_moe(rank, world, quant):
         assert out.shape == ref.shape and err <= 2e-2 * ref.abs().max().item() + 1e-3, (rank, step, err)
 
 
-@pytest.mark.parametrize("quant", ["none", "fp8"])
+@pytest.mark.parametrize("quant", ["none", "fp8", "nvfp4"])
 def test_moe_layer_world_of_one(quant):
     check_moe(0, 1, quant)
 
@@ -226,11 +234,11 @@ def test_moe_layer_two_gloo_ranks():
     assert got == {0: "ok", 1: "ok"}, got
 
 
-def test_moe_layer_rejects_nvfp4():
+def test_moe_layer_rejects_unknown_wire_formats():
     from kiwi_b200.parallel.ep_collective import CollectiveMoE
 
     with pytest.raises(ValueError):
-        CollectiveMoE(_moe_cfg(1, "nvfp4"), device="cpu")
+        CollectiveMoE(_moe_cfg(1, "int8"), device="cpu")
 
 
 def test_token_sweep_including_zero():
@@ -308,9 +316,11 @@ def test_fp8_combine_sums_codes_and_saturates():
     _, _, _, _, cnt = op.dispatch(x, w, None, idx)
     n = int(cnt.item())
     rows = (torch.randn(n, HIDDEN) * 30).to(torch.float8_e4m3fn)
+    rows[0, 0] = torch.tensor(-0.0).to(torch.float8_e4m3fn)  # always exercise the -0 code
     res, _ = op.combine(rows)
     assert res.dtype == torch.float8_e4m3fn
-    assert torch.equal(res.view(torch.uint8), rows.view(torch.uint8))  # one row per token at world 1
+    # one row per token at world 1: the same values (a -0 code comes back as +0 after the fp32 sum)
+    assert torch.equal(res.float(), rows.float())
     big = torch.full((n, HIDDEN), 1000.0)  # bf16 / fp32 rows past the FP8 range saturate, never NaN
     res, _ = op.combine(big)
     assert (res.float() == 448.0).all()
