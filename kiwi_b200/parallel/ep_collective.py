@@ -22,7 +22,9 @@ Semantics, as KiwiEpOp:
   ``out_indices`` the token's
   full top-k weights and global expert ids.  bf16 input is quantised here
   (``scales`` ignored); float8_e4m3fn input with per-token fp32 ``scales``
-  [T, S] (the reference's pre-quantised contract) travels unchanged.
+  [T, S], or packed FP4 input (uint8 / float4_e2m1fn_x2 [T, hidden / 2]) with
+  per-token scales of any dtype (the reference's pre-quantised contract),
+  travels unchanged (FP4 scales come back as their bytes).
 * ``combine(input, weights, indices, out)`` returns ``(out, None)``: row i of
   ``input`` goes back to the rank and token it came from, and each token's rows
   are summed in fp32 (no routing weights, as MORI); tokens routed nowhere get
@@ -180,6 +182,13 @@ class CollectiveEpOp:
             if self._quant != "fp8" or scales is None or scales.shape[0] != t:
                 raise ValueError("FP8 input needs an FP8 op and per-token scales [T, S]")
             rows, row_scales = x[order_tok], scales.to(self.device, torch.float32).reshape(t, -1)[order_tok]
+        elif x.dtype in (torch.uint8, _FP4):
+            # Packed e2m1 codes [T, hidden / 2] pre-quantised by the caller: codes and
+            # the caller's per-token scale bytes travel unchanged.
+            if self._quant != "nvfp4" or scales is None or scales.shape[0] != t or x.shape[1] * 2 != self.hidden_dim:
+                raise ValueError("packed FP4 input needs an NVFP4 op, [T, hidden / 2] codes and per-token scales")
+            rows = x.view(torch.uint8)[order_tok]
+            row_scales = scales.to(self.device).contiguous().view(torch.uint8).reshape(t, -1)[order_tok]
         elif self._quant == "fp8":
             codes, sc = quant_fp8(x)  # the dispatch kernel's arithmetic on CUDA tensors
             rows, row_scales = codes[order_tok], sc[order_tok]

@@ -354,3 +354,16 @@ def test_fp4_combine_sums_and_requantises():
     with pytest.raises(ValueError):
         CollectiveEpOp(hidden_dim=255, topk=1, num_experts_per_rank=1, max_num_inp_token_per_rank=1,
                        combine_dtype=torch.float4_e2m1fn_x2, device="cpu")
+
+
+def test_prequantised_fp4_input_travels_unchanged():
+    op = CollectiveEpOp(hidden_dim=HIDDEN, topk=TOPK, num_experts_per_rank=EPR, max_num_inp_token_per_rank=TOKENS,
+                        dispatch_quant_format="fp4", device="cpu")
+    x, idx, w = inputs(0, 1)
+    codes = torch.randint(0, 256, (TOKENS, HIDDEN // 2), dtype=torch.uint8)
+    scales = torch.rand(TOKENS, 5)  # the caller's own layout: 20 bytes per token
+    out, _, sc, _, cnt = op.dispatch(codes.view(torch.float4_e2m1fn_x2), w, scales, idx)
+    n = int(cnt.item())
+    assert torch.equal(out[:n], codes) and torch.equal(sc[:n], scales.view(torch.uint8))
+    with pytest.raises(ValueError):
+        op.dispatch(codes, w, None, idx)
