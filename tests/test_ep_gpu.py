@@ -359,3 +359,30 @@ def test_collective_moe_layer_on_one_gpu(quant):
         idx, w = moe.route_reference(logits, cfg.topk)
         ref = moe.moe_reference(cfg, x, idx, w, device=x.device)
         assert (out.float() - ref).abs().max().item() <= 2e-2 * ref.abs().max().item() + 1e-3
+
+
+def test_collective_op_nvfp4_rows_match_the_nvlink_op():
+    """Both transports carry NVFP4 in one wire layout (packed e2m1 bytes; fp32 row
+    scale + e4m3 block scales, padded to 16 bytes): the NVLink op quantises in
+    its dispatch kernel, the all-to-all op with the fp32 restatement, so the
+    decoded rows agree except where a value lies exactly between two codes."""
+    from kiwi_b200.parallel.ep import KiwiEpOp
+    from kiwi_b200.parallel.ep_collective import CollectiveEpOp
+
+    kw = dict(hidden_dim=512, topk=2, num_experts_per_rank=8, max_num_inp_token_per_rank=32,
+              dispatch_quant_format="fp4")
+    a, b = KiwiEpOp(**kw), CollectiveEpOp(**kw)
+    torch.manual_seed(4)
+    x = torch.randn(32, 512, device="cuda").bfloat16()
+    idx, w = moe.route_reference(torch.randn(32, 8, device="cuda"), 2)
+    ra, _, sa, _, ca = a.dispatch(x, w, None, idx)
+    rb, _, sb, _, cb = b.dispatch(x, w, None, idx)
+    torch.cuda.synchronize()
+    a.check()
+    n = int(ca.item())
+    assert n == int(cb.item()) == 32
+    assert tuple(ra[:n].shape) == tuple(rb[:n].shape) and sa.shape[1] >= sb.shape[1]
+    da = moe.dequant_nvfp4(ra[:n], sa[:n, :sb.shape[1]])
+    db = moe.dequant_nvfp4(rb[:n], sb[:n])
+    assert (da != db).float().mean().item() < 1e-2
+    assert (da - db).abs().max().item() <= 0.35 * x.float().abs().max().item()
