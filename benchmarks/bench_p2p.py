@@ -2,6 +2,7 @@
 (the P2P latency and bandwidth sweep, 8 B - 64 MB, pairs of GPUs).
 
     torchrun --nproc-per-node N --master-addr 127.0.0.1 benchmarks/bench_p2p.py [--max-bytes 67108864]
+    python benchmarks/bench_p2p.py --local     # one GPU: the put and all-to-all kernels on a one-rank heap
 
 Ranks pair up (0<->1, 2<->3, ...).  For each size 8 B .. max (powers of two):
   * kiwi_pingpong: the initiator puts `size` bytes into its partner's heap and
@@ -17,6 +18,11 @@ Ranks pair up (0<->1, 2<->3, ...).  For each size 8 B .. max (powers of two):
   * nccl_sendrecv: torch.distributed send/recv ping-pong of the same size,
     CUDA events, one-way = round trip / 2.
 Data: seeded uniform uint8.  Every number is the max over ranks.
+
+--local runs the data-plane kernels on one GPU with a one-rank heap (peer =
+this GPU): a 64 MB put with release signal (put_bw, rotating over 256 MB of
+this GPU's HBM) and 200 device all-to-all rounds; the mode a single-GPU
+kernel profile of those two kernels uses.
 """
 import argparse
 import json
@@ -37,8 +43,11 @@ def main():
     ap.add_argument("--max-bytes", type=int, default=64 << 20)
     ap.add_argument("--iters", type=int, default=200)
     ap.add_argument("--nccl", action="store_true", default=True)
+    ap.add_argument("--local", action="store_true", help="one GPU, one-rank heap (peer = this GPU)")
     args = ap.parse_args()
     rank, world = kdist.init()
+    if args.local:
+        return local_kernels()
     assert world % 2 == 0, "run on an even number of ranks"
     peer = rank ^ 1
     initiator = rank % 2 == 0
@@ -136,6 +145,38 @@ def main():
         print("RESULT " + json.dumps({"bench": "p2p_check", "ok": ok}), flush=True)
     del heap
     dist.destroy_process_group()
+
+
+def local_kernels():
+    """put_bw and all2all_rounds on a one-rank heap; one RESULT line."""
+    from kiwi_b200.parallel.collectives import DeviceCollectives
+
+    size, region = 64 << 20, 256 << 20
+    heap = SymmetricHeap(4096 + 2 * region + 4096)
+    src_off, dst_off = 4096, 4096 + region
+    g = torch.Generator(device="cuda").manual_seed(1234)
+    heap.tensor(src_off, [region], torch.uint8).copy_(torch.randint(0, 256, (region,), generator=g,
+                                                                    dtype=torch.uint8, device="cuda"))
+    flag = heap.tensor(0, [8], torch.int64)
+    status = torch.zeros(2, dtype=torch.int32, device="cuda")
+    el = torch.zeros(1, dtype=torch.int64, device="cuda")
+    gbps = []
+    for _ in range(3):
+        flag.zero_()
+        heap.native.put_bw(0, True, size, 4, src_off, dst_off, 0, 1, el, status, 132, 5_000_000_000, region)
+        torch.cuda.synchronize()
+        gbps.append(size * 4 / (el.item() / 1e9) / 1e9)
+    assert int(status[0].item()) == 0, status
+    coll = DeviceCollectives()
+    send = torch.tensor([5], dtype=torch.int32, device="cuda")
+    lat = torch.zeros(200, dtype=torch.int64, device="cuda")
+    out = coll.all2all(send, rounds=200, lat=lat)
+    torch.cuda.synchronize()
+    coll.check()
+    assert out[-1, 0].item() == 5 + 199
+    print("RESULT " + json.dumps({"bench": "p2p_local", "put_GBps_local": max(gbps),
+                                  "all2all_round_us_world1": float(lat.float().median().item()) / 1e3}), flush=True)
+    del heap
 
 
 if __name__ == "__main__":

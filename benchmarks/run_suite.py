@@ -34,9 +34,8 @@ def suite(gpus, quick):
                            "--warmup", str(it(10_000, 1_000))]),
         ("frontends", False, ["benchmarks/bench_frontends.py"]),
         ("gemm", False, ["benchmarks/bench_gemm.py"] + (["--shape", "gemm1_ep8", "--groups", "8"] if quick else [])),
-        ("tma_load", False, ["benchmarks/bench_tma_load.py", "--iters", str(it(4000, 500))]),
         ("ep_copy", False, ["benchmarks/bench_ep_copy.py", "--iters", str(it(20, 5))]),
-        ("p2p_local", False, ["benchmarks/p2p_local_kernels.py"]),
+        ("p2p_local", False, ["benchmarks/bench_p2p.py", "--local"]),
         ("p2p", True, ["benchmarks/bench_p2p.py", "--iters", str(it(2000, 200))]),
         ("collectives", True, ["benchmarks/bench_collectives.py"]),
         ("ep_stages", True, ["benchmarks/bench_ep_stages.py", "--steps", str(it(10, 3))]),

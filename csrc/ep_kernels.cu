@@ -21,6 +21,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <atomic>
 
 #include "kiwi/ep/debug_timing.hpp"
 #include "kiwi/ep/kernels.hpp"
@@ -674,12 +675,16 @@ __global__ void __launch_bounds__(kThreads) combine_rows_kernel(EpConfig c, p2p:
     grid_done_signal(c, h, &ws.done_ctas[1], c.combine_flag(c.rank), (static_cast<uint64_t>(epoch) << 32) | 1u);
 }
 
+/// SM count of the current device (cached per device: a process may drive several GPUs).
 int default_grid() {
-    static int n = 0;
+    static std::atomic<int> cached[64] = {};
+    int dev = 0;
+    KIWI_CUDA_CHECK(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= 64) throw kiwi::error("kiwi::ep: device index beyond 64");
+    int n = cached[dev].load(std::memory_order_relaxed);
     if (n == 0) {
-        int dev = 0;
-        cudaGetDevice(&dev);
-        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+        KIWI_CUDA_CHECK(cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev));
+        cached[dev].store(n, std::memory_order_relaxed);
     }
     return n;
 }

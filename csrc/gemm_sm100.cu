@@ -21,6 +21,8 @@
 // up rows 128n..128n+127] (interleave_gate_up() builds that layout), so one
 // accumulator tile holds both halves and the epilogue writes silu(g) * u.
 #include <cuda.h>
+
+#include <atomic>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
@@ -747,97 +749,6 @@ __global__ void build_schedule_kernel(const int32_t* counts, int num_groups, int
     }
 }
 
-/// TMA operand-feed probe (no MMAs).  Thread 0 of warp 0 streams `iters`
-/// boxes of box_rows x box_k bf16 through `stages` shared-memory stages, the
-/// grouped GEMM's producer pattern; thread 0 of warp 1 releases each stage as
-/// soon as its bytes land.  cycles[block] = SM cycles from the first issue to
-/// the last arrival, so bytes / cycles is what one SM's TMA path delivers with
-/// every SM loading at once.  shared_rows: every CTA walks the same rows (an
-/// L2-resident operand, as the GEMM's weight tiles are); otherwise each CTA
-/// streams rows of its own.  Every wait is bounded; on a timeout the error word
-/// is set and, before the CTA exits, thread 0 waits (bounded) for every load
-/// it issued that was not consumed.
-__global__ void __launch_bounds__(64, 1)
-    tma_rate_kernel(const __grid_constant__ CUtensorMap tmap, int box_rows, int box_k, int stages, int64_t iters,
-                    int rows, int k, int shared_rows, uint64_t* cycles, uint32_t* error) {
-    extern __shared__ uint8_t smem_raw[];
-    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    const uint32_t box_bytes = static_cast<uint32_t>(box_rows) * static_cast<uint32_t>(box_k) * 2u;
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + static_cast<size_t>(stages) * box_bytes);
-    uint64_t* empty = full + stages;
-    __shared__ int64_t s_issued, s_consumed;
-    __shared__ uint64_t s_t0, s_t1;
-    const int warp = threadIdx.x / 32;
-    const int lane = threadIdx.x & 31;
-    if (threadIdx.x == 0) {
-        for (int st = 0; st < stages; ++st) {
-            sm100::mbar_init(&full[st], 1);
-            sm100::mbar_init(&empty[st], 1);
-        }
-        sm100::fence_mbar_init();
-        sm100::tma_prefetch_desc(&tmap);
-        s_issued = s_consumed = 0;
-        s_t0 = s_t1 = 0;
-    }
-    __syncthreads();
-    const int kblocks = k / box_k;
-    const int row_tiles = rows / box_rows;
-    if (warp == 0 && lane == 0) {
-        int stage = 0;
-        uint32_t phase = 0;
-        int64_t i = 0;
-        s_t0 = clock64();
-        for (; i < iters; ++i) {
-            if (!sm100::mbar_wait(&empty[stage], phase ^ 1)) {
-                atomicCAS(error, 0u, 1u);
-                break;
-            }
-            sm100::mbar_arrive_expect_tx(&full[stage], box_bytes);
-            const int kb = static_cast<int>(i % kblocks);
-            const int64_t sweep = i / kblocks;
-            const int64_t rt = shared_rows ? sweep % row_tiles : (blockIdx.x + sweep * gridDim.x) % row_tiles;
-            sm100::tma_load_2d(smem + static_cast<size_t>(stage) * box_bytes, &tmap, &full[stage], kb * box_k,
-                               static_cast<int32_t>(rt * box_rows));
-            if (++stage == stages) {
-                stage = 0;
-                phase ^= 1;
-            }
-        }
-        s_issued = i;
-    } else if (warp == 1 && lane == 0) {
-        int stage = 0;
-        uint32_t phase = 0;
-        int64_t i = 0;
-        for (; i < iters; ++i) {
-            if (!sm100::mbar_wait(&full[stage], phase)) {
-                atomicCAS(error, 0u, 2u);
-                break;
-            }
-            sm100::mbar_arrive(&empty[stage]);
-            if (++stage == stages) {
-                stage = 0;
-                phase ^= 1;
-            }
-        }
-        s_t1 = clock64();
-        s_consumed = i;
-    }
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        // Loads issued but not consumed (only after a timeout): wait for them
-        // to land before the CTA's shared memory goes away.
-        for (int64_t j = s_consumed; j < s_issued; ++j) {
-            const int st = static_cast<int>(j % stages);
-            const uint32_t ph = static_cast<uint32_t>((j / stages) & 1);
-            if (!sm100::mbar_wait(&full[st], ph)) {
-                atomicCAS(error, 0u, 3u);
-                break;
-            }
-        }
-        cycles[blockIdx.x] = s_t1 > s_t0 ? s_t1 - s_t0 : 0;
-    }
-}
-
 }  // namespace
 
 CUtensorMap make_tmap_bf16_2d(const void* ptr, uint64_t rows, uint64_t cols, uint32_t box_rows, uint32_t box_k) {
@@ -876,12 +787,37 @@ void build_schedule(const int32_t* counts, int num_groups, int n, int bn, int32_
     KIWI_CUDA_CHECK(cudaGetLastError());
 }
 
+namespace {
+
+constexpr int kMaxCachedDevices = 64;
+
+int current_device() {
+    int dev = 0;
+    KIWI_CUDA_CHECK(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= kMaxCachedDevices) throw kiwi::error("grouped_gemm: device index beyond 64");
+    return dev;
+}
+
+/// Raises `kernel`'s dynamic shared-memory limit to `smem` on the current
+/// device.  The attribute is per device, so `done` keeps one bit per device;
+/// two threads racing on the first launch both set it, which is harmless.
+template <typename Kernel>
+void raise_smem_limit(Kernel kernel, int smem, std::atomic<uint64_t>& done) {
+    const uint64_t bit = 1ull << current_device();
+    if (done.load(std::memory_order_acquire) & bit) return;
+    KIWI_CUDA_CHECK(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    done.fetch_or(bit, std::memory_order_acq_rel);
+}
+
+}  // namespace
+
 int num_sms() {
-    static int n = 0;
+    static std::atomic<int> cached[kMaxCachedDevices] = {};
+    const int dev = current_device();
+    int n = cached[dev].load(std::memory_order_relaxed);
     if (n == 0) {
-        int dev = 0;
-        cudaGetDevice(&dev);
-        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+        KIWI_CUDA_CHECK(cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev));
+        cached[dev].store(n, std::memory_order_relaxed);
     }
     return n;
 }
@@ -893,12 +829,8 @@ void launch_grouped(const CUtensorMap& tmap_a, const CUtensorMap& tmap_b, const 
                     const ScatterArgs& sc, int grid, cudaStream_t stream, const GatherArgs& ga = GatherArgs{}) {
     constexpr int BN = 256;
     const int smem = Smem<BN, STAGES, EPI == kEpiScatter, GQ, BKT>::kBytes;
-    static bool attr = false;
-    if (!attr) {
-        KIWI_CUDA_CHECK(cudaFuncSetAttribute(grouped_gemm_kernel<BN, EPI, STAGES, GQ, BKT>,
-                                             cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-        attr = true;
-    }
+    static std::atomic<uint64_t> attr{0};
+    raise_smem_limit(grouped_gemm_kernel<BN, EPI, STAGES, GQ, BKT>, smem, attr);
     grouped_gemm_kernel<BN, EPI, STAGES, GQ, BKT>
         <<<grid, GQ >= 0 ? kGatherThreads : kThreads, smem, stream>>>(tmap_a, tmap_b, args, sc, ga);
     KIWI_CUDA_CHECK(cudaGetLastError());
@@ -923,27 +855,6 @@ void grouped_gemm(const CUtensorMap& tmap_a, const CUtensorMap& tmap_b, const Gr
 
 constexpr int kBk32Stages = 9;   // 9 x 24 KB stages
 constexpr int kBk128Stages = 2;  // 2 x 96 KB stages (half the stage hand-offs of BK 64 per FLOP)
-
-void tma_load_rate(const void* ptr, int64_t rows, int64_t k, int box_rows, int box_k, int stages, int64_t iters,
-                   int grid, bool shared_rows, uint64_t* cycles, uint32_t* error, cudaStream_t stream) {
-    if (box_k != 64 && box_k != 32) throw kiwi::error("tma_load_rate: box_k must be 64 or 32");
-    if (box_rows < 8 || box_rows > 256 || box_rows % 8) throw kiwi::error("tma_load_rate: box_rows in [8, 256], x8");
-    if (rows % box_rows || k % box_k || rows <= 0 || k <= 0) {
-        throw kiwi::error("tma_load_rate: rows and k must be multiples of the box");
-    }
-    if (stages < 1 || iters < 1) throw kiwi::error("tma_load_rate: stages and iters must be positive");
-    const size_t box_bytes = static_cast<size_t>(box_rows) * box_k * 2;
-    const size_t smem = 1024 + static_cast<size_t>(stages) * box_bytes + 2 * static_cast<size_t>(stages) * 8;
-    if (smem > 227 * 1024) throw kiwi::error("tma_load_rate: stages x box exceed 227 KB of shared memory");
-    if (grid <= 0) grid = num_sms();
-    const CUtensorMap m = make_tmap_bf16_2d(ptr, static_cast<uint64_t>(rows), static_cast<uint64_t>(k),
-                                            static_cast<uint32_t>(box_rows), static_cast<uint32_t>(box_k));
-    KIWI_CUDA_CHECK(cudaFuncSetAttribute(tma_rate_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(smem)));
-    tma_rate_kernel<<<grid, 64, smem, stream>>>(m, box_rows, box_k, stages, iters, static_cast<int>(rows),
-                                                static_cast<int>(k), shared_rows ? 1 : 0, cycles, error);
-    KIWI_CUDA_CHECK(cudaGetLastError());
-}
 
 void grouped_gemm_bk128(const CUtensorMap& tmap_a, const CUtensorMap& tmap_b, const GroupedArgs& args, bool swiglu,
                         int grid, cudaStream_t stream) {
@@ -1008,20 +919,12 @@ void grouped_gemm_pair(const CUtensorMap& tmap_a, const CUtensorMap& tmap_b_half
     grid &= ~1;  // whole clusters of two
     if (grid < 2) throw kiwi::error("grouped_gemm_pair: needs at least two SMs");
     if (swiglu) {
-        static bool attr = false;
-        if (!attr) {
-            KIWI_CUDA_CHECK(cudaFuncSetAttribute(grouped_gemm_pair_kernel<true>,
-                                                 cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-            attr = true;
-        }
+        static std::atomic<uint64_t> attr{0};
+        raise_smem_limit(grouped_gemm_pair_kernel<true>, smem, attr);
         grouped_gemm_pair_kernel<true><<<grid, kThreads, smem, stream>>>(tmap_a, tmap_b_half, args);
     } else {
-        static bool attr = false;
-        if (!attr) {
-            KIWI_CUDA_CHECK(cudaFuncSetAttribute(grouped_gemm_pair_kernel<false>,
-                                                 cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-            attr = true;
-        }
+        static std::atomic<uint64_t> attr{0};
+        raise_smem_limit(grouped_gemm_pair_kernel<false>, smem, attr);
         grouped_gemm_pair_kernel<false><<<grid, kThreads, smem, stream>>>(tmap_a, tmap_b_half, args);
     }
     KIWI_CUDA_CHECK(cudaGetLastError());

@@ -460,7 +460,8 @@ PYBIND11_MODULE(_C, m) {
     b.def("invoke_rtt",
           [rtt_to_dict](uint64_t iters, uint64_t warmup, uint32_t bytes, uint64_t seed, int cpu, uint64_t cap,
                         bool mpsc, uint32_t poll_warps, uint64_t timeout_ns, bool mailbox, uint32_t stagger_ns,
-                        uint32_t initial_delay_ns, uint32_t pipeline, bool adaptive, bool demote) {
+                        uint32_t initial_delay_ns, uint32_t pipeline, bool adaptive, bool demote,
+                        uint32_t block_threads) {
               bench::RttConfig c;
               c.iters = iters;
               c.warmup = warmup;
@@ -477,6 +478,7 @@ PYBIND11_MODULE(_C, m) {
               c.pipeline = pipeline;
               c.adaptive = adaptive;
               c.demote = demote;
+              c.block_threads = block_threads;
               bench::RttResult r;
               {
                   py::gil_scoped_release nogil;
@@ -488,7 +490,7 @@ PYBIND11_MODULE(_C, m) {
           py::arg("cpu") = -1, py::arg("capacity") = 4096, py::arg("mpsc") = false, py::arg("poll_warps") = 0,
           py::arg("timeout_ns") = 2000000000ull, py::arg("mailbox") = false, py::arg("stagger_ns") = 200,
           py::arg("initial_delay_ns") = 300, py::arg("pipeline") = 1, py::arg("adaptive") = true,
-          py::arg("demote") = true);
+          py::arg("demote") = true, py::arg("block_threads") = 0);
     b.def("pcie_floor",
           [rtt_to_dict](uint64_t iters, uint64_t warmup, int cpu, uint64_t timeout_ns) {
               bench::RttResult r;

@@ -10,26 +10,8 @@
 // (kiwi_b200._C.ops.GroupedGemm) allocates its schedule buffers with torch;
 // this one keeps them in a fixed device array instead.
 //
-// Contract:
-//   * The caller passes every input and output: A [a_rows, k] bf16, B
-//     [num_groups * n, k] bf16 (both row-major, 16-byte aligned), per-group row
-//     counts (int32 device array), C [c_rows, n] bf16 (or [c_rows, n / 2] with
-//     swiglu), an optional fp32 per-row scale, and the CUDA stream.
-//   * Scratch (group offsets, tile prefix, error word) lives in the file-scope
-//     device array below: kNoallocMaxGroups = 1024 groups at most, 8.5 KB.  Every
-//     GPU that loads this library holds the array until the process exits.
-//   * The first call on a device (with that device current) resolves the
-//     array's device address with cudaGetSymbolAddress and caches it; make that
-//     first call before any stream capture that includes this entry point.
-//   * All calls share the array, which keeps the last call's contents: the
-//     error word is cleared (cudaMemsetAsync) at the start of every call and the
-//     schedule is rewritten by every call.  Calls that overlap on the same GPU
-//     (for example on two streams) race on the array, so serialise them; calls
-//     on different GPUs use different copies of the array and do not race.
-//   * No cudaMalloc, cudaFree or allocating library routine is called.
-//   * Returns 0 on success; a non-zero code and a message readable through
-//     kiwi_noalloc_last_error() otherwise (sizes beyond the maximum, bad
-//     alignment, CUDA errors).
+// The contract (inputs, limits, the shared array, error codes) is stated in
+// include/kiwi/gemm/noalloc.h, which declares the exported symbols.
 #include <cuda.h>
 #include <cuda_runtime.h>
 
@@ -37,6 +19,7 @@
 #include <string>
 
 #include "kiwi/gemm/grouped_gemm.hpp"
+#include "kiwi/gemm/noalloc.h"
 
 namespace {
 
@@ -84,9 +67,9 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 
 }  // namespace
 
-extern "C" __attribute__((visibility("default"))) int kiwi_noalloc_max_groups() { return kNoallocMaxGroups; }
+extern "C" __attribute__((visibility("default"))) int kiwi_noalloc_max_groups(void) { return kNoallocMaxGroups; }
 
-extern "C" __attribute__((visibility("default"))) const char* kiwi_noalloc_last_error() {
+extern "C" __attribute__((visibility("default"))) const char* kiwi_noalloc_last_error(void) {
     return g_last_error.c_str();
 }
 
@@ -138,5 +121,21 @@ extern "C" __attribute__((visibility("default"))) int kiwi_grouped_gemm_bf16_noa
     } catch (const std::exception& ex) {
         return fail(7, std::string("kiwi_grouped_gemm_bf16_noalloc: ") + ex.what());
     }
+    return 0;
+}
+
+/// Copies this device's error word to caller memory and synchronises `stream`
+/// (see noalloc.h).  Allocates nothing.
+extern "C" __attribute__((visibility("default"))) int kiwi_noalloc_error_word(int32_t* host_out, void* stream) {
+    g_last_error.clear();
+    if (!host_out) return fail(3, "kiwi_noalloc_error_word: null host_out");
+    std::string err;
+    int32_t* scratch = scratch_for_current_device(err);
+    if (!scratch) return fail(5, "kiwi_noalloc_error_word: " + err);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    cudaError_t e = cudaMemcpyAsync(host_out, scratch + 2 * (kNoallocMaxGroups + 1), sizeof(int32_t),
+                                    cudaMemcpyDeviceToHost, s);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    if (e != cudaSuccess) return fail(6, std::string("kiwi_noalloc_error_word: ") + cudaGetErrorString(e));
     return 0;
 }

@@ -203,6 +203,25 @@ void register_ops(py::module_& m) {
         py::arg("x"),
         "1x128 FP8 e4m3 quantisation of bf16 rows with the dispatch kernel's arithmetic: (codes, fp32 scales).");
     o.def(
+        "quant_nvfp4",
+        [](torch::Tensor x) {
+            TORCH_CHECK(x.is_cuda() && x.scalar_type() == torch::kBFloat16 && x.dim() == 2 && x.is_contiguous(),
+                        "x must be a contiguous bf16 [rows, hidden] CUDA tensor");
+            TORCH_CHECK(x.size(1) % 16 == 0, "hidden must be a multiple of 16");
+            TORCH_CHECK(reinterpret_cast<uintptr_t>(x.data_ptr()) % 16 == 0, "x must start on a 16-byte boundary");
+            const c10::cuda::CUDAGuard guard(x.device());
+            const int hidden = static_cast<int>(x.size(1));
+            auto opts = torch::TensorOptions().device(x.device()).dtype(torch::kUInt8);
+            torch::Tensor codes = torch::empty({x.size(0), hidden / 2}, opts);
+            torch::Tensor scales = torch::empty({x.size(0), ops::nvfp4_scale_bytes(hidden)}, opts);
+            ops::quant_nvfp4_rows(x.data_ptr(), codes.data_ptr(), scales.data_ptr(), x.size(0), hidden,
+                                  cur_stream());
+            return py::make_tuple(codes, scales);
+        },
+        py::arg("x"),
+        "NVFP4 quantisation of bf16 rows into the NVLink dispatch's wire bytes: (packed e2m1 codes uint8 "
+        "[rows, hidden / 2], scale bytes uint8 [rows, S]: fp32 row scale then e4m3 block scales).");
+    o.def(
         "route_topk",
         [](torch::Tensor logits, int64_t topk) {
             TORCH_CHECK(logits.is_cuda() && logits.scalar_type() == torch::kFloat32 && logits.dim() == 2 &&
@@ -228,22 +247,4 @@ void register_ops(py::module_& m) {
     o.def("rows_accumulate", &rows_accumulate_py, py::arg("src"), py::arg("out"), py::arg("map"), py::arg("error"),
           py::arg("grid") = 0,
           "out[t] = sum_j src[map[t, j]] (bf16 rows, fp32 sums); negative entries are skipped.  Current stream.");
-    o.def(
-        "tma_load_rate",
-        [](torch::Tensor t, int box_rows, int box_k, int stages, int64_t iters, int grid, bool shared_rows) {
-            TORCH_CHECK(t.is_cuda() && t.scalar_type() == torch::kBFloat16 && t.dim() == 2 && t.is_contiguous(),
-                        "tma_load_rate: a contiguous 2-D bf16 CUDA tensor");
-            if (grid <= 0) grid = gemm::num_sms();
-            auto opts = torch::TensorOptions().device(t.device());
-            torch::Tensor cycles = torch::zeros({grid}, opts.dtype(torch::kInt64));
-            torch::Tensor error = torch::zeros({1}, opts.dtype(torch::kInt32));
-            gemm::tma_load_rate(t.data_ptr(), t.size(0), t.size(1), box_rows, box_k, stages, iters, grid, shared_rows,
-                                reinterpret_cast<uint64_t*>(cycles.data_ptr<int64_t>()),
-                                reinterpret_cast<uint32_t*>(error.data_ptr<int32_t>()),
-                                at::cuda::getCurrentCUDAStream().stream());
-            return py::make_tuple(cycles, error);
-        },
-        py::arg("tensor"), py::arg("box_rows"), py::arg("box_k"), py::arg("stages"), py::arg("iters"),
-        py::arg("grid") = 0, py::arg("shared_rows") = false,
-        "TMA operand-feed probe (no MMAs): (cycles per CTA, error word), enqueued on the current stream.");
 }

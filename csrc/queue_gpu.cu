@@ -83,6 +83,46 @@ int pick_cpu(int cpu) {
     return cpus.empty() ? -1 : cpus[0];
 }
 
+/// Runs the host side of a benchmark kernel on its own thread, started (on
+/// the caller's device, pinned to `cpu` when it is >= 0) BEFORE `launch()`
+/// runs on the calling thread.  A tool that blocks inside the launch call (a
+/// profiler that replays the kernel) then cannot leave the kernel without its
+/// host side until the kernel's bounded waits expire.  `serve(launched, quit)`
+/// polls until its work is done; it may ask whether the launch has returned
+/// (`launched`, so an empty stream before the launch is not taken for a
+/// finished kernel) and must return when `quit` turns true (the launch threw).
+template <typename Launch, typename Serve>
+void launch_with_server(int cpu, Launch&& launch, Serve&& serve) {
+    std::atomic<bool> launched{false}, quit{false};
+    std::exception_ptr err;
+    int dev = 0;
+    KIWI_CUDA_CHECK(cudaGetDevice(&dev));
+    std::thread th([&] {
+        try {
+            KIWI_CUDA_CHECK(cudaSetDevice(dev));
+            if (cpu >= 0) topology::bind_current_thread({cpu});
+            serve(launched, quit);
+        } catch (...) {
+            err = std::current_exception();
+        }
+    });
+    try {
+        launch();
+    } catch (...) {
+        quit.store(true);
+        th.join();
+        throw;
+    }
+    launched.store(true, std::memory_order_release);
+    th.join();
+    if (err) std::rethrow_exception(err);
+}
+
+/// True when `stream` has no work left; only asked after the launch returned.
+bool stream_idle(cudaStream_t stream, const std::atomic<bool>& launched) {
+    return launched.load(std::memory_order_acquire) && cudaStreamQuery(stream) != cudaErrorNotReady;
+}
+
 }  // namespace
 
 // ---------------------------------------------------------------------------
@@ -111,6 +151,9 @@ __global__ void __launch_bounds__(256) invoke_rtt_kernel(
         sh.stop = 0;
     }
     __syncthreads();
+    // Warps past the reply pollers in use (a block launched wider than the
+    // benchmark needs, e.g. 1 x 64 threads as a wave64 block) have no role.
+    if (warp > 0 && (use_mailbox || warp > poll_warps)) return;
 
     if (warp > 0) {
         // Helper pollers: keep one read of the watched reply line in flight each,
@@ -287,28 +330,36 @@ static RttResult run_invoke_rtt(const RttConfig& cfg) {
     KIWI_CUDA_CHECK(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking));
 
     const int cpu = pick_cpu(cfg.cpu);
-    if (cpu >= 0) topology::bind_current_thread({cpu});
-    const uint32_t threads = 32 * (1 + (cfg.mailbox ? 0 : cfg.poll_warps));
-    invoke_rtt_kernel<Q><<<1, threads, 0, stream>>>(
-        ctx.device_context(), reply.device_handle(), cb, cfg.iters, cfg.warmup, cfg.payload_bytes,
-        payload.p, cfg.seed, lat.p, cyc.p, totals.p, status.p, cfg.poll_warps,
-        /*stagger_ns=*/cfg.poll_warps ? 800 / cfg.poll_warps : 0, cfg.timeout_ns, done.p, mailbox.device_handle(),
-        cfg.mailbox ? 1u : 0u);
-    KIWI_CUDA_CHECK(cudaGetLastError());
-
-    auto poll = ctx.poll_state(0);
-    uint64_t idle = 0;
-    while (true) {
-        if (poll.ready()) {
-            ctx.progress(0);
-            poll.refresh();
-            idle = 0;
-            continue;
-        }
-        if (*done.p) break;
-        if ((++idle & 0xfffff) == 0 && cudaStreamQuery(stream) != cudaErrorNotReady) break;
+    const uint32_t used = 32 * (1 + (cfg.mailbox ? 0 : cfg.poll_warps));
+    if (cfg.block_threads && (cfg.block_threads % 32 || cfg.block_threads < used || cfg.block_threads > 256)) {
+        throw kiwi::error("invoke_rtt: block_threads must be a multiple of 32 in [warps used, 256]");
     }
-    ctx.progress(0);
+    const uint32_t threads = cfg.block_threads ? cfg.block_threads : used;
+    launch_with_server(
+        cpu,
+        [&] {
+            invoke_rtt_kernel<Q><<<1, threads, 0, stream>>>(
+                ctx.device_context(), reply.device_handle(), cb, cfg.iters, cfg.warmup, cfg.payload_bytes,
+                payload.p, cfg.seed, lat.p, cyc.p, totals.p, status.p, cfg.poll_warps,
+                /*stagger_ns=*/cfg.poll_warps ? 800 / cfg.poll_warps : 0, cfg.timeout_ns, done.p,
+                mailbox.device_handle(), cfg.mailbox ? 1u : 0u);
+            KIWI_CUDA_CHECK(cudaGetLastError());
+        },
+        [&](const std::atomic<bool>& launched, const std::atomic<bool>& quit) {
+            auto poll = ctx.poll_state(0);
+            uint64_t idle = 0;
+            while (!quit.load(std::memory_order_relaxed)) {
+                if (poll.ready()) {
+                    ctx.progress(0);
+                    poll.refresh();
+                    idle = 0;
+                    continue;
+                }
+                if (*done.p) break;
+                if ((++idle & 0xfffff) == 0 && stream_idle(stream, launched)) break;
+            }
+            ctx.progress(0);
+        });
     KIWI_CUDA_CHECK(cudaStreamSynchronize(stream));
     cudaStreamDestroy(stream);
 
@@ -384,25 +435,28 @@ RttResult pcie_floor(uint64_t iters, uint64_t warmup, int cpu, uint64_t timeout_
     DevBuf<uint32_t> status(2);
     cudaStream_t stream;
     KIWI_CUDA_CHECK(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking));
-    const int c = pick_cpu(cpu);
-    if (c >= 0) topology::bind_current_thread({c});
-    pcie_floor_kernel<<<1, 32, 0, stream>>>(const_cast<uint64_t*>(d2h), const_cast<uint64_t*>(h2d),
-                                            iters, warmup, lat.p, cyc.p, totals.p, status.p,
-                                            timeout_ns);
-    KIWI_CUDA_CHECK(cudaGetLastError());
-    uint64_t expect = 1;
-    uint64_t idle = 0;
-    while (true) {
-        const uint64_t v = *d2h;
-        if (v == ~0ull) break;
-        if (v == expect) {
-            *h2d = v;
-            ++expect;
-            idle = 0;
-        } else if ((++idle & 0xfffff) == 0 && cudaStreamQuery(stream) != cudaErrorNotReady) {
-            break;
-        }
-    }
+    launch_with_server(
+        pick_cpu(cpu),
+        [&] {
+            pcie_floor_kernel<<<1, 32, 0, stream>>>(const_cast<uint64_t*>(d2h), const_cast<uint64_t*>(h2d), iters,
+                                                    warmup, lat.p, cyc.p, totals.p, status.p, timeout_ns);
+            KIWI_CUDA_CHECK(cudaGetLastError());
+        },
+        [&](const std::atomic<bool>& launched, const std::atomic<bool>& quit) {
+            uint64_t expect = 1;
+            uint64_t idle = 0;
+            while (!quit.load(std::memory_order_relaxed)) {
+                const uint64_t v = *d2h;
+                if (v == ~0ull) break;
+                if (v == expect) {
+                    *h2d = v;
+                    ++expect;
+                    idle = 0;
+                } else if ((++idle & 0xfffff) == 0 && stream_idle(stream, launched)) {
+                    break;
+                }
+            }
+        });
     KIWI_CUDA_CHECK(cudaStreamSynchronize(stream));
     cudaStreamDestroy(stream);
     RttResult r;
@@ -673,24 +727,28 @@ RttResult rtt_lab(uint64_t iters, uint64_t warmup, uint32_t pollers, uint32_t mi
     DevBuf<uint32_t> status(2);
     cudaStream_t stream;
     KIWI_CUDA_CHECK(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking));
-    const int c = pick_cpu(cpu);
-    if (c >= 0) topology::bind_current_thread({c});
-    rtt_lab_kernel<<<1, 32 * (1 + pollers), 0, stream>>>(
-        const_cast<uint64_t*>(d2h), const_cast<uint64_t*>(acks), mirrors, iters, warmup, lat.p, cyc.p, totals.p,
-        status.p, pollers, stagger_ns, fence, pipeline, 2000000000ull, initial_delay_ns);
-    KIWI_CUDA_CHECK(cudaGetLastError());
-    uint64_t expect = 1, idle = 0;
-    while (true) {
-        const uint64_t v = *d2h;
-        if (v == ~0ull) break;
-        if (v == expect) {
-            for (uint32_t m = 0; m < mirrors; ++m) acks[16 * m] = v;
-            ++expect;
-            idle = 0;
-        } else if ((++idle & 0xfffff) == 0 && cudaStreamQuery(stream) != cudaErrorNotReady) {
-            break;
-        }
-    }
+    launch_with_server(
+        pick_cpu(cpu),
+        [&] {
+            rtt_lab_kernel<<<1, 32 * (1 + pollers), 0, stream>>>(
+                const_cast<uint64_t*>(d2h), const_cast<uint64_t*>(acks), mirrors, iters, warmup, lat.p, cyc.p,
+                totals.p, status.p, pollers, stagger_ns, fence, pipeline, 2000000000ull, initial_delay_ns);
+            KIWI_CUDA_CHECK(cudaGetLastError());
+        },
+        [&](const std::atomic<bool>& launched, const std::atomic<bool>& quit) {
+            uint64_t expect = 1, idle = 0;
+            while (!quit.load(std::memory_order_relaxed)) {
+                const uint64_t v = *d2h;
+                if (v == ~0ull) break;
+                if (v == expect) {
+                    for (uint32_t m = 0; m < mirrors; ++m) acks[16 * m] = v;
+                    ++expect;
+                    idle = 0;
+                } else if ((++idle & 0xfffff) == 0 && stream_idle(stream, launched)) {
+                    break;
+                }
+            }
+        });
     KIWI_CUDA_CHECK(cudaStreamSynchronize(stream));
     cudaStreamDestroy(stream);
     RttResult r;

@@ -25,6 +25,7 @@ struct RttConfig {
     bool demote = true;              // mailbox: CLDEMOTE each reply line after writing it
     bool adaptive = true;            // mailbox: adapt the delay
     uint64_t timeout_ns = 2000000000ull;
+    uint32_t block_threads = 0;      // launch width (0: the warps used; wider blocks idle the extra warps)
 };
 
 struct RttResult {

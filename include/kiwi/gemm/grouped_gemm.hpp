@@ -101,14 +101,6 @@ void grouped_gemm(const CUtensorMap& tmap_a, const CUtensorMap& tmap_b, const Gr
 /// 4 x 48 KB stages of grouped_gemm do not cover.  Tensor maps from
 /// make_tmap_bf16_2d(..., box_k = 32).  Same results as grouped_gemm (the
 /// same K = 16 MMA sequence).
-/// TMA operand-feed probe: `grid` CTAs (0: one per SM) each stream `iters`
-/// boxes of box_rows x box_k bf16 from the [rows, k] tensor at `ptr` through
-/// `stages` shared-memory stages, releasing each as it lands (no MMAs).
-/// cycles[grid] receives each CTA's SM cycles; error (one word) is non-zero if
-/// a bounded wait ran out.
-void tma_load_rate(const void* ptr, int64_t rows, int64_t k, int box_rows, int box_k, int stages, int64_t iters,
-                   int grid, bool shared_rows, uint64_t* cycles, uint32_t* error, cudaStream_t stream);
-
 /// The 1-SM kernel with 128 columns of K per stage: two 64-column boxes per
 /// operand (the default 128-byte-swizzled maps), 2 stages of 96 KB, the same
 /// MMA order as grouped_gemm.  K must be a multiple of 128.

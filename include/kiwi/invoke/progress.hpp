@@ -70,9 +70,12 @@ public:
         stop_.store(false);
         error_ = nullptr;
         {
+            // A thread that starts after a request has polled nothing the request
+            // drops, so it has applied every generation published before start().
+            const uint32_t gen = static_cast<uint32_t>(active_.load(std::memory_order_acquire) >> 32);
             std::lock_guard<std::mutex> g(seen_mu_);
             seen_.reset(new std::atomic<uint32_t>[num_threads]);
-            for (size_t t = 0; t < num_threads; ++t) seen_[t].store(0, std::memory_order_relaxed);
+            for (size_t t = 0; t < num_threads; ++t) seen_[t].store(gen, std::memory_order_relaxed);
             seen_count_ = num_threads;
         }
         for (size_t t = 0; t < num_threads; ++t) {

@@ -118,10 +118,21 @@ public:
                               " bytes does not fit a ring of " + std::to_string(capacity_) +
                               " lines");
         }
+        // The padding chunks of the last line carry no data but are validated
+        // too, before any payload is copied: the consumer position published
+        // after this pop is the producers' credit, and a padding store still in
+        // flight when a line is handed back could land on the next lap's
+        // message there (from another producer, on an MPSC ring) and leave it
+        // with a stale tag.
+        for (uint32_t k = nchunks > 1 ? nchunks : 1; k < nlines * kChunksPerLine; ++k) {
+            const uint64_t line = line0 + k / kChunksPerLine;
+            const uint32_t tag = lap_tag(line, log2_);
+            const Chunk* c = chunk(line, k % kChunksPerLine);
+            if (!half_has_tag(host::load_half(&c->lo), tag) || !half_has_tag(host::load_half(&c->hi), tag)) {
+                return false;
+            }
+        }
         uint8_t* dst = static_cast<uint8_t*>(out);
-        // Only chunks that carry payload are read: every word is tagged on its
-        // own, and the padding after the last payload chunk carries no data
-        // (the next message starts on the next line).
         for (uint32_t k = 1; k < nchunks; ++k) {
             const uint64_t line = line0 + k / kChunksPerLine;
             const uint32_t tag = lap_tag(line, log2_);

@@ -28,8 +28,9 @@
 //   * A message of B bytes occupies message_lines(B) whole lines starting on a
 //     line; padding chunks of its last line carry tags (and zero data) so the
 //     producer always writes whole 64-byte lines (one PCIe write each).  The
-//     consumer validates the header and payload chunks (one masked compare of
-//     a chunk's 4 tags) and never reads the padding.
+//     consumer validates every chunk of the message's lines, padding included
+//     (one masked compare of a chunk's 4 tags), before it advances and grants
+//     the lines back as credit.
 //   * A message that reaches the end of the ring continues at line 0 with the
 //     next lap's tag.
 //

@@ -116,8 +116,11 @@ def quant_fp8_codes(x, block=128):
     t, h = x.shape
     xf = x.float().view(t, h // block, block)
     amax = xf.abs().amax(-1, keepdim=True)
-    scale = torch.where(amax > 0, amax / FP8_MAX, torch.ones_like(amax))
-    inv = torch.where(amax > 0, FP8_MAX / amax, torch.zeros_like(amax))  # multiply by the reciprocal, as on the device
+    # Tensor operands keep both divisions IEEE, as on the device (a Python
+    # scalar operand makes CUDA multiply by a reciprocal instead).
+    fmax = torch.full_like(amax, FP8_MAX)
+    scale = torch.where(amax > 0, amax / fmax, torch.ones_like(amax))
+    inv = torch.where(amax > 0, fmax / amax, torch.zeros_like(amax))  # then multiply by it, as on the device
     q = (xf * inv).clamp(-FP8_MAX, FP8_MAX).to(torch.float8_e4m3fn)
     return q.view(t, h), scale.view(t, h // block)
 
@@ -171,7 +174,10 @@ def _nvfp4_parts(x, block=16):
     t, h = x.shape
     xf = x.float()
     row_amax = xf.abs().amax(-1, keepdim=True)
-    row_scale = torch.where(row_amax > 0, row_amax / (FP8_MAX * FP4_MAX), torch.zeros_like(row_amax))
+    # A tensor divisor keeps this an IEEE division (a Python scalar divisor
+    # becomes a multiply by its reciprocal on CUDA), as the kernels divide.
+    row_scale = torch.where(row_amax > 0, row_amax / torch.full_like(row_amax, FP8_MAX * FP4_MAX),
+                            torch.zeros_like(row_amax))
     xb = xf.view(t, h // block, block)
     bamax = xb.abs().amax(-1, keepdim=True)
     s = torch.where(row_scale[:, :, None] > 0, bamax / (FP4_MAX * row_scale[:, :, None]), torch.zeros_like(bamax))

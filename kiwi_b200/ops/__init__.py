@@ -11,17 +11,17 @@
 
 * :func:`route_topk`: top-k routing with the softmax over the selected logits
   (the EP layer's routing kernel).
-* :func:`quant_fp8`: 1x128 FP8 quantisation with the dispatch kernel's
-  arithmetic.
+* :func:`quant_fp8` / :func:`quant_nvfp4`: 1x128 FP8 and NVFP4 quantisation
+  with the dispatch kernel's arithmetic (its wire bytes).
 
 Inside the NVLink EP layer, routing and FP8 / NVFP4 quantisation run fused
 into its own kernels (:mod:`kiwi_b200.parallel.ep`); the fp32 references are
 in :mod:`kiwi_b200.models.moe`.
 """
 from .grouped_gemm import ExpertFFN, GroupedGemm, grouped_gemm, grouped_gemm_reference
-from .quant import quant_fp8
+from .quant import quant_fp8, quant_nvfp4
 from .routing import route_topk
 from .rows import accumulate_rows, check_error, copy_rows
 
 __all__ = ["ExpertFFN", "GroupedGemm", "grouped_gemm", "grouped_gemm_reference", "accumulate_rows", "check_error",
-           "copy_rows", "quant_fp8", "route_topk"]
+           "copy_rows", "quant_fp8", "quant_nvfp4", "route_topk"]

@@ -48,7 +48,7 @@ import torch
 import torch.distributed as dist
 
 from ..models import moe as moe_model
-from ..ops import ExpertFFN, quant_fp8, route_topk
+from ..ops import ExpertFFN, quant_fp8, quant_nvfp4, route_topk
 from ..utils import dist as kdist
 
 _FORMATS = {"none": "none", "fp8": "fp8", "fp4": "nvfp4", "nvfp4": "nvfp4"}
@@ -193,7 +193,7 @@ class CollectiveEpOp:
             codes, sc = quant_fp8(x)  # the dispatch kernel's arithmetic on CUDA tensors
             rows, row_scales = codes[order_tok], sc[order_tok]
         elif self._quant == "nvfp4":
-            codes, sc = moe_model.quant_nvfp4_codes(x)  # the NVLink op's wire bytes
+            codes, sc = quant_nvfp4(x)  # the NVLink op's wire bytes (its kernel's arithmetic on CUDA)
             rows, row_scales = codes[order_tok], sc[order_tok]
         else:
             rows, row_scales = x.to(torch.bfloat16)[order_tok], None

@@ -51,3 +51,20 @@ def test_argument_checks(lib, groups, n, k, a, c, rows, code, words):
 
 def test_max_groups(lib):
     assert lib.kiwi_noalloc_max_groups() == 1024
+
+
+def test_error_word_reader_rejects_a_null_destination(lib):
+    """kiwi_noalloc_error_word checks its host pointer before any CUDA call."""
+    fn = lib.kiwi_noalloc_error_word
+    fn.restype = ctypes.c_int
+    fn.argtypes = [ctypes.c_void_p, ctypes.c_void_p]
+    assert fn(None, None) == 3
+    assert "null host_out" in lib.kiwi_noalloc_last_error().decode()
+
+
+def test_header_declares_every_exported_symbol():
+    """include/kiwi/gemm/noalloc.h declares the four C symbols the library exports."""
+    text = open(os.path.join(ROOT, "include", "kiwi", "gemm", "noalloc.h")).read()
+    for name in ("kiwi_noalloc_max_groups", "kiwi_noalloc_last_error", "kiwi_grouped_gemm_bf16_noalloc",
+                 "kiwi_noalloc_error_word"):
+        assert name + "(" in text

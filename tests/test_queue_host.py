@@ -145,15 +145,44 @@ def test_corrupt_length_raises():
         q.try_pop()
 
 
-def test_padding_chunks_are_not_read():
-    """Only chunks that carry payload are validated: a message whose padding
-    chunks were never written pops (the next message starts on the next line)."""
+def test_missing_padding_blocks_pop_and_credit():
+    """The padding chunks of a message's last line are validated before the
+    consumer advances (reference: src/queue/chunk_consumer.hpp:117-121 of
+    AMDResearch/kiwi): a message whose padding has not landed is not popped and
+    its line is not handed back as credit; once the padding lands it pops."""
     q = kq.SPSCD2HQueue(4, host_only=True)
     w = q.host_writer()
-    w.write_chunks(b"12345678", 3, 0, 2)  # header + the one payload chunk
+    w.write_chunks(b"12345678", 3, 0, 2)  # header + the one payload chunk, no padding yet
+    assert q.try_pop() is None
+    assert q.consumer_position == 0
+    w.write_chunks(b"12345678", 3, 2, 4)  # the padding lands
     w.advance(1)
     assert q.try_pop() == (b"12345678", 3)
+    assert q.consumer_position == 1
     assert q.try_pop() is None
+
+
+def test_late_padding_store_cannot_reach_the_next_lap():
+    """MPSC hazard: producer A's padding store is delayed while producer B
+    writes the next line.  The consumer holds A (and the credit for A's line)
+    until A's padding lands, so A's late store lands on A's own lap and the
+    next lap's message written at that line afterwards pops intact."""
+    q = kq.MPSCD2HQueue(2, host_only=True)
+    w = q.host_writer()
+    w.write_chunks(b"AAAAAAAA", 1, 0, 2)  # A at line 0, padding delayed
+    w.advance(1)
+    assert w.try_push(b"BBBBBBBB", 2)     # B at line 1, complete
+    assert q.try_pop() is None           # A is held: no line goes back as credit
+    assert q.consumer_position == 0
+    assert not w.try_push(b"CCCCCCCC", 3)  # the ring is full until A is consumed
+    # A's late padding store: it carries A's (lap 0) tag and lands on A's line
+    tag0 = kq.lap_tag(0, 2)
+    for chunk in (2, 3):
+        q.corrupt_line(0, chunk, 0, tag0, 0, tag0)
+    assert q.try_pop() == (b"AAAAAAAA", 1)
+    assert q.try_pop() == (b"BBBBBBBB", 2)
+    assert w.try_push(b"CCCCCCCC", 3)      # lap 1 at line 0, after A's padding landed
+    assert q.try_pop() == (b"CCCCCCCC", 3)
 
 
 def test_wrong_tag_in_payload_chunk_blocks_pop():

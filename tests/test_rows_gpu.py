@@ -64,3 +64,27 @@ def test_quant_fp8_matches_the_reference(hidden):
     diff = (codes.float() - rc.float()).abs()
     assert (diff > 0).float().mean().item() < 5e-3
     assert (diff <= torch.maximum(rc.float().abs(), codes.float().abs()) * 0.125 + 2.0 ** -9).all()  # one code
+
+
+@pytest.mark.parametrize("hidden", [512, 4096, 7168, 80])
+def test_quant_nvfp4_matches_the_reference(hidden):
+    """kiwi_b200.ops.quant_nvfp4 (the dispatch kernel's NVFP4 arithmetic in a
+    kernel of its own) against the fp32 reference: equal row scales, block
+    scales and padding; codes equal except where a value lies exactly between
+    two e2m1 codes; an all-zero row gets zero scales and codes."""
+    from kiwi_b200.models import moe
+
+    torch.manual_seed(hidden + 1)
+    x = (torch.randn(41, hidden, device="cuda") * 2).bfloat16()
+    x[7] = 0
+    codes, scales = ops.quant_nvfp4(x)
+    rc, rs = moe.quant_nvfp4_codes(x)
+    assert codes.dtype == torch.uint8 and tuple(codes.shape) == (41, hidden // 2)
+    assert tuple(scales.shape) == tuple(rs.shape) == (41, moe.nvfp4_scale_bytes(hidden))
+    assert torch.equal(scales, rs)
+    assert bool((codes[7] == 0).all()) and bool((scales[7] == 0).all())
+    d = moe.dequant_nvfp4(codes, scales)
+    r = moe.dequant_nvfp4(rc, rs)
+    assert (d != r).float().mean().item() < 1e-3
+    ref = moe.quant_nvfp4_reference(x)
+    assert torch.equal(r, ref)
