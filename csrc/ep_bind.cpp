@@ -36,6 +36,20 @@ ep::EpConfig config_from_dict(const py::dict& d) {
     c.num_experts = d["num_experts"].cast<int>();
     c.topk = d["topk"].cast<int>();
     c.max_tokens = d["max_tokens"].cast<int>();
+    if (d.contains("comb_dtype")) {
+        if (py::isinstance<py::int_>(d["comb_dtype"])) {
+            c.comb_dtype = d["comb_dtype"].cast<int>();
+        } else {
+            const std::string cd = d["comb_dtype"].cast<std::string>();
+            if (cd == "bf16") c.comb_dtype = static_cast<int>(ep::CombDtype::kBf16);
+            else if (cd == "f32" || cd == "float32") c.comb_dtype = static_cast<int>(ep::CombDtype::kF32);
+            else if (cd == "fp8") c.comb_dtype = static_cast<int>(ep::CombDtype::kFp8);
+            else if (cd == "fp4") c.comb_dtype = static_cast<int>(ep::CombDtype::kFp4);
+            else throw kiwi::error("unknown combine dtype " + cd);
+        }
+    }
+    if (d.contains("comb_weights")) c.comb_weights = d["comb_weights"].cast<bool>() ? 1 : 0;
+    if (d.contains("min_scale_bytes")) c.min_scale_bytes = d["min_scale_bytes"].cast<int>();
     if (py::isinstance<py::int_>(d["quant"])) {
         c.quant = d["quant"].cast<int>();
         return ep::finalize(c);
@@ -58,6 +72,11 @@ py::dict config_to_dict(const ep::EpConfig& c) {
     d["topk"] = c.topk;
     d["max_tokens"] = c.max_tokens;
     d["quant"] = c.quant;
+    d["comb_dtype"] = c.comb_dtype;
+    d["comb_weights"] = c.comb_weights;
+    d["min_scale_bytes"] = c.min_scale_bytes;
+    d["comb_row_bytes"] = c.comb_row_bytes;
+    d["comb_bytes"] = c.comb_bytes;
     d["row_bytes"] = c.row_bytes;
     d["scale_bytes"] = c.scale_bytes;
     d["meta_bytes"] = c.meta_bytes;
@@ -238,7 +257,11 @@ public:
 
     void receive() {
         cudaStream_t s = cur_stream();
-        ep::launch_recv_count(cfg_, heap_.view(), ws_, timeout_ns_, s);
+        // The flag wait runs in a 32-thread kernel of its own, so no kernel that
+        // fills the GPU spins on other ranks (two layers' rounds may run on two
+        // streams at once).
+        ep::launch_wait_flags(cfg_, heap_.view(), ws_, 0, timeout_ns_, s);
+        ep::launch_recv_count(cfg_, heap_.view(), ws_, timeout_ns_, s, /*waited=*/true);
         const int bm = pair_ ? 256 : 128;
         gemm::build_schedule(ws_.expert_count, cfg_.experts_per_rank, static_cast<int>(2 * ffn_), 256, ws_.offsets,
                              ws_.tiles1, s, bm);
@@ -326,16 +349,18 @@ public:
                         idx.size(1) == cfg_.topk && idx.size(0) == out.size(0) && out.size(0) <= cfg_.max_tokens,
                     "idx must be the round's contiguous int32 [T, topk] with T = out rows <= max_tokens");
         if (fused_) {
+            ep::launch_wait_flags(cfg_, heap_.view(), ws_, 1, timeout_ns_, s);
             ep::launch_combine_recv_fused(cfg_, heap_.view(), idx.data_ptr<int32_t>(), static_cast<int>(out.size(0)),
                                           reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), ws_, timeout_ns_, s,
-                                          tuning_.combine_blocks);
+                                          tuning_.combine_blocks, /*waited=*/true);
             return;
         }
         ep::launch_combine_send(cfg_, heap_.view(), reinterpret_cast<const __nv_bfloat16*>(y_.data_ptr()), ws_,
                                 tuning_.combine_blocks, s);
+        ep::launch_wait_flags(cfg_, heap_.view(), ws_, 1, timeout_ns_, s);
         ep::launch_combine_recv(cfg_, heap_.view(), idx.data_ptr<int32_t>(), static_cast<int>(out.size(0)),
                                 reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), ws_, timeout_ns_, s,
-                                tuning_.combine_blocks);
+                                tuning_.combine_blocks, nullptr, /*waited=*/true);
     }
 
     /// The whole layer: x [T, hidden] bf16, idx [T, topk] int32, w [T, topk] fp32 -> out [T, hidden] bf16.
@@ -468,19 +493,53 @@ public:
         ws_.error = reinterpret_cast<uint32_t*>(error_.data_ptr<int32_t>());
     }
 
-    py::tuple dispatch(torch::Tensor x, torch::Tensor idx, torch::Tensor w) {
-        TORCH_CHECK(x.scalar_type() == torch::kBFloat16 && x.is_contiguous() && x.size(1) == cfg_.hidden,
-                    "x must be contiguous bf16 [T, hidden]");
+    /// x: bf16 [T, hidden] (quantised here on an FP8 / NVFP4 op), or the
+    /// caller's wire bytes [T, row_bytes] (any one-byte dtype) on an FP8 /
+    /// NVFP4 op.  scales: the caller's per-token scales [T, ...] (any dtype),
+    /// carried as bytes; not allowed with bf16 input on an FP8 / NVFP4 op.
+    py::tuple dispatch(torch::Tensor x, torch::Tensor idx, torch::Tensor w, py::object scales, int grid) {
+        TORCH_CHECK(x.is_cuda() && x.is_contiguous() && x.dim() == 2, "x must be a contiguous 2-D CUDA tensor");
         TORCH_CHECK(x.size(0) <= cfg_.max_tokens, "more tokens than max_tokens");
-        TORCH_CHECK(idx.scalar_type() == torch::kInt32 && idx.is_contiguous() && idx.size(1) == cfg_.topk, "idx");
-        TORCH_CHECK(w.scalar_type() == torch::kFloat32 && w.is_contiguous() && w.size(1) == cfg_.topk, "w");
+        TORCH_CHECK(idx.scalar_type() == torch::kInt32 && idx.is_contiguous() && idx.size(1) == cfg_.topk &&
+                        idx.size(0) == x.size(0),
+                    "idx must be contiguous int32 [T, topk]");
+        TORCH_CHECK(w.scalar_type() == torch::kFloat32 && w.is_contiguous() && w.size(1) == cfg_.topk &&
+                        w.size(0) == x.size(0),
+                    "w must be contiguous fp32 [T, topk]");
+        const void* sp = nullptr;
+        int sbytes = 0;
+        if (!scales.is_none()) {
+            torch::Tensor sc = scales.cast<torch::Tensor>();
+            TORCH_CHECK(sc.is_cuda() && sc.is_contiguous() && sc.dim() >= 1 && sc.size(0) == x.size(0),
+                        "scales must be a contiguous CUDA tensor with one row per token");
+            if (sc.size(0) > 0 && sc.numel() > 0) {
+                sbytes = static_cast<int>(sc.numel() / sc.size(0) * sc.element_size());
+                TORCH_CHECK(sbytes <= cfg_.scale_bytes, "scales: ", sbytes, " bytes per token exceed the op's ",
+                            cfg_.scale_bytes, " (set dispatch_scale_dim / dispatch_scale_type_size)");
+                sp = sc.data_ptr();
+                scales_in_ = sc;
+            }
+        }
         cudaStream_t s = cur_stream();
         idx_in_ = idx;
         tokens_ = static_cast<int>(x.size(0));
         debug_.reset(s);
         ep::launch_begin(cfg_, ws_, s);
-        ep::launch_dispatch(cfg_, heap_.view(), reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()),
-                            idx.data_ptr<int32_t>(), w.data_ptr<float>(), tokens_, ws_, 0, s);
+        if (x.scalar_type() != torch::kBFloat16) {
+            TORCH_CHECK(cfg_.quant != static_cast<int>(ep::Quant::kNone),
+                        "pre-quantised rows need an FP8 or NVFP4 op (dispatch_quant_format)");
+            TORCH_CHECK(x.size(1) * x.element_size() == cfg_.row_bytes, "pre-quantised rows must be [T, ",
+                        cfg_.row_bytes, " bytes]");
+            ep::launch_dispatch_raw(cfg_, heap_.view(), x.data_ptr(), sp, sbytes, idx.data_ptr<int32_t>(),
+                                    w.data_ptr<float>(), tokens_, ws_, grid, s);
+        } else {
+            TORCH_CHECK(x.size(1) == cfg_.hidden, "x must be bf16 [T, hidden]");
+            TORCH_CHECK(sp == nullptr || cfg_.quant == static_cast<int>(ep::Quant::kNone),
+                        "an FP8 / NVFP4 op quantises bf16 rows itself and makes their scales; pass pre-quantised "
+                        "rows to use your own scales");
+            ep::launch_dispatch(cfg_, heap_.view(), reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()),
+                                idx.data_ptr<int32_t>(), w.data_ptr<float>(), tokens_, ws_, grid, s, sp, sbytes);
+        }
         ep::launch_recv_count(cfg_, heap_.view(), ws_, timeout_ns_, s);
         ep::launch_recv_compact(cfg_, heap_.view(), ws_, slot_compact_.data_ptr<int32_t>(),
                                 recv_count_.data_ptr<int32_t>(), s);
@@ -490,18 +549,38 @@ public:
         return py::make_tuple(rows_, w_, scales_, idx_, recv_count_);
     }
 
-    torch::Tensor combine(torch::Tensor rows, torch::Tensor out) {
-        TORCH_CHECK(rows.scalar_type() == torch::kBFloat16 && rows.is_contiguous() && rows.size(1) == cfg_.hidden,
-                    "rows must be contiguous bf16 [>= recv_count, hidden]");
-        TORCH_CHECK(out.scalar_type() == torch::kBFloat16 && out.is_contiguous() && out.size(0) >= tokens_ &&
-                        out.size(1) == cfg_.hidden,
-                    "out must be contiguous bf16 [T, hidden]");
+    /// rows: [>= recv_count, comb_row_bytes] in the combine dtype; weights: fp32
+    /// [>= recv_count, topk] or None; out: [>= T, comb_row_bytes]; out_w: fp32
+    /// [>= T, topk] (required with weights).
+    torch::Tensor combine(torch::Tensor rows, torch::Tensor out, py::object weights, py::object out_w) {
+        TORCH_CHECK(rows.is_cuda() && rows.is_contiguous() && rows.dim() == 2 &&
+                        rows.size(1) * rows.element_size() == cfg_.comb_row_bytes,
+                    "rows must be contiguous [>= recv_count, hidden] in the combine dtype");
+        TORCH_CHECK(out.is_cuda() && out.is_contiguous() && out.dim() == 2 && out.size(0) >= tokens_ &&
+                        out.size(1) * out.element_size() == cfg_.comb_row_bytes,
+                    "out must be contiguous [T, hidden] in the combine dtype");
         TORCH_CHECK(idx_in_.defined(), "combine needs a prior dispatch");
+        const float* wp = nullptr;
+        float* owp = nullptr;
+        if (!weights.is_none()) {
+            torch::Tensor wt = weights.cast<torch::Tensor>();
+            TORCH_CHECK(wt.scalar_type() == torch::kFloat32 && wt.is_contiguous() && wt.dim() == 2 &&
+                            wt.size(1) == cfg_.topk && wt.size(0) >= rows.size(0),
+                        "weights must be contiguous fp32 [rows, topk]");
+            TORCH_CHECK(!out_w.is_none(), "weights need an output weight buffer");
+            torch::Tensor ow = out_w.cast<torch::Tensor>();
+            TORCH_CHECK(ow.scalar_type() == torch::kFloat32 && ow.is_contiguous() && ow.dim() == 2 &&
+                            ow.size(1) == cfg_.topk && ow.size(0) >= tokens_,
+                        "out_weights must be contiguous fp32 [T, topk]");
+            wp = wt.data_ptr<float>();
+            owp = ow.data_ptr<float>();
+            weights_in_ = wt;
+        }
         cudaStream_t s = cur_stream();
-        ep::launch_combine_rows(cfg_, heap_.view(), reinterpret_cast<const __nv_bfloat16*>(rows.data_ptr()),
-                                src_pos_.data_ptr<int32_t>(), recv_count_.data_ptr<int32_t>(), ws_, s);
-        ep::launch_combine_recv(cfg_, heap_.view(), idx_in_.data_ptr<int32_t>(), tokens_,
-                                reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), ws_, timeout_ns_, s);
+        ep::launch_combine_rows(cfg_, heap_.view(), rows.data_ptr(), wp, src_pos_.data_ptr<int32_t>(),
+                                recv_count_.data_ptr<int32_t>(), ws_, s);
+        ep::launch_combine_recv(cfg_, heap_.view(), idx_in_.data_ptr<int32_t>(), tokens_, out.data_ptr(), ws_,
+                                timeout_ns_, s, 0, owp);
         return out;
     }
 
@@ -537,7 +616,7 @@ private:
     uint64_t timeout_ns_;
     int tokens_ = 0;
     torch::Tensor epoch_, done_, counts_, cursor_, slot_tokens_, error_, slot_compact_, recv_count_, rows_, scales_,
-        idx_, w_, src_pos_, idx_in_;
+        idx_, w_, src_pos_, idx_in_, scales_in_, weights_in_;
     ep::EpWorkspace ws_{};
     DebugTiming debug_;
 };
@@ -583,8 +662,10 @@ void register_ep(py::module_& m) {
     py::class_<Transport>(e, "Transport")
         .def(py::init<p2p::SymmetricHeap&, const py::dict&, uint64_t>(), py::arg("heap"), py::arg("config"),
              py::arg("timeout_ns") = 5000000000ull, py::keep_alive<1, 2>())
-        .def("dispatch", &Transport::dispatch)
-        .def("combine", &Transport::combine)
+        .def("dispatch", &Transport::dispatch, py::arg("x"), py::arg("idx"), py::arg("w"),
+             py::arg("scales") = py::none(), py::arg("grid") = 0)
+        .def("combine", &Transport::combine, py::arg("rows"), py::arg("out"), py::arg("weights") = py::none(),
+             py::arg("out_weights") = py::none())
         .def("error", &Transport::error)
         .def("set_debug_timing_enabled", &Transport::set_debug_timing_enabled, py::arg("enabled"))
         .def_property_readonly("debug_timing_enabled", &Transport::debug_timing_enabled)

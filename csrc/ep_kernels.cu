@@ -33,6 +33,7 @@ namespace kiwi::ep {
 namespace {
 
 constexpr int kThreads = 256;
+constexpr int kDispatchRaw = 3;  // dispatch_kernel mode: caller-quantised rows travel as bytes
 
 KIWI_DEV void set_error(const EpWorkspace& ws, uint32_t code, uint32_t site, uint32_t info, int rank) {
     if (atomicCAS(&ws.error[0], 0u, code) == 0u) {
@@ -53,6 +54,11 @@ KIWI_DEV uint4 ld_cg_v4(const void* p) {
     asm volatile("ld.global.cg.v4.u32 {%0, %1, %2, %3}, [%4];"
                  : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
                  : "l"(p));
+    return v;
+}
+KIWI_DEV uint2 ld_cg_v2(const void* p) {
+    uint2 v;
+    asm volatile("ld.global.cg.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p));
     return v;
 }
 KIWI_DEV uint32_t ld_cg_u32(const void* p) {
@@ -199,7 +205,8 @@ KIWI_DEV void warp_copy_out(uint8_t* dst, const uint8_t* src, int bytes, int lan
 template <int QUANT>
 __global__ void __launch_bounds__(kThreads) dispatch_kernel(EpConfig c, p2p::HeapView h, const __nv_bfloat16* x,
                                                             const int32_t* idx, const float* w, int tokens,
-                                                            EpWorkspace ws) {
+                                                            EpWorkspace ws, const uint8_t* raw_scales,
+                                                            int raw_scale_bytes) {
     PhaseScope ps_(ws.debug_time, kPhaseDispatch);
     extern __shared__ __align__(16) uint8_t dyn_smem[];
     const int lane = threadIdx.x & 31;
@@ -228,7 +235,17 @@ __global__ void __launch_bounds__(kThreads) dispatch_kernel(EpConfig c, p2p::Hea
             *reinterpret_cast<uint32_t*>(s_meta + o) = 0;
         }
         const __nv_bfloat16* xr = x + static_cast<int64_t>(t) * c.hidden;
-        if constexpr (QUANT == static_cast<int>(Quant::kNone)) {
+        if constexpr (QUANT == kDispatchRaw) {
+            // Pre-quantised by the caller: the row's wire bytes travel unchanged.
+            const uint8_t* rr = reinterpret_cast<const uint8_t*>(x) + static_cast<int64_t>(t) * c.row_bytes;
+            for (int o = lane * 16; o < c.row_bytes; o += 32 * 16) {
+                const uint4 v = ptx::ld_nc_v4(rr + o);
+                for (uint32_t m = mask; m; m &= m - 1) {
+                    const int r = __ffs(m) - 1;
+                    ptx::st_v4(h.base[r] + c.row_off(slot) + o, v);
+                }
+            }
+        } else if constexpr (QUANT == static_cast<int>(Quant::kNone)) {
             for (int col = lane * 8; col < c.hidden; col += 256) {
                 const uint4 v = ptx::ld_nc_v4(xr + col);
                 for (uint32_t m = mask; m; m &= m - 1) {
@@ -281,6 +298,12 @@ __global__ void __launch_bounds__(kThreads) dispatch_kernel(EpConfig c, p2p::Hea
             // Zero the staging tail past the last block scale (the slot layout pads to 16 bytes).
             for (int o = 4 + c.hidden / kFp4Block + lane; o < c.scale_bytes; o += 32) s_scale[o] = 0;
         }
+        if (raw_scales) {
+            // The caller's own per-token scales (bf16 or pre-quantised rows): copied
+            // as bytes, zero padded to the slot's scale room.
+            const uint8_t* sr = raw_scales + static_cast<int64_t>(t) * raw_scale_bytes;
+            for (int o = lane; o < c.scale_bytes; o += 32) s_scale[o] = o < raw_scale_bytes ? sr[o] : 0;
+        }
         __syncwarp();
         for (uint32_t m = mask; m; m &= m - 1) {
             const int r = __ffs(m) - 1;
@@ -292,16 +315,47 @@ __global__ void __launch_bounds__(kThreads) dispatch_kernel(EpConfig c, p2p::Hea
                      (static_cast<uint64_t>(epoch) << 32) | static_cast<uint32_t>(tokens));
 }
 
+/// One warp waits for every rank's dispatch (which == 0) or combine
+/// (which == 1) flag of this round and, for dispatch, records each source's
+/// token count in ws.slot_tokens.  Launched on its own ahead of the kernel
+/// that reads the data (which is then launched with waited = true), so the
+/// only kernel that spins on another GPU is this 32-thread one: it never
+/// holds the SMs that a concurrently scheduled kernel of another stream needs.
+__global__ void __launch_bounds__(32) wait_flags_kernel(EpConfig c, p2p::HeapView h, EpWorkspace ws, int which,
+                                                        uint64_t timeout_ns) {
+    PhaseScope ps_(ws.debug_time, which == 0 ? kPhaseDispatchWait : kPhaseCombineWait);
+    __shared__ uint32_t s_tokens[kMaxRanks];
+    const uint32_t epoch = *reinterpret_cast<volatile uint32_t*>(ws.epoch);
+    const bool ok = which == 0
+                        ? wait_all_flags(c, h, ws, epoch, [&](int src) { return c.dispatch_flag(src); },
+                                         kSiteDispatchWait, timeout_ns, s_tokens, ps_)
+                        : wait_all_flags(c, h, ws, epoch, [&](int src) { return c.combine_flag(src); },
+                                         kSiteCombineWait, timeout_ns, nullptr, ps_);
+    if (ok && which == 0 && threadIdx.x < static_cast<unsigned>(c.world)) ws.slot_tokens[threadIdx.x] = s_tokens[threadIdx.x];
+}
+
+/// True when an earlier kernel of this round recorded an error (a wait ran out).
+KIWI_DEV bool round_failed(const EpWorkspace& ws) { return *reinterpret_cast<volatile uint32_t*>(ws.error) != 0; }
+
 __global__ void __launch_bounds__(kThreads) recv_count_kernel(EpConfig c, p2p::HeapView h, EpWorkspace ws,
-                                                              uint64_t timeout_ns) {
+                                                              uint64_t timeout_ns, int waited) {
     PhaseScope ps_(ws.debug_time, kPhaseRecvCount);
     __shared__ uint32_t s_tokens[kMaxRanks];
     const uint32_t epoch = *reinterpret_cast<volatile uint32_t*>(ws.epoch);
-    if (!wait_all_flags(c, h, ws, epoch, [&](int src) { return c.dispatch_flag(src); }, kSiteDispatchWait,
-                        timeout_ns, s_tokens, ps_)) {
-        return;
+    if (waited) {
+        // wait_flags_kernel ran first on this stream and stored the counts.
+        if (round_failed(ws)) return;
+        if (threadIdx.x < static_cast<unsigned>(c.world)) {
+            s_tokens[threadIdx.x] = static_cast<uint32_t>(*reinterpret_cast<volatile int32_t*>(ws.slot_tokens + threadIdx.x));
+        }
+        __syncthreads();
+    } else {
+        if (!wait_all_flags(c, h, ws, epoch, [&](int src) { return c.dispatch_flag(src); }, kSiteDispatchWait,
+                            timeout_ns, s_tokens, ps_)) {
+            return;
+        }
+        if (blockIdx.x == 0 && threadIdx.x < static_cast<unsigned>(c.world)) ws.slot_tokens[threadIdx.x] = s_tokens[threadIdx.x];
     }
-    if (blockIdx.x == 0 && threadIdx.x < static_cast<unsigned>(c.world)) ws.slot_tokens[threadIdx.x] = s_tokens[threadIdx.x];
     const int e0 = c.rank * c.experts_per_rank;
     const uint8_t* base = h.base[h.rank];
     for (uint64_t s = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x; s < c.slots();
@@ -510,26 +564,119 @@ __global__ void __launch_bounds__(kThreads) combine_send_kernel(EpConfig c, p2p:
     grid_done_signal(c, h, &ws.done_ctas[1], c.combine_flag(c.rank), (static_cast<uint64_t>(epoch) << 32) | 1u);
 }
 
+/// Raw bytes of 8 consecutive elements of a combine row in CombDtype DT
+/// (bf16: 16 bytes, fp32: 32, FP8: 8, FP4: 4).
+struct Comb8 {
+    uint4 a, b;
+};
+
+template <int DT>
+KIWI_DEV Comb8 comb_load8(const uint8_t* row, int col) {
+    Comb8 r{make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0)};
+    if constexpr (DT == static_cast<int>(CombDtype::kBf16)) {
+        r.a = ld_cg_v4(row + 2ull * col);
+    } else if constexpr (DT == static_cast<int>(CombDtype::kF32)) {
+        r.a = ld_cg_v4(row + 4ull * col);
+        r.b = ld_cg_v4(row + 4ull * col + 16);
+    } else if constexpr (DT == static_cast<int>(CombDtype::kFp8)) {
+        const uint2 v = ld_cg_v2(row + col);
+        r.a.x = v.x;
+        r.a.y = v.y;
+    } else {
+        r.a.x = ld_cg_u32(row + col / 2);
+    }
+    return r;
+}
+
+template <int DT>
+KIWI_DEV void comb_decode8(const Comb8& r, float (&f)[8]) {
+    if constexpr (DT == static_cast<int>(CombDtype::kBf16)) {
+        bf16x8_to_f32(r.a, f);
+    } else if constexpr (DT == static_cast<int>(CombDtype::kF32)) {
+        f[0] = __uint_as_float(r.a.x); f[1] = __uint_as_float(r.a.y);
+        f[2] = __uint_as_float(r.a.z); f[3] = __uint_as_float(r.a.w);
+        f[4] = __uint_as_float(r.b.x); f[5] = __uint_as_float(r.b.y);
+        f[6] = __uint_as_float(r.b.z); f[7] = __uint_as_float(r.b.w);
+    } else if constexpr (DT == static_cast<int>(CombDtype::kFp8)) {
+        const uint32_t w[2] = {r.a.x, r.a.y};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const __half2_raw hr = __nv_cvt_fp8x2_to_halfraw2(
+                static_cast<__nv_fp8x2_storage_t>((w[i / 2] >> (16 * (i & 1))) & 0xffffu), __NV_E4M3);
+            const float2 t = __half22float2(*reinterpret_cast<const __half2*>(&hr));
+            f[2 * i] = t.x;
+            f[2 * i + 1] = t.y;
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const __half2_raw hr =
+                __nv_cvt_fp4x2_to_halfraw2(static_cast<__nv_fp4x2_storage_t>((r.a.x >> (8 * i)) & 0xffu), __NV_E2M1);
+            const float2 t = __half22float2(*reinterpret_cast<const __half2*>(&hr));
+            f[2 * i] = t.x;
+            f[2 * i + 1] = t.y;
+        }
+    }
+}
+
+/// Stores 8 fp32 values as combine-row elements of CombDtype DT; FP8 and FP4
+/// round to nearest and saturate (e4m3 at +-448, e2m1 at +-6).
+template <int DT>
+KIWI_DEV void comb_store8(uint8_t* row, int col, const float (&f)[8]) {
+    if constexpr (DT == static_cast<int>(CombDtype::kBf16)) {
+        ptx::st_v4(row + 2ull * col, f32x8_to_bf16(f));
+    } else if constexpr (DT == static_cast<int>(CombDtype::kF32)) {
+        ptx::st_v4(row + 4ull * col, make_uint4(__float_as_uint(f[0]), __float_as_uint(f[1]), __float_as_uint(f[2]),
+                                                 __float_as_uint(f[3])));
+        ptx::st_v4(row + 4ull * col + 16, make_uint4(__float_as_uint(f[4]), __float_as_uint(f[5]),
+                                                      __float_as_uint(f[6]), __float_as_uint(f[7])));
+    } else if constexpr (DT == static_cast<int>(CombDtype::kFp8)) {
+        uint32_t w[2];
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+            const uint32_t lo = __nv_cvt_float2_to_fp8x2(make_float2(f[4 * i], f[4 * i + 1]), __NV_SATFINITE, __NV_E4M3);
+            const uint32_t hi =
+                __nv_cvt_float2_to_fp8x2(make_float2(f[4 * i + 2], f[4 * i + 3]), __NV_SATFINITE, __NV_E4M3);
+            w[i] = lo | (hi << 16);
+        }
+        *reinterpret_cast<uint2*>(row + col) = make_uint2(w[0], w[1]);
+    } else {
+        uint32_t w = 0;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            w |= static_cast<uint32_t>(__nv_cvt_float2_to_fp4x2(make_float2(f[2 * i], f[2 * i + 1]), __NV_E2M1,
+                                                                 cudaRoundNearest))
+                 << (8 * i);
+        }
+        *reinterpret_cast<uint32_t*>(row + col / 2) = w;
+    }
+}
+
 /// Combine, receive side: after every rank's flag, each (token, 256-column
-/// block) sums the rows the token's destination ranks returned.
-template <int MAXR>
+/// block) sums, in fp32, the rows the token's destination ranks returned and
+/// writes the sum in the combine dtype DT.  With out_w, the (token, block 0)
+/// item also sums the top-k weights that came back with those rows.
+template <int DT, int MAXR>
 __global__ void __launch_bounds__(kThreads) combine_recv_kernel(EpConfig c, p2p::HeapView h, const int32_t* idx,
-                                                                int tokens, __nv_bfloat16* out, EpWorkspace ws,
-                                                                uint64_t timeout_ns) {
+                                                                int tokens, uint8_t* out, float* out_w,
+                                                                EpWorkspace ws, uint64_t timeout_ns, int waited) {
     PhaseScope ps_(ws.debug_time, kPhaseCombineRecv);
     const int lane = threadIdx.x & 31;
     const int warps = gridDim.x * (blockDim.x / 32);
     const uint32_t epoch = *reinterpret_cast<volatile uint32_t*>(ws.epoch);
-    if (!wait_all_flags(c, h, ws, epoch, [&](int src) { return c.combine_flag(src); }, kSiteCombineWait, timeout_ns,
-                        nullptr, ps_)) {
+    if (waited) {
+        if (round_failed(ws)) return;
+    } else if (!wait_all_flags(c, h, ws, epoch, [&](int src) { return c.combine_flag(src); }, kSiteCombineWait,
+                               timeout_ns, nullptr, ps_)) {
         return;
     }
     const uint8_t* base = h.base[h.rank];
-    const int blocks = c.hidden / 256;
+    const int blocks = (c.hidden + 255) / 256;
     const uint64_t items = static_cast<uint64_t>(tokens) * blocks;
     for (uint64_t it = (blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x) / 32; it < items; it += warps) {
         const int t = static_cast<int>(it / blocks);
-        const int col = static_cast<int>(it % blocks) * 256 + lane * 8;
+        const int blk = static_cast<int>(it % blocks);
+        const int col = blk * 256 + lane * 8;
         const int e = lane < c.topk ? idx[static_cast<int64_t>(t) * c.topk + lane] : -1;
         const bool ok_e = e >= 0 && e < c.num_experts;
         uint32_t m = __reduce_or_sync(0xffffffffu, ok_e ? (1u << (e / c.experts_per_rank)) : 0u);
@@ -543,9 +690,31 @@ __global__ void __launch_bounds__(kThreads) combine_recv_kernel(EpConfig c, p2p:
                 m &= m - 1;
             }
         }
-        float acc[8];
-        sum_rows<MAXR>(nr, [&](int j) { return ld_cg_v4(base + c.comb_off(rl[j], t) + 2ull * col); }, acc);
-        ptx::st_v4(out + static_cast<int64_t>(t) * c.hidden + col, f32x8_to_bf16(acc));
+        if (col < c.hidden) {
+            Comb8 v[MAXR];
+#pragma unroll
+            for (int j = 0; j < MAXR; ++j) {
+                if (j < nr) v[j] = comb_load8<DT>(base + c.comb_off(rl[j], t), col);
+            }
+            float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+            for (int j = 0; j < MAXR; ++j) {
+                if (j < nr) {
+                    float f[8];
+                    comb_decode8<DT>(v[j], f);
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) acc[i] += f[i];
+                }
+            }
+            comb_store8<DT>(out + static_cast<int64_t>(t) * c.comb_row_bytes, col, acc);
+        }
+        if (out_w && blk == 0 && lane < c.topk) {
+            float sw = 0.f;
+            for (int j = 0; j < nr; ++j) {
+                sw += ld_cg_f32(base + c.comb_off(rl[j], t) + c.comb_row_bytes + 4 * lane);
+            }
+            out_w[static_cast<int64_t>(t) * c.topk + lane] = sw;
+        }
     }
 }
 
@@ -554,13 +723,15 @@ __global__ void __launch_bounds__(kThreads) combine_recv_kernel(EpConfig c, p2p:
 template <int MAXK>
 __global__ void __launch_bounds__(kThreads) combine_recv_fused_kernel(EpConfig c, p2p::HeapView h, const int32_t* idx,
                                                                       int tokens, __nv_bfloat16* out, EpWorkspace ws,
-                                                                      uint64_t timeout_ns) {
+                                                                      uint64_t timeout_ns, int waited) {
     PhaseScope ps_(ws.debug_time, kPhaseCombineRecv);
     const int lane = threadIdx.x & 31;
     const int warps = gridDim.x * (blockDim.x / 32);
     const uint32_t epoch = *reinterpret_cast<volatile uint32_t*>(ws.epoch);
-    if (!wait_all_flags(c, h, ws, epoch, [&](int src) { return c.combine_flag(src); }, kSiteCombineWait, timeout_ns,
-                        nullptr, ps_)) {
+    if (waited) {
+        if (round_failed(ws)) return;
+    } else if (!wait_all_flags(c, h, ws, epoch, [&](int src) { return c.combine_flag(src); }, kSiteCombineWait,
+                               timeout_ns, nullptr, ps_)) {
         return;
     }
     const uint8_t* base = h.base[h.rank];
@@ -656,8 +827,8 @@ __global__ void __launch_bounds__(kThreads) gather_rows_kernel(EpConfig c, p2p::
     }
 }
 
-__global__ void __launch_bounds__(kThreads) combine_rows_kernel(EpConfig c, p2p::HeapView h,
-                                                                const __nv_bfloat16* rows, const int32_t* src_pos,
+__global__ void __launch_bounds__(kThreads) combine_rows_kernel(EpConfig c, p2p::HeapView h, const uint8_t* rows,
+                                                                const float* weights, const int32_t* src_pos,
                                                                 const int32_t* recv_count, EpWorkspace ws) {
     PhaseScope ps_(ws.debug_time, kPhaseCombineRows);
     const int lane = threadIdx.x & 31;
@@ -669,8 +840,12 @@ __global__ void __launch_bounds__(kThreads) combine_rows_kernel(EpConfig c, p2p:
         const int src = sp / c.max_tokens;
         const int t = sp % c.max_tokens;
         uint8_t* dst = h.base[src] + c.comb_off(c.rank, t);
-        const __nv_bfloat16* r = rows + static_cast<int64_t>(i) * c.hidden;
-        for (int col = lane * 8; col < c.hidden; col += 256) ptx::st_v4(dst + 2ull * col, ptx::ld_v4(r + col));
+        const uint8_t* r = rows + static_cast<int64_t>(i) * c.comb_row_bytes;
+        for (int o = lane * 16; o < c.comb_row_bytes; o += 32 * 16) ptx::st_v4(dst + o, ptx::ld_v4(r + o));
+        if (weights && c.comb_weights && lane < c.topk) {
+            *reinterpret_cast<float*>(dst + c.comb_row_bytes + 4 * lane) =
+                weights[static_cast<int64_t>(i) * c.topk + lane];
+        }
     }
     grid_done_signal(c, h, &ws.done_ctas[1], c.combine_flag(c.rank), (static_cast<uint64_t>(epoch) << 32) | 1u);
 }
@@ -717,30 +892,65 @@ int dispatch_grid(int tokens, int tuned, int sms) {
 }
 
 void launch_dispatch(const EpConfig& c, const p2p::HeapView& h, const __nv_bfloat16* x, const int32_t* idx,
-                     const float* w, int tokens, const EpWorkspace& ws, int grid, cudaStream_t s) {
+                     const float* w, int tokens, const EpWorkspace& ws, int grid, cudaStream_t s,
+                     const void* raw_scales, int raw_scale_bytes) {
     if (tokens > c.max_tokens) throw kiwi::error("dispatch: more tokens than max_tokens");
+    if (raw_scales && (raw_scale_bytes <= 0 || raw_scale_bytes > c.scale_bytes)) {
+        throw kiwi::error("dispatch: caller scales need 1..scale_bytes bytes per token");
+    }
+    if (raw_scales && c.quant != static_cast<int>(Quant::kNone)) {
+        throw kiwi::error("dispatch: an FP8 / NVFP4 op makes its own scales from bf16 rows (use launch_dispatch_raw)");
+    }
     grid = dispatch_grid(tokens, grid, default_grid());
     const size_t smem = static_cast<size_t>(kThreads / 32) * (c.meta_bytes + c.scale_bytes);
     if (smem > 48 * 1024) throw kiwi::error("dispatch: per-token staging exceeds 48 KB per block (hidden too large)");
+    const uint8_t* rs = static_cast<const uint8_t*>(raw_scales);
     switch (static_cast<Quant>(c.quant)) {
         case Quant::kNone:
-            dispatch_kernel<0><<<grid, kThreads, smem, s>>>(c, h, x, idx, w, tokens, ws);
+            dispatch_kernel<0><<<grid, kThreads, smem, s>>>(c, h, x, idx, w, tokens, ws, rs, raw_scale_bytes);
             break;
         case Quant::kFp8:
-            dispatch_kernel<1><<<grid, kThreads, smem, s>>>(c, h, x, idx, w, tokens, ws);
+            dispatch_kernel<1><<<grid, kThreads, smem, s>>>(c, h, x, idx, w, tokens, ws, nullptr, 0);
             break;
         case Quant::kNvfp4:
-            dispatch_kernel<2><<<grid, kThreads, smem, s>>>(c, h, x, idx, w, tokens, ws);
+            dispatch_kernel<2><<<grid, kThreads, smem, s>>>(c, h, x, idx, w, tokens, ws, nullptr, 0);
             break;
     }
     KIWI_CUDA_CHECK(cudaGetLastError());
 }
 
+void launch_dispatch_raw(const EpConfig& c, const p2p::HeapView& h, const void* rows, const void* scales,
+                         int scale_row_bytes, const int32_t* idx, const float* w, int tokens, const EpWorkspace& ws,
+                         int grid, cudaStream_t s) {
+    if (tokens > c.max_tokens) throw kiwi::error("dispatch_raw: more tokens than max_tokens");
+    if (c.quant == static_cast<int>(Quant::kNone)) throw kiwi::error("dispatch_raw: needs an FP8 or NVFP4 op");
+    if (c.row_bytes % 16 != 0 || (reinterpret_cast<uintptr_t>(rows) & 15u) != 0) {
+        throw kiwi::error("dispatch_raw: rows must be 16-byte aligned with a 16-byte multiple per row");
+    }
+    if (scales && (scale_row_bytes <= 0 || scale_row_bytes > c.scale_bytes)) {
+        throw kiwi::error("dispatch_raw: caller scales need 1..scale_bytes bytes per token");
+    }
+    grid = dispatch_grid(tokens, grid, default_grid());
+    const size_t smem = static_cast<size_t>(kThreads / 32) * (c.meta_bytes + c.scale_bytes);
+    if (smem > 48 * 1024) throw kiwi::error("dispatch: per-token staging exceeds 48 KB per block (hidden too large)");
+    dispatch_kernel<kDispatchRaw><<<grid, kThreads, smem, s>>>(c, h, static_cast<const __nv_bfloat16*>(rows), idx, w,
+                                                               tokens, ws, static_cast<const uint8_t*>(scales),
+                                                               scales ? scale_row_bytes : 0);
+    KIWI_CUDA_CHECK(cudaGetLastError());
+}
+
+void launch_wait_flags(const EpConfig& c, const p2p::HeapView& h, const EpWorkspace& ws, int which,
+                       uint64_t timeout_ns, cudaStream_t s) {
+    if (which != 0 && which != 1) throw kiwi::error("wait_flags: which is 0 (dispatch) or 1 (combine)");
+    wait_flags_kernel<<<1, 32, 0, s>>>(c, h, ws, which, timeout_ns);
+    KIWI_CUDA_CHECK(cudaGetLastError());
+}
+
 void launch_recv_count(const EpConfig& c, const p2p::HeapView& h, const EpWorkspace& ws, uint64_t timeout_ns,
-                       cudaStream_t s) {
+                       cudaStream_t s, bool waited) {
     const uint64_t blocks = (c.slots() + kThreads - 1) / kThreads;
     const int grid = static_cast<int>(blocks < 4u * default_grid() ? blocks : 4u * default_grid());
-    recv_count_kernel<<<grid, kThreads, 0, s>>>(c, h, ws, timeout_ns);
+    recv_count_kernel<<<grid, kThreads, 0, s>>>(c, h, ws, timeout_ns, waited ? 1 : 0);
     KIWI_CUDA_CHECK(cudaGetLastError());
 }
 
@@ -776,23 +986,46 @@ void launch_combine_send(const EpConfig& c, const p2p::HeapView& h, const __nv_b
 
 void launch_combine_recv_fused(const EpConfig& c, const p2p::HeapView& h, const int32_t* idx, int tokens,
                                __nv_bfloat16* out, const EpWorkspace& ws, uint64_t timeout_ns, cudaStream_t s,
-                               int grid) {
+                               int grid, bool waited) {
     if (grid <= 0) grid = 8 * default_grid();
+    const int wt = waited ? 1 : 0;
     if (c.topk <= 8) {
-        combine_recv_fused_kernel<8><<<grid, kThreads, 0, s>>>(c, h, idx, tokens, out, ws, timeout_ns);
+        combine_recv_fused_kernel<8><<<grid, kThreads, 0, s>>>(c, h, idx, tokens, out, ws, timeout_ns, wt);
     } else {
-        combine_recv_fused_kernel<kMaxTopk><<<grid, kThreads, 0, s>>>(c, h, idx, tokens, out, ws, timeout_ns);
+        combine_recv_fused_kernel<kMaxTopk><<<grid, kThreads, 0, s>>>(c, h, idx, tokens, out, ws, timeout_ns, wt);
     }
     KIWI_CUDA_CHECK(cudaGetLastError());
 }
 
-void launch_combine_recv(const EpConfig& c, const p2p::HeapView& h, const int32_t* idx, int tokens,
-                         __nv_bfloat16* out, const EpWorkspace& ws, uint64_t timeout_ns, cudaStream_t s, int grid) {
-    if (grid <= 0) grid = 8 * default_grid();
-    if (c.world <= 8 && c.topk <= 8) {
-        combine_recv_kernel<8><<<grid, kThreads, 0, s>>>(c, h, idx, tokens, out, ws, timeout_ns);
+namespace {
+
+template <int DT>
+void launch_combine_recv_dt(const EpConfig& c, const p2p::HeapView& h, const int32_t* idx, int tokens, uint8_t* out,
+                            float* out_w, const EpWorkspace& ws, uint64_t timeout_ns, cudaStream_t s, int grid,
+                            int waited) {
+    // A token's rows come from at most min(world, topk) ranks.
+    if (c.world <= 8 || c.topk <= 8) {
+        combine_recv_kernel<DT, 8><<<grid, kThreads, 0, s>>>(c, h, idx, tokens, out, out_w, ws, timeout_ns, waited);
     } else {
-        combine_recv_kernel<kMaxTopk><<<grid, kThreads, 0, s>>>(c, h, idx, tokens, out, ws, timeout_ns);
+        combine_recv_kernel<DT, kMaxTopk>
+            <<<grid, kThreads, 0, s>>>(c, h, idx, tokens, out, out_w, ws, timeout_ns, waited);
+    }
+}
+
+}  // namespace
+
+void launch_combine_recv(const EpConfig& c, const p2p::HeapView& h, const int32_t* idx, int tokens, void* out,
+                         const EpWorkspace& ws, uint64_t timeout_ns, cudaStream_t s, int grid, float* out_w,
+                         bool waited) {
+    if (grid <= 0) grid = 8 * default_grid();
+    if (out_w && !c.comb_weights) throw kiwi::error("combine_recv: the op's combine slots carry no weights");
+    uint8_t* o = static_cast<uint8_t*>(out);
+    const int wt = waited ? 1 : 0;
+    switch (static_cast<CombDtype>(c.comb_dtype)) {
+        case CombDtype::kBf16: launch_combine_recv_dt<0>(c, h, idx, tokens, o, out_w, ws, timeout_ns, s, grid, wt); break;
+        case CombDtype::kF32: launch_combine_recv_dt<1>(c, h, idx, tokens, o, out_w, ws, timeout_ns, s, grid, wt); break;
+        case CombDtype::kFp8: launch_combine_recv_dt<2>(c, h, idx, tokens, o, out_w, ws, timeout_ns, s, grid, wt); break;
+        case CombDtype::kFp4: launch_combine_recv_dt<3>(c, h, idx, tokens, o, out_w, ws, timeout_ns, s, grid, wt); break;
     }
     KIWI_CUDA_CHECK(cudaGetLastError());
 }
@@ -811,9 +1044,12 @@ void launch_gather_rows(const EpConfig& c, const p2p::HeapView& h, const EpWorks
     KIWI_CUDA_CHECK(cudaGetLastError());
 }
 
-void launch_combine_rows(const EpConfig& c, const p2p::HeapView& h, const __nv_bfloat16* rows,
+void launch_combine_rows(const EpConfig& c, const p2p::HeapView& h, const void* rows, const float* weights,
                          const int32_t* src_pos, const int32_t* recv_count, const EpWorkspace& ws, cudaStream_t s) {
-    combine_rows_kernel<<<2 * default_grid(), kThreads, 0, s>>>(c, h, rows, src_pos, recv_count, ws);
+    if ((reinterpret_cast<uintptr_t>(rows) & 15u) != 0) throw kiwi::error("combine_rows: rows must be 16-byte aligned");
+    if (weights && !c.comb_weights) throw kiwi::error("combine_rows: the op's combine slots carry no weights");
+    combine_rows_kernel<<<2 * default_grid(), kThreads, 0, s>>>(c, h, static_cast<const uint8_t*>(rows), weights,
+                                                               src_pos, recv_count, ws);
     KIWI_CUDA_CHECK(cudaGetLastError());
 }
 

@@ -43,6 +43,8 @@ enum DebugPhase : int {
     kPhaseRecvCompact,
     kPhaseGatherRows,
     kPhaseCombineRows,
+    kPhaseDispatchWait,  // wait_flags_kernel ahead of recv_count
+    kPhaseCombineWait,   // wait_flags_kernel ahead of the combine reduce
     kNumDebugPhases
 };
 

@@ -47,12 +47,33 @@ void launch_route(const float* logits, int tokens, int experts, int topk, int32_
 
 /// Quantises (per cfg.quant) and stores each token's row, scales and metadata
 /// into every destination rank's receive slot; the last CTA signals all ranks.
+/// On a bf16 op (Quant::kNone), `raw_scales` [tokens, raw_scale_bytes] are the
+/// caller's own per-token scales, carried as bytes next to each row.
 void launch_dispatch(const EpConfig& c, const p2p::HeapView& h, const __nv_bfloat16* x, const int32_t* idx,
-                     const float* w, int tokens, const EpWorkspace& ws, int grid, cudaStream_t s);
+                     const float* w, int tokens, const EpWorkspace& ws, int grid, cudaStream_t s,
+                     const void* raw_scales = nullptr, int raw_scale_bytes = 0);
 
-/// Waits for every source's dispatch flag and counts rows per local expert.
+/// Dispatch of rows the caller already quantised (an FP8 or NVFP4 op): each
+/// token's row_bytes of `rows` and scale_row_bytes of `scales` (may be null)
+/// travel unchanged into the receive slots (the reference's pre-quantised
+/// contract); otherwise as launch_dispatch.
+void launch_dispatch_raw(const EpConfig& c, const p2p::HeapView& h, const void* rows, const void* scales,
+                         int scale_row_bytes, const int32_t* idx, const float* w, int tokens, const EpWorkspace& ws,
+                         int grid, cudaStream_t s);
+
+/// One 32-thread block waits (bounded) for every rank's dispatch (which = 0)
+/// or combine (which = 1) flag of this round; for dispatch it records each
+/// source's token count.  Launch it ahead of the kernel that reads the data
+/// and pass waited = true to that kernel: then the only kernel that spins on
+/// other GPUs is this one, which cannot keep a kernel of another stream from
+/// being scheduled.
+void launch_wait_flags(const EpConfig& c, const p2p::HeapView& h, const EpWorkspace& ws, int which,
+                       uint64_t timeout_ns, cudaStream_t s);
+
+/// Counts rows per local expert, after waiting for every source's dispatch
+/// flag itself (waited = false) or after launch_wait_flags(which = 0).
 void launch_recv_count(const EpConfig& c, const p2p::HeapView& h, const EpWorkspace& ws, uint64_t timeout_ns,
-                       cudaStream_t s);
+                       cudaStream_t s, bool waited = false);
 
 /// Assigns expert-major rows: pair_slot / pair_w / pair_dst of every row and
 /// the slot -> rows map (slot_pos).
@@ -73,17 +94,20 @@ void launch_combine_send(const EpConfig& c, const p2p::HeapView& h, const __nv_b
                          int grid, cudaStream_t s);
 
 /// Waits for every rank's combine flag and reduces the returned rows of each
-/// local token (over the ranks it was sent to) into out [T, hidden].
-void launch_combine_recv(const EpConfig& c, const p2p::HeapView& h, const int32_t* idx, int tokens,
-                         __nv_bfloat16* out, const EpWorkspace& ws, uint64_t timeout_ns, cudaStream_t s,
-                         int grid = 0);
+/// local token (over the ranks it was sent to), in fp32, into out [T,
+/// comb_row_bytes] in the op's combine dtype.  With out_w [T, topk] (an op
+/// whose comb slots carry weights), each token's returned top-k weights are
+/// summed there too.
+void launch_combine_recv(const EpConfig& c, const p2p::HeapView& h, const int32_t* idx, int tokens, void* out,
+                         const EpWorkspace& ws, uint64_t timeout_ns, cudaStream_t s, int grid = 0,
+                         float* out_w = nullptr, bool waited = false);
 
 /// Fused combine, receive side: after every rank's combine flag (set by the
 /// last CTA of each rank's scatter GEMM2), sums each local token's top-k rows
 /// of combk (already routing-weighted) into out [T, hidden].
 void launch_combine_recv_fused(const EpConfig& c, const p2p::HeapView& h, const int32_t* idx, int tokens,
                                __nv_bfloat16* out, const EpWorkspace& ws, uint64_t timeout_ns, cudaStream_t s,
-                               int grid = 0);
+                               int grid = 0, bool waited = false);
 
 // ---- transport-only (MORI-compatible) path ----
 
@@ -99,9 +123,11 @@ void launch_gather_rows(const EpConfig& c, const p2p::HeapView& h, const EpWorks
                         const int32_t* slot_compact, uint8_t* out_rows, uint8_t* out_scales, int32_t* out_idx,
                         float* out_w, int32_t* out_src_pos, cudaStream_t s);
 
-/// Sends row i of `rows` (bf16 [recv_count, hidden]) to its token's rank
-/// (src_pos[i]); the last CTA signals every rank's combine flag.
-void launch_combine_rows(const EpConfig& c, const p2p::HeapView& h, const __nv_bfloat16* rows,
+/// Sends row i of `rows` ([recv_count, comb_row_bytes] in the combine dtype,
+/// 16-byte aligned) and, when given, its top-k `weights` (fp32 [recv_count,
+/// topk]) to its token's rank (src_pos[i]); the last CTA signals every rank's
+/// combine flag.
+void launch_combine_rows(const EpConfig& c, const p2p::HeapView& h, const void* rows, const float* weights,
                          const int32_t* src_pos, const int32_t* recv_count, const EpWorkspace& ws, cudaStream_t s);
 
 }  // namespace kiwi::ep

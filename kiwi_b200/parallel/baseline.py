@@ -1,7 +1,7 @@
 """On-box baseline of the EP MoE layer: NCCL all-to-all + cuBLAS/CUTLASS grouped
 GEMM through stock PyTorch (the path the fused kernels must beat).
 
-Same routing, same 1x128 FP8 dispatch format (quantised with torch ops), same
+Same routing, same dispatch format (1x128 FP8 or NVFP4, quantised with torch ops), same
 bf16 expert FFN (``torch._grouped_mm``) and the same weights as
 :class:`kiwi_b200.parallel.ep.ExpertParallelMoE`; the all-to-alls are
 ``torch.distributed.all_to_all_single`` over NCCL.  Not product code: it
@@ -45,10 +45,15 @@ def _grouped_mm(a, w, offs):
 
 class NcclMoEBaseline:
     """The same MoE layer built from library calls, for the on-box baseline:
-    torch top-k routing and FP8 quantisation, NCCL all-to-all
-    (``all_to_all_single``) of rows, scales, ids and weights, ``torch._grouped_mm``
-    for both expert GEMMs, all-to-all back and a per-token sum.  Not product
-    code: ``bench.py --impl nccl`` times it."""
+    torch top-k routing and block quantisation (1x128 FP8, or NVFP4 for an
+    ``nvfp4`` config), NCCL all-to-all (``all_to_all_single``) of one packed
+    record per (token, destination rank) -- row, scales, top-k ids and weights
+    in one buffer, so one all-to-all per direction after the row-count
+    exchange -- ``torch._grouped_mm`` for both expert GEMMs, one all-to-all of
+    the per-(token, rank) partial sums back and a per-token sum.  The row
+    counts must reach the host to size the uneven all-to-all (one
+    synchronisation per step, as in every all_to_all_single EP layer).  Not
+    product code: ``bench.py`` times it next to the fused layer."""
     def __init__(self, cfg, group=None):
         self.cfg = cfg
         self.group = group
@@ -71,21 +76,32 @@ class NcclMoEBaseline:
         else:
             dist.all_to_all_single(out, inp, out_splits, in_splits, group=self.group)
 
+    def _quant(self, x):
+        """(wire rows uint8 [T, B], scale bytes uint8 [T, S]) of bf16 rows."""
+        if self.cfg.quant == "nvfp4":
+            return moe_model.quant_nvfp4_codes(x)
+        q, s = _quant_fp8(x)
+        return q.view(torch.uint8), s.contiguous().view(torch.uint8).view(x.shape[0], -1)
+
+    def _dequant(self, rows, scales):
+        if self.cfg.quant == "nvfp4":
+            return moe_model.dequant_nvfp4(rows, scales).to(torch.bfloat16)
+        return _dequant_fp8(rows.view(torch.float8_e4m3fn), scales.contiguous().view(torch.float32))
+
     def forward(self, x, logits):
         cfg = self.cfg
-        t = x.shape[0]
-        v, idx = torch.topk(logits, cfg.topk, dim=-1)
+        t, k = x.shape[0], cfg.topk
+        v, idx = torch.topk(logits, k, dim=-1)
         w = torch.softmax(v, dim=-1)
         dest = idx // self.epr
         mask = torch.zeros(t, self.world, dtype=torch.bool, device=x.device)
         mask.scatter_(1, dest, True)
-        r_of, t_of = mask.t().nonzero(as_tuple=True)          # (rank, token) pairs sorted by rank
+        _, t_of = mask.t().nonzero(as_tuple=True)              # (rank, token) pairs sorted by rank
         send_counts = mask.sum(0)
-        q, s = _quant_fp8(x)
-        send_q = q.view(torch.uint8)[t_of]
-        send_s = s[t_of]
-        send_i = idx[t_of].to(torch.int32)
-        send_w = w[t_of]
+        q, s = self._quant(x)
+        rb, sb = q.shape[1], s.shape[1]
+        rec = torch.cat([q, s, idx.to(torch.int32).view(torch.uint8).view(t, 4 * k),
+                         w.view(torch.uint8).view(t, 4 * k)], dim=1)[t_of]
         if self.world > 1:
             recv_counts = torch.empty_like(send_counts)
             dist.all_to_all_single(recv_counts, send_counts, group=self.group)
@@ -94,15 +110,11 @@ class NcclMoEBaseline:
         in_splits = send_counts.tolist()
         out_splits = recv_counts.tolist()
         n = sum(out_splits)
-        rq = torch.empty(n, cfg.hidden, dtype=torch.uint8, device=x.device)
-        rs = torch.empty(n, s.shape[1], dtype=torch.float32, device=x.device)
-        ri = torch.empty(n, cfg.topk, dtype=torch.int32, device=x.device)
-        rw = torch.empty(n, cfg.topk, dtype=torch.float32, device=x.device)
-        self._a2a(rq, send_q, out_splits, in_splits)
-        self._a2a(rs, send_s, out_splits, in_splits)
-        self._a2a(ri, send_i, out_splits, in_splits)
-        self._a2a(rw, send_w, out_splits, in_splits)
-        rows = _dequant_fp8(rq.view(torch.float8_e4m3fn), rs)
+        got = torch.empty(n, rec.shape[1], dtype=torch.uint8, device=x.device)
+        self._a2a(got, rec, out_splits, in_splits)
+        rows = self._dequant(got[:, :rb], got[:, rb:rb + sb])
+        ri = got[:, rb + sb:rb + sb + 4 * k].contiguous().view(torch.int32)
+        rw = got[:, rb + sb + 4 * k:].contiguous().view(torch.float32)
         local = ri - self.rank * self.epr
         ok = (local >= 0) & (local < self.epr)
         row_id, slot = ok.nonzero(as_tuple=True)
@@ -118,7 +130,7 @@ class NcclMoEBaseline:
         back = torch.zeros(n, cfg.hidden, dtype=torch.float32, device=x.device)
         back.index_add_(0, row_id, y)
         back = back.to(torch.bfloat16)
-        ret = torch.empty(int(send_counts.sum().item()), cfg.hidden, dtype=torch.bfloat16, device=x.device)
+        ret = torch.empty(t_of.shape[0], cfg.hidden, dtype=torch.bfloat16, device=x.device)
         self._a2a(ret, back, in_splits, out_splits)
         out = torch.zeros(t, cfg.hidden, dtype=torch.float32, device=x.device)
         out.index_add_(0, t_of, ret.float())

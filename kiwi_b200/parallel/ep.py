@@ -134,12 +134,52 @@ def layer_config(cfg, rank, world, max_tokens=None):
     return _C.ep.finalize_config(d)
 
 
-class ExpertParallelMoE(_DebugTimingMixin):
-    """One rank's expert-parallel MoE layer (collective constructor)."""
+class _Slot:
+    """One round's worth of layer state: a native layer (its own symmetric
+    heap, workspace and expert buffers; the weights are shared), its routing
+    and output buffers and, with several rounds in flight, its own stream."""
 
-    def __init__(self, cfg, group=None, max_tokens=None, weights=None, timeout_s=5.0, heap=None):
+    __slots__ = ("heap", "native", "idx", "w", "out", "stream", "pending")
+
+    def __init__(self, heap, native, idx, w, out, stream):
+        self.heap, self.native, self.idx, self.w, self.out, self.stream = heap, native, idx, w, out, stream
+        self.pending = None
+
+
+class Pending:
+    """A round submitted with :meth:`ExpertParallelMoE.submit`: ``out`` is
+    valid on a stream once that stream waited for ``event``
+    (:meth:`ExpertParallelMoE.wait` does it for the current stream)."""
+
+    __slots__ = ("event", "out")
+
+    def __init__(self, event, out):
+        self.event, self.out = event, out
+
+
+class ExpertParallelMoE(_DebugTimingMixin):
+    """One rank's expert-parallel MoE layer (collective constructor).
+
+    ``in_flight`` > 1 gives the layer that many independent round states
+    (each with its own symmetric heap, workspace and stream).  Rounds handed to
+    :meth:`submit` then run on those streams in turn, so the dispatch, receive
+    and combine of one round overlap the expert GEMMs of another, as a serving
+    engine keeps two batches in flight; :meth:`wait` orders a round's output
+    before later work on the current stream.  ``forward`` stays synchronous
+    with the current stream whatever ``in_flight`` is.  Every kernel that
+    waits on other GPUs is a 32-thread kernel of its own, so two rounds'
+    kernels can share the GPU without one spinning round holding the SMs the
+    other needs.  A round reuses its slot only after the slot's previous round
+    has finished on every rank (its combine waited for all ranks), so the
+    slots' buffers are never overwritten while a peer still reads them."""
+
+    def __init__(self, cfg, group=None, max_tokens=None, weights=None, timeout_s=5.0, heap=None, in_flight=1):
         if cfg.quant not in QUANTS:
             raise ValueError(f"quant must be one of {QUANTS}")
+        if int(in_flight) < 1:
+            raise ValueError("in_flight must be >= 1")
+        if heap is not None and int(in_flight) > 1:
+            raise ValueError("a caller-provided heap serves one round in flight")
         self.cfg = cfg
         self.group = group
         self.rank = kdist.rank(group)
@@ -148,17 +188,24 @@ class ExpertParallelMoE(_DebugTimingMixin):
             raise ValueError("num_experts must be divisible by the world size")
         self.max_tokens = max_tokens or cfg.tokens_per_rank
         self.layout = layer_config(cfg, self.rank, self.world, self.max_tokens)
-        self.heap = heap or SymmetricHeap(self.layout["heap_bytes"], group)
         dev = torch.device("cuda", torch.cuda.current_device())
         if weights is None:
             weights = moe_model.local_expert_weights(cfg, self.rank, self.world, dev)
         self.w13, self.w2 = weights
-        self._layer = _C.ep.MoeLayer(self.heap.native, self.layout, cfg.ffn, self.w13, self.w2,
-                                     int(timeout_s * 1e9))
+        self.in_flight = int(in_flight)
         k = cfg.topk
-        self._idx = torch.empty(self.max_tokens, k, dtype=torch.int32, device=dev)
-        self._w = torch.empty(self.max_tokens, k, dtype=torch.float32, device=dev)
-        self._out = torch.empty(self.max_tokens, cfg.hidden, dtype=torch.bfloat16, device=dev)
+        self._slots = []
+        for i in range(self.in_flight):
+            hp = heap if (heap is not None and i == 0) else SymmetricHeap(self.layout["heap_bytes"], group)
+            native = _C.ep.MoeLayer(hp.native, self.layout, cfg.ffn, self.w13, self.w2, int(timeout_s * 1e9))
+            self._slots.append(_Slot(hp, native, torch.empty(self.max_tokens, k, dtype=torch.int32, device=dev),
+                                     torch.empty(self.max_tokens, k, dtype=torch.float32, device=dev),
+                                     torch.empty(self.max_tokens, cfg.hidden, dtype=torch.bfloat16, device=dev),
+                                     torch.cuda.Stream(device=dev) if self.in_flight > 1 else None))
+        self._next = 0
+        s0 = self._slots[0]
+        self.heap, self._layer = s0.heap, s0.native
+        self._idx, self._w, self._out = s0.idx, s0.w, s0.out
 
     # -- the layer -------------------------------------------------------------
     def route(self, router_logits):
@@ -168,8 +215,11 @@ class ExpertParallelMoE(_DebugTimingMixin):
         return idx, w
 
     def forward(self, x, router_logits, out=None):
-        """x [T, hidden] bf16, router_logits [T, num_experts] fp32 -> [T, hidden] bf16.
-        The returned tensor is operator-owned unless `out` is given."""
+        """x [T, hidden] bf16, router_logits [T, num_experts] fp32 -> [T, hidden] bf16,
+        ordered on the current stream.  The returned tensor is operator-owned
+        unless `out` is given."""
+        if self.in_flight > 1:
+            return self.wait(self.submit(x, router_logits, out))
         t = x.shape[0]
         with _nvtx_range("kiwi.ep.forward"):
             idx, w = self.route(router_logits)
@@ -178,6 +228,45 @@ class ExpertParallelMoE(_DebugTimingMixin):
         return out
 
     __call__ = forward
+
+    def submit(self, x, router_logits, out=None):
+        """Enqueues one round on the next slot's stream after the work already
+        on the current stream (which produced `x` and `router_logits`) and
+        returns a :class:`Pending` without ordering anything after it on the
+        current stream.  An operator-owned `out` belongs to the slot and is
+        overwritten when the slot runs again (every ``in_flight`` rounds)."""
+        slot = self._slots[self._next % self.in_flight]
+        self._next += 1
+        t = x.shape[0]
+        cur = torch.cuda.current_stream()
+        s = slot.stream if slot.stream is not None else cur
+        if s is not cur:
+            s.wait_stream(cur)
+        x = x.contiguous()
+        logits = router_logits.contiguous()
+        out = slot.out[:t] if out is None else out
+        with torch.cuda.stream(s), _nvtx_range("kiwi.ep.submit"):
+            idx, w = slot.idx[:t], slot.w[:t]
+            slot.native.route(logits, idx, w)
+            slot.native.forward(x, idx, w, out)
+            ev = torch.cuda.Event()
+            ev.record(s)
+        if s is not cur:
+            for tensor in (x, logits, out):  # keep the caller's memory alive until the slot's stream is done
+                tensor.record_stream(s)
+        slot.pending = Pending(ev, out)
+        return slot.pending
+
+    def wait(self, pending):
+        """Makes the current stream wait for a submitted round; returns its output."""
+        torch.cuda.current_stream().wait_event(pending.event)
+        return pending.out
+
+    def wait_all(self):
+        """Makes the current stream wait for every slot's last submitted round."""
+        for slot in self._slots:
+            if slot.pending is not None:
+                self.wait(slot.pending)
 
     def forward_routed(self, x, idx, w, out=None):
         """Same layer with precomputed routing (idx int32 [T, k], w fp32 [T, k])."""
@@ -200,10 +289,20 @@ class ExpertParallelMoE(_DebugTimingMixin):
 
     # -- diagnostics --------------------------------------------------------------
     def check(self):
-        """Raises if a device-side wait timed out or a capacity check failed."""
-        code, site, info, rank, gemm = self._layer.error()
-        if code or gemm:
-            raise RuntimeError(f"kiwi ep error: code={code} site={site} info={info} rank={rank} gemm={gemm}")
+        """Raises if a device-side wait timed out or a capacity check failed (any slot)."""
+        for i, slot in enumerate(self._slots):
+            code, site, info, rank, gemm = slot.native.error()
+            if code or gemm:
+                raise RuntimeError(f"kiwi ep error: slot={i} code={code} site={site} info={info} rank={rank} "
+                                   f"gemm={gemm}")
+
+    def set_flags(self, fused_combine=None, gather_a=None):
+        """Sets the fused_combine / gather_a switches of every slot's native layer."""
+        for slot in self._slots:
+            if fused_combine is not None:
+                slot.native.fused_combine = bool(fused_combine)
+            if gather_a is not None:
+                slot.native.gather_a = bool(gather_a)
 
     @property
     def expert_counts(self):
@@ -272,6 +371,10 @@ def _to_send_flat_idx(pos, max_tokens, world):
     return (pos // max_tokens) * (world * max_tokens) + pos % max_tokens
 
 
+_FP4 = torch.float4_e2m1fn_x2
+_COMBINE_DTYPES = {torch.bfloat16: "bf16", torch.float32: "f32", torch.float8_e4m3fn: "fp8", _FP4: "fp4"}
+
+
 class KiwiEpOp(_DebugTimingMixin):
     """Expert-parallel dispatch/combine with the reference's operator contract
     (``KiwiEpOp`` of apps/ep/python/kiwi_ep_bindings.hip.cpp:123-574 of
@@ -281,44 +384,73 @@ class KiwiEpOp(_DebugTimingMixin):
       out_scales, out_indices, recv_count)``: the rows this rank received, one
       per (source rank, token) that routes at least one expert here, in
       (source rank, token) order, as operator-owned views.  ``out`` holds the
-      wire format (``dispatch_dtype`` bf16, or FP8 e4m3 bytes with fp32 1x128
-      scales in ``out_scales``, or packed NVFP4 with e4m3 block scales after a
-      4-byte fp32 row scale).  The quantisation happens inside dispatch, so
-      ``scales`` is accepted and ignored.
-    * ``combine(input, weights, indices, out=None)`` -> ``(out, None)``: row i
-      of ``input`` goes back to the rank and token it came from; each token's
-      rows are summed (no routing weights applied, as MORI).
+      wire format: bf16; FP8 e4m3 codes; or packed NVFP4 (uint8, two e2m1 codes
+      per byte).  The input is either bf16 rows, which an FP8 / FP4 op
+      quantises inside the dispatch kernel (1x128 fp32 scales, or an fp32 row
+      scale then e4m3 block scales per 16 elements, returned in
+      ``out_scales``), or rows the caller already quantised (FP8 codes
+      [T, hidden], packed FP4 [T, hidden / 2]) with the caller's own per-token
+      ``scales``, which travel unchanged (the reference's pre-quantised
+      contract; ``dispatch_scale_dim`` x ``dispatch_scale_type_size`` bytes per
+      token, returned as ``dispatch_scale_dtype``).  A bf16 op also carries the
+      caller's scales when they are given.
+    * ``combine(input, weights, indices, out=None)`` -> ``(out, out_weights)``:
+      row i of ``input`` goes back to the rank and token it came from; each
+      token's rows are summed in fp32 (no routing weights applied, as MORI) and
+      written in ``combine_dtype``: bfloat16, float32, float8_e4m3fn (e4m3
+      codes, saturating) or packed FP4 (float4_e2m1fn_x2 or uint8 with
+      ``combine_quant_format="fp4"``, [rows, hidden / 2]).  When ``weights``
+      (fp32 [rows, topk], e.g. dispatch's out_weights) is given, each row's
+      weights travel back with it and ``out_weights`` [T, topk] holds each
+      token's sum of them, as the reference returns; otherwise it is None.
     """
 
-    _DTYPES = {torch.bfloat16: "none", torch.float8_e4m3fn: "fp8", "fp8": "fp8", "nvfp4": "nvfp4", "none": "none"}
-
     _QUANT_FORMATS = {"none": None, "fp8": "fp8", "fp4": "nvfp4"}
+    _RCOMP = ("auto", "hybrid", "nvlink")
 
     def __init__(self, device_id=None, world_size=None, hidden_dim=None, topk=None, num_experts_per_rank=None,
                  max_num_inp_token_per_rank=None, dispatch_dtype=torch.bfloat16, combine_dtype=torch.bfloat16,
-                 *_launch_args, group=None, timeout_s=5.0, dispatch_quant_format="none", combine_quant_format="none",
-                 **_ignored):
-        """Arguments in the reference's order and names (device_id, world_size,
-        hidden_dim, topk, num_experts_per_rank, max_num_inp_token_per_rank,
-        dispatch_dtype, combine_dtype, ...); its launch arguments (num_blocks,
-        num_proxy_threads, scale sizes, queue_capacity, rcomp_backend, ...) are
-        accepted and ignored.  ``device_id`` selects the CUDA device and
-        ``world_size`` must equal the size of ``group``.  The wire format is
-        ``dispatch_quant_format`` ("fp8" / "fp4") when given, else follows
-        ``dispatch_dtype``; dispatch always takes bf16 rows and quantises them."""
+                 num_blocks=None, num_proxy_threads=4, dispatch_elem_size=-1, dispatch_scale_dim=0,
+                 dispatch_scale_type_size=0, combine_scale_dim=0, combine_scale_type_size=0,
+                 dispatch_scale_dtype=None, device_name="", dispatch_quant_format="none",
+                 combine_quant_format="none", queue_capacity=2048, rcomp_backend="auto", *, group=None,
+                 timeout_s=5.0):
+        """Arguments in the reference's order and names.  ``device_id`` selects
+        the CUDA device and ``world_size`` must equal the size of ``group``.
+        ``num_blocks`` (positive) sets the dispatch grid, else the B200 tuning
+        table does.  ``num_proxy_threads``, ``queue_capacity`` and
+        ``device_name`` configure the reference's RDMA proxies and NIC, which
+        the NVLink transport does not have: any value is accepted and changes
+        nothing.  ``rcomp_backend`` "auto", "hybrid" or "nvlink" (every peer is
+        reached over NVLink); "rdma-only" cannot be honoured and raises.
+        Combine scales (``combine_scale_dim`` > 0) are not carried and raise.
+        Arguments that are not the reference's raise TypeError."""
         missing = [n for n, v in (("hidden_dim", hidden_dim), ("topk", topk),
                                   ("num_experts_per_rank", num_experts_per_rank),
                                   ("max_num_inp_token_per_rank", max_num_inp_token_per_rank)) if v is None]
         if missing:
             raise TypeError("KiwiEpOp missing required arguments: " + ", ".join(missing))
-        if combine_dtype != torch.bfloat16 or str(combine_quant_format).lower() != "none":
-            raise ValueError("combine_dtype must be torch.bfloat16 (combine_quant_format 'none')")
+        rb = str(rcomp_backend).lower()
+        if rb not in self._RCOMP:
+            raise ValueError(f"rcomp_backend {rcomp_backend!r}: every peer is reached over NVLink "
+                             f"(one of {self._RCOMP}); there is no RDMA path")
+        if int(combine_scale_dim) or int(combine_scale_type_size):
+            raise ValueError("combine scales are not carried (combine_scale_dim / combine_scale_type_size must be 0)")
         fmt = str(dispatch_quant_format).lower()
         if fmt not in self._QUANT_FORMATS:
             raise ValueError(f"unsupported dispatch_quant_format {dispatch_quant_format!r} (none, fp8 or fp4)")
-        quant = self._QUANT_FORMATS[fmt] or self._DTYPES.get(dispatch_dtype)
+        quant = self._QUANT_FORMATS[fmt]
         if quant is None:
-            raise ValueError(f"unsupported dispatch_dtype {dispatch_dtype}")
+            quant = {torch.bfloat16: "none", torch.float8_e4m3fn: "fp8", torch.uint8: None}.get(dispatch_dtype)
+            if quant is None:
+                raise ValueError(f"unsupported dispatch_dtype {dispatch_dtype} for dispatch_quant_format 'none' "
+                                 "(bfloat16 or float8_e4m3fn)")
+        elem = 2 if quant == "none" else 1
+        if int(dispatch_elem_size) > 0 and int(dispatch_elem_size) != elem:
+            raise ValueError(f"dispatch_elem_size {dispatch_elem_size} differs from the wire format's {elem}")
+        comb = self._combine_kind(combine_dtype, combine_quant_format)
+        if comb == "fp4" and hidden_dim % 2:
+            raise ValueError("FP4 combine needs an even hidden_dim")
         if device_id is not None:
             torch.cuda.set_device(int(device_id))
         self.group = group
@@ -329,26 +461,82 @@ class KiwiEpOp(_DebugTimingMixin):
         self.hidden_dim = hidden_dim
         self.topk = topk
         self.max_tokens = max_num_inp_token_per_rank
+        self.num_blocks = int(num_blocks) if num_blocks else 0
+        self.num_proxy_threads = num_proxy_threads
+        self.queue_capacity = queue_capacity
+        self.device_name = device_name
+        self._scale_bytes = int(dispatch_scale_dim) * int(dispatch_scale_type_size)
+        self._scale_dim = int(dispatch_scale_dim)
+        self._scale_dtype = torch.float32 if dispatch_scale_dtype is None else dispatch_scale_dtype
+        self._combine_dtype = combine_dtype
+        self._comb = comb
         self.layout = _C.ep.finalize_config(dict(
             world=self.world_size, rank=self.rank, hidden=hidden_dim, num_experts=num_experts_per_rank * self.world_size,
-            topk=topk, max_tokens=max_num_inp_token_per_rank, quant=quant))
+            topk=topk, max_tokens=max_num_inp_token_per_rank, quant=quant, comb_dtype=comb, comb_weights=True,
+            min_scale_bytes=self._scale_bytes))
         self.heap = SymmetricHeap(self.layout["heap_bytes"], group)
         self._op = _C.ep.Transport(self.heap.native, self.layout, int(timeout_s * 1e9))
         self._quant = quant
         self._last_tokens = 0
         self._out = None
+        self._out_w = None
+        self._caller_scales = False
+
+    @staticmethod
+    def _combine_kind(dtype, fmt):
+        fmt = str(fmt).lower()
+        if fmt not in ("none", "fp8", "fp4"):
+            raise ValueError(f"unsupported combine_quant_format {fmt!r} (none, fp8 or fp4)")
+        if fmt == "fp4" and dtype in (torch.uint8, _FP4):
+            return "fp4"
+        if fmt == "fp8" and dtype in (torch.uint8, torch.float8_e4m3fn):
+            return "fp8"
+        if fmt == "none" and dtype in _COMBINE_DTYPES:
+            return _COMBINE_DTYPES[dtype]
+        raise ValueError(f"combine_dtype {dtype} with combine_quant_format {fmt!r}: supported are bfloat16 / "
+                         "float32 / float8_e4m3fn / float4_e2m1fn_x2 ('none'), float8_e4m3fn or uint8 ('fp8'), "
+                         "float4_e2m1fn_x2 or uint8 ('fp4')")
+
+    def _combine_cols(self):
+        return self.hidden_dim // 2 if self._comb == "fp4" else self.hidden_dim
 
     def dispatch(self, input, weights, scales=None, indices=None, **_launch_kwargs):
-        rows, w, sc, idx, count = self._op.dispatch(input.contiguous(), indices.to(torch.int32).contiguous(),
-                                                    weights.float().contiguous())
+        x = input.contiguous()
+        pre = x.dtype != torch.bfloat16
+        if pre:
+            if self._quant == "none":
+                raise ValueError("a bf16 op takes bf16 rows; pre-quantised rows need dispatch_quant_format fp8 / fp4")
+            x = x.view(torch.uint8)
+        sc = None
+        if scales is not None and scales.numel():
+            if not pre and self._quant != "none":
+                raise ValueError("bf16 rows are quantised inside dispatch, which makes their scales; pass "
+                                 "pre-quantised rows to carry your own scales")
+            sc = scales.contiguous()
+            per_token = sc.numel() // max(1, sc.shape[0]) * sc.element_size()
+            if self._scale_bytes and per_token != self._scale_bytes:
+                raise ValueError(f"scales carry {per_token} bytes per token; the op was built for "
+                                 f"dispatch_scale_dim x dispatch_scale_type_size = {self._scale_bytes}")
+        grid = _launch_kwargs.get("num_blocks", self.num_blocks) or 0
+        rows, w, sc_out, idx, count = self._op.dispatch(x, indices.to(torch.int32).contiguous(),
+                                                        weights.float().contiguous(), sc, int(grid))
         self._last_tokens = input.shape[0]
         self._count = count
+        self._caller_scales = sc is not None
         if self._quant == "none":
             rows = rows.view(torch.bfloat16)
         elif self._quant == "fp8":
             rows = rows.view(torch.float8_e4m3fn)
-            sc = sc.view(torch.float32)
-        return rows, w, (None if self._quant == "none" else sc), idx, count
+        if self._caller_scales:
+            nbytes = sc.numel() // max(1, sc.shape[0]) * sc.element_size()
+            out_sc = sc_out[:, :nbytes].view(sc.dtype).view(sc_out.shape[0], *sc.shape[1:])
+        elif self._quant == "fp8":
+            out_sc = sc_out[:, :self.hidden_dim // 128 * 4].view(torch.float32)
+        elif self._quant == "nvfp4":
+            out_sc = sc_out
+        else:
+            out_sc = None
+        return rows, w, out_sc, idx, count
 
     dispatch_send = dispatch
 
@@ -357,17 +545,31 @@ class KiwiEpOp(_DebugTimingMixin):
 
     def combine(self, input, weights=None, indices=None, out=None, **_launch_kwargs):
         t = self._last_tokens
+        cols = self._combine_cols()
+        rows = input.contiguous()
+        if rows.dtype != self._combine_dtype and not (rows.dtype == torch.uint8 and self._comb in ("fp8", "fp4")):
+            raise ValueError(f"combine input must be {self._combine_dtype}, got {rows.dtype}")
+        if rows.dim() != 2 or rows.shape[1] != cols:
+            raise ValueError(f"combine input must be [rows, {cols}]")
         if out is None:
-            if self._out is None or self._out.shape[0] < self.max_tokens:
-                self._out = torch.empty(self.max_tokens, self.hidden_dim, dtype=torch.bfloat16, device=input.device)
+            if self._out is None:
+                self._out = torch.empty(self.max_tokens, cols, dtype=self._combine_dtype, device=rows.device)
             out = self._out[:t]
-        self._op.combine(input.contiguous(), out)
-        return out, None
+        ow = None
+        if weights is not None:
+            if self._out_w is None:
+                self._out_w = torch.empty(self.max_tokens, self.topk, dtype=torch.float32, device=rows.device)
+            ow = self._out_w[:t]
+            weights = weights.float().contiguous()
+        self._op.combine(rows.view(torch.uint8) if rows.dtype in (_FP4, torch.float8_e4m3fn) else rows,
+                         out.view(torch.uint8) if out.dtype in (_FP4, torch.float8_e4m3fn) else out, weights, ow)
+        self._last_out, self._last_out_w = out, ow
+        return out, ow
 
     combine_send = combine
 
     def combine_recv(self, **_kwargs):
-        return self._out[:self._last_tokens] if self._out is not None else None, None
+        return getattr(self, "_last_out", None), getattr(self, "_last_out_w", None)
 
     def reset(self):
         """Ends the current round on the host.  Device slots are epoch-tagged,
@@ -416,18 +618,20 @@ class KiwiEpOp(_DebugTimingMixin):
         n = int(self._count.item()) if getattr(self, "_count", None) is not None else 0
         return _to_send_flat_idx(self._op.src_token_pos[:n], self.max_tokens, self.world_size)
 
-    def get_registered_combine_input_buffer(self, combine_dtype=torch.bfloat16, hidden_dim=-1):
-        """Operator-owned [max_num_tokens_to_recv(), hidden] buffer a caller can
-        write expert outputs into and pass to combine() without a copy."""
-        if combine_dtype != torch.bfloat16:
-            raise ValueError("combine_dtype must be torch.bfloat16")
+    def get_registered_combine_input_buffer(self, combine_dtype=None, hidden_dim=-1):
+        """Operator-owned [max_num_tokens_to_recv(), hidden] buffer (hidden / 2
+        for FP4) in the combine dtype, which a caller can write expert outputs
+        into and pass to combine() without a copy."""
+        dt = self._combine_dtype if combine_dtype is None else combine_dtype
+        if dt != self._combine_dtype:
+            raise ValueError(f"combine_dtype must be the op's combine dtype {self._combine_dtype}")
         if hidden_dim > 0 and hidden_dim != self.hidden_dim:
             raise ValueError("get_registered_combine_input_buffer hidden_dim must match the configured hidden_dim")
         buf = getattr(self, "_combine_in", None)
         if buf is None:
             dev = torch.device("cuda", torch.cuda.current_device())
-            buf = self._combine_in = torch.empty(self.max_num_tokens_to_recv(), self.hidden_dim,
-                                                 dtype=torch.bfloat16, device=dev)
+            buf = self._combine_in = torch.empty(self.max_num_tokens_to_recv(), self._combine_cols(), dtype=dt,
+                                                 device=dev)
         return buf
 
     def _debug_native(self):
@@ -494,6 +698,6 @@ def recommended_num_blocks(num_tokens, world_size, gpu_arch="", nic_family=""):
     return recommended_runtime_defaults(num_tokens, world_size, gpu_arch, nic_family)["num_blocks"]
 
 
-__all__ = ["ExpertParallelMoE", "EpDispatchCombine", "KiwiEpOp", "layer_config", "debug_phases",
+__all__ = ["ExpertParallelMoE", "Pending", "EpDispatchCombine", "KiwiEpOp", "layer_config", "debug_phases",
            "format_debug_timing", "barrier", "get_rank", "get_nranks", "get_hca_name_for_gpu",
            "get_hca_name_for_current_gpu", "recommended_num_blocks", "recommended_runtime_defaults"]

@@ -25,14 +25,15 @@ Semantics, as KiwiEpOp:
   [T, S], or packed FP4 input (uint8 / float4_e2m1fn_x2 [T, hidden / 2]) with
   per-token scales of any dtype (the reference's pre-quantised contract),
   travels unchanged (FP4 scales come back as their bytes).
-* ``combine(input, weights, indices, out)`` returns ``(out, None)``: row i of
+* ``combine(input, weights, indices, out)`` returns ``(out, out_weights)``: row i of
   ``input`` goes back to the rank and token it came from, and each token's rows
   are summed in fp32 (no routing weights, as MORI); tokens routed nowhere get
   zeros.  Rows travel and the result is returned in ``combine_dtype``: bf16,
   float32, float8_e4m3fn or float4_e2m1fn_x2 (codes without scales, the sum
   re-quantised with saturation; FP4 rows are hidden / 2 bytes, element 2i in
-  the low nibble), as the reference also accepts (the NVLink op combines bf16
-  only).
+  the low nibble), as the reference also accepts.  With ``weights`` (fp32
+  [rows, topk]) the rows' weights travel back and ``out_weights`` [T, topk]
+  holds each token's sum; otherwise it is None.
 * ``get_dispatch_src_token_pos()`` encodes each received row's source as
   ``src_rank * (world * max_tokens) + token`` and ``decode_send_flat_idx``
   inverts it.
@@ -80,16 +81,30 @@ class CollectiveEpOp:
 
     def __init__(self, device_id=None, world_size=None, hidden_dim=None, topk=None, num_experts_per_rank=None,
                  max_num_inp_token_per_rank=None, dispatch_dtype=torch.bfloat16, combine_dtype=torch.bfloat16,
-                 *_launch_args, group=None, dispatch_quant_format="none", combine_quant_format="none", device=None,
-                 **_ignored):
+                 num_blocks=None, num_proxy_threads=4, dispatch_elem_size=-1, dispatch_scale_dim=0,
+                 dispatch_scale_type_size=0, combine_scale_dim=0, combine_scale_type_size=0,
+                 dispatch_scale_dtype=None, device_name="", dispatch_quant_format="none",
+                 combine_quant_format="none", queue_capacity=2048, rcomp_backend="auto", *, group=None,
+                 device=None):
+        """Arguments as KiwiEpOp (the reference's names and order).  The launch
+        and proxy arguments (num_blocks, num_proxy_threads, queue_capacity,
+        device_name, rcomp_backend) have no meaning for an all-to-all transport
+        and change nothing; combine scales are not carried and raise."""
         missing = [n for n, v in (("hidden_dim", hidden_dim), ("topk", topk),
                                   ("num_experts_per_rank", num_experts_per_rank),
                                   ("max_num_inp_token_per_rank", max_num_inp_token_per_rank)) if v is None]
         if missing:
             raise TypeError("CollectiveEpOp missing required arguments: " + ", ".join(missing))
-        if combine_dtype not in _COMBINE_DTYPES or str(combine_quant_format).lower() != "none":
+        if int(combine_scale_dim) or int(combine_scale_type_size):
+            raise ValueError("combine scales are not carried (combine_scale_dim / combine_scale_type_size must be 0)")
+        cfmt = str(combine_quant_format).lower()
+        if cfmt == "fp8" and combine_dtype in (torch.uint8, torch.float8_e4m3fn):
+            combine_dtype = torch.float8_e4m3fn
+        elif cfmt == "fp4" and combine_dtype in (torch.uint8, _FP4):
+            combine_dtype = _FP4
+        elif cfmt != "none" or combine_dtype not in _COMBINE_DTYPES:
             raise ValueError("combine_dtype must be torch.bfloat16, torch.float32, torch.float8_e4m3fn or "
-                             "torch.float4_e2m1fn_x2 (combine_quant_format 'none')")
+                             "torch.float4_e2m1fn_x2 (or uint8 with combine_quant_format 'fp8' / 'fp4')")
         self._combine_dtype = combine_dtype
         if combine_dtype == _FP4 and hidden_dim % 2:
             raise ValueError("FP4 combine needs an even hidden_dim (two elements per byte)")
@@ -221,17 +236,22 @@ class CollectiveEpOp:
         """dispatch() already completes the receive (kept for call-shape parity)."""
 
     def combine(self, input, weights=None, indices=None, out=None, **_launch_kwargs):
-        """See the module docstring; collective over the group."""
+        """See the module docstring; collective over the group.  With
+        ``weights`` (fp32 [rows, topk]) each row's weights travel back with it
+        and the second return value holds each token's sum of them."""
         if self._send_counts is None:
             raise RuntimeError("combine needs a prior dispatch")
         n = int(sum(self._recv_counts))
         rows = _to_combine_dtype(input[:n].to(self.device), self._combine_dtype)
-        back = self._a2a(self._wire(rows), self._recv_counts, self._send_counts)       # (dest, token) order
-        back = back.view(self._combine_dtype).view(back.shape[0], self._combine_cols())
+        fields = [rows]
+        if weights is not None:
+            fields.append(weights[:n].to(self.device, torch.float32).reshape(n, self.topk))
+        back = self._a2a(torch.cat([self._wire(f) for f in fields], dim=1), self._recv_counts, self._send_counts)
+        parts = self._unwire(back, fields)                                          # (dest, token) order
         t = self._last_tokens
         acc = torch.zeros(t, self.hidden_dim, dtype=torch.float32, device=self.device)
         if back.shape[0]:
-            acc.index_add_(0, self._send_tokens, _to_float(back))
+            acc.index_add_(0, self._send_tokens, _to_float(parts[0]))
         if out is None:
             out = torch.empty(t, self._combine_cols(), dtype=self._combine_dtype, device=self.device)
         res = _to_combine_dtype(acc, out.dtype)
@@ -239,8 +259,13 @@ class CollectiveEpOp:
             out[:t].view(torch.uint8).copy_(res.view(torch.uint8))
         else:
             out[:t].copy_(res)
-        self._out = out
-        return out, None
+        out_w = None
+        if weights is not None:
+            out_w = torch.zeros(t, self.topk, dtype=torch.float32, device=self.device)
+            if back.shape[0]:
+                out_w.index_add_(0, self._send_tokens, parts[1])
+        self._out, self._out_w = out, out_w
+        return out, out_w
 
     combine_send = combine
 
@@ -249,7 +274,8 @@ class CollectiveEpOp:
         return self.hidden_dim // 2 if self._combine_dtype == _FP4 else self.hidden_dim
 
     def combine_recv(self, **_kwargs):
-        return (self._out[:self._last_tokens] if self._out is not None else None), None
+        return ((self._out[:self._last_tokens] if self._out is not None else None),
+                getattr(self, "_out_w", None))
 
     def reset(self):
         """Ends the current round (nothing to clear between rounds)."""

@@ -33,6 +33,21 @@ EpConfig finalize(EpConfig c) {
         default:
             bad("unknown quant format");
     }
+    if (c.min_scale_bytes < 0) bad("min_scale_bytes must be >= 0");
+    if (c.min_scale_bytes > c.scale_bytes) c.scale_bytes = static_cast<int32_t>(round_up(c.min_scale_bytes, 16));
+    switch (static_cast<CombDtype>(c.comb_dtype)) {
+        case CombDtype::kBf16: c.comb_row_bytes = c.hidden * 2; break;
+        case CombDtype::kF32: c.comb_row_bytes = c.hidden * 4; break;
+        case CombDtype::kFp8: c.comb_row_bytes = c.hidden; break;
+        case CombDtype::kFp4:
+            if (c.hidden % 2 != 0) bad("FP4 combine needs an even hidden");
+            c.comb_row_bytes = c.hidden / 2;
+            break;
+        default:
+            bad("unknown combine dtype");
+    }
+    if (c.comb_row_bytes % 16 != 0) bad("combine rows must be a multiple of 16 bytes (hidden too small or odd)");
+    c.comb_bytes = c.comb_row_bytes + (c.comb_weights ? static_cast<int32_t>(round_up(4ull * c.topk, 16)) : 0);
     c.meta_bytes = static_cast<int32_t>(round_up(sizeof(DispatchMetaHeader) + 8ull * c.topk, 16));
     const uint64_t slots = c.slots();
     uint64_t off = 0;
@@ -45,7 +60,7 @@ EpConfig finalize(EpConfig c) {
     c.off_scale = off;
     off += round_up(slots * static_cast<uint64_t>(c.scale_bytes), 256);
     c.off_comb = off;
-    off += round_up(slots * static_cast<uint64_t>(c.hidden) * 2, 256);
+    off += round_up(slots * static_cast<uint64_t>(c.comb_bytes), 256);
     c.off_combk = off;
     off += round_up(static_cast<uint64_t>(c.max_tokens) * c.topk * static_cast<uint64_t>(c.hidden) * 2, 256);
     c.heap_bytes = off;

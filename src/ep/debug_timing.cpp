@@ -7,6 +7,7 @@ namespace {
 constexpr const char* kPhaseNames[kNumDebugPhases] = {
     "route",        "begin",     "dispatch",     "recv_count",    "recv_assign",  "recv_copy",    "gemm1",
     "gemm2",        "combine_send", "combine_recv", "recv_compact", "gather_rows", "combine_rows",
+    "dispatch_wait", "combine_wait",
 };
 constexpr const char* kMetaNames[kNumDebugMeta] = {
     "rank",          "world",          "tokens",           "recv_tokens",      "recv_remote_tokens",

@@ -27,9 +27,9 @@ def test_kernels_per_step_counts_each_path():
     sys.path.insert(0, ROOT)
     import bench
 
-    assert bench.kernels_per_step(True, False) == 11
-    assert bench.kernels_per_step(False, False) == 12
-    assert bench.kernels_per_step(True, True) == 10
+    assert bench.kernels_per_step(True, False) == 13
+    assert bench.kernels_per_step(False, False) == 14
+    assert bench.kernels_per_step(True, True) == 12
 
 
 @pytest.fixture()

@@ -196,6 +196,7 @@ def test_kiwi_ep_op_source_position_encoding_round_trips():
     enc = _to_send_flat_idx(slots, max_tokens, world)
     op = KiwiEpOp.__new__(KiwiEpOp)
     op.world_size, op.max_tokens, op.hidden_dim = world, max_tokens, 64
+    op._combine_dtype, op._comb = torch.bfloat16, "bf16"
     assert op.max_num_tokens_to_send() == 40 and op.max_num_tokens_to_recv_per_rank() == 10
     for s, e in zip(slots.tolist(), enc.tolist()):
         assert op.decode_send_flat_idx(e) == (s // max_tokens, s % max_tokens)
@@ -220,6 +221,32 @@ def test_kiwi_ep_ext_module_surface():
     with pytest.raises(TypeError):
         ext.KiwiEpOp(0, 1, 512)  # topk, experts per rank and max tokens missing
     with pytest.raises(ValueError):
-        ext.KiwiEpOp(0, 1, 512, 2, 8, 16, torch.bfloat16, torch.float32)
-    with pytest.raises(ValueError):
         ext.KiwiEpOp(0, 1, 512, 2, 8, 16, torch.bfloat16, torch.bfloat16, dispatch_quant_format="int4")
+
+
+@pytest.mark.parametrize("kwargs", [
+    dict(combine_dtype=torch.int32),                                    # no such combine dtype
+    dict(combine_dtype=torch.uint8),                                    # one-byte combine needs a quant format
+    dict(combine_scale_dim=4, combine_scale_type_size=4),               # combine scales are not carried
+    dict(rcomp_backend="rdma-only"),                                    # no RDMA path
+    dict(dispatch_quant_format="fp8", dispatch_elem_size=2),            # FP8 wire bytes are one byte each
+    dict(dispatch_dtype=torch.float16),                                 # no fp16 wire format
+])
+def test_kiwi_ep_op_rejects_what_it_cannot_honour(kwargs):
+    """Arguments the NVLink op cannot honour raise ValueError before any device
+    work (the reference raises on the same combinations or has no B200 meaning)."""
+    from kiwi_b200.parallel.ep import KiwiEpOp
+
+    base = dict(device_id=None, world_size=None, hidden_dim=512, topk=2, num_experts_per_rank=8,
+                max_num_inp_token_per_rank=16)
+    with pytest.raises(ValueError):
+        KiwiEpOp(**{**base, **kwargs})
+
+
+def test_kiwi_ep_op_rejects_unknown_arguments():
+    """Keyword arguments that are not the reference's raise TypeError instead of
+    being dropped."""
+    from kiwi_b200.parallel.ep import KiwiEpOp
+
+    with pytest.raises(TypeError):
+        KiwiEpOp(hidden_dim=512, topk=2, num_experts_per_rank=8, max_num_inp_token_per_rank=16, use_fast_path=True)

@@ -224,6 +224,140 @@ def test_kiwi_ep_op_token_sweep():
         op.reset()
 
 
+@pytest.mark.parametrize("quant", ["fp8", "nvfp4"])
+def test_rounds_in_flight_match_reference(quant):
+    """Two rounds in flight: five rounds with different inputs submitted back
+    to back on the two slots' streams, each output checked against the fp32
+    reference once waited for; forward() on the same layer stays synchronous."""
+    cfg = small_cfg(quant, tokens=160)
+    layer = ExpertParallelMoE(cfg, in_flight=2)
+    ins = [moe.synthetic_inputs(cfg, 0, "cuda", step=i, tokens=160 - 8 * i) for i in range(5)]
+    outs = [torch.empty(x.shape[0], cfg.hidden, dtype=torch.bfloat16, device="cuda") for x, _ in ins]
+    pend = [layer.submit(x, lg, out=o) for (x, lg), o in zip(ins, outs)]
+    for p in pend:
+        layer.wait(p)
+    for (x, lg), o in zip(ins, outs):
+        _check(layer, cfg, x, lg, o, rel=5e-2 if quant == "nvfp4" else 2e-2)
+    x, lg = ins[0]
+    _check(layer, cfg, x, lg, layer(x, lg).clone(), rel=5e-2 if quant == "nvfp4" else 2e-2)
+
+
+_FP4 = torch.float4_e2m1fn_x2
+
+
+@pytest.mark.parametrize("comb", ["f32", "fp8", "fp4", "bf16"])
+def test_kiwi_ep_op_combine_dtypes_and_weight_sums(comb):
+    """Combine in every dtype the reference accepts (float32, bfloat16, FP8
+    e4m3 codes, packed FP4 e2m1 codes), with the rows' top-k weights travelling
+    back and summed per token.  On one rank every token returns exactly one
+    row, so the output is that row (codes re-encoded exactly) and the weight
+    sum is the row's own weights."""
+    from kiwi_b200.models.moe import fp4_codes, fp4_pack, fp4_unpack
+    from kiwi_b200.parallel.ep import KiwiEpOp
+
+    dt, fmt = {"f32": (torch.float32, "none"), "bf16": (torch.bfloat16, "none"),
+               "fp8": (torch.float8_e4m3fn, "fp8"), "fp4": (_FP4, "fp4")}[comb]
+    op = KiwiEpOp(hidden_dim=512, topk=3, num_experts_per_rank=8, max_num_inp_token_per_rank=40,
+                  combine_dtype=dt, combine_quant_format=fmt)
+    torch.manual_seed(7)
+    x = torch.randn(37, 512, device="cuda").bfloat16()
+    idx, w = moe.route_reference(torch.randn(37, 8, device="cuda"), 3)
+    rows, ow, _, oidx, cnt = op.dispatch(x, w, None, idx)
+    torch.cuda.synchronize()
+    n = int(cnt.item())
+    assert n == 37
+    y = rows[:n].float() * 3.0                      # values past the FP8 / FP4 ranges too
+    if comb == "fp4":
+        inp = fp4_pack(fp4_codes(y)).view(_FP4)
+        expect = fp4_unpack(inp)
+    elif comb == "fp8":
+        inp = y.clamp(-448, 448).to(torch.float8_e4m3fn)
+        expect = inp.float()
+    else:
+        inp = y.to(dt)
+        expect = inp.float()
+    out, out_w = op.combine(inp, ow[:n], oidx[:n])
+    torch.cuda.synchronize()
+    op.check()
+    assert out.dtype == dt and out.shape[0] == 37
+    got = fp4_unpack(out) if comb == "fp4" else out.float()
+    assert torch.equal(got, expect)
+    assert out_w is not None and torch.equal(out_w, ow[:n])
+    out2, none_w = op.combine(inp, None, oidx[:n])
+    torch.cuda.synchronize()
+    assert none_w is None and torch.equal(fp4_unpack(out2) if comb == "fp4" else out2.float(), expect)
+
+
+def test_kiwi_ep_op_pre_quantised_fp8_dispatch():
+    """FP8 codes the caller quantised, with its own per-token scales
+    (dispatch_scale_dim x dispatch_scale_type_size bytes), travel unchanged:
+    the received codes and scales equal the sent ones (the reference's
+    pre-quantised contract)."""
+    from kiwi_b200.parallel.ep import KiwiEpOp
+
+    op = KiwiEpOp(hidden_dim=512, topk=2, num_experts_per_rank=8, max_num_inp_token_per_rank=32,
+                  dispatch_dtype=torch.float8_e4m3fn, dispatch_quant_format="fp8", dispatch_scale_dim=16,
+                  dispatch_scale_type_size=4)
+    torch.manual_seed(3)
+    codes = (torch.randn(32, 512, device="cuda") * 40).to(torch.float8_e4m3fn)
+    scales = torch.rand(32, 16, device="cuda")      # e.g. 1x32 blocks, the caller's choice
+    idx, w = moe.route_reference(torch.randn(32, 8, device="cuda"), 2)
+    rows, ow, sc, oidx, cnt = op.dispatch(codes, w, scales, idx)
+    torch.cuda.synchronize()
+    op.check()
+    n = int(cnt.item())
+    assert n == 32
+    assert rows.dtype == torch.float8_e4m3fn and torch.equal(rows[:n].view(torch.uint8), codes.view(torch.uint8))
+    assert sc.dtype == torch.float32 and tuple(sc.shape[1:]) == (16,) and torch.equal(sc[:n], scales)
+    with pytest.raises(ValueError):
+        op.dispatch(codes, w, scales[:, :8], idx)   # not the configured scale size
+
+
+def test_kiwi_ep_op_pre_quantised_fp4_dispatch_and_own_quantisation():
+    """An FP4 op takes packed e2m1 rows [T, hidden / 2] with the caller's scale
+    bytes unchanged, and bf16 rows it quantises itself (scale bytes of the
+    NVLink wire format); bf16 rows with caller scales are refused there."""
+    from kiwi_b200.parallel.ep import KiwiEpOp
+
+    op = KiwiEpOp(hidden_dim=512, topk=2, num_experts_per_rank=8, max_num_inp_token_per_rank=32,
+                  dispatch_dtype=torch.uint8, dispatch_quant_format="fp4", dispatch_scale_dim=32,
+                  dispatch_scale_type_size=1, dispatch_scale_dtype=torch.uint8)
+    torch.manual_seed(5)
+    packed = torch.randint(0, 256, (32, 256), dtype=torch.uint8, device="cuda")
+    sbytes = torch.randint(0, 256, (32, 32), dtype=torch.uint8, device="cuda")
+    idx, w = moe.route_reference(torch.randn(32, 8, device="cuda"), 2)
+    rows, _, sc, _, cnt = op.dispatch(packed.view(_FP4), w, sbytes, idx)
+    torch.cuda.synchronize()
+    op.check()
+    n = int(cnt.item())
+    assert torch.equal(rows[:n].view(torch.uint8), packed) and torch.equal(sc[:n], sbytes)
+    x = torch.randn(32, 512, device="cuda").bfloat16()
+    rows, _, sc, _, cnt = op.dispatch(x, w, None, idx)
+    torch.cuda.synchronize()
+    op.check()
+    ref_codes, ref_sc = kiwi_b200.ops.quant_nvfp4(x)
+    assert torch.equal(rows[:n].view(torch.uint8), ref_codes)
+    assert torch.equal(sc[:n, :ref_sc.shape[1]], ref_sc)
+    with pytest.raises(ValueError):
+        op.dispatch(x, w, sbytes, idx)
+
+
+def test_kiwi_ep_op_bf16_rows_carry_caller_scales():
+    """A bf16 op carries the caller's per-token scales next to the rows."""
+    from kiwi_b200.parallel.ep import KiwiEpOp
+
+    op = KiwiEpOp(hidden_dim=256, topk=2, num_experts_per_rank=4, max_num_inp_token_per_rank=16,
+                  dispatch_scale_dim=3, dispatch_scale_type_size=4)
+    x = torch.randn(16, 256, device="cuda").bfloat16()
+    scales = torch.randn(16, 3, device="cuda")
+    idx, w = moe.route_reference(torch.randn(16, 4, device="cuda"), 2)
+    rows, _, sc, _, cnt = op.dispatch(x, w, scales, idx)
+    torch.cuda.synchronize()
+    op.check()
+    n = int(cnt.item())
+    assert torch.equal(rows[:n], x) and torch.equal(sc[:n], scales)
+
+
 @pytest.mark.filterwarnings("ignore:The CUDA Graph is empty")
 @pytest.mark.parametrize("fused", [True, False])
 def test_debug_timing_spans_every_kernel_of_a_round(fused):
@@ -244,15 +378,16 @@ def test_debug_timing_spans_every_kernel_of_a_round(fused):
         snap = layer.get_debug_timing_snapshot()
     _check(layer, cfg, x, logits, out)
     ph = snap["phases"]
-    order = ["route", "begin", "dispatch", "recv_count", "recv_assign", "recv_copy", "gemm1", "gemm2"]
-    order += ["combine_recv"] if fused else ["combine_send", "combine_recv"]
+    order = ["route", "begin", "dispatch", "dispatch_wait", "recv_count", "recv_assign", "recv_copy", "gemm1",
+             "gemm2"]
+    order += ["combine_wait", "combine_recv"] if fused else ["combine_send", "combine_wait", "combine_recv"]
     assert set(order) <= set(ph), sorted(ph)
     slack = 2.0  # us: %globaltimer granularity
     for a, b in zip(order, order[1:]):
         assert ph[a]["end_us"] <= ph[b]["start_us"] + slack, (a, b, ph[a], ph[b])
     for name in order:
         assert ph[name]["us"] >= 0
-    for name in ("recv_count", "combine_recv"):
+    for name in ("dispatch_wait", "combine_wait"):  # the flag waits run in a 32-thread kernel of their own
         assert "wait_us" in ph[name]
         assert ph[name]["start_us"] - slack <= ph[name]["wait_start_us"] <= ph[name]["wait_end_us"] + slack
         assert ph[name]["wait_end_us"] <= ph[name]["end_us"] + slack

@@ -25,8 +25,8 @@ def _one_gpu_per_rank(request):
     """Every rank needs its own GPU: ranks whose kernels wait on one another
     must never share a GPU (they would run as separate launches that nothing
     schedules together).  Each test names its world size in its node id."""
-    name = request.node.name
-    world = 4 if "world4" in name or name.endswith("_4") else 2
+    name = request.node.name.split("[")[0]
+    world = 8 if "world8" in name or name.endswith("_8") else 4 if "world4" in name or name.endswith("_4") else 2
     if _ngpu() < world:
         pytest.skip(f"needs {world} GPUs, one per rank")
 
@@ -81,17 +81,22 @@ def _all_pairs(rank, world):
     del heap
 
 
-def _ep_layer(rank, world, quant, fused=True):
+def _ep_layer(rank, world, quant, fused=True, in_flight=1):
     from kiwi_b200.models import moe
     from kiwi_b200.parallel.ep import ExpertParallelMoE
 
     cfg = moe.MoEConfig(hidden=1024, ffn=256, num_experts=8 * world, topk=4, tokens_per_rank=96, quant=quant,
                         name="t")
-    layer = ExpertParallelMoE(cfg)
-    layer.native.fused_combine = fused
+    layer = ExpertParallelMoE(cfg, in_flight=in_flight)
+    layer.set_flags(fused_combine=fused)
+    ins = [moe.synthetic_inputs(cfg, rank, "cuda", step=step, tokens=96 - 16 * step) for step in range(3)]
+    if in_flight > 1:  # every round submitted before any is waited for
+        outs = [torch.empty(x.shape[0], cfg.hidden, dtype=torch.bfloat16, device="cuda") for x, _ in ins]
+        for p in [layer.submit(x, lg, out=o) for (x, lg), o in zip(ins, outs)]:
+            layer.wait(p)
     for step in range(3):
-        x, logits = moe.synthetic_inputs(cfg, rank, "cuda", step=step, tokens=96 - 16 * step)
-        out = layer(x, logits).clone()
+        x, logits = ins[step]
+        out = outs[step] if in_flight > 1 else layer(x, logits).clone()
         torch.cuda.synchronize()
         layer.check()
         idx, w = moe.route_reference(logits, cfg.topk)
@@ -181,6 +186,182 @@ def _nvls(rank, world):
     expect = torch.arange(n, device="cuda", dtype=torch.float32) * (world * (world + 1) / 2)
     assert torch.allclose(data, expect), (data[:4], expect[:4])
     assert int(status[0].item()) == 0
+
+
+def _gather_inputs(x, idx, w, tmax):
+    """Every rank's (x, idx, w) of this round, each padded to tmax rows, and the
+    token counts (all_gather over NCCL)."""
+    import torch.distributed as dist
+
+    world = dist.get_world_size()
+    t = x.shape[0]
+    pad = lambda a: torch.cat([a, a.new_zeros((tmax - t,) + tuple(a.shape[1:]))]) if t < tmax else a  # noqa: E731
+    out = []
+    for a in (x, idx, w):
+        buf = [torch.empty_like(pad(a)) for _ in range(world)]
+        dist.all_gather(buf, pad(a).contiguous())
+        out.append(buf)
+    counts = [torch.zeros(1, dtype=torch.int64, device="cuda") for _ in range(world)]
+    dist.all_gather(counts, torch.tensor([t], device="cuda"))
+    return out[0], out[1], out[2], [int(c.item()) for c in counts]
+
+
+_COMB = {"bf16": (torch.bfloat16, "none"), "f32": (torch.float32, "none"), "fp8": (torch.float8_e4m3fn, "fp8"),
+         "fp4": (torch.float4_e2m1fn_x2, "fp4")}
+
+
+def _encode(v, comb):
+    """fp32 rows -> the combine dtype (FP8 / FP4 round to nearest, saturating)."""
+    from kiwi_b200.models.moe import fp4_codes, fp4_pack
+
+    if comb == "fp4":
+        return fp4_pack(fp4_codes(v)).view(torch.float4_e2m1fn_x2)
+    if comb == "fp8":
+        return v.clamp(-448, 448).to(torch.float8_e4m3fn)
+    return v.to(_COMB[comb][0])
+
+
+def _decode(r, comb):
+    from kiwi_b200.models.moe import fp4_unpack
+
+    return fp4_unpack(r) if comb == "fp4" else r.float()
+
+
+def _transport_matrix(rank, world, quant, comb):
+    """KiwiEpOp at `world` ranks (the reference's drop-in matrix,
+    apps/ep/python/CMakeLists.txt:118-317 of AMDResearch/kiwi): rounds of T,
+    17 (rank 1 sends nothing), 1 and T tokens.  Each rank checks the rows it
+    received (order, sources, ids, weights and the wire bytes against the
+    same quantisation of the senders' rows), returns each row times
+    (rank + 1) in the combine dtype with its weights, and checks every token's
+    sum over the ranks it went to, in that dtype, and its weight sum."""
+    from kiwi_b200 import ops
+    from kiwi_b200.models import moe
+    from kiwi_b200.parallel.ep import KiwiEpOp
+
+    H, K, EPR, T = 512, 4, 4, 64
+    comb_dt, comb_fmt = _COMB[comb]
+    fmt = {"none": "none", "fp8": "fp8", "nvfp4": "fp4"}[quant]
+    op = KiwiEpOp(hidden_dim=H, topk=K, num_experts_per_rank=EPR, max_num_inp_token_per_rank=T,
+                  dispatch_quant_format=fmt, combine_dtype=comb_dt, combine_quant_format=comb_fmt)
+    for step, t in enumerate((T, 0 if rank == 1 else 17, 1, T)):
+        g = torch.Generator(device="cuda").manual_seed(1000 * step + rank)
+        x = torch.randn(t, H, device="cuda", generator=g).bfloat16()
+        idx, w = moe.route_reference(torch.randn(t, EPR * world, device="cuda", generator=g), K)
+        xs, idxs, ws, ts = _gather_inputs(x, idx, w, T)
+        rows, ow, sc, oidx, cnt = op.dispatch(x, w, None, idx)
+        torch.cuda.synchronize()
+        op.check()
+        n = int(cnt.item())
+        expect = [(s, tok) for s in range(world) for tok in range(ts[s])
+                  if bool(((idxs[s][tok] // EPR) == rank).any())]
+        assert n == len(expect), (rank, step, n, len(expect))
+        pos = op.get_dispatch_src_token_pos()[:n].tolist()
+        assert [op.decode_send_flat_idx(p) for p in pos] == expect, (rank, step)
+        src_rows = torch.stack([xs[s][tok] for s, tok in expect]) if n else x[:0]
+        if n:
+            assert torch.equal(oidx[:n], torch.stack([idxs[s][tok] for s, tok in expect]))
+            assert torch.equal(ow[:n], torch.stack([ws[s][tok] for s, tok in expect]))
+        if quant == "none":
+            assert torch.equal(rows[:n], src_rows)
+            deq = rows[:n].float()
+        elif quant == "fp8":
+            codes, scales = ops.quant_fp8(src_rows)
+            assert torch.equal(rows[:n].view(torch.uint8), codes.view(torch.uint8)) and torch.equal(sc[:n], scales)
+            deq = (rows[:n].float().view(n, H // 128, 128) * sc[:n, :, None]).view(n, H)
+        else:
+            codes, scales = ops.quant_nvfp4(src_rows)
+            assert torch.equal(rows[:n].view(torch.uint8), codes)
+            assert torch.equal(sc[:n, :scales.shape[1]], scales)
+            deq = moe.dequant_nvfp4(rows[:n], sc[:n, :scales.shape[1]])
+        back = _encode(deq * (rank + 1), comb)
+        out, out_w = op.combine(back, ow[:n], oidx[:n])
+        torch.cuda.synchronize()
+        op.check()
+        # Each token's sum over its destination ranks, in rank order (the kernel's order).
+        for tok in range(t):
+            dests = sorted(set((idx[tok] // EPR).tolist()))
+            acc = torch.zeros(H, device="cuda")
+            wsum = torch.zeros(K, device="cuda")
+            for r in dests:
+                q = moe.dispatch_reference(x[tok:tok + 1], quant)
+                if quant == "fp8":
+                    c8, s8 = ops.quant_fp8(x[tok:tok + 1])
+                    q = (c8.float().view(1, H // 128, 128) * s8[:, :, None]).view(1, H)
+                elif quant == "nvfp4":
+                    c4, s4 = ops.quant_nvfp4(x[tok:tok + 1])
+                    q = moe.dequant_nvfp4(c4, s4)
+                acc += _decode(_encode(q * (r + 1), comb), comb)[0]
+                wsum += w[tok]
+            want = _decode(_encode(acc[None], comb), comb)[0]
+            got = _decode(out[tok:tok + 1], comb)[0]
+            bad = (got != want).float().mean().item()
+            assert bad < (2e-3 if comb == "fp4" else 1e-9), (rank, step, tok, bad)
+            assert torch.allclose(out_w[tok], wsum, rtol=1e-6, atol=1e-6), (rank, step, tok)
+        op.reset()
+
+
+def _token_sweep(rank, world):
+    """One op, rounds of 1..256 tokens per rank (the reference's sweeps), rank 0
+    sending a different count than the others: every round returns each
+    token's rows summed over the ranks it went to."""
+    from kiwi_b200.models import moe
+    from kiwi_b200.parallel.ep import KiwiEpOp
+
+    H, K, EPR = 256, 2, 2
+    op = KiwiEpOp(hidden_dim=H, topk=K, num_experts_per_rank=EPR, max_num_inp_token_per_rank=256)
+    for i, t in enumerate((1, 2, 31, 128, 255, 256, 7)):
+        t = t if rank else max(1, t // 3)
+        g = torch.Generator(device="cuda").manual_seed(77 * i + rank)
+        x = torch.randn(t, H, device="cuda", generator=g).bfloat16()
+        idx, w = moe.route_reference(torch.randn(t, EPR * world, device="cuda", generator=g), K)
+        rows, ow, _, oidx, cnt = op.dispatch(x, w, None, idx)
+        torch.cuda.synchronize()
+        n = int(cnt.item())
+        out, _ = op.combine(rows[:n].clone(), None, oidx[:n])
+        torch.cuda.synchronize()
+        op.check()
+        ndest = torch.tensor([len(set((r // EPR).tolist())) for r in idx], device="cuda", dtype=torch.float32)
+        ref = (x.float() * ndest[:, None]).bfloat16()
+        assert (out[:t].float() - ref.float()).abs().max().item() <= 1e-2 * ref.float().abs().max().item() + 1e-2
+        op.reset()
+
+
+@pytest.mark.parametrize("quant,comb", [("none", "bf16"), ("fp8", "f32"), ("nvfp4", "fp8"), ("fp8", "fp4")])
+def test_transport_matrix_world2(quant, comb):
+    _run(_transport_matrix, 2, quant, comb)
+
+
+@pytest.mark.parametrize("quant,comb", [("fp8", "bf16"), ("nvfp4", "f32")])
+def test_transport_matrix_world4(quant, comb):
+    _run(_transport_matrix, 4, quant, comb)
+
+
+@pytest.mark.parametrize("quant,comb", [("none", "bf16"), ("fp8", "bf16"), ("nvfp4", "fp8"), ("fp8", "fp4"),
+                                        ("nvfp4", "f32")])
+def test_transport_matrix_world8(quant, comb):
+    _run(_transport_matrix, 8, quant, comb)
+
+
+def test_token_sweep_2():
+    _run(_token_sweep, 2)
+
+
+def test_token_sweep_8():
+    _run(_token_sweep, 8)
+
+
+@pytest.mark.parametrize("quant,fused", [("fp8", True), ("nvfp4", True), ("fp8", False)])
+def test_ep_layer_world8(quant, fused):
+    _run(_ep_layer, 8, quant, fused)
+
+
+def test_ep_layer_rounds_in_flight_world2():
+    _run(_ep_layer, 2, "fp8", True, 2)
+
+
+def test_ep_layer_rounds_in_flight_world8():
+    _run(_ep_layer, 8, "fp8", True, 2)
 
 
 def test_all_pairs_puts_2():
