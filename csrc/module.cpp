@@ -429,6 +429,41 @@ PYBIND11_MODULE(_C, m) {
           py::arg("idle_polls") = 0, py::arg("loaded") = false, py::arg("cpu_c") = -1, py::arg("cpu_d") = -1,
           "Host-only queue baselines (kiwi ring, head/tail ring, per-slot sequence ring, raw word): ping-pong, "
           "stream, and optionally the idle-poll cost and the loaded ping-pong.");
+    b.def("gpu_queue_baseline",
+          [](const std::string& queue, const std::string& mode, uint64_t iters, uint64_t warmup, uint32_t warps,
+             uint64_t capacity, int cpu, uint64_t timeout_ns) {
+              bench::GpuQueueBaselineOptions o;
+              o.queue = queue;
+              o.mode = mode;
+              o.iters = iters;
+              o.warmup = warmup;
+              o.warps = warps;
+              o.capacity = capacity;
+              o.cpu = cpu;
+              o.timeout_ns = timeout_ns;
+              bench::GpuQueueBaselineResult r;
+              {
+                  py::gil_scoped_release nogil;
+                  r = bench::gpu_queue_baseline(o);
+              }
+              py::dict d;
+              d["queue"] = r.queue;
+              d["mode"] = r.mode;
+              d["ok"] = r.ok;
+              d["status"] = r.status;
+              d["messages"] = r.messages;
+              d["bad"] = r.bad;
+              d["order_errors"] = r.order_errors;
+              d["seconds"] = r.seconds;
+              d["cycles_per_push"] = r.cycles_per_push;
+              d["lat_ns"] = to_numpy(r.lat_ns);
+              return d;
+          },
+          py::arg("queue"), py::arg("mode") = "latency", py::arg("iters") = 10000, py::arg("warmup") = 1000,
+          py::arg("warps") = 1, py::arg("capacity") = 4096, py::arg("cpu") = -1,
+          py::arg("timeout_ns") = 2000000000ull,
+          "GPU-producer queue comparators (kiwi_spsc, kiwi_mpsc, fifo_trigger, proxy_channel, raw_store) in latency, "
+          "throughput or push_cost mode; a pinned host thread consumes and validates every message.");
     b.def("host_ring_stream",
           [](uint64_t n, uint64_t cap, uint32_t bytes, uint64_t seed, int a, int c) {
               bench::HostRingResult r;

@@ -17,6 +17,7 @@
 #include <thread>
 
 #include "kiwi/bench/gpu_bench.hpp"
+#include "kiwi/bench/host_server.hpp"
 #include "kiwi/bench/host_bench.hpp"
 #include "kiwi/invoke/invoke.hpp"
 #include "kiwi/queue/mailbox.cuh"
@@ -83,45 +84,6 @@ int pick_cpu(int cpu) {
     return cpus.empty() ? -1 : cpus[0];
 }
 
-/// Runs the host side of a benchmark kernel on its own thread, started (on
-/// the caller's device, pinned to `cpu` when it is >= 0) BEFORE `launch()`
-/// runs on the calling thread.  A tool that blocks inside the launch call (a
-/// profiler that replays the kernel) then cannot leave the kernel without its
-/// host side until the kernel's bounded waits expire.  `serve(launched, quit)`
-/// polls until its work is done; it may ask whether the launch has returned
-/// (`launched`, so an empty stream before the launch is not taken for a
-/// finished kernel) and must return when `quit` turns true (the launch threw).
-template <typename Launch, typename Serve>
-void launch_with_server(int cpu, Launch&& launch, Serve&& serve) {
-    std::atomic<bool> launched{false}, quit{false};
-    std::exception_ptr err;
-    int dev = 0;
-    KIWI_CUDA_CHECK(cudaGetDevice(&dev));
-    std::thread th([&] {
-        try {
-            KIWI_CUDA_CHECK(cudaSetDevice(dev));
-            if (cpu >= 0) topology::bind_current_thread({cpu});
-            serve(launched, quit);
-        } catch (...) {
-            err = std::current_exception();
-        }
-    });
-    try {
-        launch();
-    } catch (...) {
-        quit.store(true);
-        th.join();
-        throw;
-    }
-    launched.store(true, std::memory_order_release);
-    th.join();
-    if (err) std::rethrow_exception(err);
-}
-
-/// True when `stream` has no work left; only asked after the launch returned.
-bool stream_idle(cudaStream_t stream, const std::atomic<bool>& launched) {
-    return launched.load(std::memory_order_acquire) && cudaStreamQuery(stream) != cudaErrorNotReady;
-}
 
 }  // namespace
 

@@ -50,6 +50,31 @@ RttResult pcie_floor(uint64_t iters, uint64_t warmup, int cpu, uint64_t timeout_
 RttResult rtt_lab(uint64_t iters, uint64_t warmup, uint32_t pollers, uint32_t mirrors, uint32_t stagger_ns,
                   uint32_t fence, uint32_t pipeline, int cpu, uint32_t initial_delay_ns = 0);
 
+/// GPU-producer queue comparators (csrc/queue_baselines_gpu.cu): one driver
+/// kernel, one pinned host consumer thread, per-message validation.
+struct GpuQueueBaselineOptions {
+    std::string queue = "kiwi_spsc";   // kiwi_spsc, kiwi_mpsc, fifo_trigger, proxy_channel, raw_store
+    std::string mode = "latency";      // latency, throughput, push_cost
+    uint64_t iters = 10000;            // per warp (throughput, push_cost) or timed round trips (latency)
+    uint64_t warmup = 1000;            // latency mode
+    uint32_t warps = 1;                // producer warps (throughput, push_cost)
+    uint64_t capacity = 4096;          // messages the queue holds
+    int cpu = -1;                      // consumer thread core (-1: a GPU-local core)
+    uint64_t timeout_ns = 2000000000ull;
+};
+
+struct GpuQueueBaselineResult {
+    std::string queue, mode;
+    bool ok = false;                   // every message arrived once, in per-producer order, with its check word
+    uint32_t status = 0;               // kiwi::Status of the device side (0 = ok)
+    uint64_t messages = 0, bad = 0, order_errors = 0;
+    double seconds = 0;                // host wall clock from launch to the last pop
+    double cycles_per_push = 0;        // throughput / push_cost: SM cycles per push, mean over warps
+    std::vector<uint64_t> lat_ns;      // latency: push -> host pop -> ack seen, per timed iteration
+};
+
+GpuQueueBaselineResult gpu_queue_baseline(const GpuQueueBaselineOptions& options);
+
 struct AtomicityResult {
     uint64_t reads = 0;    // 16-byte chunks the host read while the GPU wrote
     uint64_t torn8 = 0;    // 8-byte halves whose two words came from different rounds
