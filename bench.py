@@ -12,11 +12,10 @@ block-scaled FP8 e4m3 dispatch, random-init N(0,0.02) weights, seeded
 synthetic data.  A step is one full layer forward: routing, FP8 dispatch over
 NVLink, expert-major layout, two grouped GEMMs, combine over NVLink and the
 final reduction.  Weak scaling: tokens per rank are fixed as N grows.  The
-timed steps keep two rounds in flight (--in-flight 2, the serving
-configuration: each round is a full layer forward of its own 4096 tokens per
-rank on its own buffers and stream, so one round's dispatch / receive /
-combine overlap another round's GEMMs); `serial` reports the same layer one
-round at a time.
+timed steps run one round at a time; --in-flight 2 keeps two rounds in flight
+instead (each a full layer forward of its own 4096 tokens per rank on its own
+buffers and stream, so one round's dispatch / receive / combine overlap the
+other's GEMMs) and then also reports the one-at-a-time time as `serial`.
 
 Timing: W warm-up steps, then K steps bracketed by a barrier and
 torch.cuda.synchronize() on both sides, CUDA events on the launching stream,
@@ -70,7 +69,7 @@ def parse():
     ap.add_argument("--invoke-warmup", type=int, default=10_000)
     ap.add_argument("--sweep-iters", type=int, default=100_000, help="iterations per payload size of the sweep")
     ap.add_argument("--check-tokens", type=int, default=16, help="tokens per rank the correctness check samples")
-    ap.add_argument("--in-flight", type=int, default=2,
+    ap.add_argument("--in-flight", type=int, default=1,
                     help="rounds of the fused layer in flight during the timed steps (1: one round at a time)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-baseline", action="store_true", help="skip the in-process NCCL baseline")

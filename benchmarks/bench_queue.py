@@ -11,6 +11,11 @@ benchmarks/invoke/bench_{throughput,overhead}.hip.cpp of AMDResearch/kiwi).
   per-slot sequence ring, single-word floor), plus the cost of one poll of an
   empty queue and the ping-pong under a concurrent stream; reference:
   benchmarks/queue_baselines.
+* gpu_queue_baseline: the device-producer comparators (this repository's SPSC
+  and MPSC rings, an index-publishing trigger FIFO in the style of MSCCL++'s
+  proxy FIFO, a lap-parity proxy channel in the style of NVSHMEM's, and the
+  raw-store floor) in latency, throughput (W warps, one host consumer) and
+  push-cost modes; reference: benchmarks/queue_baselines (GPU side).
 * invoke_throughput: E producer warps x T progress threads, messages/s.
 * push_cost: SM cycles one warp spends per push (payload 8 .. 256 B).
 """
@@ -49,6 +54,20 @@ def main():
               "loaded_bg_Mmsg_per_s": q["loaded_bg_msgs_per_s"] / 1e6})
     if not C.cuda_device_available():
         return
+    for q in ("kiwi_spsc", "kiwi_mpsc", "fifo_trigger", "proxy_channel", "raw_store"):
+        r = C.bench.gpu_queue_baseline(q, "latency", iters=100_000, warmup=10_000, capacity=4096)
+        lat = np.asarray(r["lat_ns"], dtype=np.float64)
+        emit({"bench": "gpu_queue_baseline", "queue": q, "mode": "latency", "ok": r["ok"],
+              "p50_us": float(np.percentile(lat, 50)) / 1e3, "p99_us": float(np.percentile(lat, 99)) / 1e3})
+    for q in ("kiwi_spsc", "kiwi_mpsc", "fifo_trigger", "proxy_channel"):
+        for w in ((1,) if q == "kiwi_spsc" else (1, 16, 64)):
+            r = C.bench.gpu_queue_baseline(q, "throughput", iters=50_000, warps=w, capacity=4096)
+            emit({"bench": "gpu_queue_baseline", "queue": q, "mode": "throughput", "warps": w, "ok": r["ok"],
+                  "Mmsg_per_s": r["messages"] / max(r["seconds"], 1e-9) / 1e6,
+                  "cycles_per_push": r["cycles_per_push"]})
+        r = C.bench.gpu_queue_baseline(q, "push_cost", iters=20_000, warps=1, capacity=32768)
+        emit({"bench": "gpu_queue_baseline", "queue": q, "mode": "push_cost", "ok": r["ok"],
+              "cycles_per_push": r["cycles_per_push"]})
     for e, t in [(1, 1), (4, 1), (8, 2), (16, 4), (64, 4)]:
         r = C.bench.invoke_throughput(e, t, 20000, 8, 4096)
         emit({"bench": "invoke_throughput", "endpoints": e, "threads": t, "ok": r["ok"],

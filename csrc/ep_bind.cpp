@@ -100,6 +100,7 @@ py::dict tuning_dict(const ep::EpTuning& t) {
     d["fused_combine"] = t.fused_combine;
     d["gather_a"] = t.gather_a;
     d["gemm_pair"] = t.gemm_pair;
+    d["gemm_pair_auto"] = t.gemm_pair_auto;
     d["source"] = t.source;
     return d;
 }
@@ -228,6 +229,7 @@ public:
         tmap_b2h_ = gemm::make_tmap_bf16_2d(w2.data_ptr(), w2.size(0), ffn, 128);
         tuning_ = ep::tune(cfg_, gemm::num_sms());
         pair_ = tuning_.gemm_pair;
+        pair_auto_ = tuning_.gemm_pair_auto;
         fused_ = tuning_.fused_combine;
         gather_ = tuning_.gather_a;
     }
@@ -249,6 +251,9 @@ public:
         if (!routed_) debug_.reset(s);  // a round starts at route() when the layer routes
         routed_ = false;
         tokens_ = static_cast<int>(x.size(0));
+        // Rows each local expert expects this round, if every rank sends as many tokens.
+        const int64_t rows = static_cast<int64_t>(cfg_.world) * tokens_ * cfg_.topk / cfg_.num_experts;
+        use_pair_ = pair_ || (pair_auto_ && rows >= ep::kPairMinRows);
         ep::launch_begin(cfg_, ws_, s);
         ep::launch_dispatch(cfg_, heap_.view(), reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()),
                             idx.data_ptr<int32_t>(), w.data_ptr<float>(), static_cast<int>(x.size(0)), ws_,
@@ -262,10 +267,13 @@ public:
         // streams at once).
         ep::launch_wait_flags(cfg_, heap_.view(), ws_, 0, timeout_ns_, s);
         ep::launch_recv_count(cfg_, heap_.view(), ws_, timeout_ns_, s, /*waited=*/true);
-        const int bm = pair_ ? 256 : 128;
+        // Rows per tile of each GEMM's kernel: the 2-SM kernel takes 256-row tiles;
+        // the gathering GEMM1 and the scatter GEMM2 (fused combine) are 1-SM kernels.
+        const int bm1 = use_pair_ && !gathers() ? 256 : 128;
+        const int bm2 = use_pair_ ? 256 : 128;
         gemm::build_schedule(ws_.expert_count, cfg_.experts_per_rank, static_cast<int>(2 * ffn_), 256, ws_.offsets,
-                             ws_.tiles1, s, bm);
-        gemm::build_schedule(ws_.expert_count, cfg_.experts_per_rank, cfg_.hidden, 256, ws_.offsets, ws_.tiles2, s, bm);
+                             ws_.tiles1, s, bm1);
+        gemm::build_schedule(ws_.expert_count, cfg_.experts_per_rank, cfg_.hidden, 256, ws_.offsets, ws_.tiles2, s, bm2);
         ep::launch_recv_assign(cfg_, heap_.view(), ws_, s, tuning_.recv_blocks);
         if (!gathers()) ep::launch_recv_copy(cfg_, heap_.view(), ws_, s, tuning_.recv_blocks);
     }
@@ -307,7 +315,7 @@ public:
                 ga.scale_bytes = cfg_.scale_bytes;
                 ga.quant = cfg_.quant;
                 gemm::grouped_gemm_gather(tmap_b1_, g1, ga, 0, s);
-            } else if (pair_) {
+            } else if (use_pair_) {
                 gemm::grouped_gemm_pair(tmap_a1_, tmap_b1h_, g1, /*swiglu=*/true, 0, s);
             } else {
                 gemm::grouped_gemm(tmap_a1_, tmap_b1_, g1, /*swiglu=*/true, 0, s);
@@ -332,8 +340,9 @@ public:
             sc.epoch = ws_.epoch;
             sc.flag_off = cfg_.combine_flag(cfg_.rank);
             sc.world = cfg_.world;
-            gemm::grouped_gemm_scatter(tmap_a2_, tmap_b2_, g2, sc, 0, s);
-        } else if (pair_) {
+            if (use_pair_) gemm::grouped_gemm_pair_scatter(tmap_a2_, tmap_b2h_, g2, sc, 0, s);
+            else gemm::grouped_gemm_scatter(tmap_a2_, tmap_b2_, g2, sc, 0, s);
+        } else if (use_pair_) {
             gemm::grouped_gemm_pair(tmap_a2_, tmap_b2h_, g2, /*swiglu=*/false, 0, s);
         } else {
             gemm::grouped_gemm(tmap_a2_, tmap_b2_, g2, /*swiglu=*/false, 0, s);
@@ -402,7 +411,7 @@ public:
         m[ep::kMetaQuant] = cfg_.quant;
         m[ep::kMetaFusedCombine] = fused_;
         m[ep::kMetaGatherA] = gathers();
-        m[ep::kMetaGemmPair] = pair_;
+        m[ep::kMetaGemmPair] = use_pair_;
         return debug_.snapshot(m);
     }
 
@@ -441,7 +450,9 @@ private:
         slot_pos_, a_, h_, y_, error_, gemm_error_, pair_dst_;
     ep::EpWorkspace ws_{};
     CUtensorMap tmap_a1_, tmap_b1_, tmap_a2_, tmap_b2_, tmap_b1h_, tmap_b2h_;
-    bool pair_ = false;
+    bool pair_ = false;       // 2-SM GEMMs in every round
+    bool pair_auto_ = true;   // 2-SM GEMMs when a round expects kPairMinRows rows per local expert
+    bool use_pair_ = false;   // this round's choice (set by dispatch)
     bool fused_ = true;
     bool gather_ = false;
     ep::EpTuning tuning_{};
@@ -454,6 +465,9 @@ public:
     void set_gather(bool v) { gather_ = v; }
     bool pair() const { return pair_; }
     void set_pair(bool v) { pair_ = v; }
+    bool pair_auto() const { return pair_auto_; }
+    void set_pair_auto(bool v) { pair_auto_ = v; }
+    bool pair_in_use() const { return use_pair_; }
     bool fused() const { return fused_; }
     py::dict tuning() const { return tuning_dict(tuning_); }
     void set_fused(bool v) { fused_ = v; }
@@ -699,8 +713,13 @@ void register_ep(py::module_& m) {
         .def_property_readonly("expert_hidden", &MoeLayer::expert_hidden)
         .def_property_readonly("expert_output", &MoeLayer::expert_output)
         .def_property_readonly("epoch", &MoeLayer::epoch)
+        .def_property("gemm_pair_auto", &MoeLayer::pair_auto, &MoeLayer::set_pair_auto,
+                      "Use the 2-SM GEMMs in rounds whose expected rows per local expert reach 512 (default on).")
+        .def_property_readonly("gemm_pair_in_use", &MoeLayer::pair_in_use,
+                               "Whether the last dispatched round uses the 2-SM GEMMs.")
         .def_property("gemm_pair", &MoeLayer::pair, &MoeLayer::set_pair,
-                      "Use the 2-SM (256-row tile) grouped GEMM (unfused combine only; off by default).")
+                      "Use the 2-SM (256-row tile) grouped GEMMs in every round (off by default; gemm_pair_auto "
+                      "picks them per round).")
         .def_property_readonly("tuning", &MoeLayer::tuning, "Launch tuning in effect (B200 table + KIWI_EP_TUNING).")
         .def_property("gather_a", &MoeLayer::gather, &MoeLayer::set_gather,
                       "GEMM1 gathers and dequantises its A rows from the receive buffer (FP8 / NVFP4 dispatch; "

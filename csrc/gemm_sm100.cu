@@ -111,6 +111,77 @@ __device__ __forceinline__ void store_row32(__nv_bfloat16* dst, const float (&v)
     for (int i = 0; i < 4; ++i) d[i] = out[i];
 }
 
+/// Scatter epilogue of one 256-column accumulator tile for the 32 rows of the
+/// calling warp (TMEM lane quadrant = the warp's rows): per half tile (128
+/// columns) the warp stages its rows, routing-weight scaled, as bf16 in
+/// XOR-swizzled shared memory, then stores them as 256-byte row segments (16
+/// lanes per row, two rows per instruction) straight into each row's
+/// destination (`my_dst` = (rank << 48) | byte offset, -1 = none) in the
+/// ranks' heaps.  `release()` runs once the accumulator has been read, before
+/// the second half's stores, so the next tile's MMAs overlap them.
+template <typename Release>
+__device__ __forceinline__ void scatter_tile(uint32_t taddr, uint8_t* stg, int64_t my_dst, float scale, int nt,
+                                             uint8_t* const* s_base, Release&& release) {
+    constexpr int BN = 256;
+    constexpr int kStride = BN;  // BN / 2 bf16 columns = BN bytes per staged row
+    const int lane = threadIdx.x & 31;
+    const int half_lane = lane & 15;
+#pragma unroll 1
+    for (int half = 0; half < 2; ++half) {
+#pragma unroll 1
+        for (int c = 0; c < BN / 2; c += 32) {
+            float v[32];
+            sm100::tmem_ld_32cols(taddr + half * (BN / 2) + c, v);
+            uint32_t w[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+                __nv_bfloat162 hv = __floats2bfloat162_rn(v[2 * i] * scale, v[2 * i + 1] * scale);
+                w[i] = *reinterpret_cast<uint32_t*>(&hv);
+            }
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const int chunk = (c / 8 + j) ^ (lane & 15);
+                *reinterpret_cast<uint4*>(stg + lane * kStride + chunk * 16) =
+                    make_uint4(w[4 * j], w[4 * j + 1], w[4 * j + 2], w[4 * j + 3]);
+            }
+        }
+        if (half == 1) release();
+        __syncwarp();
+#pragma unroll 1
+        for (int rr = 0; rr < 32; rr += 2) {
+            const int row = rr + (lane >> 4);
+            const long long d = __shfl_sync(0xffffffffu, static_cast<long long>(my_dst), row);
+            if (d >= 0) {
+                const int rank = static_cast<int>(d >> 48);
+                uint8_t* dst = s_base[rank] + (d & kScatterOffMask) +
+                               (static_cast<int64_t>(nt) * BN + half * (BN / 2)) * 2 + half_lane * 16;
+                const uint4 val =
+                    *reinterpret_cast<const uint4*>(stg + row * kStride + ((half_lane ^ (row & 15)) * 16));
+                asm volatile("st.global.v4.u32 [%0], {%1, %2, %3, %4};" ::"l"(dst), "r"(val.x), "r"(val.y),
+                             "r"(val.z), "r"(val.w)
+                             : "memory");
+            }
+        }
+        __syncwarp();
+    }
+}
+
+/// Completion of a scatter GEMM: every CTA that did not abort releases its
+/// stores at system scope and counts itself; the last one publishes
+/// (epoch << 32) | 1 to every rank's flag.  Thread 0 only.
+__device__ __forceinline__ void scatter_done(const ScatterArgs& sc, uint8_t* const* s_base) {
+    asm volatile("fence.sc.sys;" ::: "memory");
+    const uint32_t prev = atomicAdd(sc.done_ctas, 1u);
+    if (prev == gridDim.x - 1) {
+        asm volatile("fence.sc.sys;" ::: "memory");
+        const uint64_t v = (static_cast<uint64_t>(*reinterpret_cast<const volatile uint32_t*>(sc.epoch)) << 32) | 1u;
+        for (int r = 0; r < sc.world; ++r) {
+            asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(s_base[r] + sc.flag_off), "l"(v) : "memory");
+        }
+        *reinterpret_cast<volatile uint32_t*>(sc.done_ctas) = 0;
+    }
+}
+
 template <int BN, int EPI, int STAGES, int GQ = -1, int BKT = kBK>
 __global__ void __launch_bounds__(GQ >= 0 ? kGatherThreads : kThreads, 1)
     grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
@@ -435,48 +506,10 @@ __global__ void __launch_bounds__(GQ >= 0 ? kGatherThreads : kThreads, 1)
                 static_assert(BN == 256, "scatter staging assumes 256-column tiles");
                 uint8_t* stg = smem + S::kStgOffset + q * 32 * S::kStgStride;
                 const int64_t my_dst = valid ? __ldg(&sc.row_dst[out_row]) : -1;
-                const int half_lane = lane & 15;
-#pragma unroll 1
-                for (int half = 0; half < 2; ++half) {
-#pragma unroll 1
-                    for (int c = 0; c < BN / 2; c += 32) {
-                        float v[32];
-                        sm100::tmem_ld_32cols(taddr + half * (BN / 2) + c, v);
-                        uint32_t w[16];
-#pragma unroll
-                        for (int i = 0; i < 16; ++i) {
-                            __nv_bfloat162 hv = __floats2bfloat162_rn(v[2 * i] * scale, v[2 * i + 1] * scale);
-                            w[i] = *reinterpret_cast<uint32_t*>(&hv);
-                        }
-#pragma unroll
-                        for (int j = 0; j < 4; ++j) {
-                            const int chunk = (c / 8 + j) ^ (lane & 15);
-                            *reinterpret_cast<uint4*>(stg + lane * S::kStgStride + chunk * 16) =
-                                make_uint4(w[4 * j], w[4 * j + 1], w[4 * j + 2], w[4 * j + 3]);
-                        }
-                    }
-                    if (half == 1) {
-                        sm100::tc_fence_before();
-                        sm100::mbar_arrive(&tmem_empty[acc]);
-                    }
-                    __syncwarp();
-#pragma unroll 1
-                    for (int rr = 0; rr < 32; rr += 2) {
-                        const int row = rr + (lane >> 4);
-                        const long long d = __shfl_sync(0xffffffffu, static_cast<long long>(my_dst), row);
-                        if (d >= 0) {
-                            const int rank = static_cast<int>(d >> 48);
-                            uint8_t* dst = s_base[rank] + (d & kScatterOffMask) +
-                                           (static_cast<int64_t>(nt) * BN + half * (BN / 2)) * 2 + half_lane * 16;
-                            const uint4 val = *reinterpret_cast<const uint4*>(
-                                stg + row * S::kStgStride + ((half_lane ^ (row & 15)) * 16));
-                            asm volatile("st.global.v4.u32 [%0], {%1, %2, %3, %4};" ::"l"(dst), "r"(val.x),
-                                         "r"(val.y), "r"(val.z), "r"(val.w)
-                                         : "memory");
-                        }
-                    }
-                    __syncwarp();
-                }
+                scatter_tile(taddr, stg, my_dst, scale, nt, s_base, [&] {
+                    sm100::tc_fence_before();
+                    sm100::mbar_arrive(&tmem_empty[acc]);
+                });
             }
             if (++acc == 2) {
                 acc = 0;
@@ -492,19 +525,7 @@ __global__ void __launch_bounds__(GQ >= 0 ? kGatherThreads : kThreads, 1)
         // Completion: every CTA releases its stores at system scope and counts
         // itself; the last one publishes (epoch << 32) | 1 to every rank.  A CTA
         // that aborted does not count, so the receivers' bounded waits report it.
-        if (threadIdx.x == 0 && !*reinterpret_cast<volatile int*>(&s_abort)) {
-            asm volatile("fence.sc.sys;" ::: "memory");
-            const uint32_t prev = atomicAdd(sc.done_ctas, 1u);
-            if (prev == gridDim.x - 1) {
-                asm volatile("fence.sc.sys;" ::: "memory");
-                const uint64_t v = (static_cast<uint64_t>(*reinterpret_cast<const volatile uint32_t*>(sc.epoch)) << 32) | 1u;
-                for (int r = 0; r < sc.world; ++r) {
-                    asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(s_base[r] + sc.flag_off), "l"(v)
-                                 : "memory");
-                }
-                *reinterpret_cast<volatile uint32_t*>(sc.done_ctas) = 0;
-            }
-        }
+        if (threadIdx.x == 0 && !*reinterpret_cast<volatile int*>(&s_abort)) scatter_done(sc, s_base);
     }
     if (threadIdx.x == 0) ep::span_end(p.span);
 }
@@ -525,19 +546,32 @@ constexpr int kPairStages = 6;
 constexpr int kPairBM = 256;  // rows per pair tile (128 per CTA)
 constexpr int kPairBN = 256;
 
+/// Shared memory of one CTA of the pair: kPairStages x (A half + B half), then
+/// (scatter epilogue) one 32-row x 128-column bf16 staging tile per epilogue
+/// warp, then the barriers.  6 x 32 KB + 32 KB + 1.25 KB fits the 227 KB limit.
+template <bool STAGING = false>
 struct PairSmem {
     static constexpr int kABytes = 128 * kBK * 2;     // this CTA's 128 rows of A
     static constexpr int kBBytes = 128 * kBK * 2;     // this CTA's half of the B tile
     static constexpr int kStageBytes = kABytes + kBBytes;
-    static constexpr int kBarOffset = kPairStages * kStageBytes;
+    static constexpr int kStgOffset = kPairStages * kStageBytes;
+    static constexpr int kStgStride = kPairBN;        // 128 bf16 columns = 256 bytes per staged row
+    static constexpr int kStgBytes = STAGING ? 4 * 32 * kStgStride : 0;
+    static constexpr int kBarOffset = kStgOffset + kStgBytes;
     static constexpr int kBytes = kBarOffset + 256 + 1024;
 };
+static_assert(PairSmem<true>::kBytes <= 227 * 1024, "pair scatter kernel exceeds the shared-memory limit");
 
-template <bool SWIGLU>
+template <int EPI>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     grouped_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
-                             GroupedArgs p) {
-    using S = PairSmem;
+                             GroupedArgs p, const __grid_constant__ ScatterArgs sc) {
+    constexpr bool SWIGLU = EPI == kEpiSwiGLU;
+    using S = PairSmem<EPI == kEpiScatter>;
+    __shared__ uint8_t* s_base[kScatterMaxRanks];
+    if constexpr (EPI == kEpiScatter) {
+        if (threadIdx.x < kScatterMaxRanks) s_base[threadIdx.x] = sc.base[threadIdx.x];
+    }
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::kBarOffset);
@@ -681,7 +715,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             const bool valid = r < g_rows && out_row < p.max_rows;
             const float scale = (valid && p.row_scale) ? p.row_scale[out_row] : 1.0f;
             const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * kPairBN;
-            if constexpr (SWIGLU) {
+            if constexpr (EPI == kEpiScatter) {
+                uint8_t* stg = smem + S::kStgOffset + q * 32 * S::kStgStride;
+                const int64_t my_dst = valid ? __ldg(&sc.row_dst[out_row]) : -1;
+                scatter_tile(taddr, stg, my_dst, scale, nt, s_base, [&] {
+                    sm100::tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) {
+                        sm100::mbar_arrive_cluster(empty_leader + acc * static_cast<uint32_t>(sizeof(uint64_t)));
+                    }
+                });
+            } else if constexpr (SWIGLU) {
                 __nv_bfloat16* crow = p.c + out_row * p.ldc + nt * (kPairBN / 2);
 #pragma unroll 1
                 for (int c = 0; c < kPairBN / 2; c += 32) {
@@ -703,9 +747,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                     if (valid) store_row32(crow + c, v);
                 }
             }
-            sm100::tc_fence_before();
-            __syncwarp();
-            if (lane == 0) sm100::mbar_arrive_cluster(empty_leader + acc * static_cast<uint32_t>(sizeof(uint64_t)));
+            if constexpr (EPI != kEpiScatter) {  // the scatter epilogue released the accumulator itself
+                sm100::tc_fence_before();
+                __syncwarp();
+                if (lane == 0) {
+                    sm100::mbar_arrive_cluster(empty_leader + acc * static_cast<uint32_t>(sizeof(uint64_t)));
+                }
+            }
             if (++acc == 2) {
                 acc = 0;
                 acc_phase ^= 1;
@@ -717,6 +765,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     sm100::cluster_sync();  // neither CTA leaves while its peer may still touch its barriers
     sm100::tc_fence_after();
     if (warp == 1) sm100::tmem_dealloc_pair(tmem_base, 2 * kPairBN);
+    if constexpr (EPI == kEpiScatter) {
+        if (threadIdx.x == 0 && !abort_flag()) scatter_done(sc, s_base);
+    }
     if (threadIdx.x == 0) ep::span_end(p.span);
 }
 
@@ -909,32 +960,51 @@ void grouped_gemm_scatter(const CUtensorMap& tmap_a, const CUtensorMap& tmap_b, 
     launch_grouped<kEpiScatter, kScatterStages>(tmap_a, tmap_b, args, sc, grid, stream);
 }
 
-void grouped_gemm_pair(const CUtensorMap& tmap_a, const CUtensorMap& tmap_b_half, const GroupedArgs& args,
-                       bool swiglu, int grid, cudaStream_t stream) {
+namespace {
+
+template <int EPI>
+void launch_pair(const CUtensorMap& tmap_a, const CUtensorMap& tmap_b_half, const GroupedArgs& args,
+                 const ScatterArgs& sc, int grid, cudaStream_t stream) {
     if (args.n % kPairBN != 0 || args.k % kBK != 0) {
         throw kiwi::error("grouped_gemm_pair: N must be a multiple of 256 and K of 64");
     }
-    const int smem = PairSmem::kBytes;
+    const int smem = PairSmem<EPI == kEpiScatter>::kBytes;
     if (grid <= 0) grid = num_sms();
     grid &= ~1;  // whole clusters of two
     if (grid < 2) throw kiwi::error("grouped_gemm_pair: needs at least two SMs");
-    if (swiglu) {
-        static std::atomic<uint64_t> attr{0};
-        raise_smem_limit(grouped_gemm_pair_kernel<true>, smem, attr);
-        grouped_gemm_pair_kernel<true><<<grid, kThreads, smem, stream>>>(tmap_a, tmap_b_half, args);
-    } else {
-        static std::atomic<uint64_t> attr{0};
-        raise_smem_limit(grouped_gemm_pair_kernel<false>, smem, attr);
-        grouped_gemm_pair_kernel<false><<<grid, kThreads, smem, stream>>>(tmap_a, tmap_b_half, args);
-    }
+    static std::atomic<uint64_t> attr{0};
+    raise_smem_limit(grouped_gemm_pair_kernel<EPI>, smem, attr);
+    grouped_gemm_pair_kernel<EPI><<<grid, kThreads, smem, stream>>>(tmap_a, tmap_b_half, args, sc);
     KIWI_CUDA_CHECK(cudaGetLastError());
+}
+
+}  // namespace
+
+void grouped_gemm_pair(const CUtensorMap& tmap_a, const CUtensorMap& tmap_b_half, const GroupedArgs& args,
+                       bool swiglu, int grid, cudaStream_t stream) {
+    const ScatterArgs none{};
+    if (swiglu) launch_pair<kEpiSwiGLU>(tmap_a, tmap_b_half, args, none, grid, stream);
+    else launch_pair<kEpiStore>(tmap_a, tmap_b_half, args, none, grid, stream);
+}
+
+void grouped_gemm_pair_scatter(const CUtensorMap& tmap_a, const CUtensorMap& tmap_b_half, const GroupedArgs& args,
+                               const ScatterArgs& sc, int grid, cudaStream_t stream) {
+    if (!sc.row_dst || !sc.done_ctas || !sc.epoch) throw kiwi::error("grouped_gemm_pair_scatter: missing arguments");
+    if (sc.world < 1 || sc.world > kScatterMaxRanks) throw kiwi::error("grouped_gemm_pair_scatter: world out of range");
+    launch_pair<kEpiScatter>(tmap_a, tmap_b_half, args, sc, grid, stream);
 }
 
 KernelInfo gemm_pair_kernel_info(bool swiglu) {
     cudaFuncAttributes a{};
-    if (swiglu) KIWI_CUDA_CHECK(cudaFuncGetAttributes(&a, grouped_gemm_pair_kernel<true>));
-    else KIWI_CUDA_CHECK(cudaFuncGetAttributes(&a, grouped_gemm_pair_kernel<false>));
-    return {static_cast<int>(a.localSizeBytes), a.numRegs, PairSmem::kBytes};
+    if (swiglu) KIWI_CUDA_CHECK(cudaFuncGetAttributes(&a, grouped_gemm_pair_kernel<kEpiSwiGLU>));
+    else KIWI_CUDA_CHECK(cudaFuncGetAttributes(&a, grouped_gemm_pair_kernel<kEpiStore>));
+    return {static_cast<int>(a.localSizeBytes), a.numRegs, PairSmem<false>::kBytes};
+}
+
+KernelInfo gemm_pair_scatter_kernel_info() {
+    cudaFuncAttributes a{};
+    KIWI_CUDA_CHECK(cudaFuncGetAttributes(&a, grouped_gemm_pair_kernel<kEpiScatter>));
+    return {static_cast<int>(a.localSizeBytes), a.numRegs, PairSmem<true>::kBytes};
 }
 
 KernelInfo gemm_kernel_info(bool swiglu) {

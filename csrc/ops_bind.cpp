@@ -184,6 +184,10 @@ void register_ops(py::module_& m) {
         const auto i = gemm::gemm_pair_kernel_info(swiglu);
         return py::make_tuple(i.local_bytes, i.registers, i.smem_bytes);
     });
+    o.def("gemm_scatter_kernel_info", [](bool pair) {
+        const auto i = pair ? gemm::gemm_pair_scatter_kernel_info() : gemm::gemm_scatter_kernel_info();
+        return py::make_tuple(i.local_bytes, i.registers, i.smem_bytes);
+    }, py::arg("pair") = false, "(local bytes, registers, shared bytes) of the NVLink scatter GEMM (1-SM or 2-SM).");
     o.def("num_sms", &gemm::num_sms);
     o.def(
         "quant_fp8",

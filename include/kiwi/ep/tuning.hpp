@@ -8,7 +8,7 @@
 // fused paths the layer uses, keyed by the rank's token capacity, and records
 // where each choice was measured.  KIWI_EP_TUNING="key=value,..." overrides
 // any field (keys: dispatch_blocks, recv_blocks, combine_blocks,
-// fused_combine, gather_a, gemm_pair).
+// fused_combine, gather_a, gemm_pair, gemm_pair_auto).
 #pragma once
 
 #include <string>
@@ -23,9 +23,14 @@ struct EpTuning {
     int32_t combine_blocks;   // combine send / reduce grid
     bool fused_combine;       // GEMM2 epilogue stores over NVLink
     bool gather_a;            // GEMM1 gathers A from the receive slots
-    bool gemm_pair;           // 2-SM (256-row tile) grouped GEMM
+    bool gemm_pair;           // 2-SM (256-row tile) grouped GEMMs in every round
+    bool gemm_pair_auto;      // 2-SM GEMMs in rounds whose expected rows per local expert reach kPairMinRows
     std::string source;       // table entry (and overrides) this came from
 };
+
+/// Expected rows per local expert from which a round uses the 2-SM GEMMs
+/// (with fewer, half of a 256-row tile is padding more often than not).
+inline constexpr int kPairMinRows = 512;
 
 /// Tuning for configuration `c` on a GPU with `sms` SMs, then the
 /// KIWI_EP_TUNING overrides (`env` stands in for the variable in tests;

@@ -131,6 +131,13 @@ KernelInfo gemm_kernel_info(bool swiglu);
 KernelInfo gemm_gather_kernel_info(int quant);
 KernelInfo gemm_scatter_kernel_info();
 KernelInfo gemm_pair_kernel_info(bool swiglu);
+KernelInfo gemm_pair_scatter_kernel_info();
+
+/// The 2-SM kernel (256-row tiles, cta_group::2) with the NVLink scatter
+/// epilogue of grouped_gemm_scatter (same ScatterArgs, same completion
+/// signal); tmap_b_half as grouped_gemm_pair.  Schedules with bm = 256.
+void grouped_gemm_pair_scatter(const CUtensorMap& tmap_a, const CUtensorMap& tmap_b_half, const GroupedArgs& args,
+                               const ScatterArgs& sc, int grid, cudaStream_t stream);
 int num_sms();
 
 }  // namespace kiwi::gemm

@@ -163,8 +163,9 @@ class ExpertParallelMoE(_DebugTimingMixin):
     ``in_flight`` > 1 gives the layer that many independent round states
     (each with its own symmetric heap, workspace and stream).  Rounds handed to
     :meth:`submit` then run on those streams in turn, so the dispatch, receive
-    and combine of one round overlap the expert GEMMs of another, as a serving
-    engine keeps two batches in flight; :meth:`wait` orders a round's output
+    and combine of one round overlap the expert GEMMs of another (the rounds'
+    GEMMs themselves run in submission order), as a serving engine keeps two
+    batches in flight; :meth:`wait` orders a round's output
     before later work on the current stream.  ``forward`` stays synchronous
     with the current stream whatever ``in_flight`` is.  Every kernel that
     waits on other GPUs is a 32-thread kernel of its own, so two rounds'
@@ -203,6 +204,7 @@ class ExpertParallelMoE(_DebugTimingMixin):
                                      torch.empty(self.max_tokens, cfg.hidden, dtype=torch.bfloat16, device=dev),
                                      torch.cuda.Stream(device=dev) if self.in_flight > 1 else None))
         self._next = 0
+        self._gemms_done = None
         s0 = self._slots[0]
         self.heap, self._layer = s0.heap, s0.native
         self._idx, self._w, self._out = s0.idx, s0.w, s0.out
@@ -248,7 +250,18 @@ class ExpertParallelMoE(_DebugTimingMixin):
         with torch.cuda.stream(s), _nvtx_range("kiwi.ep.submit"):
             idx, w = slot.idx[:t], slot.w[:t]
             slot.native.route(logits, idx, w)
-            slot.native.forward(x, idx, w, out)
+            slot.native.dispatch(x, idx, w)
+            slot.native.receive()
+            # The rounds' expert GEMMs run one after another: two GEMMs sharing
+            # the SMs would split L2 between two experts' weights.  Only the
+            # communication and the copies of one round overlap another's GEMMs.
+            if self._gemms_done is not None and s is not cur:
+                s.wait_event(self._gemms_done)
+            slot.native.experts()
+            if self.in_flight > 1:
+                self._gemms_done = torch.cuda.Event()
+                self._gemms_done.record(s)
+            slot.native.combine(idx, out)
             ev = torch.cuda.Event()
             ev.record(s)
         if s is not cur:

@@ -66,8 +66,14 @@ EpTuning tune(const EpConfig& c, int sms, const char* env) {
     // Gathering GEMM1: 2605 us vs 1483 us TMA-fed (+105 us receive copy) at
     // one EP8 rank's shape.
     t.gather_a = false;
-    // 2-SM tiles: within +-6 % of the 1-SM kernel at the EP shapes.
+    // 2-SM tiles (cta_group::2, 256 x 256): a third less L2 -> shared-memory
+    // traffic per MMA; at one EP8 rank's GEMM1 shape 82 % tensor-pipe activity
+    // vs 72 % and 12 % fewer SM cycles (ncu), but at N = 1 (128 rows per expert)
+    // half of each tile is padding and the layer is 12 % slower.  So rounds pick
+    // the 2-SM kernels when the expected rows per local expert reach
+    // kPairMinRows.
     t.gemm_pair = false;
+    t.gemm_pair_auto = true;
     t.source = e->source;
     const char* ov = env ? env : std::getenv("KIWI_EP_TUNING");
     if (ov && *ov) {
@@ -85,6 +91,7 @@ EpTuning tune(const EpConfig& c, int sms, const char* env) {
                 else if (k == "fused_combine") t.fused_combine = parse_bool(v);
                 else if (k == "gather_a") t.gather_a = parse_bool(v);
                 else if (k == "gemm_pair") t.gemm_pair = parse_bool(v);
+                else if (k == "gemm_pair_auto") t.gemm_pair_auto = parse_bool(v);
                 else throw kiwi::error("KIWI_EP_TUNING: unknown key '" + k + "'");
             } catch (const std::invalid_argument&) {
                 throw kiwi::error("KIWI_EP_TUNING: bad number in '" + item + "'");

@@ -4,6 +4,7 @@ import pytest
 import torch
 
 import kiwi_b200
+from kiwi_b200 import ops
 from kiwi_b200.models import moe
 from kiwi_b200.parallel.ep import EpDispatchCombine, ExpertParallelMoE
 
@@ -224,6 +225,33 @@ def test_kiwi_ep_op_token_sweep():
         op.reset()
 
 
+@pytest.mark.parametrize("fused", [True, False])
+def test_layer_with_2sm_gemm(fused):
+    """The 2-SM (256-row tile) GEMM1, with the 1-SM scatter GEMM2 of the fused
+    combine or the 2-SM GEMM2 of the unfused one: each GEMM's tile schedule
+    uses its own kernel's tile height."""
+    cfg = small_cfg("fp8", tokens=300, experts=8)
+    layer = ExpertParallelMoE(cfg)
+    layer.native.gemm_pair = True
+    layer.native.fused_combine = fused
+    x, logits = moe.synthetic_inputs(cfg, 0, "cuda")
+    _check(layer, cfg, x, logits, layer(x, logits).clone())
+
+
+def test_2sm_gemms_chosen_when_experts_get_enough_rows():
+    """Rounds whose expected rows per local expert reach 512 use the 2-SM GEMMs
+    (both; GEMM2 with the NVLink scatter epilogue), smaller rounds the 1-SM
+    ones, on one layer; both match the reference."""
+    cfg = small_cfg("fp8", tokens=1024, experts=8)
+    layer = ExpertParallelMoE(cfg)
+    assert layer.native.gemm_pair_auto and not layer.native.gemm_pair
+    for t, pair in ((1024, True), (200, False)):
+        x, logits = moe.synthetic_inputs(cfg, 0, "cuda", tokens=t)
+        out = layer(x, logits).clone()
+        assert layer.native.gemm_pair_in_use == pair
+        _check(layer, cfg, x, logits, out)
+
+
 @pytest.mark.parametrize("quant", ["fp8", "nvfp4"])
 def test_rounds_in_flight_match_reference(quant):
     """Two rounds in flight: five rounds with different inputs submitted back
@@ -335,7 +363,7 @@ def test_kiwi_ep_op_pre_quantised_fp4_dispatch_and_own_quantisation():
     rows, _, sc, _, cnt = op.dispatch(x, w, None, idx)
     torch.cuda.synchronize()
     op.check()
-    ref_codes, ref_sc = kiwi_b200.ops.quant_nvfp4(x)
+    ref_codes, ref_sc = ops.quant_nvfp4(x)
     assert torch.equal(rows[:n].view(torch.uint8), ref_codes)
     assert torch.equal(sc[:n, :ref_sc.shape[1]], ref_sc)
     with pytest.raises(ValueError):

@@ -87,6 +87,9 @@ def test_gemm_kernels_use_no_local_memory():
         assert local == 0, (sw, local)
         local, regs, smem = C.ops.gemm_pair_kernel_info(sw)
         assert local == 0, (sw, local)
+    for pair in (False, True):
+        local, regs, smem = C.ops.gemm_scatter_kernel_info(pair)
+        assert local == 0 and smem <= 227 * 1024, (pair, local, smem)
 
 
 @pytest.mark.parametrize("pair", [False, True])
