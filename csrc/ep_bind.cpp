@@ -714,7 +714,7 @@ void register_ep(py::module_& m) {
         .def_property_readonly("expert_output", &MoeLayer::expert_output)
         .def_property_readonly("epoch", &MoeLayer::epoch)
         .def_property("gemm_pair_auto", &MoeLayer::pair_auto, &MoeLayer::set_pair_auto,
-                      "Use the 2-SM GEMMs in rounds whose expected rows per local expert reach 512 (default on).")
+                      "Use the 2-SM GEMMs in rounds whose expected rows per local expert reach 2048 (default on).")
         .def_property_readonly("gemm_pair_in_use", &MoeLayer::pair_in_use,
                                "Whether the last dispatched round uses the 2-SM GEMMs.")
         .def_property("gemm_pair", &MoeLayer::pair, &MoeLayer::set_pair,

@@ -28,9 +28,13 @@ struct EpTuning {
     std::string source;       // table entry (and overrides) this came from
 };
 
-/// Expected rows per local expert from which a round uses the 2-SM GEMMs
-/// (with fewer, half of a 256-row tile is padding more often than not).
-inline constexpr int kPairMinRows = 512;
+/// Expected rows per local expert from which a round uses the 2-SM GEMMs.
+/// The last tile of every expert is part padding (on average half a tile: 128
+/// rows with 256-row tiles, 64 with 128-row ones), which has to be small
+/// against the 2-SM kernel's gain: measured at 8 B200s, 1024 rows per expert
+/// (the FP8 headline config) ran 6.6 % slower with the 2-SM GEMMs and 6144
+/// rows (the NVFP4 config) 4 % faster.
+inline constexpr int kPairMinRows = 2048;
 
 /// Tuning for configuration `c` on a GPU with `sms` SMs, then the
 /// KIWI_EP_TUNING overrides (`env` stands in for the variable in tests;

@@ -239,13 +239,13 @@ def test_layer_with_2sm_gemm(fused):
 
 
 def test_2sm_gemms_chosen_when_experts_get_enough_rows():
-    """Rounds whose expected rows per local expert reach 512 use the 2-SM GEMMs
+    """Rounds whose expected rows per local expert reach 2048 use the 2-SM GEMMs
     (both; GEMM2 with the NVLink scatter epilogue), smaller rounds the 1-SM
     ones, on one layer; both match the reference."""
-    cfg = small_cfg("fp8", tokens=1024, experts=8)
+    cfg = small_cfg("fp8", tokens=4096, experts=8)
     layer = ExpertParallelMoE(cfg)
     assert layer.native.gemm_pair_auto and not layer.native.gemm_pair
-    for t, pair in ((1024, True), (200, False)):
+    for t, pair in ((4096, True), (1000, False)):
         x, logits = moe.synthetic_inputs(cfg, 0, "cuda", tokens=t)
         out = layer(x, logits).clone()
         assert layer.native.gemm_pair_in_use == pair
