@@ -101,6 +101,7 @@ py::dict tuning_dict(const ep::EpTuning& t) {
     d["gather_a"] = t.gather_a;
     d["gemm_pair"] = t.gemm_pair;
     d["gemm_pair_auto"] = t.gemm_pair_auto;
+    d["gemm_split"] = t.gemm_split;
     d["source"] = t.source;
     return d;
 }
@@ -195,6 +196,8 @@ public:
         offsets_ = torch::zeros({el + 1}, i32);
         tiles1_ = torch::zeros({el + 1}, i32);
         tiles2_ = torch::zeros({el + 1}, i32);
+        pair_end_ = torch::zeros({el}, i32);
+        split_tiles_ = torch::zeros({4 * (el + 1)}, i32);
         slot_tokens_ = torch::zeros({ep::kMaxTopk}, i32);
         pair_slot_ = torch::zeros({pairs}, i32);
         pair_dst_ = torch::full({pairs}, -1, torch::TensorOptions().dtype(torch::kInt64).device(dev));
@@ -230,6 +233,7 @@ public:
         tuning_ = ep::tune(cfg_, gemm::num_sms());
         pair_ = tuning_.gemm_pair;
         pair_auto_ = tuning_.gemm_pair_auto;
+        split_ = tuning_.gemm_split;
         fused_ = tuning_.fused_combine;
         gather_ = tuning_.gather_a;
     }
@@ -253,7 +257,8 @@ public:
         tokens_ = static_cast<int>(x.size(0));
         // Rows each local expert expects this round, if every rank sends as many tokens.
         const int64_t rows = static_cast<int64_t>(cfg_.world) * tokens_ * cfg_.topk / cfg_.num_experts;
-        use_pair_ = pair_ || (pair_auto_ && rows >= ep::kPairMinRows);
+        use_pair_ = pair_ || (!split_ && pair_auto_ && rows >= ep::kPairMinRows);
+        use_split_ = !use_pair_ && split_ && !gathers();
         ep::launch_begin(cfg_, ws_, s);
         ep::launch_dispatch(cfg_, heap_.view(), reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()),
                             idx.data_ptr<int32_t>(), w.data_ptr<float>(), static_cast<int>(x.size(0)), ws_,
@@ -267,13 +272,21 @@ public:
         // streams at once).
         ep::launch_wait_flags(cfg_, heap_.view(), ws_, 0, timeout_ns_, s);
         ep::launch_recv_count(cfg_, heap_.view(), ws_, timeout_ns_, s, /*waited=*/true);
-        // Rows per tile of each GEMM's kernel: the 2-SM kernel takes 256-row tiles;
-        // the gathering GEMM1 and the scatter GEMM2 (fused combine) are 1-SM kernels.
-        const int bm1 = use_pair_ && !gathers() ? 256 : 128;
-        const int bm2 = use_pair_ ? 256 : 128;
-        gemm::build_schedule(ws_.expert_count, cfg_.experts_per_rank, static_cast<int>(2 * ffn_), 256, ws_.offsets,
-                             ws_.tiles1, s, bm1);
-        gemm::build_schedule(ws_.expert_count, cfg_.experts_per_rank, cfg_.hidden, 256, ws_.offsets, ws_.tiles2, s, bm2);
+        if (use_split_) {
+            // Both GEMMs as a 2-SM pass over every expert's full 256-row tiles
+            // plus a 1-SM pass over its tail (fewer than 256 rows).
+            gemm::build_split_schedule(ws_.expert_count, cfg_.experts_per_rank, static_cast<int>(2 * ffn_),
+                                       cfg_.hidden, split_schedule(), s);
+        } else {
+            // Rows per tile of each GEMM's kernel: the 2-SM kernel takes 256-row
+            // tiles; the gathering GEMM1 is a 1-SM kernel.
+            const int bm1 = use_pair_ && !gathers() ? 256 : 128;
+            const int bm2 = use_pair_ ? 256 : 128;
+            gemm::build_schedule(ws_.expert_count, cfg_.experts_per_rank, static_cast<int>(2 * ffn_), 256,
+                                 ws_.offsets, ws_.tiles1, s, bm1);
+            gemm::build_schedule(ws_.expert_count, cfg_.experts_per_rank, cfg_.hidden, 256, ws_.offsets, ws_.tiles2, s,
+                                 bm2);
+        }
         ep::launch_recv_assign(cfg_, heap_.view(), ws_, s, tuning_.recv_blocks);
         if (!gathers()) ep::launch_recv_copy(cfg_, heap_.view(), ws_, s, tuning_.recv_blocks);
     }
@@ -281,6 +294,34 @@ public:
     /// GEMM1 reads its A rows in place from the receive buffer (FP8 / NVFP4
     /// dispatch), so the expert-major bf16 copy is skipped.
     bool gathers() const { return gather_ && cfg_.quant != static_cast<int>(ep::Quant::kNone); }
+
+    gemm::SplitSchedule split_schedule() {
+        gemm::SplitSchedule ss{};
+        ss.offsets = ws_.offsets;
+        ss.pair_end = pair_end_.data_ptr<int32_t>();
+        ss.pair_tiles1 = split_tiles_.data_ptr<int32_t>();
+        ss.tail_tiles1 = ss.pair_tiles1 + (cfg_.experts_per_rank + 1);
+        ss.pair_tiles2 = ss.tail_tiles1 + (cfg_.experts_per_rank + 1);
+        ss.tail_tiles2 = ss.pair_tiles2 + (cfg_.experts_per_rank + 1);
+        return ss;
+    }
+
+    /// Runs one GEMM of a split round: the 2-SM pass over full 256-row tiles,
+    /// then the 1-SM pass over the tails (rows [pair_end[g], offsets[g + 1])).
+    /// `pair(args)` / `tail(args)` launch each pass's kernel.
+    template <typename Pair, typename Tail>
+    void run_split(const gemm::GroupedArgs& base, const int32_t* pair_tiles, const int32_t* tail_tiles, Pair&& pair,
+                   Tail&& tail) {
+        gemm::GroupedArgs a = base;
+        a.tile_prefix = pair_tiles;
+        a.group_end = pair_end_.data_ptr<int32_t>();
+        pair(a);
+        gemm::GroupedArgs b = base;
+        b.tile_prefix = tail_tiles;
+        b.group_offset = pair_end_.data_ptr<int32_t>();
+        b.group_end = ws_.offsets + 1;
+        tail(b);
+    }
 
     void experts() {
         experts_gemm(1);
@@ -315,6 +356,12 @@ public:
                 ga.scale_bytes = cfg_.scale_bytes;
                 ga.quant = cfg_.quant;
                 gemm::grouped_gemm_gather(tmap_b1_, g1, ga, 0, s);
+            } else if (use_split_) {
+                const gemm::SplitSchedule ss = split_schedule();
+                run_split(
+                    g1, ss.pair_tiles1, ss.tail_tiles1,
+                    [&](const gemm::GroupedArgs& a) { gemm::grouped_gemm_pair(tmap_a1_, tmap_b1h_, a, true, 0, s); },
+                    [&](const gemm::GroupedArgs& a) { gemm::grouped_gemm(tmap_a1_, tmap_b1_, a, true, 0, s); });
             } else if (use_pair_) {
                 gemm::grouped_gemm_pair(tmap_a1_, tmap_b1h_, g1, /*swiglu=*/true, 0, s);
             } else {
@@ -340,8 +387,27 @@ public:
             sc.epoch = ws_.epoch;
             sc.flag_off = cfg_.combine_flag(cfg_.rank);
             sc.world = cfg_.world;
-            if (use_pair_) gemm::grouped_gemm_pair_scatter(tmap_a2_, tmap_b2h_, g2, sc, 0, s);
-            else gemm::grouped_gemm_scatter(tmap_a2_, tmap_b2_, g2, sc, 0, s);
+            if (use_split_) {
+                // The 2-SM pass publishes nothing; the tail pass, ordered after it on
+                // this stream, signals the round once both passes' rows are out.
+                const gemm::SplitSchedule ss = split_schedule();
+                gemm::ScatterArgs first = sc;
+                first.skip_signal = 1;
+                run_split(
+                    g2, ss.pair_tiles2, ss.tail_tiles2,
+                    [&](const gemm::GroupedArgs& a) { gemm::grouped_gemm_pair_scatter(tmap_a2_, tmap_b2h_, a, first, 0, s); },
+                    [&](const gemm::GroupedArgs& a) { gemm::grouped_gemm_scatter(tmap_a2_, tmap_b2_, a, sc, 0, s); });
+            } else if (use_pair_) {
+                gemm::grouped_gemm_pair_scatter(tmap_a2_, tmap_b2h_, g2, sc, 0, s);
+            } else {
+                gemm::grouped_gemm_scatter(tmap_a2_, tmap_b2_, g2, sc, 0, s);
+            }
+        } else if (use_split_) {
+            const gemm::SplitSchedule ss = split_schedule();
+            run_split(
+                g2, ss.pair_tiles2, ss.tail_tiles2,
+                [&](const gemm::GroupedArgs& a) { gemm::grouped_gemm_pair(tmap_a2_, tmap_b2h_, a, false, 0, s); },
+                [&](const gemm::GroupedArgs& a) { gemm::grouped_gemm(tmap_a2_, tmap_b2_, a, false, 0, s); });
         } else if (use_pair_) {
             gemm::grouped_gemm_pair(tmap_a2_, tmap_b2h_, g2, /*swiglu=*/false, 0, s);
         } else {
@@ -411,7 +477,7 @@ public:
         m[ep::kMetaQuant] = cfg_.quant;
         m[ep::kMetaFusedCombine] = fused_;
         m[ep::kMetaGatherA] = gathers();
-        m[ep::kMetaGemmPair] = use_pair_;
+        m[ep::kMetaGemmPair] = use_pair_ ? 1 : (use_split_ ? 2 : 0);
         return debug_.snapshot(m);
     }
 
@@ -450,9 +516,12 @@ private:
         slot_pos_, a_, h_, y_, error_, gemm_error_, pair_dst_;
     ep::EpWorkspace ws_{};
     CUtensorMap tmap_a1_, tmap_b1_, tmap_a2_, tmap_b2_, tmap_b1h_, tmap_b2h_;
-    bool pair_ = false;       // 2-SM GEMMs in every round
+    bool pair_ = false;       // 2-SM GEMMs (256-row tiles only) in every round
+    bool split_ = false;      // 2-SM pass over full 256-row tiles + 1-SM pass over the tails, every round
     bool pair_auto_ = true;   // 2-SM GEMMs when a round expects kPairMinRows rows per local expert
-    bool use_pair_ = false;   // this round's choice (set by dispatch)
+    bool use_pair_ = false;   // this round's choices (set by dispatch)
+    bool use_split_ = false;
+    torch::Tensor pair_end_, split_tiles_;
     bool fused_ = true;
     bool gather_ = false;
     ep::EpTuning tuning_{};
@@ -468,6 +537,9 @@ public:
     bool pair_auto() const { return pair_auto_; }
     void set_pair_auto(bool v) { pair_auto_ = v; }
     bool pair_in_use() const { return use_pair_; }
+    bool split_in_use() const { return use_split_; }
+    bool split() const { return split_; }
+    void set_split(bool v) { split_ = v; }
     bool fused() const { return fused_; }
     py::dict tuning() const { return tuning_dict(tuning_); }
     void set_fused(bool v) { fused_ = v; }
@@ -714,9 +786,14 @@ void register_ep(py::module_& m) {
         .def_property_readonly("expert_output", &MoeLayer::expert_output)
         .def_property_readonly("epoch", &MoeLayer::epoch)
         .def_property("gemm_pair_auto", &MoeLayer::pair_auto, &MoeLayer::set_pair_auto,
-                      "Use the 2-SM GEMMs in rounds whose expected rows per local expert reach 2048 (default on).")
+                      "Run the 2-SM GEMMs in rounds whose expected rows per local expert reach 4096 (default on).")
+        .def_property("gemm_split", &MoeLayer::split, &MoeLayer::set_split,
+                      "Split both GEMMs into a 2-SM pass over every expert's full 256-row tiles and a 1-SM pass "
+                      "over its tail (opt-in: measured slower under the power cap).")
         .def_property_readonly("gemm_pair_in_use", &MoeLayer::pair_in_use,
-                               "Whether the last dispatched round uses the 2-SM GEMMs.")
+                               "Whether the last dispatched round runs the 2-SM GEMMs alone (gemm_pair).")
+        .def_property_readonly("gemm_split_in_use", &MoeLayer::split_in_use,
+                               "Whether the last dispatched round runs the split (2-SM + 1-SM tail) GEMMs.")
         .def_property("gemm_pair", &MoeLayer::pair, &MoeLayer::set_pair,
                       "Use the 2-SM (256-row tile) grouped GEMMs in every round (off by default; gemm_pair_auto "
                       "picks them per round).")

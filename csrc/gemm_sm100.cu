@@ -96,6 +96,11 @@ __device__ __forceinline__ void locate_tile(const int32_t* tile_prefix, int num_
     m_tile = local - n_tile * m_tiles;
 }
 
+/// One past the last row of group g (group_end, when given, bounds one pass of a split GEMM).
+__device__ __forceinline__ int group_end_row(const GroupedArgs& p, int g) {
+    return p.group_end ? __ldg(&p.group_end[g]) : __ldg(&p.group_offset[g + 1]);
+}
+
 __device__ __forceinline__ float silu(float x) { return x / (1.0f + __expf(-x)); }
 
 __device__ __forceinline__ void store_row32(__nv_bfloat16* dst, const float (&v)[32]) {
@@ -168,9 +173,12 @@ __device__ __forceinline__ void scatter_tile(uint32_t taddr, uint8_t* stg, int64
 
 /// Completion of a scatter GEMM: every CTA that did not abort releases its
 /// stores at system scope and counts itself; the last one publishes
-/// (epoch << 32) | 1 to every rank's flag.  Thread 0 only.
+/// (epoch << 32) | 1 to every rank's flag.  With skip_signal (the first pass of
+/// a split GEMM, ordered before the second on its stream) the CTA only fences.
+/// Thread 0 only.
 __device__ __forceinline__ void scatter_done(const ScatterArgs& sc, uint8_t* const* s_base) {
     asm volatile("fence.sc.sys;" ::: "memory");
+    if (sc.skip_signal) return;  // a later pass of the same GEMM publishes the round
     const uint32_t prev = atomicAdd(sc.done_ctas, 1u);
     if (prev == gridDim.x - 1) {
         asm volatile("fence.sc.sys;" ::: "memory");
@@ -351,7 +359,7 @@ __global__ void __launch_bounds__(GQ >= 0 ? kGatherThreads : kThreads, 1)
                 locate_tile(p.tile_prefix, p.num_groups, n_tiles, tile, g, mt, nt);
                 const int g_off = __ldg(&p.group_offset[g]);
                 const int rr = mt * kBM + r;
-                if (rr >= __ldg(&p.group_offset[g + 1]) - g_off || g_off + rr >= p.max_rows) return -1;
+                if (rr >= group_end_row(p, g) - g_off || g_off + rr >= p.max_rows) return -1;
                 return __ldg(&ga.row_slot[g_off + rr]);
             };
             int i_tile = blockIdx.x, i_kb = 0;
@@ -465,7 +473,7 @@ __global__ void __launch_bounds__(GQ >= 0 ? kGatherThreads : kThreads, 1)
             }
             sm100::tc_fence_after();
             const int g_off = __ldg(&p.group_offset[g]);
-            const int g_rows = __ldg(&p.group_offset[g + 1]) - g_off;
+            const int g_rows = group_end_row(p, g) - g_off;
             const int r = mt * kBM + row_in_tile;
             const int64_t out_row = static_cast<int64_t>(g_off) + r;
             const bool valid = r < g_rows && out_row < p.max_rows;
@@ -709,7 +717,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             }
             sm100::tc_fence_after();
             const int g_off = __ldg(&p.group_offset[g]);
-            const int g_rows = __ldg(&p.group_offset[g + 1]) - g_off;
+            const int g_rows = group_end_row(p, g) - g_off;
             const int r = mt * kPairBM + row_in_tile;
             const int64_t out_row = static_cast<int64_t>(g_off) + r;
             const bool valid = r < g_rows && out_row < p.max_rows;
@@ -800,6 +808,52 @@ __global__ void build_schedule_kernel(const int32_t* counts, int num_groups, int
     }
 }
 
+/// One block of a power-of-two thread count >= num_groups: per group, full
+/// 256-row tiles for the 2-SM pass and 128-row tail tiles for the 1-SM pass,
+/// prefix-summed for one or two GEMMs.
+__global__ void build_split_schedule_kernel(const int32_t* counts, int num_groups, int n_tiles1, int n_tiles2,
+                                            SplitSchedule out) {
+    __shared__ int32_t s_rows[1024];
+    __shared__ int32_t s_pair[1024];
+    __shared__ int32_t s_tail[1024];
+    const int t = threadIdx.x;
+    const int rows = t < num_groups ? counts[t] : 0;
+    const int full = rows / 256;
+    s_rows[t] = rows;
+    s_pair[t] = full;
+    s_tail[t] = (rows - 256 * full + 127) / 128;
+    __syncthreads();
+    for (int d = 1; d < blockDim.x; d <<= 1) {
+        const int a = t >= d ? s_rows[t - d] : 0;
+        const int b = t >= d ? s_pair[t - d] : 0;
+        const int c = t >= d ? s_tail[t - d] : 0;
+        __syncthreads();
+        s_rows[t] += a;
+        s_pair[t] += b;
+        s_tail[t] += c;
+        __syncthreads();
+    }
+    if (t < num_groups) {
+        out.offsets[t + 1] = s_rows[t];
+        out.pair_end[t] = s_rows[t] - rows + 256 * full;
+        out.pair_tiles1[t + 1] = s_pair[t] * n_tiles1;
+        out.tail_tiles1[t + 1] = s_tail[t] * n_tiles1;
+        if (out.pair_tiles2) {
+            out.pair_tiles2[t + 1] = s_pair[t] * n_tiles2;
+            out.tail_tiles2[t + 1] = s_tail[t] * n_tiles2;
+        }
+    }
+    if (t == 0) {
+        out.offsets[0] = 0;
+        out.pair_tiles1[0] = 0;
+        out.tail_tiles1[0] = 0;
+        if (out.pair_tiles2) {
+            out.pair_tiles2[0] = 0;
+            out.tail_tiles2[0] = 0;
+        }
+    }
+}
+
 }  // namespace
 
 CUtensorMap make_tmap_bf16_2d(const void* ptr, uint64_t rows, uint64_t cols, uint32_t box_rows, uint32_t box_k) {
@@ -835,6 +889,22 @@ void build_schedule(const int32_t* counts, int num_groups, int n, int bn, int32_
     int threads = 32;
     while (threads < num_groups) threads <<= 1;
     build_schedule_kernel<<<1, threads, 0, stream>>>(counts, num_groups, n / bn, bm, offsets, tile_prefix);
+    KIWI_CUDA_CHECK(cudaGetLastError());
+}
+
+void build_split_schedule(const int32_t* counts, int num_groups, int n1, int n2, const SplitSchedule& out,
+                          cudaStream_t stream) {
+    if (num_groups < 1 || num_groups > 1024) throw kiwi::error("build_split_schedule: 1..1024 groups");
+    if (n1 <= 0 || n1 % 256 || (out.pair_tiles2 && (n2 <= 0 || n2 % 256))) {
+        throw kiwi::error("build_split_schedule: N must be a positive multiple of 256");
+    }
+    if (!out.offsets || !out.pair_end || !out.pair_tiles1 || !out.tail_tiles1 ||
+        (out.pair_tiles2 == nullptr) != (out.tail_tiles2 == nullptr)) {
+        throw kiwi::error("build_split_schedule: missing output arrays");
+    }
+    int threads = 32;
+    while (threads < num_groups) threads <<= 1;
+    build_split_schedule_kernel<<<1, threads, 0, stream>>>(counts, num_groups, n1 / 256, n2 > 0 ? n2 / 256 : 0, out);
     KIWI_CUDA_CHECK(cudaGetLastError());
 }
 

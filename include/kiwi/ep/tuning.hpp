@@ -8,7 +8,7 @@
 // fused paths the layer uses, keyed by the rank's token capacity, and records
 // where each choice was measured.  KIWI_EP_TUNING="key=value,..." overrides
 // any field (keys: dispatch_blocks, recv_blocks, combine_blocks,
-// fused_combine, gather_a, gemm_pair, gemm_pair_auto).
+// fused_combine, gather_a, gemm_pair, gemm_pair_auto, gemm_split).
 #pragma once
 
 #include <string>
@@ -23,18 +23,20 @@ struct EpTuning {
     int32_t combine_blocks;   // combine send / reduce grid
     bool fused_combine;       // GEMM2 epilogue stores over NVLink
     bool gather_a;            // GEMM1 gathers A from the receive slots
-    bool gemm_pair;           // 2-SM (256-row tile) grouped GEMMs in every round
-    bool gemm_pair_auto;      // 2-SM GEMMs in rounds whose expected rows per local expert reach kPairMinRows
+    bool gemm_pair;           // 2-SM (256-row tile) grouped GEMMs alone in every round
+    bool gemm_pair_auto;      // 2-SM GEMMs in rounds expecting kPairMinRows rows per local expert
+    bool gemm_split;          // 2-SM pass over full 256-row tiles + 1-SM pass over the tails, every round
     std::string source;       // table entry (and overrides) this came from
 };
 
-/// Expected rows per local expert from which a round uses the 2-SM GEMMs.
-/// The last tile of every expert is part padding (on average half a tile: 128
-/// rows with 256-row tiles, 64 with 128-row ones), which has to be small
-/// against the 2-SM kernel's gain: measured at 8 B200s, 1024 rows per expert
-/// (the FP8 headline config) ran 6.6 % slower with the 2-SM GEMMs and 6144
-/// rows (the NVFP4 config) 4 % faster.
-inline constexpr int kPairMinRows = 2048;
+/// Expected rows per local expert from which a round runs the 2-SM GEMMs
+/// (256-row tiles).  Under the B200's power cap the 2-SM kernels lost where an
+/// expert's last, part-padding tile is a noticeable share of its rows: at 8
+/// GPUs 3.09 vs 2.90 ms per step with 1024 rows per expert, and on one GPU with
+/// 1024 rows per expert the split variant (2-SM over full tiles, 1-SM over the
+/// tails) took 27.0 vs 22.5 ms at a median clock of 1102 vs 1387 MHz; with 6144
+/// rows per expert (the NVFP4 config at 8 GPUs) they won, 3.22 vs 3.36 ms.
+inline constexpr int kPairMinRows = 4096;
 
 /// Tuning for configuration `c` on a GPU with `sms` SMs, then the
 /// KIWI_EP_TUNING overrides (`env` stands in for the variable in tests;

@@ -33,6 +33,10 @@ struct GroupedArgs {
     // span[1] = last CTA end, %globaltimer ns, both updated with atomicMax
     // (the layout of one phase of kiwi::ep's debug timing buffer).
     uint64_t* span;
+    // Optional [G] device: group g's rows end at group_end[g] instead of
+    // group_offset[g + 1] (one pass of a GEMM split into full 256-row tiles and
+    // tails; group_offset then only needs G entries).
+    const int32_t* group_end;
 };
 
 inline constexpr int kTraceSlots = 4;
@@ -54,7 +58,7 @@ struct ScatterArgs {
     const uint32_t* epoch;
     uint64_t flag_off;
     int32_t world;
-    int32_t pad_;
+    int32_t skip_signal;  // 1: fence this launch's stores and publish nothing (a split GEMM's first pass)
 };
 
 /// Gathering A producer (fused EP receive -> GEMM1): expert-major row i of A is
@@ -91,6 +95,23 @@ CUtensorMap make_tmap_bf16_2d(const void* ptr, uint64_t rows, uint64_t cols, uin
 /// `bm` = rows per tile: 128 for grouped_gemm, 256 for grouped_gemm_pair.
 void build_schedule(const int32_t* counts, int num_groups, int n, int bn, int32_t* offsets, int32_t* tile_prefix,
                     cudaStream_t stream, int bm = 128);
+
+/// Device arrays of a grouped GEMM split into a 2-SM pass over every group's
+/// full 256-row tiles and a 1-SM pass over the remaining rows (< 256 per
+/// group), for up to two GEMMs over the same row counts (different N).
+struct SplitSchedule {
+    int32_t* offsets;      // [G + 1] first row of each group
+    int32_t* pair_end;     // [G] end of each group's full 256-row tiles (= start of its tail)
+    int32_t* pair_tiles1;  // [G + 1] cumulative 256-row x 256-column tiles of GEMM 1
+    int32_t* tail_tiles1;  // [G + 1] cumulative 128-row x 256-column tail tiles of GEMM 1
+    int32_t* pair_tiles2;  // same for GEMM 2 (null: one GEMM)
+    int32_t* tail_tiles2;
+};
+
+/// Fills a SplitSchedule from per-group row counts on the device (one block,
+/// at most 1024 groups); n1 / n2: each GEMM's N (multiples of 256).
+void build_split_schedule(const int32_t* counts, int num_groups, int n1, int n2, const SplitSchedule& out,
+                          cudaStream_t stream);
 
 /// Launches the persistent grouped GEMM (BN = 256).  `grid` <= 0: one CTA per SM.
 void grouped_gemm(const CUtensorMap& tmap_a, const CUtensorMap& tmap_b, const GroupedArgs& args, bool swiglu,

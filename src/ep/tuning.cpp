@@ -68,13 +68,13 @@ EpTuning tune(const EpConfig& c, int sms, const char* env) {
     t.gather_a = false;
     // 2-SM tiles (cta_group::2, 256 x 256): a third less L2 -> shared-memory
     // traffic per MMA; at one EP8 rank's GEMM1 shape 82 % tensor-pipe activity
-    // vs 72 % and 12 % fewer SM cycles (ncu), but at N = 1 (128 rows per expert)
-    // half of each tile is padding and the layer is 12 % slower.  So rounds pick
-    // the 2-SM kernels when the expected rows per local expert reach
-    // kPairMinRows (at 8 GPUs: 3.09 vs 2.90 ms per step with 1024 rows per
-    // expert, 3.22 vs 3.36 ms with 6144).
+    // vs 72 % and 12 % fewer SM cycles (ncu).  Under the power cap that turned
+    // into a lower clock rather than a shorter step unless experts get many
+    // rows (see kPairMinRows), so the 2-SM kernels run only from kPairMinRows
+    // rows per local expert and the split variant is opt-in.
     t.gemm_pair = false;
     t.gemm_pair_auto = true;
+    t.gemm_split = false;
     t.source = e->source;
     const char* ov = env ? env : std::getenv("KIWI_EP_TUNING");
     if (ov && *ov) {
@@ -93,6 +93,7 @@ EpTuning tune(const EpConfig& c, int sms, const char* env) {
                 else if (k == "gather_a") t.gather_a = parse_bool(v);
                 else if (k == "gemm_pair") t.gemm_pair = parse_bool(v);
                 else if (k == "gemm_pair_auto") t.gemm_pair_auto = parse_bool(v);
+                else if (k == "gemm_split") t.gemm_split = parse_bool(v);
                 else throw kiwi::error("KIWI_EP_TUNING: unknown key '" + k + "'");
             } catch (const std::invalid_argument&) {
                 throw kiwi::error("KIWI_EP_TUNING: bad number in '" + item + "'");

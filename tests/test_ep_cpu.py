@@ -131,7 +131,7 @@ def test_tuning_table_and_overrides():
     ep = load().ep
     cfg = dict(world=8, rank=0, hidden=7168, num_experts=256, topk=8, max_tokens=4096, quant="fp8")
     t = ep.tune(cfg, 148, "")
-    assert t["fused_combine"] and not t["gather_a"] and not t["gemm_pair"] and t["gemm_pair_auto"]
+    assert t["fused_combine"] and not t["gather_a"] and not t["gemm_pair"] and t["gemm_pair_auto"] and not t["gemm_split"]
     assert t["recv_blocks"] == 8 * 148 and t["combine_blocks"] == 8 * 148 and t["dispatch_blocks"] == 0
     assert "throughput" in t["source"]
     lat = ep.tune({**cfg, "max_tokens": 128}, 148, "")

@@ -238,18 +238,39 @@ def test_layer_with_2sm_gemm(fused):
     _check(layer, cfg, x, logits, layer(x, logits).clone())
 
 
-def test_2sm_gemms_chosen_when_experts_get_enough_rows():
-    """Rounds whose expected rows per local expert reach 2048 use the 2-SM GEMMs
-    (both; GEMM2 with the NVLink scatter epilogue), smaller rounds the 1-SM
-    ones, on one layer; both match the reference."""
-    cfg = small_cfg("fp8", tokens=4096, experts=8)
+@pytest.mark.parametrize("fused", [True, False])
+def test_split_gemms_match_reference(fused):
+    """gemm_split runs each GEMM as a 2-SM pass over every expert's full 256-row
+    tiles plus a 1-SM pass over its tail (GEMM2 with the NVLink scatter
+    epilogue in both passes, the second one signalling the round).  Row counts
+    are ragged (routing from random logits), so experts have tails."""
+    cfg = small_cfg("fp8", tokens=1536, experts=8)
     layer = ExpertParallelMoE(cfg)
-    assert layer.native.gemm_pair_auto and not layer.native.gemm_pair
-    for t, pair in ((4096, True), (1000, False)):
-        x, logits = moe.synthetic_inputs(cfg, 0, "cuda", tokens=t)
+    layer.native.fused_combine = fused
+    layer.native.gemm_split = True
+    for t in (1536, 200, 1024):
+        x, logits = moe.synthetic_inputs(cfg, 0, "cuda", tokens=t, step=t)
         out = layer(x, logits).clone()
-        assert layer.native.gemm_pair_in_use == pair
+        assert layer.native.gemm_split_in_use and not layer.native.gemm_pair_in_use
+        counts = layer.expert_counts.tolist()
+        assert any(c % 256 for c in counts)
         _check(layer, cfg, x, logits, out)
+
+
+def test_2sm_gemms_chosen_from_4096_rows_per_expert():
+    """With the defaults a round runs the 2-SM GEMMs when it expects at least
+    4096 rows per local expert, the 1-SM ones otherwise; both match the
+    reference."""
+    cfg = small_cfg("fp8", tokens=8192, experts=8)
+    layer = ExpertParallelMoE(cfg)
+    assert layer.native.gemm_pair_auto and not layer.native.gemm_pair and not layer.native.gemm_split
+    for t, pair in ((8192, True), (1024, False)):
+        x, logits = moe.synthetic_inputs(cfg, 0, "cuda", tokens=t, step=t)
+        out = layer(x, logits).clone()
+        assert layer.native.gemm_pair_in_use == pair and not layer.native.gemm_split_in_use
+        g = torch.Generator(device="cpu").manual_seed(t)
+        pick = torch.randperm(t, generator=g)[:64].to(x.device)
+        _check(layer, cfg, x[pick], logits[pick], out[pick])
 
 
 @pytest.mark.parametrize("quant", ["fp8", "nvfp4"])
