@@ -142,3 +142,33 @@ def test_noalloc_rejects_too_many_groups():
     rc = _call(fn, a, b, maxg + 1, 256, 64, counts, out, False, None)
     assert rc != 0
     assert b"num_groups must be in [1, 1024]" in lib.kiwi_noalloc_last_error()
+
+
+def test_noalloc_and_regular_entry_on_two_devices():
+    """One process drives two GPUs in turn (0, 1, 0, 1): the raised shared-memory
+    limit, the SM count and the no-alloc scratch array are kept per device, so
+    the 1-SM and 2-SM kernels and the no-alloc entry run on the second device
+    after the first and each result matches the fp32 reference."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs in one process")
+    lib, fn = _lib()
+    C = kiwi_b200.native()
+    k, n, counts_list = 256, 512, [100, 0, 257, 31]
+    rows, groups = sum(counts_list), len(counts_list)
+    for call, dev in enumerate((0, 1, 0, 1)):
+        with torch.cuda.device(dev):
+            torch.manual_seed(10 + call)
+            a = (torch.randn(rows, k, device="cuda") * 0.5).bfloat16()
+            b = (torch.randn(groups * n, k, device="cuda") * 0.05).bfloat16()
+            counts = torch.tensor(counts_list, dtype=torch.int32, device="cuda")
+            exact = grouped_gemm_reference(a, b, counts_list, swiglu=True)
+            tol = 2e-2 * exact.abs().max().item() + 1e-2
+            plan = C.ops.GroupedGemm(a, b, groups)
+            for pair in (False, True):
+                got = torch.zeros(rows, n // 2, device="cuda", dtype=torch.bfloat16)
+                plan.run(counts, got, True, None, 0, pair)
+                assert (got.float() - exact).abs().max().item() <= tol, f"device {dev}, pair={pair}"
+            got = torch.zeros(rows, n // 2, device="cuda", dtype=torch.bfloat16)
+            assert _call(fn, a, b, groups, n, k, counts, got, True, None) == 0, lib.kiwi_noalloc_last_error()
+            assert _error_word(lib) == 0
+            assert (got.float() - exact).abs().max().item() <= tol, f"device {dev}, no-alloc entry"
