@@ -102,6 +102,7 @@ py::dict tuning_dict(const ep::EpTuning& t) {
     d["gemm_pair"] = t.gemm_pair;
     d["gemm_pair_auto"] = t.gemm_pair_auto;
     d["gemm_split"] = t.gemm_split;
+    d["gemm2_pair"] = t.gemm2_pair;
     d["source"] = t.source;
     return d;
 }
@@ -234,6 +235,7 @@ public:
         pair_ = tuning_.gemm_pair;
         pair_auto_ = tuning_.gemm_pair_auto;
         split_ = tuning_.gemm_split;
+        pair2_ = tuning_.gemm2_pair;
         fused_ = tuning_.fused_combine;
         gather_ = tuning_.gather_a;
     }
@@ -259,6 +261,7 @@ public:
         const int64_t rows = static_cast<int64_t>(cfg_.world) * tokens_ * cfg_.topk / cfg_.num_experts;
         use_pair_ = pair_ || (!split_ && pair_auto_ && rows >= ep::kPairMinRows);
         use_split_ = !use_pair_ && split_ && !gathers();
+        use_pair2_ = use_pair_ || (pair2_ && !use_split_);
         ep::launch_begin(cfg_, ws_, s);
         ep::launch_dispatch(cfg_, heap_.view(), reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()),
                             idx.data_ptr<int32_t>(), w.data_ptr<float>(), static_cast<int>(x.size(0)), ws_,
@@ -281,7 +284,7 @@ public:
             // Rows per tile of each GEMM's kernel: the 2-SM kernel takes 256-row
             // tiles; the gathering GEMM1 is a 1-SM kernel.
             const int bm1 = use_pair_ && !gathers() ? 256 : 128;
-            const int bm2 = use_pair_ ? 256 : 128;
+            const int bm2 = use_pair2_ ? 256 : 128;
             gemm::build_schedule(ws_.expert_count, cfg_.experts_per_rank, static_cast<int>(2 * ffn_), 256,
                                  ws_.offsets, ws_.tiles1, s, bm1);
             gemm::build_schedule(ws_.expert_count, cfg_.experts_per_rank, cfg_.hidden, 256, ws_.offsets, ws_.tiles2, s,
@@ -397,7 +400,7 @@ public:
                     g2, ss.pair_tiles2, ss.tail_tiles2,
                     [&](const gemm::GroupedArgs& a) { gemm::grouped_gemm_pair_scatter(tmap_a2_, tmap_b2h_, a, first, 0, s); },
                     [&](const gemm::GroupedArgs& a) { gemm::grouped_gemm_scatter(tmap_a2_, tmap_b2_, a, sc, 0, s); });
-            } else if (use_pair_) {
+            } else if (use_pair2_) {
                 gemm::grouped_gemm_pair_scatter(tmap_a2_, tmap_b2h_, g2, sc, 0, s);
             } else {
                 gemm::grouped_gemm_scatter(tmap_a2_, tmap_b2_, g2, sc, 0, s);
@@ -408,7 +411,7 @@ public:
                 g2, ss.pair_tiles2, ss.tail_tiles2,
                 [&](const gemm::GroupedArgs& a) { gemm::grouped_gemm_pair(tmap_a2_, tmap_b2h_, a, false, 0, s); },
                 [&](const gemm::GroupedArgs& a) { gemm::grouped_gemm(tmap_a2_, tmap_b2_, a, false, 0, s); });
-        } else if (use_pair_) {
+        } else if (use_pair2_) {
             gemm::grouped_gemm_pair(tmap_a2_, tmap_b2h_, g2, /*swiglu=*/false, 0, s);
         } else {
             gemm::grouped_gemm(tmap_a2_, tmap_b2_, g2, /*swiglu=*/false, 0, s);
@@ -477,7 +480,7 @@ public:
         m[ep::kMetaQuant] = cfg_.quant;
         m[ep::kMetaFusedCombine] = fused_;
         m[ep::kMetaGatherA] = gathers();
-        m[ep::kMetaGemmPair] = use_pair_ ? 1 : (use_split_ ? 2 : 0);
+        m[ep::kMetaGemmPair] = use_pair_ ? 1 : (use_split_ ? 2 : (use_pair2_ ? 3 : 0));
         return debug_.snapshot(m);
     }
 
@@ -521,6 +524,8 @@ private:
     bool pair_auto_ = true;   // 2-SM GEMMs when a round expects kPairMinRows rows per local expert
     bool use_pair_ = false;   // this round's choices (set by dispatch)
     bool use_split_ = false;
+    bool pair2_ = false;      // GEMM2 alone on the 2-SM kernel in every round (GEMM1 stays 1-SM)
+    bool use_pair2_ = false;  // this round: GEMM2 on the 2-SM kernel (gemm_pair or gemm2_pair)
     torch::Tensor pair_end_, split_tiles_;
     bool fused_ = true;
     bool gather_ = false;
@@ -540,6 +545,9 @@ public:
     bool split_in_use() const { return use_split_; }
     bool split() const { return split_; }
     void set_split(bool v) { split_ = v; }
+    bool pair2() const { return pair2_; }
+    void set_pair2(bool v) { pair2_ = v; }
+    bool pair2_in_use() const { return use_pair2_; }
     bool fused() const { return fused_; }
     py::dict tuning() const { return tuning_dict(tuning_); }
     void set_fused(bool v) { fused_ = v; }
@@ -794,6 +802,11 @@ void register_ep(py::module_& m) {
                                "Whether the last dispatched round runs the 2-SM GEMMs alone (gemm_pair).")
         .def_property_readonly("gemm_split_in_use", &MoeLayer::split_in_use,
                                "Whether the last dispatched round runs the split (2-SM + 1-SM tail) GEMMs.")
+        .def_property("gemm2_pair", &MoeLayer::pair2, &MoeLayer::set_pair2,
+                      "Run the down projection (GEMM2, with its combine epilogue) on the 2-SM kernel and the "
+                      "gate/up GEMM on the 1-SM kernel in every round (opt-in).")
+        .def_property_readonly("gemm2_pair_in_use", &MoeLayer::pair2_in_use,
+                               "Whether the last dispatched round runs GEMM2 on the 2-SM kernel.")
         .def_property("gemm_pair", &MoeLayer::pair, &MoeLayer::set_pair,
                       "Use the 2-SM (256-row tile) grouped GEMMs in every round (off by default; gemm_pair_auto "
                       "picks them per round).")

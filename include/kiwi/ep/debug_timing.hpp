@@ -74,7 +74,7 @@ enum DebugMeta : int {
     kMetaQuant,
     kMetaFusedCombine,
     kMetaGatherA,
-    kMetaGemmPair,
+    kMetaGemmPair,  // 0: 1-SM GEMMs, 1: 2-SM both, 2: split (2-SM + 1-SM tails), 3: GEMM2 alone on 2-SM
     kNumDebugMeta
 };
 static_assert(kNumDebugMeta <= kDebugMetaWords, "meta buffer too small");

@@ -75,6 +75,7 @@ EpTuning tune(const EpConfig& c, int sms, const char* env) {
     t.gemm_pair = false;
     t.gemm_pair_auto = true;
     t.gemm_split = false;
+    t.gemm2_pair = false;
     t.source = e->source;
     const char* ov = env ? env : std::getenv("KIWI_EP_TUNING");
     if (ov && *ov) {
@@ -94,6 +95,7 @@ EpTuning tune(const EpConfig& c, int sms, const char* env) {
                 else if (k == "gemm_pair") t.gemm_pair = parse_bool(v);
                 else if (k == "gemm_pair_auto") t.gemm_pair_auto = parse_bool(v);
                 else if (k == "gemm_split") t.gemm_split = parse_bool(v);
+                else if (k == "gemm2_pair") t.gemm2_pair = parse_bool(v);
                 else throw kiwi::error("KIWI_EP_TUNING: unknown key '" + k + "'");
             } catch (const std::invalid_argument&) {
                 throw kiwi::error("KIWI_EP_TUNING: bad number in '" + item + "'");

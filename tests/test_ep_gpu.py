@@ -227,15 +227,30 @@ def test_kiwi_ep_op_token_sweep():
 
 @pytest.mark.parametrize("fused", [True, False])
 def test_layer_with_2sm_gemm(fused):
-    """The 2-SM (256-row tile) GEMM1, with the 1-SM scatter GEMM2 of the fused
-    combine or the 2-SM GEMM2 of the unfused one: each GEMM's tile schedule
-    uses its own kernel's tile height."""
+    """Both GEMMs on the 2-SM (256-row tile) kernels: GEMM2 with the NVLink
+    scatter epilogue of the fused combine, or plain for the unfused one."""
     cfg = small_cfg("fp8", tokens=300, experts=8)
     layer = ExpertParallelMoE(cfg)
     layer.native.gemm_pair = True
     layer.native.fused_combine = fused
     x, logits = moe.synthetic_inputs(cfg, 0, "cuda")
     _check(layer, cfg, x, logits, layer(x, logits).clone())
+
+
+@pytest.mark.parametrize("fused", [True, False])
+def test_layer_with_2sm_gemm2_only(fused):
+    """gemm2_pair: GEMM1 on the 1-SM kernel (128-row tiles), GEMM2 on the 2-SM
+    kernel (256-row tiles, scatter epilogue when fused); each GEMM's tile
+    schedule uses its own kernel's tile height.  Ragged row counts."""
+    cfg = small_cfg("fp8", tokens=700, experts=8)
+    layer = ExpertParallelMoE(cfg)
+    layer.native.gemm2_pair = True
+    layer.native.fused_combine = fused
+    for t in (700, 90):
+        x, logits = moe.synthetic_inputs(cfg, 0, "cuda", tokens=t, step=t)
+        out = layer(x, logits).clone()
+        assert layer.native.gemm2_pair_in_use and not layer.native.gemm_pair_in_use
+        _check(layer, cfg, x, logits, out)
 
 
 @pytest.mark.parametrize("fused", [True, False])
