@@ -85,6 +85,8 @@ def main():
     ap.add_argument("--bk", type=int, default=64, choices=(64, 32, 128),
                     help="K columns per pipeline stage of the 1-SM kernel (32: 64-byte swizzle, 9 stages; "
                          "128: two 64-column boxes per operand, 2 stages)")
+    ap.add_argument("--no-m64", action="store_true",
+                    help="1-SM kernel: M = 128 MMAs on every tile (default: M = 64 on tiles with <= 64 rows left)")
     args = ap.parse_args()
     C = kiwi_b200.native()
     torch.manual_seed(0)
@@ -98,7 +100,8 @@ def main():
         counts = torch.full((groups,), rows, dtype=torch.int32, device="cuda")
         out = torch.empty(total, n // 2 if swiglu else n, device="cuda", dtype=torch.bfloat16)
         plan = C.ops.GroupedGemm(a, b, groups)
-        ms = timeit(lambda: plan.run(counts, out, swiglu, None, 0, False, None, args.bk), args.iters)
+        ms = timeit(lambda: plan.run(counts, out, swiglu, None, 0, False, None, args.bk, not args.no_m64),
+                    args.iters)
         ms_pair = float("nan")
         if rows >= 256 and not args.no_pair:
             ms_pair = timeit(lambda: plan.run(counts, out, swiglu, None, 0, True), args.iters)

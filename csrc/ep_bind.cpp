@@ -103,6 +103,7 @@ py::dict tuning_dict(const ep::EpTuning& t) {
     d["gemm_pair_auto"] = t.gemm_pair_auto;
     d["gemm_split"] = t.gemm_split;
     d["gemm2_pair"] = t.gemm2_pair;
+    d["gemm_m64_tails"] = t.gemm_m64_tails;
     d["source"] = t.source;
     return d;
 }
@@ -236,6 +237,7 @@ public:
         pair_auto_ = tuning_.gemm_pair_auto;
         split_ = tuning_.gemm_split;
         pair2_ = tuning_.gemm2_pair;
+        m64_ = tuning_.gemm_m64_tails;
         fused_ = tuning_.fused_combine;
         gather_ = tuning_.gather_a;
     }
@@ -347,6 +349,7 @@ public:
         g1.row_scale = nullptr;
         g1.error = reinterpret_cast<uint32_t*>(gemm_error_.data_ptr<int32_t>());
         g1.max_rows = cfg_.max_pairs();
+        g1.m64_tails = m64_ ? 1 : 0;  // read by the 1-SM kernels only
         g1.span = debug_.on() ? ws_.debug_time + ep::kDebugWordsPerPhase * ep::kPhaseGemm1 : nullptr;
         if (which == 1) {
             if (gathers()) {
@@ -525,6 +528,7 @@ private:
     bool use_pair_ = false;   // this round's choices (set by dispatch)
     bool use_split_ = false;
     bool pair2_ = false;      // GEMM2 alone on the 2-SM kernel in every round (GEMM1 stays 1-SM)
+    bool m64_ = true;         // 1-SM kernels: M = 64 MMAs on tiles with <= 64 rows of their expert left
     bool use_pair2_ = false;  // this round: GEMM2 on the 2-SM kernel (gemm_pair or gemm2_pair)
     torch::Tensor pair_end_, split_tiles_;
     bool fused_ = true;
@@ -548,6 +552,8 @@ public:
     bool pair2() const { return pair2_; }
     void set_pair2(bool v) { pair2_ = v; }
     bool pair2_in_use() const { return use_pair2_; }
+    bool m64() const { return m64_; }
+    void set_m64(bool v) { m64_ = v; }
     bool fused() const { return fused_; }
     py::dict tuning() const { return tuning_dict(tuning_); }
     void set_fused(bool v) { fused_ = v; }
@@ -805,6 +811,9 @@ void register_ep(py::module_& m) {
         .def_property("gemm2_pair", &MoeLayer::pair2, &MoeLayer::set_pair2,
                       "Run the down projection (GEMM2, with its combine epilogue) on the 2-SM kernel and the "
                       "gate/up GEMM on the 1-SM kernel in every round (opt-in).")
+        .def_property("gemm_m64_tails", &MoeLayer::m64, &MoeLayer::set_m64,
+                      "1-SM GEMM tiles with at most 64 rows of their expert left run M = 64 MMAs (default on; the "
+                      "result is bit-identical).")
         .def_property_readonly("gemm2_pair_in_use", &MoeLayer::pair2_in_use,
                                "Whether the last dispatched round runs GEMM2 on the 2-SM kernel.")
         .def_property("gemm_pair", &MoeLayer::pair, &MoeLayer::set_pair,

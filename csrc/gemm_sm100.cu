@@ -101,6 +101,19 @@ __device__ __forceinline__ int group_end_row(const GroupedArgs& p, int g) {
     return p.group_end ? __ldg(&p.group_end[g]) : __ldg(&p.group_offset[g + 1]);
 }
 
+/// Rows of group g that tile row block mt still covers (above kBM: a full tile).
+__device__ __forceinline__ int tile_rows_left(const GroupedArgs& p, int g, int mt) {
+    return group_end_row(p, g) - __ldg(&p.group_offset[g]) - mt * kBM;
+}
+
+/// Row of the tile whose accumulator is in `lane` of TMEM lane quadrant q, -1
+/// for none: an M = 128 accumulator fills all 32 lanes of each quadrant, an
+/// M = 64 one the first 16 (rows 16q..16q+15).
+__device__ __forceinline__ int acc_row(int q, int lane, bool m64) {
+    if (!m64) return q * 32 + lane;
+    return lane < 16 ? q * 16 + lane : -1;
+}
+
 __device__ __forceinline__ float silu(float x) { return x / (1.0f + __expf(-x)); }
 
 __device__ __forceinline__ void store_row32(__nv_bfloat16* dst, const float (&v)[32]) {
@@ -291,13 +304,20 @@ __global__ void __launch_bounds__(GQ >= 0 ? kGatherThreads : kThreads, 1)
         }
     } else if (warp == 1) {
         if (lane == 0) {
-            const uint32_t idesc = sm100::idesc_bf16_f32(kBM, BN);
+            const uint32_t idesc128 = sm100::idesc_bf16_f32(kBM, BN);
+            const uint32_t idesc64 = sm100::idesc_bf16_f32(64, BN);
             int stage = 0;
             uint32_t phase = 0;
             int acc = 0;
             uint32_t acc_phase = 0;
             int64_t n_mma = 0;
             for (int tile = blockIdx.x; tile < total_tiles && !*reinterpret_cast<volatile int*>(&s_abort); tile += gridDim.x) {
+                uint32_t idesc = idesc128;
+                if (p.m64_tails) {
+                    int g, mt, nt;
+                    locate_tile(p.tile_prefix, p.num_groups, n_tiles, tile, g, mt, nt);
+                    if (tile_rows_left(p, g, mt) <= 64) idesc = idesc64;
+                }
                 if (!sm100::mbar_wait(&tmem_empty[acc], acc_phase ^ 1)) {
                     fail(2);
                     break;
@@ -461,7 +481,6 @@ __global__ void __launch_bounds__(GQ >= 0 ? kGatherThreads : kThreads, 1)
     } else {
         // Epilogue: warps 2..5; TMEM lane quadrant = warp % 4.
         const int q = warp & 3;
-        const int row_in_tile = q * 32 + lane;
         int acc = 0;
         uint32_t acc_phase = 0;
         for (int tile = blockIdx.x; tile < total_tiles && !*reinterpret_cast<volatile int*>(&s_abort); tile += gridDim.x) {
@@ -474,9 +493,10 @@ __global__ void __launch_bounds__(GQ >= 0 ? kGatherThreads : kThreads, 1)
             sm100::tc_fence_after();
             const int g_off = __ldg(&p.group_offset[g]);
             const int g_rows = group_end_row(p, g) - g_off;
+            const int row_in_tile = acc_row(q, lane, p.m64_tails && g_rows - mt * kBM <= 64);
             const int r = mt * kBM + row_in_tile;
             const int64_t out_row = static_cast<int64_t>(g_off) + r;
-            const bool valid = r < g_rows && out_row < p.max_rows;
+            const bool valid = row_in_tile >= 0 && r < g_rows && out_row < p.max_rows;
             const float scale = (valid && p.row_scale) ? p.row_scale[out_row] : 1.0f;
             const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN;
             if constexpr (EPI == kEpiSwiGLU) {

@@ -107,6 +107,7 @@ extern "C" __attribute__((visibility("default"))) int kiwi_grouped_gemm_bf16_noa
             kiwi::gemm::make_tmap_bf16_2d(b, static_cast<uint64_t>(num_groups) * n, k, 256);
         kiwi::gemm::build_schedule(counts, num_groups, n, 256, offsets, tiles, s);
         kiwi::gemm::GroupedArgs args{};
+        args.m64_tails = 1;
         args.group_offset = offsets;
         args.tile_prefix = tiles;
         args.num_groups = num_groups;

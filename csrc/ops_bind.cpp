@@ -46,7 +46,7 @@ public:
 
     /// counts: int32[G] rows per group (device); out: bf16 [rows, N] or [rows, N/2] with swiglu.
     void run(torch::Tensor counts, torch::Tensor out, bool swiglu, py::object row_scale, int grid, bool pair,
-             py::object trace, int bk) {
+             py::object trace, int bk, bool m64) {
         TORCH_CHECK(bk == 64 || bk == 32 || bk == 128, "bk must be 64, 32 or 128");
         TORCH_CHECK(bk == 64 || !pair, "bk = 32 and 128 are 1-SM variants");
         TORCH_CHECK(bk != 128 || k_ % 128 == 0, "bk = 128 needs K a multiple of 128");
@@ -76,6 +76,7 @@ public:
         args.row_scale = rs;
         args.error = reinterpret_cast<uint32_t*>(error_.data_ptr<int32_t>());
         args.max_rows = out.size(0);
+        args.m64_tails = !pair && m64;
         if (!trace.is_none()) {
             torch::Tensor t = trace.cast<torch::Tensor>();
             TORCH_CHECK(t.is_cuda() && t.scalar_type() == torch::kInt64 && t.is_contiguous() && !pair,
@@ -169,10 +170,12 @@ void register_ops(py::module_& m) {
         .def(py::init<torch::Tensor, torch::Tensor, int64_t>(), py::arg("a"), py::arg("b"), py::arg("num_groups"))
         .def("run", &GroupedGemm::run, py::arg("counts"), py::arg("out"), py::arg("swiglu") = false,
              py::arg("row_scale") = py::none(), py::arg("grid") = 0, py::arg("pair") = false,
-             py::arg("trace") = py::none(), py::arg("bk") = 64,
+             py::arg("trace") = py::none(), py::arg("bk") = 64, py::arg("m64") = true,
              "Grouped GEMM on the current stream.  bk: K columns per pipeline stage of the 1-SM kernel (64: "
              "4 x 48 KB stages, the default; 32: 64-byte swizzle, 9 stages; 128: two 64-column boxes per operand, "
-             "2 x 96 KB stages).  All three issue the same K = 16 MMAs in the same order.")
+             "2 x 96 KB stages).  All three issue the same K = 16 MMAs in the same order.  m64 (1-SM kernels, on by "
+             "default): tiles with at most 64 rows of their group left run M = 64 MMAs; the result is "
+             "bit-identical.")
         .def_property_readonly("offsets", &GroupedGemm::offsets)
         .def_property_readonly("tile_prefix", &GroupedGemm::tile_prefix)
         .def_property_readonly("error", &GroupedGemm::error);

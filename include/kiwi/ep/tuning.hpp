@@ -8,7 +8,8 @@
 // fused paths the layer uses, keyed by the rank's token capacity, and records
 // where each choice was measured.  KIWI_EP_TUNING="key=value,..." overrides
 // any field (keys: dispatch_blocks, recv_blocks, combine_blocks,
-// fused_combine, gather_a, gemm_pair, gemm_pair_auto, gemm_split, gemm2_pair).
+// fused_combine, gather_a, gemm_pair, gemm_pair_auto, gemm_split, gemm2_pair,
+// gemm_m64_tails).
 #pragma once
 
 #include <string>
@@ -26,6 +27,7 @@ struct EpTuning {
     bool gemm_pair;           // 2-SM (256-row tile) grouped GEMMs alone in every round
     bool gemm_pair_auto;      // 2-SM GEMMs in rounds expecting kPairMinRows rows per local expert
     bool gemm_split;          // 2-SM pass over full 256-row tiles + 1-SM pass over the tails, every round
+    bool gemm_m64_tails;      // 1-SM GEMMs: M = 64 MMAs for tiles with <= 64 rows of their expert left
     bool gemm2_pair;          // down projection (GEMM2) on the 2-SM kernel, gate/up (GEMM1) on the 1-SM one;
                               // one B200 at 1024 rows per expert: 25.09 vs 23.19 ms per step (1-SM both)
     std::string source;       // table entry (and overrides) this came from

@@ -17,7 +17,11 @@ struct GroupedArgs {
     int32_t num_groups;
     int32_t n;                    // B rows per group (C columns before SwiGLU halves them)
     int32_t k;
-    int32_t pad_;
+    // 1-SM kernel only, non-zero: a tile whose group has at most 64 rows left
+    // runs M = 64 MMAs (half the tensor work of a mostly-padding tile, same
+    // K order, so the result is bit-identical); its accumulator holds rows
+    // 16q..16q+15 in TMEM lanes 32q..32q+15 of lane quadrant q.
+    int32_t m64_tails;
     __nv_bfloat16* c;
     int64_t ldc;                  // C row stride, elements
     const float* row_scale;       // optional per-row factor applied in the epilogue

@@ -63,11 +63,12 @@ class GroupedGemm:
     """A grouped GEMM bound to fixed A and B buffers (the kernel's tensor maps
     are built once; refill ``a`` in place between calls).
 
-    ``__call__(counts, out=None, swiglu=False, row_scale=None, bk=64, pair=False)``
+    ``__call__(counts, out=None, swiglu=False, row_scale=None, bk=64, pair=False, m64=True)``
     enqueues the GEMM on the current stream and returns ``out`` (bf16, at least
     ``a.shape[0]`` rows; rows past ``sum(counts)`` are left as they were).
     ``bk`` picks the K columns per pipeline stage (64 default; 32 and 128 are
-    opt-in 1-SM variants) and ``pair`` the 2-SM kernel; both compute the same
+    opt-in 1-SM variants), ``pair`` the 2-SM kernel and ``m64`` M = 64 MMAs on
+    1-SM tiles with at most 64 rows of their group left; all compute the same
     result.  :meth:`check` raises if the kernel reported an error (a wait that
     ran out, or a schedule that did not fit ``out``)."""
 
@@ -85,7 +86,7 @@ class GroupedGemm:
     def out_columns(self, swiglu):
         return self.n // 2 if swiglu else self.n
 
-    def __call__(self, counts, out=None, swiglu=False, row_scale=None, bk=64, pair=False):
+    def __call__(self, counts, out=None, swiglu=False, row_scale=None, bk=64, pair=False, m64=True):
         cols = self.out_columns(swiglu)
         if out is None:
             out = torch.empty(self.a.shape[0], cols, dtype=torch.bfloat16, device=self.a.device)
@@ -97,7 +98,7 @@ class GroupedGemm:
             return out
         if not torch.is_tensor(counts) or not counts.is_cuda:
             counts = torch.as_tensor(counts, dtype=torch.int32).to(self.a.device)
-        self._plan.run(counts.to(torch.int32), out, bool(swiglu), row_scale, 0, bool(pair), None, int(bk))
+        self._plan.run(counts.to(torch.int32), out, bool(swiglu), row_scale, 0, bool(pair), None, int(bk), bool(m64))
         return out
 
     def check(self):

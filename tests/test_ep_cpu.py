@@ -132,7 +132,7 @@ def test_tuning_table_and_overrides():
     cfg = dict(world=8, rank=0, hidden=7168, num_experts=256, topk=8, max_tokens=4096, quant="fp8")
     t = ep.tune(cfg, 148, "")
     assert t["fused_combine"] and not t["gather_a"] and not t["gemm_pair"] and t["gemm_pair_auto"] and not t["gemm_split"]
-    assert not t["gemm2_pair"]
+    assert not t["gemm2_pair"] and t["gemm_m64_tails"]
     assert t["recv_blocks"] == 8 * 148 and t["combine_blocks"] == 8 * 148 and t["dispatch_blocks"] == 0
     assert "throughput" in t["source"]
     lat = ep.tune({**cfg, "max_tokens": 128}, 148, "")
@@ -141,6 +141,7 @@ def test_tuning_table_and_overrides():
     assert o["gather_a"] and o["dispatch_blocks"] == 296 and not o["fused_combine"]
     assert o["source"].endswith("KIWI_EP_TUNING")
     assert ep.tune(cfg, 148, "gemm2_pair=1")["gemm2_pair"]
+    assert not ep.tune(cfg, 148, "gemm_m64_tails=0")["gemm_m64_tails"]
     for bad in ("nope=1", "gather_a=maybe", "recv_blocks=0", "dispatch_blocks", "dispatch_blocks=12abc",
                 "recv_blocks=99999999999", "combine_blocks=2000000", "dispatch_blocks=-1", "recv_blocks= 5"):
         with pytest.raises(Exception):

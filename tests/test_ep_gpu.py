@@ -254,6 +254,25 @@ def test_layer_with_2sm_gemm2_only(fused):
 
 
 @pytest.mark.parametrize("fused", [True, False])
+def test_layer_m64_tail_tiles_are_bit_identical(fused):
+    """gemm_m64_tails (default on) runs M = 64 MMAs on the 1-SM GEMM tiles with
+    at most 64 rows of their expert left; the layer's output equals the
+    M = 128 run bit for bit and the fp32 reference within tolerance."""
+    cfg = small_cfg("fp8", tokens=600, experts=8)
+    layer = ExpertParallelMoE(cfg)
+    layer.native.fused_combine = fused
+    assert layer.native.gemm_m64_tails
+    x, logits = moe.synthetic_inputs(cfg, 0, "cuda")
+    on = layer(x, logits).clone()
+    assert any(c % 128 and c % 128 <= 64 for c in layer.expert_counts.tolist())
+    layer.native.gemm_m64_tails = False
+    off = layer(x, logits).clone()
+    torch.cuda.synchronize()
+    assert torch.equal(on, off)
+    _check(layer, cfg, x, logits, on)
+
+
+@pytest.mark.parametrize("fused", [True, False])
 def test_split_gemms_match_reference(fused):
     """gemm_split runs each GEMM as a 2-SM pass over every expert's full 256-row
     tiles plus a 1-SM pass over its tail (GEMM2 with the NVLink scatter

@@ -80,6 +80,35 @@ def test_bk32_stages_match_bk64_bitwise(swiglu):
     assert torch.equal(o64, o32)
 
 
+@pytest.mark.parametrize("bk", [64, 32])
+@pytest.mark.parametrize("swiglu", [False, True])
+def test_m64_tail_tiles_match_m128_bitwise(swiglu, bk):
+    """Tiles with at most 64 rows of their group left run M = 64 MMAs (the
+    default) and give the same bits as M = 128 MMAs over the same K order, and
+    the fp32 reference within tolerance.  Groups leave tails of 1, 5, 6, 44,
+    64 and 65 rows, plus empty and whole-tile groups."""
+    torch.manual_seed(5)
+    C = kiwi_b200.native()
+    counts = [70, 0, 200, 5, 64, 65, 1, 128, 130, 300]
+    k, n = 512, 512
+    rows, groups = sum(counts), len(counts)
+    a = (torch.randn(rows, k, device="cuda") * 0.5).bfloat16()
+    b = (torch.randn(groups * n, k, device="cuda") * 0.05).bfloat16()
+    cnt = torch.tensor(counts, dtype=torch.int32, device="cuda")
+    scale = torch.rand(rows, device="cuda") + 0.5
+    cols = n // 2 if swiglu else n
+    plan = C.ops.GroupedGemm(a, b, groups)
+    m128 = torch.zeros(rows, cols, device="cuda", dtype=torch.bfloat16)
+    plan.run(cnt, m128, swiglu, scale, 0, False, None, bk, False)
+    m64 = torch.full((rows, cols), 3.0, device="cuda", dtype=torch.bfloat16)
+    plan.run(cnt, m64, swiglu, scale, 0, False, None, bk, True)
+    torch.cuda.synchronize()
+    assert int(plan.error.item()) == 0
+    assert torch.equal(m64, m128)
+    exact = _ref(a, b, counts, n, swiglu, scale)
+    assert (m64.float() - exact).abs().max().item() <= 2e-2 * exact.abs().max().item() + 1e-2
+
+
 def test_gemm_kernels_use_no_local_memory():
     C = kiwi_b200.native()
     for sw in (False, True):
