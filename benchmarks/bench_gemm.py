@@ -16,6 +16,7 @@ sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
 import torch  # noqa: E402
 
 import kiwi_b200  # noqa: E402
+from kiwi_b200.ops import block_weights  # noqa: E402
 
 
 def timeit(fn, iters=20):
@@ -85,6 +86,8 @@ def main():
     ap.add_argument("--bk", type=int, default=64, choices=(64, 32, 128),
                     help="K columns per pipeline stage of the 1-SM kernel (32: 64-byte swizzle, 9 stages; "
                          "128: two 64-column boxes per operand, 2 stages)")
+    ap.add_argument("--blocked", action="store_true",
+                    help="weights (B) in the blocked layout: one contiguous 256 x 64 box per TMA load")
     ap.add_argument("--no-m64", action="store_true",
                     help="1-SM kernel: M = 128 MMAs on every tile (default: M = 64 on tiles with <= 64 rows left)")
     args = ap.parse_args()
@@ -99,7 +102,8 @@ def main():
         b = (torch.randn(groups * n, k, device="cuda") * 0.02).bfloat16()
         counts = torch.full((groups,), rows, dtype=torch.int32, device="cuda")
         out = torch.empty(total, n // 2 if swiglu else n, device="cuda", dtype=torch.bfloat16)
-        plan = C.ops.GroupedGemm(a, b, groups)
+        plan = C.ops.GroupedGemm(a, block_weights(b, groups) if args.blocked else b, groups,
+                                 b_blocked=args.blocked)
         ms = timeit(lambda: plan.run(counts, out, swiglu, None, 0, False, None, args.bk, not args.no_m64),
                     args.iters)
         ms_pair = float("nan")

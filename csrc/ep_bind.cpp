@@ -173,17 +173,25 @@ std::array<int32_t, 3> recv_token_meta(const torch::Tensor& slot_tokens, const e
 class MoeLayer {
 public:
     MoeLayer(p2p::SymmetricHeap& heap, const py::dict& cfg, int64_t ffn, torch::Tensor w13, torch::Tensor w2,
-             uint64_t timeout_ns)
-        : heap_(heap), cfg_(config_from_dict(cfg)), ffn_(ffn), w13_(w13), w2_(w2), timeout_ns_(timeout_ns) {
+             uint64_t timeout_ns, bool weights_blocked)
+        : heap_(heap), cfg_(config_from_dict(cfg)), ffn_(ffn), w13_(w13), w2_(w2), timeout_ns_(timeout_ns),
+          blocked_(weights_blocked) {
         TORCH_CHECK(heap.size() >= cfg_.heap_bytes, "symmetric heap too small: need ", cfg_.heap_bytes, " bytes");
         TORCH_CHECK(heap.rank() == cfg_.rank && heap.world() == cfg_.world, "heap rank/world differ from config");
         const int64_t el = cfg_.experts_per_rank;
+        // Row-major [E * N, K] or blocked [E * N * K / 64, 64] (kiwi_b200.ops.block_weights).
+        const int64_t w13_rows = blocked_ ? el * 2 * ffn * cfg_.hidden / 64 : el * 2 * ffn;
+        const int64_t w13_cols = blocked_ ? 64 : cfg_.hidden;
+        const int64_t w2_rows = blocked_ ? el * cfg_.hidden * ffn / 64 : el * cfg_.hidden;
+        const int64_t w2_cols = blocked_ ? 64 : ffn;
         TORCH_CHECK(w13.is_cuda() && w13.scalar_type() == torch::kBFloat16 && w13.is_contiguous() &&
-                        w13.dim() == 2 && w13.size(0) == el * 2 * ffn && w13.size(1) == cfg_.hidden,
-                    "w13 must be contiguous bf16 [experts_per_rank * 2 * ffn, hidden] (gate/up interleaved by 128)");
+                        w13.dim() == 2 && w13.size(0) == w13_rows && w13.size(1) == w13_cols,
+                    "w13 must be contiguous bf16 [experts_per_rank * 2 * ffn, hidden] (gate/up interleaved by 128), "
+                    "or that matrix in the blocked layout with weights_blocked");
         TORCH_CHECK(w2.is_cuda() && w2.scalar_type() == torch::kBFloat16 && w2.is_contiguous() && w2.dim() == 2 &&
-                        w2.size(0) == el * cfg_.hidden && w2.size(1) == ffn,
-                    "w2 must be contiguous bf16 [experts_per_rank * hidden, ffn]");
+                        w2.size(0) == w2_rows && w2.size(1) == w2_cols,
+                    "w2 must be contiguous bf16 [experts_per_rank * hidden, ffn], or that matrix in the blocked "
+                    "layout with weights_blocked");
         TORCH_CHECK((2 * ffn) % 256 == 0 && cfg_.hidden % 256 == 0 && ffn % 64 == 0 && cfg_.hidden % 64 == 0,
                     "GEMM tiling needs 2*ffn and hidden multiples of 256, ffn of 64");
         auto dev = w13.device();
@@ -227,11 +235,11 @@ public:
         ws_.error = reinterpret_cast<uint32_t*>(error_.data_ptr<int32_t>());
 
         tmap_a1_ = gemm::make_tmap_bf16_2d(a_.data_ptr(), pairs, cfg_.hidden, 128);
-        tmap_b1_ = gemm::make_tmap_bf16_2d(w13.data_ptr(), w13.size(0), cfg_.hidden, 256);
-        tmap_b1h_ = gemm::make_tmap_bf16_2d(w13.data_ptr(), w13.size(0), cfg_.hidden, 128);
+        tmap_b1_ = gemm::make_tmap_bf16_2d(w13.data_ptr(), w13.size(0), w13.size(1), 256);
+        tmap_b1h_ = gemm::make_tmap_bf16_2d(w13.data_ptr(), w13.size(0), w13.size(1), 128);
         tmap_a2_ = gemm::make_tmap_bf16_2d(h_.data_ptr(), pairs, ffn, 128);
-        tmap_b2_ = gemm::make_tmap_bf16_2d(w2.data_ptr(), w2.size(0), ffn, 256);
-        tmap_b2h_ = gemm::make_tmap_bf16_2d(w2.data_ptr(), w2.size(0), ffn, 128);
+        tmap_b2_ = gemm::make_tmap_bf16_2d(w2.data_ptr(), w2.size(0), w2.size(1), 256);
+        tmap_b2h_ = gemm::make_tmap_bf16_2d(w2.data_ptr(), w2.size(0), w2.size(1), 128);
         tuning_ = ep::tune(cfg_, gemm::num_sms());
         pair_ = tuning_.gemm_pair;
         pair_auto_ = tuning_.gemm_pair_auto;
@@ -350,6 +358,7 @@ public:
         g1.error = reinterpret_cast<uint32_t*>(gemm_error_.data_ptr<int32_t>());
         g1.max_rows = cfg_.max_pairs();
         g1.m64_tails = m64_ ? 1 : 0;  // read by the 1-SM kernels only
+        g1.b_blocked = blocked_ ? 1 : 0;
         g1.span = debug_.on() ? ws_.debug_time + ep::kDebugWordsPerPhase * ep::kPhaseGemm1 : nullptr;
         if (which == 1) {
             if (gathers()) {
@@ -529,6 +538,7 @@ private:
     bool use_split_ = false;
     bool pair2_ = false;      // GEMM2 alone on the 2-SM kernel in every round (GEMM1 stays 1-SM)
     bool m64_ = true;         // 1-SM kernels: M = 64 MMAs on tiles with <= 64 rows of their expert left
+    bool blocked_ = false;    // w13 / w2 in the blocked layout (one contiguous 256 x 64 box per TMA load)
     bool use_pair2_ = false;  // this round: GEMM2 on the 2-SM kernel (gemm_pair or gemm2_pair)
     torch::Tensor pair_end_, split_tiles_;
     bool fused_ = true;
@@ -773,9 +783,9 @@ void register_ep(py::module_& m) {
         .def_property_readonly("src_token_pos", &Transport::src_token_pos)
         .def_property_readonly("config", &Transport::config);
     py::class_<MoeLayer>(e, "MoeLayer")
-        .def(py::init<p2p::SymmetricHeap&, const py::dict&, int64_t, torch::Tensor, torch::Tensor, uint64_t>(),
+        .def(py::init<p2p::SymmetricHeap&, const py::dict&, int64_t, torch::Tensor, torch::Tensor, uint64_t, bool>(),
              py::arg("heap"), py::arg("config"), py::arg("ffn"), py::arg("w13"), py::arg("w2"),
-             py::arg("timeout_ns") = 5000000000ull, py::keep_alive<1, 2>())
+             py::arg("timeout_ns") = 5000000000ull, py::arg("weights_blocked") = false, py::keep_alive<1, 2>())
         .def("route", &MoeLayer::route)
         .def("dispatch", &MoeLayer::dispatch)
         .def("receive", &MoeLayer::receive)

@@ -268,7 +268,9 @@ __global__ void __launch_bounds__(GQ >= 0 ? kGatherThreads : kThreads, 1)
                 int g, mt, nt;
                 locate_tile(p.tile_prefix, p.num_groups, n_tiles, tile, g, mt, nt);
                 const int row0 = __ldg(&p.group_offset[g]) + mt * kBM;
-                const int brow0 = g * p.n + nt * BN;
+                // B row of k-block 0 in either layout (row-major: x = kb * kBK
+                // at brow0; blocked: x = 0 at brow0 + kb * BN).
+                const int brow0 = p.b_blocked ? (g * n_tiles + nt) * k_blocks * BN : g * p.n + nt * BN;
                 for (int kb = 0; kb < k_blocks; ++kb) {
                     const uint64_t tw0 = p.trace ? clock64() : 0;
                     if (!sm100::mbar_wait(&empty[stage], phase ^ 1)) {
@@ -291,7 +293,12 @@ __global__ void __launch_bounds__(GQ >= 0 ? kGatherThreads : kThreads, 1)
                             sm100::tma_load_2d(sa + S::kASub, &tmap_a, &full[stage], kb * kBK + 64, row0);
                         }
                     }
-                    sm100::tma_load_2d(sb, &tmap_b, &full[stage], kb * kBK, brow0);
+                    if constexpr (BKT == 64) {
+                        if (p.b_blocked) sm100::tma_load_2d(sb, &tmap_b, &full[stage], 0, brow0 + kb * BN);
+                        else sm100::tma_load_2d(sb, &tmap_b, &full[stage], kb * kBK, brow0);
+                    } else {
+                        sm100::tma_load_2d(sb, &tmap_b, &full[stage], kb * kBK, brow0);
+                    }
                     if constexpr (BKT == 128) {
                         sm100::tma_load_2d(sb + S::kBSub, &tmap_b, &full[stage], kb * kBK + 64, brow0);
                     }
@@ -657,7 +664,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 int g, mt, nt;
                 locate_tile(p.tile_prefix, p.num_groups, n_tiles, tile, g, mt, nt);
                 const int row0 = __ldg(&p.group_offset[g]) + mt * kPairBM + static_cast<int>(crank) * 128;
-                const int brow0 = g * p.n + nt * kPairBN + static_cast<int>(crank) * 128;
+                // This CTA's 128-row half of the B tile (blocked: of each
+                // 256-row k-block box).
+                const int brow0 = p.b_blocked ? (g * n_tiles + nt) * k_blocks * kPairBN + static_cast<int>(crank) * 128
+                                              : g * p.n + nt * kPairBN + static_cast<int>(crank) * 128;
                 for (int kb = 0; kb < k_blocks; ++kb) {
                     if (!sm100::mbar_wait(&empty[stage], phase ^ 1)) {
                         fail(11);
@@ -668,7 +678,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                     if (leader) sm100::mbar_arrive_expect_tx(&full[stage], 2 * S::kStageBytes);
                     const uint32_t bar = sm100::mapa(&full[stage], 0);
                     sm100::tma_load_2d_pair(sa, &tmap_a, bar, kb * kBK, row0);
-                    sm100::tma_load_2d_pair(sb, &tmap_b, bar, kb * kBK, brow0);
+                    if (p.b_blocked) sm100::tma_load_2d_pair(sb, &tmap_b, bar, 0, brow0 + kb * kPairBN);
+                    else sm100::tma_load_2d_pair(sb, &tmap_b, bar, kb * kBK, brow0);
                     if (++stage == kPairStages) {
                         stage = 0;
                         phase ^= 1;
@@ -1002,6 +1013,7 @@ void grouped_gemm_bk128(const CUtensorMap& tmap_a, const CUtensorMap& tmap_b, co
     if (args.n % 256 != 0 || args.k % 128 != 0) {
         throw kiwi::error("grouped_gemm_bk128: N must be a multiple of 256 and K of 128");
     }
+    if (args.b_blocked) throw kiwi::error("grouped_gemm_bk128: the blocked B layout needs 64-column k-blocks");
     if (grid <= 0) grid = num_sms();
     const ScatterArgs none{};
     if (swiglu) launch_grouped<kEpiSwiGLU, kBk128Stages, -1, 128>(tmap_a, tmap_b, args, none, grid, stream);
@@ -1013,6 +1025,7 @@ void grouped_gemm_bk32(const CUtensorMap& tmap_a32, const CUtensorMap& tmap_b32,
     if (args.n % 256 != 0 || args.k % 32 != 0) {
         throw kiwi::error("grouped_gemm_bk32: N must be a multiple of 256 and K of 32");
     }
+    if (args.b_blocked) throw kiwi::error("grouped_gemm_bk32: the blocked B layout needs 64-column k-blocks");
     if (grid <= 0) grid = num_sms();
     const ScatterArgs none{};
     if (swiglu) launch_grouped<kEpiSwiGLU, kBk32Stages, -1, 32>(tmap_a32, tmap_b32, args, none, grid, stream);

@@ -21,20 +21,28 @@ cudaStream_t cur_stream() { return at::cuda::getCurrentCUDAStream().stream(); }
 /// A grouped GEMM bound to fixed A and B buffers (their tensor maps are built once).
 class GroupedGemm {
 public:
-    GroupedGemm(torch::Tensor a, torch::Tensor b, int64_t num_groups)
-        : a_(a), b_(b), num_groups_(static_cast<int>(num_groups)) {
+    GroupedGemm(torch::Tensor a, torch::Tensor b, int64_t num_groups, bool b_blocked)
+        : a_(a), b_(b), num_groups_(static_cast<int>(num_groups)), b_blocked_(b_blocked) {
         TORCH_CHECK(a.is_cuda() && b.is_cuda(), "A and B must be CUDA tensors");
         TORCH_CHECK(a.scalar_type() == torch::kBFloat16 && b.scalar_type() == torch::kBFloat16, "bf16 only");
         TORCH_CHECK(a.dim() == 2 && b.dim() == 2 && a.is_contiguous() && b.is_contiguous(), "2-D contiguous");
-        TORCH_CHECK(a.size(1) == b.size(1), "A and B must share K");
-        TORCH_CHECK(b.size(0) % num_groups == 0, "B rows must be num_groups * N");
         k_ = static_cast<int>(a.size(1));
-        n_ = static_cast<int>(b.size(0) / num_groups);
+        if (b_blocked) {
+            // [G * N * K / 64, 64]: one contiguous 256 x 64 box per (group, n-tile, k-block).
+            TORCH_CHECK(b.size(1) == 64 && k_ % 64 == 0 && (b.size(0) * 64) % (num_groups * k_) == 0,
+                        "blocked B must be [num_groups * N * K / 64, 64]");
+            n_ = static_cast<int>(b.size(0) * 64 / (num_groups * k_));
+        } else {
+            TORCH_CHECK(a.size(1) == b.size(1), "A and B must share K");
+            TORCH_CHECK(b.size(0) % num_groups == 0, "B rows must be num_groups * N");
+            n_ = static_cast<int>(b.size(0) / num_groups);
+        }
         TORCH_CHECK(k_ % 64 == 0 && n_ % 256 == 0, "K % 64 == 0 and N % 256 == 0 required");
+        const int64_t b_cols = b_blocked ? 64 : k_;
         tmap_a_ = gemm::make_tmap_bf16_2d(a.data_ptr(), a.size(0), k_, 128);
-        tmap_b_ = gemm::make_tmap_bf16_2d(b.data_ptr(), b.size(0), k_, 256);
-        tmap_b_half_ = gemm::make_tmap_bf16_2d(b.data_ptr(), b.size(0), k_, 128);
-        if (k_ % 32 == 0) {
+        tmap_b_ = gemm::make_tmap_bf16_2d(b.data_ptr(), b.size(0), b_cols, 256);
+        tmap_b_half_ = gemm::make_tmap_bf16_2d(b.data_ptr(), b.size(0), b_cols, 128);
+        if (k_ % 32 == 0 && !b_blocked) {
             tmap_a32_ = gemm::make_tmap_bf16_2d(a.data_ptr(), a.size(0), k_, 128, 32);
             tmap_b32_ = gemm::make_tmap_bf16_2d(b.data_ptr(), b.size(0), k_, 256, 32);
         }
@@ -49,6 +57,7 @@ public:
              py::object trace, int bk, bool m64) {
         TORCH_CHECK(bk == 64 || bk == 32 || bk == 128, "bk must be 64, 32 or 128");
         TORCH_CHECK(bk == 64 || !pair, "bk = 32 and 128 are 1-SM variants");
+        TORCH_CHECK(bk == 64 || !b_blocked_, "the blocked B layout runs with bk = 64 only");
         TORCH_CHECK(bk != 128 || k_ % 128 == 0, "bk = 128 needs K a multiple of 128");
         TORCH_CHECK(counts.is_cuda() && counts.scalar_type() == torch::kInt32 && counts.numel() == num_groups_,
                     "counts must be int32[num_groups] on the device");
@@ -77,6 +86,7 @@ public:
         args.error = reinterpret_cast<uint32_t*>(error_.data_ptr<int32_t>());
         args.max_rows = out.size(0);
         args.m64_tails = !pair && m64;
+        args.b_blocked = b_blocked_ ? 1 : 0;
         if (!trace.is_none()) {
             torch::Tensor t = trace.cast<torch::Tensor>();
             TORCH_CHECK(t.is_cuda() && t.scalar_type() == torch::kInt64 && t.is_contiguous() && !pair,
@@ -103,6 +113,7 @@ public:
 private:
     torch::Tensor a_, b_, offsets_, tile_prefix_, error_, row_scale_ref_, trace_ref_;
     int num_groups_, n_, k_;
+    bool b_blocked_ = false;
     CUtensorMap tmap_a_, tmap_b_, tmap_b_half_, tmap_a32_, tmap_b32_;
 };
 
@@ -167,7 +178,10 @@ void rows_accumulate_py(torch::Tensor src, torch::Tensor out, torch::Tensor map,
 void register_ops(py::module_& m) {
     auto o = m.def_submodule("ops", "sm_100a compute kernels");
     py::class_<GroupedGemm>(o, "GroupedGemm")
-        .def(py::init<torch::Tensor, torch::Tensor, int64_t>(), py::arg("a"), py::arg("b"), py::arg("num_groups"))
+        .def(py::init<torch::Tensor, torch::Tensor, int64_t, bool>(), py::arg("a"), py::arg("b"),
+             py::arg("num_groups"), py::arg("b_blocked") = false,
+             "b: [num_groups * N, K] row-major, or with b_blocked the layout of kiwi_b200.ops.block_weights "
+             "([num_groups * N * K / 64, 64], one contiguous 256 x 64 box per group, n-tile and k-block).")
         .def("run", &GroupedGemm::run, py::arg("counts"), py::arg("out"), py::arg("swiglu") = false,
              py::arg("row_scale") = py::none(), py::arg("grid") = 0, py::arg("pair") = false,
              py::arg("trace") = py::none(), py::arg("bk") = 64, py::arg("m64") = true,

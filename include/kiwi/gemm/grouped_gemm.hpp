@@ -22,6 +22,14 @@ struct GroupedArgs {
     // K order, so the result is bit-identical); its accumulator holds rows
     // 16q..16q+15 in TMEM lanes 32q..32q+15 of lane quadrant q.
     int32_t m64_tails;
+    // Non-zero: B is in the blocked layout (kiwi_b200.ops.block_weights): the
+    // 256-row x 64-column box of (group g, n-tile nt, k-block kb) is 32 KB of
+    // contiguous memory at row ((g * N / 256 + nt) * K / 64 + kb) * 256 of a
+    // [G * N * K / 64, 64] matrix, so a weight load reads whole DRAM pages
+    // instead of 128-byte pieces one B row stride apart.  64-column k-blocks
+    // only (not the bk = 32 / 128 variants).
+    int32_t b_blocked;
+    int32_t pad_;
     __nv_bfloat16* c;
     int64_t ldc;                  // C row stride, elements
     const float* row_scale;       // optional per-row factor applied in the epilogue

@@ -59,6 +59,26 @@ def grouped_gemm_reference(a, b, counts, swiglu=False, row_scale=None):
     return torch.cat(outs, 0)
 
 
+def block_weights(w, num_groups):
+    """Row-major grouped weights [G * N, K] -> the blocked layout the GEMM
+    kernels read with ``b_blocked``: a [G * N * K / 64, 64] matrix in which the
+    256-row x 64-column box of group g, n-tile nt and k-block kb is contiguous
+    (32 KB) at row ((g * N / 256 + nt) * K / 64 + kb) * 256, so every TMA load
+    of a weight tile reads whole DRAM pages.  Returns a new tensor."""
+    if w.dim() != 2 or w.shape[0] % num_groups:
+        raise ValueError("w must be [num_groups * N, K]")
+    n, k = w.shape[0] // num_groups, w.shape[1]
+    if n % 256 or k % 64:
+        raise ValueError("N must be a multiple of 256 and K of 64")
+    return w.view(num_groups, n // 256, 256, k // 64, 64).permute(0, 1, 3, 2, 4).contiguous().view(-1, 64)
+
+
+def unblock_weights(wb, num_groups, k):
+    """Inverse of :func:`block_weights` ([G * N * K / 64, 64] -> [G * N, K])."""
+    n = wb.numel() // (num_groups * k)
+    return wb.view(num_groups, n // 256, k // 64, 256, 64).permute(0, 1, 3, 2, 4).contiguous().view(-1, k)
+
+
 class GroupedGemm:
     """A grouped GEMM bound to fixed A and B buffers (the kernel's tensor maps
     are built once; refill ``a`` in place between calls).
@@ -158,4 +178,4 @@ class ExpertFFN:
         self.gemm2.check()
 
 
-__all__ = ["GroupedGemm", "grouped_gemm", "grouped_gemm_reference", "ExpertFFN"]
+__all__ = ["GroupedGemm", "grouped_gemm", "grouped_gemm_reference", "ExpertFFN", "block_weights", "unblock_weights"]

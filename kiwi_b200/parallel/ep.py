@@ -35,6 +35,7 @@ import os
 import torch
 
 from .._native import load as _load
+from .. import ops
 from ..models import moe as moe_model
 from ..utils import dist as kdist
 from .p2p import SymmetricHeap
@@ -174,7 +175,8 @@ class ExpertParallelMoE(_DebugTimingMixin):
     has finished on every rank (its combine waited for all ranks), so the
     slots' buffers are never overwritten while a peer still reads them."""
 
-    def __init__(self, cfg, group=None, max_tokens=None, weights=None, timeout_s=5.0, heap=None, in_flight=1):
+    def __init__(self, cfg, group=None, max_tokens=None, weights=None, timeout_s=5.0, heap=None, in_flight=1,
+                 weight_layout="rows"):
         if cfg.quant not in QUANTS:
             raise ValueError(f"quant must be one of {QUANTS}")
         if int(in_flight) < 1:
@@ -190,15 +192,26 @@ class ExpertParallelMoE(_DebugTimingMixin):
         self.max_tokens = max_tokens or cfg.tokens_per_rank
         self.layout = layer_config(cfg, self.rank, self.world, self.max_tokens)
         dev = torch.device("cuda", torch.cuda.current_device())
+        if weight_layout not in ("rows", "blocked"):
+            raise ValueError("weight_layout must be 'rows' or 'blocked'")
         if weights is None:
             weights = moe_model.local_expert_weights(cfg, self.rank, self.world, dev)
         self.w13, self.w2 = weights
+        self.weight_layout = weight_layout
+        if weight_layout == "blocked":
+            # The GEMMs' weight loads then read one contiguous 32 KB box each
+            # (the layer keeps the blocked copies; row-major inputs are not kept).
+            epr = cfg.num_experts // self.world
+            self.w13 = ops.block_weights(self.w13, epr)
+            self.w2 = ops.block_weights(self.w2, epr)
+            weights = None
         self.in_flight = int(in_flight)
         k = cfg.topk
         self._slots = []
         for i in range(self.in_flight):
             hp = heap if (heap is not None and i == 0) else SymmetricHeap(self.layout["heap_bytes"], group)
-            native = _C.ep.MoeLayer(hp.native, self.layout, cfg.ffn, self.w13, self.w2, int(timeout_s * 1e9))
+            native = _C.ep.MoeLayer(hp.native, self.layout, cfg.ffn, self.w13, self.w2, int(timeout_s * 1e9),
+                                    weight_layout == "blocked")
             self._slots.append(_Slot(hp, native, torch.empty(self.max_tokens, k, dtype=torch.int32, device=dev),
                                      torch.empty(self.max_tokens, k, dtype=torch.float32, device=dev),
                                      torch.empty(self.max_tokens, cfg.hidden, dtype=torch.bfloat16, device=dev),

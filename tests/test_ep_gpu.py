@@ -272,6 +272,26 @@ def test_layer_m64_tail_tiles_are_bit_identical(fused):
     _check(layer, cfg, x, logits, on)
 
 
+@pytest.mark.parametrize("pair", [False, True])
+def test_layer_blocked_weights_are_bit_identical(pair):
+    """weight_layout="blocked" (the layer keeps w13 / w2 as one contiguous
+    256 x 64 box per TMA load) gives the row-major layer's output bit for bit,
+    with the 1-SM and the 2-SM GEMMs (fused combine)."""
+    cfg = small_cfg("fp8", tokens=400, experts=8)
+    rows = ExpertParallelMoE(cfg)
+    blocked = ExpertParallelMoE(cfg, weight_layout="blocked")
+    for layer in (rows, blocked):
+        layer.native.gemm_pair = pair
+    x, logits = moe.synthetic_inputs(cfg, 0, "cuda")
+    a = rows(x, logits).clone()
+    b = blocked(x, logits).clone()
+    torch.cuda.synchronize()
+    rows.check()
+    blocked.check()
+    assert torch.equal(a, b)
+    _check(blocked, cfg, x, logits, b)
+
+
 @pytest.mark.parametrize("fused", [True, False])
 def test_split_gemms_match_reference(fused):
     """gemm_split runs each GEMM as a 2-SM pass over every expert's full 256-row

@@ -109,6 +109,34 @@ def test_m64_tail_tiles_match_m128_bitwise(swiglu, bk):
     assert (m64.float() - exact).abs().max().item() <= 2e-2 * exact.abs().max().item() + 1e-2
 
 
+@pytest.mark.parametrize("pair", [False, True])
+@pytest.mark.parametrize("swiglu", [False, True])
+def test_blocked_weights_match_row_major_bitwise(swiglu, pair):
+    """B in the blocked layout (one contiguous 256 x 64 box per TMA load) gives
+    the same bits as row-major B, on the 1-SM and the 2-SM kernel."""
+    from kiwi_b200.ops import block_weights
+
+    torch.manual_seed(6)
+    C = kiwi_b200.native()
+    counts = [300, 0, 129, 64, 512]
+    k, n = 448, 768
+    rows, groups = sum(counts), len(counts)
+    a = (torch.randn(rows, k, device="cuda") * 0.5).bfloat16()
+    b = (torch.randn(groups * n, k, device="cuda") * 0.05).bfloat16()
+    cnt = torch.tensor(counts, dtype=torch.int32, device="cuda")
+    cols = n // 2 if swiglu else n
+    ref = torch.zeros(rows, cols, device="cuda", dtype=torch.bfloat16)
+    C.ops.GroupedGemm(a, b, groups).run(cnt, ref, swiglu, None, 0, pair)
+    plan = C.ops.GroupedGemm(a, block_weights(b, groups), groups, b_blocked=True)
+    got = torch.full((rows, cols), 5.0, device="cuda", dtype=torch.bfloat16)
+    plan.run(cnt, got, swiglu, None, 0, pair)
+    torch.cuda.synchronize()
+    assert int(plan.error.item()) == 0
+    assert torch.equal(got, ref)
+    exact = _ref(a, b, counts, n, swiglu)
+    assert (got.float() - exact).abs().max().item() <= 2e-2 * exact.abs().max().item() + 1e-2
+
+
 def test_gemm_kernels_use_no_local_memory():
     C = kiwi_b200.native()
     for sw in (False, True):

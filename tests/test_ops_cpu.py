@@ -127,3 +127,22 @@ def test_quant_fp8_on_cpu_is_the_reference():
     codes, scales = quant_fp8(x)
     rc, rs = moe.quant_fp8_codes(x)
     assert torch.equal(codes.view(torch.uint8), rc.view(torch.uint8)) and torch.equal(scales, rs)
+
+
+def test_block_weights_places_each_box_contiguously_and_round_trips():
+    """block_weights: the 256 x 64 box of (group g, n-tile nt, k-block kb) is
+    rows [r, r + 256) of the [G * N * K / 64, 64] result with
+    r = ((g * N / 256 + nt) * K / 64 + kb) * 256; unblock_weights inverts it."""
+    from kiwi_b200.ops import block_weights, unblock_weights
+
+    g, n, k = 3, 512, 192
+    w = torch.randn(g * n, k).to(torch.bfloat16)
+    wb = block_weights(w, g)
+    assert wb.shape == (g * n * k // 64, 64) and wb.is_contiguous()
+    for gi, nt, kb in [(0, 0, 0), (1, 1, 2), (2, 0, 1), (2, 1, 2)]:
+        r = ((gi * (n // 256) + nt) * (k // 64) + kb) * 256
+        box = w[gi * n + nt * 256:gi * n + nt * 256 + 256, kb * 64:kb * 64 + 64]
+        assert torch.equal(wb[r:r + 256], box)
+    assert torch.equal(unblock_weights(wb, g, k), w)
+    with pytest.raises(ValueError):
+        block_weights(torch.zeros(3 * 100, 64), 3)
