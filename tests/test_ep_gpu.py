@@ -274,12 +274,13 @@ def test_layer_m64_tail_tiles_are_bit_identical(fused):
 
 @pytest.mark.parametrize("pair", [False, True])
 def test_layer_blocked_weights_are_bit_identical(pair):
-    """weight_layout="blocked" (the layer keeps w13 / w2 as one contiguous
-    256 x 64 box per TMA load) gives the row-major layer's output bit for bit,
-    with the 1-SM and the 2-SM GEMMs (fused combine)."""
+    """weight_layout="blocked" (the default: the layer keeps w13 / w2 as one
+    contiguous 256 x 64 box per TMA load) gives the row-major layer's output
+    bit for bit, with the 1-SM and the 2-SM GEMMs (fused combine)."""
     cfg = small_cfg("fp8", tokens=400, experts=8)
-    rows = ExpertParallelMoE(cfg)
-    blocked = ExpertParallelMoE(cfg, weight_layout="blocked")
+    rows = ExpertParallelMoE(cfg, weight_layout="rows")
+    blocked = ExpertParallelMoE(cfg)
+    assert blocked.weight_layout == "blocked" and blocked.w13.shape[1] == 64
     for layer in (rows, blocked):
         layer.native.gemm_pair = pair
     x, logits = moe.synthetic_inputs(cfg, 0, "cuda")
