@@ -90,18 +90,29 @@ class GroupedGemm:
     opt-in 1-SM variants), ``pair`` the 2-SM kernel and ``m64`` M = 64 MMAs on
     1-SM tiles with at most 64 rows of their group left; all compute the same
     result.  :meth:`check` raises if the kernel reported an error (a wait that
-    ran out, or a schedule that did not fit ``out``)."""
+    ran out, or a schedule that did not fit ``out``).
 
-    def __init__(self, a, b, num_groups):
+    ``b_layout="blocked"`` keeps a copy of ``b`` in the layout of
+    :func:`block_weights` for the kernel (each weight load reads one contiguous
+    32 KB box; same result) and drops the reference to the row-major ``b`` on
+    CUDA (``self.b`` is then the blocked copy); CPU tensors always use ``b`` as
+    given."""
+
+    def __init__(self, a, b, num_groups, b_layout="rows"):
         if a.dim() != 2 or b.dim() != 2 or a.shape[1] != b.shape[1] or b.shape[0] % num_groups:
             raise ValueError("a [rows, K] and b [num_groups * N, K] are required")
+        if b_layout not in ("rows", "blocked"):
+            raise ValueError("b_layout must be 'rows' or 'blocked'")
         self.a, self.b, self.num_groups = a, b, int(num_groups)
         self.n, self.k = b.shape[0] // self.num_groups, a.shape[1]
+        self.b_layout = b_layout if a.is_cuda else "rows"
         self._plan = None
         if a.is_cuda:
             from .. import native
 
-            self._plan = native().ops.GroupedGemm(a, b, self.num_groups)
+            if self.b_layout == "blocked":
+                self.b = block_weights(b, self.num_groups)
+            self._plan = native().ops.GroupedGemm(a, self.b, self.num_groups, b_blocked=self.b_layout == "blocked")
 
     def out_columns(self, swiglu):
         return self.n // 2 if swiglu else self.n
@@ -145,9 +156,11 @@ class ExpertFFN:
     its first ``sum(counts)`` rows in expert order and calls ``ffn(counts,
     row_scale)``, which runs GEMM1 with the SwiGLU epilogue into the owned
     hidden buffer and GEMM2 with the per-row scale (the routing weight) and
-    returns the bf16 rows [max_rows, H] (the first ``sum(counts)`` valid)."""
+    returns the bf16 rows [max_rows, H] (the first ``sum(counts)`` valid).
+    ``weight_layout="blocked"`` (the default) gives both GEMMs blocked copies
+    of the weights (:func:`block_weights`; same result, faster weight loads)."""
 
-    def __init__(self, w13, w2, num_experts, max_rows):
+    def __init__(self, w13, w2, num_experts, max_rows, weight_layout="blocked"):
         e = int(num_experts)
         if w13.shape[0] % (2 * e) or w2.shape[0] % e:
             raise ValueError("w13 must be [E * 2F, H] and w2 [E * H, F]")
@@ -162,8 +175,8 @@ class ExpertFFN:
         self._a = torch.zeros(rows, hidden, dtype=torch.bfloat16, device=dev)
         self._h = torch.zeros(rows, ffn, dtype=torch.bfloat16, device=dev)
         self._y = torch.zeros(rows, hidden, dtype=torch.bfloat16, device=dev)
-        self.gemm1 = GroupedGemm(self._a, w13, e)
-        self.gemm2 = GroupedGemm(self._h, w2, e)
+        self.gemm1 = GroupedGemm(self._a, w13, e, b_layout=weight_layout)
+        self.gemm2 = GroupedGemm(self._h, w2, e, b_layout=weight_layout)
 
     def input_buffer(self):
         return self._a

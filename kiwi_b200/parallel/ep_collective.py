@@ -353,9 +353,10 @@ class CollectiveMoE:
         self.device, self.rank, self.world = self.op.device, self.op.rank, self.op.world_size
         if weights is None:
             weights = moe_model.local_expert_weights(cfg, self.rank, self.world, self.device)
-        self.w13, self.w2 = weights
         max_pairs = self.world * self.max_tokens * min(cfg.topk, self.experts_per_rank)
-        self.experts = ExpertFFN(self.w13, self.w2, self.experts_per_rank, max_pairs)
+        self.experts = ExpertFFN(weights[0], weights[1], self.experts_per_rank, max_pairs)
+        # The expert GEMMs' own weights (on CUDA, blocked copies of the row-major inputs).
+        self.w13, self.w2 = self.experts.gemm1.b, self.experts.gemm2.b
         self._scale = torch.zeros(max(max_pairs, 1), dtype=torch.float32, device=self.device)
 
     def forward(self, x, router_logits):

@@ -201,3 +201,28 @@ def test_ops_route_topk_matches_the_reference(experts, topk):
     ridx, rw = moe.route_reference(logits, topk)
     assert torch.equal(idx, ridx)
     assert torch.allclose(w, rw, atol=1e-6)
+
+
+def test_expert_ffn_blocked_weights_match_rows_and_reference():
+    """kiwi_b200.ops.ExpertFFN with its default blocked weight copies gives the
+    row-major op's bits, and the MoE reference's expert math within tolerance."""
+    from kiwi_b200.ops import ExpertFFN, grouped_gemm_reference
+
+    torch.manual_seed(7)
+    e, hidden, ffn, counts = 4, 512, 256, [70, 0, 200, 33]
+    rows = sum(counts)
+    w13 = (torch.randn(e * 2 * ffn, hidden, device="cuda") * 0.05).bfloat16()
+    w2 = (torch.randn(e * hidden, ffn, device="cuda") * 0.05).bfloat16()
+    x = (torch.randn(rows, hidden, device="cuda") * 0.5).bfloat16()
+    scale = torch.rand(rows, device="cuda") + 0.5
+    outs = {}
+    for layout in ("blocked", "rows"):
+        op = ExpertFFN(w13, w2, e, rows, weight_layout=layout)
+        assert op.gemm1.b_layout == layout
+        op.input_buffer()[:rows].copy_(x)
+        outs[layout] = op(counts, scale)[:rows].clone()
+        op.check()
+    assert torch.equal(outs["blocked"], outs["rows"])
+    h = grouped_gemm_reference(x, w13, counts, swiglu=True).bfloat16()
+    ref = grouped_gemm_reference(h, w2, counts, row_scale=scale)
+    assert (outs["blocked"].float() - ref).abs().max().item() <= 3e-2 * ref.abs().max().item() + 1e-2
