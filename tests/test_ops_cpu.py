@@ -146,3 +146,20 @@ def test_block_weights_places_each_box_contiguously_and_round_trips():
     assert torch.equal(unblock_weights(wb, g, k), w)
     with pytest.raises(ValueError):
         block_weights(torch.zeros(3 * 100, 64), 3)
+
+
+def test_blocked_layout_request_on_cpu_keeps_row_major_reference():
+    """b_layout="blocked" only changes what the CUDA kernel reads; CPU tensors
+    keep the row-major B and the fp32 reference path, and a bad layout name
+    raises."""
+    torch.manual_seed(1)
+    a = torch.randn(40, 128).bfloat16()
+    b = (torch.randn(2 * 256, 128) * 0.05).bfloat16()
+    plan = GroupedGemm(a, b, 2, b_layout="blocked")
+    assert plan.b_layout == "rows" and plan.b is b
+    out = plan([30, 10])
+    assert torch.allclose(out[:40].float(), grouped_gemm_reference(a, b, [30, 10]), atol=1e-2)
+    with pytest.raises(ValueError):
+        GroupedGemm(a, b, 2, b_layout="tiled")
+    ffn = ExpertFFN(torch.zeros(2 * 2 * 128, 128).bfloat16(), torch.zeros(2 * 128, 128).bfloat16(), 2, 8)
+    assert ffn.gemm1.b_layout == "rows"
