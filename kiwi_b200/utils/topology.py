@@ -13,15 +13,18 @@ from .._native import load as _load
 
 
 def gpu_local_cpus(device):
-    """CPUs local to CUDA device `device` that this process may run on."""
+    """CPUs local to CUDA device `device` that this process may run on; all the
+    CPUs it may run on when the device's local CPUs are unknown (no GPU, no
+    sysfs entry) or none of them is allowed."""
     local = set(_load().topology.gpu_local_cpus(int(device)))
     allowed = os.sched_getaffinity(0)
     return sorted(local & allowed)
 
 
 def bind_process_to_gpu(device):
-    """Restricts this process to `device`'s local CPUs; returns them (empty list,
-    and nothing changed, when the node's CPUs are unknown or not allowed)."""
+    """Restricts this process to `device`'s local CPUs and returns them.  When
+    those are unknown or not allowed, :func:`gpu_local_cpus` returns every CPU
+    the process may already use, so the affinity does not change."""
     cpus = gpu_local_cpus(device)
     if cpus:
         os.sched_setaffinity(0, cpus)

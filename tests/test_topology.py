@@ -27,3 +27,24 @@ def test_poller_cpus_differ_per_device():
     if len(usable) >= 8:
         flat = [c for p in picks for c in p]
         assert len(set(flat)) == len(flat), picks
+
+
+def test_bind_process_to_gpu_changes_nothing_without_local_cpus():
+    """Without a GPU the device's local CPUs are unknown: gpu_local_cpus falls
+    back to every allowed CPU, and bind_process_to_gpu leaves the affinity as
+    it was (run in a child process so the test runner's own affinity is never
+    touched)."""
+    import subprocess
+    import sys
+
+    code = ("import os, torch\n"
+            "from kiwi_b200.utils.topology import bind_process_to_gpu, gpu_local_cpus\n"
+            "before = os.sched_getaffinity(0)\n"
+            "if torch.cuda.is_available():\n"
+            "    print('skip'); raise SystemExit\n"
+            "assert gpu_local_cpus(0) == sorted(before) and bind_process_to_gpu(0) == sorted(before)\n"
+            "assert os.sched_getaffinity(0) == before\n"
+            "print('ok')\n")
+    r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stderr
+    assert r.stdout.strip() in ("ok", "skip")
